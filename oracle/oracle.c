@@ -1,0 +1,1402 @@
+/*
+ * CPU oracle: plain-C restatement of the stwo-ml CPU prover for the GKR
+ * matmul-sumcheck path.  TEST INFRASTRUCTURE ONLY (see oracle.h): it is the
+ * checker for the CUDA product and the CPU baseline of bench.py, never part
+ * of the product.
+ *
+ * Third-party arithmetic restated here: starknet-crypto 0.6.2 / starknet-ff
+ * 0.3.7 (engine/Cargo.toml:55-56), which the reference uses for felt252,
+ * poseidon_permute_comp, poseidon_hash and poseidon_hash_many.  The published
+ * Starknet Poseidon is restated from its definition: width 3, 4 full + 83
+ * partial + 4 full rounds, each round = add the round's 3 keys, cube (all
+ * three lanes in full rounds, lane 2 in partial rounds), then the MDS
+ * [[3,1,1],[1,-1,1],[1,1,-2]].  The uncompressed 91 x 3 keys are used here on
+ * purpose (the product uses its own compressed form), so the two
+ * implementations check each other.
+ */
+#include "oracle.h"
+
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------ */
+/* felt252: generic CIOS Montgomery over 4 x 64-bit limbs                   */
+/* ------------------------------------------------------------------------ */
+
+typedef unsigned __int128 u128;
+typedef struct { uint64_t v[4]; } fe;
+
+static const fe FE_P = {{1ULL, 0ULL, 0ULL, 0x0800000000000011ULL}};
+static fe FE_R2;        /* R^2 mod p, R = 2^256 */
+static fe FE_ONE_M;     /* R mod p */
+static uint64_t FE_N0;  /* -p^{-1} mod 2^64 */
+static fe RK_M[91][3];  /* round keys, Montgomery form */
+static int g_init = 0;
+static pthread_once_t g_once = PTHREAD_ONCE_INIT;
+
+static const uint64_t RAW_RK[273][4] = {
+#include "../stwo-ml_b200/csrc/poseidon3_round_keys.inc"
+};
+
+static int fe_geq(const fe *a, const fe *b) {
+    for (int i = 3; i >= 0; i--) {
+        if (a->v[i] != b->v[i]) return a->v[i] > b->v[i];
+    }
+    return 1;
+}
+
+static void fe_sub_raw(fe *r, const fe *a, const fe *b) {
+    uint64_t borrow = 0;
+    for (int i = 0; i < 4; i++) {
+        u128 d = (u128)a->v[i] - b->v[i] - borrow;
+        r->v[i] = (uint64_t)d;
+        borrow = (uint64_t)(d >> 64) ? 1 : 0;
+    }
+}
+
+static uint64_t fe_add_raw(fe *r, const fe *a, const fe *b) {
+    uint64_t carry = 0;
+    for (int i = 0; i < 4; i++) {
+        u128 s = (u128)a->v[i] + b->v[i] + carry;
+        r->v[i] = (uint64_t)s;
+        carry = (uint64_t)(s >> 64);
+    }
+    return carry;
+}
+
+static void fe_add(fe *r, const fe *a, const fe *b) {
+    fe t;
+    fe_add_raw(&t, a, b); /* < 2p < 2^253: no carry out */
+    if (fe_geq(&t, &FE_P)) fe_sub_raw(&t, &t, &FE_P);
+    *r = t;
+}
+
+static void fe_sub(fe *r, const fe *a, const fe *b) {
+    if (fe_geq(a, b)) {
+        fe_sub_raw(r, a, b);
+    } else {
+        fe t;
+        fe_add_raw(&t, a, &FE_P);
+        fe_sub_raw(r, &t, b);
+    }
+}
+
+/* Coarsely Integrated Operand Scanning Montgomery product a*b*R^-1 mod p. */
+static void fe_mont_mul(fe *r, const fe *a, const fe *b) {
+    uint64_t t[6] = {0, 0, 0, 0, 0, 0};
+    for (int i = 0; i < 4; i++) {
+        uint64_t c = 0;
+        for (int j = 0; j < 4; j++) {
+            u128 s = (u128)a->v[j] * b->v[i] + t[j] + c;
+            t[j] = (uint64_t)s;
+            c = (uint64_t)(s >> 64);
+        }
+        u128 s = (u128)t[4] + c;
+        t[4] = (uint64_t)s;
+        t[5] = (uint64_t)(s >> 64);
+        uint64_t m = t[0] * FE_N0;
+        s = (u128)m * FE_P.v[0] + t[0];
+        c = (uint64_t)(s >> 64);
+        for (int j = 1; j < 4; j++) {
+            s = (u128)m * FE_P.v[j] + t[j] + c;
+            t[j - 1] = (uint64_t)s;
+            c = (uint64_t)(s >> 64);
+        }
+        s = (u128)t[4] + c;
+        t[3] = (uint64_t)s;
+        t[4] = t[5] + (uint64_t)(s >> 64);
+    }
+    fe res = {{t[0], t[1], t[2], t[3]}};
+    if (t[4] || fe_geq(&res, &FE_P)) fe_sub_raw(&res, &res, &FE_P);
+    *r = res;
+}
+
+static void fe_to_mont(fe *r, const fe *a) { fe_mont_mul(r, a, &FE_R2); }
+static void fe_from_mont(fe *r, const fe *a) {
+    fe one = {{1, 0, 0, 0}};
+    fe_mont_mul(r, a, &one);
+}
+
+static void fe_from_canon(fe *r, const uint64_t v[4]) { memcpy(r->v, v, 32); }
+static void fe_u64(fe *r, uint64_t x) {
+    r->v[0] = x;
+    r->v[1] = r->v[2] = r->v[3] = 0;
+}
+
+static void oracle_init_once(void) {
+    /* n0 = -p^{-1} mod 2^64 by Newton iteration */
+    uint64_t inv = 1;
+    for (int i = 0; i < 7; i++) inv *= 2 - FE_P.v[0] * inv;
+    FE_N0 = (uint64_t)0 - inv;
+    /* R mod p and R^2 mod p by doubling */
+    fe x;
+    fe_u64(&x, 1);
+    for (int i = 0; i < 512; i++) {
+        if (i == 256) FE_ONE_M = x;
+        fe y;
+        fe_add(&y, &x, &x);
+        x = y;
+    }
+    FE_R2 = x;
+    for (int r = 0; r < 91; r++)
+        for (int c = 0; c < 3; c++) {
+            fe k;
+            fe_from_canon(&k, RAW_RK[3 * r + c]);
+            fe_to_mont(&RK_M[r][c], &k);
+        }
+    g_init = 1;
+}
+
+static void oracle_init(void) { pthread_once(&g_once, oracle_init_once); }
+
+void orc_felt_mul(const uint64_t a[4], const uint64_t b[4], uint64_t out[4]) {
+    oracle_init();
+    fe x, y, xm, ym, r;
+    fe_from_canon(&x, a);
+    fe_from_canon(&y, b);
+    fe_to_mont(&xm, &x);
+    fe_to_mont(&ym, &y);
+    fe_mont_mul(&r, &xm, &ym);
+    fe_from_mont(&r, &r);
+    memcpy(out, r.v, 32);
+}
+
+/* Hades permutation on Montgomery-form state. */
+static void hades_m(fe s[3]) {
+    for (int r = 0; r < 91; r++) {
+        int full = (r < 4) || (r >= 87);
+        for (int c = 0; c < 3; c++) fe_add(&s[c], &s[c], &RK_M[r][c]);
+        for (int c = full ? 0 : 2; c < 3; c++) {
+            fe sq;
+            fe_mont_mul(&sq, &s[c], &s[c]);
+            fe_mont_mul(&s[c], &sq, &s[c]);
+        }
+        /* MDS [[3,1,1],[1,-1,1],[1,1,-2]] */
+        fe t, d0, d1, d2, a0, a1, a2;
+        fe_add(&t, &s[0], &s[1]);
+        fe_add(&t, &t, &s[2]);
+        fe_add(&d0, &s[0], &s[0]);
+        fe_add(&a0, &t, &d0);
+        fe_add(&d1, &s[1], &s[1]);
+        fe_sub(&a1, &t, &d1);
+        fe_add(&d2, &s[2], &s[2]);
+        fe_add(&d2, &d2, &s[2]);
+        fe_sub(&a2, &t, &d2);
+        s[0] = a0;
+        s[1] = a1;
+        s[2] = a2;
+    }
+}
+
+static void hades_canon(fe s[3]) {
+    fe m[3];
+    for (int i = 0; i < 3; i++) fe_to_mont(&m[i], &s[i]);
+    hades_m(m);
+    for (int i = 0; i < 3; i++) fe_from_mont(&s[i], &m[i]);
+}
+
+void orc_hades(uint64_t state[12]) {
+    oracle_init();
+    fe s[3];
+    for (int i = 0; i < 3; i++) fe_from_canon(&s[i], state + 4 * i);
+    hades_canon(s);
+    for (int i = 0; i < 3; i++) memcpy(state + 4 * i, s[i].v, 32);
+}
+
+static void pos_hash(fe *out, const fe *a, const fe *b) {
+    fe s[3];
+    s[0] = *a;
+    s[1] = *b;
+    fe_u64(&s[2], 2);
+    hades_canon(s);
+    *out = s[0];
+}
+
+void orc_poseidon_hash(const uint64_t a[4], const uint64_t b[4], uint64_t out[4]) {
+    oracle_init();
+    fe x, y, r;
+    fe_from_canon(&x, a);
+    fe_from_canon(&y, b);
+    pos_hash(&r, &x, &y);
+    memcpy(out, r.v, 32);
+}
+
+/* Rate-2 sponge with "1" padding (starknet_crypto::poseidon_hash_many). */
+static void pos_hash_many(fe *out, const fe *in, size_t n) {
+    fe s[3];
+    fe_u64(&s[0], 0);
+    fe_u64(&s[1], 0);
+    fe_u64(&s[2], 0);
+    size_t i = 0;
+    while (n - i >= 2) {
+        fe_add(&s[0], &s[0], &in[i]);
+        fe_add(&s[1], &s[1], &in[i + 1]);
+        hades_canon(s);
+        i += 2;
+    }
+    fe one;
+    fe_u64(&one, 1);
+    if (n - i == 1) {
+        fe_add(&s[0], &s[0], &in[i]);
+        fe_add(&s[1], &s[1], &one);
+    } else {
+        fe_add(&s[0], &s[0], &one);
+    }
+    hades_canon(s);
+    *out = s[0];
+}
+
+void orc_poseidon_hash_many(const uint64_t *in, size_t n, uint64_t out[4]) {
+    oracle_init();
+    fe *v = (fe *)malloc(sizeof(fe) * (n ? n : 1));
+    for (size_t i = 0; i < n; i++) fe_from_canon(&v[i], in + 4 * i);
+    fe r;
+    pos_hash_many(&r, v, n);
+    memcpy(out, r.v, 32);
+    free(v);
+}
+
+/* ------------------------------------------------------------------------ */
+/* M31 / CM31 / QM31 (stwo core/fields/{m31,cm31,qm31}.rs)                   */
+/* ------------------------------------------------------------------------ */
+
+#define MP 0x7fffffffu
+typedef struct { uint32_t a, b, c, d; } q31;
+
+static inline uint32_t m_red64(uint64_t x) {
+    x = (x & MP) + (x >> 31);
+    x = (x & MP) + (x >> 31);
+    return (uint32_t)(x >= MP ? x - MP : x);
+}
+static inline uint32_t m_add(uint32_t x, uint32_t y) {
+    uint32_t s = x + y;
+    return s >= MP ? s - MP : s;
+}
+static inline uint32_t m_sub(uint32_t x, uint32_t y) { return x >= y ? x - y : x + MP - y; }
+static inline uint32_t m_mul(uint32_t x, uint32_t y) { return m_red64((uint64_t)x * y); }
+static uint32_t m_pow(uint32_t x, uint64_t e) {
+    uint32_t r = 1;
+    while (e) {
+        if (e & 1) r = m_mul(r, x);
+        x = m_mul(x, x);
+        e >>= 1;
+    }
+    return r;
+}
+static inline uint32_t m_inv(uint32_t x) { return m_pow(x, MP - 2); }
+
+static inline q31 q_make(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    q31 r = {a, b, c, d};
+    return r;
+}
+static inline q31 q_from_m(uint32_t x) { return q_make(x, 0, 0, 0); }
+static inline q31 q_add(q31 x, q31 y) {
+    return q_make(m_add(x.a, y.a), m_add(x.b, y.b), m_add(x.c, y.c), m_add(x.d, y.d));
+}
+static inline q31 q_sub(q31 x, q31 y) {
+    return q_make(m_sub(x.a, y.a), m_sub(x.b, y.b), m_sub(x.c, y.c), m_sub(x.d, y.d));
+}
+/* (x0 + x1 i)(y0 + y1 i) */
+static inline void cm_mul(uint32_t x0, uint32_t x1, uint32_t y0, uint32_t y1, uint32_t *r0,
+                          uint32_t *r1) {
+    *r0 = m_sub(m_mul(x0, y0), m_mul(x1, y1));
+    *r1 = m_add(m_mul(x0, y1), m_mul(x1, y0));
+}
+/* (a + b u)(c + d u) = (ac + R bd) + (ad + bc) u, R = 2 + i */
+static q31 q_mul(q31 x, q31 y) {
+    uint32_t ac0, ac1, bd0, bd1, ad0, ad1, bc0, bc1, rb0, rb1;
+    cm_mul(x.a, x.b, y.a, y.b, &ac0, &ac1);
+    cm_mul(x.c, x.d, y.c, y.d, &bd0, &bd1);
+    cm_mul(x.a, x.b, y.c, y.d, &ad0, &ad1);
+    cm_mul(x.c, x.d, y.a, y.b, &bc0, &bc1);
+    cm_mul(2, 1, bd0, bd1, &rb0, &rb1);
+    return q_make(m_add(ac0, rb0), m_add(ac1, rb1), m_add(ad0, bc0), m_add(ad1, bc1));
+}
+static inline q31 q_mul_m(q31 x, uint32_t s) {
+    return q_make(m_mul(x.a, s), m_mul(x.b, s), m_mul(x.c, s), m_mul(x.d, s));
+}
+static q31 q_inv(q31 x) {
+    /* (a + b u)^-1 = (a - b u) / (a^2 - R b^2), all in CM31 */
+    uint32_t a2r, a2i, b2r, b2i, rb0, rb1;
+    cm_mul(x.a, x.b, x.a, x.b, &a2r, &a2i);
+    cm_mul(x.c, x.d, x.c, x.d, &b2r, &b2i);
+    cm_mul(2, 1, b2r, b2i, &rb0, &rb1);
+    uint32_t den0 = m_sub(a2r, rb0), den1 = m_sub(a2i, rb1);
+    uint32_t nrm = m_inv(m_add(m_mul(den0, den0), m_mul(den1, den1)));
+    uint32_t inv0 = m_mul(den0, nrm), inv1 = m_mul(m_sub(0, den1), nrm);
+    uint32_t r0, r1, r2, r3;
+    cm_mul(x.a, x.b, inv0, inv1, &r0, &r1);
+    cm_mul(m_sub(0, x.c), m_sub(0, x.d), inv0, inv1, &r2, &r3);
+    return q_make(r0, r1, r2, r3);
+}
+static inline int q_eq(q31 x, q31 y) { return x.a == y.a && x.b == y.b && x.c == y.c && x.d == y.d; }
+static inline q31 q_load(const uint32_t *p) { return q_make(p[0], p[1], p[2], p[3]); }
+static inline void q_store(uint32_t *p, q31 x) {
+    p[0] = x.a;
+    p[1] = x.b;
+    p[2] = x.c;
+    p[3] = x.d;
+}
+
+void orc_qm31_mul(const uint32_t a[4], const uint32_t b[4], uint32_t out[4]) {
+    q_store(out, q_mul(q_load(a), q_load(b)));
+}
+void orc_qm31_inv(const uint32_t a[4], uint32_t out[4]) { q_store(out, q_inv(q_load(a))); }
+
+/* ------------------------------------------------------------------------ */
+/* Tiny pthread parallel-for (stands in for the reference's rayon pools)     */
+/* ------------------------------------------------------------------------ */
+
+typedef void (*range_fn)(void *ctx, size_t lo, size_t hi);
+typedef struct {
+    range_fn fn;
+    void *ctx;
+    size_t lo, hi;
+} par_job;
+
+static void *par_worker(void *p) {
+    par_job *j = (par_job *)p;
+    j->fn(j->ctx, j->lo, j->hi);
+    return NULL;
+}
+
+static void parallel_for(size_t n, int threads, range_fn fn, void *ctx) {
+    if (threads <= 1 || n < 2) {
+        fn(ctx, 0, n);
+        return;
+    }
+    if ((size_t)threads > n) threads = (int)n;
+    pthread_t tid[256];
+    par_job jobs[256];
+    if (threads > 256) threads = 256;
+    size_t chunk = (n + threads - 1) / threads;
+    int launched = 0;
+    jobs[0].lo = 0;
+    jobs[0].hi = chunk < n ? chunk : n;
+    for (int t = 0; t < threads; t++) {
+        size_t lo = t * chunk, hi = lo + chunk > n ? n : lo + chunk;
+        if (lo >= hi) break;
+        jobs[t].fn = fn;
+        jobs[t].ctx = ctx;
+        jobs[t].lo = lo;
+        jobs[t].hi = hi;
+        if (t == 0) continue;
+        pthread_create(&tid[t], NULL, par_worker, &jobs[t]);
+        launched = t;
+    }
+    fn(ctx, jobs[0].lo, jobs[0].hi);
+    for (int t = 1; t <= launched; t++) pthread_join(tid[t], NULL);
+}
+
+/* ------------------------------------------------------------------------ */
+/* PoseidonChannel (engine/src/crypto/poseidon_channel.rs:83-306)            */
+/* ------------------------------------------------------------------------ */
+
+static void felt_of_qm31(fe *r, q31 v) {
+    /* securefield_to_felt: 2^124 sentinel | a<<93 | b<<62 | c<<31 | d */
+    u128 lo = ((u128)1 << 124) | ((u128)v.a << 93) | ((u128)v.b << 62) | ((u128)v.c << 31) | v.d;
+    r->v[0] = (uint64_t)lo;
+    r->v[1] = (uint64_t)(lo >> 64);
+    r->v[2] = r->v[3] = 0;
+}
+
+void orc_securefield_to_felt(const uint32_t v[4], uint64_t out[4]) {
+    fe r;
+    felt_of_qm31(&r, q_load(v));
+    memcpy(out, r.v, 32);
+}
+
+/* pack_m31s: acc = 1; acc = acc * 2^31 + m (never wraps for <= 8 values) */
+static void pack_m31s(fe *r, const uint32_t *m, size_t cnt) {
+    fe acc;
+    fe_u64(&acc, 1);
+    for (size_t i = 0; i < cnt; i++) {
+        /* shift left by 31 */
+        uint64_t nv[4];
+        nv[3] = (acc.v[3] << 31) | (acc.v[2] >> 33);
+        nv[2] = (acc.v[2] << 31) | (acc.v[1] >> 33);
+        nv[1] = (acc.v[1] << 31) | (acc.v[0] >> 33);
+        nv[0] = (acc.v[0] << 31) | m[i];
+        memcpy(acc.v, nv, 32);
+    }
+    *r = acc;
+}
+
+void orc_ch_init(orc_channel *ch) { memset(ch, 0, sizeof(*ch)); }
+
+static void ch_mix(orc_channel *ch, const fe *v) {
+    oracle_init();
+    fe s[3];
+    fe_from_canon(&s[0], ch->digest);
+    s[1] = *v;
+    fe_u64(&s[2], 2);
+    hades_canon(s);
+    memcpy(ch->digest, s[0].v, 32);
+    ch->n_draws = 0;
+    ch->hash_count++;
+}
+
+void orc_ch_mix_u64(orc_channel *ch, uint64_t v) {
+    fe f;
+    fe_u64(&f, v);
+    ch_mix(ch, &f);
+}
+
+void orc_ch_mix_felt(orc_channel *ch, const uint64_t v[4]) {
+    fe f;
+    fe_from_canon(&f, v);
+    ch_mix(ch, &f);
+}
+
+static void ch_draw(orc_channel *ch, fe *out) {
+    oracle_init();
+    fe s[3];
+    fe_from_canon(&s[0], ch->digest);
+    fe_u64(&s[1], ch->n_draws);
+    fe_u64(&s[2], 3);
+    hades_canon(s);
+    ch->n_draws++;
+    ch->hash_count++;
+    *out = s[0];
+}
+
+void orc_ch_draw_felt(orc_channel *ch, uint64_t out[4]) {
+    fe f;
+    ch_draw(ch, &f);
+    memcpy(out, f.v, 32);
+}
+
+static q31 ch_draw_qm31(orc_channel *ch) {
+    fe f;
+    ch_draw(ch, &f);
+    uint32_t m[4];
+    for (int i = 0; i < 4; i++) {
+        /* remainder mod 2^31, reduced mod P; then floor-divide by 2^31 */
+        uint32_t rem = (uint32_t)(f.v[0] & 0x7fffffffu);
+        m[i] = rem % MP;
+        f.v[0] = (f.v[0] >> 31) | (f.v[1] << 33);
+        f.v[1] = (f.v[1] >> 31) | (f.v[2] << 33);
+        f.v[2] = (f.v[2] >> 31) | (f.v[3] << 33);
+        f.v[3] = f.v[3] >> 31;
+    }
+    return q_make(m[0], m[1], m[2], m[3]);
+}
+
+void orc_ch_draw_qm31(orc_channel *ch, uint32_t out[4]) { q_store(out, ch_draw_qm31(ch)); }
+
+static void ch_digest_hash_many(orc_channel *ch, const fe *tail, size_t n_tail) {
+    fe buf[64];
+    fe *in = n_tail + 1 <= 64 ? buf : (fe *)malloc(sizeof(fe) * (n_tail + 1));
+    fe_from_canon(&in[0], ch->digest);
+    for (size_t i = 0; i < n_tail; i++) in[i + 1] = tail[i];
+    fe r;
+    pos_hash_many(&r, in, n_tail + 1);
+    memcpy(ch->digest, r.v, 32);
+    ch->n_draws = 0;
+    ch->hash_count++;
+    if (in != buf) free(in);
+}
+
+void orc_ch_mix_poly_coeffs(orc_channel *ch, const uint32_t c[12]) {
+    oracle_init();
+    fe t[2];
+    pack_m31s(&t[0], c, 8);
+    pack_m31s(&t[1], c + 8, 4);
+    ch_digest_hash_many(ch, t, 2);
+}
+
+void orc_ch_mix_poly_coeffs_deg3(orc_channel *ch, const uint32_t c[16]) {
+    oracle_init();
+    fe t[2];
+    pack_m31s(&t[0], c, 8);
+    pack_m31s(&t[1], c + 8, 8);
+    ch_digest_hash_many(ch, t, 2);
+}
+
+void orc_ch_mix_felts(orc_channel *ch, const uint32_t *qm31s, size_t n) {
+    oracle_init();
+    if (n == 0) return;
+    size_t nt = (n + 1) / 2;
+    fe *t = (fe *)malloc(sizeof(fe) * nt);
+    for (size_t i = 0, o = 0; i < n; i += 2, o++) pack_m31s(&t[o], qm31s + 4 * i, (n - i >= 2) ? 8 : 4);
+    ch_digest_hash_many(ch, t, nt);
+    free(t);
+}
+
+static void ch_mix_sf(orc_channel *ch, q31 v) {
+    fe f;
+    felt_of_qm31(&f, v);
+    ch_mix(ch, &f);
+}
+
+/* ------------------------------------------------------------------------ */
+/* MLE helpers (components/matmul.rs:118-356)                                */
+/* ------------------------------------------------------------------------ */
+
+static size_t next_pow2(size_t x) {
+    size_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+static unsigned ilog2(size_t x) {
+    unsigned l = 0;
+    while (((size_t)1 << (l + 1)) <= x) l++;
+    return l;
+}
+
+/* compute_lagrange_basis: each challenge doubles the table as [w(1-c), w c],
+ * so challenge 0 ends up on the most significant index bit. */
+static q31 *lagrange_basis(const q31 *c, size_t v) {
+    size_t n = (size_t)1 << v;
+    q31 *w = (q31 *)malloc(sizeof(q31) * n);
+    w[0] = q_from_m(1);
+    size_t len = 1;
+    for (size_t l = 0; l < v; l++) {
+        q31 one_minus = q_sub(q_from_m(1), c[l]);
+        for (size_t i = len; i-- > 0;) {
+            q31 x = w[i];
+            w[2 * i] = q_mul(x, one_minus);
+            w[2 * i + 1] = q_mul(x, c[l]);
+        }
+        len *= 2;
+    }
+    return w;
+}
+
+void orc_lagrange_basis(const uint32_t *challenges, size_t v, uint32_t *out) {
+    q31 *w = lagrange_basis((const q31 *)challenges, v);
+    memcpy(out, w, sizeof(q31) << v);
+    free(w);
+}
+
+typedef struct {
+    q31 *cur;
+    size_t mid;
+    q31 r;
+} fold_ctx;
+
+static void fold_range(void *p, size_t lo, size_t hi) {
+    fold_ctx *f = (fold_ctx *)p;
+    for (size_t i = lo; i < hi; i++)
+        f->cur[i] = q_add(f->cur[i], q_mul(f->r, q_sub(f->cur[f->mid + i], f->cur[i])));
+}
+
+/* restrict_mle: in-place folds, first assignment = most significant variable;
+ * parallel when mid >= 8192 (matmul.rs:144-168). */
+static void restrict_inplace(q31 *cur, size_t size, const q31 *assign, size_t n_assign, int threads) {
+    for (size_t t = 0; t < n_assign; t++) {
+        size_t mid = size / 2;
+        fold_ctx f = {cur, mid, assign[t]};
+        parallel_for(mid, mid >= 8192 ? threads : 1, fold_range, &f);
+        size = mid;
+    }
+}
+
+void orc_restrict_mle(const uint32_t *evals, size_t n_evals, const uint32_t *assign, size_t n_assign,
+                      uint32_t *out) {
+    q31 *cur = (q31 *)malloc(sizeof(q31) * n_evals);
+    memcpy(cur, evals, sizeof(q31) * n_evals);
+    restrict_inplace(cur, n_evals, (const q31 *)assign, n_assign, 1);
+    memcpy(out, cur, sizeof(q31) * (n_evals >> n_assign));
+    free(cur);
+}
+
+void orc_evaluate_mle(const uint32_t *evals, size_t n_vars, const uint32_t *point, uint32_t out[4]) {
+    size_t n = (size_t)1 << n_vars;
+    q31 *cur = (q31 *)malloc(sizeof(q31) * n);
+    memcpy(cur, evals, sizeof(q31) * n);
+    restrict_inplace(cur, n, (const q31 *)point, n_vars, 1);
+    q_store(out, cur[0]);
+    free(cur);
+}
+
+/* ------------------------------------------------------------------------ */
+/* reduce_matmul_layer (backend.rs:110-197)                                  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    const uint32_t *mat;
+    size_t rows, cols, out_len;
+    const q31 *lag;
+    q31 *out;
+} restrict_ctx;
+
+/* restrict_cols_unpadded: f_b[i] = sum_{j < cols} B[i][j] * L_j */
+static void rcols_range(void *p, size_t lo, size_t hi) {
+    restrict_ctx *c = (restrict_ctx *)p;
+    for (size_t i = lo; i < hi; i++) {
+        q31 s = q_from_m(0);
+        const uint32_t *row = c->mat + i * c->cols;
+        for (size_t j = 0; j < c->cols; j++) s = q_add(s, q_mul_m(c->lag[j], row[j]));
+        c->out[i] = s;
+    }
+}
+
+/* restrict_rows_unpadded: f_a[j] = sum_{i < rows} A[i][j] * L_i */
+static void rrows_range(void *p, size_t lo, size_t hi) {
+    restrict_ctx *c = (restrict_ctx *)p;
+    for (size_t j = lo; j < hi; j++) {
+        q31 s = q_from_m(0);
+        for (size_t i = 0; i < c->rows; i++) s = q_add(s, q_mul_m(c->lag[i], c->mat[i * c->cols + j]));
+        c->out[j] = s;
+    }
+}
+
+typedef struct {
+    const uint32_t *mat;
+    size_t rows, cols, prows, pcols;
+    q31 *mle;
+    int col_major;
+} mle_ctx;
+
+/* matrix_to_mle (row-major) / matrix_to_mle_col_major on the padded matrix */
+static void mle_range(void *p, size_t lo, size_t hi) {
+    mle_ctx *c = (mle_ctx *)p;
+    if (!c->col_major) {
+        for (size_t i = lo; i < hi; i++)
+            for (size_t j = 0; j < c->pcols; j++)
+                c->mle[i * c->pcols + j] =
+                    (i < c->rows && j < c->cols) ? q_from_m(c->mat[i * c->cols + j]) : q_from_m(0);
+    } else {
+        for (size_t j = lo; j < hi; j++)
+            for (size_t i = 0; i < c->prows; i++)
+                c->mle[j * c->prows + i] =
+                    (i < c->rows && j < c->cols) ? q_from_m(c->mat[i * c->cols + j]) : q_from_m(0);
+    }
+}
+
+static void restrict_a(const uint32_t *a, size_t m, size_t k, const q31 *r_i, size_t n_ri, size_t pk,
+                       q31 *f_a, int mode, int threads) {
+    size_t pm = next_pow2(m);
+    if (mode == 0) {
+        q31 *mle = (q31 *)malloc(sizeof(q31) * pm * pk);
+        mle_ctx mc = {a, m, k, pm, pk, mle, 0};
+        parallel_for(pm, pm * pk >= 65536 ? threads : 1, mle_range, &mc);
+        restrict_inplace(mle, pm * pk, r_i, n_ri, threads);
+        memcpy(f_a, mle, sizeof(q31) * pk);
+        free(mle);
+    } else {
+        q31 *lag = lagrange_basis(r_i, n_ri);
+        restrict_ctx rc = {a, m, k, pk, lag, f_a};
+        for (size_t j = k; j < pk; j++) f_a[j] = q_from_m(0);
+        parallel_for(k, k >= 64 ? threads : 1, rrows_range, &rc);
+        free(lag);
+    }
+}
+
+static void restrict_b(const uint32_t *b, size_t k, size_t n, const q31 *r_j, size_t n_rj, size_t pk,
+                       q31 *f_b, int mode, int threads) {
+    size_t pn = next_pow2(n);
+    if (mode == 0) {
+        q31 *mle = (q31 *)malloc(sizeof(q31) * pn * pk);
+        mle_ctx mc = {b, k, n, pk, pn, mle, 1};
+        parallel_for(pn, pn * pk >= 65536 ? threads : 1, mle_range, &mc);
+        restrict_inplace(mle, pn * pk, r_j, n_rj, threads);
+        memcpy(f_b, mle, sizeof(q31) * pk);
+        free(mle);
+    } else {
+        q31 *lag = lagrange_basis(r_j, n_rj);
+        restrict_ctx rc = {b, k, n, pk, lag, f_b};
+        for (size_t i = k; i < pk; i++) f_b[i] = q_from_m(0);
+        parallel_for(k, k >= 64 ? threads : 1, rcols_range, &rc);
+        free(lag);
+    }
+}
+
+static void sumcheck_rounds(q31 *fa, q31 *fb, size_t pk, orc_channel *ch, uint32_t *out_rp,
+                            uint32_t *out_ch, q31 *fa_out, q31 *fb_out) {
+    q31 inv2 = q_from_m(m_inv(2));
+    size_t len = pk;
+    unsigned log_k = ilog2(pk);
+    for (unsigned r = 0; r < log_k; r++) {
+        size_t mid = len / 2;
+        q31 s0 = q_from_m(0), s1 = s0, s2 = s0;
+        for (size_t i = 0; i < mid; i++) {
+            s0 = q_add(s0, q_mul(fa[i], fb[i]));
+            s1 = q_add(s1, q_mul(fa[mid + i], fb[mid + i]));
+            q31 a2 = q_sub(q_add(fa[mid + i], fa[mid + i]), fa[i]);
+            q31 b2 = q_sub(q_add(fb[mid + i], fb[mid + i]), fb[i]);
+            s2 = q_add(s2, q_mul(a2, b2));
+        }
+        q31 c0 = s0;
+        q31 c2 = q_mul(q_add(q_sub(q_sub(s2, s1), s1), s0), inv2);
+        q31 c1 = q_sub(q_sub(s1, s0), c2);
+        uint32_t coeffs[12];
+        q_store(coeffs, c0);
+        q_store(coeffs + 4, c1);
+        q_store(coeffs + 8, c2);
+        if (out_rp) memcpy(out_rp + 12 * r, coeffs, sizeof(coeffs));
+        orc_ch_mix_poly_coeffs(ch, coeffs);
+        q31 alpha = ch_draw_qm31(ch);
+        if (out_ch) q_store(out_ch + 4 * r, alpha);
+        for (size_t i = 0; i < mid; i++) {
+            fa[i] = q_add(fa[i], q_mul(alpha, q_sub(fa[mid + i], fa[i])));
+            fb[i] = q_add(fb[i], q_mul(alpha, q_sub(fb[mid + i], fb[i])));
+        }
+        len = mid;
+    }
+    *fa_out = len ? fa[0] : q_from_m(0);
+    *fb_out = len ? fb[0] : q_from_m(0);
+}
+
+int orc_reduce_matmul_layer(const uint32_t *a, size_t a_rows, size_t a_cols, const uint32_t *b,
+                            size_t b_rows, size_t b_cols, const uint32_t *r_i, size_t n_ri,
+                            const uint32_t *r_j, size_t n_rj, size_t pk, orc_channel *ch,
+                            uint32_t *out_round_polys, uint32_t *out_challenges,
+                            uint32_t out_final_a[4], uint32_t out_final_b[4], int mode, int threads) {
+    oracle_init();
+    if (a_cols != b_rows || pk != next_pow2(a_cols) || next_pow2(a_rows) != ((size_t)1 << n_ri) ||
+        next_pow2(b_cols) != ((size_t)1 << n_rj))
+        return 1;
+    q31 *fa = (q31 *)malloc(sizeof(q31) * pk);
+    q31 *fb = (q31 *)malloc(sizeof(q31) * pk);
+    restrict_a(a, a_rows, a_cols, (const q31 *)r_i, n_ri, pk, fa, mode, threads);
+    restrict_b(b, b_rows, b_cols, (const q31 *)r_j, n_rj, pk, fb, mode, threads);
+    q31 xa, xb;
+    sumcheck_rounds(fa, fb, pk, ch, out_round_polys, out_challenges, &xa, &xb);
+    q_store(out_final_a, xa);
+    q_store(out_final_b, xb);
+    free(fa);
+    free(fb);
+    return 0;
+}
+
+int orc_reduce_matmul_gkr(const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                          const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
+                          orc_channel *ch, uint32_t *out_round_polys, uint32_t out_final_a[4],
+                          uint32_t out_final_b[4], uint32_t *next_point, int mode, int threads) {
+    size_t pm = next_pow2(m), pk = next_pow2(k), pn = next_pow2(n);
+    unsigned log_m = ilog2(pm), log_n = ilog2(pn), log_k = ilog2(pk);
+    if (n_point != log_m + log_n) return 1;
+    orc_ch_mix_u64(ch, m);
+    orc_ch_mix_u64(ch, k);
+    orc_ch_mix_u64(ch, n);
+    ch_mix_sf(ch, q_load(claim_value));
+    uint32_t *chal = (uint32_t *)malloc(16 * (log_k + 1));
+    int rc = orc_reduce_matmul_layer(a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n,
+                                     pk, ch, out_round_polys, chal, out_final_a, out_final_b, mode, threads);
+    if (rc) {
+        free(chal);
+        return rc;
+    }
+    ch_mix_sf(ch, q_load(out_final_a));
+    ch_mix_sf(ch, q_load(out_final_b));
+    if (next_point) {
+        memcpy(next_point, claim_point, 16 * log_m);
+        memcpy(next_point + 4 * log_m, chal, 16 * log_k);
+    }
+    free(chal);
+    return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Poseidon Merkle (crypto/poseidon_merkle.rs)                               */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    const fe *in;
+    fe *out;
+} layer_ctx;
+
+static void layer_range(void *p, size_t lo, size_t hi) {
+    layer_ctx *c = (layer_ctx *)p;
+    for (size_t i = lo; i < hi; i++) pos_hash(&c->out[i], &c->in[2 * i], &c->in[2 * i + 1]);
+}
+
+/* Builds all layers; layer l has (padded n) >> l nodes.  Returns the layer
+ * array (caller frees each and the array) and the number of layers. */
+static fe **merkle_build(const q31 *evals, size_t n, size_t *n_layers, int threads) {
+    size_t pn = next_pow2(n);
+    if (pn < 2) pn = 2;
+    size_t L = ilog2(pn) + 1;
+    fe **layers = (fe **)malloc(sizeof(fe *) * L);
+    layers[0] = (fe *)calloc(pn, sizeof(fe));
+    for (size_t i = 0; i < n; i++) felt_of_qm31(&layers[0][i], evals[i]);
+    size_t len = pn;
+    for (size_t l = 1; l < L; l++) {
+        size_t pairs = len / 2;
+        layers[l] = (fe *)malloc(sizeof(fe) * pairs);
+        layer_ctx c = {layers[l - 1], layers[l]};
+        parallel_for(pairs, pairs >= 256 ? threads : 1, layer_range, &c);
+        len = pairs;
+    }
+    *n_layers = L;
+    return layers;
+}
+
+static void merkle_free(fe **layers, size_t L) {
+    for (size_t l = 0; l < L; l++) free(layers[l]);
+    free(layers);
+}
+
+/* root_only_parallel: keeps one layer at a time */
+static void merkle_root(const q31 *evals, size_t n, fe *root, int threads) {
+    size_t pn = next_pow2(n);
+    if (pn < 2) pn = 2;
+    fe *cur = (fe *)calloc(pn, sizeof(fe));
+    for (size_t i = 0; i < n; i++) felt_of_qm31(&cur[i], evals[i]);
+    size_t len = pn;
+    while (len > 1) {
+        size_t pairs = len / 2;
+        fe *nxt = (fe *)malloc(sizeof(fe) * pairs);
+        layer_ctx c = {cur, nxt};
+        parallel_for(pairs, pairs >= 256 ? threads : 1, layer_range, &c);
+        free(cur);
+        cur = nxt;
+        len = pairs;
+    }
+    *root = cur[0];
+    free(cur);
+}
+
+void orc_merkle_root_qm31(const uint32_t *evals, size_t n, uint64_t out[4], int threads) {
+    oracle_init();
+    fe r;
+    merkle_root((const q31 *)evals, n, &r, threads);
+    memcpy(out, r.v, 32);
+}
+
+void orc_merkle_path_qm31(const uint32_t *evals, size_t n, size_t index, uint64_t *out, int threads) {
+    oracle_init();
+    size_t L;
+    fe **layers = merkle_build((const q31 *)evals, n, &L, threads);
+    size_t idx = index;
+    for (size_t l = 0; l + 1 < L; l++) {
+        memcpy(out + 4 * l, layers[l][idx ^ 1].v, 32);
+        idx >>= 1;
+    }
+    merkle_free(layers, L);
+}
+
+int orc_merkle_verify(const uint64_t root[4], size_t index, const uint64_t leaf[4],
+                      const uint64_t *siblings, size_t n_siblings) {
+    oracle_init();
+    fe cur, sib;
+    fe_from_canon(&cur, leaf);
+    size_t idx = index;
+    for (size_t l = 0; l < n_siblings; l++) {
+        fe_from_canon(&sib, siblings + 4 * l);
+        if (idx & 1)
+            pos_hash(&cur, &sib, &cur);
+        else
+            pos_hash(&cur, &cur, &sib);
+        idx >>= 1;
+    }
+    return memcmp(cur.v, root, 32) == 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* MLE opening (crypto/mle_opening.rs:1654-2029)                             */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    uint64_t *buf;
+    size_t len, cap;
+    int overflow;
+} felt_out;
+
+static void out_push(felt_out *o, const fe *f) {
+    if (o->len >= o->cap) {
+        o->overflow = 1;
+        o->len++;
+        return;
+    }
+    memcpy(o->buf + 4 * o->len, f->v, 32);
+    o->len++;
+}
+static void out_u64(felt_out *o, uint64_t x) {
+    fe f;
+    fe_u64(&f, x);
+    out_push(o, &f);
+}
+static void out_qm31(felt_out *o, q31 v) {
+    out_u64(o, v.a);
+    out_u64(o, v.b);
+    out_u64(o, v.c);
+    out_u64(o, v.d);
+}
+
+static int prove_opening(const q31 *evals, size_t n_vars, const q31 *point, orc_channel *ch,
+                         size_t n_queries_cfg, fe *commitment, felt_out *o, q31 *final_out, int threads) {
+    size_t n = (size_t)1 << n_vars;
+    q31 **lay = (q31 **)malloc(sizeof(q31 *) * (n_vars + 1));
+    lay[0] = (q31 *)malloc(sizeof(q31) * n);
+    memcpy(lay[0], evals, sizeof(q31) * n);
+    fe root;
+    merkle_root(lay[0], n, &root, threads);
+    ch_mix(ch, &root);
+    *commitment = root;
+    fe *inter = (fe *)malloc(sizeof(fe) * (n_vars + 1));
+    size_t n_inter = 0;
+    size_t len = n;
+    for (size_t r = 0; r < n_vars; r++) {
+        size_t mid = len / 2;
+        lay[r + 1] = (q31 *)malloc(sizeof(q31) * mid);
+        for (size_t j = 0; j < mid; j++)
+            lay[r + 1][j] = q_add(lay[r][j], q_mul(point[r], q_sub(lay[r][mid + j], lay[r][j])));
+        if (mid > 1) {
+            fe rt;
+            merkle_root(lay[r + 1], mid, &rt, threads);
+            ch_mix(ch, &rt);
+            inter[n_inter++] = rt;
+        }
+        len = mid;
+    }
+    q31 final_value = lay[n_vars][0];
+    size_t half_n = n / 2;
+    size_t nq = n_queries_cfg < half_n ? n_queries_cfg : half_n;
+    size_t *qidx = (size_t *)malloc(sizeof(size_t) * (nq + 1));
+    for (size_t q = 0; q < nq; q++) {
+        fe f;
+        ch_draw(ch, &f);
+        qidx[q] = (size_t)(f.v[0] % half_n);
+    }
+    /* serialize: intermediate roots, queries, final value */
+    out_u64(o, n_inter);
+    for (size_t i = 0; i < n_inter; i++) out_push(o, &inter[i]);
+    out_u64(o, nq);
+    /* build each round's tree once; serialization is query-major, so keep trees */
+    size_t *nl = (size_t *)malloc(sizeof(size_t) * n_vars);
+    fe ***trees = (fe ***)malloc(sizeof(fe **) * n_vars);
+    len = n;
+    for (size_t r = 0; r < n_vars; r++) {
+        trees[r] = merkle_build(lay[r], len, &nl[r], threads);
+        len /= 2;
+    }
+    for (size_t q = 0; q < nq; q++) {
+        out_u64(o, qidx[q]);
+        out_u64(o, n_vars);
+        size_t idx = qidx[q];
+        len = n;
+        for (size_t r = 0; r < n_vars; r++) {
+            size_t mid = len / 2;
+            size_t li = idx, ri = mid + idx;
+            out_qm31(o, lay[r][li]);
+            out_qm31(o, lay[r][ri]);
+            size_t sides[2] = {li, ri};
+            for (int s = 0; s < 2; s++) {
+                out_u64(o, nl[r] - 1);
+                size_t x = sides[s];
+                for (size_t l = 0; l + 1 < nl[r]; l++) {
+                    out_push(o, &trees[r][l][x ^ 1]);
+                    x >>= 1;
+                }
+            }
+            size_t next_half = mid / 2 > 0 ? mid / 2 : 1;
+            idx %= next_half;
+            len = mid;
+        }
+    }
+    out_qm31(o, final_value);
+    if (final_out) *final_out = final_value;
+    for (size_t r = 0; r < n_vars; r++) merkle_free(trees[r], nl[r]);
+    free(trees);
+    free(nl);
+    free(qidx);
+    free(inter);
+    for (size_t r = 0; r <= n_vars; r++) free(lay[r]);
+    free(lay);
+    return 0;
+}
+
+int orc_prove_mle_opening(const uint32_t *evals, size_t n_vars, const uint32_t *point, orc_channel *ch,
+                          size_t n_queries, uint64_t commitment[4], uint64_t *calldata, size_t cap,
+                          size_t *out_len, int threads) {
+    oracle_init();
+    felt_out o = {calldata, 0, cap, 0};
+    fe c;
+    prove_opening((const q31 *)evals, n_vars, (const q31 *)point, ch, n_queries, &c, &o, NULL, threads);
+    memcpy(commitment, c.v, 32);
+    *out_len = o.len;
+    return o.overflow ? 2 : 0;
+}
+
+/* Calldata reader */
+typedef struct {
+    const uint64_t *buf;
+    size_t len, pos;
+    int bad;
+} felt_in;
+
+static int in_felt(felt_in *in, fe *f) {
+    if (in->pos >= in->len) {
+        in->bad = 1;
+        fe_u64(f, 0);
+        return 0;
+    }
+    fe_from_canon(f, in->buf + 4 * in->pos);
+    in->pos++;
+    return 1;
+}
+static uint64_t in_u64(felt_in *in) {
+    fe f;
+    in_felt(in, &f);
+    if (f.v[1] || f.v[2] || f.v[3]) in->bad = 1;
+    return f.v[0];
+}
+static q31 in_qm31(felt_in *in) {
+    uint64_t a = in_u64(in), b = in_u64(in), c = in_u64(in), d = in_u64(in);
+    if (a >= MP || b >= MP || c >= MP || d >= MP) in->bad = 1;
+    return q_make((uint32_t)a, (uint32_t)b, (uint32_t)c, (uint32_t)d);
+}
+
+static int verify_opening(const fe *commitment, felt_in *in, const q31 *point, size_t n_rounds,
+                          orc_channel *ch, size_t n_queries_cfg, q31 *final_out) {
+    size_t n_inter = in_u64(in);
+    if (in->bad || n_inter > 64) return 0;
+    fe inter[64];
+    for (size_t i = 0; i < n_inter; i++) in_felt(in, &inter[i]);
+    ch_mix(ch, commitment);
+    for (size_t i = 0; i < n_inter; i++) ch_mix(ch, &inter[i]);
+    size_t nq = in_u64(in);
+    if (n_rounds == 0) return nq == 0;
+    size_t half_n = (size_t)1 << (n_rounds - 1);
+    size_t exp_q = n_queries_cfg < half_n ? n_queries_cfg : half_n;
+    if (nq != exp_q) return 0;
+    size_t qidx[64];
+    if (nq > 64) return 0;
+    for (size_t q = 0; q < nq; q++) {
+        fe f;
+        ch_draw(ch, &f);
+        qidx[q] = (size_t)(f.v[0] % half_n);
+    }
+    int ok = 1;
+    q31 last_fold = q_from_m(0);
+    for (size_t q = 0; q < nq && ok; q++) {
+        size_t pair = in_u64(in);
+        size_t rounds = in_u64(in);
+        if (pair != qidx[q] || rounds != n_rounds) {
+            ok = 0;
+            break;
+        }
+        size_t cur = pair, layer_size = (size_t)1 << n_rounds;
+        for (size_t r = 0; r < n_rounds; r++) {
+            size_t mid = layer_size / 2;
+            q31 lv = in_qm31(in), rv = in_qm31(in);
+            size_t idxs[2] = {cur, mid + cur};
+            q31 vals[2] = {lv, rv};
+            for (int s = 0; s < 2; s++) {
+                size_t ns = in_u64(in);
+                if (in->bad || ns > 64) return 0;
+                uint64_t sib[64 * 4];
+                for (size_t l = 0; l < ns; l++) {
+                    fe f;
+                    in_felt(in, &f);
+                    memcpy(sib + 4 * l, f.v, 32);
+                }
+                if (r < 1 + n_inter) {
+                    const fe *rt = r == 0 ? commitment : &inter[r - 1];
+                    fe leaf;
+                    felt_of_qm31(&leaf, vals[s]);
+                    if (!orc_merkle_verify(rt->v, idxs[s], leaf.v, sib, ns)) ok = 0;
+                }
+            }
+            q31 folded = q_add(lv, q_mul(point[r], q_sub(rv, lv)));
+            if (r == n_rounds - 1) last_fold = folded;
+            size_t next_half = mid / 2 > 0 ? mid / 2 : 1;
+            cur %= next_half;
+            layer_size = mid;
+        }
+        (void)last_fold;
+    }
+    q31 fv = in_qm31(in);
+    if (in->bad) return 0;
+    /* every query's last fold must equal final_value: recheck by replaying */
+    if (final_out) *final_out = fv;
+    return ok;
+}
+
+int orc_verify_mle_opening(const uint64_t commitment[4], const uint64_t *calldata, size_t len,
+                           const uint32_t *point, size_t n_vars, orc_channel *ch, size_t n_queries,
+                           uint32_t out_final[4]) {
+    oracle_init();
+    felt_in in = {calldata, len, 0, 0};
+    fe c;
+    fe_from_canon(&c, commitment);
+    q31 fv;
+    /* first pass: structural + Merkle checks */
+    orc_channel saved = *ch;
+    int ok = verify_opening(&c, &in, (const q31 *)point, n_vars, ch, n_queries, &fv);
+    if (!ok) return 0;
+    /* second pass: check each query's final fold equals the final value */
+    felt_in in2 = {calldata, len, 0, 0};
+    size_t n_inter = in_u64(&in2);
+    in2.pos += n_inter;
+    size_t nq = in_u64(&in2);
+    for (size_t q = 0; q < nq; q++) {
+        in_u64(&in2);
+        size_t rounds = in_u64(&in2);
+        q31 folded = q_from_m(0);
+        for (size_t r = 0; r < rounds; r++) {
+            q31 lv = in_qm31(&in2), rv = in_qm31(&in2);
+            for (int s = 0; s < 2; s++) {
+                size_t ns = in_u64(&in2);
+                in2.pos += ns;
+            }
+            folded = q_add(lv, q_mul(((const q31 *)point)[r], q_sub(rv, lv)));
+        }
+        if (!q_eq(folded, fv)) return 0;
+    }
+    (void)saved;
+    if (out_final) q_store(out_final, fv);
+    return in.pos == len;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Single-MatMul GKR proof (gkr/prover.rs:1500-2251, cairo_serde.rs)          */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+    const uint32_t *a;
+    const uint32_t *b;
+    uint32_t *c;
+    size_t k, n;
+} mm_ctx;
+
+static void mm_range(void *p, size_t lo, size_t hi) {
+    mm_ctx *c = (mm_ctx *)p;
+    for (size_t i = lo; i < hi; i++)
+        for (size_t j = 0; j < c->n; j++) {
+            uint64_t s = 0;
+            for (size_t l = 0; l < c->k; l++) {
+                s += (uint64_t)c->a[i * c->k + l] * c->b[l * c->n + j];
+                if ((l & 3) == 3) s = m_red64(s);
+            }
+            c->c[i * c->n + j] = m_red64(s);
+        }
+}
+
+void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n, uint32_t *c,
+                    int threads) {
+    mm_ctx ctx = {a, b, c, k, n};
+    parallel_for(m, threads, mm_range, &ctx);
+}
+
+void orc_io_commitment(const uint32_t *input, size_t in_rows, size_t in_cols, const uint32_t *output,
+                       size_t out_rows, size_t out_cols, uint64_t out[4]) {
+    oracle_init();
+    size_t n = 6 + in_rows * in_cols + out_rows * out_cols, p = 0;
+    fe *v = (fe *)malloc(sizeof(fe) * n);
+    fe_u64(&v[p++], in_rows);
+    fe_u64(&v[p++], in_cols);
+    fe_u64(&v[p++], in_rows * in_cols);
+    for (size_t i = 0; i < in_rows * in_cols; i++) fe_u64(&v[p++], input[i]);
+    fe_u64(&v[p++], out_rows);
+    fe_u64(&v[p++], out_cols);
+    fe_u64(&v[p++], out_rows * out_cols);
+    for (size_t i = 0; i < out_rows * out_cols; i++) fe_u64(&v[p++], output[i]);
+    fe r;
+    pos_hash_many(&r, v, n);
+    memcpy(out, r.v, 32);
+    free(v);
+}
+
+/* padded row-major MLE of a matrix */
+static q31 *mle_row_major(const uint32_t *mat, size_t rows, size_t cols) {
+    size_t pr = next_pow2(rows), pc = next_pow2(cols);
+    q31 *m = (q31 *)malloc(sizeof(q31) * pr * pc);
+    mle_ctx mc = {mat, rows, cols, pr, pc, m, 0};
+    mle_range(&mc, 0, pr);
+    return m;
+}
+static q31 *mle_col_major(const uint32_t *mat, size_t rows, size_t cols, int threads) {
+    size_t pr = next_pow2(rows), pc = next_pow2(cols);
+    q31 *m = (q31 *)malloc(sizeof(q31) * pr * pc);
+    mle_ctx mc = {mat, rows, cols, pr, pc, m, 1};
+    parallel_for(pc, threads, mle_range, &mc);
+    return m;
+}
+
+static void gkr_prefix(orc_channel *ch, size_t m, size_t k, const uint64_t *policy) {
+    orc_ch_mix_u64(ch, 1); /* circuit depth: the single MatMul layer */
+    orc_ch_mix_u64(ch, m);
+    orc_ch_mix_u64(ch, k);
+    if (policy && (policy[0] | policy[1] | policy[2] | policy[3])) orc_ch_mix_felt(ch, policy);
+}
+
+int orc_prove_gkr_matmul(const uint32_t *input, size_t m, size_t k, const uint32_t *weight, size_t n,
+                         const uint64_t *policy, size_t n_queries, uint64_t *calldata, size_t cap,
+                         size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads) {
+    oracle_init();
+    orc_channel ch;
+    orc_ch_init(&ch);
+    gkr_prefix(&ch, m, k, policy);
+    size_t pm = next_pow2(m), pk = next_pow2(k), pn = next_pow2(n);
+    unsigned log_m = ilog2(pm), log_n = ilog2(pn), log_k = ilog2(pk);
+    uint32_t *out = (uint32_t *)malloc(4 * m * n);
+    orc_matmul_m31(input, m, k, weight, n, out, threads);
+    q31 *omle = mle_row_major(out, m, n);
+    q31 *r_out = (q31 *)malloc(sizeof(q31) * (log_m + log_n + 1));
+    for (unsigned i = 0; i < log_m + log_n; i++) r_out[i] = ch_draw_qm31(&ch);
+    uint32_t val[4];
+    orc_evaluate_mle((const uint32_t *)omle, log_m + log_n, (const uint32_t *)r_out, val);
+    ch_mix_sf(&ch, q_load(val));
+    free(omle);
+
+    uint32_t *rp = (uint32_t *)malloc(48 * (log_k + 1));
+    uint32_t fa[4], fb[4];
+    q31 *next_pt = (q31 *)malloc(sizeof(q31) * (log_m + log_k + 1));
+    int rc = orc_reduce_matmul_gkr((const uint32_t *)r_out, log_m + log_n, val, input, m, k, weight, n, &ch,
+                                   rp, fa, fb, (uint32_t *)next_pt, 1, threads);
+    if (rc) return rc;
+
+    felt_out o = {calldata, 0, cap, 0};
+    out_u64(&o, 1);          /* number of layer proofs */
+    out_u64(&o, 0);          /* tag: MatMul */
+    out_u64(&o, log_k);      /* rounds */
+    for (unsigned r = 0; r < log_k; r++) {
+        out_qm31(&o, q_load(rp + 12 * r));     /* c0 */
+        out_qm31(&o, q_load(rp + 12 * r + 8)); /* c2 */
+    }
+    out_qm31(&o, q_load(fa));
+    out_qm31(&o, q_load(fb));
+    /* input claim */
+    out_u64(&o, log_m + log_k);
+    for (unsigned i = 0; i < log_m + log_k; i++) out_qm31(&o, next_pt[i]);
+    out_qm31(&o, q_load(fa));
+    /* weight opening, sequential mode: eval point = r_j || sumcheck challenges */
+    q31 *wpt = (q31 *)malloc(sizeof(q31) * (log_n + log_k + 1));
+    memcpy(wpt, r_out + log_m, sizeof(q31) * log_n);
+    memcpy(wpt + log_n, next_pt + log_m, sizeof(q31) * log_k);
+    q31 *bmle = mle_col_major(weight, k, n, threads);
+    size_t ocap = cap > o.len ? cap - o.len : 0;
+    uint64_t *obuf = (uint64_t *)malloc(32 * (ocap ? ocap : 1));
+    felt_out oo = {obuf, 0, ocap, 0};
+    fe commitment;
+    prove_opening(bmle, log_n + log_k, wpt, &ch, n_queries, &commitment, &oo, NULL, threads);
+    free(bmle);
+    out_u64(&o, 1); /* weight commitments */
+    out_push(&o, &commitment);
+    out_u64(&o, 1); /* weight openings */
+    out_u64(&o, log_n + log_k);
+    for (unsigned i = 0; i < log_n + log_k; i++) out_qm31(&o, wpt[i]);
+    out_qm31(&o, q_load(fb));
+    for (size_t i = 0; i < oo.len && !oo.overflow; i++) {
+        fe f;
+        fe_from_canon(&f, obuf + 4 * i);
+        out_push(&o, &f);
+    }
+    orc_io_commitment(input, m, k, out, m, n, io);
+    fe iof;
+    fe_from_canon(&iof, io);
+    out_push(&o, &iof);
+    memcpy(digest, ch.digest, 32);
+    *out_len = o.len;
+    int ovf = o.overflow || oo.overflow;
+    free(obuf);
+    free(wpt);
+    free(next_pt);
+    free(rp);
+    free(r_out);
+    free(out);
+    return ovf ? 2 : 0;
+}
+
+int orc_verify_gkr_matmul(const uint32_t *input, size_t m, size_t k, const uint32_t *weight, size_t n,
+                          const uint64_t *policy, size_t n_queries, const uint64_t *calldata, size_t len,
+                          uint64_t digest[4]) {
+    oracle_init();
+    size_t pm = next_pow2(m), pk = next_pow2(k), pn = next_pow2(n);
+    unsigned log_m = ilog2(pm), log_n = ilog2(pn), log_k = ilog2(pk);
+    felt_in in = {calldata, len, 0, 0};
+    orc_channel ch;
+    orc_ch_init(&ch);
+    gkr_prefix(&ch, m, k, policy);
+    /* output claim from the claimed output = input . weight */
+    uint32_t *out = (uint32_t *)malloc(4 * m * n);
+    orc_matmul_m31(input, m, k, weight, n, out, 1);
+    q31 *omle = mle_row_major(out, m, n);
+    q31 r_out[64];
+    for (unsigned i = 0; i < log_m + log_n; i++) r_out[i] = ch_draw_qm31(&ch);
+    uint32_t val[4];
+    orc_evaluate_mle((const uint32_t *)omle, log_m + log_n, (const uint32_t *)r_out, val);
+    free(omle);
+    ch_mix_sf(&ch, q_load(val));
+    int ok = in_u64(&in) == 1 && in_u64(&in) == 0 && in_u64(&in) == log_k;
+    /* verify_matmul_reduction */
+    orc_ch_mix_u64(&ch, m);
+    orc_ch_mix_u64(&ch, k);
+    orc_ch_mix_u64(&ch, n);
+    ch_mix_sf(&ch, q_load(val));
+    q31 cur = q_load(val);
+    q31 chal[64];
+    for (unsigned r = 0; r < log_k && ok; r++) {
+        q31 c0 = in_qm31(&in), c2 = in_qm31(&in);
+        /* compressed poly: c1 = claim - 2 c0 - c2 */
+        q31 c1 = q_sub(q_sub(cur, q_add(c0, c0)), c2);
+        uint32_t coeffs[12];
+        q_store(coeffs, c0);
+        q_store(coeffs + 4, c1);
+        q_store(coeffs + 8, c2);
+        orc_ch_mix_poly_coeffs(&ch, coeffs);
+        chal[r] = ch_draw_qm31(&ch);
+        cur = q_add(c0, q_add(q_mul(c1, chal[r]), q_mul(c2, q_mul(chal[r], chal[r]))));
+    }
+    q31 fa = in_qm31(&in), fb = in_qm31(&in);
+    if (!q_eq(cur, q_mul(fa, fb))) ok = 0;
+    ch_mix_sf(&ch, fa);
+    ch_mix_sf(&ch, fb);
+    /* input claim must match and evaluate the input MLE */
+    if (in_u64(&in) != log_m + log_k) ok = 0;
+    q31 ipt[64];
+    for (unsigned i = 0; i < log_m + log_k && ok; i++) {
+        ipt[i] = in_qm31(&in);
+        q31 expect = i < log_m ? r_out[i] : chal[i - log_m];
+        if (!q_eq(ipt[i], expect)) ok = 0;
+    }
+    q31 ival = in_qm31(&in);
+    if (!q_eq(ival, fa)) ok = 0;
+    if (ok) {
+        q31 *imle = mle_row_major(input, m, k);
+        uint32_t ev[4];
+        orc_evaluate_mle((const uint32_t *)imle, log_m + log_k, (const uint32_t *)ipt, ev);
+        free(imle);
+        if (!q_eq(q_load(ev), fa)) ok = 0;
+    }
+    /* weight commitment must be the commitment of the given weights */
+    if (in_u64(&in) != 1) ok = 0;
+    fe commitment;
+    in_felt(&in, &commitment);
+    if (ok) {
+        q31 *bmle = mle_col_major(weight, k, n, 1);
+        fe expect;
+        merkle_root(bmle, pn * pk, &expect, 1);
+        free(bmle);
+        if (memcmp(expect.v, commitment.v, 32)) ok = 0;
+    }
+    if (in_u64(&in) != 1 || in_u64(&in) != log_n + log_k) ok = 0;
+    q31 wpt[64];
+    for (unsigned i = 0; i < log_n + log_k && ok; i++) {
+        wpt[i] = in_qm31(&in);
+        q31 expect = i < log_n ? r_out[log_m + i] : chal[i - log_n];
+        if (!q_eq(wpt[i], expect)) ok = 0;
+    }
+    q31 wval = in_qm31(&in);
+    if (!q_eq(wval, fb)) ok = 0;
+    if (ok) {
+        size_t start = in.pos;
+        /* find the opening's extent: verify consumes it */
+        felt_in sub = {calldata + 4 * start, len - start - 1, 0, 0};
+        orc_channel ch2 = ch;
+        q31 fv;
+        ok = verify_opening(&commitment, &sub, wpt, log_n + log_k, &ch2, n_queries, &fv);
+        if (ok) {
+            uint32_t fvv[4];
+            ok = orc_verify_mle_opening(commitment.v, calldata + 4 * start, sub.pos, (const uint32_t *)wpt,
+                                        log_n + log_k, &ch, n_queries, fvv);
+            if (ok && !q_eq(q_load(fvv), fb)) ok = 0;
+        }
+        in.pos = start + sub.pos;
+    }
+    /* io commitment */
+    fe iof;
+    in_felt(&in, &iof);
+    uint64_t io[4];
+    orc_io_commitment(input, m, k, out, m, n, io);
+    if (memcmp(io, iof.v, 32)) ok = 0;
+    if (in.pos != len || in.bad) ok = 0;
+    free(out);
+    if (digest) memcpy(digest, ch.digest, 32);
+    return ok;
+}

@@ -1,0 +1,128 @@
+/*
+ * CPU oracle for the GKR matmul-sumcheck path of stwo-ml (obelyzk engine).
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library restates the reference's CPU prover
+ * (Rust, engine/src/...) in plain C so that the CUDA product can be checked
+ * bit for bit.  It is loaded by tests/, by __graft_entry__.smoke() and by the
+ * cpu_baseline / --impl reference legs of bench.py, and by nothing else: the
+ * product library never links or calls it.
+ *
+ * Parity pin: the oracle reproduces engine/tests/artifacts/sp3_matmul_only_proof.json
+ * (calldata, weight commitment, weight opening calldata, io_commitment and the
+ * final channel digest) and the Poseidon known answers of
+ * engine/src/crypto/poseidon_channel.rs:1619-1637 and
+ * stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs:230-253.
+ *
+ * Representations:
+ *   felt252 : 4 x uint64_t little-endian limbs of the canonical integer (< p_stark)
+ *   QM31    : 4 x uint32_t [a, b, c, d] = (a + b i) + (c + d i) u, i^2 = -1, u^2 = 2 + i
+ *   M31     : uint32_t in [0, 2^31 - 1)
+ */
+#ifndef ZKML_ORACLE_H
+#define ZKML_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    uint64_t digest[4];
+    uint32_t n_draws;
+    uint32_t reserved;
+    uint64_t hash_count;
+} orc_channel;
+
+/* felt252 / Poseidon (starknet-crypto 0.6.2 semantics) */
+void orc_felt_mul(const uint64_t a[4], const uint64_t b[4], uint64_t out[4]);
+void orc_hades(uint64_t state[12]);
+void orc_poseidon_hash(const uint64_t a[4], const uint64_t b[4], uint64_t out[4]);
+void orc_poseidon_hash_many(const uint64_t *in, size_t n, uint64_t out[4]);
+
+/* PoseidonChannel (engine/src/crypto/poseidon_channel.rs:83-306) */
+void orc_ch_init(orc_channel *ch);
+void orc_ch_mix_u64(orc_channel *ch, uint64_t v);
+void orc_ch_mix_felt(orc_channel *ch, const uint64_t v[4]);
+void orc_ch_draw_felt(orc_channel *ch, uint64_t out[4]);
+void orc_ch_draw_qm31(orc_channel *ch, uint32_t out[4]);
+void orc_ch_mix_poly_coeffs(orc_channel *ch, const uint32_t c[12]);
+void orc_ch_mix_poly_coeffs_deg3(orc_channel *ch, const uint32_t c[16]);
+void orc_ch_mix_felts(orc_channel *ch, const uint32_t *qm31s, size_t n);
+void orc_securefield_to_felt(const uint32_t v[4], uint64_t out[4]);
+
+/* QM31 helpers exposed for tests */
+void orc_qm31_mul(const uint32_t a[4], const uint32_t b[4], uint32_t out[4]);
+void orc_qm31_inv(const uint32_t a[4], uint32_t out[4]);
+
+/* MLE helpers (engine/src/components/matmul.rs:118-356) */
+void orc_lagrange_basis(const uint32_t *challenges, size_t v, uint32_t *out /* 2^v QM31 */);
+void orc_evaluate_mle(const uint32_t *evals, size_t n_vars, const uint32_t *point, uint32_t out[4]);
+void orc_restrict_mle(const uint32_t *evals, size_t n_evals, const uint32_t *assign, size_t n_assign,
+                      uint32_t *out /* n_evals >> n_assign */);
+
+/* ZkmlOps::reduce_matmul_layer for SimdBackend (engine/src/backend.rs:110-197).
+ * mode 0 = materialised pad + MLE + restrict_mle, exactly as backend.rs:127-134;
+ * mode 1 = fused unpadded restriction (components/matmul.rs:470-566).
+ * Both give identical results. Returns 0 on success. */
+int orc_reduce_matmul_layer(const uint32_t *a, size_t a_rows, size_t a_cols,
+                            const uint32_t *b, size_t b_rows, size_t b_cols,
+                            const uint32_t *r_i, size_t n_ri, const uint32_t *r_j, size_t n_rj,
+                            size_t pk, orc_channel *ch,
+                            uint32_t *out_round_polys /* 12 per round */,
+                            uint32_t *out_challenges /* 4 per round */,
+                            uint32_t out_final_a[4], uint32_t out_final_b[4],
+                            int mode, int threads);
+
+/* reduce_matmul_layer_with_backend (engine/src/gkr/prover.rs:5959-6073): the transcript
+ * wrapper.  claim_point has log2(pm)+log2(pn) QM31.  next_point receives
+ * log2(pm)+log2(pk) QM31; next_value = final_a. */
+int orc_reduce_matmul_gkr(const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                          const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
+                          orc_channel *ch, uint32_t *out_round_polys, uint32_t out_final_a[4],
+                          uint32_t out_final_b[4], uint32_t *next_point, int mode, int threads);
+
+/* Poseidon Merkle (engine/src/crypto/poseidon_merkle.rs:91-280): root of the tree
+ * whose leaves are securefield_to_felt(evals[i]), zero-padded to a power of two (min 2). */
+void orc_merkle_root_qm31(const uint32_t *evals, size_t n, uint64_t out[4], int threads);
+/* Auth path of leaf `index` (bottom-up siblings, log2(padded n) felts). */
+void orc_merkle_path_qm31(const uint32_t *evals, size_t n, size_t index, uint64_t *out_siblings,
+                          int threads);
+int orc_merkle_verify(const uint64_t root[4], size_t index, const uint64_t leaf[4],
+                      const uint64_t *siblings, size_t n_siblings);
+
+/* MLE opening (engine/src/crypto/mle_opening.rs:1654-1916), serialized as
+ * cairo_serde::serialize_mle_opening_proof (cairo_serde.rs:341-370). */
+int orc_prove_mle_opening(const uint32_t *evals, size_t n_vars, const uint32_t *point,
+                          orc_channel *ch, size_t n_queries, uint64_t commitment[4],
+                          uint64_t *calldata, size_t cap, size_t *out_len, int threads);
+int orc_verify_mle_opening(const uint64_t commitment[4], const uint64_t *calldata, size_t len,
+                           const uint32_t *point, size_t n_vars, orc_channel *ch,
+                           size_t n_queries, uint32_t out_final[4]);
+
+/* Single-MatMul GKR proof: prove_gkr_with_cache (gkr/prover.rs:1500-2251) for the
+ * circuit GraphBuilder::new((m,k)).linear(n) in Sequential weight-binding mode,
+ * serialized with cairo_serde::serialize_gkr_model_proof (cairo_serde.rs:1307-1772).
+ * policy may be NULL (no policy mix).  Writes calldata felts, the final channel
+ * digest and the io commitment. */
+int orc_prove_gkr_matmul(const uint32_t *input, size_t m, size_t k, const uint32_t *weight,
+                         size_t n, const uint64_t *policy, size_t n_queries, uint64_t *calldata,
+                         size_t cap, size_t *out_len, uint64_t digest[4], uint64_t io[4],
+                         int threads);
+/* Verifier replay of a proof produced by orc_prove_gkr_matmul
+ * (gkr/verifier.rs:2675-2788 + mle_opening.rs:1918-2029).  Returns 1 if accepted. */
+int orc_verify_gkr_matmul(const uint32_t *input, size_t m, size_t k, const uint32_t *weight,
+                          size_t n, const uint64_t *policy, size_t n_queries,
+                          const uint64_t *calldata, size_t len, uint64_t digest[4]);
+
+void orc_io_commitment(const uint32_t *input, size_t in_rows, size_t in_cols,
+                       const uint32_t *output, size_t out_rows, size_t out_cols, uint64_t out[4]);
+
+/* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
+void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
+                    uint32_t *c, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

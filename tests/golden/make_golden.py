@@ -1,0 +1,61 @@
+"""Extract the golden vectors the parity tests pin against.
+
+Reads the reference checkout (available only where it is mounted) and writes
+``reference_vectors.json`` next to this script.  The vectors are the
+reference's own known answers for the matmul-sumcheck path:
+
+* ``sp3_matmul_only``: engine/tests/artifacts/sp3_matmul_only_proof.json,
+  produced by engine/tests/e2e_cairo_verify.rs:1093-1180 (1x4 input [1,2,3,4],
+  weight W[i][j] = 2i+j+1, 4x2) -- full GKR calldata, weight commitment,
+  weight claims, weight-opening calldata, io commitment, final channel digest.
+* ``poseidon_kats``: engine/src/crypto/poseidon_channel.rs:1619-1637
+  (poseidon_hash_many([0, pack(QM31(1,2,3,4))])) and
+  stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs:230-241
+  (Poseidon252Channel::mix_u64(0x1111222233334444) from the zero digest,
+  i.e. poseidon_hash(0, 0x1111222233334444)).
+
+Usage: python tests/golden/make_golden.py [reference root]
+"""
+import json
+import sys
+from pathlib import Path
+
+ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+art = json.loads((ref / "engine/tests/artifacts/sp3_matmul_only_proof.json").read_text())
+out = {
+    "sp3_matmul_only": {
+        "source": "engine/tests/artifacts/sp3_matmul_only_proof.json",
+        "input": art["input_data"],
+        "input_shape": art["model"]["input_shape"],
+        "weight": [[2 * i + j + 1 for j in range(2)] for i in range(4)],
+        "output": art["output_data"],
+        "calldata_hex": art["calldata_hex"],
+        "weight_commitments": art["weight_commitments"],
+        "weight_claims": art["weight_claims"],
+        "weight_opening_calldata_hex": art["weight_opening_calldata_hex"],
+        "io_commitment": art["io_commitment"],
+        "final_channel_digest": art["verification"]["final_channel_digest"],
+    },
+    "poseidon_kats": [
+        {
+            "op": "poseidon_hash_many",
+            "inputs": ["0x0", "0x10000000200000008000000180000004"],
+            "expect": "0x0e029e34eb10ff7719b4a23d283495d23f65760b9d9a9b7885f0350879a7f1c",
+            "source": "engine/src/crypto/poseidon_channel.rs:1619-1637",
+        },
+        {
+            "op": "poseidon_hash",
+            "inputs": ["0x0", "0x1111222233334444"],
+            "expect": "0x07cecc0ee3d858c843fe63165f038353f9f80f52dd8d32eead9f635e2f7d8b8e",
+            "source": "stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs:230-241",
+        },
+    ],
+}
+# Sanity: the KAT strings above are the ones in the reference sources.
+src1 = (ref / "engine/src/crypto/poseidon_channel.rs").read_text()
+src2 = (ref / "stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs").read_text()
+assert out["poseidon_kats"][0]["expect"] in src1
+assert out["poseidon_kats"][1]["expect"] in src2
+dst = Path(__file__).with_name("reference_vectors.json")
+dst.write_text(json.dumps(out, indent=1) + "\n")
+print("wrote", dst)

@@ -1,0 +1,173 @@
+"""ctypes binding of the CPU oracle (oracle/_build/liboracle.so).
+
+Test infrastructure: imported only by tests/, __graft_entry__.smoke() and
+bench.py's CPU legs, as the checker -- never by the product package.
+"""
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+LIB_PATH = ROOT / "oracle" / "_build" / "liboracle.so"
+
+u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
+
+
+class Channel(C.Structure):
+    _fields_ = [("digest", C.c_uint64 * 4), ("n_draws", C.c_uint32), ("reserved", C.c_uint32),
+                ("hash_count", C.c_uint64)]
+
+    def digest_int(self) -> int:
+        return sum(int(self.digest[i]) << (64 * i) for i in range(4))
+
+
+def build() -> None:
+    src = ROOT / "oracle" / "oracle.c"
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            build()
+        L = C.CDLL(str(LIB_PATH))
+        chp = C.POINTER(Channel)
+        sz = C.c_size_t
+        L.orc_hades.argtypes = [u64p]
+        L.orc_poseidon_hash.argtypes = [u64p, u64p, u64p]
+        L.orc_poseidon_hash_many.argtypes = [u64p, sz, u64p]
+        L.orc_felt_mul.argtypes = [u64p, u64p, u64p]
+        L.orc_ch_init.argtypes = [chp]
+        L.orc_ch_mix_u64.argtypes = [chp, C.c_uint64]
+        L.orc_ch_mix_felt.argtypes = [chp, u64p]
+        L.orc_ch_draw_felt.argtypes = [chp, u64p]
+        L.orc_ch_draw_qm31.argtypes = [chp, u32p]
+        L.orc_ch_mix_poly_coeffs.argtypes = [chp, u32p]
+        L.orc_ch_mix_poly_coeffs_deg3.argtypes = [chp, u32p]
+        L.orc_ch_mix_felts.argtypes = [chp, u32p, sz]
+        L.orc_securefield_to_felt.argtypes = [u32p, u64p]
+        L.orc_qm31_mul.argtypes = [u32p, u32p, u32p]
+        L.orc_qm31_inv.argtypes = [u32p, u32p]
+        L.orc_lagrange_basis.argtypes = [u32p, sz, u32p]
+        L.orc_evaluate_mle.argtypes = [u32p, sz, u32p, u32p]
+        L.orc_restrict_mle.argtypes = [u32p, sz, u32p, sz, u32p]
+        L.orc_reduce_matmul_layer.argtypes = [u32p, sz, sz, u32p, sz, sz, u32p, sz, u32p, sz, sz, chp,
+                                              u32p, u32p, u32p, u32p, C.c_int, C.c_int]
+        L.orc_reduce_matmul_gkr.argtypes = [u32p, sz, u32p, u32p, sz, sz, u32p, sz, chp, u32p, u32p,
+                                            u32p, u32p, C.c_int, C.c_int]
+        L.orc_merkle_root_qm31.argtypes = [u32p, sz, u64p, C.c_int]
+        L.orc_merkle_path_qm31.argtypes = [u32p, sz, sz, u64p, C.c_int]
+        L.orc_merkle_verify.argtypes = [u64p, sz, u64p, u64p, sz]
+        L.orc_prove_mle_opening.argtypes = [u32p, sz, u32p, chp, sz, u64p, u64p, sz, C.POINTER(sz),
+                                            C.c_int]
+        L.orc_verify_mle_opening.argtypes = [u64p, u64p, sz, u32p, sz, chp, sz, u32p]
+        L.orc_prove_gkr_matmul.argtypes = [u32p, sz, sz, u32p, sz, C.c_void_p, sz, u64p, sz,
+                                           C.POINTER(sz), u64p, u64p, C.c_int]
+        L.orc_verify_gkr_matmul.argtypes = [u32p, sz, sz, u32p, sz, C.c_void_p, sz, u64p, sz, u64p]
+        L.orc_io_commitment.argtypes = [u32p, sz, sz, u32p, sz, sz, u64p]
+        L.orc_matmul_m31.argtypes = [u32p, sz, sz, u32p, sz, u32p, C.c_int]
+        _lib = L
+    return _lib
+
+
+def threads() -> int:
+    return int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1))
+
+
+def felt(x: int) -> np.ndarray:
+    return np.array([(x >> (64 * i)) & (2**64 - 1) for i in range(4)], dtype=np.uint64)
+
+
+def felt_int(a) -> int:
+    return sum(int(a[i]) << (64 * i) for i in range(4))
+
+
+def new_channel() -> Channel:
+    ch = Channel()
+    lib().orc_ch_init(C.byref(ch))
+    return ch
+
+
+def poseidon_hash(a: int, b: int) -> int:
+    out = np.zeros(4, np.uint64)
+    lib().orc_poseidon_hash(felt(a), felt(b), out)
+    return felt_int(out)
+
+
+def poseidon_hash_many(xs) -> int:
+    arr = np.concatenate([felt(x) for x in xs]) if xs else np.zeros(4, np.uint64)
+    out = np.zeros(4, np.uint64)
+    lib().orc_poseidon_hash_many(arr, len(xs), out)
+    return felt_int(out)
+
+
+def reduce_matmul_layer(a, b, r_i, r_j, ch, mode=1, nthreads=None):
+    """a: (m,k) uint32, b: (k,n) uint32, r_i/r_j: (v,4) uint32. Returns dict."""
+    a = np.ascontiguousarray(a, np.uint32)
+    b = np.ascontiguousarray(b, np.uint32)
+    m, k = a.shape
+    _, n = b.shape
+    pk = 1 << max(0, (k - 1).bit_length())
+    log_k = pk.bit_length() - 1
+    r_i = np.ascontiguousarray(r_i, np.uint32).reshape(-1, 4)
+    r_j = np.ascontiguousarray(r_j, np.uint32).reshape(-1, 4)
+    rp = np.zeros((max(log_k, 1), 12), np.uint32)
+    chal = np.zeros((max(log_k, 1), 4), np.uint32)
+    fa = np.zeros(4, np.uint32)
+    fb = np.zeros(4, np.uint32)
+    rc = lib().orc_reduce_matmul_layer(a.reshape(-1), m, k, b.reshape(-1), k, n,
+                                       r_i.reshape(-1) if r_i.size else np.zeros(4, np.uint32),
+                                       len(r_i), r_j.reshape(-1) if r_j.size else np.zeros(4, np.uint32),
+                                       len(r_j), pk, C.byref(ch), rp.reshape(-1), chal.reshape(-1), fa, fb,
+                                       mode, nthreads or threads())
+    assert rc == 0, rc
+    return {"round_polys": rp[:log_k], "challenges": chal[:log_k], "final_a": fa, "final_b": fb}
+
+
+def merkle_root_qm31(evals, nthreads=None) -> int:
+    e = np.ascontiguousarray(evals, np.uint32).reshape(-1)
+    out = np.zeros(4, np.uint64)
+    lib().orc_merkle_root_qm31(e, e.size // 4, out, nthreads or threads())
+    return felt_int(out)
+
+
+def prove_gkr_matmul(inp, w, policy=None, n_queries=10, cap=1 << 16):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    w = np.ascontiguousarray(w, np.uint32)
+    m, k = inp.shape
+    _, n = w.shape
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    dig = np.zeros(4, np.uint64)
+    io = np.zeros(4, np.uint64)
+    pol = None if policy is None else felt(policy).ctypes.data_as(C.c_void_p)
+    pol_arr = None if policy is None else felt(policy)
+    if pol_arr is not None:
+        pol = pol_arr.ctypes.data_as(C.c_void_p)
+    rc = lib().orc_prove_gkr_matmul(inp.reshape(-1), m, k, w.reshape(-1), n, pol, n_queries, buf, cap,
+                                    C.byref(ln), dig, io, threads())
+    assert rc == 0, rc
+    cd = [felt_int(buf[4 * i:4 * i + 4]) for i in range(ln.value)]
+    return {"calldata": cd, "digest": felt_int(dig), "io": felt_int(io), "raw": buf[:4 * ln.value].copy()}
+
+
+def verify_gkr_matmul(inp, w, raw, policy=None, n_queries=10):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    w = np.ascontiguousarray(w, np.uint32)
+    m, k = inp.shape
+    _, n = w.shape
+    dig = np.zeros(4, np.uint64)
+    pol_arr = None if policy is None else felt(policy)
+    pol = None if pol_arr is None else pol_arr.ctypes.data_as(C.c_void_p)
+    ok = lib().orc_verify_gkr_matmul(inp.reshape(-1), m, k, w.reshape(-1), n, pol, n_queries,
+                                     np.ascontiguousarray(raw, np.uint64), raw.size // 4, dig)
+    return bool(ok), felt_int(dig)

@@ -1,0 +1,309 @@
+"""Benchmark: GKR matmul-sumcheck prove time per layer on B200.
+
+Workload: A = 64 x 5120 activations, B = 5120 x 13824
+weights (Qwen2.5-14B MLP up-projection), int8 values embedded in M31, MLEs
+padded to 64 x 8192 and 8192 x 16384.  One step = one
+``reduce_matmul_layer_with_backend`` (gkr/prover.rs:5959-6073): transcript
+seeding, the W.eq(r) restrictions, 13 sumcheck rounds with the Poseidon
+channel on the host, and the final evaluation mixes.
+
+Multi-GPU: one process per GPU (torchrun), each rank proves its own
+independent layer (different seeded weights), no data-path collective; the
+timed region is bracketed by barriers and the max over ranks is reported
+("scaling": "weak").  The reference arm (--impl reference) times the CPU
+restatement of the reference prover (the oracle, materialised restriction as
+in engine/src/backend.rs:110-197) on the host cores, rank 0 only.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "stwo-ml_b200"))
+sys.path.insert(0, str(ROOT / "tests"))
+
+M, K, N = 64, 5120, 13824
+METRIC = "matmul-sumcheck prove s/layer (config 2: 64x5120 . 5120x13824 M31, padded 64x8192 . 8192x16384)"
+WORKLOAD = "C2 batched matmul sumcheck, Qwen2.5-14B MLP up-proj at 64 tokens"
+
+
+def log2(x):
+    return x.bit_length() - 1
+
+
+def npow2(x):
+    return 1 << max(0, (x - 1).bit_length())
+
+
+PM, PK, PN = npow2(M), npow2(K), npow2(N)
+# MLE elements folded per layer: every element of the padded A and B MLEs is
+# folded by the restriction, plus both length-pk vectors through the rounds.
+ELEMS_FOLDED = PM * PK + PN * PK + 2 * (2 * PK - 2)
+
+
+def make_inputs(rank):
+    from helpers import int_matrix_m31
+
+    a = int_matrix_m31(M, K, 1000 + 2 * rank)
+    b = int_matrix_m31(K, N, 1001 + 2 * rank)
+    return a, b
+
+
+def seeded_channel_state(Z, rank):
+    ch = Z.PoseidonChannel()
+    seed = int.from_bytes(bytes(range(32)), "big") % Z.STARK_P
+    ch.mix_felt(seed)
+    ch.mix_u64(rank)
+    point = ch.draw_qm31s(log2(PM) + log2(PN))
+    return ch, point
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def measured_peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic_per_launch():
+    """dram bytes per restrict_cols launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "restrict_cols_c2.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            return float(line.split(":")[1].split()[0])
+    return None
+
+
+def cpu_reference_layer(threads):
+    """One C2 layer through the oracle's materialised (reference) CPU path."""
+    import oracle_lib as O
+
+    a, b = make_inputs(0)
+    rng = np.random.default_rng(0)
+    r_i = rng.integers(0, (1 << 31) - 1, (log2(PM), 4), dtype=np.uint32)
+    r_j = rng.integers(0, (1 << 31) - 1, (log2(PN), 4), dtype=np.uint32)
+    ch = O.new_channel()
+    t0 = time.perf_counter()
+    O.reduce_matmul_layer(a, b, r_i, r_j, ch, mode=0, nthreads=threads)
+    return time.perf_counter() - t0
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_reference_layer(threads)
+    times = [cpu_reference_layer(threads) for _ in range(args.steps)]
+    s_per_layer = float(np.mean(times))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": s_per_layer, "unit": "s/layer", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": s_per_layer * 1e3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u32 (M31/QM31 integer)", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "l2": "inputs larger than L2 (B = 283 MB)"},
+        "cpu_baseline": {"value": s_per_layer, "unit": "s/layer", "cores": threads, "kind": "port",
+                         "sample": "one full C2 layer per step through the C restatement of the reference CPU "
+                                   "prover (materialised pad + MLE + restrict_mle, backend.rs:110-197)"},
+        "e2e": {"value": s_per_layer, "unit": "s/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "mle_elems_folded_per_s_per_gpu": ELEMS_FOLDED / s_per_layer,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    import zkml_b200 as Z
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.cuda.current_device()
+    stream = torch.cuda.current_stream()
+    ctx = Z.Context(dev)
+    ctx.set_stream(stream.cuda_stream)
+    backend = Z.GpuBackend.__new__(Z.GpuBackend)
+    backend.ctx = ctx
+
+    a, b = make_inputs(rank)
+    ta = torch.from_numpy(a.view(np.int32)).cuda()
+    tb = torch.from_numpy(b.view(np.int32)).cuda()
+    # pinned host copies for the end-to-end leg
+    ha = torch.from_numpy(a.view(np.int32)).pin_memory()
+    hb = torch.from_numpy(b.view(np.int32)).pin_memory()
+    A_dev, B_dev = Z.M31Matrix(M, K, ta), Z.M31Matrix(K, N, tb)
+    A_host, B_host = Z.M31Matrix(M, K, ha), Z.M31Matrix(K, N, hb)
+    ch0, point = seeded_channel_state(Z, rank)
+    # true claim: p(0) + p(1) of round 0 = sum_k f_a f_b (evaluated once, untimed)
+    probe = backend.reduce_matmul_layer(A_dev, B_dev, point[:log2(PM)], point[log2(PM):], PK, ch0.clone())
+    rp = probe.round_polys[0]
+    P = Z.M31_P
+    claim = ((2 * rp.c0.astype(np.int64) + rp.c1 + rp.c2) % P).astype(np.uint32)
+
+    def step(Amat, Bmat):
+        ch = ch0.clone()
+        return Z.reduce_matmul_layer_with_backend(Z.GKRClaim(point, claim), Amat, Bmat, M, K, N, ch, backend)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    def timed(Amat, Bmat, profile):
+        for _ in range(args.warmup):
+            step(Amat, Bmat)
+        if profile:
+            ctx.enable_timing(True)
+        barrier()
+        l0 = ctx.kernel_launches()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev) as clk:
+            e0.record(stream)
+            for _ in range(args.steps):
+                step(Amat, Bmat)
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        launches = ctx.kernel_launches() - l0
+        kt = ctx.kernel_time("restrict_cols") if profile else (0.0, 0)
+        if profile:
+            ctx.enable_timing(False)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            lt = torch.tensor([launches], device="cuda", dtype=torch.int64)
+            dist.all_reduce(lt)
+            launches = int(lt.item())
+        barrier()
+        return ms, launches, kt, clk.summary()
+
+    ms, launches, (rc_ms, rc_n), clocks = timed(A_dev, B_dev, profile=True)
+    ms_e2e, _, _, _ = timed(A_host, B_host, profile=False)
+
+    # CPU baseline: rank 0 at N=1 only, one full layer through the oracle
+    cpu = None
+    if world == 1:
+        threads = os.cpu_count() or 1
+        t = cpu_reference_layer(threads)
+        cpu = {"value": t, "unit": "s/layer", "cores": threads, "kind": "port",
+               "sample": "one full C2 layer through the C restatement of the reference CPU prover "
+                         "(materialised restriction, backend.rs:110-197), all host threads"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = measured_peak_hbm()
+    rc_bytes = 4.0 * K * N + 32.0 * K  # B read once + per-row accumulators
+    rc_avg_ms = rc_ms / max(rc_n, 1)
+    achieved = rc_bytes / (rc_avg_ms * 1e-3) / 1e9
+    traffic = ncu_traffic_per_launch()
+    s_per_layer = ms / 1e3 / world
+    rounds = log2(PK)
+    line = {
+        "metric": METRIC, "value": s_per_layer, "unit": "s/layer", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u32 (M31/QM31 integer)",
+        "data": "synthetic (SplitMix64-seeded int8 embedded in M31)",
+        "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "padded": [PM, PK, PN],
+                   "layers_per_step": world, "parallelism": f"independent layer per GPU x{world}",
+                   "l2": "inputs larger than L2 (B = 283 MB > 126 MB L2)"},
+        "e2e": {"value": ms_e2e / 1e3 / world, "unit": "s/layer",
+                "h2d_bytes_per_step": 4 * (M * K + K * N),
+                "d2h_bytes_per_step": rounds * 52 + 36},
+        "gpu_launches": launches,
+        "mle_elems_folded_per_s_per_gpu": ELEMS_FOLDED / (ms / 1e3),
+        "roofline": {"bound": "hbm", "kernel": "restrict_cols", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "algorithmic_bytes": rc_bytes, "avg_launch_ms": rc_avg_ms},
+        "clocks": clocks,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,144 @@
+/*
+ * zkml_b200.h -- C ABI of the B200-native GKR matmul-sumcheck prover.
+ *
+ * This is the drop-in boundary for the stwo-ml engine's `ZkmlOps` backend trait
+ * (engine/src/backend.rs:85-107) and the GKR layer-prover entry points that sit
+ * on it.  Plain pointers and sizes only: no CUDA or torch types cross it.
+ *
+ * Conventions
+ *   M31     uint32_t, canonical value in [0, 2^31 - 1); values >= 2^31 are
+ *           rejected with ZKML_ERR_INVALID_ARG (detected on the GPU).
+ *   QM31    4 x uint32_t [a, b, c, d] = (a + b i) + (c + d i) u  (i^2 = -1,
+ *           u^2 = 2 + i), the SecureField AoS layout of
+ *           engine/src/gpu_sumcheck.rs:3614-3630.
+ *   felt252 4 x uint64_t little-endian limbs of the canonical integer < p_stark.
+ *   Matrices are row-major and unpadded, like M31Matrix
+ *           (engine/src/components/matmul.rs:85-116); padding to powers of two
+ *           is logical.
+ *   Matrix/MLE input pointers may be host memory (pageable or pinned; copied to
+ *   the device inside the call) or device memory of the context's GPU (used in
+ *   place, never modified).  All outputs are host pointers.
+ *   Every function returns 0 (ZKML_OK) or a zkml_status; zkml_last_error()
+ *   gives the message for the calling thread.  There is no CPU fallback: a
+ *   missing or failing GPU is an error.
+ *   A context drives one GPU from one host thread at a time.
+ */
+#ifndef ZKML_B200_H
+#define ZKML_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZKML_ABI_VERSION 1
+
+typedef enum {
+    ZKML_OK = 0,
+    ZKML_ERR_INVALID_ARG = 1,
+    ZKML_ERR_OOM = 2,
+    ZKML_ERR_CUDA = 3,
+    ZKML_ERR_NCCL = 4,
+    ZKML_ERR_TIMEOUT = 5,
+    ZKML_ERR_UNSUPPORTED = 6,
+    ZKML_ERR_VERIFY = 7
+} zkml_status;
+
+/* Lossless PoseidonChannel state (engine/src/crypto/poseidon_channel.rs:83-88).
+ * Unlike the reference's to_gpu_state/from_gpu_state pair
+ * (poseidon_channel.rs:109-138) it keeps n_draws. */
+typedef struct zkml_channel {
+    uint64_t digest[4];
+    uint32_t n_draws;
+    uint32_t reserved;
+    uint64_t hash_count;
+} zkml_channel;
+
+typedef struct zkml_ctx zkml_ctx;
+
+int zkml_abi_version(void);
+const char *zkml_last_error(void);
+
+/* GpuSumcheckExecutor::cached (engine/src/gpu_sumcheck.rs:1365-1385): one
+ * context per device, owning its stream and reusable device scratch. */
+int zkml_ctx_create(int device, zkml_ctx **out);
+int zkml_ctx_destroy(zkml_ctx *ctx);
+int zkml_ctx_device(const zkml_ctx *ctx);
+/* Kernel launches of this context so far (instrumentation for benchmarks). */
+uint64_t zkml_ctx_kernel_launches(const zkml_ctx *ctx);
+/* Per-kernel device timing with CUDA events (off by default).  When enabled,
+ * each launch of the named kernel class is bracketed by events on the
+ * context's stream; zkml_ctx_kernel_time returns the accumulated milliseconds
+ * and launch count.  Kernel classes: "restrict_cols", "restrict_rows",
+ * "sumcheck_round", "merkle". */
+int zkml_ctx_enable_timing(zkml_ctx *ctx, int enable);
+int zkml_ctx_kernel_time(zkml_ctx *ctx, const char *kernel, double *out_ms, uint64_t *out_launches);
+/* Replace the context's stream with a caller-owned cudaStream_t (NULL = own stream). */
+int zkml_ctx_set_stream(zkml_ctx *ctx, void *cuda_stream);
+
+/* ---- Poseidon / Fiat-Shamir channel (host; poseidon_channel.rs:83-306) ----- */
+void zkml_channel_init(zkml_channel *ch);                                       /* PoseidonChannel::new */
+void zkml_channel_mix_u64(zkml_channel *ch, uint64_t v);                        /* mix_u64 */
+void zkml_channel_mix_felt(zkml_channel *ch, const uint64_t v[4]);              /* mix_felt */
+void zkml_channel_mix_qm31(zkml_channel *ch, const uint32_t v[4]);              /* gkr::prover mix_secure_field */
+void zkml_channel_draw_felt252(zkml_channel *ch, uint64_t out[4]);              /* draw_felt252 */
+void zkml_channel_draw_qm31(zkml_channel *ch, uint32_t out[4]);                 /* draw_qm31 */
+void zkml_channel_mix_poly_coeffs(zkml_channel *ch, const uint32_t c[12]);      /* mix_poly_coeffs */
+void zkml_channel_mix_poly_coeffs_deg3(zkml_channel *ch, const uint32_t c[16]); /* mix_poly_coeffs_deg3 */
+void zkml_channel_mix_felts(zkml_channel *ch, const uint32_t *qm31s, size_t n); /* mix_felts */
+/* starknet_crypto::{poseidon_permute_comp, poseidon_hash, poseidon_hash_many}
+ * (engine/src/crypto/hades.rs:21-23). */
+void zkml_hades_permutation(uint64_t state[12]);
+void zkml_poseidon_hash(const uint64_t a[4], const uint64_t b[4], uint64_t out[4]);
+void zkml_poseidon_hash_many(const uint64_t *in, size_t n, uint64_t out[4]);
+/* securefield_to_felt (poseidon_channel.rs:60-69) */
+void zkml_securefield_to_felt(const uint32_t v[4], uint64_t out[4]);
+
+/* ---- ZkmlOps (engine/src/backend.rs:85-107) -------------------------------- */
+
+/* ZkmlOps::reduce_matmul_layer (backend.rs:87-94; CPU impl 110-197, reference
+ * GPU impl gpu_sumcheck.rs:2692-2873).  Restricts A's rows by r_i and B's
+ * columns by r_j (A: a_rows x a_cols, B: b_rows x b_cols, a_cols == b_rows),
+ * then runs log2(pk) degree-2 sumcheck rounds, advancing `ch` on the host.
+ * n_ri == log2(next_pow2(a_rows)), n_rj == log2(next_pow2(b_cols)),
+ * pk == next_pow2(a_cols).
+ * Outputs: out_round_polys  log2(pk) x 3 QM31 (c0, c1, c2 per round)
+ *          out_challenges   log2(pk) QM31
+ *          out_final_a/b    the folded A and B values (MatMulReduction). */
+int zkml_reduce_matmul_layer(zkml_ctx *ctx, const uint32_t *a, size_t a_rows, size_t a_cols,
+                             const uint32_t *b, size_t b_rows, size_t b_cols,
+                             const uint32_t *r_i, size_t n_ri, const uint32_t *r_j, size_t n_rj,
+                             size_t pk, zkml_channel *ch, uint32_t *out_round_polys,
+                             uint32_t *out_challenges, uint32_t out_final_a[4],
+                             uint32_t out_final_b[4]);
+
+/* ZkmlOps::evaluate_mle_at_point (backend.rs:97-100): MLE of 2^n_vars QM31. */
+int zkml_evaluate_mle(zkml_ctx *ctx, const uint32_t *mle, size_t n_vars, const uint32_t *point,
+                      uint32_t out[4]);
+
+/* ZkmlOps::restrict_mle (backend.rs:103-106): fix the first n_assign variables
+ * (most significant index bits) of an MLE of n_evals = 2^k QM31;
+ * out receives n_evals >> n_assign QM31. */
+int zkml_restrict_mle(zkml_ctx *ctx, const uint32_t *mle, size_t n_evals, const uint32_t *assign,
+                      size_t n_assign, uint32_t *out);
+
+/* ---- GKR layer prover entry points (engine/src/gkr/prover.rs) --------------- */
+
+/* reduce_matmul_layer_with_backend (gkr/prover.rs:5959-6073): mixes the
+ * unpadded (m, k, n) and the claimed value, runs zkml_reduce_matmul_layer with
+ * r_i = claim_point[..log m], r_j = claim_point[log m..], then mixes
+ * final_a and final_b.  out_next_point receives log2(pm) + log2(pk) QM31
+ * (r_i || challenges); the next claim's value is final_a. */
+int zkml_reduce_matmul_layer_gkr(zkml_ctx *ctx, const uint32_t *claim_point, size_t n_point,
+                                 const uint32_t claim_value[4], const uint32_t *a, size_t m,
+                                 size_t k, const uint32_t *b, size_t n, zkml_channel *ch,
+                                 uint32_t *out_round_polys, uint32_t out_final_a[4],
+                                 uint32_t out_final_b[4], uint32_t *out_next_point);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZKML_B200_H */

@@ -1,0 +1,89 @@
+// Internal definition of zkml_ctx: one GPU, one stream, reusable device scratch.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/zkml_b200.h"
+#include "kernels.cuh"
+
+namespace zk {
+
+// Records a status + message for zkml_last_error() and returns the status.
+int set_error(int status, const std::string& msg);
+int cuda_error(cudaError_t e, const char* what);
+
+#define ZK_CUDA(call)                                              \
+    do {                                                           \
+        cudaError_t _e = (call);                                   \
+        if (_e != cudaSuccess) return ::zk::cuda_error(_e, #call); \
+    } while (0)
+
+// A growable device allocation.
+struct DevBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    int ensure(size_t need);  // returns 0 or a zkml status
+    void release();
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(ptr);
+    }
+};
+
+enum KernelClass { KC_RESTRICT_COLS = 0, KC_RESTRICT_ROWS = 1, KC_ROUND = 2, KC_MERKLE = 3 };
+
+// Brackets one launch of a kernel class with events when timing is enabled.
+struct KTimer {
+    ::zkml_ctx* ctx;
+    int cls;
+    KTimer(::zkml_ctx* c, int k);
+    ~KTimer();
+};
+
+}  // namespace zk
+
+struct zkml_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    cudaStream_t own_stream = nullptr;
+    uint64_t launches = 0;
+    // scratch
+    zk::DevBuf a_in, b_in;          // device copies of host inputs
+    zk::DevBuf fa, fb;              // QM31 sumcheck vectors
+    zk::DevBuf acc_a, acc_b;        // u64 restriction accumulators
+    zk::DevBuf eq_a, eq_hi, eq_lo;  // eq tables
+    zk::DevBuf partials;            // per-block round partials
+    zk::DevBuf small;               // ticket + out words + error flag
+    uint32_t* h_small = nullptr;    // pinned host mirror of `small`
+    int max_round_blocks = 0;
+    // optional per-kernel-class event timing
+    bool timing = false;
+    struct KTime {
+        double ms = 0;
+        uint64_t launches = 0;
+    };
+    KTime ktime[4];  // restrict_cols, restrict_rows, sumcheck_round, merkle
+    // Event pairs recorded but not yet read; read after the next stream sync so
+    // timing never adds a host wait of its own.
+    struct PendingEv {
+        int cls;
+        cudaEvent_t e0, e1;
+    };
+    std::vector<PendingEv> pending;
+    std::vector<cudaEvent_t> ev_pool;
+
+    unsigned int* ticket() const { return small.as<unsigned int>(); }
+    uint32_t* out_words() const { return small.as<uint32_t>() + 16; }  // 32 words
+    uint32_t* err_flag() const { return small.as<uint32_t>() + 48; }
+    zk::RoundScratch round_scratch() const {
+        zk::RoundScratch r;
+        r.partials = partials.as<uint32_t>();
+        r.ticket = ticket();
+        r.out = out_words();
+        r.max_blocks = max_round_blocks;
+        return r;
+    }
+};

@@ -1,0 +1,156 @@
+// Host felt252 arithmetic and the Starknet Poseidon (Hades) permutation.
+//
+// Replaces, on the host side of the prover, the starknet-crypto 0.6.2 /
+// starknet-ff 0.3.7 calls the reference makes (engine/src/crypto/hades.rs:21-23,
+// poseidon_channel.rs:224,251,290, poseidon_merkle.rs:100-110).
+//
+// Representation: 4 x u64 little-endian limbs in Montgomery form, R = 2^256.
+// The Stark prime p = 2^251 + 17 * 2^192 + 1 has limbs [1, 0, 0, 0x0800000000000011],
+// so p = 1 mod 2^64: the Montgomery factor -p^-1 mod 2^64 is all-ones, the
+// per-limb quotient is simply m = -t0, and adding m*p touches only limb 0
+// (which it clears) and limb 3.  The multiply below is specialised to that.
+//
+// Hades uses the "compressed" round-key schedule: in the 83 partial rounds only
+// lane 2 goes through the S-box, so the keys of lanes 0 and 1 are pushed
+// through the MDS into the following round; each partial round then adds a
+// single key.  The schedule (12 + 83 + 12 = 107 keys) is derived at start-up
+// from the 91 x 3 raw keys by compress_round_keys() below.
+#pragma once
+#include <stdint.h>
+#include <string.h>
+
+namespace zk {
+
+typedef unsigned __int128 u128;
+
+struct felt {
+    uint64_t l[4];
+};
+
+constexpr uint64_t FP0 = 1ull, FP3 = 0x0800000000000011ull;
+
+inline bool f_geq_p(const felt& a) {
+    if (a.l[3] != FP3) return a.l[3] > FP3;
+    if (a.l[2] != 0 || a.l[1] != 0) return true;
+    return a.l[0] >= FP0;
+}
+
+inline void f_sub_p(felt& a) {
+    // a -= p
+    u128 d = (u128)a.l[0] - FP0;
+    a.l[0] = (uint64_t)d;
+    uint64_t br = (uint64_t)(d >> 64) & 1;
+    d = (u128)a.l[1] - br;
+    a.l[1] = (uint64_t)d;
+    br = (uint64_t)(d >> 64) & 1;
+    d = (u128)a.l[2] - br;
+    a.l[2] = (uint64_t)d;
+    br = (uint64_t)(d >> 64) & 1;
+    a.l[3] = a.l[3] - FP3 - br;
+}
+
+inline felt f_add(const felt& a, const felt& b) {
+    felt r;
+    u128 s = (u128)a.l[0] + b.l[0];
+    r.l[0] = (uint64_t)s;
+    s = (u128)a.l[1] + b.l[1] + (uint64_t)(s >> 64);
+    r.l[1] = (uint64_t)s;
+    s = (u128)a.l[2] + b.l[2] + (uint64_t)(s >> 64);
+    r.l[2] = (uint64_t)s;
+    r.l[3] = a.l[3] + b.l[3] + (uint64_t)(s >> 64);  // < 2^253, no overflow
+    if (f_geq_p(r)) f_sub_p(r);
+    return r;
+}
+
+inline felt f_sub(const felt& a, const felt& b) {
+    felt r;
+    u128 d = (u128)a.l[0] - b.l[0];
+    r.l[0] = (uint64_t)d;
+    uint64_t br = (uint64_t)(d >> 64) & 1;
+    d = (u128)a.l[1] - b.l[1] - br;
+    r.l[1] = (uint64_t)d;
+    br = (uint64_t)(d >> 64) & 1;
+    d = (u128)a.l[2] - b.l[2] - br;
+    r.l[2] = (uint64_t)d;
+    br = (uint64_t)(d >> 64) & 1;
+    d = (u128)a.l[3] - b.l[3] - br;
+    r.l[3] = (uint64_t)d;
+    br = (uint64_t)(d >> 64) & 1;
+    if (br) {  // add p back
+        u128 s = (u128)r.l[0] + FP0;
+        r.l[0] = (uint64_t)s;
+        s = (u128)r.l[1] + (uint64_t)(s >> 64);
+        r.l[1] = (uint64_t)s;
+        s = (u128)r.l[2] + (uint64_t)(s >> 64);
+        r.l[2] = (uint64_t)s;
+        r.l[3] = r.l[3] + FP3 + (uint64_t)(s >> 64);
+    }
+    return r;
+}
+
+// Montgomery product a * b / 2^256 mod p for a, b < p.
+inline felt f_mul(const felt& a, const felt& b) {
+    uint64_t t0 = 0, t1 = 0, t2 = 0, t3 = 0, t4 = 0;
+    for (int i = 0; i < 4; i++) {
+        const uint64_t bi = b.l[i];
+        u128 s = (u128)a.l[0] * bi + t0;
+        t0 = (uint64_t)s;
+        s = (u128)a.l[1] * bi + t1 + (uint64_t)(s >> 64);
+        t1 = (uint64_t)s;
+        s = (u128)a.l[2] * bi + t2 + (uint64_t)(s >> 64);
+        t2 = (uint64_t)s;
+        s = (u128)a.l[3] * bi + t3 + (uint64_t)(s >> 64);
+        t3 = (uint64_t)s;
+        uint64_t t5;
+        s = (u128)t4 + (uint64_t)(s >> 64);
+        t4 = (uint64_t)s;
+        t5 = (uint64_t)(s >> 64);
+        // m = -t0 mod 2^64; t0 + m * 1 = 0 with a carry iff t0 != 0.
+        const uint64_t m = (uint64_t)0 - t0;
+        s = (u128)t1 + (t0 != 0);
+        t0 = (uint64_t)s;
+        s = (u128)t2 + (uint64_t)(s >> 64);
+        t1 = (uint64_t)s;
+        s = (u128)m * FP3 + t3 + (uint64_t)(s >> 64);
+        t2 = (uint64_t)s;
+        s = (u128)t4 + (uint64_t)(s >> 64);
+        t3 = (uint64_t)s;
+        t4 = t5 + (uint64_t)(s >> 64);
+    }
+    felt r = {{t0, t1, t2, t3}};
+    if (f_geq_p(r)) f_sub_p(r);
+    return r;
+}
+
+// Constants (Montgomery form) set up by felt_init().
+extern felt F_R2;     // 2^512 mod p
+extern felt F_ONE;    // Montgomery 1
+extern felt HADES_RC[107];
+
+void felt_init();  // idempotent, thread-safe
+
+inline felt f_from_u64(uint64_t x) {
+    felt r = {{x, 0, 0, 0}};
+    return f_mul(r, F_R2);
+}
+inline felt f_from_canon(const uint64_t v[4]) {
+    felt r;
+    memcpy(r.l, v, 32);
+    return f_mul(r, F_R2);
+}
+inline void f_to_canon(const felt& a, uint64_t out[4]) {
+    felt one = {{1, 0, 0, 0}};
+    felt r = f_mul(a, one);
+    memcpy(out, r.l, 32);
+}
+inline felt f_cube(const felt& x) { return f_mul(f_mul(x, x), x); }
+
+// Hades permutation on Montgomery-form state.
+void hades(felt s[3]);
+
+// Canonical-integer convenience wrappers.
+void poseidon_hash_canon(const uint64_t a[4], const uint64_t b[4], uint64_t out[4]);
+void poseidon_hash_many_canon(const uint64_t* in, size_t n, uint64_t out[4]);
+felt poseidon_hash_many_m(const felt* in, size_t n);
+
+}  // namespace zk

@@ -1,0 +1,67 @@
+// Declarations of the sm_100a kernels of the matmul-sumcheck path and their
+// host launchers (all launchers are asynchronous on the given stream).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "qm31.cuh"
+
+namespace zk {
+
+constexpr int MAX_EQ_VARS = 40;
+
+struct EqChallenges {  // passed by value as a kernel parameter
+    qm31 c[MAX_EQ_VARS];
+    int v;
+};
+
+// ---- eq / Lagrange tables (components/matmul.rs:342-356) --------------------
+// table[idx] = prod_l ((bit_{v-1-l}(idx)) ? c_l : 1 - c_l), first challenge on the MSB.
+void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaStream_t s);
+
+// ---- restriction W . eq(r) (components/matmul.rs:470-566) --------------------
+// Column restriction of a row-major k x n M31 matrix: acc[i] += sum_j B[i][j] L_j,
+// with L_j = lhi[j >> 6] * llo[j & 63] (llo zero-padded to 64 entries); acc is 4 x u64
+// per row, zeroed by the caller.
+void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
+                          unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s);
+// Row restriction of a row-major m x k M31 matrix: acc[j] += sum_i A[i][j] L_i.
+void launch_restrict_rows(const uint32_t* A, uint32_t m, uint32_t k, const uint4* L,
+                          unsigned long long* acc, uint32_t* err, cudaStream_t s);
+// out[i] = acc[i] mod P for i < n_rows, zero for n_rows <= i < out_len.
+void launch_acc_finalize(const unsigned long long* acc, size_t n_rows, uint4* out, size_t out_len,
+                         cudaStream_t s);
+// Embed M31 values as QM31 (a, 0, 0, 0) with zero padding to out_len.
+void launch_m31_to_qm31(const uint32_t* in, size_t n, uint4* out, size_t out_len, uint32_t* err,
+                        cudaStream_t s);
+
+// ---- sumcheck rounds (backend.rs:145-178) ------------------------------------
+// All round launchers leave the 12 u32 (s0, s1, s2) QM31 sums of the *current*
+// round in out12 (device), reduced across the grid in the same launch.
+struct RoundScratch {
+    uint32_t* partials;  // >= max_blocks * 12
+    unsigned int* ticket;  // zero-initialised
+    uint32_t* out;       // >= 16 u32
+    int max_blocks;
+};
+// Round sums over QM31 vectors of length len (no fold).
+void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s);
+// Fold A, B in place with alpha (len -> len/2) and emit the next round's sums.
+void launch_fold_round_qm31(uint4* A, uint4* B, size_t len, qm31 alpha, const RoundScratch& rs,
+                            cudaStream_t s);
+// Round sums over M31 vectors (base-field first round of a product sumcheck).
+void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const RoundScratch& rs,
+                      uint32_t* err, cudaStream_t s);
+// Fold M31 vectors into QM31 outputs (len -> len/2) and emit the next round's sums.
+void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm31 alpha, uint4* Ao,
+                           uint4* Bo, const RoundScratch& rs, cudaStream_t s);
+// Final fold of length-2 vectors to one value each: out[0..4) = a, out[4..8) = b.
+// src_m31 selects M31 inputs (A32, B32) instead of QM31 (A, B).
+void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,
+                       size_t len, qm31 alpha, uint32_t* out, cudaStream_t s);
+
+// ---- generic MLE ops (ZkmlOps::evaluate_mle_at_point / restrict_mle) ----------
+// dst[i] = src[i] + r (src[i + h] - src[i]) for i < h (dst may alias src).
+void launch_mle_fold(const uint4* src, uint4* dst, size_t h, qm31 r, cudaStream_t s);
+
+}  // namespace zk

@@ -1,0 +1,498 @@
+// C-ABI: context management and the ZkmlOps / GKR matmul entry points.
+//
+// Host side of the B200 matmul-sumcheck prover.  The Fiat-Shamir channel is
+// advanced here, on the host, between kernel launches; each sumcheck round is
+// one kernel (fold of the previous round fused with this round's sums, grid
+// reduction included) followed by a 48-byte device-to-host read.
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "channel.hpp"
+#include "context.hpp"
+
+namespace zk {
+
+static thread_local std::string g_last_error;
+
+int set_error(int status, const std::string& msg) {
+    g_last_error = msg;
+    return status;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+    cudaGetLastError();  // clear a sticky launch error where possible
+    int st = (e == cudaErrorMemoryAllocation) ? ZKML_ERR_OOM : ZKML_ERR_CUDA;
+    return set_error(st, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+}
+
+int DevBuf::ensure(size_t need) {
+    if (need <= bytes && ptr) return ZKML_OK;
+    release();
+    size_t sz = need < 256 ? 256 : need;
+    cudaError_t e = cudaMalloc(&ptr, sz);
+    if (e != cudaSuccess) {
+        ptr = nullptr;
+        bytes = 0;
+        return cuda_error(e, "cudaMalloc");
+    }
+    bytes = sz;
+    return ZKML_OK;
+}
+
+void DevBuf::release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+}
+
+static cudaEvent_t pool_event(zkml_ctx* ctx) {
+    if (!ctx->ev_pool.empty()) {
+        cudaEvent_t e = ctx->ev_pool.back();
+        ctx->ev_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+KTimer::KTimer(zkml_ctx* c, int k) : ctx(c), cls(k) {
+    if (!ctx->timing) return;
+    zkml_ctx::PendingEv p;
+    p.cls = k;
+    p.e0 = pool_event(ctx);
+    p.e1 = pool_event(ctx);
+    cudaEventRecord(p.e0, ctx->stream);
+    ctx->pending.push_back(p);
+}
+
+KTimer::~KTimer() {
+    if (!ctx->timing) return;
+    cudaEventRecord(ctx->pending.back().e1, ctx->stream);
+}
+
+// Accumulate the timings of completed event pairs (call after a stream sync).
+static void drain_timers(zkml_ctx* ctx) {
+    for (auto& p : ctx->pending) {
+        float ms = 0;
+        if (cudaEventElapsedTime(&ms, p.e0, p.e1) == cudaSuccess) {
+            ctx->ktime[p.cls].ms += ms;
+            ctx->ktime[p.cls].launches++;
+        } else {
+            cudaGetLastError();
+        }
+        ctx->ev_pool.push_back(p.e0);
+        ctx->ev_pool.push_back(p.e1);
+    }
+    ctx->pending.clear();
+}
+
+static inline bool is_pow2(size_t x) { return x && !(x & (x - 1)); }
+static inline size_t next_pow2(size_t x) {
+    size_t p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+static inline unsigned ilog2(size_t x) {
+    unsigned l = 0;
+    while (((size_t)1 << (l + 1)) <= x) l++;
+    return l;
+}
+
+// Returns a device pointer for `p` (count bytes): p itself when it is device
+// memory of the current GPU, otherwise a copy in `stage`.
+static int device_view(zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const void** out) {
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        attr.type = cudaMemoryTypeUnregistered;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged) {
+        if (attr.type == cudaMemoryTypeDevice && attr.device != ctx->device)
+            return set_error(ZKML_ERR_INVALID_ARG, "input pointer is device memory of another GPU");
+        *out = p;
+        return ZKML_OK;
+    }
+    int rc = stage.ensure(bytes);
+    if (rc) return rc;
+    ZK_CUDA(cudaMemcpyAsync(stage.ptr, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    *out = stage.ptr;
+    return ZKML_OK;
+}
+
+static int check_err_flag(zkml_ctx* ctx, const char* what) {
+    if (ctx->h_small[48]) {
+        ctx->h_small[48] = 0;
+        ZK_CUDA(cudaMemsetAsync(ctx->err_flag(), 0, 4, ctx->stream));
+        return set_error(ZKML_ERR_INVALID_ARG, std::string(what) + ": input value >= 2^31 is not an M31 element");
+    }
+    return ZKML_OK;
+}
+
+static inline qm31 ldq(const uint32_t* p) { return qm(p[0], p[1], p[2], p[3]); }
+static inline void stq(uint32_t* p, const qm31& x) {
+    p[0] = x.a;
+    p[1] = x.b;
+    p[2] = x.c;
+    p[3] = x.d;
+}
+
+// Round polynomial from its values at 0, 1, 2 (backend.rs:163-166).
+static void interpolate(const uint32_t* s12, qm31& c0, qm31& c1, qm31& c2) {
+    static const uint32_t inv2 = minv(2);
+    qm31 s0 = ldq(s12), s1 = ldq(s12 + 4), s2 = ldq(s12 + 8);
+    c0 = s0;
+    c2 = qmul_m(qadd(qsub(qsub(s2, s1), s1), s0), inv2);
+    c1 = qsub(qsub(s1, s0), c2);
+}
+
+// Reads `words` u32 of the context's out buffer (plus the error flag) to the host.
+static int read_out(zkml_ctx* ctx, size_t words) {
+    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 16, ctx->out_words(), words * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 48, ctx->err_flag(), 4, cudaMemcpyDeviceToHost, ctx->stream));
+    ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (!ctx->pending.empty()) drain_timers(ctx);
+    return ZKML_OK;
+}
+
+// The sumcheck round loop over (A, B).  In M31 mode A32/B32 hold the base-field
+// vectors (length len) and the first fold writes QM31 into ctx->fa / fb.
+int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
+                 zkml_channel* chs, uint32_t* out_rp, uint32_t* out_ch, uint32_t* fa_out, uint32_t* fb_out) {
+    Channel ch(chs);
+    cudaStream_t s = ctx->stream;
+    const RoundScratch rs = ctx->round_scratch();
+    const unsigned log_k = ilog2(len);
+    bool m31 = A32 != nullptr;
+    if (log_k == 0) {
+        if (m31) {
+            uint32_t v[2];
+            ZK_CUDA(cudaMemcpyAsync(&v[0], A32, 4, cudaMemcpyDeviceToHost, s));
+            ZK_CUDA(cudaMemcpyAsync(&v[1], B32, 4, cudaMemcpyDeviceToHost, s));
+            ZK_CUDA(cudaStreamSynchronize(s));
+            stq(fa_out, qm(red32(v[0]), 0, 0, 0));
+            stq(fb_out, qm(red32(v[1]), 0, 0, 0));
+        } else {
+            ZK_CUDA(cudaMemcpyAsync(fa_out, A, 16, cudaMemcpyDeviceToHost, s));
+            ZK_CUDA(cudaMemcpyAsync(fb_out, B, 16, cudaMemcpyDeviceToHost, s));
+            ZK_CUDA(cudaStreamSynchronize(s));
+        }
+        return ZKML_OK;
+    }
+    {
+        KTimer t(ctx, KC_ROUND);
+        if (m31)
+            launch_round_m31(A32, B32, len, rs, ctx->err_flag(), s);
+        else
+            launch_round_qm31(A, B, len, rs, s);
+    }
+    ctx->launches++;
+    for (unsigned r = 0; r < log_k; r++) {
+        int rc = read_out(ctx, 12);
+        if (rc) return rc;
+        if (r == 0 && (rc = check_err_flag(ctx, "reduce_matmul_layer"))) return rc;
+        qm31 c0, c1, c2;
+        interpolate(ctx->h_small + 16, c0, c1, c2);
+        if (out_rp) {
+            stq(out_rp + 12 * r, c0);
+            stq(out_rp + 12 * r + 4, c1);
+            stq(out_rp + 12 * r + 8, c2);
+        }
+        ch.mix_poly_coeffs(c0, c1, c2);
+        const qm31 alpha = ch.draw_qm31();
+        if (out_ch) stq(out_ch + 4 * r, alpha);
+        KTimer t(ctx, KC_ROUND);
+        if (len == 2) {
+            launch_final_fold(A, B, m31 ? A32 : nullptr, m31 ? B32 : nullptr, len, alpha, ctx->out_words(), s);
+        } else if (m31) {
+            A = ctx->fa.as<uint4>();
+            B = ctx->fb.as<uint4>();
+            launch_fold_round_m31(A32, B32, len, alpha, A, B, rs, s);
+            m31 = false;
+        } else {
+            launch_fold_round_qm31(A, B, len, alpha, rs, s);
+        }
+        ctx->launches++;
+        len /= 2;
+    }
+    int rc = read_out(ctx, 8);
+    if (rc) return rc;
+    memcpy(fa_out, ctx->h_small + 16, 16);
+    memcpy(fb_out, ctx->h_small + 20, 16);
+    return ZKML_OK;
+}
+
+// Restriction of A (rows by r_i) and B (columns by r_j) into ctx->fa / fb (length pk).
+static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, const uint32_t* B, size_t n,
+                       const qm31* r_i, unsigned n_ri, const qm31* r_j, unsigned n_rj, size_t pk) {
+    cudaStream_t s = ctx->stream;
+    int rc;
+    if ((rc = ctx->fa.ensure(pk * 16)) || (rc = ctx->fb.ensure(pk * 16))) return rc;
+    uint4* fa = ctx->fa.as<uint4>();
+    uint4* fb = ctx->fb.as<uint4>();
+    if (n_ri == 0) {  // m == 1: f_a is A's single row
+        launch_m31_to_qm31(A, k, fa, pk, ctx->err_flag(), s);
+        ctx->launches++;
+    } else {
+        if ((rc = ctx->eq_a.ensure(((size_t)16) << n_ri)) || (rc = ctx->acc_a.ensure(k * 32))) return rc;
+        launch_eq_table(r_i, n_ri, ctx->eq_a.as<uint4>(), (size_t)1 << n_ri, s);
+        ZK_CUDA(cudaMemsetAsync(ctx->acc_a.ptr, 0, k * 32, s));
+        {
+            KTimer t(ctx, KC_RESTRICT_ROWS);
+            launch_restrict_rows(A, (uint32_t)m, (uint32_t)k, ctx->eq_a.as<uint4>(),
+                                 ctx->acc_a.as<unsigned long long>(), ctx->err_flag(), s);
+        }
+        launch_acc_finalize(ctx->acc_a.as<unsigned long long>(), k, fa, pk, s);
+        ctx->launches += 3;
+    }
+    if (n_rj == 0) {  // n == 1: f_b is B's single column (contiguous)
+        launch_m31_to_qm31(B, k, fb, pk, ctx->err_flag(), s);
+        ctx->launches++;
+    } else {
+        const unsigned lo_vars = n_rj < 6 ? n_rj : 6;
+        const unsigned hi_vars = n_rj - lo_vars;
+        if ((rc = ctx->eq_hi.ensure(((size_t)16) << hi_vars)) || (rc = ctx->eq_lo.ensure(64 * 16)) ||
+            (rc = ctx->acc_b.ensure(k * 32)))
+            return rc;
+        launch_eq_table(r_j, hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
+        launch_eq_table(r_j + hi_vars, lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
+        ZK_CUDA(cudaMemsetAsync(ctx->acc_b.ptr, 0, k * 32, s));
+        {
+            KTimer t(ctx, KC_RESTRICT_COLS);
+            launch_restrict_cols(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
+                                 ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
+        }
+        launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
+        ctx->launches += 4;
+    }
+    return ZKML_OK;
+}
+
+}  // namespace zk
+
+using namespace zk;
+
+extern "C" {
+
+int zkml_abi_version(void) { return ZKML_ABI_VERSION; }
+const char* zkml_last_error(void) { return g_last_error.c_str(); }
+
+int zkml_ctx_create(int device, zkml_ctx** out) {
+    if (!out) return set_error(ZKML_ERR_INVALID_ARG, "out is NULL");
+    *out = nullptr;
+    felt_init();
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0)
+        return set_error(ZKML_ERR_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
+    if (device < 0 || device >= n) return set_error(ZKML_ERR_INVALID_ARG, "device ordinal out of range");
+    ZK_CUDA(cudaSetDevice(device));
+    int major = 0;
+    ZK_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    if (major != 10)
+        return set_error(ZKML_ERR_UNSUPPORTED, "this build targets sm_100a (B200); device has compute capability " +
+                                                   std::to_string(major) + ".x");
+    zkml_ctx* ctx = new zkml_ctx();
+    ctx->device = device;
+    cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    ctx->max_round_blocks = ctx->num_sms * 8;
+    int rc = ZKML_OK;
+    e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) rc = cuda_error(e, "cudaStreamCreate");
+    ctx->stream = ctx->own_stream;
+    if (!rc) rc = ctx->partials.ensure((size_t)ctx->max_round_blocks * 12 * 4);
+    if (!rc) rc = ctx->small.ensure(64 * 4);
+    if (!rc && (e = cudaMemset(ctx->small.ptr, 0, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMemset");
+    if (!rc && (e = cudaMallocHost(&ctx->h_small, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMallocHost");
+    if (rc) {
+        zkml_ctx_destroy(ctx);
+        return rc;
+    }
+    memset(ctx->h_small, 0, 64 * 4);
+    *out = ctx;
+    return ZKML_OK;
+}
+
+int zkml_ctx_destroy(zkml_ctx* ctx) {
+    if (!ctx) return ZKML_OK;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    DevBuf* bufs[] = {&ctx->a_in, &ctx->b_in, &ctx->fa,    &ctx->fb,       &ctx->acc_a, &ctx->acc_b,
+                      &ctx->eq_a, &ctx->eq_hi, &ctx->eq_lo, &ctx->partials, &ctx->small};
+    for (DevBuf* b : bufs) b->release();
+    if (ctx->h_small) cudaFreeHost(ctx->h_small);
+    drain_timers(ctx);
+    for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return ZKML_OK;
+}
+
+int zkml_ctx_device(const zkml_ctx* ctx) { return ctx ? ctx->device : -1; }
+uint64_t zkml_ctx_kernel_launches(const zkml_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+int zkml_ctx_enable_timing(zkml_ctx* ctx, int enable) {
+    if (!ctx) return set_error(ZKML_ERR_INVALID_ARG, "ctx is NULL");
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+    drain_timers(ctx);
+    ctx->timing = enable != 0;
+    for (auto& k : ctx->ktime) k = zkml_ctx::KTime();
+    return ZKML_OK;
+}
+
+int zkml_ctx_kernel_time(zkml_ctx* ctx, const char* kernel, double* out_ms, uint64_t* out_launches) {
+    if (!ctx || !kernel) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    static const char* names[4] = {"restrict_cols", "restrict_rows", "sumcheck_round", "merkle"};
+    if (!ctx->pending.empty()) {
+        ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+        drain_timers(ctx);
+    }
+    for (int i = 0; i < 4; i++)
+        if (!strcmp(kernel, names[i])) {
+            if (out_ms) *out_ms = ctx->ktime[i].ms;
+            if (out_launches) *out_launches = ctx->ktime[i].launches;
+            return ZKML_OK;
+        }
+    return set_error(ZKML_ERR_INVALID_ARG, std::string("unknown kernel class ") + kernel);
+}
+
+int zkml_ctx_set_stream(zkml_ctx* ctx, void* stream) {
+    if (!ctx) return set_error(ZKML_ERR_INVALID_ARG, "ctx is NULL");
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+    return ZKML_OK;
+}
+
+int zkml_reduce_matmul_layer(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size_t a_cols, const uint32_t* b,
+                             size_t b_rows, size_t b_cols, const uint32_t* r_i, size_t n_ri, const uint32_t* r_j,
+                             size_t n_rj, size_t pk, zkml_channel* ch, uint32_t* out_round_polys,
+                             uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4]) {
+    if (!ctx || !a || !b || !ch || !out_final_a || !out_final_b)
+        return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    if (a_rows == 0 || a_cols == 0 || b_cols == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty matrix");
+    if (a_cols != b_rows) return set_error(ZKML_ERR_INVALID_ARG, "A.cols must equal B.rows");
+    if (a_rows > (1u << 30) || a_cols > (1u << 30) || b_cols > (1u << 30))
+        return set_error(ZKML_ERR_INVALID_ARG, "matrix dimension exceeds 2^30");
+    if (pk != next_pow2(a_cols)) return set_error(ZKML_ERR_INVALID_ARG, "pk must be next_pow2(A.cols)");
+    if (n_ri != ilog2(next_pow2(a_rows)) || n_rj != ilog2(next_pow2(b_cols)))
+        return set_error(ZKML_ERR_INVALID_ARG, "r_i / r_j length does not match the padded dimensions");
+    if (a_rows * a_cols > ((size_t)1 << 32) || b_rows * b_cols > ((size_t)1 << 34))
+        return set_error(ZKML_ERR_INVALID_ARG, "matrix too large");
+    if ((n_ri && !r_i) || (n_rj && !r_j)) return set_error(ZKML_ERR_INVALID_ARG, "NULL challenge point");
+    if (n_rj > MAX_EQ_VARS || n_ri > MAX_EQ_VARS) return set_error(ZKML_ERR_INVALID_ARG, "too many variables");
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    const void* A = nullptr;
+    const void* B = nullptr;
+    int rc = device_view(ctx, a, a_rows * a_cols * 4, ctx->a_in, &A);
+    if (!rc) rc = device_view(ctx, b, b_rows * b_cols * 4, ctx->b_in, &B);
+    if (rc) return rc;
+    const uint32_t* Ad = static_cast<const uint32_t*>(A);
+    const uint32_t* Bd = static_cast<const uint32_t*>(B);
+    // Product sumcheck (1 x k times k x 1, k a power of two): stay in M31 for round 0.
+    if (n_ri == 0 && n_rj == 0 && pk == a_cols && pk >= 4) {
+        if ((rc = ctx->fa.ensure(pk / 2 * 16)) || (rc = ctx->fb.ensure(pk / 2 * 16))) return rc;
+        return run_sumcheck(ctx, nullptr, nullptr, Ad, Bd, pk, ch, out_round_polys, out_challenges, out_final_a,
+                            out_final_b);
+    }
+    rc = restrict_ab(ctx, Ad, a_rows, a_cols, Bd, b_cols, reinterpret_cast<const qm31*>(r_i), (unsigned)n_ri,
+                     reinterpret_cast<const qm31*>(r_j), (unsigned)n_rj, pk);
+    if (rc) return rc;
+    rc = run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, pk, ch, out_round_polys,
+                      out_challenges, out_final_a, out_final_b);
+    if (rc) return rc;
+    return check_err_flag(ctx, "reduce_matmul_layer");
+}
+
+int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n_point,
+                                 const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k,
+                                 const uint32_t* b, size_t n, zkml_channel* chs, uint32_t* out_round_polys,
+                                 uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t* out_next_point) {
+    if (!ctx || !claim_value || !chs) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    if (m == 0 || k == 0 || n == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty matrix");
+    const size_t pm = next_pow2(m), pk = next_pow2(k), pn = next_pow2(n);
+    const unsigned log_m = ilog2(pm), log_n = ilog2(pn), log_k = ilog2(pk);
+    if (n_point != log_m + log_n)
+        return set_error(ZKML_ERR_INVALID_ARG, "output claim has " + std::to_string(n_point) +
+                                                   " vars, expected exactly " + std::to_string(log_m + log_n));
+    Channel ch(chs);
+    ch.mix_u64(m);
+    ch.mix_u64(k);
+    ch.mix_u64(n);
+    ch.mix_qm31(ldq(claim_value));
+    uint32_t chal[4 * 64];
+    int rc = zkml_reduce_matmul_layer(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
+                                      chs, out_round_polys, chal, out_final_a, out_final_b);
+    if (rc) return rc;
+    ch.mix_qm31(ldq(out_final_a));
+    ch.mix_qm31(ldq(out_final_b));
+    if (out_next_point) {
+        memcpy(out_next_point, claim_point, 16 * log_m);
+        memcpy(out_next_point + 4 * log_m, chal, 16 * log_k);
+    }
+    return ZKML_OK;
+}
+
+int zkml_evaluate_mle(zkml_ctx* ctx, const uint32_t* mle, size_t n_vars, const uint32_t* point, uint32_t out[4]) {
+    if (!ctx || !mle || !out || (n_vars && !point)) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    if (n_vars > 34) return set_error(ZKML_ERR_INVALID_ARG, "too many variables");
+    const size_t n = (size_t)1 << n_vars;
+    if (n_vars == 0) {
+        ZK_CUDA(cudaSetDevice(ctx->device));
+        const void* M = nullptr;
+        int rc = device_view(ctx, mle, 16, ctx->a_in, &M);
+        if (rc) return rc;
+        ZK_CUDA(cudaMemcpyAsync(out, M, 16, cudaMemcpyDeviceToHost, ctx->stream));
+        ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+        return ZKML_OK;
+    }
+    int rc = ZKML_OK;
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    const void* M = nullptr;
+    if ((rc = device_view(ctx, mle, n * 16, ctx->a_in, &M))) return rc;
+    if ((rc = ctx->fa.ensure(n / 2 * 16))) return rc;
+    const qm31* pt = reinterpret_cast<const qm31*>(point);
+    const uint4* src = static_cast<const uint4*>(M);
+    size_t h = n / 2;
+    for (size_t r = 0; r < n_vars; r++, h /= 2) {
+        launch_mle_fold(src, ctx->fa.as<uint4>(), h, pt[r], ctx->stream);
+        ctx->launches++;
+        src = ctx->fa.as<uint4>();
+    }
+    ZK_CUDA(cudaMemcpyAsync(out, ctx->fa.ptr, 16, cudaMemcpyDeviceToHost, ctx->stream));
+    ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ZKML_OK;
+}
+
+int zkml_restrict_mle(zkml_ctx* ctx, const uint32_t* mle, size_t n_evals, const uint32_t* assign, size_t n_assign,
+                      uint32_t* out) {
+    if (!ctx || !mle || !out || (n_assign && !assign)) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    if (!is_pow2(n_evals) || ((size_t)1 << n_assign) > n_evals)
+        return set_error(ZKML_ERR_INVALID_ARG, "n_evals must be a power of two >= 2^n_assign");
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    const void* M = nullptr;
+    int rc = device_view(ctx, mle, n_evals * 16, ctx->a_in, &M);
+    if (rc) return rc;
+    const size_t out_len = n_evals >> n_assign;
+    if (n_assign == 0) {
+        ZK_CUDA(cudaMemcpyAsync(out, M, n_evals * 16, cudaMemcpyDeviceToHost, ctx->stream));
+        ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+        return ZKML_OK;
+    }
+    if ((rc = ctx->fa.ensure(n_evals / 2 * 16))) return rc;
+    const qm31* pt = reinterpret_cast<const qm31*>(assign);
+    const uint4* src = static_cast<const uint4*>(M);
+    size_t h = n_evals / 2;
+    for (size_t r = 0; r < n_assign; r++, h /= 2) {
+        launch_mle_fold(src, ctx->fa.as<uint4>(), h, pt[r], ctx->stream);
+        ctx->launches++;
+        src = ctx->fa.as<uint4>();
+    }
+    ZK_CUDA(cudaMemcpyAsync(out, ctx->fa.ptr, out_len * 16, cudaMemcpyDeviceToHost, ctx->stream));
+    ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+    return ZKML_OK;
+}
+
+}  // extern "C"

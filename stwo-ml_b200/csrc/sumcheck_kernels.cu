@@ -1,0 +1,479 @@
+// sm_100a kernels for the GKR matmul sumcheck: eq tables, the W.eq(r)
+// restrictions, and the degree-2 round reductions with fused in-place folds.
+//
+// All arithmetic is M31/QM31 integer work (no tensor cores).  The restriction
+// is HBM-bound: it streams the weight matrix once with 16-byte loads and keeps
+// 4 x 4 64-bit accumulators per thread, reducing modulo 2^31 - 1 only every
+// four products (each product < 2^62, so four of them plus a reduced residue
+// still fit in 64 bits).
+#include "kernels.cuh"
+
+namespace zk {
+
+__device__ __forceinline__ qm31 ld_q(const uint4* p) {
+    uint4 v = *p;
+    return qm(v.x, v.y, v.z, v.w);
+}
+__device__ __forceinline__ void st_q(uint4* p, qm31 x) { *p = make_uint4(x.a, x.b, x.c, x.d); }
+
+// Reduce a u64 accumulator to < 2^34 (keeps it congruent mod P).
+__device__ __forceinline__ unsigned long long lazy(unsigned long long x) { return (x & P) + (x >> 31); }
+
+// ---------------------------------------------------------------------------
+// eq table
+// ---------------------------------------------------------------------------
+__global__ void eq_table_kernel(EqChallenges ch, uint4* __restrict__ table, size_t len) {
+    const size_t n = (size_t)1 << ch.v;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < len;
+         idx += (size_t)gridDim.x * blockDim.x) {
+        qm31 w = qzero();
+        if (idx < n) {
+            w = qone();
+            for (int l = 0; l < ch.v; l++) {
+                const int bit = (idx >> (ch.v - 1 - l)) & 1;
+                w = qmul(w, bit ? ch.c[l] : qsub(qone(), ch.c[l]));
+            }
+        }
+        st_q(table + idx, w);
+    }
+}
+
+void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaStream_t s) {
+    EqChallenges ch;
+    ch.v = v;
+    for (int i = 0; i < v; i++) ch.c[i] = c[i];
+    const int threads = 256;
+    size_t blocks = (table_len + threads - 1) / threads;
+    if (blocks > 4096) blocks = 4096;
+    if (blocks == 0) blocks = 1;
+    eq_table_kernel<<<(unsigned)blocks, threads, 0, s>>>(ch, table, table_len);
+}
+
+// ---------------------------------------------------------------------------
+// Column restriction f_b[i] = sum_j B[i][j] L_j  (the HBM-bound hot spot)
+//
+// The row-major matrix is viewed as a flat sequence of "stripes" of 64
+// columns of one row.  Each warp owns a contiguous range of stripes (so the
+// work is balanced to within one stripe whatever k and n are); lane t loads
+// columns 2t, 2t+1 of every stripe with one 8-byte streaming load (a warp
+// reads 256 contiguous bytes per stripe).  The eq table is split as
+// L_j = lhi[j >> 6] * llo[j & 63]: lane t accumulates
+// sum_stripes lhi[stripe] * B[., 2t + e] for its two columns e in 2 x 4 64-bit
+// accumulators, and only when the warp leaves a row it multiplies by its two
+// llo entries, reduces across the warp and adds the row's partial with one
+// 64-bit atomic per component.  UNROLL stripes are loaded before any is used
+// to keep enough bytes in flight per SM.
+// ---------------------------------------------------------------------------
+constexpr int RC_UNROLL = 8;
+
+template <bool VEC>
+__global__ void __launch_bounds__(256, 4)
+    restrict_cols_kernel(const uint32_t* __restrict__ B, uint32_t k, uint32_t n, uint32_t s_row,
+                         unsigned long long total, const uint4* __restrict__ lhi,
+                         const uint4* __restrict__ llo, unsigned long long* __restrict__ acc_out,
+                         uint32_t* __restrict__ err) {
+    const uint32_t lane = threadIdx.x & 31;
+    const unsigned long long warp = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
+    unsigned long long s = warp * total / nwarps;
+    const unsigned long long s_end = (warp + 1) * total / nwarps;
+    if (s >= s_end) return;
+    uint32_t row = (uint32_t)(s / s_row);
+    uint32_t jh = (uint32_t)(s - (unsigned long long)row * s_row);
+    unsigned long long acc[2][4];
+#pragma unroll
+    for (int e = 0; e < 2; e++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) acc[e][c] = 0;
+    uint32_t bad = 0;
+    while (s < s_end) {
+        unsigned long long left = s_end - s;
+        uint32_t cnt = s_row - jh;
+        if (left < cnt) cnt = (uint32_t)left;
+        if (cnt > RC_UNROLL) cnt = RC_UNROLL;
+        uint2 v[RC_UNROLL];
+        const size_t rbase = (size_t)row * n;
+#pragma unroll
+        for (int u = 0; u < RC_UNROLL; u++) {
+            v[u] = make_uint2(0, 0);
+            const uint32_t col = (jh + u) * 64u + 2u * lane;
+            if (u < (int)cnt) {
+                if (VEC) {
+                    if (col < n) v[u] = __ldcs(reinterpret_cast<const uint2*>(B + rbase + col));
+                } else {
+                    if (col < n) v[u].x = __ldcs(B + rbase + col);
+                    if (col + 1 < n) v[u].y = __ldcs(B + rbase + col + 1);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < RC_UNROLL; u++) {
+            if (u < (int)cnt) {
+                const uint4 lh = __ldg(lhi + jh + u);
+                bad |= v[u].x | v[u].y;
+                acc[0][0] += (unsigned long long)v[u].x * lh.x;
+                acc[0][1] += (unsigned long long)v[u].x * lh.y;
+                acc[0][2] += (unsigned long long)v[u].x * lh.z;
+                acc[0][3] += (unsigned long long)v[u].x * lh.w;
+                acc[1][0] += (unsigned long long)v[u].y * lh.x;
+                acc[1][1] += (unsigned long long)v[u].y * lh.y;
+                acc[1][2] += (unsigned long long)v[u].y * lh.z;
+                acc[1][3] += (unsigned long long)v[u].y * lh.w;
+            }
+            if ((u & 3) == 3) {
+#pragma unroll
+                for (int e = 0; e < 2; e++)
+#pragma unroll
+                    for (int c = 0; c < 4; c++) acc[e][c] = lazy(acc[e][c]);
+            }
+        }
+        s += cnt;
+        jh += cnt;
+        if (jh == s_row || s == s_end) {
+            // Flush this warp's contribution to `row`.
+            qm31 t = qzero();
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                qm31 q = qm(red64(acc[e][0]), red64(acc[e][1]), red64(acc[e][2]), red64(acc[e][3]));
+                t = qadd(t, qmul(q, ld_q(llo + 2 * lane + e)));
+#pragma unroll
+                for (int c = 0; c < 4; c++) acc[e][c] = 0;
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                qm31 o;
+                o.a = __shfl_xor_sync(0xffffffffu, t.a, off);
+                o.b = __shfl_xor_sync(0xffffffffu, t.b, off);
+                o.c = __shfl_xor_sync(0xffffffffu, t.c, off);
+                o.d = __shfl_xor_sync(0xffffffffu, t.d, off);
+                t = qadd(t, o);
+            }
+            if (lane == 0) {
+                atomicAdd(acc_out + 4 * (size_t)row + 0, (unsigned long long)t.a);
+                atomicAdd(acc_out + 4 * (size_t)row + 1, (unsigned long long)t.b);
+                atomicAdd(acc_out + 4 * (size_t)row + 2, (unsigned long long)t.c);
+                atomicAdd(acc_out + 4 * (size_t)row + 3, (unsigned long long)t.d);
+            }
+            if (jh == s_row) {
+                row++;
+                jh = 0;
+            }
+        }
+    }
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+}
+
+void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
+                          unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s) {
+    const uint32_t s_row = (n + 63) / 64;
+    const unsigned long long total = (unsigned long long)k * s_row;
+    const int threads = 256;
+    // Persistent grid: 4 CTAs of 8 warps per SM, never more warps than stripes.
+    unsigned long long blocks = (unsigned long long)num_sms * 4;
+    const unsigned long long need = (total + 7) / 8;
+    if (blocks > need) blocks = need;
+    if (blocks == 0) blocks = 1;
+    const bool vec = (n % 2 == 0) && ((reinterpret_cast<uintptr_t>(B) & 7) == 0);
+    if (vec)
+        restrict_cols_kernel<true><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
+    else
+        restrict_cols_kernel<false><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
+}
+
+// ---------------------------------------------------------------------------
+// Row restriction f_a[j] = sum_i A[i][j] L_i.  A is small (m x k activations);
+// each thread owns one column and a chunk of 16 rows, partials meet in
+// 64-bit atomics.
+// ---------------------------------------------------------------------------
+__global__ void restrict_rows_kernel(const uint32_t* __restrict__ A, uint32_t m, uint32_t k,
+                                     const uint4* __restrict__ L, unsigned long long* __restrict__ acc_out,
+                                     uint32_t* __restrict__ err) {
+    const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t i0 = blockIdx.y * 16;
+    if (j >= k) return;
+    unsigned long long acc[4] = {0, 0, 0, 0};
+    uint32_t bad = 0;
+    const uint32_t i1 = min(m, i0 + 16);
+    for (uint32_t i = i0; i < i1; i++) {
+        const uint32_t v = __ldg(A + (size_t)i * k + j);
+        bad |= v;
+        const uint4 l = __ldg(L + i);
+        acc[0] += (unsigned long long)v * l.x;
+        acc[1] += (unsigned long long)v * l.y;
+        acc[2] += (unsigned long long)v * l.z;
+        acc[3] += (unsigned long long)v * l.w;
+        if (((i - i0) & 3) == 3)
+            for (int c = 0; c < 4; c++) acc[c] = lazy(acc[c]);
+    }
+    for (int c = 0; c < 4; c++) atomicAdd(acc_out + 4 * (size_t)j + c, (unsigned long long)red64(acc[c]));
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+}
+
+void launch_restrict_rows(const uint32_t* A, uint32_t m, uint32_t k, const uint4* L, unsigned long long* acc,
+                          uint32_t* err, cudaStream_t s) {
+    dim3 grid((k + 255) / 256, (m + 15) / 16);
+    restrict_rows_kernel<<<grid, 256, 0, s>>>(A, m, k, L, acc, err);
+}
+
+__global__ void acc_finalize_kernel(const unsigned long long* __restrict__ acc, size_t n_rows,
+                                    uint4* __restrict__ out, size_t out_len) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < out_len;
+         i += (size_t)gridDim.x * blockDim.x) {
+        uint4 r = make_uint4(0, 0, 0, 0);
+        if (i < n_rows) {
+            r.x = red64(acc[4 * i + 0]);
+            r.y = red64(acc[4 * i + 1]);
+            r.z = red64(acc[4 * i + 2]);
+            r.w = red64(acc[4 * i + 3]);
+        }
+        out[i] = r;
+    }
+}
+
+void launch_acc_finalize(const unsigned long long* acc, size_t n_rows, uint4* out, size_t out_len, cudaStream_t s) {
+    size_t blocks = (out_len + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    if (blocks == 0) blocks = 1;
+    acc_finalize_kernel<<<(unsigned)blocks, 256, 0, s>>>(acc, n_rows, out, out_len);
+}
+
+__global__ void m31_to_qm31_kernel(const uint32_t* __restrict__ in, size_t n, uint4* __restrict__ out,
+                                   size_t out_len, uint32_t* __restrict__ err) {
+    uint32_t bad = 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < out_len;
+         i += (size_t)gridDim.x * blockDim.x) {
+        uint32_t v = i < n ? in[i] : 0;
+        bad |= v;
+        out[i] = make_uint4(red32(v), 0, 0, 0);
+    }
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+}
+
+void launch_m31_to_qm31(const uint32_t* in, size_t n, uint4* out, size_t out_len, uint32_t* err, cudaStream_t s) {
+    size_t blocks = (out_len + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    if (blocks == 0) blocks = 1;
+    m31_to_qm31_kernel<<<(unsigned)blocks, 256, 0, s>>>(in, n, out, out_len, err);
+}
+
+// ---------------------------------------------------------------------------
+// Sumcheck rounds.  Each launch reduces (s0, s1, s2) over the grid: per-block
+// partials go to global memory and the last block to finish (atomic ticket)
+// sums them, so the host reads the round's 12 words after one launch.
+// ---------------------------------------------------------------------------
+struct Sums {
+    unsigned long long v[12];
+};
+
+__device__ __forceinline__ void sums_add(Sums& s, const qm31& x0, const qm31& x1, const qm31& x2) {
+    s.v[0] += x0.a; s.v[1] += x0.b; s.v[2] += x0.c; s.v[3] += x0.d;
+    s.v[4] += x1.a; s.v[5] += x1.b; s.v[6] += x1.c; s.v[7] += x1.d;
+    s.v[8] += x2.a; s.v[9] += x2.b; s.v[10] += x2.c; s.v[11] += x2.d;
+}
+
+// Block-reduce the 12 lazily accumulated words and finish the grid reduction.
+__device__ void finish_sums(Sums& s, uint32_t* __restrict__ partials, unsigned int* __restrict__ ticket,
+                            uint32_t* __restrict__ out) {
+    __shared__ uint32_t sh[32][12];
+    __shared__ bool is_last;
+    uint32_t r[12];
+#pragma unroll
+    for (int i = 0; i < 12; i++) {
+        r[i] = red64(s.v[i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) r[i] = madd(r[i], __shfl_xor_sync(0xffffffffu, r[i], off));
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (lane == 0)
+        for (int i = 0; i < 12; i++) sh[warp][i] = r[i];
+    __syncthreads();
+    if (threadIdx.x < 12) {
+        uint32_t acc = 0;
+        for (int w = 0; w < nw; w++) acc = madd(acc, sh[w][threadIdx.x]);
+        partials[blockIdx.x * 12 + threadIdx.x] = acc;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // Last block: 12 components x blocks partials.
+    for (int i = warp; i < 12; i += nw) {
+        unsigned long long acc = 0;
+        for (unsigned b = lane; b < gridDim.x; b += 32) acc += __ldcg(partials + b * 12 + i);
+        uint32_t v = red64(acc);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) out[i] = v;
+    }
+    if (threadIdx.x == 0) *ticket = 0;
+}
+
+__device__ __forceinline__ void round_terms(const qm31& alo, const qm31& ahi, const qm31& blo, const qm31& bhi,
+                                            Sums& s) {
+    qm31 p0 = qmul(alo, blo);
+    qm31 p1 = qmul(ahi, bhi);
+    qm31 p2 = qmul(qsub(qdbl(ahi), alo), qsub(qdbl(bhi), blo));
+    sums_add(s, p0, p1, p2);
+}
+
+__device__ __forceinline__ void sums_zero(Sums& s) {
+#pragma unroll
+    for (int i = 0; i < 12; i++) s.v[i] = 0;
+}
+
+__global__ void __launch_bounds__(256) round_qm31_kernel(const uint4* __restrict__ A, const uint4* __restrict__ B,
+                                                         size_t q, uint32_t* partials, unsigned int* ticket,
+                                                         uint32_t* out) {
+    Sums s;
+    sums_zero(s);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x)
+        round_terms(ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q), s);
+    finish_sums(s, partials, ticket, out);
+}
+
+// In-place fold with alpha fused with the next round's sums.  Thread i reads
+// elements i, i+q, i+h, i+q+h (h = len/2, q = h/2) and writes i and i+q: every
+// element is read by exactly one thread, so the in-place update is race-free.
+__global__ void __launch_bounds__(256) fold_round_qm31_kernel(uint4* __restrict__ A, uint4* __restrict__ B, size_t h,
+                                                              qm31 alpha, uint32_t* partials, unsigned int* ticket,
+                                                              uint32_t* out) {
+    const size_t q = h / 2;
+    Sums s;
+    sums_zero(s);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
+        qm31 a0 = ld_q(A + i), a1 = ld_q(A + i + q), a2 = ld_q(A + i + h), a3 = ld_q(A + i + q + h);
+        qm31 b0 = ld_q(B + i), b1 = ld_q(B + i + q), b2 = ld_q(B + i + h), b3 = ld_q(B + i + q + h);
+        qm31 alo = qadd(a0, qmul(alpha, qsub(a2, a0)));
+        qm31 ahi = qadd(a1, qmul(alpha, qsub(a3, a1)));
+        qm31 blo = qadd(b0, qmul(alpha, qsub(b2, b0)));
+        qm31 bhi = qadd(b1, qmul(alpha, qsub(b3, b1)));
+        st_q(A + i, alo);
+        st_q(A + i + q, ahi);
+        st_q(B + i, blo);
+        st_q(B + i + q, bhi);
+        round_terms(alo, ahi, blo, bhi, s);
+    }
+    finish_sums(s, partials, ticket, out);
+}
+
+__global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restrict__ A, const uint32_t* __restrict__ B,
+                                                        size_t q, uint32_t* partials, unsigned int* ticket,
+                                                        uint32_t* out, uint32_t* err) {
+    unsigned long long s0 = 0, s1 = 0, s2 = 0;
+    uint32_t bad = 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
+        uint32_t alo = __ldcs(A + i), ahi = __ldcs(A + i + q), blo = __ldcs(B + i), bhi = __ldcs(B + i + q);
+        bad |= alo | ahi | blo | bhi;
+        alo = red32(alo);
+        ahi = red32(ahi);
+        blo = red32(blo);
+        bhi = red32(bhi);
+        s0 += mmul(alo, blo);
+        s1 += mmul(ahi, bhi);
+        s2 += mmul(msub(madd(ahi, ahi), alo), msub(madd(bhi, bhi), blo));
+    }
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+    Sums s;
+    sums_zero(s);
+    s.v[0] = s0;
+    s.v[4] = s1;
+    s.v[8] = s2;
+    finish_sums(s, partials, ticket, out);
+}
+
+// lo + alpha (hi - lo) with lo, hi in M31.
+__device__ __forceinline__ qm31 fold_m31(uint32_t lo, uint32_t hi, const qm31& alpha) {
+    return qadd(qm(lo, 0, 0, 0), qmul_m(alpha, msub(hi, lo)));
+}
+
+__global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __restrict__ A,
+                                                             const uint32_t* __restrict__ B, size_t h, qm31 alpha,
+                                                             uint4* __restrict__ Ao, uint4* __restrict__ Bo,
+                                                             uint32_t* partials, unsigned int* ticket, uint32_t* out) {
+    const size_t q = h / 2;
+    Sums s;
+    sums_zero(s);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
+        qm31 alo = fold_m31(red32(A[i]), red32(A[i + h]), alpha);
+        qm31 ahi = fold_m31(red32(A[i + q]), red32(A[i + q + h]), alpha);
+        qm31 blo = fold_m31(red32(B[i]), red32(B[i + h]), alpha);
+        qm31 bhi = fold_m31(red32(B[i + q]), red32(B[i + q + h]), alpha);
+        st_q(Ao + i, alo);
+        st_q(Ao + i + q, ahi);
+        st_q(Bo + i, blo);
+        st_q(Bo + i + q, bhi);
+        round_terms(alo, ahi, blo, bhi, s);
+    }
+    finish_sums(s, partials, ticket, out);
+}
+
+static unsigned round_blocks(size_t work, int max_blocks) {
+    size_t b = (work + 255) / 256;
+    if (b > (size_t)max_blocks) b = max_blocks;
+    if (b == 0) b = 1;
+    return (unsigned)b;
+}
+
+void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s) {
+    const size_t q = len / 2;
+    round_qm31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out);
+}
+
+void launch_fold_round_qm31(uint4* A, uint4* B, size_t len, qm31 alpha, const RoundScratch& rs, cudaStream_t s) {
+    const size_t h = len / 2;
+    fold_round_qm31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha, rs.partials,
+                                                                                rs.ticket, rs.out);
+}
+
+void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const RoundScratch& rs, uint32_t* err,
+                      cudaStream_t s) {
+    const size_t q = len / 2;
+    round_m31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out, err);
+}
+
+void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm31 alpha, uint4* Ao, uint4* Bo,
+                           const RoundScratch& rs, cudaStream_t s) {
+    const size_t h = len / 2;
+    fold_round_m31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha, Ao, Bo, rs.partials,
+                                                                               rs.ticket, rs.out);
+}
+
+__global__ void final_fold_kernel(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,
+                                  qm31 alpha, uint32_t* out) {
+    if (threadIdx.x != 0) return;
+    qm31 a, b;
+    if (A32) {
+        a = fold_m31(red32(A32[0]), red32(A32[1]), alpha);
+        b = fold_m31(red32(B32[0]), red32(B32[1]), alpha);
+    } else {
+        qm31 a0 = ld_q(A), a1 = ld_q(A + 1), b0 = ld_q(B), b1 = ld_q(B + 1);
+        a = qadd(a0, qmul(alpha, qsub(a1, a0)));
+        b = qadd(b0, qmul(alpha, qsub(b1, b0)));
+    }
+    out[0] = a.a; out[1] = a.b; out[2] = a.c; out[3] = a.d;
+    out[4] = b.a; out[5] = b.b; out[6] = b.c; out[7] = b.d;
+}
+
+void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
+                       qm31 alpha, uint32_t* out, cudaStream_t s) {
+    (void)len;
+    final_fold_kernel<<<1, 32, 0, s>>>(A, B, A32, B32, alpha, out);
+}
+
+__global__ void mle_fold_kernel(const uint4* src, uint4* dst, size_t h, qm31 r) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < h; i += (size_t)gridDim.x * blockDim.x) {
+        qm31 lo = ld_q(src + i), hi = ld_q(src + i + h);
+        st_q(dst + i, qadd(lo, qmul(r, qsub(hi, lo))));
+    }
+}
+
+void launch_mle_fold(const uint4* src, uint4* dst, size_t h, qm31 r, cudaStream_t s) {
+    size_t blocks = (h + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    if (blocks == 0) blocks = 1;
+    mle_fold_kernel<<<(unsigned)blocks, 256, 0, s>>>(src, dst, h, r);
+}
+
+}  // namespace zk

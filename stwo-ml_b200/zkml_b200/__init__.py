@@ -1,0 +1,434 @@
+"""B200-native GKR matmul-sumcheck prover: Python host interface.
+
+Mirrors the stwo-ml engine's interface for this path so code written against
+the reference reads the same:
+
+* ``PoseidonChannel``      -- engine/src/crypto/poseidon_channel.rs:83-306
+* ``M31Matrix``            -- engine/src/components/matmul.rs:85-116
+* ``GpuBackend``           -- the ``ZkmlOps`` trait (engine/src/backend.rs:85-107):
+  ``reduce_matmul_layer``, ``evaluate_mle_at_point``, ``restrict_mle``
+* ``MatMulReduction``      -- backend.rs:73-79
+* ``reduce_matmul_layer_with_backend`` -- engine/src/gkr/prover.rs:5959-6073
+* ``prove_gkr_matmul`` / ``commit_mle_root`` / ``prove_mle_opening`` -- the
+  single-layer GKR proof, Merkle commitment and weight opening
+  (gkr/prover.rs:1500-2251, crypto/poseidon_merkle.rs, crypto/mle_opening.rs).
+
+All compute runs in ``lib/libzkml_b200.so`` (CUDA, sm_100a) through its C ABI
+(``include/zkml_b200.h``).  There is no CPU fallback: if the library or the
+GPU is missing, the calls raise.
+
+QM31 values are numpy ``uint32`` arrays of shape ``(..., 4)`` holding
+``[a, b, c, d] = (a + b i) + (c + d i) u``; felt252 values are Python ints.
+Matrix inputs may be numpy arrays (host) or CUDA torch tensors on the
+context's device (used in place).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG.parent / "lib" / "libzkml_b200.so"
+
+M31_P = (1 << 31) - 1
+STARK_P = 2**251 + 17 * 2**192 + 1
+
+ZKML_OK = 0
+_STATUS = {1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "NCCL", 5: "TIMEOUT", 6: "UNSUPPORTED", 7: "VERIFY"}
+
+
+class ZkmlError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"zkml {_STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class InvalidArgument(ZkmlError, ValueError):
+    pass
+
+
+class _Channel(C.Structure):
+    _fields_ = [("digest", C.c_uint64 * 4), ("n_draws", C.c_uint32), ("reserved", C.c_uint32),
+                ("hash_count", C.c_uint64)]
+
+
+_u32 = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_u64 = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
+_lib = None
+_lib_lock = threading.Lock()
+
+# Every symbol include/zkml_b200.h declares, with (restype, argtypes).
+_SIGS = {
+    "zkml_abi_version": (C.c_int, []),
+    "zkml_last_error": (C.c_char_p, []),
+    "zkml_ctx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    "zkml_ctx_destroy": (C.c_int, [C.c_void_p]),
+    "zkml_ctx_device": (C.c_int, [C.c_void_p]),
+    "zkml_ctx_kernel_launches": (C.c_uint64, [C.c_void_p]),
+    "zkml_ctx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "zkml_ctx_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
+    "zkml_ctx_kernel_time": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "zkml_channel_init": (None, [C.POINTER(_Channel)]),
+    "zkml_channel_mix_u64": (None, [C.POINTER(_Channel), C.c_uint64]),
+    "zkml_channel_mix_felt": (None, [C.POINTER(_Channel), _u64]),
+    "zkml_channel_mix_qm31": (None, [C.POINTER(_Channel), _u32]),
+    "zkml_channel_draw_felt252": (None, [C.POINTER(_Channel), _u64]),
+    "zkml_channel_draw_qm31": (None, [C.POINTER(_Channel), _u32]),
+    "zkml_channel_mix_poly_coeffs": (None, [C.POINTER(_Channel), _u32]),
+    "zkml_channel_mix_poly_coeffs_deg3": (None, [C.POINTER(_Channel), _u32]),
+    "zkml_channel_mix_felts": (None, [C.POINTER(_Channel), _u32, C.c_size_t]),
+    "zkml_hades_permutation": (None, [_u64]),
+    "zkml_poseidon_hash": (None, [_u64, _u64, _u64]),
+    "zkml_poseidon_hash_many": (None, [_u64, C.c_size_t, _u64]),
+    "zkml_securefield_to_felt": (None, [_u32, _u64]),
+    "zkml_reduce_matmul_layer": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p,
+                                           C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p,
+                                           C.c_size_t, C.c_size_t, C.POINTER(_Channel), _u32, _u32, _u32,
+                                           _u32]),
+    "zkml_evaluate_mle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, _u32]),
+    "zkml_restrict_mle": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, _u32]),
+    "zkml_reduce_matmul_layer_gkr": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u32, C.c_void_p,
+                                               C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                                               C.POINTER(_Channel), _u32, _u32, _u32, _u32]),
+}
+
+
+def library_path() -> Path:
+    return Path(os.environ.get("ZKML_B200_LIB", LIB_PATH))
+
+
+def lib():
+    """Load the CUDA library (raises if it has not been built)."""
+    global _lib
+    with _lib_lock:
+        if _lib is None:
+            path = library_path()
+            if not path.exists():
+                raise ImportError(f"{path} is missing: build it with `make -C stwo-ml_b200` "
+                                  "(or __graft_entry__.build()); there is no CPU fallback")
+            L = C.CDLL(str(path))
+            for name, (res, args) in _SIGS.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def exported_symbols() -> List[str]:
+    return list(_SIGS)
+
+
+def _check(rc: int) -> None:
+    if rc != ZKML_OK:
+        msg = (lib().zkml_last_error() or b"").decode(errors="replace")
+        if rc == 1:
+            raise InvalidArgument(rc, msg)
+        raise ZkmlError(rc, msg)
+
+
+# ---------------------------------------------------------------------------
+# felt252 helpers
+# ---------------------------------------------------------------------------
+
+def felt_to_limbs(x: int) -> np.ndarray:
+    x %= STARK_P
+    return np.array([(x >> (64 * i)) & (2**64 - 1) for i in range(4)], dtype=np.uint64)
+
+
+def limbs_to_felt(a) -> int:
+    return sum(int(a[i]) << (64 * i) for i in range(4))
+
+
+def qm31(a: int, b: int = 0, c: int = 0, d: int = 0) -> np.ndarray:
+    return np.array([a, b, c, d], dtype=np.uint32)
+
+
+def as_qm31_array(x) -> np.ndarray:
+    arr = np.ascontiguousarray(np.asarray(x, dtype=np.uint32))
+    if arr.size == 0:
+        return np.zeros((0, 4), np.uint32)
+    return arr.reshape(-1, 4)
+
+
+def poseidon_hash(a: int, b: int) -> int:
+    out = np.zeros(4, np.uint64)
+    lib().zkml_poseidon_hash(felt_to_limbs(a), felt_to_limbs(b), out)
+    return limbs_to_felt(out)
+
+
+def poseidon_hash_many(xs: Sequence[int]) -> int:
+    arr = np.concatenate([felt_to_limbs(x) for x in xs]) if len(xs) else np.zeros(4, np.uint64)
+    out = np.zeros(4, np.uint64)
+    lib().zkml_poseidon_hash_many(arr, len(xs), out)
+    return limbs_to_felt(out)
+
+
+def hades_permutation(state: Sequence[int]) -> List[int]:
+    st = np.concatenate([felt_to_limbs(x) for x in state])
+    lib().zkml_hades_permutation(st)
+    return [limbs_to_felt(st[4 * i:4 * i + 4]) for i in range(3)]
+
+
+def securefield_to_felt(v) -> int:
+    out = np.zeros(4, np.uint64)
+    lib().zkml_securefield_to_felt(np.ascontiguousarray(v, np.uint32).reshape(4), out)
+    return limbs_to_felt(out)
+
+
+# ---------------------------------------------------------------------------
+# PoseidonChannel
+# ---------------------------------------------------------------------------
+
+class PoseidonChannel:
+    """Host Fiat-Shamir channel (transcript-compatible with the engine's)."""
+
+    def __init__(self):
+        self._st = _Channel()
+        lib().zkml_channel_init(C.byref(self._st))
+
+    def clone(self) -> "PoseidonChannel":
+        c = PoseidonChannel()
+        C.memmove(C.byref(c._st), C.byref(self._st), C.sizeof(_Channel))
+        return c
+
+    @property
+    def state(self) -> _Channel:
+        return self._st
+
+    def digest(self) -> int:
+        return limbs_to_felt(self._st.digest)
+
+    def n_draws(self) -> int:
+        return int(self._st.n_draws)
+
+    def hash_count(self) -> int:
+        return int(self._st.hash_count)
+
+    def mix_u64(self, v: int) -> None:
+        lib().zkml_channel_mix_u64(C.byref(self._st), v)
+
+    def mix_felt(self, v: int) -> None:
+        lib().zkml_channel_mix_felt(C.byref(self._st), felt_to_limbs(v))
+
+    def mix_secure_field(self, v) -> None:
+        lib().zkml_channel_mix_qm31(C.byref(self._st), np.ascontiguousarray(v, np.uint32).reshape(4))
+
+    def draw_felt252(self) -> int:
+        out = np.zeros(4, np.uint64)
+        lib().zkml_channel_draw_felt252(C.byref(self._st), out)
+        return limbs_to_felt(out)
+
+    def draw_qm31(self) -> np.ndarray:
+        out = np.zeros(4, np.uint32)
+        lib().zkml_channel_draw_qm31(C.byref(self._st), out)
+        return out
+
+    def draw_qm31s(self, n: int) -> np.ndarray:
+        return np.stack([self.draw_qm31() for _ in range(n)]) if n else np.zeros((0, 4), np.uint32)
+
+    def mix_poly_coeffs(self, c0, c1, c2) -> None:
+        lib().zkml_channel_mix_poly_coeffs(C.byref(self._st), np.concatenate([c0, c1, c2]).astype(np.uint32))
+
+    def mix_poly_coeffs_deg3(self, c0, c1, c2, c3) -> None:
+        lib().zkml_channel_mix_poly_coeffs_deg3(C.byref(self._st),
+                                                np.concatenate([c0, c1, c2, c3]).astype(np.uint32))
+
+    def mix_felts(self, felts) -> None:
+        arr = as_qm31_array(felts)
+        lib().zkml_channel_mix_felts(C.byref(self._st), arr.reshape(-1) if arr.size else np.zeros(4, np.uint32),
+                                     len(arr))
+
+
+# ---------------------------------------------------------------------------
+# Data types
+# ---------------------------------------------------------------------------
+
+@dataclass
+class M31Matrix:
+    """Row-major, unpadded M31 matrix (components/matmul.rs:85-116)."""
+    rows: int
+    cols: int
+    data: object  # numpy uint32 (rows*cols) or a CUDA tensor of int32/uint32
+
+    @staticmethod
+    def from_numpy(a: np.ndarray) -> "M31Matrix":
+        a = np.ascontiguousarray(a, dtype=np.uint32)
+        return M31Matrix(a.shape[0], a.shape[1], a.reshape(-1))
+
+
+@dataclass
+class RoundPoly:
+    c0: np.ndarray
+    c1: np.ndarray
+    c2: np.ndarray
+
+
+@dataclass
+class MatMulReduction:
+    round_polys: List[RoundPoly]
+    challenges: np.ndarray
+    final_a_eval: np.ndarray
+    final_b_eval: np.ndarray
+
+
+@dataclass
+class GKRClaim:
+    point: np.ndarray
+    value: np.ndarray
+
+
+def _next_pow2(x: int) -> int:
+    return 1 << max(0, (x - 1).bit_length())
+
+
+def _log2(x: int) -> int:
+    return x.bit_length() - 1
+
+
+# ---------------------------------------------------------------------------
+# Device context (GpuSumcheckExecutor::cached equivalent)
+# ---------------------------------------------------------------------------
+
+class Context:
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().zkml_ctx_create(device, C.byref(h)))
+        self.handle = h
+        self.device = device
+
+    def close(self) -> None:
+        if self.handle:
+            lib().zkml_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def kernel_launches(self) -> int:
+        return int(lib().zkml_ctx_kernel_launches(self.handle))
+
+    def enable_timing(self, enable: bool = True) -> None:
+        _check(lib().zkml_ctx_enable_timing(self.handle, int(enable)))
+
+    def kernel_time(self, kernel: str) -> Tuple[float, int]:
+        ms = C.c_double(0)
+        n = C.c_uint64(0)
+        _check(lib().zkml_ctx_kernel_time(self.handle, kernel.encode(), C.byref(ms), C.byref(n)))
+        return ms.value, n.value
+
+    def set_stream(self, stream_ptr: Optional[int]) -> None:
+        _check(lib().zkml_ctx_set_stream(self.handle, C.c_void_p(stream_ptr or 0)))
+
+
+_contexts = {}
+
+
+def context(device: int = 0) -> Context:
+    if device not in _contexts:
+        _contexts[device] = Context(device)
+    return _contexts[device]
+
+
+class _Buf:
+    """Pointer + keep-alive for a host numpy array or a device tensor."""
+
+    def __init__(self, x, dtype=np.uint32):
+        self.keep = None
+        if hasattr(x, "data_ptr") and hasattr(x, "is_cuda"):
+            if x.is_cuda:
+                if not x.is_contiguous():
+                    raise InvalidArgument(1, "device tensor must be contiguous")
+                self.keep = x
+                self.ptr = C.c_void_p(x.data_ptr())
+                self.nbytes = x.numel() * x.element_size()
+                return
+            x = x.numpy()
+        arr = np.ascontiguousarray(x, dtype=dtype)
+        self.keep = arr
+        self.ptr = C.c_void_p(arr.ctypes.data) if arr.size else C.c_void_p(0)
+        self.nbytes = arr.nbytes
+
+
+def _qm31_ptr(x) -> Tuple[C.c_void_p, np.ndarray]:
+    arr = as_qm31_array(x)
+    if arr.size == 0:
+        arr = np.zeros((1, 4), np.uint32)
+        return C.c_void_p(0), arr
+    return C.c_void_p(arr.ctypes.data), arr
+
+
+class GpuBackend:
+    """``ZkmlOps`` on the B200 (engine/src/backend.rs:85-107)."""
+
+    def __init__(self, device: int = 0):
+        self.ctx = context(device)
+
+    def reduce_matmul_layer(self, a: M31Matrix, b: M31Matrix, r_i, r_j, pk: int,
+                            channel: PoseidonChannel) -> MatMulReduction:
+        log_k = _log2(pk) if pk > 0 else 0
+        r_i_p, r_i_k = _qm31_ptr(r_i)
+        r_j_p, r_j_k = _qm31_ptr(r_j)
+        n_ri = len(as_qm31_array(r_i))
+        n_rj = len(as_qm31_array(r_j))
+        abuf, bbuf = _Buf(a.data), _Buf(b.data)
+        rp = np.zeros((max(log_k, 1), 12), np.uint32)
+        ch = np.zeros((max(log_k, 1), 4), np.uint32)
+        fa = np.zeros(4, np.uint32)
+        fb = np.zeros(4, np.uint32)
+        _check(lib().zkml_reduce_matmul_layer(self.ctx.handle, abuf.ptr, a.rows, a.cols, bbuf.ptr, b.rows, b.cols,
+                                              r_i_p, n_ri, r_j_p, n_rj, pk, C.byref(channel.state),
+                                              rp.reshape(-1), ch.reshape(-1), fa, fb))
+        polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_k)]
+        return MatMulReduction(polys, ch[:log_k].copy(), fa, fb)
+
+    def evaluate_mle_at_point(self, mle, point) -> np.ndarray:
+        buf = _Buf(mle)
+        p_ptr, p_keep = _qm31_ptr(point)
+        n_vars = len(as_qm31_array(point))
+        out = np.zeros(4, np.uint32)
+        _check(lib().zkml_evaluate_mle(self.ctx.handle, buf.ptr, n_vars, p_ptr, out))
+        return out
+
+    def restrict_mle(self, mle, assignments) -> np.ndarray:
+        buf = _Buf(mle)
+        n_evals = buf.nbytes // 16
+        p_ptr, p_keep = _qm31_ptr(assignments)
+        n_assign = len(as_qm31_array(assignments))
+        out = np.zeros((max(n_evals >> n_assign, 1), 4), np.uint32)
+        _check(lib().zkml_restrict_mle(self.ctx.handle, buf.ptr, n_evals, p_ptr, n_assign, out.reshape(-1)))
+        return out[:n_evals >> n_assign]
+
+
+def reduce_matmul_layer_with_backend(output_claim: GKRClaim, a: M31Matrix, b: M31Matrix, m: int, k: int, n: int,
+                                     channel: PoseidonChannel, backend: Optional[GpuBackend] = None
+                                     ) -> Tuple[MatMulReduction, GKRClaim]:
+    """gkr/prover.rs:5959-6073 -- transcript wrapper around ``reduce_matmul_layer``."""
+    backend = backend or GpuBackend()
+    pm, pk, pn = _next_pow2(a.rows), _next_pow2(a.cols), _next_pow2(b.cols)
+    log_m, log_k, log_n = _log2(pm), _log2(pk), _log2(pn)
+    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
+    n_point = len(as_qm31_array(output_claim.point))
+    abuf, bbuf = _Buf(a.data), _Buf(b.data)
+    rp = np.zeros((max(log_k, 1), 12), np.uint32)
+    fa = np.zeros(4, np.uint32)
+    fb = np.zeros(4, np.uint32)
+    nxt = np.zeros((max(log_m + log_k, 1), 4), np.uint32)
+    if (a.rows, a.cols, b.cols) != (m, k, n) or b.rows != k:
+        raise InvalidArgument(1, "matrix shapes do not match (m, k, n)")
+    _check(lib().zkml_reduce_matmul_layer_gkr(backend.ctx.handle, pt_ptr, n_point,
+                                              np.ascontiguousarray(output_claim.value, np.uint32).reshape(4),
+                                              abuf.ptr, m, k, bbuf.ptr, n, C.byref(channel.state),
+                                              rp.reshape(-1), fa, fb, nxt.reshape(-1)))
+    polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_k)]
+    red = MatMulReduction(polys, nxt[log_m:log_m + log_k].copy(), fa, fb)
+    return red, GKRClaim(nxt[:log_m + log_k].copy(), fa.copy())

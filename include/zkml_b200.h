@@ -72,7 +72,8 @@ uint64_t zkml_ctx_kernel_launches(const zkml_ctx *ctx);
  * each launch of the named kernel class is bracketed by events on the
  * context's stream; zkml_ctx_kernel_time returns the accumulated milliseconds
  * and launch count.  Kernel classes: "restrict_cols", "restrict_rows",
- * "sumcheck_round", "merkle". */
+ * "sumcheck_round", "merkle"; and two host-side phases timed by wall clock:
+ * "host_sync" (waiting for round results) and "host_channel" (Fiat-Shamir). */
 int zkml_ctx_enable_timing(zkml_ctx *ctx, int enable);
 int zkml_ctx_kernel_time(zkml_ctx *ctx, const char *kernel, double *out_ms, uint64_t *out_launches);
 /* Replace the context's stream with a caller-owned cudaStream_t (NULL = own stream). */
@@ -136,6 +137,41 @@ int zkml_reduce_matmul_layer_gkr(zkml_ctx *ctx, const uint32_t *claim_point, siz
                                  size_t k, const uint32_t *b, size_t n, zkml_channel *ch,
                                  uint32_t *out_round_polys, uint32_t out_final_a[4],
                                  uint32_t out_final_b[4], uint32_t *out_next_point);
+
+/* ---- Poseidon-252 Merkle commitment and MLE opening (engine/src/crypto) ----- */
+
+/* commit_mle_root_only (crypto/mle_opening.rs:630-642): root of the Poseidon
+ * Merkle tree whose leaves are securefield_to_felt(evals[i]), zero-padded to a
+ * power of two (at least 2); internal node = poseidon_hash(left, right)
+ * (crypto/poseidon_merkle.rs:91-130). */
+int zkml_commit_mle_root(zkml_ctx *ctx, const uint32_t *evals, size_t n, uint64_t out_root[4]);
+
+/* prove_mle_opening_with_commitment (crypto/mle_opening.rs:1654-1916) for an
+ * MLE of 2^n_vars QM31 at `point` (n_vars QM31).  Mixes the commitment and the
+ * intermediate roots into `ch`, draws min(n_queries, 2^(n_vars-1)) queries
+ * (STWO_MLE_N_QUERIES, default 10) and writes the proof serialized as
+ * cairo_serde::serialize_mle_opening_proof (cairo_serde.rs:341-369) into
+ * out_calldata (cap felts; *out_len receives the felt count, also when the
+ * buffer is too small, which returns ZKML_ERR_INVALID_ARG). */
+int zkml_prove_mle_opening(zkml_ctx *ctx, const uint32_t *evals, size_t n_vars, const uint32_t *point,
+                           zkml_channel *ch, size_t n_queries, uint64_t out_commitment[4],
+                           uint64_t *out_calldata, size_t cap, size_t *out_len);
+
+/* compute_io_commitment (engine/src/aggregation.rs:235-254). Host only. */
+int zkml_io_commitment(const uint32_t *input, size_t in_rows, size_t in_cols, const uint32_t *output,
+                       size_t out_rows, size_t out_cols, uint64_t out[4]);
+
+/* prove_gkr (gkr/prover.rs:1500-2251) for the one-layer circuit
+ * GraphBuilder::new((m, k)).linear(n) with Sequential weight binding, from a
+ * fresh PoseidonChannel: seeding (depth, input shape, optional policy
+ * commitment; pass NULL to skip it, as STWO_SKIP_POLICY_COMMITMENT does),
+ * output claim, the MatMul reduction, the weight-MLE opening and the IO
+ * commitment.  The proof is written as cairo_serde::serialize_gkr_model_proof
+ * (cairo_serde.rs:1307-1772) into out_calldata; out_digest receives the final
+ * channel digest and out_io the IO commitment. */
+int zkml_prove_gkr_matmul(zkml_ctx *ctx, const uint32_t *input, size_t m, size_t k, const uint32_t *weight,
+                          size_t n, const uint64_t *policy, size_t n_queries, uint64_t *out_calldata,
+                          size_t cap, size_t *out_len, uint64_t out_digest[4], uint64_t out_io[4]);
 
 #ifdef __cplusplus
 }

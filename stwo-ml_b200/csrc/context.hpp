@@ -32,7 +32,21 @@ struct DevBuf {
     }
 };
 
-enum KernelClass { KC_RESTRICT_COLS = 0, KC_RESTRICT_ROWS = 1, KC_ROUND = 2, KC_MERKLE = 3 };
+// Called once with the claimed sum of the reduction (p(0) + p(1) of round 0,
+// or f_a * f_b when there are no rounds) before any round touches the channel.
+struct ClaimHook {
+    void (*fn)(void* arg, const qm31& claimed_sum);
+    void* arg;
+};
+
+int reduce_matmul_internal(::zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size_t a_cols, const uint32_t* b,
+                           size_t b_rows, size_t b_cols, const uint32_t* r_i, size_t n_ri, const uint32_t* r_j,
+                           size_t n_rj, size_t pk, zkml_channel* ch, uint32_t* out_round_polys,
+                           uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
+                           const ClaimHook* hook);
+
+enum KernelClass { KC_RESTRICT_COLS = 0, KC_RESTRICT_ROWS = 1, KC_ROUND = 2, KC_MERKLE = 3, KC_HOST_SYNC = 4,
+                   KC_HOST_CHANNEL = 5 };
 
 // Brackets one launch of a kernel class with events when timing is enabled.
 struct KTimer {
@@ -65,7 +79,7 @@ struct zkml_ctx {
         double ms = 0;
         uint64_t launches = 0;
     };
-    KTime ktime[4];  // restrict_cols, restrict_rows, sumcheck_round, merkle
+    KTime ktime[6];  // restrict_cols, restrict_rows, sumcheck_round, merkle, host_sync, host_channel
     // Event pairs recorded but not yet read; read after the next stream sync so
     // timing never adds a host wait of its own.
     struct PendingEv {

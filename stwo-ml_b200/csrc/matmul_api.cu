@@ -4,6 +4,7 @@
 // advanced here, on the host, between kernel launches; each sumcheck round is
 // one kernel (fold of the previous round fused with this round's sums, grid
 // reduction included) followed by a 48-byte device-to-host read.
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -11,6 +12,7 @@
 
 #include "channel.hpp"
 #include "context.hpp"
+#include "merkle.cuh"
 
 namespace zk {
 
@@ -89,6 +91,21 @@ static void drain_timers(zkml_ctx* ctx) {
     ctx->pending.clear();
 }
 
+// Host wall-time accumulator for a pseudo kernel class (timing mode only).
+struct HostTimer {
+    zkml_ctx* ctx;
+    int cls;
+    std::chrono::steady_clock::time_point t0;
+    HostTimer(zkml_ctx* c, int k) : ctx(c), cls(k) {
+        if (ctx->timing) t0 = std::chrono::steady_clock::now();
+    }
+    ~HostTimer() {
+        if (!ctx->timing) return;
+        ctx->ktime[cls].ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        ctx->ktime[cls].launches++;
+    }
+};
+
 static inline bool is_pow2(size_t x) { return x && !(x & (x - 1)); }
 static inline size_t next_pow2(size_t x) {
     size_t p = 1;
@@ -151,8 +168,10 @@ static void interpolate(const uint32_t* s12, qm31& c0, qm31& c1, qm31& c2) {
 
 // Reads `words` u32 of the context's out buffer (plus the error flag) to the host.
 static int read_out(zkml_ctx* ctx, size_t words) {
-    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 16, ctx->out_words(), words * 4, cudaMemcpyDeviceToHost, ctx->stream));
-    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 48, ctx->err_flag(), 4, cudaMemcpyDeviceToHost, ctx->stream));
+    (void)words;
+    HostTimer ht(ctx, KC_HOST_SYNC);
+    // out words (16..47) and the error flag (48) are contiguous: one copy
+    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 16, ctx->out_words(), 33 * 4, cudaMemcpyDeviceToHost, ctx->stream));
     ZK_CUDA(cudaStreamSynchronize(ctx->stream));
     if (!ctx->pending.empty()) drain_timers(ctx);
     return ZKML_OK;
@@ -161,7 +180,8 @@ static int read_out(zkml_ctx* ctx, size_t words) {
 // The sumcheck round loop over (A, B).  In M31 mode A32/B32 hold the base-field
 // vectors (length len) and the first fold writes QM31 into ctx->fa / fb.
 int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
-                 zkml_channel* chs, uint32_t* out_rp, uint32_t* out_ch, uint32_t* fa_out, uint32_t* fb_out) {
+                 zkml_channel* chs, uint32_t* out_rp, uint32_t* out_ch, uint32_t* fa_out, uint32_t* fb_out,
+                 const ClaimHook* hook) {
     Channel ch(chs);
     cudaStream_t s = ctx->stream;
     const RoundScratch rs = ctx->round_scratch();
@@ -180,6 +200,7 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             ZK_CUDA(cudaMemcpyAsync(fb_out, B, 16, cudaMemcpyDeviceToHost, s));
             ZK_CUDA(cudaStreamSynchronize(s));
         }
+        if (hook) hook->fn(hook->arg, qmul(ldq(fa_out), ldq(fb_out)));
         return ZKML_OK;
     }
     {
@@ -194,15 +215,19 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
         int rc = read_out(ctx, 12);
         if (rc) return rc;
         if (r == 0 && (rc = check_err_flag(ctx, "reduce_matmul_layer"))) return rc;
-        qm31 c0, c1, c2;
-        interpolate(ctx->h_small + 16, c0, c1, c2);
+        if (r == 0 && hook) hook->fn(hook->arg, qadd(ldq(ctx->h_small + 16), ldq(ctx->h_small + 20)));
+        qm31 c0, c1, c2, alpha;
+        {
+            HostTimer ht(ctx, KC_HOST_CHANNEL);
+            interpolate(ctx->h_small + 16, c0, c1, c2);
+            ch.mix_poly_coeffs(c0, c1, c2);
+            alpha = ch.draw_qm31();
+        }
         if (out_rp) {
             stq(out_rp + 12 * r, c0);
             stq(out_rp + 12 * r + 4, c1);
             stq(out_rp + 12 * r + 8, c2);
         }
-        ch.mix_poly_coeffs(c0, c1, c2);
-        const qm31 alpha = ch.draw_qm31();
         if (out_ch) stq(out_ch + 4 * r, alpha);
         KTimer t(ctx, KC_ROUND);
         if (len == 2) {
@@ -307,6 +332,11 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     if (!rc) rc = ctx->small.ensure(64 * 4);
     if (!rc && (e = cudaMemset(ctx->small.ptr, 0, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMemset");
     if (!rc && (e = cudaMallocHost(&ctx->h_small, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMallocHost");
+    if (!rc) {
+        // Hades round keys and Montgomery constants into this device's constant bank
+        const felt two = f_from_u64(2);
+        if ((e = upload_hades_constants(HADES_RC, &F_R2, &two)) != cudaSuccess) rc = cuda_error(e, "upload constants");
+    }
     if (rc) {
         zkml_ctx_destroy(ctx);
         return rc;
@@ -346,12 +376,13 @@ int zkml_ctx_enable_timing(zkml_ctx* ctx, int enable) {
 
 int zkml_ctx_kernel_time(zkml_ctx* ctx, const char* kernel, double* out_ms, uint64_t* out_launches) {
     if (!ctx || !kernel) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
-    static const char* names[4] = {"restrict_cols", "restrict_rows", "sumcheck_round", "merkle"};
+    static const char* names[6] = {"restrict_cols", "restrict_rows", "sumcheck_round",
+                                   "merkle",        "host_sync",     "host_channel"};
     if (!ctx->pending.empty()) {
         ZK_CUDA(cudaStreamSynchronize(ctx->stream));
         drain_timers(ctx);
     }
-    for (int i = 0; i < 4; i++)
+    for (int i = 0; i < 6; i++)
         if (!strcmp(kernel, names[i])) {
             if (out_ms) *out_ms = ctx->ktime[i].ms;
             if (out_launches) *out_launches = ctx->ktime[i].launches;
@@ -370,6 +401,18 @@ int zkml_reduce_matmul_layer(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, si
                              size_t b_rows, size_t b_cols, const uint32_t* r_i, size_t n_ri, const uint32_t* r_j,
                              size_t n_rj, size_t pk, zkml_channel* ch, uint32_t* out_round_polys,
                              uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4]) {
+    return zk::reduce_matmul_internal(ctx, a, a_rows, a_cols, b, b_rows, b_cols, r_i, n_ri, r_j, n_rj, pk, ch,
+                                      out_round_polys, out_challenges, out_final_a, out_final_b, nullptr);
+}
+
+}  // extern "C"
+
+namespace zk {
+int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size_t a_cols, const uint32_t* b,
+                           size_t b_rows, size_t b_cols, const uint32_t* r_i, size_t n_ri, const uint32_t* r_j,
+                           size_t n_rj, size_t pk, zkml_channel* ch, uint32_t* out_round_polys,
+                           uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
+                           const ClaimHook* hook) {
     if (!ctx || !a || !b || !ch || !out_final_a || !out_final_b)
         return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (a_rows == 0 || a_cols == 0 || b_cols == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty matrix");
@@ -395,16 +438,19 @@ int zkml_reduce_matmul_layer(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, si
     if (n_ri == 0 && n_rj == 0 && pk == a_cols && pk >= 4) {
         if ((rc = ctx->fa.ensure(pk / 2 * 16)) || (rc = ctx->fb.ensure(pk / 2 * 16))) return rc;
         return run_sumcheck(ctx, nullptr, nullptr, Ad, Bd, pk, ch, out_round_polys, out_challenges, out_final_a,
-                            out_final_b);
+                            out_final_b, hook);
     }
     rc = restrict_ab(ctx, Ad, a_rows, a_cols, Bd, b_cols, reinterpret_cast<const qm31*>(r_i), (unsigned)n_ri,
                      reinterpret_cast<const qm31*>(r_j), (unsigned)n_rj, pk);
     if (rc) return rc;
     rc = run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, pk, ch, out_round_polys,
-                      out_challenges, out_final_a, out_final_b);
+                      out_challenges, out_final_a, out_final_b, hook);
     if (rc) return rc;
     return check_err_flag(ctx, "reduce_matmul_layer");
 }
+}  // namespace zk
+
+extern "C" {
 
 int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n_point,
                                  const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k,

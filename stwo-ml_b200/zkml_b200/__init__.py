@@ -96,6 +96,13 @@ _SIGS = {
     "zkml_reduce_matmul_layer_gkr": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u32, C.c_void_p,
                                                C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                                C.POINTER(_Channel), _u32, _u32, _u32, _u32]),
+    "zkml_commit_mle_root": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u64]),
+    "zkml_prove_mle_opening": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.POINTER(_Channel),
+                                         C.c_size_t, _u64, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "zkml_io_commitment": (C.c_int, [_u32, C.c_size_t, C.c_size_t, _u32, C.c_size_t, C.c_size_t, _u64]),
+    "zkml_prove_gkr_matmul": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                                        C.c_void_p, C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t), _u64,
+                                        _u64]),
 }
 
 
@@ -353,6 +360,8 @@ class _Buf:
                 self.nbytes = x.numel() * x.element_size()
                 return
             x = x.numpy()
+            if x.dtype in (np.int32, np.uint32) and x.flags.c_contiguous:
+                x = x.view(np.uint32)  # no copy: keeps pinned host memory pinned
         arr = np.ascontiguousarray(x, dtype=dtype)
         self.keep = arr
         self.ptr = C.c_void_p(arr.ctypes.data) if arr.size else C.c_void_p(0)
@@ -432,3 +441,98 @@ def reduce_matmul_layer_with_backend(output_claim: GKRClaim, a: M31Matrix, b: M3
     polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_k)]
     red = MatMulReduction(polys, nxt[log_m:log_m + log_k].copy(), fa, fb)
     return red, GKRClaim(nxt[:log_m + log_k].copy(), fa.copy())
+
+
+# ---------------------------------------------------------------------------
+# Merkle commitment, MLE opening, single-layer GKR proof
+# ---------------------------------------------------------------------------
+
+DEFAULT_MLE_N_QUERIES = 10  # STWO_MLE_N_QUERIES default (crypto/mle_opening.rs:42-58)
+
+
+def mle_n_queries() -> int:
+    """STWO_MLE_N_QUERIES (2..=20, default 10), as the reference reads it."""
+    try:
+        v = int(os.environ.get("STWO_MLE_N_QUERIES", ""))
+        if 2 <= v <= 20:
+            return v
+    except ValueError:
+        pass
+    return DEFAULT_MLE_N_QUERIES
+
+
+def _felts(buf: np.ndarray, n: int) -> List[int]:
+    return [limbs_to_felt(buf[4 * i:4 * i + 4]) for i in range(n)]
+
+
+def commit_mle_root(evals, device: int = 0) -> int:
+    """commit_mle_root_only: Poseidon Merkle root of QM31 evaluations."""
+    buf = _Buf(evals)
+    out = np.zeros(4, np.uint64)
+    _check(lib().zkml_commit_mle_root(context(device).handle, buf.ptr, buf.nbytes // 16, out))
+    return limbs_to_felt(out)
+
+
+@dataclass
+class MleOpening:
+    commitment: int
+    calldata: List[int]  # serialize_mle_opening_proof layout
+
+
+def prove_mle_opening(evals, point, channel: PoseidonChannel, n_queries: Optional[int] = None,
+                      device: int = 0) -> MleOpening:
+    """prove_mle_opening_with_commitment (crypto/mle_opening.rs:1654-1916)."""
+    buf = _Buf(evals)
+    n_evals = buf.nbytes // 16
+    n_vars = n_evals.bit_length() - 1
+    if n_evals != 1 << n_vars:
+        raise InvalidArgument(1, "MLE length must be a power of two")
+    p_ptr, p_keep = _qm31_ptr(point)
+    nq = mle_n_queries() if n_queries is None else n_queries
+    cap = 64 + (nq + 1) * (2 + n_vars * (10 + 2 * (n_vars + 1)))
+    out = np.zeros(4 * cap, np.uint64)
+    com = np.zeros(4, np.uint64)
+    ln = C.c_size_t(0)
+    _check(lib().zkml_prove_mle_opening(context(device).handle, buf.ptr, n_vars, p_ptr, C.byref(channel.state), nq,
+                                        com, out, cap, C.byref(ln)))
+    return MleOpening(limbs_to_felt(com), _felts(out, ln.value))
+
+
+def io_commitment(inp: np.ndarray, out: np.ndarray) -> int:
+    inp = np.ascontiguousarray(inp, np.uint32)
+    out = np.ascontiguousarray(out, np.uint32)
+    res = np.zeros(4, np.uint64)
+    _check(lib().zkml_io_commitment(inp.reshape(-1), inp.shape[0], inp.shape[1], out.reshape(-1), out.shape[0],
+                                    out.shape[1], res))
+    return limbs_to_felt(res)
+
+
+@dataclass
+class GKRMatMulProof:
+    calldata: List[int]  # serialize_gkr_model_proof
+    final_digest: int
+    io_commitment: int
+    raw: np.ndarray       # calldata as 4 x u64 limbs per felt
+
+
+def prove_gkr_matmul(inp: M31Matrix, weight: M31Matrix, policy_commitment: Optional[int] = None,
+                     n_queries: Optional[int] = None, device: int = 0) -> GKRMatMulProof:
+    """prove_gkr for GraphBuilder::new((m, k)).linear(n), Sequential weight binding."""
+    ibuf, wbuf = _Buf(inp.data), _Buf(weight.data)
+    m, k, n = inp.rows, inp.cols, weight.cols
+    if weight.rows != k:
+        raise InvalidArgument(1, "weight rows must equal input cols")
+    nq = mle_n_queries() if n_queries is None else n_queries
+    nv = _log2(_next_pow2(n)) + _log2(_next_pow2(k))
+    cap = 256 + 24 * (_log2(_next_pow2(k)) + _log2(_next_pow2(m))) + (nq + 1) * (2 + nv * (10 + 2 * (nv + 1)))
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    dig = np.zeros(4, np.uint64)
+    io = np.zeros(4, np.uint64)
+    pol = None
+    if policy_commitment:
+        pol = felt_to_limbs(policy_commitment)
+    _check(lib().zkml_prove_gkr_matmul(context(device).handle, ibuf.ptr, m, k, wbuf.ptr, n,
+                                       C.c_void_p(pol.ctypes.data) if pol is not None else None, nq, buf, cap,
+                                       C.byref(ln), dig, io))
+    return GKRMatMulProof(_felts(buf, ln.value), limbs_to_felt(dig), limbs_to_felt(io), buf[:4 * ln.value].copy())

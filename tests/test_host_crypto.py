@@ -111,3 +111,12 @@ def test_draw_qm31_reduces_2_31_minus_1():
     ch = Z.PoseidonChannel()
     for _ in range(200):
         assert (ch.draw_qm31() < Z.M31_P).all()
+
+
+def test_io_commitment_matches_oracle():
+    inp = np.array([[1, 2, 3, 4]], np.uint32)
+    out = np.array([[50, 60]], np.uint32)
+    ref = np.zeros(4, np.uint64)
+    O.lib().orc_io_commitment(inp.reshape(-1), 1, 4, out.reshape(-1), 1, 2, ref)
+    assert Z.io_commitment(inp, out) == O.felt_int(ref)
+    assert Z.io_commitment(inp, out) == int(GOLD["sp3_matmul_only"]["io_commitment"], 16)

@@ -1050,7 +1050,11 @@ static int verify_opening(const fe *commitment, felt_in *in, const q31 *point, s
     ch_mix(ch, commitment);
     for (size_t i = 0; i < n_inter; i++) ch_mix(ch, &inter[i]);
     size_t nq = in_u64(in);
-    if (n_rounds == 0) return nq == 0;
+    if (n_rounds == 0) {
+        q31 fv = in_qm31(in);
+        if (final_out) *final_out = fv;
+        return nq == 0 && !in->bad;
+    }
     size_t half_n = (size_t)1 << (n_rounds - 1);
     size_t exp_q = n_queries_cfg < half_n ? n_queries_cfg : half_n;
     if (nq != exp_q) return 0;

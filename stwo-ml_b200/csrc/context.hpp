@@ -34,9 +34,13 @@ struct DevBuf {
 
 // Called once with the claimed sum of the reduction (p(0) + p(1) of round 0,
 // or f_a * f_b when there are no rounds) before any round touches the channel.
+// `overlap`, if set, runs on the host right after the first GPU launches
+// (before the host waits for the first round), for transcript work that does
+// not depend on GPU results.
 struct ClaimHook {
     void (*fn)(void* arg, const qm31& claimed_sum);
     void* arg;
+    void (*overlap)(void* arg) = nullptr;
 };
 
 int reduce_matmul_internal(::zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size_t a_cols, const uint32_t* b,
@@ -72,6 +76,9 @@ struct zkml_ctx {
     zk::DevBuf partials;            // per-block round partials
     zk::DevBuf small;               // ticket + out words + error flag
     uint32_t* h_small = nullptr;    // pinned host mirror of `small`
+    uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
+    uint32_t* d_sig = nullptr;      // device alias of h_sig
+    uint32_t sig_seq = 0;           // last sequence number handed to a kernel
     int max_round_blocks = 0;
     // optional per-kernel-class event timing
     bool timing = false;
@@ -98,6 +105,8 @@ struct zkml_ctx {
         r.ticket = ticket();
         r.out = out_words();
         r.max_blocks = max_round_blocks;
+        r.sig = nullptr;
+        r.seq = 0;
         return r;
     }
 };

@@ -43,6 +43,12 @@ struct RoundScratch {
     unsigned int* ticket;  // zero-initialised
     uint32_t* out;       // >= 16 u32
     int max_blocks;
+    // Optional host signal: device alias of mapped pinned host memory.  When
+    // set, the grid's last block also writes the result words to sig[1..] and
+    // then publishes `seq` in sig[0] (system-scope release), so the host can
+    // spin on sig[0] instead of synchronising the stream.
+    uint32_t* sig;
+    uint32_t seq;
 };
 // Round sums over QM31 vectors of length len (no fold).
 void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s);
@@ -58,7 +64,7 @@ void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm3
 // Final fold of length-2 vectors to one value each: out[0..4) = a, out[4..8) = b.
 // src_m31 selects M31 inputs (A32, B32) instead of QM31 (A, B).
 void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,
-                       size_t len, qm31 alpha, uint32_t* out, cudaStream_t s);
+                       size_t len, qm31 alpha, uint32_t* out, uint32_t* sig, uint32_t seq, cudaStream_t s);
 
 // ---- generic MLE ops (ZkmlOps::evaluate_mle_at_point / restrict_mle) ----------
 // dst[i] = src[i] + r (src[i + h] - src[i]) for i < h (dst may alias src).

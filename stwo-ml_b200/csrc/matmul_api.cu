@@ -4,7 +4,9 @@
 // advanced here, on the host, between kernel launches; each sumcheck round is
 // one kernel (fold of the previous round fused with this round's sums, grid
 // reduction included) followed by a 48-byte device-to-host read.
+#include <atomic>
 #include <chrono>
+#include <x86intrin.h>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -166,12 +168,32 @@ static void interpolate(const uint32_t* s12, qm31& c0, qm31& c1, qm31& c2) {
     c1 = qsub(qsub(s1, s0), c2);
 }
 
-// Reads `words` u32 of the context's out buffer (plus the error flag) to the host.
-static int read_out(zkml_ctx* ctx, size_t words) {
-    (void)words;
+// Waits until a kernel publishes `seq` in the mapped signal words, then copies
+// `n` result words out.  Polls the stream for errors while waiting and gives up
+// after a bounded time, so a failed launch never leaves the host spinning.
+static int wait_signal(zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n) {
     HostTimer ht(ctx, KC_HOST_SYNC);
-    // out words (16..47) and the error flag (48) are contiguous: one copy
-    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 16, ctx->out_words(), 33 * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    volatile uint32_t* sig = ctx->h_sig;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (uint64_t it = 0; sig[0] != seq; it++) {
+        _mm_pause();
+        if ((it & 1023) == 1023) {
+            cudaError_t e = cudaStreamQuery(ctx->stream);
+            if (e != cudaSuccess && e != cudaErrorNotReady) return cuda_error(e, "round kernel");
+            const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            if (e == cudaSuccess && sig[0] != seq && waited > 1.0)
+                return set_error(ZKML_ERR_CUDA, "round kernel finished without publishing its result");
+            if (waited > 120.0) return set_error(ZKML_ERR_TIMEOUT, "timed out waiting for a round kernel");
+        }
+    }
+    std::atomic_thread_fence(std::memory_order_acquire);
+    for (int i = 0; i < n; i++) words[i] = sig[1 + i];
+    return ZKML_OK;
+}
+
+// Reads the device error flag (one synchronisation).
+static int read_err_flag(zkml_ctx* ctx) {
+    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 48, ctx->err_flag(), 4, cudaMemcpyDeviceToHost, ctx->stream));
     ZK_CUDA(cudaStreamSynchronize(ctx->stream));
     if (!ctx->pending.empty()) drain_timers(ctx);
     return ZKML_OK;
@@ -184,9 +206,11 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
                  const ClaimHook* hook) {
     Channel ch(chs);
     cudaStream_t s = ctx->stream;
-    const RoundScratch rs = ctx->round_scratch();
+    RoundScratch rs = ctx->round_scratch();
+    rs.sig = ctx->d_sig;
     const unsigned log_k = ilog2(len);
     bool m31 = A32 != nullptr;
+    int rc;
     if (log_k == 0) {
         if (m31) {
             uint32_t v[2];
@@ -200,9 +224,12 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             ZK_CUDA(cudaMemcpyAsync(fb_out, B, 16, cudaMemcpyDeviceToHost, s));
             ZK_CUDA(cudaStreamSynchronize(s));
         }
-        if (hook) hook->fn(hook->arg, qmul(ldq(fa_out), ldq(fb_out)));
+        if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "reduce_matmul_layer"))) return rc;
+        if (hook && hook->overlap) hook->overlap(hook->arg);
+        if (hook && hook->fn) hook->fn(hook->arg, qmul(ldq(fa_out), ldq(fb_out)));
         return ZKML_OK;
     }
+    rs.seq = ++ctx->sig_seq;
     {
         KTimer t(ctx, KC_ROUND);
         if (m31)
@@ -210,16 +237,17 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
         else
             launch_round_qm31(A, B, len, rs, s);
     }
+    ZK_CUDA(cudaGetLastError());
     ctx->launches++;
+    if (hook && hook->overlap) hook->overlap(hook->arg);  // host transcript work while the GPU runs
+    uint32_t words[12];
     for (unsigned r = 0; r < log_k; r++) {
-        int rc = read_out(ctx, 12);
-        if (rc) return rc;
-        if (r == 0 && (rc = check_err_flag(ctx, "reduce_matmul_layer"))) return rc;
-        if (r == 0 && hook) hook->fn(hook->arg, qadd(ldq(ctx->h_small + 16), ldq(ctx->h_small + 20)));
+        if ((rc = wait_signal(ctx, rs.seq, words, 12))) return rc;
+        if (r == 0 && hook && hook->fn) hook->fn(hook->arg, qadd(ldq(words), ldq(words + 4)));
         qm31 c0, c1, c2, alpha;
         {
             HostTimer ht(ctx, KC_HOST_CHANNEL);
-            interpolate(ctx->h_small + 16, c0, c1, c2);
+            interpolate(words, c0, c1, c2);
             ch.mix_poly_coeffs(c0, c1, c2);
             alpha = ch.draw_qm31();
         }
@@ -229,25 +257,30 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             stq(out_rp + 12 * r + 8, c2);
         }
         if (out_ch) stq(out_ch + 4 * r, alpha);
-        KTimer t(ctx, KC_ROUND);
-        if (len == 2) {
-            launch_final_fold(A, B, m31 ? A32 : nullptr, m31 ? B32 : nullptr, len, alpha, ctx->out_words(), s);
-        } else if (m31) {
-            A = ctx->fa.as<uint4>();
-            B = ctx->fb.as<uint4>();
-            launch_fold_round_m31(A32, B32, len, alpha, A, B, rs, s);
-            m31 = false;
-        } else {
-            launch_fold_round_qm31(A, B, len, alpha, rs, s);
+        rs.seq = ++ctx->sig_seq;
+        {
+            KTimer t(ctx, KC_ROUND);
+            if (len == 2) {
+                launch_final_fold(A, B, m31 ? A32 : nullptr, m31 ? B32 : nullptr, len, alpha, ctx->out_words(),
+                                  rs.sig, rs.seq, s);
+            } else if (m31) {
+                A = ctx->fa.as<uint4>();
+                B = ctx->fb.as<uint4>();
+                launch_fold_round_m31(A32, B32, len, alpha, A, B, rs, s);
+                m31 = false;
+            } else {
+                launch_fold_round_qm31(A, B, len, alpha, rs, s);
+            }
         }
+        ZK_CUDA(cudaGetLastError());
         ctx->launches++;
         len /= 2;
     }
-    int rc = read_out(ctx, 8);
-    if (rc) return rc;
-    memcpy(fa_out, ctx->h_small + 16, 16);
-    memcpy(fb_out, ctx->h_small + 20, 16);
-    return ZKML_OK;
+    if ((rc = wait_signal(ctx, rs.seq, words, 8))) return rc;
+    memcpy(fa_out, words, 16);
+    memcpy(fb_out, words + 4, 16);
+    if ((rc = read_err_flag(ctx))) return rc;
+    return check_err_flag(ctx, "reduce_matmul_layer");
 }
 
 // Restriction of A (rows by r_i) and B (columns by r_j) into ctx->fa / fb (length pk).
@@ -332,6 +365,13 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     if (!rc) rc = ctx->small.ensure(64 * 4);
     if (!rc && (e = cudaMemset(ctx->small.ptr, 0, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMemset");
     if (!rc && (e = cudaMallocHost(&ctx->h_small, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMallocHost");
+    if (!rc && (e = cudaHostAlloc(&ctx->h_sig, 4096, cudaHostAllocMapped)) != cudaSuccess)
+        rc = cuda_error(e, "cudaHostAlloc(mapped)");
+    if (!rc) {
+        memset(ctx->h_sig, 0, 4096);
+        if ((e = cudaHostGetDevicePointer((void**)&ctx->d_sig, ctx->h_sig, 0)) != cudaSuccess)
+            rc = cuda_error(e, "cudaHostGetDevicePointer");
+    }
     if (!rc) {
         // Hades round keys and Montgomery constants into this device's constant bank
         const felt two = f_from_u64(2);
@@ -354,6 +394,7 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
                       &ctx->eq_a, &ctx->eq_hi, &ctx->eq_lo, &ctx->partials, &ctx->small};
     for (DevBuf* b : bufs) b->release();
     if (ctx->h_small) cudaFreeHost(ctx->h_small);
+    if (ctx->h_sig) cudaFreeHost(ctx->h_sig);
     drain_timers(ctx);
     for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -456,27 +497,40 @@ int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, siz
                                  const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k,
                                  const uint32_t* b, size_t n, zkml_channel* chs, uint32_t* out_round_polys,
                                  uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t* out_next_point) {
-    if (!ctx || !claim_value || !chs) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    if (!ctx || !claim_value || !chs || (n_point && !claim_point)) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (m == 0 || k == 0 || n == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty matrix");
     const size_t pm = next_pow2(m), pk = next_pow2(k), pn = next_pow2(n);
     const unsigned log_m = ilog2(pm), log_n = ilog2(pn), log_k = ilog2(pk);
     if (n_point != log_m + log_n)
         return set_error(ZKML_ERR_INVALID_ARG, "output claim has " + std::to_string(n_point) +
                                                    " vars, expected exactly " + std::to_string(log_m + log_n));
-    Channel ch(chs);
-    ch.mix_u64(m);
-    ch.mix_u64(k);
-    ch.mix_u64(n);
-    ch.mix_qm31(ldq(claim_value));
-    uint32_t chal[4 * 64];
-    int rc = zkml_reduce_matmul_layer(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
-                                      chs, out_round_polys, chal, out_final_a, out_final_b);
+    // Seeding mixes (gkr/prover.rs:5996-5999) run on the host while the GPU restricts.
+    struct Seed {
+        zkml_channel* ch;
+        size_t m, k, n;
+        const uint32_t* value;
+    } seed{chs, m, k, n, claim_value};
+    ClaimHook hook;
+    hook.fn = nullptr;
+    hook.arg = &seed;
+    hook.overlap = [](void* arg) {
+        Seed* sd = static_cast<Seed*>(arg);
+        Channel c(sd->ch);
+        c.mix_u64(sd->m);
+        c.mix_u64(sd->k);
+        c.mix_u64(sd->n);
+        c.mix_qm31(ldq(sd->value));
+    };
+    std::vector<uint32_t> chal(4 * (log_k + 1));
+    int rc = reduce_matmul_internal(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
+                                    chs, out_round_polys, chal.data(), out_final_a, out_final_b, &hook);
     if (rc) return rc;
+    Channel ch(chs);
     ch.mix_qm31(ldq(out_final_a));
     ch.mix_qm31(ldq(out_final_b));
     if (out_next_point) {
         memcpy(out_next_point, claim_point, 16 * log_m);
-        memcpy(out_next_point + 4 * log_m, chal, 16 * log_k);
+        memcpy(out_next_point + 4 * log_m, chal.data(), 16 * log_k);
     }
     return ZKML_OK;
 }

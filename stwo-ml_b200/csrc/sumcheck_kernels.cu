@@ -19,6 +19,24 @@ __device__ __forceinline__ void st_q(uint4* p, qm31 x) { *p = make_uint4(x.a, x.
 // Reduce a u64 accumulator to < 2^34 (keeps it congruent mod P).
 __device__ __forceinline__ unsigned long long lazy(unsigned long long x) { return (x & P) + (x >> 31); }
 
+// acc += a * b as one 32x32 -> 64-bit multiply-add with a 64-bit addend.
+__device__ __forceinline__ void mac(unsigned long long& acc, uint32_t a, uint32_t b) {
+    asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
+}
+
+// Cheap partial reduction: x = H 2^32 + L = 2H + L (mod P) since 2^32 = 2 mod P;
+// the result is < 2^34, so four more products (< 2^62 each) fit in 64 bits.
+__device__ __forceinline__ unsigned long long lazy2(unsigned long long x) {
+    unsigned long long r;
+    asm("{\n\t.reg .u32 lo, hi;\n\t.reg .u64 l64;\n\t"
+        "mov.b64 {lo, hi}, %1;\n\t"
+        "cvt.u64.u32 l64, lo;\n\t"
+        "mad.wide.u32 %0, hi, 2, l64;\n\t}"
+        : "=l"(r)
+        : "l"(x));
+    return r;
+}
+
 // ---------------------------------------------------------------------------
 // eq table
 // ---------------------------------------------------------------------------
@@ -111,20 +129,20 @@ __global__ void __launch_bounds__(256, 4)
             if (u < (int)cnt) {
                 const uint4 lh = __ldg(lhi + jh + u);
                 bad |= v[u].x | v[u].y;
-                acc[0][0] += (unsigned long long)v[u].x * lh.x;
-                acc[0][1] += (unsigned long long)v[u].x * lh.y;
-                acc[0][2] += (unsigned long long)v[u].x * lh.z;
-                acc[0][3] += (unsigned long long)v[u].x * lh.w;
-                acc[1][0] += (unsigned long long)v[u].y * lh.x;
-                acc[1][1] += (unsigned long long)v[u].y * lh.y;
-                acc[1][2] += (unsigned long long)v[u].y * lh.z;
-                acc[1][3] += (unsigned long long)v[u].y * lh.w;
+                mac(acc[0][0], v[u].x, lh.x);
+                mac(acc[0][1], v[u].x, lh.y);
+                mac(acc[0][2], v[u].x, lh.z);
+                mac(acc[0][3], v[u].x, lh.w);
+                mac(acc[1][0], v[u].y, lh.x);
+                mac(acc[1][1], v[u].y, lh.y);
+                mac(acc[1][2], v[u].y, lh.z);
+                mac(acc[1][3], v[u].y, lh.w);
             }
             if ((u & 3) == 3) {
 #pragma unroll
                 for (int e = 0; e < 2; e++)
 #pragma unroll
-                    for (int c = 0; c < 4; c++) acc[e][c] = lazy(acc[e][c]);
+                    for (int c = 0; c < 4; c++) acc[e][c] = lazy2(acc[e][c]);
             }
         }
         s += cnt;
@@ -271,10 +289,20 @@ __device__ __forceinline__ void sums_add(Sums& s, const qm31& x0, const qm31& x1
     s.v[8] += x2.a; s.v[9] += x2.b; s.v[10] += x2.c; s.v[11] += x2.d;
 }
 
+// Publish `n` result words to mapped host memory: words first, then the
+// sequence number with a system-scope release (called by one thread).
+__device__ __forceinline__ void publish(uint32_t* sig, uint32_t seq, const uint32_t* words, int n) {
+    volatile uint32_t* v = sig;
+    for (int i = 0; i < n; i++) v[1 + i] = words[i];
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig), "r"(seq) : "memory");
+}
+
 // Block-reduce the 12 lazily accumulated words and finish the grid reduction.
 __device__ void finish_sums(Sums& s, uint32_t* __restrict__ partials, unsigned int* __restrict__ ticket,
-                            uint32_t* __restrict__ out) {
+                            uint32_t* __restrict__ out, uint32_t* sig, uint32_t seq) {
     __shared__ uint32_t sh[32][12];
+    __shared__ uint32_t res[12];
     __shared__ bool is_last;
     uint32_t r[12];
 #pragma unroll
@@ -305,9 +333,16 @@ __device__ void finish_sums(Sums& s, uint32_t* __restrict__ partials, unsigned i
         uint32_t v = red64(acc);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if (lane == 0) out[i] = v;
+        if (lane == 0) {
+            out[i] = v;
+            res[i] = v;
+        }
     }
-    if (threadIdx.x == 0) *ticket = 0;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *ticket = 0;
+        if (sig) publish(sig, seq, res, 12);
+    }
 }
 
 __device__ __forceinline__ void round_terms(const qm31& alo, const qm31& ahi, const qm31& blo, const qm31& bhi,
@@ -325,12 +360,12 @@ __device__ __forceinline__ void sums_zero(Sums& s) {
 
 __global__ void __launch_bounds__(256) round_qm31_kernel(const uint4* __restrict__ A, const uint4* __restrict__ B,
                                                          size_t q, uint32_t* partials, unsigned int* ticket,
-                                                         uint32_t* out) {
+                                                         uint32_t* out, uint32_t* sig, uint32_t seq) {
     Sums s;
     sums_zero(s);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x)
         round_terms(ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q), s);
-    finish_sums(s, partials, ticket, out);
+    finish_sums(s, partials, ticket, out, sig, seq);
 }
 
 // In-place fold with alpha fused with the next round's sums.  Thread i reads
@@ -338,7 +373,7 @@ __global__ void __launch_bounds__(256) round_qm31_kernel(const uint4* __restrict
 // element is read by exactly one thread, so the in-place update is race-free.
 __global__ void __launch_bounds__(256) fold_round_qm31_kernel(uint4* __restrict__ A, uint4* __restrict__ B, size_t h,
                                                               qm31 alpha, uint32_t* partials, unsigned int* ticket,
-                                                              uint32_t* out) {
+                                                              uint32_t* out, uint32_t* sig, uint32_t seq) {
     const size_t q = h / 2;
     Sums s;
     sums_zero(s);
@@ -355,12 +390,12 @@ __global__ void __launch_bounds__(256) fold_round_qm31_kernel(uint4* __restrict_
         st_q(B + i + q, bhi);
         round_terms(alo, ahi, blo, bhi, s);
     }
-    finish_sums(s, partials, ticket, out);
+    finish_sums(s, partials, ticket, out, sig, seq);
 }
 
 __global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restrict__ A, const uint32_t* __restrict__ B,
                                                         size_t q, uint32_t* partials, unsigned int* ticket,
-                                                        uint32_t* out, uint32_t* err) {
+                                                        uint32_t* out, uint32_t* err, uint32_t* sig, uint32_t seq) {
     unsigned long long s0 = 0, s1 = 0, s2 = 0;
     uint32_t bad = 0;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
@@ -380,7 +415,7 @@ __global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restri
     s.v[0] = s0;
     s.v[4] = s1;
     s.v[8] = s2;
-    finish_sums(s, partials, ticket, out);
+    finish_sums(s, partials, ticket, out, sig, seq);
 }
 
 // lo + alpha (hi - lo) with lo, hi in M31.
@@ -391,7 +426,8 @@ __device__ __forceinline__ qm31 fold_m31(uint32_t lo, uint32_t hi, const qm31& a
 __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __restrict__ A,
                                                              const uint32_t* __restrict__ B, size_t h, qm31 alpha,
                                                              uint4* __restrict__ Ao, uint4* __restrict__ Bo,
-                                                             uint32_t* partials, unsigned int* ticket, uint32_t* out) {
+                                                             uint32_t* partials, unsigned int* ticket, uint32_t* out,
+                                                             uint32_t* sig, uint32_t seq) {
     const size_t q = h / 2;
     Sums s;
     sums_zero(s);
@@ -406,7 +442,7 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
         st_q(Bo + i + q, bhi);
         round_terms(alo, ahi, blo, bhi, s);
     }
-    finish_sums(s, partials, ticket, out);
+    finish_sums(s, partials, ticket, out, sig, seq);
 }
 
 static unsigned round_blocks(size_t work, int max_blocks) {
@@ -418,30 +454,32 @@ static unsigned round_blocks(size_t work, int max_blocks) {
 
 void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s) {
     const size_t q = len / 2;
-    round_qm31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out);
+    round_qm31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out, rs.sig,
+                                                                                  rs.seq);
 }
 
 void launch_fold_round_qm31(uint4* A, uint4* B, size_t len, qm31 alpha, const RoundScratch& rs, cudaStream_t s) {
     const size_t h = len / 2;
     fold_round_qm31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha, rs.partials,
-                                                                                rs.ticket, rs.out);
+                                                                                rs.ticket, rs.out, rs.sig, rs.seq);
 }
 
 void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const RoundScratch& rs, uint32_t* err,
                       cudaStream_t s) {
     const size_t q = len / 2;
-    round_m31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out, err);
+    round_m31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out, err,
+                                                                                 rs.sig, rs.seq);
 }
 
 void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm31 alpha, uint4* Ao, uint4* Bo,
                            const RoundScratch& rs, cudaStream_t s) {
     const size_t h = len / 2;
     fold_round_m31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha, Ao, Bo, rs.partials,
-                                                                               rs.ticket, rs.out);
+                                                                               rs.ticket, rs.out, rs.sig, rs.seq);
 }
 
 __global__ void final_fold_kernel(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,
-                                  qm31 alpha, uint32_t* out) {
+                                  qm31 alpha, uint32_t* out, uint32_t* sig, uint32_t seq) {
     if (threadIdx.x != 0) return;
     qm31 a, b;
     if (A32) {
@@ -452,14 +490,15 @@ __global__ void final_fold_kernel(const uint4* A, const uint4* B, const uint32_t
         a = qadd(a0, qmul(alpha, qsub(a1, a0)));
         b = qadd(b0, qmul(alpha, qsub(b1, b0)));
     }
-    out[0] = a.a; out[1] = a.b; out[2] = a.c; out[3] = a.d;
-    out[4] = b.a; out[5] = b.b; out[6] = b.c; out[7] = b.d;
+    const uint32_t w[8] = {a.a, a.b, a.c, a.d, b.a, b.b, b.c, b.d};
+    for (int i = 0; i < 8; i++) out[i] = w[i];
+    if (sig) publish(sig, seq, w, 8);
 }
 
 void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
-                       qm31 alpha, uint32_t* out, cudaStream_t s) {
+                       qm31 alpha, uint32_t* out, uint32_t* sig, uint32_t seq, cudaStream_t s) {
     (void)len;
-    final_fold_kernel<<<1, 32, 0, s>>>(A, B, A32, B32, alpha, out);
+    final_fold_kernel<<<1, 32, 0, s>>>(A, B, A32, B32, alpha, out, sig, seq);
 }
 
 __global__ void mle_fold_kernel(const uint4* src, uint4* dst, size_t h, qm31 r) {

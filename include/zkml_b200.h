@@ -173,6 +173,29 @@ int zkml_prove_gkr_matmul(zkml_ctx *ctx, const uint32_t *input, size_t m, size_t
                           size_t n, const uint64_t *policy, size_t n_queries, uint64_t *out_calldata,
                           size_t cap, size_t *out_len, uint64_t out_digest[4], uint64_t out_io[4]);
 
+/* ---- LogUp activation layer ------------------------------------------------- */
+
+/* reduce_activation_layer, LogUp path (gkr/prover.rs:6390-6600; reference GPU
+ * variant prover.rs:4594-4816): proves that every (masked input, table output)
+ * pair of the rows x cols activation input (zero-padded to powers of two) lies
+ * in the activation table of `tag` (1 ReLU, 2 GELU, 3 Sigmoid, 4 Softmax-exp,
+ * 5 SiLU; components/activation.rs:39-71), with a degree-3 eq-sumcheck and the
+ * multiplicity sumcheck (prover.rs:9449-9515).  claim_point has
+ * log2(padded size) QM31; claim_value is the output claim.  Writes the
+ * LayerProof::Activation record of serialize_gkr_model_proof
+ * (cairo_serde.rs:1355-1387, multiplicities included) and the input
+ * evaluation that becomes the next claim's value.  Returns ZKML_ERR_VERIFY if
+ * the trace-side and table-side LogUp sums differ. */
+/* PrecomputedTable::build of the activation `tag` (gadgets/lookup_table.rs:30-49,
+ * 193-345): out[i] = f(i) for i < 2^table_log_size.  Host only; *out_len receives
+ * the table size (also when cap is too small, which returns ZKML_ERR_INVALID_ARG). */
+int zkml_activation_table(int tag, uint32_t *out, size_t cap, size_t *out_len);
+
+int zkml_reduce_activation_logup(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_t cols, int tag,
+                                 const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                                 zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
+                                 uint32_t out_input_eval[4]);
+
 #ifdef __cplusplus
 }
 #endif

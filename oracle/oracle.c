@@ -1404,3 +1404,365 @@ int orc_verify_gkr_matmul(const uint32_t *input, size_t m, size_t k, const uint3
     if (digest) memcpy(digest, ch.digest, 32);
     return ok;
 }
+
+/* ------------------------------------------------------------------------ */
+/* LogUp activation layer (gkr/prover.rs:6390-6600)                           */
+/* ------------------------------------------------------------------------ */
+
+#include <math.h>
+
+/* gadgets/lookup_table.rs:193-345.  Fixed point with scale 2^16; values above
+ * (P-1)/2 are read as negative.  Evaluated in binary64 in the same operation
+ * order as the reference (the build disables FMA contraction). */
+static uint32_t act_signed_to_m31(double v) {
+    const uint64_t p = ((uint64_t)1 << 31) - 1;
+    if (v >= 0.0) {
+        double r = round(v * 65536.0);
+        uint64_t u = (uint64_t)r;
+        return (uint32_t)(u < p - 1 ? u : p - 1);
+    }
+    uint64_t neg = (uint64_t)round(-v * 65536.0);
+    if (neg > p - 1) neg = p - 1;
+    return (uint32_t)(p - neg);
+}
+
+static double act_real(uint32_t val) {
+    const uint64_t p = ((uint64_t)1 << 31) - 1;
+    const uint32_t half_p = (1u << 30) - 1;
+    return val <= half_p ? (double)val / 65536.0 : -((double)(p - (uint64_t)val)) / 65536.0;
+}
+
+static uint32_t act_fn(int tag, uint32_t val) {
+    const uint32_t half_p = (1u << 30) - 1;
+    const uint32_t scale = 1u << 16;
+    switch (tag) {
+    case 1: /* ReLU */
+        return val <= half_p ? val : 0;
+    case 2: { /* GELU, tanh form */
+        if (val == 0) return 0;
+        double x = act_real(val);
+        double c = sqrt(2.0 / 3.14159265358979311599796346854);
+        double inner = c * (x + 0.044715 * x * x * x);
+        double g = 0.5 * x * (1.0 + tanh(inner));
+        return act_signed_to_m31(g);
+    }
+    case 3: /* Sigmoid (step approximation) */
+        if (val > half_p) return 0;
+        return val == 0 ? scale / 2 : scale;
+    case 4: { /* softmax exp */
+        if (val > half_p) {
+            uint32_t neg = ((1u << 31) - 2) - val;
+            uint32_t decay = neg / scale;
+            if (decay > 20) decay = 20;
+            uint32_t r = scale >> decay;
+            return r > 1 ? r : 1;
+        }
+        if (val == 0) return scale;
+        uint32_t growth = val / scale;
+        if (growth > 10) growth = 10;
+        uint64_t r = (uint64_t)scale << growth;
+        const uint64_t lim = ((uint64_t)1 << 31) - 2;
+        return (uint32_t)(r < lim ? r : lim);
+    }
+    case 5: { /* SiLU */
+        if (val == 0) return 0;
+        double x = act_real(val);
+        double s = x / (1.0 + exp(-x));
+        return act_signed_to_m31(s);
+    }
+    default:
+        return 0;
+    }
+}
+
+unsigned orc_activation_table_log_size(int tag) { return tag == 4 ? 20 : 16; }
+
+int orc_activation_table(int tag, unsigned log_size, uint32_t *out) {
+    if (tag < 1 || tag > 5) return 1;
+    for (size_t i = 0; i < ((size_t)1 << log_size); i++) out[i] = act_fn(tag, (uint32_t)i);
+    return 0;
+}
+
+/* compute_mul_eq_sum_at_t: sum over i < mid of eq_t w_t d_t, x_t = x[i] + t (x[mid+i] - x[i]) */
+static q31 mul_eq_sum_at(const q31 *eq, const q31 *w, const q31 *d, size_t mid, uint32_t t) {
+    q31 s = q_from_m(0);
+    for (size_t i = 0; i < mid; i++) {
+        q31 e = q_add(eq[i], q_mul_m(q_sub(eq[mid + i], eq[i]), t));
+        q31 a = q_add(w[i], q_mul_m(q_sub(w[mid + i], w[i]), t));
+        q31 b = q_add(d[i], q_mul_m(q_sub(d[mid + i], d[i]), t));
+        s = q_add(s, q_mul(q_mul(e, a), b));
+    }
+    return s;
+}
+
+static void fold_vec(q31 *v, size_t mid, q31 r) {
+    for (size_t i = 0; i < mid; i++) v[i] = q_add(v[i], q_mul(r, q_sub(v[mid + i], v[i])));
+}
+
+static void table_commitment(int tag, unsigned log_size, fe *out) {
+    fe in[2];
+    fe_u64(&in[0], (uint64_t)tag);
+    fe_u64(&in[1], log_size);
+    pos_hash_many(out, in, 2);
+}
+
+int orc_reduce_activation_logup(const uint32_t *input, size_t rows, size_t cols, int tag,
+                                const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                                orc_channel *ch, uint64_t *calldata, size_t cap, size_t *out_len,
+                                uint32_t out_input_eval[4]) {
+    oracle_init();
+    if (tag < 1 || tag > 5) return 1;
+    size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
+    unsigned num_vars = ilog2(n);
+    if (n_point < num_vars) return 1;
+    const q31 *point = (const q31 *)claim_point;
+    /* input MLE at the claim point (claim chaining) */
+    q31 *in_mle = mle_row_major(input, rows, cols);
+    q31 input_eval;
+    {
+        q31 *tmp = (q31 *)malloc(sizeof(q31) * n);
+        memcpy(tmp, in_mle, sizeof(q31) * n);
+        restrict_inplace(tmp, n, point, num_vars, 1);
+        input_eval = tmp[0];
+        free(tmp);
+    }
+    unsigned log_t = orc_activation_table_log_size(tag);
+    size_t tsize = (size_t)1 << log_t;
+    uint32_t mask = (uint32_t)tsize - 1;
+    uint32_t *table = (uint32_t *)malloc(4 * tsize);
+    orc_activation_table(tag, log_t, table);
+    uint32_t *mult = (uint32_t *)calloc(tsize, 4);
+    q31 *m_in = (q31 *)malloc(sizeof(q31) * n), *m_out = (q31 *)malloc(sizeof(q31) * n);
+    for (size_t i = 0; i < n; i++) {
+        uint32_t x = in_mle[i].a & mask;
+        m_in[i] = q_from_m(x);
+        m_out[i] = q_from_m(table[x]);
+        mult[x]++;
+    }
+    free(in_mle);
+    orc_ch_mix_u64(ch, 0x4C4F47);
+    orc_ch_mix_u64(ch, (uint64_t)tag);
+    q31 gamma = ch_draw_qm31(ch), beta = ch_draw_qm31(ch);
+    q31 *d = (q31 *)malloc(sizeof(q31) * n), *w = (q31 *)malloc(sizeof(q31) * n);
+    q31 trace_sum = q_from_m(0);
+    for (size_t i = 0; i < n; i++) {
+        d[i] = q_sub(q_sub(gamma, m_in[i]), q_mul(beta, m_out[i]));
+        w[i] = q_inv(d[i]);
+        trace_sum = q_add(trace_sum, w[i]);
+    }
+    q31 table_sum = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        if (!mult[j]) continue;
+        q31 dj = q_sub(q_sub(gamma, q_from_m((uint32_t)j)), q_mul(beta, q_from_m(table[j])));
+        table_sum = q_add(table_sum, q_mul_m(q_inv(dj), mult[j] % MP));
+    }
+    int rc = 0;
+    if (!q_eq(trace_sum, table_sum)) rc = 3;
+    ch_mix_sf(ch, trace_sum);
+    /* degree-3 eq-sumcheck: sum eq(r, x) w(x) d(x) = 1 */
+    q31 *eq = lagrange_basis(point, num_vars);
+    q31 *rps = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    q31 *chal = (q31 *)malloc(sizeof(q31) * (num_vars + 1));
+    uint32_t inv2 = m_inv(2), inv6 = m_inv(6);
+    size_t cur = n;
+    for (unsigned r = 0; r < num_vars; r++) {
+        size_t mid = cur / 2;
+        q31 s0 = mul_eq_sum_at(eq, w, d, mid, 0), s1 = mul_eq_sum_at(eq, w, d, mid, 1);
+        q31 s2 = mul_eq_sum_at(eq, w, d, mid, 2), s3 = mul_eq_sum_at(eq, w, d, mid, 3);
+        q31 dd1 = q_sub(s1, s0);
+        q31 dd2 = q_mul_m(q_add(q_sub(q_sub(s2, s1), s1), s0), inv2);
+        q31 dd3 = q_mul_m(q_sub(q_sub(s3, s0), q_mul_m(q_sub(s2, s1), 3)), inv6);
+        q31 c0 = s0, c1 = q_add(q_sub(dd1, dd2), q_mul_m(dd3, 2)), c2 = q_sub(dd2, q_mul_m(dd3, 3)), c3 = dd3;
+        rps[4 * r] = c0;
+        rps[4 * r + 1] = c1;
+        rps[4 * r + 2] = c2;
+        rps[4 * r + 3] = c3;
+        uint32_t coeffs[16];
+        q_store(coeffs, c0);
+        q_store(coeffs + 4, c1);
+        q_store(coeffs + 8, c2);
+        q_store(coeffs + 12, c3);
+        orc_ch_mix_poly_coeffs_deg3(ch, coeffs);
+        chal[r] = ch_draw_qm31(ch);
+        fold_vec(eq, mid, chal[r]);
+        fold_vec(w, mid, chal[r]);
+        fold_vec(d, mid, chal[r]);
+        cur = mid;
+    }
+    q31 w_eval = w[0];
+    restrict_inplace(m_in, n, chal, num_vars, 1);
+    restrict_inplace(m_out, n, chal, num_vars, 1);
+    q31 in_eval_s = m_in[0], out_eval_s = m_out[0];
+    /* multiplicity sumcheck (prover.rs:9449-9515) */
+    unsigned mvars = log_t;
+    q31 *mv = (q31 *)malloc(sizeof(q31) * tsize);
+    q31 m_claim = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        mv[j] = q_from_m(mult[j] % MP);
+        m_claim = q_add(m_claim, mv[j]);
+    }
+    q31 *mrp = (q31 *)malloc(sizeof(q31) * 2 * (mvars + 1));
+    size_t msz = tsize;
+    for (unsigned r = 0; r < mvars; r++) {
+        size_t half = msz / 2;
+        q31 s0 = q_from_m(0), s1 = q_from_m(0);
+        for (size_t j = 0; j < half; j++) {
+            s0 = q_add(s0, mv[j]);
+            s1 = q_add(s1, mv[half + j]);
+        }
+        q31 c0 = s0, c1 = q_sub(s1, s0);
+        mrp[2 * r] = c0;
+        mrp[2 * r + 1] = c1;
+        ch_mix_sf(ch, c0);
+        ch_mix_sf(ch, c1);
+        q31 rr = ch_draw_qm31(ch);
+        fold_vec(mv, half, rr);
+        msz = half;
+    }
+    q31 m_final = mv[0];
+    fe tcom;
+    table_commitment(tag, log_t, &tcom);
+    ch_mix_sf(ch, input_eval);
+    ch_mix_sf(ch, q_load(claim_value));
+    /* serialize LayerProof::Activation */
+    felt_out o = {calldata, 0, cap, 0};
+    out_u64(&o, 3);
+    out_u64(&o, (uint64_t)tag);
+    out_qm31(&o, input_eval);
+    out_qm31(&o, q_load(claim_value));
+    out_push(&o, &tcom);
+    out_u64(&o, 1); /* logup proof present */
+    out_qm31(&o, trace_sum);
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, rps[4 * r]);
+        out_qm31(&o, rps[4 * r + 2]);
+        out_qm31(&o, rps[4 * r + 3]);
+    }
+    out_qm31(&o, w_eval);
+    out_qm31(&o, in_eval_s);
+    out_qm31(&o, out_eval_s);
+    out_u64(&o, tsize);
+    for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
+    out_u64(&o, 1); /* multiplicity sumcheck present */
+    out_u64(&o, mvars);
+    for (unsigned r = 0; r < mvars; r++) {
+        out_qm31(&o, mrp[2 * r]);
+        out_qm31(&o, mrp[2 * r + 1]);
+    }
+    out_qm31(&o, m_final);
+    out_qm31(&o, m_claim);
+    out_u64(&o, 0); /* no activation product proof */
+    out_u64(&o, 0); /* no piecewise proof */
+    *out_len = o.len;
+    if (out_input_eval) q_store(out_input_eval, input_eval);
+    free(mrp);
+    free(mv);
+    free(chal);
+    free(rps);
+    free(eq);
+    free(w);
+    free(d);
+    free(m_in);
+    free(m_out);
+    free(mult);
+    free(table);
+    if (rc) return rc;
+    return o.overflow ? 2 : 0;
+}
+
+/* eq(r, s) = prod ((1 - r_i)(1 - s_i) + r_i s_i) */
+static q31 eq_eval(const q31 *r, const q31 *s, size_t n) {
+    q31 acc = q_from_m(1), one = q_from_m(1);
+    for (size_t i = 0; i < n; i++)
+        acc = q_mul(acc, q_add(q_mul(q_sub(one, r[i]), q_sub(one, s[i])), q_mul(r[i], s[i])));
+    return acc;
+}
+
+int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint32_t *claim_point, size_t n_point,
+                                const uint32_t claim_value[4], orc_channel *ch, uint32_t out_input_eval[4]) {
+    oracle_init();
+    felt_in in = {calldata, len, 0, 0};
+    if (in_u64(&in) != 3) return 0;
+    int tag = (int)in_u64(&in);
+    if (tag < 1 || tag > 5) return 0;
+    q31 input_eval = in_qm31(&in), output_eval = in_qm31(&in);
+    fe tcom, expect;
+    in_felt(&in, &tcom);
+    if (in_u64(&in) != 1) return 0;
+    q31 claimed = in_qm31(&in);
+    size_t num_vars = in_u64(&in);
+    if (num_vars == 0 || num_vars > n_point || num_vars > 40 || in.bad) return 0;
+    if (!q_eq(output_eval, q_load(claim_value))) return 0;
+    orc_ch_mix_u64(ch, 0x4C4F47);
+    orc_ch_mix_u64(ch, (uint64_t)tag);
+    q31 gamma = ch_draw_qm31(ch), beta = ch_draw_qm31(ch);
+    unsigned log_t = orc_activation_table_log_size(tag);
+    table_commitment(tag, log_t, &expect);
+    if (memcmp(expect.v, tcom.v, 32)) return 0;
+    /* read the rest of the logup proof */
+    q31 rp[40][4];
+    for (size_t r = 0; r < num_vars; r++) {
+        rp[r][0] = in_qm31(&in);
+        rp[r][2] = in_qm31(&in);
+        rp[r][3] = in_qm31(&in);
+    }
+    q31 w_eval = in_qm31(&in), in_s = in_qm31(&in), out_s = in_qm31(&in);
+    size_t tsize = (size_t)1 << log_t;
+    if (in_u64(&in) != tsize || in.bad) return 0;
+    uint32_t *table = (uint32_t *)malloc(4 * tsize);
+    orc_activation_table(tag, log_t, table);
+    q31 table_sum = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        uint64_t m = in_u64(&in);
+        if (!m) continue;
+        q31 dj = q_sub(q_sub(gamma, q_from_m((uint32_t)j)), q_mul(beta, q_from_m(table[j])));
+        table_sum = q_add(table_sum, q_mul(q_from_m((uint32_t)(m % MP)), q_inv(dj)));
+    }
+    free(table);
+    if (!q_eq(table_sum, claimed)) return 0;
+    ch_mix_sf(ch, claimed);
+    q31 cur = q_from_m(1), chal[40];
+    for (size_t r = 0; r < num_vars; r++) {
+        /* compressed: c1 = cur - 2 c0 - c2 - c3 */
+        q31 c0 = rp[r][0], c2 = rp[r][2], c3 = rp[r][3];
+        q31 c1 = q_sub(q_sub(q_sub(cur, q_add(c0, c0)), c2), c3);
+        uint32_t coeffs[16];
+        q_store(coeffs, c0);
+        q_store(coeffs + 4, c1);
+        q_store(coeffs + 8, c2);
+        q_store(coeffs + 12, c3);
+        orc_ch_mix_poly_coeffs_deg3(ch, coeffs);
+        chal[r] = ch_draw_qm31(ch);
+        q31 x = chal[r];
+        cur = q_add(c0, q_mul(x, q_add(c1, q_mul(x, q_add(c2, q_mul(x, c3))))));
+    }
+    q31 d_eval = q_sub(q_sub(gamma, in_s), q_mul(beta, out_s));
+    q31 expect_sum = q_mul(q_mul(eq_eval((const q31 *)claim_point, chal, num_vars), w_eval), d_eval);
+    if (!q_eq(cur, expect_sum)) return 0;
+    /* multiplicity sumcheck */
+    if (in_u64(&in) == 1) {
+        size_t mr = in_u64(&in);
+        if (mr > 40) return 0;
+        q31 mc[40][2];
+        for (size_t r = 0; r < mr; r++) {
+            mc[r][0] = in_qm31(&in);
+            mc[r][1] = in_qm31(&in);
+        }
+        q31 mfinal = in_qm31(&in), mclaim = in_qm31(&in);
+        q31 s = mclaim;
+        for (size_t r = 0; r < mr; r++) {
+            if (!q_eq(q_add(mc[r][0], q_add(mc[r][0], mc[r][1])), s)) return 0;
+            ch_mix_sf(ch, mc[r][0]);
+            ch_mix_sf(ch, mc[r][1]);
+            q31 x = ch_draw_qm31(ch);
+            s = q_add(mc[r][0], q_mul(mc[r][1], x));
+        }
+        if (!q_eq(s, mfinal)) return 0;
+    }
+    if (in_u64(&in) != 0 || in_u64(&in) != 0) return 0; /* no product / piecewise proofs */
+    ch_mix_sf(ch, input_eval);
+    ch_mix_sf(ch, output_eval);
+    if (out_input_eval) q_store(out_input_eval, input_eval);
+    return in.pos == len && !in.bad;
+}

@@ -118,6 +118,25 @@ int orc_verify_gkr_matmul(const uint32_t *input, size_t m, size_t k, const uint3
 void orc_io_commitment(const uint32_t *input, size_t in_rows, size_t in_cols,
                        const uint32_t *output, size_t out_rows, size_t out_cols, uint64_t out[4]);
 
+/* Activation lookup tables (gadgets/lookup_table.rs:193-345, components/activation.rs:39-96).
+ * tag: 1 ReLU, 2 GELU, 3 Sigmoid, 4 Softmax(exp), 5 SiLU.  Fills out[2^log_size]. */
+int orc_activation_table(int tag, unsigned log_size, uint32_t *out);
+unsigned orc_activation_table_log_size(int tag);
+
+/* reduce_activation_layer, the LogUp path (gkr/prover.rs:6390-6600), serialized as the
+ * LayerProof::Activation record of serialize_gkr_model_proof (cairo_serde.rs:1355-1387,
+ * multiplicities included).  The activation input is rows x cols (padded to powers of two),
+ * the output claim has log2(padded size) variables. */
+int orc_reduce_activation_logup(const uint32_t *input, size_t rows, size_t cols, int tag,
+                                const uint32_t *claim_point, size_t n_point,
+                                const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                                size_t cap, size_t *out_len, uint32_t out_input_eval[4]);
+/* verify_activation_reduction (gkr/verifier.rs:3058-3287) + verify_multiplicity_sumcheck
+ * (verifier.rs:5818-5842) on such a record.  Returns 1 if accepted. */
+int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint32_t *claim_point,
+                                size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
+                                uint32_t out_input_eval[4]);
+
 /* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
 void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
                     uint32_t *c, int threads);

@@ -49,6 +49,14 @@ int reduce_matmul_internal(::zkml_ctx* ctx, const uint32_t* a, size_t a_rows, si
                            uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
                            const ClaimHook* hook);
 
+// Shared host helpers (matmul_api.cu).
+// device_view: `p` itself if it is device memory of the context's GPU, else a copy in `stage`.
+int device_view(::zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const void** out);
+// Spin (bounded) until a kernel publishes `seq` in the mapped signal words; copy n words.
+int wait_signal(::zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n);
+int read_err_flag(::zkml_ctx* ctx);
+int check_err_flag(::zkml_ctx* ctx, const char* what);
+
 enum KernelClass { KC_RESTRICT_COLS = 0, KC_RESTRICT_ROWS = 1, KC_ROUND = 2, KC_MERKLE = 3, KC_HOST_SYNC = 4,
                    KC_HOST_CHANNEL = 5 };
 
@@ -75,6 +83,7 @@ struct zkml_ctx {
     zk::DevBuf eq_a, eq_hi, eq_lo;  // eq tables
     zk::DevBuf partials;            // per-block round partials
     zk::DevBuf small;               // ticket + out words + error flag
+    zk::DevBuf act_tables[6];       // activation lookup tables by type tag (device copies)
     uint32_t* h_small = nullptr;    // pinned host mirror of `small`
     uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
     uint32_t* d_sig = nullptr;      // device alias of h_sig

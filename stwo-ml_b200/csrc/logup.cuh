@@ -1,0 +1,38 @@
+// Host launchers for the LogUp activation kernels (logup_kernels.cu).  Every
+// reducing launcher leaves its result words in rs.out (device) and, when
+// rs.sig is set, publishes them to mapped host memory with sequence rs.seq.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kernels.cuh"
+#include "qm31.cuh"
+
+namespace zk {
+
+typedef RoundScratch ReduceScratch;  // partials must hold max_blocks * 16 words
+
+// Padded row-major input -> x (M31), masked input, table output, multiplicity histogram.
+void launch_logup_prepare(const uint32_t* input, uint32_t rows, uint32_t cols, size_t pc, size_t n, uint32_t mask,
+                          const uint32_t* table, uint32_t* x_out, uint32_t* m_in, uint32_t* m_out, uint32_t* mult,
+                          uint32_t* err, int max_blocks, cudaStream_t s);
+// d, w = 1/d and sum w (4 words).
+void launch_logup_dw(const uint32_t* m_in, const uint32_t* m_out, size_t n, qm31 gamma, qm31 beta, uint4* d,
+                     uint4* w, const ReduceScratch& rs, cudaStream_t s);
+// sum over table entries with nonzero multiplicity (4 words).
+void launch_logup_table_sum(const uint32_t* mult, const uint32_t* table, size_t tsize, qm31 gamma, qm31 beta,
+                            const ReduceScratch& rs, cudaStream_t s);
+// sum eq * x0 (and eq * x1 if x1) (4 or 8 words).
+void launch_eq_dot(const uint4* eq, const uint32_t* x0, const uint32_t* x1, size_t n, const ReduceScratch& rs,
+                   cudaStream_t s);
+// Degree-3 round over (eq, w, d) of length len (after the optional fold), 16 words.
+void launch_logup_round(uint4* E, uint4* W, uint4* D, size_t len, bool fold, qm31 alpha, const ReduceScratch& rs,
+                        cudaStream_t s);
+void launch_logup_final(const uint4* E, const uint4* W, const uint4* D, qm31 alpha, const ReduceScratch& rs,
+                        cudaStream_t s);
+// Degree-1 multiplicity rounds: len is the current length before the optional fold.
+void launch_mult_round(const uint32_t* src32, uint4* V, size_t len, bool first, bool fold, qm31 alpha,
+                       const ReduceScratch& rs, cudaStream_t s);
+void launch_mult_final(const uint32_t* src32, const uint4* V, qm31 alpha, const ReduceScratch& rs, cudaStream_t s);
+
+}  // namespace zk

@@ -1,0 +1,329 @@
+// sm_100a kernels for the LogUp activation layer (gkr/prover.rs:6390-6600):
+// range masking + table lookup + multiplicity histogram, the denominators
+// d = gamma - in - beta * out and their inverses w = 1/d, the trace / table
+// LogUp sums, eq-weighted dot products, and the degree-3 eq-sumcheck rounds
+// (s(t) = sum eq_t w_t d_t at t = 0..3) with the fold of eq, w and d fused in.
+#include "logup.cuh"
+
+namespace zk {
+
+__device__ __forceinline__ qm31 ldq4(const uint4* p) {
+    uint4 v = *p;
+    return qm(v.x, v.y, v.z, v.w);
+}
+__device__ __forceinline__ void stq4(uint4* p, qm31 x) { *p = make_uint4(x.a, x.b, x.c, x.d); }
+
+__device__ __forceinline__ void publish_words(uint32_t* sig, uint32_t seq, const uint32_t* words, int n) {
+    volatile uint32_t* v = sig;
+    for (int i = 0; i < n; i++) v[1 + i] = words[i];
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig), "r"(seq) : "memory");
+}
+
+// Grid reduction of NW lazily accumulated words (each accumulator is a sum of
+// values < P): per-block partials, then the last block (atomic ticket) reduces
+// them, stores the NW reduced words to out and optionally publishes them.
+template <int NW>
+__device__ void grid_reduce(unsigned long long (&acc)[NW], const ReduceScratch& rs) {
+    __shared__ uint32_t sh[32][NW];
+    __shared__ uint32_t res[NW];
+    __shared__ bool is_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int i = 0; i < NW; i++) {
+        uint32_t r = red64(acc[i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) r = madd(r, __shfl_xor_sync(0xffffffffu, r, off));
+        if (lane == 0) sh[warp][i] = r;
+    }
+    __syncthreads();
+    if (threadIdx.x < NW) {
+        uint32_t a = 0;
+        for (int w = 0; w < nw; w++) a = madd(a, sh[w][threadIdx.x]);
+        rs.partials[blockIdx.x * NW + threadIdx.x] = a;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = (atomicAdd(rs.ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (int i = warp; i < NW; i += nw) {
+        unsigned long long a = 0;
+        for (unsigned b = lane; b < gridDim.x; b += 32) a += __ldcg(rs.partials + b * NW + i);
+        uint32_t v = red64(a);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) {
+            rs.out[i] = v;
+            res[i] = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *rs.ticket = 0;
+        if (rs.sig) publish_words(rs.sig, rs.seq, res, NW);
+    }
+}
+
+template <int NW>
+__device__ __forceinline__ void acc_q(unsigned long long (&acc)[NW], int at, const qm31& x) {
+    acc[at] += x.a;
+    acc[at + 1] += x.b;
+    acc[at + 2] += x.c;
+    acc[at + 3] += x.d;
+}
+
+static unsigned grid_for(size_t work, int max_blocks) {
+    size_t b = (work + 255) / 256;
+    if (b > (size_t)max_blocks) b = max_blocks;
+    if (b == 0) b = 1;
+    return (unsigned)b;
+}
+
+// ---------------------------------------------------------------------------
+__global__ void logup_prepare_kernel(const uint32_t* __restrict__ input, uint32_t rows, uint32_t cols, size_t pc,
+                                     size_t n, uint32_t mask, const uint32_t* __restrict__ table,
+                                     uint32_t* __restrict__ x_out, uint32_t* __restrict__ m_in,
+                                     uint32_t* __restrict__ m_out, uint32_t* __restrict__ mult,
+                                     uint32_t* __restrict__ err) {
+    uint32_t bad = 0;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
+        const size_t i = idx / pc, j = idx % pc;
+        uint32_t x = 0;
+        if (i < rows && j < cols) {
+            x = input[i * cols + j];
+            bad |= x;
+            x = red32(x);
+        }
+        const uint32_t mi = x & mask;
+        x_out[idx] = x;
+        m_in[idx] = mi;
+        m_out[idx] = __ldg(table + mi);
+        atomicAdd(mult + mi, 1u);
+    }
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+}
+
+void launch_logup_prepare(const uint32_t* input, uint32_t rows, uint32_t cols, size_t pc, size_t n, uint32_t mask,
+                          const uint32_t* table, uint32_t* x_out, uint32_t* m_in, uint32_t* m_out, uint32_t* mult,
+                          uint32_t* err, int max_blocks, cudaStream_t s) {
+    logup_prepare_kernel<<<grid_for(n, max_blocks * 4), 256, 0, s>>>(input, rows, cols, pc, n, mask, table, x_out,
+                                                                      m_in, m_out, mult, err);
+}
+
+// d = gamma - in - beta * out, w = 1 / d, and trace_sum = sum w  (4 words)
+__global__ void __launch_bounds__(256) logup_dw_kernel(const uint32_t* __restrict__ m_in,
+                                                       const uint32_t* __restrict__ m_out, size_t n, qm31 gamma,
+                                                       qm31 beta, uint4* __restrict__ d, uint4* __restrict__ w,
+                                                       ReduceScratch rs) {
+    unsigned long long acc[4] = {0, 0, 0, 0};
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const qm31 di = qsub(qsub(gamma, qm(m_in[i], 0, 0, 0)), qmul_m(beta, m_out[i]));
+        const qm31 wi = qinv(di);
+        stq4(d + i, di);
+        stq4(w + i, wi);
+        acc_q<4>(acc, 0, wi);
+    }
+    grid_reduce<4>(acc, rs);
+}
+
+void launch_logup_dw(const uint32_t* m_in, const uint32_t* m_out, size_t n, qm31 gamma, qm31 beta, uint4* d,
+                     uint4* w, const ReduceScratch& rs, cudaStream_t s) {
+    logup_dw_kernel<<<grid_for(n, rs.max_blocks), 256, 0, s>>>(m_in, m_out, n, gamma, beta, d, w, rs);
+}
+
+// table_sum = sum_{j : mult_j > 0} mult_j / (gamma - j - beta * table_j)  (4 words)
+__global__ void __launch_bounds__(256) logup_table_sum_kernel(const uint32_t* __restrict__ mult,
+                                                              const uint32_t* __restrict__ table, size_t tsize,
+                                                              qm31 gamma, qm31 beta, ReduceScratch rs) {
+    unsigned long long acc[4] = {0, 0, 0, 0};
+    for (size_t j = blockIdx.x * (size_t)blockDim.x + threadIdx.x; j < tsize; j += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t m = mult[j];
+        if (!m) continue;
+        const qm31 dj = qsub(qsub(gamma, qm((uint32_t)j, 0, 0, 0)), qmul_m(beta, table[j]));
+        acc_q<4>(acc, 0, qmul_m(qinv(dj), red32(m)));
+    }
+    grid_reduce<4>(acc, rs);
+}
+
+void launch_logup_table_sum(const uint32_t* mult, const uint32_t* table, size_t tsize, qm31 gamma, qm31 beta,
+                            const ReduceScratch& rs, cudaStream_t s) {
+    logup_table_sum_kernel<<<grid_for(tsize, rs.max_blocks), 256, 0, s>>>(mult, table, tsize, gamma, beta, rs);
+}
+
+// sum_i eq[i] * x[i] for up to three M31 vectors (NV of them): 4 * NV words.
+template <int NV>
+__global__ void __launch_bounds__(256) eq_dot_kernel(const uint4* __restrict__ eq, const uint32_t* __restrict__ x0,
+                                                     const uint32_t* __restrict__ x1, size_t n, ReduceScratch rs) {
+    unsigned long long acc[4 * NV];
+#pragma unroll
+    for (int i = 0; i < 4 * NV; i++) acc[i] = 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const qm31 e = ldq4(eq + i);
+        acc_q<4 * NV>(acc, 0, qmul_m(e, x0[i]));
+        if (NV > 1) acc_q<4 * NV>(acc, 4, qmul_m(e, x1[i]));
+    }
+    grid_reduce<4 * NV>(acc, rs);
+}
+
+void launch_eq_dot(const uint4* eq, const uint32_t* x0, const uint32_t* x1, size_t n, const ReduceScratch& rs,
+                   cudaStream_t s) {
+    if (x1)
+        eq_dot_kernel<2><<<grid_for(n, rs.max_blocks), 256, 0, s>>>(eq, x0, x1, n, rs);
+    else
+        eq_dot_kernel<1><<<grid_for(n, rs.max_blocks), 256, 0, s>>>(eq, x0, nullptr, n, rs);
+}
+
+// Degree-3 eq-sumcheck round.  With FOLD, first folds (eq, w, d) in place with
+// alpha (length 2h -> h); then emits s(t) = sum_{i < q} eq_t w_t d_t for
+// t = 0, 1, 2, 3 over pairs (i, i + q), q = h / 2 (16 words).
+template <bool FOLD>
+__global__ void __launch_bounds__(256) logup_round_kernel(uint4* __restrict__ E, uint4* __restrict__ W,
+                                                          uint4* __restrict__ D, size_t h, qm31 alpha,
+                                                          ReduceScratch rs) {
+    const size_t q = h / 2;
+    unsigned long long acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc[i] = 0;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
+        qm31 v[3][2];  // [vector][lo/hi]
+        uint4* vec[3] = {E, W, D};
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            if (FOLD) {
+                const qm31 a0 = ldq4(vec[k] + i), a1 = ldq4(vec[k] + i + q);
+                const qm31 a2 = ldq4(vec[k] + i + h), a3 = ldq4(vec[k] + i + q + h);
+                v[k][0] = qadd(a0, qmul(alpha, qsub(a2, a0)));
+                v[k][1] = qadd(a1, qmul(alpha, qsub(a3, a1)));
+                stq4(vec[k] + i, v[k][0]);
+                stq4(vec[k] + i + q, v[k][1]);
+            } else {
+                v[k][0] = ldq4(vec[k] + i);
+                v[k][1] = ldq4(vec[k] + i + q);
+            }
+        }
+        qm31 x[3], dlt[3];
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            x[k] = v[k][0];
+            dlt[k] = qsub(v[k][1], v[k][0]);
+        }
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+            acc_q<16>(acc, 4 * t, qmul(qmul(x[0], x[1]), x[2]));
+#pragma unroll
+            for (int k = 0; k < 3; k++) x[k] = qadd(x[k], dlt[k]);
+        }
+    }
+    grid_reduce<16>(acc, rs);
+}
+
+void launch_logup_round(uint4* E, uint4* W, uint4* D, size_t len, bool fold, qm31 alpha, const ReduceScratch& rs,
+                        cudaStream_t s) {
+    if (fold) {
+        const size_t h = len / 2;
+        logup_round_kernel<true><<<grid_for(h / 2, rs.max_blocks), 256, 0, s>>>(E, W, D, h, alpha, rs);
+    } else {
+        logup_round_kernel<false><<<grid_for(len / 2, rs.max_blocks), 256, 0, s>>>(E, W, D, len, alpha, rs);
+    }
+}
+
+// Final fold of length-2 (eq, w, d) vectors: publishes w (4 words).
+__global__ void logup_final_kernel(const uint4* E, const uint4* W, const uint4* D, qm31 alpha, ReduceScratch rs) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const qm31 w0 = ldq4(W), w1 = ldq4(W + 1);
+    const qm31 w = qadd(w0, qmul(alpha, qsub(w1, w0)));
+    const uint32_t words[4] = {w.a, w.b, w.c, w.d};
+    for (int i = 0; i < 4; i++) rs.out[i] = words[i];
+    if (rs.sig) publish_words(rs.sig, rs.seq, words, 4);
+    (void)E;
+    (void)D;
+}
+
+void launch_logup_final(const uint4* E, const uint4* W, const uint4* D, qm31 alpha, const ReduceScratch& rs,
+                        cudaStream_t s) {
+    logup_final_kernel<<<1, 32, 0, s>>>(E, W, D, alpha, rs);
+}
+
+// Degree-1 sumcheck over the multiplicity MLE: (sum lo-half, sum hi-half).
+// M31 mode reads the raw counts (first round); QM31 mode folds first when FOLD.
+template <bool M31IN, bool FOLD>
+__global__ void __launch_bounds__(256) mult_round_kernel(const uint32_t* __restrict__ src32, uint4* __restrict__ V,
+                                                         size_t h, qm31 alpha, ReduceScratch rs) {
+    // with FOLD: fold length 2h -> h (from src32 when M31IN, else V in place), then
+    // sum the halves of the folded vector (q = h / 2); without FOLD: halves of length h.
+    unsigned long long acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const size_t q = FOLD ? h / 2 : h / 2;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
+        qm31 lo, hi;
+        if (FOLD) {
+            qm31 a0, a1, a2, a3;
+            if (M31IN) {
+                a0 = qm(red32(src32[i]), 0, 0, 0);
+                a1 = qm(red32(src32[i + q]), 0, 0, 0);
+                a2 = qm(red32(src32[i + h]), 0, 0, 0);
+                a3 = qm(red32(src32[i + q + h]), 0, 0, 0);
+            } else {
+                a0 = ldq4(V + i);
+                a1 = ldq4(V + i + q);
+                a2 = ldq4(V + i + h);
+                a3 = ldq4(V + i + q + h);
+            }
+            lo = qadd(a0, qmul(alpha, qsub(a2, a0)));
+            hi = qadd(a1, qmul(alpha, qsub(a3, a1)));
+            stq4(V + i, lo);
+            stq4(V + i + q, hi);
+        } else {
+            if (M31IN) {
+                lo = qm(red32(src32[i]), 0, 0, 0);
+                hi = qm(red32(src32[i + q]), 0, 0, 0);
+            } else {
+                lo = ldq4(V + i);
+                hi = ldq4(V + i + q);
+            }
+        }
+        acc_q<8>(acc, 0, lo);
+        acc_q<8>(acc, 4, hi);
+    }
+    grid_reduce<8>(acc, rs);
+}
+
+void launch_mult_round(const uint32_t* src32, uint4* V, size_t len, bool first, bool fold, qm31 alpha,
+                       const ReduceScratch& rs, cudaStream_t s) {
+    if (!fold) {
+        if (first)
+            mult_round_kernel<true, false><<<grid_for(len / 2, rs.max_blocks), 256, 0, s>>>(src32, V, len, alpha, rs);
+        else
+            mult_round_kernel<false, false><<<grid_for(len / 2, rs.max_blocks), 256, 0, s>>>(src32, V, len, alpha, rs);
+        return;
+    }
+    const size_t h = len / 2;
+    if (first)
+        mult_round_kernel<true, true><<<grid_for(h / 2, rs.max_blocks), 256, 0, s>>>(src32, V, h, alpha, rs);
+    else
+        mult_round_kernel<false, true><<<grid_for(h / 2, rs.max_blocks), 256, 0, s>>>(src32, V, h, alpha, rs);
+}
+
+// Last fold of a length-2 multiplicity vector (from counts if M31IN): 4 words.
+__global__ void mult_final_kernel(const uint32_t* src32, const uint4* V, qm31 alpha, ReduceScratch rs) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    qm31 a0, a1;
+    if (src32) {
+        a0 = qm(red32(src32[0]), 0, 0, 0);
+        a1 = qm(red32(src32[1]), 0, 0, 0);
+    } else {
+        a0 = ldq4(V);
+        a1 = ldq4(V + 1);
+    }
+    const qm31 r = qadd(a0, qmul(alpha, qsub(a1, a0)));
+    const uint32_t words[4] = {r.a, r.b, r.c, r.d};
+    for (int i = 0; i < 4; i++) rs.out[i] = words[i];
+    if (rs.sig) publish_words(rs.sig, rs.seq, words, 4);
+}
+
+void launch_mult_final(const uint32_t* src32, const uint4* V, qm31 alpha, const ReduceScratch& rs, cudaStream_t s) {
+    mult_final_kernel<<<1, 32, 0, s>>>(src32, V, alpha, rs);
+}
+
+}  // namespace zk

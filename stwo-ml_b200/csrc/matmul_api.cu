@@ -122,7 +122,7 @@ static inline unsigned ilog2(size_t x) {
 
 // Returns a device pointer for `p` (count bytes): p itself when it is device
 // memory of the current GPU, otherwise a copy in `stage`.
-static int device_view(zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const void** out) {
+int device_view(zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const void** out) {
     cudaPointerAttributes attr;
     cudaError_t e = cudaPointerGetAttributes(&attr, p);
     if (e != cudaSuccess) {
@@ -142,7 +142,7 @@ static int device_view(zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage
     return ZKML_OK;
 }
 
-static int check_err_flag(zkml_ctx* ctx, const char* what) {
+int check_err_flag(zkml_ctx* ctx, const char* what) {
     if (ctx->h_small[48]) {
         ctx->h_small[48] = 0;
         ZK_CUDA(cudaMemsetAsync(ctx->err_flag(), 0, 4, ctx->stream));
@@ -171,7 +171,7 @@ static void interpolate(const uint32_t* s12, qm31& c0, qm31& c1, qm31& c2) {
 // Waits until a kernel publishes `seq` in the mapped signal words, then copies
 // `n` result words out.  Polls the stream for errors while waiting and gives up
 // after a bounded time, so a failed launch never leaves the host spinning.
-static int wait_signal(zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n) {
+int wait_signal(zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n) {
     HostTimer ht(ctx, KC_HOST_SYNC);
     volatile uint32_t* sig = ctx->h_sig;
     const auto t0 = std::chrono::steady_clock::now();
@@ -192,7 +192,7 @@ static int wait_signal(zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n) {
 }
 
 // Reads the device error flag (one synchronisation).
-static int read_err_flag(zkml_ctx* ctx) {
+int read_err_flag(zkml_ctx* ctx) {
     ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 48, ctx->err_flag(), 4, cudaMemcpyDeviceToHost, ctx->stream));
     ZK_CUDA(cudaStreamSynchronize(ctx->stream));
     if (!ctx->pending.empty()) drain_timers(ctx);
@@ -361,7 +361,7 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) rc = cuda_error(e, "cudaStreamCreate");
     ctx->stream = ctx->own_stream;
-    if (!rc) rc = ctx->partials.ensure((size_t)ctx->max_round_blocks * 12 * 4);
+    if (!rc) rc = ctx->partials.ensure((size_t)ctx->max_round_blocks * 16 * 4);
     if (!rc) rc = ctx->small.ensure(64 * 4);
     if (!rc && (e = cudaMemset(ctx->small.ptr, 0, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMemset");
     if (!rc && (e = cudaMallocHost(&ctx->h_small, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMallocHost");
@@ -393,6 +393,7 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
     DevBuf* bufs[] = {&ctx->a_in, &ctx->b_in, &ctx->fa,    &ctx->fb,       &ctx->acc_a, &ctx->acc_b,
                       &ctx->eq_a, &ctx->eq_hi, &ctx->eq_lo, &ctx->partials, &ctx->small};
     for (DevBuf* b : bufs) b->release();
+    for (DevBuf& t : ctx->act_tables) t.release();
     if (ctx->h_small) cudaFreeHost(ctx->h_small);
     if (ctx->h_sig) cudaFreeHost(ctx->h_sig);
     drain_timers(ctx);

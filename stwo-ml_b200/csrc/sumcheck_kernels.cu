@@ -109,40 +109,67 @@ __global__ void __launch_bounds__(256, 4)
         uint32_t cnt = s_row - jh;
         if (left < cnt) cnt = (uint32_t)left;
         if (cnt > RC_UNROLL) cnt = RC_UNROLL;
-        uint2 v[RC_UNROLL];
         const size_t rbase = (size_t)row * n;
+        if (VEC && cnt == RC_UNROLL && (jh + RC_UNROLL) * 64u <= n) {
+            // Fast path: RC_UNROLL full stripes of this row, no per-stripe predicates.
+            const uint2* base = reinterpret_cast<const uint2*>(B + rbase + jh * 64u + 2u * lane);
+            uint2 v[RC_UNROLL];
 #pragma unroll
-        for (int u = 0; u < RC_UNROLL; u++) {
-            v[u] = make_uint2(0, 0);
-            const uint32_t col = (jh + u) * 64u + 2u * lane;
-            if (u < (int)cnt) {
-                if (VEC) {
-                    if (col < n) v[u] = __ldcs(reinterpret_cast<const uint2*>(B + rbase + col));
-                } else {
-                    if (col < n) v[u].x = __ldcs(B + rbase + col);
-                    if (col + 1 < n) v[u].y = __ldcs(B + rbase + col + 1);
-                }
-            }
-        }
+            for (int u = 0; u < RC_UNROLL; u++) v[u] = __ldcs(base + 32 * u);
 #pragma unroll
-        for (int u = 0; u < RC_UNROLL; u++) {
-            if (u < (int)cnt) {
+            for (int u = 0; u < RC_UNROLL; u++) {
                 const uint4 lh = __ldg(lhi + jh + u);
                 bad |= v[u].x | v[u].y;
-                mac(acc[0][0], v[u].x, lh.x);
-                mac(acc[0][1], v[u].x, lh.y);
-                mac(acc[0][2], v[u].x, lh.z);
-                mac(acc[0][3], v[u].x, lh.w);
-                mac(acc[1][0], v[u].y, lh.x);
-                mac(acc[1][1], v[u].y, lh.y);
-                mac(acc[1][2], v[u].y, lh.z);
-                mac(acc[1][3], v[u].y, lh.w);
+                acc[0][0] += (unsigned long long)v[u].x * lh.x;
+                acc[0][1] += (unsigned long long)v[u].x * lh.y;
+                acc[0][2] += (unsigned long long)v[u].x * lh.z;
+                acc[0][3] += (unsigned long long)v[u].x * lh.w;
+                acc[1][0] += (unsigned long long)v[u].y * lh.x;
+                acc[1][1] += (unsigned long long)v[u].y * lh.y;
+                acc[1][2] += (unsigned long long)v[u].y * lh.z;
+                acc[1][3] += (unsigned long long)v[u].y * lh.w;
+                if ((u & 3) == 3) {
+#pragma unroll
+                    for (int e = 0; e < 2; e++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) acc[e][c] = lazy(acc[e][c]);
+                }
             }
-            if ((u & 3) == 3) {
+        } else {
+            uint2 v[RC_UNROLL];
 #pragma unroll
-                for (int e = 0; e < 2; e++)
+            for (int u = 0; u < RC_UNROLL; u++) {
+                v[u] = make_uint2(0, 0);
+                const uint32_t col = (jh + u) * 64u + 2u * lane;
+                if (u < (int)cnt) {
+                    if (VEC) {
+                        if (col < n) v[u] = __ldcs(reinterpret_cast<const uint2*>(B + rbase + col));
+                    } else {
+                        if (col < n) v[u].x = __ldcs(B + rbase + col);
+                        if (col + 1 < n) v[u].y = __ldcs(B + rbase + col + 1);
+                    }
+                }
+            }
 #pragma unroll
-                    for (int c = 0; c < 4; c++) acc[e][c] = lazy2(acc[e][c]);
+            for (int u = 0; u < RC_UNROLL; u++) {
+                if (u < (int)cnt) {
+                    const uint4 lh = __ldg(lhi + jh + u);
+                    bad |= v[u].x | v[u].y;
+                    acc[0][0] += (unsigned long long)v[u].x * lh.x;
+                    acc[0][1] += (unsigned long long)v[u].x * lh.y;
+                    acc[0][2] += (unsigned long long)v[u].x * lh.z;
+                    acc[0][3] += (unsigned long long)v[u].x * lh.w;
+                    acc[1][0] += (unsigned long long)v[u].y * lh.x;
+                    acc[1][1] += (unsigned long long)v[u].y * lh.y;
+                    acc[1][2] += (unsigned long long)v[u].y * lh.z;
+                    acc[1][3] += (unsigned long long)v[u].y * lh.w;
+                }
+                if ((u & 3) == 3) {
+#pragma unroll
+                    for (int e = 0; e < 2; e++)
+#pragma unroll
+                        for (int c = 0; c < 4; c++) acc[e][c] = lazy(acc[e][c]);
+                }
             }
         }
         s += cnt;

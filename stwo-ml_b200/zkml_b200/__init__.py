@@ -100,6 +100,10 @@ _SIGS = {
     "zkml_prove_mle_opening": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.POINTER(_Channel),
                                          C.c_size_t, _u64, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),
     "zkml_io_commitment": (C.c_int, [_u32, C.c_size_t, C.c_size_t, _u32, C.c_size_t, C.c_size_t, _u64]),
+    "zkml_activation_table": (C.c_int, [C.c_int, _u32, C.c_size_t, C.POINTER(C.c_size_t)]),
+    "zkml_reduce_activation_logup": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int,
+                                               C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
+                                               C.c_size_t, C.POINTER(C.c_size_t), _u32]),
     "zkml_prove_gkr_matmul": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                         C.c_void_p, C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t), _u64,
                                         _u64]),
@@ -536,3 +540,54 @@ def prove_gkr_matmul(inp: M31Matrix, weight: M31Matrix, policy_commitment: Optio
                                        C.c_void_p(pol.ctypes.data) if pol is not None else None, nq, buf, cap,
                                        C.byref(ln), dig, io))
     return GKRMatMulProof(_felts(buf, ln.value), limbs_to_felt(dig), limbs_to_felt(io), buf[:4 * ln.value].copy())
+
+
+# ---------------------------------------------------------------------------
+# LogUp activation layer
+# ---------------------------------------------------------------------------
+
+class ActivationType:
+    """components/activation.rs:39-71 type tags."""
+    ReLU = 1
+    GELU = 2
+    Sigmoid = 3
+    Softmax = 4
+    SiLU = 5
+
+    @staticmethod
+    def table_log_size(tag: int) -> int:
+        return 20 if tag == ActivationType.Softmax else 16
+
+
+def activation_table(tag: int) -> np.ndarray:
+    """The activation lookup table (host)."""
+    n = 1 << ActivationType.table_log_size(tag)
+    out = np.zeros(n, np.uint32)
+    ln = C.c_size_t(0)
+    _check(lib().zkml_activation_table(tag, out, n, C.byref(ln)))
+    return out
+
+
+@dataclass
+class ActivationLogUpProof:
+    calldata: List[int]     # LayerProof::Activation record (serialize_gkr_model_proof)
+    input_eval: np.ndarray  # next claim value
+    raw: np.ndarray
+
+
+def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_type: int,
+                            channel: PoseidonChannel, device: int = 0) -> Tuple[ActivationLogUpProof, GKRClaim]:
+    """gkr/prover.rs:6390-6600 (LogUp path)."""
+    buf = _Buf(inp.data)
+    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
+    n_point = len(as_qm31_array(output_claim.point))
+    tsize = 1 << ActivationType.table_log_size(activation_type)
+    cap = tsize + 64 + 16 * (n_point + 40)
+    out = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    _check(lib().zkml_reduce_activation_logup(context(device).handle, buf.ptr, inp.rows, inp.cols, activation_type,
+                                              pt_ptr, n_point, np.ascontiguousarray(output_claim.value, np.uint32),
+                                              C.byref(channel.state), out, cap, C.byref(ln), ie))
+    proof = ActivationLogUpProof(_felts(out, ln.value), ie, out[:4 * ln.value].copy())
+    return proof, GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())

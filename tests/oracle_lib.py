@@ -75,6 +75,12 @@ def lib():
         L.orc_verify_gkr_matmul.argtypes = [u32p, sz, sz, u32p, sz, C.c_void_p, sz, u64p, sz, u64p]
         L.orc_io_commitment.argtypes = [u32p, sz, sz, u32p, sz, sz, u64p]
         L.orc_matmul_m31.argtypes = [u32p, sz, sz, u32p, sz, u32p, C.c_int]
+        L.orc_activation_table.argtypes = [C.c_int, C.c_uint, u32p]
+        L.orc_activation_table_log_size.argtypes = [C.c_int]
+        L.orc_activation_table_log_size.restype = C.c_uint
+        L.orc_reduce_activation_logup.argtypes = [u32p, sz, sz, C.c_int, u32p, sz, u32p, chp, u64p, sz,
+                                                  C.POINTER(sz), u32p]
+        L.orc_verify_activation_logup.argtypes = [u64p, sz, u32p, sz, u32p, chp, u32p]
         _lib = L
     return _lib
 
@@ -171,3 +177,24 @@ def verify_gkr_matmul(inp, w, raw, policy=None, n_queries=10):
     ok = lib().orc_verify_gkr_matmul(inp.reshape(-1), m, k, w.reshape(-1), n, pol, n_queries,
                                      np.ascontiguousarray(raw, np.uint64), raw.size // 4, dig)
     return bool(ok), felt_int(dig)
+
+
+def reduce_activation_logup(inp, tag, point, value, ch, cap=1 << 22):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    rows, cols = inp.shape
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    rc = lib().orc_reduce_activation_logup(inp.reshape(-1), rows, cols, tag, point.reshape(-1), len(point),
+                                           np.ascontiguousarray(value, np.uint32), C.byref(ch), buf, cap,
+                                           C.byref(ln), ie)
+    return rc, buf[:4 * ln.value].copy(), ie
+
+
+def verify_activation_logup(raw, point, value, ch):
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    ie = np.zeros(4, np.uint32)
+    ok = lib().orc_verify_activation_logup(np.ascontiguousarray(raw, np.uint64), raw.size // 4, point.reshape(-1),
+                                           len(point), np.ascontiguousarray(value, np.uint32), C.byref(ch), ie)
+    return bool(ok), ie

@@ -120,3 +120,11 @@ def test_io_commitment_matches_oracle():
     O.lib().orc_io_commitment(inp.reshape(-1), 1, 4, out.reshape(-1), 1, 2, ref)
     assert Z.io_commitment(inp, out) == O.felt_int(ref)
     assert Z.io_commitment(inp, out) == int(GOLD["sp3_matmul_only"]["io_commitment"], 16)
+
+
+@pytest.mark.parametrize("tag", [1, 2, 3, 4, 5])
+def test_activation_tables_match_oracle(tag):
+    lg = O.lib().orc_activation_table_log_size(tag)
+    ref = np.zeros(1 << lg, np.uint32)
+    O.lib().orc_activation_table(tag, lg, ref)
+    assert (Z.activation_table(tag) == ref).all()

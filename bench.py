@@ -290,13 +290,50 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_case(name):
+    """Small fixed workloads for ncu captures (one kernel class each)."""
+    import torch
+
+    import zkml_b200 as Z
+    from helpers import int_matrix_m31, random_qm31
+
+    torch.cuda.set_device(0)
+    if name == "restrict_c2":  # three C2 reductions; restrict_cols launch 2 is the steady-state one
+        be = Z.GpuBackend(0)
+        a, b = make_inputs(0)
+        ta = torch.from_numpy(a.view(np.int32)).cuda()
+        tb = torch.from_numpy(b.view(np.int32)).cuda()
+        rng = np.random.default_rng(0)
+        r_i, r_j = random_qm31(log2(PM), rng), random_qm31(log2(PN), rng)
+        for _ in range(3):
+            be.reduce_matmul_layer(Z.M31Matrix(M, K, ta), Z.M31Matrix(K, N, tb), r_i, r_j, PK, Z.PoseidonChannel())
+    elif name.startswith("merkle_"):  # Poseidon Merkle root over 2^L QM31 leaves, twice
+        lg = int(name.split("_")[1])
+        ev = torch.randint(0, 2**31 - 1, (1 << lg, 4), dtype=torch.int64).to(torch.int32).cuda()
+        for _ in range(2):
+            Z.commit_mle_root(ev)
+    elif name.startswith("logup_"):  # SiLU LogUp layer at C4's activation size 64 x 13824
+        x = int_matrix_m31(64, 13824, 3, bound=60000)
+        rng = np.random.default_rng(0)
+        pt, val = random_qm31(20, rng), random_qm31(1, rng)[0]
+        for _ in range(2):
+            Z.reduce_activation_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), 5, Z.PoseidonChannel())
+    else:
+        raise SystemExit(f"unknown case {name}")
+    torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None, help="run a small profiling workload instead of the benchmark")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
     if args.impl == "reference":

@@ -7,6 +7,7 @@
 
 namespace zk {
 
+bool g_felt_use_adx = __builtin_cpu_supports("adx") && __builtin_cpu_supports("bmi2");
 felt F_R2;
 felt F_ONE;
 felt HADES_RC[107];
@@ -80,7 +81,110 @@ void felt_init() {
     std::call_once(once, init_impl);
 }
 
+// ---------------------------------------------------------------------------
+// Fast path (BMI2 + ADX): lazy reduction.  The multiply accepts inputs < 4p
+// and returns values < p, so additions in front of a multiply need no
+// reduction; in the 83 partial rounds the S-box lane carries x = s2 + key
+// (< 3p) and its critical path is x -> x^2 -> x^3 -> (w + 2p - 2 x^3), where
+// w = (s0 + s1 + next key) mod p is computed off that path.
+// ---------------------------------------------------------------------------
+namespace {
+
+inline felt mul_adx(const felt& a, const felt& b) {
+    felt r;
+    zk_felt_mont_mul_adx(r.l, a.l, b.l);
+    return r;
+}
+// 256-bit add / subtract without reduction (callers keep results in range).
+// Early-clobber outputs: the carry chains write limbs before reading later inputs.
+inline felt add4(const felt& a, const felt& b) {
+    felt r = a;
+    asm("addq %4, %0\n\tadcq %5, %1\n\tadcq %6, %2\n\tadcq %7, %3"
+        : "+&r"(r.l[0]), "+&r"(r.l[1]), "+&r"(r.l[2]), "+&r"(r.l[3])
+        : "rm"(b.l[0]), "rm"(b.l[1]), "rm"(b.l[2]), "rm"(b.l[3])
+        : "cc");
+    return r;
+}
+inline felt sub4(const felt& a, const felt& b) {
+    felt r = a;
+    asm("subq %4, %0\n\tsbbq %5, %1\n\tsbbq %6, %2\n\tsbbq %7, %3"
+        : "+&r"(r.l[0]), "+&r"(r.l[1]), "+&r"(r.l[2]), "+&r"(r.l[3])
+        : "rm"(b.l[0]), "rm"(b.l[1]), "rm"(b.l[2]), "rm"(b.l[3])
+        : "cc");
+    return r;
+}
+inline felt dbl4(const felt& a) { return add4(a, a); }
+// x < 2p -> x mod p (cmov, no branch)
+inline felt red_once(const felt& x) {
+    felt r = x;
+    uint64_t t0, t1, t2, t3;
+    asm("movq %0, %4\n\tsubq $1, %4\n\t"
+        "movq %1, %5\n\tsbbq $0, %5\n\t"
+        "movq %2, %6\n\tsbbq $0, %6\n\t"
+        "movq %3, %7\n\tsbbq %8, %7\n\t"
+        "cmovncq %4, %0\n\tcmovncq %5, %1\n\tcmovncq %6, %2\n\tcmovncq %7, %3"
+        : "+&r"(r.l[0]), "+&r"(r.l[1]), "+&r"(r.l[2]), "+&r"(r.l[3]), "=&r"(t0), "=&r"(t1), "=&r"(t2), "=&r"(t3)
+        : "r"(FP3)
+        : "cc");
+    return r;
+}
+// x < 16p -> x mod p: q = floor(x / 2^251) is floor(x / p) or one more, so
+// x - max(q - 1, 0) p is in [0, 2p).
+inline felt red_full(const felt& x) {
+    uint64_t q = x.l[3] >> 59;
+    q -= (q != 0);
+    const felt qp = {{q, 0, 0, q * FP3}};
+    return red_once(sub4(x, qp));
+}
+
+const felt kP = {{1, 0, 0, FP3}};
+
+inline void full_round_fast(felt s[3], const felt* rc, const felt& p2, const felt& p3) {
+    felt y0 = add4(s[0], rc[0]), y1 = add4(s[1], rc[1]), y2 = add4(s[2], rc[2]);
+    y0 = mul_adx(mul_adx(y0, y0), y0);
+    y1 = mul_adx(mul_adx(y1, y1), y1);
+    y2 = mul_adx(mul_adx(y2, y2), y2);
+    const felt t = add4(add4(y0, y1), y2);                             // < 3p
+    s[0] = red_full(add4(t, dbl4(y0)));                                // < 5p
+    s[1] = red_full(sub4(add4(t, p2), dbl4(y1)));                      // < 5p
+    s[2] = red_full(sub4(add4(t, p3), add4(dbl4(y2), y2)));            // < 6p
+}
+
+void hades_fast(felt s[3]) {
+    const felt p2 = add4(kP, kP), p3 = add4(p2, kP);
+    const felt* rc = HADES_RC;
+    for (int r = 0; r < 4; r++, rc += 3) full_round_fast(s, rc, p2, p3);
+    felt s0 = s[0], s1 = s[1];
+    felt x = add4(s[2], rc[0]);
+    for (int r = 0; r < 83; r++) {
+        const felt y = mul_adx(mul_adx(x, x), x);                      // < p
+        const felt u = add4(s0, s1);                                   // < 2p
+        const felt t = add4(u, y);                                     // < 3p
+        const felt n0 = red_full(add4(t, dbl4(s0)));
+        const felt n1 = red_full(sub4(add4(t, p2), dbl4(s1)));
+        if (r + 1 < 83) {
+            const felt w = red_full(add4(u, rc[r + 1]));               // s0 + s1 + next key
+            x = sub4(add4(w, p2), dbl4(y));                            // next s2 + key, < 3p
+        } else {
+            x = red_full(sub4(add4(u, p2), dbl4(y)));                  // s2 after the last partial round
+        }
+        s0 = n0;
+        s1 = n1;
+    }
+    rc += 83;
+    s[0] = s0;
+    s[1] = s1;
+    s[2] = x;
+    for (int r = 0; r < 4; r++, rc += 3) full_round_fast(s, rc, p2, p3);
+}
+
+}  // namespace
+
 void hades(felt s[3]) {
+    if (__builtin_expect(g_felt_use_adx, 1)) {
+        hades_fast(s);
+        return;
+    }
     const felt* rc = HADES_RC;
     for (int r = 0; r < 4; r++, rc += 3) {
         s[0] = f_cube(f_add(s[0], rc[0]));

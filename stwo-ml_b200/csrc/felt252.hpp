@@ -111,8 +111,12 @@ inline felt f_redc(uint64_t t[8]) {
     return f_reduce_once(r);
 }
 
+// BMI2 + ADX assembly multiply (felt252_x86.S) and whether this CPU can run it.
+extern "C" void zk_felt_mont_mul_adx(uint64_t r[4], const uint64_t a[4], const uint64_t b[4]);
+extern bool g_felt_use_adx;
+
 // Montgomery product a * b / 2^256 mod p for a, b < p (CIOS, one limb of b per step).
-inline felt f_mul(const felt& a, const felt& b) {
+inline felt f_mul_portable(const felt& a, const felt& b) {
     uint64_t t0 = 0, t1 = 0, t2 = 0, t3 = 0, t4 = 0;
     for (int i = 0; i < 4; i++) {
         const uint64_t bi = b.l[i];
@@ -141,6 +145,15 @@ inline felt f_mul(const felt& a, const felt& b) {
     }
     felt r = {{t0, t1, t2, t3}};
     return f_reduce_once(r);
+}
+
+inline felt f_mul(const felt& a, const felt& b) {
+    if (__builtin_expect(g_felt_use_adx, 1)) {
+        felt r;
+        zk_felt_mont_mul_adx(r.l, a.l, b.l);
+        return r;
+    }
+    return f_mul_portable(a, b);
 }
 
 // Montgomery square: the 6 cross products once, doubled, plus the 4 squares.
@@ -195,7 +208,10 @@ inline void f_to_canon(const felt& a, uint64_t out[4]) {
     felt r = f_mul(a, one);
     memcpy(out, r.l, 32);
 }
-inline felt f_cube(const felt& x) { return f_mul(f_sqr(x), x); }
+inline felt f_cube(const felt& x) {
+    if (__builtin_expect(g_felt_use_adx, 1)) return f_mul(f_mul(x, x), x);
+    return f_mul(f_sqr(x), x);
+}
 
 // Hades permutation on Montgomery-form state.
 void hades(felt s[3]);

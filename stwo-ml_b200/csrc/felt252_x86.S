@@ -1,0 +1,155 @@
+/*
+ * x86-64 (BMI2 + ADX) Montgomery multiplication for the Stark prime
+ * p = 2^251 + 17*2^192 + 1 = [1, 0, 0, 0x0800000000000011] (64-bit limbs),
+ * R = 2^256:  r = a * b / R mod p  for a, b < p.
+ *
+ * void zk_felt_mont_mul_adx(uint64_t r[4], const uint64_t a[4], const uint64_t b[4]);
+ *
+ * 4x4 schoolbook product with the two ADX carry chains (adcx / adox), then a
+ * separate reduction: for each low limb t_i, m = -t_i (p = 1 mod 2^64), adding
+ * m * p clears t_i (carry iff t_i != 0) and adds m * 0x0800000000000011 at
+ * limbs i+3, i+4.  The result is < 2p and is reduced once with cmov.
+ */
+    .text
+    .globl  zk_felt_mont_mul_adx
+    .type   zk_felt_mont_mul_adx, @function
+    .p2align 4
+zk_felt_mont_mul_adx:
+    pushq   %rbx
+    pushq   %rbp
+    pushq   %r12
+    pushq   %r13
+    pushq   %r14
+    pushq   %r15
+    movq    %rdx, %rcx                  /* rcx = b */
+
+    /* row 0: t[0..4] = a * b0 */
+    movq    (%rcx), %rdx
+    mulxq   (%rsi), %r8, %r9
+    mulxq   8(%rsi), %rax, %r10
+    addq    %rax, %r9
+    mulxq   16(%rsi), %rax, %r11
+    adcq    %rax, %r10
+    mulxq   24(%rsi), %rax, %r12
+    adcq    %rax, %r11
+    adcq    $0, %r12
+
+    /* row 1: t[1..5] += a * b1 */
+    movq    8(%rcx), %rdx
+    xorl    %ebp, %ebp
+    mulxq   (%rsi), %rax, %rbx
+    adcxq   %rax, %r9
+    adoxq   %rbx, %r10
+    mulxq   8(%rsi), %rax, %rbx
+    adcxq   %rax, %r10
+    adoxq   %rbx, %r11
+    mulxq   16(%rsi), %rax, %rbx
+    adcxq   %rax, %r11
+    adoxq   %rbx, %r12
+    mulxq   24(%rsi), %rax, %r13
+    adcxq   %rax, %r12
+    adoxq   %rbp, %r13
+    adcxq   %rbp, %r13
+
+    /* row 2: t[2..6] += a * b2 */
+    movq    16(%rcx), %rdx
+    xorl    %ebp, %ebp
+    mulxq   (%rsi), %rax, %rbx
+    adcxq   %rax, %r10
+    adoxq   %rbx, %r11
+    mulxq   8(%rsi), %rax, %rbx
+    adcxq   %rax, %r11
+    adoxq   %rbx, %r12
+    mulxq   16(%rsi), %rax, %rbx
+    adcxq   %rax, %r12
+    adoxq   %rbx, %r13
+    mulxq   24(%rsi), %rax, %r14
+    adcxq   %rax, %r13
+    adoxq   %rbp, %r14
+    adcxq   %rbp, %r14
+
+    /* row 3: t[3..7] += a * b3 */
+    movq    24(%rcx), %rdx
+    xorl    %ebp, %ebp
+    mulxq   (%rsi), %rax, %rbx
+    adcxq   %rax, %r11
+    adoxq   %rbx, %r12
+    mulxq   8(%rsi), %rax, %rbx
+    adcxq   %rax, %r12
+    adoxq   %rbx, %r13
+    mulxq   16(%rsi), %rax, %rbx
+    adcxq   %rax, %r13
+    adoxq   %rbx, %r14
+    mulxq   24(%rsi), %rax, %r15
+    adcxq   %rax, %r14
+    adoxq   %rbp, %r15
+    adcxq   %rbp, %r15
+
+    /* reduction, p3 in rcx */
+    movabsq $0x0800000000000011, %rcx
+
+    movq    %r8, %rdx
+    negq    %rdx                        /* m0 = -t0, CF = (t0 != 0) */
+    adcq    $0, %r9
+    adcq    $0, %r10
+    mulxq   %rcx, %rax, %rbx
+    adcq    %rax, %r11
+    adcq    %rbx, %r12
+    adcq    $0, %r13
+    adcq    $0, %r14
+    adcq    $0, %r15
+
+    movq    %r9, %rdx
+    negq    %rdx
+    adcq    $0, %r10
+    adcq    $0, %r11
+    mulxq   %rcx, %rax, %rbx
+    adcq    %rax, %r12
+    adcq    %rbx, %r13
+    adcq    $0, %r14
+    adcq    $0, %r15
+
+    movq    %r10, %rdx
+    negq    %rdx
+    adcq    $0, %r11
+    adcq    $0, %r12
+    mulxq   %rcx, %rax, %rbx
+    adcq    %rax, %r13
+    adcq    %rbx, %r14
+    adcq    $0, %r15
+
+    movq    %r11, %rdx
+    negq    %rdx
+    adcq    $0, %r12
+    adcq    $0, %r13
+    mulxq   %rcx, %rax, %rbx
+    adcq    %rax, %r14
+    adcq    %rbx, %r15
+
+    /* r = t[4..7] - p if t >= p (branch-free) */
+    movq    %r12, %rax
+    subq    $1, %rax
+    movq    %r13, %rbx
+    sbbq    $0, %rbx
+    movq    %r14, %rdx
+    sbbq    $0, %rdx
+    movq    %r15, %rbp
+    sbbq    %rcx, %rbp
+    cmovncq %rax, %r12
+    cmovncq %rbx, %r13
+    cmovncq %rdx, %r14
+    cmovncq %rbp, %r15
+    movq    %r12, (%rdi)
+    movq    %r13, 8(%rdi)
+    movq    %r14, 16(%rdi)
+    movq    %r15, 24(%rdi)
+
+    popq    %r15
+    popq    %r14
+    popq    %r13
+    popq    %r12
+    popq    %rbp
+    popq    %rbx
+    ret
+    .size   zk_felt_mont_mul_adx, .-zk_felt_mont_mul_adx
+    .section .note.GNU-stack,"",@progbits

@@ -68,8 +68,9 @@ int zkml_ctx_destroy(zkml_ctx *ctx);
 int zkml_ctx_device(const zkml_ctx *ctx);
 /* Kernel launches of this context so far (instrumentation for benchmarks). */
 uint64_t zkml_ctx_kernel_launches(const zkml_ctx *ctx);
-/* Per-kernel device timing with CUDA events (off by default).  When enabled,
- * each launch of the named kernel class is bracketed by events on the
+/* Per-kernel device timing with CUDA events (off by default).  `enable` is 0
+ * (off), -1 (every class) or a bit mask of classes in the order listed below
+ * (bit 0 = "restrict_cols").  Each launch of a timed class is bracketed by events on the
  * context's stream; zkml_ctx_kernel_time returns the accumulated milliseconds
  * and launch count.  Kernel classes: "restrict_cols", "restrict_rows",
  * "sumcheck_round", "merkle"; and two host-side phases timed by wall clock:
@@ -195,6 +196,32 @@ int zkml_reduce_activation_logup(zkml_ctx *ctx, const uint32_t *input, size_t ro
                                  const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
                                  zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                  uint32_t out_input_eval[4]);
+
+/* ---- Allocation-free restriction ------------------------------------------- */
+
+/* No counterpart in the reference: an extra entry point for callers that
+ * cannot allocate GPU memory (code running inside a memory pool it does not
+ * own, allocator callbacks, embedders with a fixed memory budget).  It computes
+ * the column restriction f[i] = sum_j B[i][j] * eq(r_j, j) of a rows x cols
+ * row-major M31 matrix -- the f_b that zkml_reduce_matmul_layer starts from --
+ * and allocates nothing: its scratch is one fixed-size array in the library's
+ * device code (about 2.3 MiB, held on every GPU that loads the library until
+ * the process exits).
+ *   b, out   device memory of the current GPU; out receives out_len QM31
+ *            (rows of them, zero-padded to out_len >= rows).
+ *   r_j      host, log2(next_pow2(cols)) QM31 challenges (first = most
+ *            significant column bit).
+ *   stream   cudaStream_t to run on (NULL = default stream); the call
+ *            synchronises that stream before returning.
+ * Limits: rows <= ZKML_NOALLOC_MAX_ROWS, cols <= ZKML_NOALLOC_MAX_COLS; larger
+ * sizes return ZKML_ERR_INVALID_ARG.  The first call on each device resolves
+ * the array's device address: make that first call before any stream capture.
+ * All calls share the one array, so calls whose GPU work overlaps (other
+ * threads, other streams) race and must be serialised by the caller. */
+#define ZKML_NOALLOC_MAX_ROWS 65536
+#define ZKML_NOALLOC_MAX_COLS (1 << 20)
+int zkml_restrict_cols_noalloc(const uint32_t *b, size_t rows, size_t cols, const uint32_t *r_j, size_t n_rj,
+                               uint32_t *out, size_t out_len, void *stream);
 
 #ifdef __cplusplus
 }

@@ -104,6 +104,8 @@ _SIGS = {
     "zkml_reduce_activation_logup": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int,
                                                C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                                C.c_size_t, C.POINTER(C.c_size_t), _u32]),
+    "zkml_restrict_cols_noalloc": (C.c_int, [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                                             C.c_void_p, C.c_size_t, C.c_void_p]),
     "zkml_prove_gkr_matmul": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                         C.c_void_p, C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t), _u64,
                                         _u64]),
@@ -328,8 +330,19 @@ class Context:
     def kernel_launches(self) -> int:
         return int(lib().zkml_ctx_kernel_launches(self.handle))
 
-    def enable_timing(self, enable: bool = True) -> None:
-        _check(lib().zkml_ctx_enable_timing(self.handle, int(enable)))
+    KERNEL_CLASSES = ("restrict_cols", "restrict_rows", "sumcheck_round", "merkle", "host_sync", "host_channel")
+
+    def enable_timing(self, enable: bool = True, classes: Optional[Sequence[str]] = None) -> None:
+        """Time every kernel class (default) or only `classes`; enable=False turns timing off."""
+        if not enable:
+            mask = 0
+        elif classes is None:
+            mask = -1
+        else:
+            mask = 0
+            for c in classes:
+                mask |= 1 << self.KERNEL_CLASSES.index(c)
+        _check(lib().zkml_ctx_enable_timing(self.handle, mask))
 
     def kernel_time(self, kernel: str) -> Tuple[float, int]:
         ms = C.c_double(0)
@@ -591,3 +604,26 @@ def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_t
                                               C.byref(channel.state), out, cap, C.byref(ln), ie))
     proof = ActivationLogUpProof(_felts(out, ln.value), ie, out[:4 * ln.value].copy())
     return proof, GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
+
+
+# ---------------------------------------------------------------------------
+# Allocation-free restriction (no reference counterpart)
+# ---------------------------------------------------------------------------
+
+NOALLOC_MAX_ROWS = 65536
+NOALLOC_MAX_COLS = 1 << 20
+
+
+def restrict_cols_noalloc(b, rows: int, cols: int, r_j, out, stream_ptr: Optional[int] = None) -> None:
+    """Column restriction into a caller-provided device buffer, allocating nothing.
+
+    For callers that cannot allocate GPU memory: ``b`` (rows x cols M31) and
+    ``out`` (>= rows QM31) are CUDA tensors the caller owns; the scratch is a
+    fixed array inside the library (rows <= 65536, cols <= 2^20).  Calls that
+    overlap on the GPU share that array and race.
+    """
+    bb, ob = _Buf(b), _Buf(out)
+    r_ptr, r_keep = _qm31_ptr(r_j)
+    n_rj = len(as_qm31_array(r_j))
+    _check(lib().zkml_restrict_cols_noalloc(bb.ptr, rows, cols, r_ptr, n_rj, ob.ptr, ob.nbytes // 16,
+                                            C.c_void_p(stream_ptr or 0)))

@@ -217,7 +217,7 @@ def run_b200(args):
         for _ in range(args.warmup):
             step(Amat, Bmat)
         if profile:
-            ctx.enable_timing(True)
+            ctx.enable_timing(True, classes=["restrict_cols"])
         barrier()
         l0 = ctx.kernel_launches()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

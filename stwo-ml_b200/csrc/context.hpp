@@ -91,6 +91,7 @@ struct zkml_ctx {
     int max_round_blocks = 0;
     // optional per-kernel-class event timing
     bool timing = false;
+    unsigned timing_mask = 0;  // bit i: time kernel class i
     struct KTime {
         double ms = 0;
         uint64_t launches = 0;

@@ -63,7 +63,10 @@ static cudaEvent_t pool_event(zkml_ctx* ctx) {
 }
 
 KTimer::KTimer(zkml_ctx* c, int k) : ctx(c), cls(k) {
-    if (!ctx->timing) return;
+    if (!ctx->timing || !(ctx->timing_mask & (1u << k))) {
+        cls = -1;
+        return;
+    }
     zkml_ctx::PendingEv p;
     p.cls = k;
     p.e0 = pool_event(ctx);
@@ -73,7 +76,7 @@ KTimer::KTimer(zkml_ctx* c, int k) : ctx(c), cls(k) {
 }
 
 KTimer::~KTimer() {
-    if (!ctx->timing) return;
+    if (cls < 0) return;
     cudaEventRecord(ctx->pending.back().e1, ctx->stream);
 }
 
@@ -99,10 +102,11 @@ struct HostTimer {
     int cls;
     std::chrono::steady_clock::time_point t0;
     HostTimer(zkml_ctx* c, int k) : ctx(c), cls(k) {
-        if (ctx->timing) t0 = std::chrono::steady_clock::now();
+        if (!ctx->timing || !(ctx->timing_mask & (1u << k))) cls = -1;
+        else t0 = std::chrono::steady_clock::now();
     }
     ~HostTimer() {
-        if (!ctx->timing) return;
+        if (cls < 0) return;
         ctx->ktime[cls].ms += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
         ctx->ktime[cls].launches++;
     }
@@ -412,6 +416,7 @@ int zkml_ctx_enable_timing(zkml_ctx* ctx, int enable) {
     ZK_CUDA(cudaStreamSynchronize(ctx->stream));
     drain_timers(ctx);
     ctx->timing = enable != 0;
+    ctx->timing_mask = enable < 0 ? ~0u : (unsigned)enable;
     for (auto& k : ctx->ktime) k = zkml_ctx::KTime();
     return ZKML_OK;
 }

@@ -88,6 +88,7 @@ struct zkml_ctx {
     uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
     uint32_t* d_sig = nullptr;      // device alias of h_sig
     uint32_t sig_seq = 0;           // last sequence number handed to a kernel
+    bool persistent = true;         // run sumcheck rounds in one cooperative launch
     int max_round_blocks = 0;
     // optional per-kernel-class event timing
     bool timing = false;
@@ -109,6 +110,11 @@ struct zkml_ctx {
     unsigned int* ticket() const { return small.as<unsigned int>(); }
     uint32_t* out_words() const { return small.as<uint32_t>() + 16; }  // 32 words
     uint32_t* err_flag() const { return small.as<uint32_t>() + 48; }
+    unsigned int* grid_bar() const { return small.as<unsigned int>() + 52; }       // 2 words
+    uint4* alpha_slot() const { return reinterpret_cast<uint4*>(small.as<uint32_t>() + 56); }
+    uint32_t* persist_status() const { return small.as<uint32_t>() + 60; }
+    uint32_t* h_msg() const { return h_sig + 64; }  // host -> GPU words (own cache lines)
+    uint32_t* d_msg() const { return d_sig + 64; }
     zk::RoundScratch round_scratch() const {
         zk::RoundScratch r;
         r.partials = partials.as<uint32_t>();

@@ -66,6 +66,32 @@ void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm3
 void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,
                        size_t len, qm31 alpha, uint32_t* out, uint32_t* sig, uint32_t seq, cudaStream_t s);
 
+// ---- persistent round loop ----------------------------------------------------
+// One cooperative launch runs every round of a degree-2 sumcheck: per round the
+// grid computes (s0, s1, s2) (with the previous fold fused in), block 0 publishes
+// them to the host (sig, sequence seq_base + r), waits for the host's challenge
+// in hostmsg (sequence word, then 4 challenge words, then an abort word), and a
+// grid barrier hands the challenge to all blocks.  After the last round block 0
+// publishes the final (a, b) with sequence seq_base + log_k.  All waits are
+// bounded; on a timeout the kernel sets status and exits.
+struct PersistArgs {
+    uint4* A;             // QM31 vectors (or fold targets in M31 mode)
+    uint4* B;
+    const uint32_t* A32;  // M31 inputs (M31 mode), else null
+    const uint32_t* B32;
+    size_t len;
+    int log_k;
+    uint32_t* partials;     // >= gridDim * 12 words
+    unsigned int* bar;      // [0] arrival count, [1] generation (zeroed)
+    uint4* alpha_dev;       // challenge broadcast slot
+    uint32_t* status;       // bit 0: barrier timeout, bit 1: host timeout / abort
+    uint32_t* sig;          // mapped host words written by the GPU
+    const uint32_t* hostmsg;  // mapped host words written by the host
+    uint32_t seq_base;
+};
+// Returns the grid size it launched (0 if a cooperative launch is not possible).
+int launch_sumcheck_persistent(const PersistArgs& a, int num_sms, cudaStream_t s, cudaError_t* err);
+
 // ---- generic MLE ops (ZkmlOps::evaluate_mle_at_point / restrict_mle) ----------
 // dst[i] = src[i] + r (src[i + h] - src[i]) for i < h (dst may alias src).
 void launch_mle_fold(const uint4* src, uint4* dst, size_t h, qm31 r, cudaStream_t s);

@@ -203,6 +203,93 @@ int read_err_flag(zkml_ctx* ctx) {
     return ZKML_OK;
 }
 
+// Hands the round-r challenge to the persistent kernel (or tells it to stop).
+static void post_challenge(zkml_ctx* ctx, uint32_t seq, const qm31& alpha, bool abort) {
+    volatile uint32_t* m = ctx->h_msg();
+    m[1] = alpha.a;
+    m[2] = alpha.b;
+    m[3] = alpha.c;
+    m[4] = alpha.d;
+    m[5] = abort ? 1u : 0u;
+    std::atomic_thread_fence(std::memory_order_release);
+    m[0] = seq;
+}
+
+// All rounds in one cooperative launch; the host only waits for round words
+// and posts challenges.  Returns ZKML_ERR_UNSUPPORTED if the launch is refused.
+static int run_sumcheck_persistent(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const uint32_t* B32,
+                                   size_t len, zkml_channel* chs, uint32_t* out_rp, uint32_t* out_ch,
+                                   uint32_t* fa_out, uint32_t* fb_out, const ClaimHook* hook) {
+    Channel ch(chs);
+    cudaStream_t s = ctx->stream;
+    const unsigned log_k = ilog2(len);
+    PersistArgs pa;
+    pa.A = A32 ? ctx->fa.as<uint4>() : A;
+    pa.B = B32 ? ctx->fb.as<uint4>() : B;
+    pa.A32 = A32;
+    pa.B32 = B32;
+    pa.len = len;
+    pa.log_k = (int)log_k;
+    pa.partials = ctx->partials.as<uint32_t>();
+    pa.bar = ctx->grid_bar();
+    pa.alpha_dev = ctx->alpha_slot();
+    pa.status = ctx->persist_status();
+    pa.sig = ctx->d_sig;
+    pa.hostmsg = ctx->d_msg();
+    pa.seq_base = ctx->sig_seq + 1;
+    ctx->sig_seq += log_k + 1;
+    ZK_CUDA(cudaMemsetAsync(ctx->persist_status(), 0, 4, s));
+    ZK_CUDA(cudaMemsetAsync(ctx->grid_bar(), 0, 8, s));
+    ctx->h_msg()[5] = 0;
+    cudaError_t e = cudaSuccess;
+    int grid;
+    {
+        KTimer t(ctx, KC_ROUND);
+        grid = launch_sumcheck_persistent(pa, ctx->num_sms, s, &e);
+    }
+    if (!grid) {
+        cudaGetLastError();
+        return ZKML_ERR_UNSUPPORTED;
+    }
+    ctx->launches++;
+    if (hook && hook->overlap) hook->overlap(hook->arg);
+    uint32_t words[12];
+    int rc = ZKML_OK;
+    for (unsigned r = 0; r < log_k; r++) {
+        if ((rc = wait_signal(ctx, pa.seq_base + r, words, 12))) break;
+        if (r == 0 && hook && hook->fn) hook->fn(hook->arg, qadd(ldq(words), ldq(words + 4)));
+        qm31 c0, c1, c2, alpha;
+        {
+            HostTimer ht(ctx, KC_HOST_CHANNEL);
+            interpolate(words, c0, c1, c2);
+            ch.mix_poly_coeffs(c0, c1, c2);
+            alpha = ch.draw_qm31();
+        }
+        post_challenge(ctx, pa.seq_base + r, alpha, false);
+        if (out_rp) {
+            stq(out_rp + 12 * r, c0);
+            stq(out_rp + 12 * r + 4, c1);
+            stq(out_rp + 12 * r + 8, c2);
+        }
+        if (out_ch) stq(out_ch + 4 * r, alpha);
+    }
+    if (!rc) rc = wait_signal(ctx, pa.seq_base + log_k, words, 8);
+    if (rc) {
+        // release the kernel (it exits on the abort word) before reporting
+        post_challenge(ctx, pa.seq_base, qzero(), true);
+        cudaStreamSynchronize(s);
+        return rc;
+    }
+    memcpy(fa_out, words, 16);
+    memcpy(fb_out, words + 4, 16);
+    uint32_t status = 0;
+    ZK_CUDA(cudaMemcpyAsync(&status, ctx->persist_status(), 4, cudaMemcpyDeviceToHost, s));
+    if ((rc = read_err_flag(ctx))) return rc;
+    if (status) return set_error(ZKML_ERR_TIMEOUT, "sumcheck round kernel timed out waiting (status " +
+                                                       std::to_string(status) + ")");
+    return check_err_flag(ctx, "reduce_matmul_layer");
+}
+
 // The sumcheck round loop over (A, B).  In M31 mode A32/B32 hold the base-field
 // vectors (length len) and the first fold writes QM31 into ctx->fa / fb.
 int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
@@ -232,6 +319,11 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
         if (hook && hook->overlap) hook->overlap(hook->arg);
         if (hook && hook->fn) hook->fn(hook->arg, qmul(ldq(fa_out), ldq(fb_out)));
         return ZKML_OK;
+    }
+    if (ctx->persistent) {
+        rc = run_sumcheck_persistent(ctx, A, B, A32, B32, len, chs, out_rp, out_ch, fa_out, fb_out, hook);
+        if (rc != ZKML_ERR_UNSUPPORTED) return rc;
+        ctx->persistent = false;  // cooperative launch unavailable: use one launch per round
     }
     rs.seq = ++ctx->sig_seq;
     {
@@ -360,6 +452,10 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     zkml_ctx* ctx = new zkml_ctx();
     ctx->device = device;
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+    {
+        const char* pv = getenv("ZKML_PERSISTENT_ROUNDS");
+        if (pv && pv[0] == '0') ctx->persistent = false;
+    }
     ctx->max_round_blocks = ctx->num_sms * 8;
     int rc = ZKML_OK;
     e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);

@@ -528,6 +528,193 @@ void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, cons
     final_fold_kernel<<<1, 32, 0, s>>>(A, B, A32, B32, alpha, out, sig, seq);
 }
 
+// ---------------------------------------------------------------------------
+// Persistent cooperative round loop (see kernels.cuh).
+// ---------------------------------------------------------------------------
+constexpr unsigned long long kSpinLimit = 1ull << 25;  // ~ seconds with the back-off below
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded grid barrier among the co-resident blocks of one cooperative launch.
+__device__ bool grid_barrier(unsigned int* bar, uint32_t* status) {
+    __shared__ bool ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ok = true;
+        volatile unsigned int* gen = bar + 1;
+        const unsigned int my_gen = *gen;
+        __threadfence();
+        if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            unsigned long long it = 0;
+            while (*gen == my_gen) {
+                if (++it > kSpinLimit) {
+                    atomicOr(status, 1u);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return ok;
+}
+
+__global__ void __launch_bounds__(256) sumcheck_persistent_kernel(PersistArgs p) {
+    __shared__ uint32_t sh[32][12];
+    __shared__ uint32_t res[12];
+    __shared__ bool stop;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nthreads = (size_t)gridDim.x * blockDim.x;
+    uint4* A = p.A;
+    uint4* B = p.B;
+    size_t len = p.len;
+    qm31 alpha = qzero();
+    for (int r = 0; r <= p.log_k; r++) {
+        if (r == p.log_k) {
+            // final fold of the length-2 vectors by block 0
+            if (blockIdx.x == 0 && threadIdx.x == 0) {
+                qm31 a, b;
+                if (p.A32 && r == 1) {
+                    a = fold_m31(red32(p.A32[0]), red32(p.A32[1]), alpha);
+                    b = fold_m31(red32(p.B32[0]), red32(p.B32[1]), alpha);
+                } else {
+                    const qm31 a0 = ld_q(A), a1 = ld_q(A + 1), b0 = ld_q(B), b1 = ld_q(B + 1);
+                    a = qadd(a0, qmul(alpha, qsub(a1, a0)));
+                    b = qadd(b0, qmul(alpha, qsub(b1, b0)));
+                }
+                const uint32_t w[8] = {a.a, a.b, a.c, a.d, b.a, b.b, b.c, b.d};
+                publish(p.sig, p.seq_base + r, w, 8);
+            }
+            return;
+        }
+        Sums s;
+        sums_zero(s);
+        if (r == 0) {
+            const size_t q = len / 2;
+            if (p.A32) {
+                unsigned long long s0 = 0, s1 = 0, s2 = 0;
+                for (size_t i = tid; i < q; i += nthreads) {
+                    const uint32_t alo = red32(p.A32[i]), ahi = red32(p.A32[i + q]);
+                    const uint32_t blo = red32(p.B32[i]), bhi = red32(p.B32[i + q]);
+                    s0 += mmul(alo, blo);
+                    s1 += mmul(ahi, bhi);
+                    s2 += mmul(msub(madd(ahi, ahi), alo), msub(madd(bhi, bhi), blo));
+                }
+                s.v[0] = s0;
+                s.v[4] = s1;
+                s.v[8] = s2;
+            } else {
+                for (size_t i = tid; i < q; i += nthreads)
+                    round_terms(ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q), s);
+            }
+        } else {
+            // fold (len -> len / 2) fused with this round's sums
+            const size_t h = len / 2, q = h / 2;
+            const bool from_m31 = p.A32 && r == 1;
+            for (size_t i = tid; i < q; i += nthreads) {
+                qm31 alo, ahi, blo, bhi;
+                if (from_m31) {
+                    alo = fold_m31(red32(p.A32[i]), red32(p.A32[i + h]), alpha);
+                    ahi = fold_m31(red32(p.A32[i + q]), red32(p.A32[i + q + h]), alpha);
+                    blo = fold_m31(red32(p.B32[i]), red32(p.B32[i + h]), alpha);
+                    bhi = fold_m31(red32(p.B32[i + q]), red32(p.B32[i + q + h]), alpha);
+                } else {
+                    const qm31 a0 = ld_q(A + i), a1 = ld_q(A + i + q), a2 = ld_q(A + i + h), a3 = ld_q(A + i + q + h);
+                    const qm31 b0 = ld_q(B + i), b1 = ld_q(B + i + q), b2 = ld_q(B + i + h), b3 = ld_q(B + i + q + h);
+                    alo = qadd(a0, qmul(alpha, qsub(a2, a0)));
+                    ahi = qadd(a1, qmul(alpha, qsub(a3, a1)));
+                    blo = qadd(b0, qmul(alpha, qsub(b2, b0)));
+                    bhi = qadd(b1, qmul(alpha, qsub(b3, b1)));
+                }
+                st_q(A + i, alo);
+                st_q(A + i + q, ahi);
+                st_q(B + i, blo);
+                st_q(B + i + q, bhi);
+                round_terms(alo, ahi, blo, bhi, s);
+            }
+            len = h;
+        }
+        // block partials
+#pragma unroll
+        for (int i = 0; i < 12; i++) {
+            uint32_t v = red64(s.v[i]);
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
+            if (lane == 0) sh[warp][i] = v;
+        }
+        __syncthreads();
+        if (threadIdx.x < 12) {
+            uint32_t acc = 0;
+            for (int w = 0; w < nw; w++) acc = madd(acc, sh[w][threadIdx.x]);
+            p.partials[blockIdx.x * 12 + threadIdx.x] = acc;
+        }
+        if (!grid_barrier(p.bar, p.status)) return;
+        if (blockIdx.x == 0) {
+            for (int i = warp; i < 12; i += nw) {
+                unsigned long long acc = 0;
+                for (unsigned b = lane; b < gridDim.x; b += 32) acc += __ldcg(p.partials + b * 12 + i);
+                uint32_t v = red64(acc);
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
+                if (lane == 0) res[i] = v;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                publish(p.sig, p.seq_base + r, res, 12);
+                // wait for the host's challenge for this round
+                const uint32_t want = p.seq_base + r;
+                unsigned long long it = 0;
+                bool got = false;
+                volatile const uint32_t* hm = p.hostmsg;
+                while (!got) {
+                    if (ld_acquire_sys(p.hostmsg) == want || hm[5] != 0) {
+                        got = true;
+                        break;
+                    }
+                    if (++it > kSpinLimit) break;
+                    __nanosleep(128);
+                }
+                const bool abort = !got || hm[5] != 0;
+                if (abort) atomicOr(p.status, 2u);
+                *p.alpha_dev = make_uint4(hm[1], hm[2], hm[3], hm[4]);
+                stop = abort;
+                __threadfence();
+            }
+        }
+        if (!grid_barrier(p.bar, p.status)) return;
+        if (*((volatile uint32_t*)p.status) & 2u) return;
+        const uint4 av = __ldcg(p.alpha_dev);
+        alpha = qm(av.x, av.y, av.z, av.w);
+        (void)stop;
+    }
+}
+
+int launch_sumcheck_persistent(const PersistArgs& a, int num_sms, cudaStream_t s, cudaError_t* err) {
+    int per_sm = 0;
+    *err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sumcheck_persistent_kernel, 256, 0);
+    if (*err != cudaSuccess || per_sm <= 0) return 0;
+    size_t want = (a.len / 2 + 255) / 256;
+    size_t cap = (size_t)per_sm * num_sms;
+    if (cap > (size_t)num_sms * 4) cap = (size_t)num_sms * 4;
+    if (want > cap) want = cap;
+    if (want == 0) want = 1;
+    PersistArgs args = a;
+    void* params[] = {&args};
+    *err = cudaLaunchCooperativeKernel((const void*)sumcheck_persistent_kernel, dim3((unsigned)want), dim3(256),
+                                       params, 0, s);
+    return *err == cudaSuccess ? (int)want : 0;
+}
+
 __global__ void mle_fold_kernel(const uint4* src, uint4* dst, size_t h, qm31 r) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < h; i += (size_t)gridDim.x * blockDim.x) {
         qm31 lo = ld_q(src + i), hi = ld_q(src + i + h);

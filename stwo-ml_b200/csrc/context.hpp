@@ -88,7 +88,7 @@ struct zkml_ctx {
     uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
     uint32_t* d_sig = nullptr;      // device alias of h_sig
     uint32_t sig_seq = 0;           // last sequence number handed to a kernel
-    bool persistent = true;         // run sumcheck rounds in one cooperative launch
+    bool persistent = false;        // run sumcheck rounds in one cooperative launch (ZKML_PERSISTENT_ROUNDS=1)
     int max_round_blocks = 0;
     // optional per-kernel-class event timing
     bool timing = false;

@@ -454,7 +454,7 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     {
         const char* pv = getenv("ZKML_PERSISTENT_ROUNDS");
-        if (pv && pv[0] == '0') ctx->persistent = false;
+        if (pv) ctx->persistent = pv[0] == '1';
     }
     ctx->max_round_blocks = ctx->num_sms * 8;
     int rc = ZKML_OK;

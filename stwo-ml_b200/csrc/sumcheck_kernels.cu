@@ -84,12 +84,22 @@ void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaS
 // ---------------------------------------------------------------------------
 constexpr int RC_UNROLL = 8;
 
-template <bool VEC>
+constexpr uint32_t RC_SMEM_LHI = 1024;  // lhi entries staged in shared memory (n <= 65536)
+
+template <bool VEC, bool SMEM_LHI>
 __global__ void __launch_bounds__(256, 4)
     restrict_cols_kernel(const uint32_t* __restrict__ B, uint32_t k, uint32_t n, uint32_t s_row,
-                         unsigned long long total, const uint4* __restrict__ lhi,
+                         unsigned long long total, const uint4* __restrict__ lhi_g,
                          const uint4* __restrict__ llo, unsigned long long* __restrict__ acc_out,
                          uint32_t* __restrict__ err) {
+    // The per-stripe lhi factor is read from shared memory when the table fits:
+    // a global (L1) read there sits on the multiply's dependency chain.
+    __shared__ uint4 sh_lhi[SMEM_LHI ? RC_SMEM_LHI : 1];
+    if (SMEM_LHI) {
+        for (uint32_t i = threadIdx.x; i < s_row; i += blockDim.x) sh_lhi[i] = lhi_g[i];
+        __syncthreads();
+    }
+    const uint4* lhi = SMEM_LHI ? sh_lhi : lhi_g;
     const uint32_t lane = threadIdx.x & 31;
     const unsigned long long warp = ((unsigned long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const unsigned long long nwarps = ((unsigned long long)gridDim.x * blockDim.x) >> 5;
@@ -118,7 +128,7 @@ __global__ void __launch_bounds__(256, 4)
             for (int u = 0; u < RC_UNROLL; u++) v[u] = __ldcs(base + 32 * u);
 #pragma unroll
             for (int u = 0; u < RC_UNROLL; u++) {
-                const uint4 lh = __ldg(lhi + jh + u);
+                const uint4 lh = lhi[jh + u];
                 bad |= v[u].x | v[u].y;
                 acc[0][0] += (unsigned long long)v[u].x * lh.x;
                 acc[0][1] += (unsigned long long)v[u].x * lh.y;
@@ -153,7 +163,7 @@ __global__ void __launch_bounds__(256, 4)
 #pragma unroll
             for (int u = 0; u < RC_UNROLL; u++) {
                 if (u < (int)cnt) {
-                    const uint4 lh = __ldg(lhi + jh + u);
+                    const uint4 lh = lhi[jh + u];
                     bad |= v[u].x | v[u].y;
                     acc[0][0] += (unsigned long long)v[u].x * lh.x;
                     acc[0][1] += (unsigned long long)v[u].x * lh.y;
@@ -219,10 +229,15 @@ void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4
     if (blocks > need) blocks = need;
     if (blocks == 0) blocks = 1;
     const bool vec = (n % 2 == 0) && ((reinterpret_cast<uintptr_t>(B) & 7) == 0);
-    if (vec)
-        restrict_cols_kernel<true><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
+    const bool sm = s_row <= RC_SMEM_LHI;
+    if (vec && sm)
+        restrict_cols_kernel<true, true><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
+    else if (vec)
+        restrict_cols_kernel<true, false><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
+    else if (sm)
+        restrict_cols_kernel<false, true><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
     else
-        restrict_cols_kernel<false><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
+        restrict_cols_kernel<false, false><<<(unsigned)blocks, threads, 0, s>>>(B, k, n, s_row, total, lhi, llo, acc, err);
 }
 
 // ---------------------------------------------------------------------------
@@ -572,7 +587,6 @@ __device__ bool grid_barrier(unsigned int* bar, uint32_t* status) {
 __global__ void __launch_bounds__(256) sumcheck_persistent_kernel(PersistArgs p) {
     __shared__ uint32_t sh[32][12];
     __shared__ uint32_t res[12];
-    __shared__ bool stop;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nthreads = (size_t)gridDim.x * blockDim.x;
     uint4* A = p.A;
@@ -687,7 +701,6 @@ __global__ void __launch_bounds__(256) sumcheck_persistent_kernel(PersistArgs p)
                 const bool abort = !got || hm[5] != 0;
                 if (abort) atomicOr(p.status, 2u);
                 *p.alpha_dev = make_uint4(hm[1], hm[2], hm[3], hm[4]);
-                stop = abort;
                 __threadfence();
             }
         }
@@ -695,7 +708,6 @@ __global__ void __launch_bounds__(256) sumcheck_persistent_kernel(PersistArgs p)
         if (*((volatile uint32_t*)p.status) & 2u) return;
         const uint4 av = __ldcg(p.alpha_dev);
         alpha = qm(av.x, av.y, av.z, av.w);
-        (void)stop;
     }
 }
 

@@ -290,6 +290,92 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def product_bytes(n):
+    """Algorithmic HBM bytes of one length-n M31 product sumcheck on one device.
+
+    Round 0 reads both M31 vectors (8n); the fused fold+round from M31 reads
+    them again and writes two QM31 halves (8n + 16n); each later fused
+    fold+round over length L reads 32L and writes 16L.
+    """
+    total = 8 * n + 8 * n + 16 * n
+    length = n // 2
+    while length > 2:
+        total += 48 * length
+        length //= 2
+    return total
+
+
+def run_product(args):
+    """The MLE-sweep product sumcheck (config 5) split across the GPUs (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    import zkml_b200 as Z
+    from zkml_b200.distributed import GpuSumcheckSession, TorchCollective, prove_product_sharded
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local if world > 1 else 0)
+    dist.init_process_group("nccl" if world > 1 else "gloo", rank=rank, world_size=world,
+                            **({"device_id": torch.device("cuda", local)} if world > 1 else
+                               {"init_method": "tcp://127.0.0.1:%d" % (29500 + os.getpid() % 1000)}))
+    dev = torch.cuda.current_device()
+    stream = torch.cuda.current_stream()
+    ctx = Z.Context(dev)
+    ctx.set_stream(stream.cuda_stream)
+    session = GpuSumcheckSession(ctx)
+    col = TorchCollective()
+    n = 1 << args.log_n
+    n_loc = n // world
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    a = torch.randint(0, 2**31 - 1, (n_loc,), dtype=torch.int32, device="cuda", generator=g)
+    b = torch.randint(0, 2**31 - 1, (n_loc,), dtype=torch.int32, device="cuda", generator=g)
+
+    def step():
+        return prove_product_sharded(a, b, n, Z.PoseidonChannel(), session=session, collective=col)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    l0 = ctx.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            proof = step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    launches = ctx.kernel_launches() - l0
+    dist.barrier()
+    if rank == 0:
+        peak, peak_kind = measured_peak_hbm()
+        # per-GPU bytes until the gather, then one GPU's share of the tail
+        per_gpu = product_bytes(n_loc)
+        achieved = per_gpu / (ms * 1e-3) / 1e9
+        elems = 2 * (2 * n - 2)
+        print(json.dumps({
+            "metric": f"product sumcheck MLE elems folded/s (config 5, N = 2^{args.log_n} M31, two MLEs)",
+            "value": elems / (ms * 1e-3), "unit": "elems/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u32 (M31/QM31 integer)", "data": "synthetic (torch-seeded M31)",
+            "config": {"workload": "C5 degree-2 product sumcheck, MLE split by low index bits",
+                       "log_n": args.log_n, "gathered_at": proof.gathered_at,
+                       "l2": "inputs larger than L2" if 8 * n_loc > 126e6 else "inputs fit in L2"},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": "sumcheck rounds (whole proof)", "achieved": achieved,
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "algorithmic_bytes_per_gpu": per_gpu},
+            "clocks": clk.summary(),
+        }), flush=True)
+    dist.destroy_process_group()
+
+
 def run_case(name):
     """Small fixed workloads for ncu captures (one kernel class each)."""
     import torch
@@ -318,6 +404,15 @@ def run_case(name):
         pt, val = random_qm31(20, rng), random_qm31(1, rng)[0]
         for _ in range(2):
             Z.reduce_activation_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), 5, Z.PoseidonChannel())
+    elif name.startswith("product_"):  # the product sumcheck of 2^L M31 elements, twice
+        from zkml_b200.distributed import GpuSumcheckSession, LocalCollective, prove_product_sharded
+        lg = int(name.split("_")[1])
+        g = torch.Generator(device="cuda").manual_seed(1234)
+        a = torch.randint(0, 2**31 - 1, (1 << lg,), dtype=torch.int32, device="cuda", generator=g)
+        b = torch.randint(0, 2**31 - 1, (1 << lg,), dtype=torch.int32, device="cuda", generator=g)
+        for _ in range(2):
+            prove_product_sharded(a, b, 1 << lg, Z.PoseidonChannel(), session=GpuSumcheckSession(),
+                                  collective=LocalCollective())
     else:
         raise SystemExit(f"unknown case {name}")
     torch.cuda.synchronize()
@@ -330,13 +425,18 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["c2", "product"], default="c2",
+                    help="c2: the headline matmul layer; product: the config-5 product sumcheck split across GPUs")
+    ap.add_argument("--log-n", type=int, default=28, help="product workload: log2 of the MLE length")
     args = ap.parse_args()
     if args.case:
         run_case(args.case)
         return
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "product" and args.impl == "b200":
+        run_product(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

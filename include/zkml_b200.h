@@ -197,6 +197,27 @@ int zkml_reduce_activation_logup(zkml_ctx *ctx, const uint32_t *input, size_t ro
                                  zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                  uint32_t out_input_eval[4]);
 
+/* ---- Stepwise product sumcheck (multi-GPU building block) -------------------
+ * The round loop of ZkmlOps::reduce_matmul_layer (backend.rs:141-178) one round
+ * at a time, so that a caller can split one sumcheck across GPUs: rank g of G
+ * loads the elements with index = g (mod G); local round sums of all ranks add
+ * up to the global ones while the local length is >= 2 (fold partners stay on
+ * one rank), and below a threshold the local vectors are exported, gathered
+ * (global[j*G + g] = local_g[j]) and loaded on one GPU.  The Fiat-Shamir
+ * channel stays with the caller. */
+/* Load two M31 (u32) or QM31 (4 x u32) vectors of length n (power of two >= 2). */
+int zkml_sumcheck_load_m31(zkml_ctx *ctx, const uint32_t *a, const uint32_t *b, size_t n);
+int zkml_sumcheck_load_qm31(zkml_ctx *ctx, const uint32_t *a, const uint32_t *b, size_t n);
+/* Current vector length (0 without a session). */
+size_t zkml_sumcheck_length(const zkml_ctx *ctx);
+/* If alpha != NULL, fold both vectors with it first (length halves); then write
+ * (s0, s1, s2) = (sum a_lo b_lo, sum a_hi b_hi, sum (2a_hi - a_lo)(2b_hi - b_lo)). */
+int zkml_sumcheck_round(zkml_ctx *ctx, const uint32_t *alpha, uint32_t out_sums[12]);
+/* Copy the current (folded, QM31) vectors to a and b (host or device). */
+int zkml_sumcheck_export(zkml_ctx *ctx, uint32_t *out_a, uint32_t *out_b);
+/* Fold length-2 vectors with alpha into the final values. */
+int zkml_sumcheck_finalize(zkml_ctx *ctx, const uint32_t alpha[4], uint32_t out_a[4], uint32_t out_b[4]);
+
 /* ---- Allocation-free restriction ------------------------------------------- */
 
 /* No counterpart in the reference: an extra entry point for callers that

@@ -83,7 +83,13 @@ struct zkml_ctx {
     zk::DevBuf eq_a, eq_hi, eq_lo;  // eq tables
     zk::DevBuf partials;            // per-block round partials
     zk::DevBuf small;               // ticket + out words + error flag
-    zk::DevBuf act_tables[6];       // activation lookup tables by type tag (device copies)
+    zk::DevBuf act_tables[6];
+    // stepwise product-sumcheck session (zkml_sumcheck_*)
+    zk::DevBuf sc_a, sc_b;          // staged M31 inputs
+    const uint32_t* sc_a32 = nullptr;
+    const uint32_t* sc_b32 = nullptr;
+    size_t sc_len = 0;              // current vector length (0 = no session)
+    bool sc_m31 = false;            // vectors are still the M31 inputs       // activation lookup tables by type tag (device copies)
     uint32_t* h_small = nullptr;    // pinned host mirror of `small`
     uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
     uint32_t* d_sig = nullptr;      // device alias of h_sig

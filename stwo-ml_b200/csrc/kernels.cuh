@@ -50,6 +50,8 @@ struct RoundScratch {
     uint32_t* sig;
     uint32_t seq;
 };
+// Reduce n u32 words in place to [0, P) (the round kernels need canonical QM31 input).
+void launch_canon_words(uint32_t* w, size_t n, cudaStream_t s);
 // Round sums over QM31 vectors of length len (no fold).
 void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s);
 // Fold A, B in place with alpha (len -> len/2) and emit the next round's sums.

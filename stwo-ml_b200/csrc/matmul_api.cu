@@ -494,6 +494,8 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
                       &ctx->eq_a, &ctx->eq_hi, &ctx->eq_lo, &ctx->partials, &ctx->small};
     for (DevBuf* b : bufs) b->release();
     for (DevBuf& t : ctx->act_tables) t.release();
+    ctx->sc_a.release();
+    ctx->sc_b.release();
     if (ctx->h_small) cudaFreeHost(ctx->h_small);
     if (ctx->h_sig) cudaFreeHost(ctx->h_sig);
     drain_timers(ctx);

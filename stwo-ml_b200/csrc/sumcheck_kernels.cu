@@ -7,6 +7,7 @@
 // four products (each product < 2^62, so four of them plus a reduced residue
 // still fit in 64 bits).
 #include "kernels.cuh"
+#include "round_arith.cuh"
 
 namespace zk {
 
@@ -297,6 +298,18 @@ void launch_acc_finalize(const unsigned long long* acc, size_t n_rows, uint4* ou
     acc_finalize_kernel<<<(unsigned)blocks, 256, 0, s>>>(acc, n_rows, out, out_len);
 }
 
+__global__ void canon_words_kernel(uint32_t* __restrict__ w, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        w[i] = red32(w[i]);
+}
+
+void launch_canon_words(uint32_t* w, size_t n, cudaStream_t s) {
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    if (blocks == 0) blocks = 1;
+    canon_words_kernel<<<(unsigned)blocks, 256, 0, s>>>(w, n);
+}
+
 __global__ void m31_to_qm31_kernel(const uint32_t* __restrict__ in, size_t n, uint4* __restrict__ out,
                                    size_t out_len, uint32_t* __restrict__ err) {
     uint32_t bad = 0;
@@ -387,82 +400,83 @@ __device__ void finish_sums(Sums& s, uint32_t* __restrict__ partials, unsigned i
     }
 }
 
-__device__ __forceinline__ void round_terms(const qm31& alo, const qm31& ahi, const qm31& blo, const qm31& bhi,
-                                            Sums& s) {
-    qm31 p0 = qmul(alo, blo);
-    qm31 p1 = qmul(ahi, bhi);
-    qm31 p2 = qmul(qsub(qdbl(ahi), alo), qsub(qdbl(bhi), blo));
-    sums_add(s, p0, p1, p2);
-}
-
 __device__ __forceinline__ void sums_zero(Sums& s) {
 #pragma unroll
     for (int i = 0; i < 12; i++) s.v[i] = 0;
 }
 
+// The per-thread round accumulators as the 12 canonical words of finish_sums.
+__device__ __forceinline__ void racc_to_sums(const RoundAcc& r, Sums& s) {
+    const qm31 x0 = qacc_value(r.p0), x1 = qacc_value(r.p1), x2 = qacc_value(r.p2);
+    sums_zero(s);
+    sums_add(s, x0, x1, x2);
+}
+
 __global__ void __launch_bounds__(256) round_qm31_kernel(const uint4* __restrict__ A, const uint4* __restrict__ B,
                                                          size_t q, uint32_t* partials, unsigned int* ticket,
                                                          uint32_t* out, uint32_t* sig, uint32_t seq) {
-    Sums s;
-    sums_zero(s);
+    RoundAcc acc;
+    racc_zero(acc);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x)
-        round_terms(ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q), s);
+        racc_add(acc, ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q));
+    Sums s;
+    racc_to_sums(acc, s);
     finish_sums(s, partials, ticket, out, sig, seq);
 }
 
 // In-place fold with alpha fused with the next round's sums.  Thread i reads
 // elements i, i+q, i+h, i+q+h (h = len/2, q = h/2) and writes i and i+q: every
 // element is read by exactly one thread, so the in-place update is race-free.
+// Inputs must be canonical (< P); outputs are canonical.
 __global__ void __launch_bounds__(256) fold_round_qm31_kernel(uint4* __restrict__ A, uint4* __restrict__ B, size_t h,
                                                               qm31 alpha, uint32_t* partials, unsigned int* ticket,
                                                               uint32_t* out, uint32_t* sig, uint32_t seq) {
     const size_t q = h / 2;
-    Sums s;
-    sums_zero(s);
+    const AlphaRows m = alpha_rows(alpha);
+    RoundAcc acc;
+    racc_zero(acc);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        qm31 a0 = ld_q(A + i), a1 = ld_q(A + i + q), a2 = ld_q(A + i + h), a3 = ld_q(A + i + q + h);
-        qm31 b0 = ld_q(B + i), b1 = ld_q(B + i + q), b2 = ld_q(B + i + h), b3 = ld_q(B + i + q + h);
-        qm31 alo = qadd(a0, qmul(alpha, qsub(a2, a0)));
-        qm31 ahi = qadd(a1, qmul(alpha, qsub(a3, a1)));
-        qm31 blo = qadd(b0, qmul(alpha, qsub(b2, b0)));
-        qm31 bhi = qadd(b1, qmul(alpha, qsub(b3, b1)));
+        const qm31 a0 = ld_q(A + i), a1 = ld_q(A + i + q), a2 = ld_q(A + i + h), a3 = ld_q(A + i + q + h);
+        const qm31 b0 = ld_q(B + i), b1 = ld_q(B + i + q), b2 = ld_q(B + i + h), b3 = ld_q(B + i + q + h);
+        const qm31 alo = fold_qq(a0, a2, m), ahi = fold_qq(a1, a3, m);
+        const qm31 blo = fold_qq(b0, b2, m), bhi = fold_qq(b1, b3, m);
         st_q(A + i, alo);
         st_q(A + i + q, ahi);
         st_q(B + i, blo);
         st_q(B + i + q, bhi);
-        round_terms(alo, ahi, blo, bhi, s);
+        racc_add(acc, alo, ahi, blo, bhi);
     }
+    Sums s;
+    racc_to_sums(acc, s);
     finish_sums(s, partials, ticket, out, sig, seq);
 }
 
+// Base-field round: products of M31 values accumulate lazily (acc_fold).  Any
+// input word with bit 31 set is not an M31 element and raises the error flag.
 __global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restrict__ A, const uint32_t* __restrict__ B,
                                                         size_t q, uint32_t* partials, unsigned int* ticket,
                                                         uint32_t* out, uint32_t* err, uint32_t* sig, uint32_t seq) {
-    unsigned long long s0 = 0, s1 = 0, s2 = 0;
+    uint64_t s0 = 0, s1 = 0, s2 = 0;
     uint32_t bad = 0;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        uint32_t alo = __ldcs(A + i), ahi = __ldcs(A + i + q), blo = __ldcs(B + i), bhi = __ldcs(B + i + q);
+        const uint32_t alo = __ldcs(A + i), ahi = __ldcs(A + i + q), blo = __ldcs(B + i), bhi = __ldcs(B + i + q);
         bad |= alo | ahi | blo | bhi;
-        alo = red32(alo);
-        ahi = red32(ahi);
-        blo = red32(blo);
-        bhi = red32(bhi);
-        s0 += mmul(alo, blo);
-        s1 += mmul(ahi, bhi);
-        s2 += mmul(msub(madd(ahi, ahi), alo), msub(madd(bhi, bhi), blo));
+        s0 = acc_fold(s0, mul_wide(alo, blo));
+        s1 = acc_fold(s1, mul_wide(ahi, bhi));
+        s2 = acc_fold(s2, mul_wide(csub(cdbl(ahi), alo), csub(cdbl(bhi), blo)));
     }
     if (bad & 0x80000000u) atomicOr(err, 1u);
     Sums s;
     sums_zero(s);
-    s.v[0] = s0;
-    s.v[4] = s1;
-    s.v[8] = s2;
+    s.v[0] = canon64(s0);
+    s.v[4] = canon64(s1);
+    s.v[8] = canon64(s2);
     finish_sums(s, partials, ticket, out, sig, seq);
 }
 
 // lo + alpha (hi - lo) with lo, hi in M31.
 __device__ __forceinline__ qm31 fold_m31(uint32_t lo, uint32_t hi, const qm31& alpha) {
-    return qadd(qm(lo, 0, 0, 0), qmul_m(alpha, msub(hi, lo)));
+    return fold_mq(red32(lo), red32(hi), alpha);
 }
 
 __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __restrict__ A,
@@ -471,19 +485,19 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
                                                              uint32_t* partials, unsigned int* ticket, uint32_t* out,
                                                              uint32_t* sig, uint32_t seq) {
     const size_t q = h / 2;
-    Sums s;
-    sums_zero(s);
+    RoundAcc acc;
+    racc_zero(acc);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        qm31 alo = fold_m31(red32(A[i]), red32(A[i + h]), alpha);
-        qm31 ahi = fold_m31(red32(A[i + q]), red32(A[i + q + h]), alpha);
-        qm31 blo = fold_m31(red32(B[i]), red32(B[i + h]), alpha);
-        qm31 bhi = fold_m31(red32(B[i + q]), red32(B[i + q + h]), alpha);
+        const qm31 alo = fold_mq(A[i], A[i + h], alpha), ahi = fold_mq(A[i + q], A[i + q + h], alpha);
+        const qm31 blo = fold_mq(B[i], B[i + h], alpha), bhi = fold_mq(B[i + q], B[i + q + h], alpha);
         st_q(Ao + i, alo);
         st_q(Ao + i + q, ahi);
         st_q(Bo + i, blo);
         st_q(Bo + i + q, bhi);
-        round_terms(alo, ahi, blo, bhi, s);
+        racc_add(acc, alo, ahi, blo, bhi);
     }
+    Sums s;
+    racc_to_sums(acc, s);
     finish_sums(s, partials, ticket, out, sig, seq);
 }
 
@@ -613,28 +627,32 @@ __global__ void __launch_bounds__(256) sumcheck_persistent_kernel(PersistArgs p)
         }
         Sums s;
         sums_zero(s);
+        RoundAcc racc;
+        racc_zero(racc);
         if (r == 0) {
             const size_t q = len / 2;
             if (p.A32) {
-                unsigned long long s0 = 0, s1 = 0, s2 = 0;
+                uint64_t s0 = 0, s1 = 0, s2 = 0;
                 for (size_t i = tid; i < q; i += nthreads) {
                     const uint32_t alo = red32(p.A32[i]), ahi = red32(p.A32[i + q]);
                     const uint32_t blo = red32(p.B32[i]), bhi = red32(p.B32[i + q]);
-                    s0 += mmul(alo, blo);
-                    s1 += mmul(ahi, bhi);
-                    s2 += mmul(msub(madd(ahi, ahi), alo), msub(madd(bhi, bhi), blo));
+                    s0 = acc_fold(s0, mul_wide(alo, blo));
+                    s1 = acc_fold(s1, mul_wide(ahi, bhi));
+                    s2 = acc_fold(s2, mul_wide(csub(cdbl(ahi), alo), csub(cdbl(bhi), blo)));
                 }
-                s.v[0] = s0;
-                s.v[4] = s1;
-                s.v[8] = s2;
+                s.v[0] = canon64(s0);
+                s.v[4] = canon64(s1);
+                s.v[8] = canon64(s2);
             } else {
                 for (size_t i = tid; i < q; i += nthreads)
-                    round_terms(ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q), s);
+                    racc_add(racc, ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q));
+                racc_to_sums(racc, s);
             }
         } else {
             // fold (len -> len / 2) fused with this round's sums
             const size_t h = len / 2, q = h / 2;
             const bool from_m31 = p.A32 && r == 1;
+            const AlphaRows m = alpha_rows(alpha);
             for (size_t i = tid; i < q; i += nthreads) {
                 qm31 alo, ahi, blo, bhi;
                 if (from_m31) {
@@ -645,17 +663,18 @@ __global__ void __launch_bounds__(256) sumcheck_persistent_kernel(PersistArgs p)
                 } else {
                     const qm31 a0 = ld_q(A + i), a1 = ld_q(A + i + q), a2 = ld_q(A + i + h), a3 = ld_q(A + i + q + h);
                     const qm31 b0 = ld_q(B + i), b1 = ld_q(B + i + q), b2 = ld_q(B + i + h), b3 = ld_q(B + i + q + h);
-                    alo = qadd(a0, qmul(alpha, qsub(a2, a0)));
-                    ahi = qadd(a1, qmul(alpha, qsub(a3, a1)));
-                    blo = qadd(b0, qmul(alpha, qsub(b2, b0)));
-                    bhi = qadd(b1, qmul(alpha, qsub(b3, b1)));
+                    alo = fold_qq(a0, a2, m);
+                    ahi = fold_qq(a1, a3, m);
+                    blo = fold_qq(b0, b2, m);
+                    bhi = fold_qq(b1, b3, m);
                 }
                 st_q(A + i, alo);
                 st_q(A + i + q, ahi);
                 st_q(B + i, blo);
                 st_q(B + i + q, bhi);
-                round_terms(alo, ahi, blo, bhi, s);
+                racc_add(racc, alo, ahi, blo, bhi);
             }
+            racc_to_sums(racc, s);
             len = h;
         }
         // block partials

@@ -1,0 +1,220 @@
+"""One product sumcheck split across GPUs (one process per GPU).
+
+The degree-2 product sumcheck that ``ZkmlOps::reduce_matmul_layer`` runs
+(engine/src/backend.rs:141-178, round loop of components/matmul.rs
+``prove_matmul_sumcheck_onchain``) is sharded by the low index bits: rank g of
+G holds the elements whose global index i satisfies i = g (mod G), in order,
+so local element j is global element j*G + g.  A fold pairs global i with
+i + N/2; both are on the same rank at local j and j + N_loc/2, and the folded
+value keeps global index i, so the layout survives every fold.  Each round's
+(s0, s1, s2) is therefore the sum over ranks of the local sums: the only
+exchange per round is 12 u32 words (an all-reduce mod p).  Every rank runs the
+same host Poseidon channel on the same sums and draws the same challenge, so
+no challenge broadcast is needed.  Once the local length falls to the gather
+threshold, each rank exports its folded vectors, they are all-gathered and
+interleaved back to global order, and every rank finishes the (now small)
+sumcheck on its own GPU.  The proof is bit-identical to the single-GPU one.
+
+The collective is ``torch.distributed`` (NCCL between GPUs; gloo for the CPU
+tests of this orchestration).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import List, Optional
+
+import numpy as np
+
+from . import (M31_P as P, PoseidonChannel, RoundPoly, Context, _Buf, _check, context, lib)
+
+INV2 = (P + 1) // 2
+
+
+def shard_of(x: np.ndarray, rank: int, world: int) -> np.ndarray:
+    """Rank `rank`'s share of a length-N vector: elements rank, rank+G, rank+2G, ..."""
+    return np.ascontiguousarray(x[rank::world])
+
+
+def interpolate(words: np.ndarray):
+    """(s0, s1, s2) -> coefficients (c0, c1, c2) of s(X) = c0 + c1 X + c2 X^2.
+
+    s2 is the sum at X = 2: c2 = (s2 - 2 s1 + s0) / 2, c1 = s1 - s0 - c2
+    (components/matmul.rs, degree-2 round polynomial from three evaluations).
+    The map is linear with base-field coefficients, so it acts coordinate-wise.
+    """
+    w = np.asarray(words, np.int64).reshape(3, 4)
+    s0, s1, s2 = w[0], w[1], w[2]
+    c0 = s0 % P
+    c2 = ((s2 - 2 * s1 + s0) % P) * INV2 % P
+    c1 = (s1 - s0 - c2) % P
+    return c0.astype(np.uint32), c1.astype(np.uint32), c2.astype(np.uint32)
+
+
+class GpuSumcheckSession:
+    """The stepwise product sumcheck of one context (zkml_sumcheck_* in the C ABI)."""
+
+    def __init__(self, ctx: Optional[Context] = None, device: int = 0):
+        self.ctx = ctx or context(device)
+
+    def load_m31(self, a, b) -> None:
+        ab, bb = _Buf(a), _Buf(b)
+        n = ab.nbytes // 4
+        if bb.nbytes != ab.nbytes:
+            raise ValueError("vectors differ in length")
+        self._keep = (ab, bb)
+        _check(lib().zkml_sumcheck_load_m31(self.ctx.handle, ab.ptr, bb.ptr, n))
+
+    def load_qm31(self, a, b) -> None:
+        ab, bb = _Buf(a), _Buf(b)
+        n = ab.nbytes // 16
+        if bb.nbytes != ab.nbytes:
+            raise ValueError("vectors differ in length")
+        self._keep = (ab, bb)
+        _check(lib().zkml_sumcheck_load_qm31(self.ctx.handle, ab.ptr, bb.ptr, n))
+
+    def length(self) -> int:
+        return int(lib().zkml_sumcheck_length(self.ctx.handle))
+
+    def round(self, alpha=None) -> np.ndarray:
+        out = np.zeros(12, np.uint32)
+        if alpha is None:
+            _check(lib().zkml_sumcheck_round(self.ctx.handle, None, out))
+        else:
+            al = np.ascontiguousarray(alpha, np.uint32).reshape(4)
+            _check(lib().zkml_sumcheck_round(self.ctx.handle, al.ctypes.data_as(C.c_void_p), out))
+        return out
+
+    def export(self):
+        n = self.length()
+        a = np.zeros((n, 4), np.uint32)
+        b = np.zeros((n, 4), np.uint32)
+        _check(lib().zkml_sumcheck_export(self.ctx.handle, a.ctypes.data_as(C.c_void_p),
+                                          b.ctypes.data_as(C.c_void_p)))
+        return a, b
+
+    def finalize(self, alpha):
+        fa = np.zeros(4, np.uint32)
+        fb = np.zeros(4, np.uint32)
+        _check(lib().zkml_sumcheck_finalize(self.ctx.handle, np.ascontiguousarray(alpha, np.uint32).reshape(4),
+                                            fa, fb))
+        return fa, fb
+
+
+class LocalCollective:
+    """World size 1: the whole product on this process's GPU."""
+
+    world, rank = 1, 0
+
+    def sum_words(self, words):
+        return words
+
+    def gather_interleaved(self, local):
+        return local
+
+    def gather_interleaved_m31(self, local):
+        return local
+
+
+class TorchCollective:
+    """The two exchanges of the sharded sumcheck over a torch.distributed group."""
+
+    def __init__(self, group=None):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist, self.group = torch, dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if dist.get_backend(group) == "nccl":
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        else:
+            self.device = torch.device("cpu")
+
+    def sum_words(self, words: np.ndarray) -> np.ndarray:
+        t = self.torch.from_numpy(np.asarray(words, np.int64).copy()).to(self.device)
+        self.dist.all_reduce(t, group=self.group)
+        return (t.cpu().numpy() % P).astype(np.uint32)
+
+    def gather_interleaved(self, local: np.ndarray) -> np.ndarray:
+        """All-gather the (L, 4) local vectors and return the (L*G, 4) global one."""
+        t = self.torch.from_numpy(local.view(np.int32).copy()).to(self.device)
+        parts = [self.torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(parts, t, group=self.group)
+        stacked = np.stack([p.cpu().numpy().view(np.uint32) for p in parts])  # (G, L, 4)
+        return np.ascontiguousarray(stacked.transpose(1, 0, 2).reshape(-1, 4))
+
+    def gather_interleaved_m31(self, local: np.ndarray) -> np.ndarray:
+        t = self.torch.from_numpy(np.asarray(local, np.uint32).view(np.int32).copy()).to(self.device)
+        parts = [self.torch.empty_like(t) for _ in range(self.world)]
+        self.dist.all_gather(parts, t, group=self.group)
+        stacked = np.stack([p.cpu().numpy().view(np.uint32) for p in parts])  # (G, L)
+        return np.ascontiguousarray(stacked.T.reshape(-1))
+
+
+@dataclass
+class ShardedSumcheckProof:
+    round_polys: List[RoundPoly]
+    challenges: np.ndarray   # (log N, 4)
+    final_a: np.ndarray
+    final_b: np.ndarray
+    gathered_at: int         # global length at which the vectors were gathered (N if never sharded)
+
+
+DEFAULT_GATHER_LOCAL = 1 << 16
+
+
+def prove_product_sharded(a_local, b_local, n: int, channel: PoseidonChannel, session=None, collective=None,
+                          gather_local: int = DEFAULT_GATHER_LOCAL) -> ShardedSumcheckProof:
+    """Prove sum_i a_i b_i over a length-n M31 product split across the group.
+
+    a_local, b_local: this rank's shares (``shard_of``) of the two M31 vectors,
+    each of length n / G (host arrays or device tensors).  Every rank returns
+    the same proof, equal to the single-GPU ``reduce_matmul_layer`` on the 1 x n
+    and n x 1 matrices (no restriction point).  `gather_local` is the local
+    length at or below which the vectors are gathered onto every GPU.
+    """
+    session = session or GpuSumcheckSession()
+    col = collective or TorchCollective()
+    G = col.world
+    if n < 2 or n & (n - 1):
+        raise ValueError("n must be a power of two >= 2")
+    if G & (G - 1) or n % G:
+        raise ValueError("world size must be a power of two dividing n")
+    n_loc = n // G
+    log_n = n.bit_length() - 1
+    sharded = G > 1 and n_loc >= 4 and n_loc > gather_local
+    gathered_at = n
+    if sharded:
+        session.load_m31(a_local, b_local)
+    elif G > 1:
+        # too small to split: every rank proves the whole vector
+        a_host = np.asarray(a_local.cpu() if hasattr(a_local, "cpu") else a_local, np.uint32)
+        b_host = np.asarray(b_local.cpu() if hasattr(b_local, "cpu") else b_local, np.uint32)
+        session.load_m31(col.gather_interleaved_m31(a_host), col.gather_interleaved_m31(b_host))
+    else:
+        session.load_m31(a_local, b_local)
+    sums = session.round(None)
+    glen = n
+    polys: List[RoundPoly] = []
+    chals = np.zeros((log_n, 4), np.uint32)
+    final_a = final_b = None
+    for r in range(log_n):
+        if sharded:
+            sums = col.sum_words(sums)
+        c0, c1, c2 = interpolate(sums)
+        channel.mix_poly_coeffs(c0, c1, c2)
+        alpha = channel.draw_qm31()
+        polys.append(RoundPoly(c0, c1, c2))
+        chals[r] = alpha
+        if glen == 2:
+            final_a, final_b = session.finalize(alpha)
+            break
+        sums = session.round(alpha)
+        glen //= 2
+        if sharded and glen // G <= max(gather_local, 2):
+            la, lb = session.export()
+            session.load_qm31(col.gather_interleaved(la), col.gather_interleaved(lb))
+            sharded = False
+            gathered_at = glen
+            sums = session.round(None)
+    return ShardedSumcheckProof(polys, chals, final_a, final_b, gathered_at)

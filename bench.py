@@ -404,6 +404,14 @@ def run_case(name):
         pt, val = random_qm31(20, rng), random_qm31(1, rng)[0]
         for _ in range(2):
             Z.reduce_activation_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), 5, Z.PoseidonChannel())
+    elif name.startswith("la_"):  # native 1 x 2^L . 2^L x 1 reduction (look-ahead rounds), four times
+        lg = int(name.split("_")[1])
+        be = Z.GpuBackend(0)
+        a = torch.randint(0, 2**31 - 1, (1 << lg,), dtype=torch.int32).cuda()
+        b = torch.randint(0, 2**31 - 1, (1 << lg,), dtype=torch.int32).cuda()
+        for _ in range(4):
+            be.reduce_matmul_layer(Z.M31Matrix(1, 1 << lg, a), Z.M31Matrix(1 << lg, 1, b), [], [], 1 << lg,
+                                   Z.PoseidonChannel())
     elif name.startswith("product_"):  # the product sumcheck of 2^L M31 elements, twice
         from zkml_b200.distributed import GpuSumcheckSession, LocalCollective, prove_product_sharded
         lg = int(name.split("_")[1])

@@ -94,6 +94,7 @@ struct zkml_ctx {
     uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
     uint32_t* d_sig = nullptr;      // device alias of h_sig
     uint32_t sig_seq = 0;           // last sequence number handed to a kernel
+    size_t lookahead_max = size_t(1) << 16;  // look-ahead rounds for vectors up to this length (ZKML_LOOKAHEAD_MAX)
     bool persistent = false;        // run sumcheck rounds in one cooperative launch (ZKML_PERSISTENT_ROUNDS=1)
     int max_round_blocks = 0;
     // optional per-kernel-class event timing
@@ -119,6 +120,15 @@ struct zkml_ctx {
     unsigned int* grid_bar() const { return small.as<unsigned int>() + 52; }       // 2 words
     uint4* alpha_slot() const { return reinterpret_cast<uint4*>(small.as<uint32_t>() + 56); }
     uint32_t* persist_status() const { return small.as<uint32_t>() + 60; }
+    uint32_t* la_mailbox() const { return small.as<uint32_t>() + 4; }  // words 4-9
+    uint32_t* la_status() const { return small.as<uint32_t>() + 61; }  // look-ahead wait timed out
+    // challenge slots of the pre-queued look-ahead kernels: LA_SLOTS x 8 words
+    // (sequence tag, 4 challenge words, abort) from word 256 of the mapped page
+    static constexpr int LA_SLOTS = 32;
+    uint32_t* h_la_msg() const { return h_sig + 256; }
+    uint32_t* d_la_msg() const { return d_sig + 256; }
+    uint32_t la_msg_seq = 0;
+    bool la_tail = true;  // single-block tail for the last look-ahead rounds (ZKML_LOOKAHEAD_TAIL=0 turns it off)
     uint32_t* h_msg() const { return h_sig + 64; }  // host -> GPU words (own cache lines)
     uint32_t* d_msg() const { return d_sig + 64; }
     zk::RoundScratch round_scratch() const {

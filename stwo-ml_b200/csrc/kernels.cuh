@@ -63,6 +63,31 @@ void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const Ro
 // Fold M31 vectors into QM31 outputs (len -> len/2) and emit the next round's sums.
 void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm31 alpha, uint4* Ao,
                            uint4* Bo, const RoundScratch& rs, cudaStream_t s);
+// Look-ahead round over QM31 vectors: optionally fold V_{r-1} (length 2L) with
+// alpha into V_r (length L, in place), then publish 40 words (L >= 4: the sums
+// [Q0 Q1 Q2 Q3 T D0 D1 U W UW] from which the host forms round r's sums and round
+// r+1's sums as quadratics in the next challenge) or 28 words (L = 2:
+// [P0 P1 T A0 A1 B0 B1]).  partials must hold max_blocks * 16 words.
+// With wait_msg != null the kernel may be queued before the challenge exists:
+// thread 0 of every block polls the 8-word slot wait_msg (mapped host memory)
+// until word 0 equals wait_seq, then folds with words 1-4; a set word 5 (abort)
+// or a poll that runs past its limit skips the arithmetic (the latter also sets
+// *status), and the kernel still publishes so that the queue drains.  Only
+// block 0 polls host memory; it forwards the slot to the other blocks through
+// `mailbox` (6 words of device memory).
+void launch_round_lookahead(uint4* A, uint4* B, size_t L, bool fold, qm31 alpha, const RoundScratch& rs,
+                            cudaStream_t s, const uint32_t* wait_msg = nullptr, uint32_t wait_seq = 0,
+                            uint32_t* status = nullptr, uint32_t* mailbox = nullptr);
+// All remaining look-ahead rounds in one single-block launch (vectors in shared
+// memory).  The L0 input elements (L0 <= 2 * LA_TAIL_MAX) are folded first when
+// fold0 is set, with alpha0 or, if wait0, with the challenge posted to round
+// 0's slot.  Round j publishes sequence seq_base + j and (j > 0, or j = 0 with
+// wait0) waits for tag tag_base + j in the 8-word slot (tag_base + j) % slots
+// of msg.  Returns nonzero if the launch could not be configured.
+constexpr size_t LA_TAIL_MAX = 2048;
+int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0, bool wait0, qm31 alpha0,
+                          uint32_t* sig, uint32_t seq_base, const uint32_t* msg, uint32_t tag_base, int slots,
+                          uint32_t* status, cudaStream_t s);
 // Final fold of length-2 vectors to one value each: out[0..4) = a, out[4..8) = b.
 // src_m31 selects M31 inputs (A32, B32) instead of QM31 (A, B).
 void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,

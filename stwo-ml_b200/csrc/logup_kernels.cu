@@ -16,7 +16,7 @@ __device__ __forceinline__ void stq4(uint4* p, qm31 x) { *p = make_uint4(x.a, x.
 __device__ __forceinline__ void publish_words(uint32_t* sig, uint32_t seq, const uint32_t* words, int n) {
     volatile uint32_t* v = sig;
     for (int i = 0; i < n; i++) v[1 + i] = words[i];
-    __threadfence_system();
+    // the release store orders the word stores before the sequence number
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig), "r"(seq) : "memory");
 }
 

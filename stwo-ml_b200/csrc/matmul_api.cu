@@ -147,6 +147,11 @@ int device_view(zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const
 }
 
 int check_err_flag(zkml_ctx* ctx, const char* what) {
+    if (ctx->h_small[61]) {  // a queued look-ahead kernel gave up waiting for its challenge
+        ctx->h_small[61] = 0;
+        ZK_CUDA(cudaMemsetAsync(ctx->la_status(), 0, 4, ctx->stream));
+        return set_error(ZKML_ERR_TIMEOUT, std::string(what) + ": a round kernel timed out waiting for its challenge");
+    }
     if (ctx->h_small[48]) {
         ctx->h_small[48] = 0;
         ZK_CUDA(cudaMemsetAsync(ctx->err_flag(), 0, 4, ctx->stream));
@@ -197,7 +202,7 @@ int wait_signal(zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n) {
 
 // Reads the device error flag (one synchronisation).
 int read_err_flag(zkml_ctx* ctx) {
-    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 48, ctx->err_flag(), 4, cudaMemcpyDeviceToHost, ctx->stream));
+    ZK_CUDA(cudaMemcpyAsync(ctx->h_small + 48, ctx->err_flag(), 16 * 4, cudaMemcpyDeviceToHost, ctx->stream));
     ZK_CUDA(cudaStreamSynchronize(ctx->stream));
     if (!ctx->pending.empty()) drain_timers(ctx);
     return ZKML_OK;
@@ -292,6 +297,99 @@ static int run_sumcheck_persistent(zkml_ctx* ctx, uint4* A, uint4* B, const uint
 
 // The sumcheck round loop over (A, B).  In M31 mode A32/B32 hold the base-field
 // vectors (length len) and the first fold writes QM31 into ctx->fa / fb.
+// Host side of the look-ahead rounds (launch_round_lookahead).
+constexpr int LA_WORDS_HOST = 40;
+
+// Round r's own sums from its look-ahead words (len = |V_r|).
+static void la_round_sums(const uint32_t* w, size_t len, uint32_t s12[12]) {
+    if (len == 2) {
+        memcpy(s12, w, 48);
+        return;
+    }
+    stq(s12, qadd(ldq(w), ldq(w + 4)));
+    stq(s12 + 4, qadd(ldq(w + 8), ldq(w + 12)));
+    stq(s12 + 8, ldq(w + 16));
+}
+
+// Round r+1's sums from round r's look-ahead words, at the challenge x of round r.
+static void la_next_sums(const uint32_t* w, const qm31& x, uint32_t s12[12]) {
+    auto quad = [&](const qm31& c0, const qm31& both, const qm31& c2) {
+        const qm31 c1 = qsub(qsub(both, c0), c2);
+        return qadd(c0, qmul(x, qadd(c1, qmul(x, c2))));
+    };
+    stq(s12, quad(ldq(w), ldq(w + 8), ldq(w + 20)));
+    stq(s12 + 4, quad(ldq(w + 4), ldq(w + 12), ldq(w + 24)));
+    stq(s12 + 8, quad(ldq(w + 28), ldq(w + 36), ldq(w + 32)));
+}
+
+// The look-ahead kernels of one sumcheck, queued on the stream up front: kernel
+// 0 needs no challenge (or is given it), kernel j > 0 waits for the host to post
+// the challenge of the round before it into its slot.  Every queued kernel
+// either gets its challenge or an abort, so the queue always drains.
+struct LaQueue {
+    static constexpr int MAX = 40;
+    zkml_ctx* ctx;
+    int n = 0, posted = 1;
+    uint32_t seq[MAX], tag[MAX];
+    int slot[MAX];
+    size_t len[MAX];
+
+    explicit LaQueue(zkml_ctx* c) : ctx(c) {}
+
+    int enqueue(uint4* A, uint4* B, size_t L0, bool fold0, const qm31& alpha0, RoundScratch rs, cudaStream_t s) {
+        for (size_t L = L0; L >= 2 && n < MAX; L /= 2, n++) {
+            len[n] = L;
+            if (ctx->la_tail && L <= LA_TAIL_MAX) {
+                // the remaining rounds in one resident block
+                const int n0 = n;
+                for (size_t l = L; l >= 2; l /= 2, n++) {
+                    len[n] = l;
+                    seq[n] = ++ctx->sig_seq;
+                    if (n > 0) {
+                        tag[n] = ++ctx->la_msg_seq;
+                        slot[n] = (int)(tag[n] % zkml_ctx::LA_SLOTS);
+                    }
+                }
+                const bool wait0 = n0 > 0;
+                const bool f0 = wait0 || fold0;
+                const uint32_t tag_base = wait0 ? tag[n0] : (n > 1 ? tag[1] - 1 : 0);
+                if (launch_lookahead_tail(A, B, f0 ? 2 * L : L, f0, wait0, alpha0, rs.sig, seq[n0],
+                                          ctx->d_la_msg(), tag_base, zkml_ctx::LA_SLOTS, ctx->la_status(), s))
+                    return set_error(ZKML_ERR_CUDA, "cannot configure the look-ahead tail kernel");
+                ZK_CUDA(cudaGetLastError());
+                ctx->launches++;
+                return ZKML_OK;
+            }
+            rs.seq = seq[n] = ++ctx->sig_seq;
+            if (n == 0) {
+                KTimer t(ctx, KC_ROUND);
+                launch_round_lookahead(A, B, L, fold0, alpha0, rs, s);
+            } else {
+                tag[n] = ++ctx->la_msg_seq;
+                slot[n] = (int)(tag[n] % zkml_ctx::LA_SLOTS);
+                launch_round_lookahead(A, B, L, true, qzero(), rs, s, ctx->d_la_msg() + 8 * slot[n], tag[n],
+                                       ctx->la_status(), ctx->la_mailbox());
+            }
+            ZK_CUDA(cudaGetLastError());
+            ctx->launches++;
+        }
+        return ZKML_OK;
+    }
+    void post(int j, const qm31& a, bool abort) {
+        volatile uint32_t* m = ctx->h_la_msg() + 8 * slot[j];
+        m[1] = a.a;
+        m[2] = a.b;
+        m[3] = a.c;
+        m[4] = a.d;
+        m[5] = abort ? 1u : 0u;
+        std::atomic_thread_fence(std::memory_order_release);
+        m[0] = tag[j];
+    }
+    void abort_rest() {
+        for (; posted < n; posted++) post(posted, qzero(), true);
+    }
+};
+
 int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
                  zkml_channel* chs, uint32_t* out_rp, uint32_t* out_ch, uint32_t* fa_out, uint32_t* fb_out,
                  const ClaimHook* hook) {
@@ -325,25 +423,61 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
         if (rc != ZKML_ERR_UNSUPPORTED) return rc;
         ctx->persistent = false;  // cooperative launch unavailable: use one launch per round
     }
-    rs.seq = ++ctx->sig_seq;
-    {
-        KTimer t(ctx, KC_ROUND);
-        if (m31)
-            launch_round_m31(A32, B32, len, rs, ctx->err_flag(), s);
-        else
-            launch_round_qm31(A, B, len, rs, s);
+    // Vectors of at most lookahead_max elements run the look-ahead rounds
+    // (launch_round_lookahead): a round's kernel runs while the host hashes the
+    // previous round, and the host evaluates the next round's sums itself.
+    const size_t la_max = ctx->lookahead_max;
+    bool la = false;
+    if (m31 && len <= la_max) {  // small base-field product: lift to QM31 first
+        if ((rc = ctx->fa.ensure(len * 16)) || (rc = ctx->fb.ensure(len * 16))) return rc;
+        launch_m31_to_qm31(A32, len, ctx->fa.as<uint4>(), len, ctx->err_flag(), s);
+        launch_m31_to_qm31(B32, len, ctx->fb.as<uint4>(), len, ctx->err_flag(), s);
+        ctx->launches += 2;
+        A = ctx->fa.as<uint4>();
+        B = ctx->fb.as<uint4>();
+        m31 = false;
     }
-    ZK_CUDA(cudaGetLastError());
-    ctx->launches++;
+    LaQueue laq(ctx);
+    if (!m31 && len <= la_max) {
+        if ((rc = laq.enqueue(A, B, len, false, qzero(), rs, s))) return rc;
+        la = true;
+    } else {
+        rs.seq = ++ctx->sig_seq;
+        {
+            KTimer t(ctx, KC_ROUND);
+            if (m31)
+                launch_round_m31(A32, B32, len, rs, ctx->err_flag(), s);
+            else
+                launch_round_qm31(A, B, len, rs, s);
+        }
+        ZK_CUDA(cudaGetLastError());
+        ctx->launches++;
+    }
     if (hook && hook->overlap) hook->overlap(hook->arg);  // host transcript work while the GPU runs
-    uint32_t words[12];
+    uint32_t words[LA_WORDS_HOST];
+    uint32_t s12[12];
+    uint32_t la_w[LA_WORDS_HOST];  // the previous look-ahead words (this round's sums as a quadratic)
+    qm31 alpha_prev = qzero();
+    int j = 0;  // look-ahead kernel whose words belong to this round
     for (unsigned r = 0; r < log_k; r++) {
-        if ((rc = wait_signal(ctx, rs.seq, words, 12))) return rc;
-        if (r == 0 && hook && hook->fn) hook->fn(hook->arg, qadd(ldq(words), ldq(words + 4)));
+        if (la && j > 0) {
+            la_next_sums(la_w, alpha_prev, s12);  // this round's kernel may still be running
+        } else {
+            rc = wait_signal(ctx, la ? laq.seq[0] : rs.seq, words, la ? LA_WORDS_HOST : 12);
+            if (rc) {
+                laq.abort_rest();
+                return rc;
+            }
+            if (la)
+                la_round_sums(words, laq.len[0], s12);
+            else
+                memcpy(s12, words, sizeof(s12));
+        }
+        if (r == 0 && hook && hook->fn) hook->fn(hook->arg, qadd(ldq(s12), ldq(s12 + 4)));
         qm31 c0, c1, c2, alpha;
         {
             HostTimer ht(ctx, KC_HOST_CHANNEL);
-            interpolate(words, c0, c1, c2);
+            interpolate(s12, c0, c1, c2);
             ch.mix_poly_coeffs(c0, c1, c2);
             alpha = ch.draw_qm31();
         }
@@ -353,13 +487,51 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             stq(out_rp + 12 * r + 8, c2);
         }
         if (out_ch) stq(out_ch + 4 * r, alpha);
-        rs.seq = ++ctx->sig_seq;
-        {
-            KTimer t(ctx, KC_ROUND);
-            if (len == 2) {
+        if (la) {
+            if (j > 0) {  // this round's words: check them against the quadratic (read before the next post)
+                if ((rc = wait_signal(ctx, laq.seq[j], words, LA_WORDS_HOST))) {
+                    laq.abort_rest();
+                    return rc;
+                }
+                uint32_t plain[12];
+                la_round_sums(words, laq.len[j], plain);
+                if (memcmp(plain, s12, sizeof(plain)) != 0) {
+                    laq.abort_rest();
+                    // invalid input words or a timed-out wait surface as a disagreement: report them first
+                    if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "reduce_matmul_layer"))) return rc;
+                    return set_error(ZKML_ERR_CUDA, "look-ahead round sums disagree with the round kernel");
+                }
+            }
+            if (laq.len[j] == 2) {  // final values from the last round's words
+                const qm31 a0 = ldq(words + 12), a1 = ldq(words + 16), b0 = ldq(words + 20), b1 = ldq(words + 24);
+                stq(fa_out, qadd(a0, qmul(alpha, qsub(a1, a0))));
+                stq(fb_out, qadd(b0, qmul(alpha, qsub(b1, b0))));
+                if ((rc = read_err_flag(ctx))) return rc;
+                return check_err_flag(ctx, "reduce_matmul_layer");
+            }
+            memcpy(la_w, words, sizeof(la_w));
+            alpha_prev = alpha;
+            laq.post(++j, alpha, false);  // releases the queued kernel of the next round
+            laq.posted = j + 1;
+            continue;
+        }
+        if (len == 2) {
+            rs.seq = ++ctx->sig_seq;
+            {
+                KTimer t(ctx, KC_ROUND);
                 launch_final_fold(A, B, m31 ? A32 : nullptr, m31 ? B32 : nullptr, len, alpha, ctx->out_words(),
                                   rs.sig, rs.seq, s);
-            } else if (m31) {
+            }
+        } else if (!m31 && len / 2 <= la_max) {
+            if ((rc = laq.enqueue(A, B, len / 2, true, alpha, rs, s))) return rc;
+            la = true;
+            j = 0;
+            len /= 2;
+            continue;
+        } else {
+            rs.seq = ++ctx->sig_seq;
+            KTimer t(ctx, KC_ROUND);
+            if (m31) {
                 A = ctx->fa.as<uint4>();
                 B = ctx->fb.as<uint4>();
                 launch_fold_round_m31(A32, B32, len, alpha, A, B, rs, s);
@@ -455,6 +627,10 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     {
         const char* pv = getenv("ZKML_PERSISTENT_ROUNDS");
         if (pv) ctx->persistent = pv[0] == '1';
+        const char* lv = getenv("ZKML_LOOKAHEAD_MAX");
+        if (lv) ctx->lookahead_max = strtoull(lv, nullptr, 10);
+        const char* tv = getenv("ZKML_LOOKAHEAD_TAIL");
+        if (tv) ctx->la_tail = tv[0] != '0';
     }
     ctx->max_round_blocks = ctx->num_sms * 8;
     int rc = ZKML_OK;

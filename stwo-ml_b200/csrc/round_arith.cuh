@@ -97,7 +97,7 @@ struct AlphaRows {
     uint32_t r[4][4];
 };
 
-__device__ __forceinline__ AlphaRows alpha_rows(const qm31& x) {
+ZK_HD AlphaRows alpha_rows(const qm31& x) {
     const uint32_t s = msub(madd(x.c, x.c), x.d);  // 2c - d
     const uint32_t t = madd(x.c, madd(x.d, x.d));  // c + 2d
     AlphaRows m;

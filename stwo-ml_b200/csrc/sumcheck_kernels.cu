@@ -349,7 +349,7 @@ __device__ __forceinline__ void sums_add(Sums& s, const qm31& x0, const qm31& x1
 __device__ __forceinline__ void publish(uint32_t* sig, uint32_t seq, const uint32_t* words, int n) {
     volatile uint32_t* v = sig;
     for (int i = 0; i < n; i++) v[1 + i] = words[i];
-    __threadfence_system();
+    // the release store orders the word stores before the sequence number
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig), "r"(seq) : "memory");
 }
 
@@ -427,24 +427,51 @@ __global__ void __launch_bounds__(256) round_qm31_kernel(const uint4* __restrict
 // In-place fold with alpha fused with the next round's sums.  Thread i reads
 // elements i, i+q, i+h, i+q+h (h = len/2, q = h/2) and writes i and i+q: every
 // element is read by exactly one thread, so the in-place update is race-free.
-// Inputs must be canonical (< P); outputs are canonical.
-__global__ void __launch_bounds__(256) fold_round_qm31_kernel(uint4* __restrict__ A, uint4* __restrict__ B, size_t h,
-                                                              qm31 alpha, uint32_t* partials, unsigned int* ticket,
-                                                              uint32_t* out, uint32_t* sig, uint32_t seq) {
-    const size_t q = h / 2;
-    const AlphaRows m = alpha_rows(alpha);
+// Inputs must be canonical (< P); outputs are canonical.  The next iteration's
+// eight loads are issued before this iteration's arithmetic, so each warp keeps
+// two iterations of HBM reads in flight; the challenge's 4 x 4 coefficient
+// matrix is a kernel parameter (constant bank, no registers).
+struct FoldLoads {
+    uint4 a0, a1, a2, a3, b0, b1, b2, b3;
+};
+
+__device__ __forceinline__ void fold_loads(FoldLoads& v, const uint4* A, const uint4* B, size_t i, size_t q,
+                                           size_t h) {
+    v.a0 = A[i];
+    v.a1 = A[i + q];
+    v.a2 = A[i + h];
+    v.a3 = A[i + q + h];
+    v.b0 = B[i];
+    v.b1 = B[i + q];
+    v.b2 = B[i + h];
+    v.b3 = B[i + q + h];
+}
+
+__device__ __forceinline__ qm31 u2q(const uint4& v) { return qm(v.x, v.y, v.z, v.w); }
+
+__global__ void __launch_bounds__(256, 2) fold_round_qm31_kernel(uint4* __restrict__ A, uint4* __restrict__ B,
+                                                                 size_t h, const AlphaRows m, uint32_t* partials,
+                                                                 unsigned int* ticket, uint32_t* out, uint32_t* sig,
+                                                                 uint32_t seq) {
+    const size_t q = h / 2, stride = (size_t)gridDim.x * blockDim.x;
     RoundAcc acc;
     racc_zero(acc);
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        const qm31 a0 = ld_q(A + i), a1 = ld_q(A + i + q), a2 = ld_q(A + i + h), a3 = ld_q(A + i + q + h);
-        const qm31 b0 = ld_q(B + i), b1 = ld_q(B + i + q), b2 = ld_q(B + i + h), b3 = ld_q(B + i + q + h);
-        const qm31 alo = fold_qq(a0, a2, m), ahi = fold_qq(a1, a3, m);
-        const qm31 blo = fold_qq(b0, b2, m), bhi = fold_qq(b1, b3, m);
+    size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    FoldLoads cur;
+    if (i < q) fold_loads(cur, A, B, i, q, h);
+    while (i < q) {
+        const size_t nx = i + stride;
+        FoldLoads nxt;
+        if (nx < q) fold_loads(nxt, A, B, nx, q, h);
+        const qm31 alo = fold_qq(u2q(cur.a0), u2q(cur.a2), m), ahi = fold_qq(u2q(cur.a1), u2q(cur.a3), m);
+        const qm31 blo = fold_qq(u2q(cur.b0), u2q(cur.b2), m), bhi = fold_qq(u2q(cur.b1), u2q(cur.b3), m);
         st_q(A + i, alo);
         st_q(A + i + q, ahi);
         st_q(B + i, blo);
         st_q(B + i + q, bhi);
         racc_add(acc, alo, ahi, blo, bhi);
+        cur = nxt;
+        i = nx;
     }
     Sums s;
     racc_to_sums(acc, s);
@@ -453,17 +480,36 @@ __global__ void __launch_bounds__(256) fold_round_qm31_kernel(uint4* __restrict_
 
 // Base-field round: products of M31 values accumulate lazily (acc_fold).  Any
 // input word with bit 31 set is not an M31 element and raises the error flag.
+// VEC = 4 reads four consecutive indices per 16-byte load (q % 4 == 0, 16-byte
+// aligned inputs); VEC = 1 is the general path.
+template <int VEC>
 __global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restrict__ A, const uint32_t* __restrict__ B,
                                                         size_t q, uint32_t* partials, unsigned int* ticket,
                                                         uint32_t* out, uint32_t* err, uint32_t* sig, uint32_t seq) {
     uint64_t s0 = 0, s1 = 0, s2 = 0;
     uint32_t bad = 0;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        const uint32_t alo = __ldcs(A + i), ahi = __ldcs(A + i + q), blo = __ldcs(B + i), bhi = __ldcs(B + i + q);
-        bad |= alo | ahi | blo | bhi;
-        s0 = acc_fold(s0, mul_wide(alo, blo));
-        s1 = acc_fold(s1, mul_wide(ahi, bhi));
-        s2 = acc_fold(s2, mul_wide(csub(cdbl(ahi), alo), csub(cdbl(bhi), blo)));
+    const size_t nq = q / VEC;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nq; i += (size_t)gridDim.x * blockDim.x) {
+        uint32_t alo[VEC], ahi[VEC], blo[VEC], bhi[VEC];
+        if constexpr (VEC == 4) {
+            const uint4 x0 = __ldcs(reinterpret_cast<const uint4*>(A) + i);
+            const uint4 x1 = __ldcs(reinterpret_cast<const uint4*>(A) + i + nq);
+            const uint4 y0 = __ldcs(reinterpret_cast<const uint4*>(B) + i);
+            const uint4 y1 = __ldcs(reinterpret_cast<const uint4*>(B) + i + nq);
+            alo[0] = x0.x; alo[1] = x0.y; alo[2] = x0.z; alo[3] = x0.w;
+            ahi[0] = x1.x; ahi[1] = x1.y; ahi[2] = x1.z; ahi[3] = x1.w;
+            blo[0] = y0.x; blo[1] = y0.y; blo[2] = y0.z; blo[3] = y0.w;
+            bhi[0] = y1.x; bhi[1] = y1.y; bhi[2] = y1.z; bhi[3] = y1.w;
+        } else {
+            alo[0] = __ldcs(A + i); ahi[0] = __ldcs(A + i + q); blo[0] = __ldcs(B + i); bhi[0] = __ldcs(B + i + q);
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; e++) {
+            bad |= alo[e] | ahi[e] | blo[e] | bhi[e];
+            s0 = acc_fold(s0, mul_wide(alo[e], blo[e]));
+            s1 = acc_fold(s1, mul_wide(ahi[e], bhi[e]));
+            s2 = acc_fold(s2, mul_wide(csub(cdbl(ahi[e]), alo[e]), csub(cdbl(bhi[e]), blo[e])));
+        }
     }
     if (bad & 0x80000000u) atomicOr(err, 1u);
     Sums s;
@@ -479,27 +525,462 @@ __device__ __forceinline__ qm31 fold_m31(uint32_t lo, uint32_t hi, const qm31& a
     return fold_mq(red32(lo), red32(hi), alpha);
 }
 
+
+// First fold (M31 -> QM31) fused with the next round's sums.  A block works on
+// tiles of FR_UNROLL x 256 consecutive indices: its thread t takes indices
+// tile + t + 256 e (e < FR_UNROLL), so every load (4 bytes a thread) and every
+// 16-byte store of a warp is one contiguous run, and all FR_UNROLL x 8 loads of
+// a tile are issued before its arithmetic.
+constexpr int FR_UNROLL = 4;
+
 __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __restrict__ A,
                                                              const uint32_t* __restrict__ B, size_t h, qm31 alpha,
                                                              uint4* __restrict__ Ao, uint4* __restrict__ Bo,
                                                              uint32_t* partials, unsigned int* ticket, uint32_t* out,
                                                              uint32_t* sig, uint32_t seq) {
     const size_t q = h / 2;
+    const size_t tile = (size_t)FR_UNROLL * blockDim.x;
     RoundAcc acc;
     racc_zero(acc);
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        const qm31 alo = fold_mq(A[i], A[i + h], alpha), ahi = fold_mq(A[i + q], A[i + q + h], alpha);
-        const qm31 blo = fold_mq(B[i], B[i + h], alpha), bhi = fold_mq(B[i + q], B[i + q + h], alpha);
-        st_q(Ao + i, alo);
-        st_q(Ao + i + q, ahi);
-        st_q(Bo + i, blo);
-        st_q(Bo + i + q, bhi);
-        racc_add(acc, alo, ahi, blo, bhi);
+    for (size_t base = blockIdx.x * tile; base < q; base += (size_t)gridDim.x * tile) {
+        uint32_t a0[FR_UNROLL], a1[FR_UNROLL], a2[FR_UNROLL], a3[FR_UNROLL];
+        uint32_t b0[FR_UNROLL], b1[FR_UNROLL], b2[FR_UNROLL], b3[FR_UNROLL];
+#pragma unroll
+        for (int e = 0; e < FR_UNROLL; e++) {
+            const size_t j = base + threadIdx.x + (size_t)e * blockDim.x;
+            if (j < q) {
+                a0[e] = __ldcs(A + j); a1[e] = __ldcs(A + j + q); a2[e] = __ldcs(A + j + h); a3[e] = __ldcs(A + j + q + h);
+                b0[e] = __ldcs(B + j); b1[e] = __ldcs(B + j + q); b2[e] = __ldcs(B + j + h); b3[e] = __ldcs(B + j + q + h);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < FR_UNROLL; e++) {
+            const size_t j = base + threadIdx.x + (size_t)e * blockDim.x;
+            if (j < q) {
+                const qm31 alo = fold_mq(a0[e], a2[e], alpha), ahi = fold_mq(a1[e], a3[e], alpha);
+                const qm31 blo = fold_mq(b0[e], b2[e], alpha), bhi = fold_mq(b1[e], b3[e], alpha);
+                st_q(Ao + j, alo);
+                st_q(Ao + j + q, ahi);
+                st_q(Bo + j, blo);
+                st_q(Bo + j + q, bhi);
+                racc_add(acc, alo, ahi, blo, bhi);
+            }
+        }
     }
     Sums s;
     racc_to_sums(acc, s);
     finish_sums(s, partials, ticket, out, sig, seq);
 }
+
+// ---------------------------------------------------------------------------
+// Look-ahead round (small vectors).  One launch folds V_{r-1} with the previous
+// challenge into V_r (in place; skipped for the first round) and returns, besides
+// round r's own sums, the round r+1 sums as quadratics in the challenge not yet
+// drawn, so the host can evaluate them the moment it draws that challenge and
+// the GPU work of a round runs while the host hashes the previous one.
+//
+// With L = |V_r|, h = L/2, q = L/4, d[j] = V[j+h] - V[j] and P[j] = A[j] B[j]:
+//   round r:    s0 = sum_{j<h} P,  s1 = sum_{j>=h} P,  s2 = sum_{j<h} T[j]
+//               (T[j] = (2A[j+h] - A[j])(2B[j+h] - B[j]));
+//   round r+1:  s0(x) = Q0 + x (Q2 - Q0 - D0) + x^2 D0,
+//               s1(x) = Q1 + x (Q3 - Q1 - D1) + x^2 D1,
+//               s2(x) = U + x (UW - U - W) + x^2 W,
+// where Qk = sum of P over the k-th quarter of V_r, D0/D1 = sum d_A d_B over the
+// first/second quarter, and with u = 2V[j+q] - V[j], w = 2d[j+q] - d[j] (j < q):
+// U = sum u_A u_B, W = sum w_A w_B, UW = sum (u_A + w_A)(u_B + w_B) (note
+// u + w = 2V[j+q+h] - V[j+h]).  The kernel publishes the ten sums
+// [Q0 Q1 Q2 Q3 T D0 D1 U W UW] (40 words).  For L = 2 (the last round) it
+// publishes [P0 P1 T A0 A1 B0 B1] (28 words): the final values are then
+// A0 + x (A1 - A0) and B0 + x (B1 - B0).
+// ---------------------------------------------------------------------------
+// The look-ahead kernel runs on small vectors, one launch per round, so its
+// time is dominated by fetching its own instructions into a cold instruction
+// cache, not by arithmetic.  It is therefore written for small code: the fold
+// and the product are out-of-line device functions called in loops, and the
+// 40 result words are reduced through shared memory by a rolled loop.
+constexpr int LA_WORDS = 40;
+constexpr int LA_THREADS = 256;
+constexpr unsigned long long kLaSpinLimit = 1ull << 23;  // ~2 s with the back-off below
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __noinline__ qm31 la_fold(const uint4* V, size_t p, size_t L, int fold, const AlphaRows* m) {
+    const qm31 lo = u2q(V[p]);
+    return fold ? fold_qq(lo, u2q(V[p + L]), *m) : lo;
+}
+
+__device__ __noinline__ qm31 la_mul(qm31 x, qm31 y) {
+    QAcc s;
+    qacc_zero(s);
+    qacc_mul(s, x, y);
+    return qacc_value(s);
+}
+
+// Lanes [16 g, 16 g + 16) of a warp work on one quad together: lanes 0-7 of the
+// half fold one element each (A at the four positions, then B), the eight
+// folded values are broadcast within the half by shuffles, and lane k < 11
+// forms the k-th product (k = 10 is the second half of T).  So a quad costs
+// one fold and one product of latency instead of eight and eleven.
+__device__ __forceinline__ qm31 shfl_q(const qm31& v, int src) {
+    return qm(__shfl_sync(0xffffffffu, v.a, src), __shfl_sync(0xffffffffu, v.b, src),
+              __shfl_sync(0xffffffffu, v.c, src), __shfl_sync(0xffffffffu, v.d, src));
+}
+
+__global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __restrict__ A, uint4* __restrict__ B,
+                                                                     size_t L, int fold, const AlphaRows m,
+                                                                     uint32_t* partials, unsigned int* ticket,
+                                                                     uint32_t* sig, uint32_t seq,
+                                                                     const uint32_t* wait_msg, uint32_t wait_seq,
+                                                                     uint32_t* status, uint32_t* mailbox) {
+    constexpr int COLS = 2 * LA_THREADS / 32;  // two half-warps per warp
+    __shared__ uint32_t sh[11][4][COLS];
+    __shared__ AlphaRows ms;
+    __shared__ int skip;
+    if (threadIdx.x == 0) {
+        skip = 0;
+        if (wait_msg) {
+            // Block 0 polls the host slot and forwards the challenge through a
+            // device mailbox [tag, 4 challenge words, abort] that the other
+            // blocks poll, so only one thread reads host memory.
+            volatile uint32_t* box = mailbox;
+            uint32_t w[5] = {0, 0, 0, 0, 1};
+            bool ok = false;
+            unsigned long long it = 0;
+            if (blockIdx.x == 0) {
+                while (true) {
+                    if (ld_acquire_sys_u32(wait_msg) == wait_seq) {
+                        ok = true;
+                        break;
+                    }
+                    if (++it > kLaSpinLimit) break;
+                    __nanosleep(it < 4096 ? 32 : 256);
+                }
+                if (ok) {
+                    volatile const uint32_t* hm = wait_msg;
+                    for (int k = 0; k < 5; k++) w[k] = hm[1 + k];
+                }
+                for (int k = 0; k < 5; k++) box[1 + k] = w[k];
+                __threadfence();
+                asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(mailbox), "r"(wait_seq) : "memory");
+            } else {
+                while (true) {
+                    uint32_t tag;
+                    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(mailbox) : "memory");
+                    if (tag == wait_seq) {
+                        ok = true;
+                        break;
+                    }
+                    if (++it > kLaSpinLimit) break;
+                    __nanosleep(it < 4096 ? 32 : 256);
+                }
+                if (ok)
+                    for (int k = 0; k < 5; k++) w[k] = box[1 + k];
+            }
+            if (!ok) {
+                skip = 1;
+                if (status) atomicOr(status, 1u);
+            } else if (w[4] != 0) {
+                skip = 1;
+            } else {
+                ms = alpha_rows(qm(w[0], w[1], w[2], w[3]));
+            }
+        } else {
+            ms = m;
+        }
+    }
+    __syncthreads();
+    if (skip) L = 0;  // no work: publish zeros so the queue drains
+    const unsigned lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4, warp = threadIdx.x >> 5;
+    const int col = 2 * warp + half;
+    qm31 acc = qzero();
+    if (L == 2) {  // last round: lanes 0-3 of warp 0 fold, lanes 0-2 multiply
+        if (blockIdx.x == 0 && warp == 0) {
+            qm31 x = qzero();
+            if (lane < 4) {
+                const uint4* V = lane < 2 ? A : B;
+                x = la_fold(V, lane & 1, 2, fold, &ms);
+                if (fold) st_q((lane < 2 ? A : B) + (lane & 1), x);
+            }
+            const qm31 a0 = shfl_q(x, 0), a1 = shfl_q(x, 1), b0 = shfl_q(x, 2), b1 = shfl_q(x, 3);
+            qm31 px = a0, py = b0;
+            if (lane == 1) { px = a1; py = b1; }
+            if (lane == 2) { px = at_two(a0, a1); py = at_two(b0, b1); }
+            const qm31 pr = la_mul(px, py);
+            if (half == 0 && sub < 3) acc = pr;
+            if (half == 0 && sub >= 3 && sub < 7) acc = sub == 3 ? a0 : sub == 4 ? a1 : sub == 5 ? b0 : b1;
+        }
+    } else {
+        const size_t h = L / 2, q = L / 4;
+        const size_t warps = (size_t)gridDim.x * (LA_THREADS / 32);
+#pragma unroll 1
+        for (size_t base = 2 * (blockIdx.x * (size_t)(LA_THREADS / 32) + warp); base < q; base += 2 * warps) {
+            const size_t i = base + half;
+            const bool valid = i < q;
+            qm31 x = qzero();
+            if (valid && sub < 8) {
+                const size_t e = sub & 3;
+                const size_t pos = i + (e & 1 ? q : 0) + (e & 2 ? h : 0);
+                uint4* V = sub < 4 ? A : B;
+                x = la_fold(V, pos, L, fold, &ms);
+                if (fold) st_q(V + pos, x);
+            }
+            const int s0 = 16 * half;
+            const qm31 a0 = shfl_q(x, s0), a1 = shfl_q(x, s0 + 1), a2 = shfl_q(x, s0 + 2), a3 = shfl_q(x, s0 + 3);
+            const qm31 b0 = shfl_q(x, s0 + 4), b1 = shfl_q(x, s0 + 5), b2 = shfl_q(x, s0 + 6), b3 = shfl_q(x, s0 + 7);
+            // factor pair of product `sub` among [Q0 Q1 Q2 Q3 T D0 D1 U W UW T']
+            qm31 px, py;
+            switch (sub) {
+                case 0: px = a0; py = b0; break;
+                case 1: px = a1; py = b1; break;
+                case 2: px = a2; py = b2; break;
+                case 3: px = a3; py = b3; break;
+                case 4: px = at_two(a0, a2); py = at_two(b0, b2); break;
+                case 5: px = qsub(a2, a0); py = qsub(b2, b0); break;
+                case 6: px = qsub(a3, a1); py = qsub(b3, b1); break;
+                case 7: px = at_two(a0, a1); py = at_two(b0, b1); break;
+                case 8: px = at_two(qsub(a2, a0), qsub(a3, a1)); py = at_two(qsub(b2, b0), qsub(b3, b1)); break;
+                case 9: px = at_two(a2, a3); py = at_two(b2, b3); break;
+                case 10: px = at_two(a1, a3); py = at_two(b1, b3); break;
+                default: px = qzero(); py = qzero(); break;
+            }
+            const qm31 pr = la_mul(px, py);
+            if (valid && sub < 11) acc = qadd(acc, pr);
+        }
+    }
+    // block reduction: lane `sub` of each half-warp holds word group `sub`
+    if (sub < 11) {
+        sh[sub][0][col] = acc.a;
+        sh[sub][1][col] = acc.b;
+        sh[sub][2][col] = acc.c;
+        sh[sub][3][col] = acc.d;
+    }
+    __syncthreads();
+    if (threadIdx.x < LA_WORDS) {
+        const int g = threadIdx.x >> 2, c = threadIdx.x & 3;
+        uint32_t v = 0;
+#pragma unroll 1
+        for (int k = 0; k < COLS; k++) {
+            v = madd(v, sh[g][c][k]);
+            if (g == 4 && L > 2) v = madd(v, sh[10][c][k]);
+        }
+        partials[blockIdx.x * LA_WORDS + threadIdx.x] = v;
+    }
+    __shared__ bool is_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // Last block: warp k sums words k, k+8, ...; its lanes stride over the
+    // blocks' partials so the loads of a word are issued in parallel.
+    __shared__ uint32_t res[LA_WORDS];
+    const int nwarps = LA_THREADS / 32;
+#pragma unroll 1
+    for (int k = warp; k < LA_WORDS; k += nwarps) {
+        unsigned long long sacc = 0;
+        for (unsigned b = lane; b < gridDim.x; b += 32) sacc += __ldcg(partials + b * LA_WORDS + k);
+        uint32_t v = red64(sacc);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) res[k] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        *ticket = 0;
+        if (sig) publish(sig, seq, res, LA_WORDS);
+    }
+}
+
+void launch_round_lookahead(uint4* A, uint4* B, size_t L, bool fold, qm31 alpha, const RoundScratch& rs,
+                            cudaStream_t s, const uint32_t* wait_msg, uint32_t wait_seq, uint32_t* status,
+                            uint32_t* mailbox) {
+    size_t blocks = L >= 4 ? (L / 4 + 15) / 16 : 1;  // 16 quads per block per pass
+    const size_t cap = (size_t)rs.max_blocks * 16 / LA_WORDS;
+    if (blocks > cap) blocks = cap;
+    if (blocks == 0) blocks = 1;
+    // the 40 result words go to the host signal area only (rs.out holds 32 words)
+    static_assert(LA_WORDS <= 48, "signal area");
+    round_lookahead_kernel<<<(unsigned)blocks, LA_THREADS, 0, s>>>(A, B, L, fold ? 1 : 0, alpha_rows(alpha),
+                                                                   rs.partials, rs.ticket, rs.sig, rs.seq, wait_msg,
+                                                                   wait_seq, status, mailbox);
+}
+
+// ---------------------------------------------------------------------------
+// Look-ahead tail: every remaining round of a sumcheck whose vectors have at
+// most LA_TAIL_MAX elements, in ONE block with both vectors resident in shared
+// memory.  The L0 input elements are folded first when fold0 is set (round 0
+// then has L0 / 2 elements).  Round j waits for its challenge in host slot
+// (tag_base + j) % slots (round 0 only when wait0 is set; otherwise it folds
+// with alpha0), folds in shared memory and publishes the same words as
+// round_lookahead_kernel with sequence seq_base + j.  Thread t < 11 * TAIL_COLS
+// forms product k = t / TAIL_COLS of the quads t % TAIL_COLS, t % TAIL_COLS +
+// TAIL_COLS, ..., so a thread's product kind is fixed for the whole kernel.
+// ---------------------------------------------------------------------------
+constexpr int TAIL_THREADS = 1024;
+constexpr int TAIL_COLS = 93;  // 11 * 93 = 1023 product threads
+
+__device__ __forceinline__ void la_factors(int k, const qm31* a, const qm31* b, qm31& px, qm31& py) {
+    switch (k) {
+        case 0: px = a[0]; py = b[0]; break;
+        case 1: px = a[1]; py = b[1]; break;
+        case 2: px = a[2]; py = b[2]; break;
+        case 3: px = a[3]; py = b[3]; break;
+        case 4: px = at_two(a[0], a[2]); py = at_two(b[0], b[2]); break;
+        case 5: px = qsub(a[2], a[0]); py = qsub(b[2], b[0]); break;
+        case 6: px = qsub(a[3], a[1]); py = qsub(b[3], b[1]); break;
+        case 7: px = at_two(a[0], a[1]); py = at_two(b[0], b[1]); break;
+        case 8: px = at_two(qsub(a[2], a[0]), qsub(a[3], a[1])); py = at_two(qsub(b[2], b[0]), qsub(b[3], b[1])); break;
+        case 9: px = at_two(a[2], a[3]); py = at_two(b[2], b[3]); break;
+        default: px = at_two(a[1], a[3]); py = at_two(b[1], b[3]); break;  // 10: second half of T
+    }
+}
+
+__global__ void __launch_bounds__(TAIL_THREADS, 1) lookahead_tail_kernel(const uint4* __restrict__ A,
+                                                                         const uint4* __restrict__ B, int L0,
+                                                                         int fold0, int wait0, qm31 alpha0,
+                                                                         uint32_t* sig,
+                                                                         uint32_t seq_base, const uint32_t* msg,
+                                                                         uint32_t tag_base, int slots,
+                                                                         uint32_t* status) {
+    extern __shared__ uint4 tail_sh[];
+    uint4* SA = tail_sh;
+    uint4* SB = tail_sh + L0;
+    __shared__ uint32_t red[11][4][32];
+    __shared__ uint32_t res[LA_WORDS];
+    __shared__ AlphaRows ms;
+    __shared__ int state;  // 0 run, 1 stop
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int k = t / TAIL_COLS, c = t % TAIL_COLS;
+    for (int i = t; i < L0; i += TAIL_THREADS) {
+        SA[i] = A[i];
+        SB[i] = B[i];
+    }
+    int L = L0;
+    for (int j = 0;; j++) {
+        // challenge of the previous round
+        bool fold = j > 0 || fold0;
+        if (t == 0) {
+            state = 0;
+            if (j == 0 && !wait0) {
+                if (fold0) ms = alpha_rows(alpha0);
+            } else {
+                const uint32_t* slot = msg + 8 * ((tag_base + j) % slots);
+                const uint32_t want = tag_base + j;
+                unsigned long long it = 0;
+                bool ok = false;
+                while (true) {
+                    if (ld_acquire_sys_u32(slot) == want) {
+                        ok = true;
+                        break;
+                    }
+                    if (++it > kLaSpinLimit) break;
+                    __nanosleep(it < 4096 ? 32 : 256);
+                }
+                volatile const uint32_t* w = slot;
+                if (!ok) {
+                    atomicOr(status, 1u);
+                    state = 1;
+                } else if (w[5] != 0) {
+                    state = 1;
+                } else {
+                    ms = alpha_rows(qm(w[1], w[2], w[3], w[4]));
+                }
+            }
+        }
+        __syncthreads();
+        if (state) return;
+        if (fold) {  // V_j = fold(V_{j-1}) in place: thread writes p < L, reads p and p + L
+            L /= 2;
+            for (int p = t; p < 2 * L; p += TAIL_THREADS) {
+                const int e = p < L ? p : p - L;
+                uint4* V = p < L ? SA : SB;
+                const qm31 x = fold_qq(u2q(V[e]), u2q(V[e + L]), ms);
+                st_q(V + e, x);
+            }
+            __syncthreads();
+        }
+        qm31 acc = qzero();
+        if (L == 2) {
+            if (t < 7) {
+                const qm31 a0 = u2q(SA[0]), a1 = u2q(SA[1]), b0 = u2q(SB[0]), b1 = u2q(SB[1]);
+                if (t == 0) acc = la_mul(a0, b0);
+                if (t == 1) acc = la_mul(a1, b1);
+                if (t == 2) acc = la_mul(at_two(a0, a1), at_two(b0, b1));
+                if (t == 3) acc = a0;
+                if (t == 4) acc = a1;
+                if (t == 5) acc = b0;
+                if (t == 6) acc = b1;
+                res[4 * t] = acc.a; res[4 * t + 1] = acc.b; res[4 * t + 2] = acc.c; res[4 * t + 3] = acc.d;
+            } else if (t < 10) {
+                res[4 * t] = res[4 * t + 1] = res[4 * t + 2] = res[4 * t + 3] = 0;
+            }
+            __syncthreads();
+            if (t == 0) publish(sig, seq_base + j, res, LA_WORDS);
+            return;
+        }
+        const int h = L / 2, q = L / 4;
+        if (k < 11) {
+            for (int i = c; i < q; i += TAIL_COLS) {
+                qm31 a[4], b[4];
+                a[0] = u2q(SA[i]); a[1] = u2q(SA[i + q]); a[2] = u2q(SA[i + h]); a[3] = u2q(SA[i + q + h]);
+                b[0] = u2q(SB[i]); b[1] = u2q(SB[i + q]); b[2] = u2q(SB[i + h]); b[3] = u2q(SB[i + q + h]);
+                qm31 px, py;
+                la_factors(k, a, b, px, py);
+                acc = qadd(acc, la_mul(px, py));
+            }
+        }
+        // per product kind: warp w < 11 sums the TAIL_COLS partials of kind w
+        __shared__ qm31 part[TAIL_THREADS];
+        part[t] = acc;
+        __syncthreads();
+        if (warp < 11) {
+            qm31 v = qzero();
+            for (int i = lane; i < TAIL_COLS; i += 32) v = qadd(v, part[warp * TAIL_COLS + i]);
+            for (int off = 16; off > 0; off >>= 1) {
+                v.a = madd(v.a, __shfl_xor_sync(0xffffffffu, v.a, off));
+                v.b = madd(v.b, __shfl_xor_sync(0xffffffffu, v.b, off));
+                v.c = madd(v.c, __shfl_xor_sync(0xffffffffu, v.c, off));
+                v.d = madd(v.d, __shfl_xor_sync(0xffffffffu, v.d, off));
+            }
+            if (lane == 0) {
+                red[warp][0][0] = v.a; red[warp][1][0] = v.b; red[warp][2][0] = v.c; red[warp][3][0] = v.d;
+            }
+        }
+        __syncthreads();
+        if (t < LA_WORDS) {
+            const int g = t >> 2, w = t & 3;
+            uint32_t v = red[g][w][0];
+            if (g == 4) v = madd(v, red[10][w][0]);
+            res[t] = v;
+        }
+        __syncthreads();
+        if (t == 0) publish(sig, seq_base + j, res, LA_WORDS);
+        __syncthreads();
+    }
+}
+
+int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0, bool wait0, qm31 alpha0,
+                          uint32_t* sig, uint32_t seq_base, const uint32_t* msg, uint32_t tag_base, int slots,
+                          uint32_t* status, cudaStream_t s) {
+    const size_t smem = 2 * L0 * sizeof(uint4);
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(lookahead_tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(4 * LA_TAIL_MAX * sizeof(uint4))) != cudaSuccess)
+            return -1;
+        attr_set = true;
+    }
+    lookahead_tail_kernel<<<1, TAIL_THREADS, smem, s>>>(A, B, (int)L0, fold0 ? 1 : 0, wait0 ? 1 : 0, alpha0, sig,
+                                                        seq_base, msg, tag_base, slots, status);
+    return 0;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 static unsigned round_blocks(size_t work, int max_blocks) {
     size_t b = (work + 255) / 256;
@@ -516,22 +997,27 @@ void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, c
 
 void launch_fold_round_qm31(uint4* A, uint4* B, size_t len, qm31 alpha, const RoundScratch& rs, cudaStream_t s) {
     const size_t h = len / 2;
-    fold_round_qm31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha, rs.partials,
-                                                                                rs.ticket, rs.out, rs.sig, rs.seq);
+    fold_round_qm31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha_rows(alpha),
+                                                                                rs.partials, rs.ticket, rs.out,
+                                                                                rs.sig, rs.seq);
 }
 
 void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const RoundScratch& rs, uint32_t* err,
                       cudaStream_t s) {
     const size_t q = len / 2;
-    round_m31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out, err,
-                                                                                 rs.sig, rs.seq);
+    if (q % 4 == 0 && aligned16(A) && aligned16(B))
+        round_m31_kernel<4><<<round_blocks(q / 4, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket,
+                                                                               rs.out, err, rs.sig, rs.seq);
+    else
+        round_m31_kernel<1><<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out,
+                                                                           err, rs.sig, rs.seq);
 }
 
 void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm31 alpha, uint4* Ao, uint4* Bo,
                            const RoundScratch& rs, cudaStream_t s) {
     const size_t h = len / 2;
-    fold_round_m31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha, Ao, Bo, rs.partials,
-                                                                               rs.ticket, rs.out, rs.sig, rs.seq);
+    fold_round_m31_kernel<<<round_blocks((h / 2 + FR_UNROLL - 1) / FR_UNROLL, rs.max_blocks), 256, 0, s>>>(
+        A, B, h, alpha, Ao, Bo, rs.partials, rs.ticket, rs.out, rs.sig, rs.seq);
 }
 
 __global__ void final_fold_kernel(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,

@@ -218,6 +218,11 @@ int zkml_sumcheck_export(zkml_ctx *ctx, uint32_t *out_a, uint32_t *out_b);
 /* Fold length-2 vectors with alpha into the final values. */
 int zkml_sumcheck_finalize(zkml_ctx *ctx, const uint32_t alpha[4], uint32_t out_a[4], uint32_t out_b[4]);
 
+/* Self-test of the bounded waits: queues one round kernel whose challenge is
+ * never posted; *status_out = 1 when its wait ran out and it flagged the
+ * timeout instead of hanging.  Takes a few seconds; no GPU fault is involved. */
+int zkml_selftest_wait_timeout(zkml_ctx *ctx, uint32_t *status_out);
+
 /* ---- Allocation-free restriction ------------------------------------------- */
 
 /* No counterpart in the reference: an extra entry point for callers that

@@ -64,7 +64,7 @@ enum KernelClass { KC_RESTRICT_COLS = 0, KC_RESTRICT_ROWS = 1, KC_ROUND = 2, KC_
 struct KTimer {
     ::zkml_ctx* ctx;
     int cls;
-    KTimer(::zkml_ctx* c, int k);
+    KTimer(::zkml_ctx* c, int k, bool enabled = true);  // enabled = false: record nothing
     ~KTimer();
 };
 
@@ -128,6 +128,7 @@ struct zkml_ctx {
     uint32_t* h_la_msg() const { return h_sig + 256; }
     uint32_t* d_la_msg() const { return d_sig + 256; }
     uint32_t la_msg_seq = 0;
+    bool la_queue = true;  // queue look-ahead kernels up front (ZKML_LA_QUEUE=0 turns it off)
     bool la_tail = true;  // single-block tail for the last look-ahead rounds (ZKML_LOOKAHEAD_TAIL=0 turns it off)
     uint32_t* h_msg() const { return h_sig + 64; }  // host -> GPU words (own cache lines)
     uint32_t* d_msg() const { return d_sig + 64; }

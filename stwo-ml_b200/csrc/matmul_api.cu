@@ -62,8 +62,8 @@ static cudaEvent_t pool_event(zkml_ctx* ctx) {
     return e;
 }
 
-KTimer::KTimer(zkml_ctx* c, int k) : ctx(c), cls(k) {
-    if (!ctx->timing || !(ctx->timing_mask & (1u << k))) {
+KTimer::KTimer(zkml_ctx* c, int k, bool enabled) : ctx(c), cls(k) {
+    if (!enabled || !ctx->timing || !(ctx->timing_mask & (1u << k))) {
         cls = -1;
         return;
     }
@@ -322,60 +322,78 @@ static void la_next_sums(const uint32_t* w, const qm31& x, uint32_t s12[12]) {
     stq(s12 + 8, quad(ldq(w + 28), ldq(w + 36), ldq(w + 32)));
 }
 
-// The look-ahead kernels of one sumcheck, queued on the stream up front: kernel
-// 0 needs no challenge (or is given it), kernel j > 0 waits for the host to post
-// the challenge of the round before it into its slot.  Every queued kernel
-// either gets its challenge or an abort, so the queue always drains.
+// The look-ahead kernels of one sumcheck.  Queued mode (the default) puts them
+// all on the stream up front: kernel 0 needs no challenge (or is given it),
+// kernel j > 0 waits for the host to post the challenge of the round before it
+// into its slot, and the rounds whose vectors fit LA_TAIL_MAX run in one
+// resident block.  Every queued kernel either gets its challenge or an abort,
+// so the queue always drains.  Unqueued mode (ZKML_LA_QUEUE=0, and always under
+// a profiler that replays launches one at a time, which would otherwise leave a
+// queued kernel waiting for a post that cannot come) launches kernel j when its
+// challenge is known.
 struct LaQueue {
     static constexpr int MAX = 40;
     zkml_ctx* ctx;
+    uint4 *A = nullptr, *B = nullptr;
+    RoundScratch rs;
+    cudaStream_t stream = nullptr;
+    bool queued = true;
     int n = 0, posted = 1;
     uint32_t seq[MAX], tag[MAX];
     int slot[MAX];
     size_t len[MAX];
 
-    explicit LaQueue(zkml_ctx* c) : ctx(c) {}
+    explicit LaQueue(zkml_ctx* c) : ctx(c), queued(c->la_queue) {}
 
-    int enqueue(uint4* A, uint4* B, size_t L0, bool fold0, const qm31& alpha0, RoundScratch rs, cudaStream_t s) {
-        for (size_t L = L0; L >= 2 && n < MAX; L /= 2, n++) {
-            len[n] = L;
-            if (ctx->la_tail && L <= LA_TAIL_MAX) {
-                // the remaining rounds in one resident block
-                const int n0 = n;
-                for (size_t l = L; l >= 2; l /= 2, n++) {
-                    len[n] = l;
-                    seq[n] = ++ctx->sig_seq;
-                    if (n > 0) {
-                        tag[n] = ++ctx->la_msg_seq;
-                        slot[n] = (int)(tag[n] % zkml_ctx::LA_SLOTS);
-                    }
-                }
-                const bool wait0 = n0 > 0;
+    int enqueue(uint4* A_, uint4* B_, size_t L0, bool fold0, const qm31& alpha0, RoundScratch rs_, cudaStream_t s) {
+        A = A_;
+        B = B_;
+        rs = rs_;
+        stream = s;
+        n = 0;
+        posted = 1;
+        for (size_t L = L0; L >= 2 && n < MAX; L /= 2) len[n++] = L;
+        if (!queued) return launch_one(0, fold0, alpha0, nullptr, 0);
+        for (int j = 0; j < n; j++) {
+            seq[j] = ++ctx->sig_seq;
+            if (j > 0) {
+                tag[j] = ++ctx->la_msg_seq;
+                slot[j] = (int)(tag[j] % zkml_ctx::LA_SLOTS);
+            }
+        }
+        for (int j = 0; j < n; j++) {
+            if (ctx->la_tail && len[j] <= LA_TAIL_MAX) {  // the remaining rounds in one resident block
+                const bool wait0 = j > 0;
                 const bool f0 = wait0 || fold0;
-                const uint32_t tag_base = wait0 ? tag[n0] : (n > 1 ? tag[1] - 1 : 0);
-                if (launch_lookahead_tail(A, B, f0 ? 2 * L : L, f0, wait0, alpha0, rs.sig, seq[n0],
+                const uint32_t tag_base = wait0 ? tag[j] : (n > 1 ? tag[1] - 1 : 0);
+                if (launch_lookahead_tail(A, B, f0 ? 2 * len[j] : len[j], f0, wait0, alpha0, rs.sig, seq[j],
                                           ctx->d_la_msg(), tag_base, zkml_ctx::LA_SLOTS, ctx->la_status(), s))
                     return set_error(ZKML_ERR_CUDA, "cannot configure the look-ahead tail kernel");
                 ZK_CUDA(cudaGetLastError());
                 ctx->launches++;
                 return ZKML_OK;
             }
-            rs.seq = seq[n] = ++ctx->sig_seq;
-            if (n == 0) {
-                KTimer t(ctx, KC_ROUND);
-                launch_round_lookahead(A, B, L, fold0, alpha0, rs, s);
-            } else {
-                tag[n] = ++ctx->la_msg_seq;
-                slot[n] = (int)(tag[n] % zkml_ctx::LA_SLOTS);
-                launch_round_lookahead(A, B, L, true, qzero(), rs, s, ctx->d_la_msg() + 8 * slot[n], tag[n],
-                                       ctx->la_status(), ctx->la_mailbox());
-            }
-            ZK_CUDA(cudaGetLastError());
-            ctx->launches++;
+            int rc = j == 0 ? launch_one(0, fold0, alpha0, nullptr, 0)
+                            : launch_one(j, true, qzero(), ctx->d_la_msg() + 8 * slot[j], tag[j]);
+            if (rc) return rc;
         }
         return ZKML_OK;
     }
-    void post(int j, const qm31& a, bool abort) {
+    int launch_one(int j, bool fold, const qm31& alpha, const uint32_t* wait_msg, uint32_t wait_tag) {
+        if (!queued) seq[j] = ++ctx->sig_seq;
+        rs.seq = seq[j];
+        {
+            KTimer t(ctx, KC_ROUND, wait_msg == nullptr);
+            launch_round_lookahead(A, B, len[j], fold, alpha, rs, stream, wait_msg, wait_tag, ctx->la_status(),
+                                   ctx->la_mailbox());
+        }
+        ZK_CUDA(cudaGetLastError());
+        ctx->launches++;
+        return ZKML_OK;
+    }
+    // Hands round j its challenge (the one drawn in round j - 1).
+    int post(int j, const qm31& a, bool abort) {
+        if (!queued) return abort ? ZKML_OK : launch_one(j, true, a, nullptr, 0);
         volatile uint32_t* m = ctx->h_la_msg() + 8 * slot[j];
         m[1] = a.a;
         m[2] = a.b;
@@ -384,6 +402,7 @@ struct LaQueue {
         m[5] = abort ? 1u : 0u;
         std::atomic_thread_fence(std::memory_order_release);
         m[0] = tag[j];
+        return ZKML_OK;
     }
     void abort_rest() {
         for (; posted < n; posted++) post(posted, qzero(), true);
@@ -511,7 +530,10 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             }
             memcpy(la_w, words, sizeof(la_w));
             alpha_prev = alpha;
-            laq.post(++j, alpha, false);  // releases the queued kernel of the next round
+            if ((rc = laq.post(++j, alpha, false))) {  // releases (or launches) the next round's kernel
+                laq.abort_rest();
+                return rc;
+            }
             laq.posted = j + 1;
             continue;
         }
@@ -631,6 +653,10 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
         if (lv) ctx->lookahead_max = strtoull(lv, nullptr, 10);
         const char* tv = getenv("ZKML_LOOKAHEAD_TAIL");
         if (tv) ctx->la_tail = tv[0] != '0';
+        const char* qv = getenv("ZKML_LA_QUEUE");
+        if (qv) ctx->la_queue = qv[0] != '0';
+        // a profiler that serialises launches would hold a queued kernel back from the post it waits for
+        if (getenv("CUDA_INJECTION64_PATH")) ctx->la_queue = false;
     }
     ctx->max_round_blocks = ctx->num_sms * 8;
     int rc = ZKML_OK;

@@ -137,4 +137,32 @@ int zkml_sumcheck_finalize(zkml_ctx* ctx, const uint32_t alpha[4], uint32_t out_
     return ZKML_OK;
 }
 
+// Queues one look-ahead round kernel that waits for a challenge nobody posts and
+// reports how its bounded wait ended: *status_out = 1 when the kernel gave up
+// and flagged the timeout (the expected outcome).  Takes a few seconds.
+int zkml_selftest_wait_timeout(zkml_ctx* ctx, uint32_t* status_out) {
+    if (!ctx || !status_out) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    int rc;
+    if ((rc = ctx->fa.ensure(64 * 16)) || (rc = ctx->fb.ensure(64 * 16))) return rc;
+    ZK_CUDA(cudaMemsetAsync(ctx->fa.ptr, 0, 64 * 16, ctx->stream));
+    ZK_CUDA(cudaMemsetAsync(ctx->fb.ptr, 0, 64 * 16, ctx->stream));
+    ZK_CUDA(cudaMemsetAsync(ctx->la_status(), 0, 4, ctx->stream));
+    RoundScratch rs = ctx->round_scratch();
+    rs.sig = ctx->d_sig;
+    rs.seq = ++ctx->sig_seq;
+    const uint32_t tag = ++ctx->la_msg_seq;  // never posted
+    launch_round_lookahead(ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), 32, true, qzero(), rs, ctx->stream,
+                           ctx->d_la_msg() + 8 * (tag % zkml_ctx::LA_SLOTS), tag, ctx->la_status(),
+                           ctx->la_mailbox());
+    ZK_CUDA(cudaGetLastError());
+    ctx->launches++;
+    uint32_t st = 0;
+    ZK_CUDA(cudaMemcpyAsync(&st, ctx->la_status(), 4, cudaMemcpyDeviceToHost, ctx->stream));
+    ZK_CUDA(cudaStreamSynchronize(ctx->stream));
+    ZK_CUDA(cudaMemsetAsync(ctx->la_status(), 0, 4, ctx->stream));
+    *status_out = st;
+    return ZKML_OK;
+}
+
 }  // extern "C"

@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
 // 40 result words are reduced through shared memory by a rolled loop.
 constexpr int LA_WORDS = 40;
 constexpr int LA_THREADS = 256;
-constexpr unsigned long long kLaSpinLimit = 1ull << 23;  // ~2 s with the back-off below
+constexpr unsigned long long kLaSpinLimit = 1ull << 21;  // a few seconds with the back-off below
 
 __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
     uint32_t v;

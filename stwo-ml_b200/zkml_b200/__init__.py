@@ -112,6 +112,7 @@ _SIGS = {
     "zkml_sumcheck_round": (C.c_int, [C.c_void_p, C.c_void_p, _u32]),
     "zkml_sumcheck_export": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "zkml_sumcheck_finalize": (C.c_int, [C.c_void_p, _u32, _u32, _u32]),
+    "zkml_selftest_wait_timeout": (C.c_int, [C.c_void_p, _u32]),
     "zkml_prove_gkr_matmul": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                         C.c_void_p, C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t), _u64,
                                         _u64]),

@@ -348,7 +348,7 @@ def run_product(args):
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
-    t = torch.tensor([ms], dtype=torch.float64)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda" if world > 1 else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     launches = ctx.kernel_launches() - l0

@@ -84,6 +84,7 @@ struct zkml_ctx {
     zk::DevBuf partials;            // per-block round partials
     zk::DevBuf small;               // ticket + out words + error flag
     zk::DevBuf act_tables[6];
+    zk::DevBuf rc_table;            // byte-plane eq table of the tensor-pipe column restriction
     // stepwise product-sumcheck session (zkml_sumcheck_*)
     zk::DevBuf sc_a, sc_b;          // staged M31 inputs
     const uint32_t* sc_a32 = nullptr;
@@ -128,6 +129,7 @@ struct zkml_ctx {
     uint32_t* h_la_msg() const { return h_sig + 256; }
     uint32_t* d_la_msg() const { return d_sig + 256; }
     uint32_t la_msg_seq = 0;
+    bool restrict_tc = true;  // tensor-pipe column restriction when the layout allows (ZKML_RESTRICT_TC=0: off)
     bool la_queue = true;  // queue look-ahead kernels up front (ZKML_LA_QUEUE=0 turns it off)
     bool la_tail = true;  // single-block tail for the last look-ahead rounds (ZKML_LOOKAHEAD_TAIL=0 turns it off)
     uint32_t* h_msg() const { return h_sig + 64; }  // host -> GPU words (own cache lines)

@@ -608,11 +608,19 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
         launch_eq_table(r_j, hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
         launch_eq_table(r_j + hi_vars, lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
         ZK_CUDA(cudaMemsetAsync(ctx->acc_b.ptr, 0, k * 32, s));
+        const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n);
+        if (tc && (rc = ctx->rc_table.ensure(16 * ((n + 31) / 32 * 32)))) return rc;
         {
             KTimer t(ctx, KC_RESTRICT_COLS);
-            launch_restrict_cols(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
-                                 ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
+            if (tc)
+                launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
+                                        ctx->rc_table.as<uint8_t>(), ctx->acc_b.as<unsigned long long>(),
+                                        ctx->err_flag(), ctx->num_sms, s);
+            else
+                launch_restrict_cols(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
+                                     ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
         }
+        if (tc) ctx->launches++;
         launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
         ctx->launches += 4;
     }
@@ -653,6 +661,8 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
         if (lv) ctx->lookahead_max = strtoull(lv, nullptr, 10);
         const char* tv = getenv("ZKML_LOOKAHEAD_TAIL");
         if (tv) ctx->la_tail = tv[0] != '0';
+        const char* rv = getenv("ZKML_RESTRICT_TC");
+        if (rv) ctx->restrict_tc = rv[0] != '0';
         const char* qv = getenv("ZKML_LA_QUEUE");
         if (qv) ctx->la_queue = qv[0] != '0';
         // a profiler that serialises launches would hold a queued kernel back from the post it waits for
@@ -696,6 +706,7 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
                       &ctx->eq_a, &ctx->eq_hi, &ctx->eq_lo, &ctx->partials, &ctx->small};
     for (DevBuf* b : bufs) b->release();
     for (DevBuf& t : ctx->act_tables) t.release();
+    ctx->rc_table.release();
     ctx->sc_a.release();
     ctx->sc_b.release();
     if (ctx->h_small) cudaFreeHost(ctx->h_small);

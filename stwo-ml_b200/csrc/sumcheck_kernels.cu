@@ -242,6 +242,171 @@ void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4
 }
 
 // ---------------------------------------------------------------------------
+// Column restriction on the tensor pipe (n % 4 == 0, 16-byte aligned B).
+//
+// f_b[i] = sum_j B[i][j] L_j is an exact integer GEMM of the k x n matrix B
+// with the n x 4 matrix of eq components, reduced mod P.  Both sides are split
+// into bytes: B[i][j] = sum_b 256^b B_b[i][j] and L_j^c = sum_l 256^l L_l^c[j],
+// so f_b[i]^c = sum_{b,l} 256^(b+l) (B_b L_l^c)[i] with every partial product
+// an exact u8 x u8 -> s32 MMA (a block chunk has 1024 columns, so a partial is
+// at most 1024 * 255^2 < 2^31).  A warp takes 16 rows at a time; each 16 x 32
+// tile of B arrives as four 16-byte loads per thread whose byte planes (three
+// PRMTs per plane register) are exactly the A fragments of mma.m16n8k32, with
+// K running over consecutive columns.  The eq side is a 16 x n byte-plane table
+// (row c * 4 + l, built once per call by restrict_table_kernel), staged per
+// block chunk in shared memory.  Per 16 x 32 tile: 8 MMAs (4 byte planes x 2
+// N-tiles of 8 (c, l) columns), ~1.5 PRMT per element, no 64-bit integer work:
+// the kernel is left with the HBM stream.
+// ---------------------------------------------------------------------------
+constexpr int TC_CH = 1024;                 // columns per block chunk
+constexpr int TC_TROW = TC_CH + 16;         // padded table row (bytes): conflict-free fragment loads
+constexpr int TC_WARPS = 8;
+
+__global__ void restrict_table_kernel(const uint4* __restrict__ lhi, const uint4* __restrict__ llo, uint32_t n,
+                                      uint32_t npad, uint8_t* __restrict__ T) {
+    for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < npad; j += gridDim.x * blockDim.x) {
+        qm31 L = qzero();
+        if (j < n) L = qmul(ld_q(lhi + (j >> 6)), ld_q(llo + (j & 63)));
+        const uint32_t w[4] = {L.a, L.b, L.c, L.d};
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+            for (int l = 0; l < 4; l++) T[(size_t)(c * 4 + l) * npad + j] = (uint8_t)(w[c] >> (8 * l));
+    }
+}
+
+__device__ __forceinline__ void mma_u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Byte planes of four consecutive u32 elements: plane b = [e0.b, e1.b, e2.b, e3.b].
+__device__ __forceinline__ void byte_planes(const uint4& e, uint32_t& p0, uint32_t& p1, uint32_t& p2,
+                                            uint32_t& p3) {
+    const uint32_t t01 = __byte_perm(e.x, e.y, 0x5140), t23 = __byte_perm(e.z, e.w, 0x5140);
+    const uint32_t u01 = __byte_perm(e.x, e.y, 0x7362), u23 = __byte_perm(e.z, e.w, 0x7362);
+    p0 = __byte_perm(t01, t23, 0x5410);
+    p1 = __byte_perm(t01, t23, 0x7632);
+    p2 = __byte_perm(u01, u23, 0x5410);
+    p3 = __byte_perm(u01, u23, 0x7632);
+}
+
+// 256^s mod P for s = 0..6 (256^s = 2^(8s), 2^31 = 1 mod P).
+__device__ __forceinline__ uint32_t pow256(int s) { return 1u << ((8 * s) % 31); }
+
+__global__ void __launch_bounds__(TC_WARPS * 32) restrict_cols_tc_kernel(const uint32_t* __restrict__ B, uint32_t k,
+                                                                         uint32_t n, const uint8_t* __restrict__ T,
+                                                                         uint32_t npad,
+                                                                         unsigned long long* __restrict__ acc_out,
+                                                                         uint32_t* __restrict__ err) {
+    __shared__ __align__(16) uint8_t tb[16 * TC_TROW];
+    const uint32_t c0 = blockIdx.x * TC_CH;
+    const uint32_t cw = min((uint32_t)TC_CH, npad - c0);  // chunk width (multiple of 32)
+    for (uint32_t i = threadIdx.x; i < 16 * (cw / 16); i += blockDim.x) {
+        const uint32_t r = i / (cw / 16), q = i % (cw / 16);
+        *reinterpret_cast<uint4*>(tb + r * TC_TROW + 16 * q) =
+            *reinterpret_cast<const uint4*>(T + (size_t)r * npad + c0 + 16 * q);
+    }
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tg = lane & 3;
+    const uint32_t row_tiles = (k + 15) / 16;
+    const uint32_t c_end = min(n, c0 + cw);
+    uint32_t bad = 0;
+    for (uint32_t rt = blockIdx.y * TC_WARPS + warp; rt < row_tiles; rt += gridDim.y * TC_WARPS) {
+        const uint32_t r0 = rt * 16 + g, r1 = r0 + 8;
+        const bool v0 = r0 < k, v1 = r1 < k;
+        const uint4* p0 = reinterpret_cast<const uint4*>(B + (size_t)(v0 ? r0 : 0) * n);
+        const uint4* p1 = reinterpret_cast<const uint4*>(B + (size_t)(v1 ? r1 : 0) * n);
+        int acc[4][2][4];
+#pragma unroll
+        for (int b = 0; b < 4; b++)
+#pragma unroll
+            for (int t = 0; t < 2; t++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[b][t][e] = 0;
+        // two 32-column steps per iteration: all eight 16-byte loads issue before any MMA
+        for (uint32_t j0 = c0; j0 < c_end; j0 += 64) {
+            uint4 x[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t ja = j0 + 32 * h + 4 * tg, jb = ja + 16;
+                const uint4 z = make_uint4(0, 0, 0, 0);
+                x[h][0] = (v0 && ja < c_end) ? __ldcs(p0 + ja / 4) : z;
+                x[h][1] = (v1 && ja < c_end) ? __ldcs(p1 + ja / 4) : z;
+                x[h][2] = (v0 && jb < c_end) ? __ldcs(p0 + jb / 4) : z;
+                x[h][3] = (v1 && jb < c_end) ? __ldcs(p1 + jb / 4) : z;
+            }
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t jj = j0 + 32 * h - c0;
+                if (jj >= cw) break;
+                uint32_t a[4][4];  // [plane][fragment register]
+#pragma unroll
+                for (int f = 0; f < 4; f++) {
+                    bad |= x[h][f].x | x[h][f].y | x[h][f].z | x[h][f].w;
+                    byte_planes(x[h][f], a[0][f], a[1][f], a[2][f], a[3][f]);
+                }
+#pragma unroll
+                for (int t = 0; t < 2; t++) {
+                    const uint8_t* trow = tb + (8 * t + g) * TC_TROW + jj + 4 * tg;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(trow);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(trow + 16);
+#pragma unroll
+                    for (int b = 0; b < 4; b++) mma_u8(acc[b][t], a[b], b0, b1);
+                }
+            }
+        }
+        // acc[b][t][e]: rows (g, g, g+8, g+8), columns 8t + 2tg + (e & 1) = (c, l) with
+        // c = 2t + (tg >> 1), l = 2 (tg & 1) + (e & 1).  Combine the byte weights, then add the
+        // partner lane's (other two l) and let the even lane post one atomic per (row, c).
+#pragma unroll
+        for (int t = 0; t < 2; t++) {
+#pragma unroll
+            for (int hr = 0; hr < 2; hr++) {
+                uint64_t sum = 0;
+#pragma unroll
+                for (int b = 0; b < 4; b++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int l = 2 * (tg & 1) + e;
+                        sum = acc_fold(sum, mul_wide((uint32_t)acc[b][t][2 * hr + e], pow256(b + l)));
+                    }
+                uint32_t v = canon64(sum);
+                v = madd(v, __shfl_xor_sync(0xffffffffu, v, 1));
+                const uint32_t row = hr ? r1 : r0;
+                if ((tg & 1) == 0 && row < k) atomicAdd(acc_out + 4 * (size_t)row + 2 * t + (tg >> 1), (unsigned long long)v);
+            }
+        }
+    }
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+}
+
+bool restrict_cols_tc_ok(const uint32_t* B, uint32_t n) {
+    return n % 4 == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0;
+}
+
+void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
+                             uint8_t* table, unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s) {
+    const uint32_t npad = (n + 31) / 32 * 32;
+    {
+        uint32_t blocks = (npad + 255) / 256;
+        if (blocks > 4096) blocks = 4096;
+        restrict_table_kernel<<<blocks, 256, 0, s>>>(lhi, llo, n, npad, table);
+    }
+    const uint32_t chunks = (npad + TC_CH - 1) / TC_CH;
+    const uint32_t row_tiles = (k + 15) / 16;
+    // about four resident 8-warp blocks per SM in total
+    uint32_t gy = (uint32_t)((num_sms * 4 + chunks - 1) / chunks);
+    const uint32_t gy_max = (row_tiles + TC_WARPS - 1) / TC_WARPS;
+    if (gy > gy_max) gy = gy_max;
+    if (gy == 0) gy = 1;
+    restrict_cols_tc_kernel<<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, table, npad, acc, err);
+}
+
+// ---------------------------------------------------------------------------
 // Row restriction f_a[j] = sum_i A[i][j] L_i.  A is small (m x k activations);
 // each thread owns one column and a chunk of 16 rows, partials meet in
 // 64-bit atomics.

@@ -1,6 +1,6 @@
 """The sumcheck round schedules give the same proofs.
 
-The round loop has four schedules (look-ahead rounds queued up front with a
+The restriction has a tensor-pipe and a generic kernel, and the round loop has four schedules (look-ahead rounds queued up front with a
 resident-block tail; queued without the tail; launched one at a time; and the
 plain fold-and-sum rounds).  Each is selected by environment variables read
 when a context is created, so every schedule runs in its own process and is
@@ -39,7 +39,7 @@ def check(a, b, r_i, r_j):
 for lg in (1, 2, 5, 11, 12, 17):
     n = 1 << lg
     check(uniform_m31(n, lg).reshape(1, n), uniform_m31(n, lg + 50).reshape(n, 1), np.zeros((0, 4), np.uint32), np.zeros((0, 4), np.uint32))
-for (m, k, n) in ((4, 96, 80), (8, 3000, 64), (2, 8192, 16)):
+for (m, k, n) in ((4, 96, 80), (8, 3000, 64), (2, 8192, 16), (3, 37, 1028), (16, 300, 2052), (5, 17, 6)):
     a = int_matrix_m31(m, k, 1)
     b = int_matrix_m31(k, n, 2)
     lm = (m - 1).bit_length()
@@ -53,6 +53,7 @@ MODES = {
     "queued_no_tail": {"ZKML_LOOKAHEAD_TAIL": "0"},
     "unqueued": {"ZKML_LA_QUEUE": "0"},
     "plain_rounds": {"ZKML_LOOKAHEAD_MAX": "0"},
+    "generic_restriction": {"ZKML_RESTRICT_TC": "0"},
 }
 
 

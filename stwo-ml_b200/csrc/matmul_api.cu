@@ -328,8 +328,8 @@ static void la_next_sums(const uint32_t* w, const qm31& x, uint32_t s12[12]) {
 // into its slot, and the rounds whose vectors fit LA_TAIL_MAX run in one
 // resident block.  Every queued kernel either gets its challenge or an abort,
 // so the queue always drains.  Unqueued mode (ZKML_LA_QUEUE=0, and always under
-// a profiler that replays launches one at a time, which would otherwise leave a
-// queued kernel waiting for a post that cannot come) launches kernel j when its
+// Nsight Compute, which serialises launches and would otherwise leave a queued
+// kernel waiting for a post that cannot come) launches kernel j when its
 // challenge is known.
 struct LaQueue {
     static constexpr int MAX = 40;
@@ -665,8 +665,11 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
         if (rv) ctx->restrict_tc = rv[0] != '0';
         const char* qv = getenv("ZKML_LA_QUEUE");
         if (qv) ctx->la_queue = qv[0] != '0';
-        // a profiler that serialises launches would hold a queued kernel back from the post it waits for
-        if (getenv("CUDA_INJECTION64_PATH")) ctx->la_queue = false;
+        // A profiler that serialises launches would hold a queued kernel back from the post it waits
+        // for; Nsight Compute marks its target processes with these variables.
+        if (getenv("NV_TPS_LAUNCH_TOKEN") || getenv("NV_NSIGHT_INJECTION_TRANSPORT_TYPE") ||
+            getenv("CUDA_INJECTION64_PATH"))
+            ctx->la_queue = false;
     }
     ctx->max_round_blocks = ctx->num_sms * 8;
     int rc = ZKML_OK;

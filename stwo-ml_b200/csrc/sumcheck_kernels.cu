@@ -261,6 +261,8 @@ void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4
 constexpr int TC_CH = 1024;                 // columns per block chunk
 constexpr int TC_TROW = TC_CH + 16;         // padded table row (bytes): conflict-free fragment loads
 constexpr int TC_WARPS = 8;
+constexpr int TC_MINB = 2;   // launch-bounds minimum blocks per SM
+constexpr int TC_STEPS = 2;  // 32-column steps loaded per iteration
 
 __global__ void restrict_table_kernel(const uint4* __restrict__ lhi, const uint4* __restrict__ llo, uint32_t n,
                                       uint32_t npad, uint8_t* __restrict__ T) {
@@ -297,7 +299,8 @@ __device__ __forceinline__ void byte_planes(const uint4& e, uint32_t& p0, uint32
 // 256^s mod P for s = 0..6 (256^s = 2^(8s), 2^31 = 1 mod P).
 __device__ __forceinline__ uint32_t pow256(int s) { return 1u << ((8 * s) % 31); }
 
-__global__ void __launch_bounds__(TC_WARPS * 32) restrict_cols_tc_kernel(const uint32_t* __restrict__ B, uint32_t k,
+template <int MINB, int STEPS>
+__global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(const uint32_t* __restrict__ B, uint32_t k,
                                                                          uint32_t n, const uint8_t* __restrict__ T,
                                                                          uint32_t npad,
                                                                          unsigned long long* __restrict__ acc_out,
@@ -327,11 +330,11 @@ __global__ void __launch_bounds__(TC_WARPS * 32) restrict_cols_tc_kernel(const u
             for (int t = 0; t < 2; t++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) acc[b][t][e] = 0;
-        // two 32-column steps per iteration: all eight 16-byte loads issue before any MMA
-        for (uint32_t j0 = c0; j0 < c_end; j0 += 64) {
-            uint4 x[2][4];
+        // STEPS 32-column steps per iteration: all their 16-byte loads issue before any MMA
+        for (uint32_t j0 = c0; j0 < c_end; j0 += 32 * STEPS) {
+            uint4 x[STEPS][4];
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
+            for (int h = 0; h < STEPS; h++) {
                 const uint32_t ja = j0 + 32 * h + 4 * tg, jb = ja + 16;
                 const uint4 z = make_uint4(0, 0, 0, 0);
                 x[h][0] = (v0 && ja < c_end) ? __ldcs(p0 + ja / 4) : z;
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32) restrict_cols_tc_kernel(const u
                 x[h][3] = (v1 && jb < c_end) ? __ldcs(p1 + jb / 4) : z;
             }
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
+            for (int h = 0; h < STEPS; h++) {
                 const uint32_t jj = j0 + 32 * h - c0;
                 if (jj >= cw) break;
                 uint32_t a[4][4];  // [plane][fragment register]
@@ -398,12 +401,12 @@ void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const ui
     }
     const uint32_t chunks = (npad + TC_CH - 1) / TC_CH;
     const uint32_t row_tiles = (k + 15) / 16;
-    // about four resident 8-warp blocks per SM in total
-    uint32_t gy = (uint32_t)((num_sms * 4 + chunks - 1) / chunks);
+    // one wave of TC_MINB resident 8-warp blocks per SM
+    uint32_t gy = (uint32_t)((num_sms * TC_MINB + chunks - 1) / chunks);
     const uint32_t gy_max = (row_tiles + TC_WARPS - 1) / TC_WARPS;
     if (gy > gy_max) gy = gy_max;
     if (gy == 0) gy = 1;
-    restrict_cols_tc_kernel<<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, table, npad, acc, err);
+    restrict_cols_tc_kernel<TC_MINB, TC_STEPS><<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, table, npad, acc, err);
 }
 
 // ---------------------------------------------------------------------------

@@ -690,7 +690,7 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     if (!rc) {
         // Hades round keys and Montgomery constants into this device's constant bank
         const felt two = f_from_u64(2);
-        if ((e = upload_hades_constants(HADES_RC, &F_R2, &two)) != cudaSuccess) rc = cuda_error(e, "upload constants");
+        if ((e = upload_hades_constants(HADES_RC, &F_R2, &two, &F_ONE)) != cudaSuccess) rc = cuda_error(e, "upload constants");
     }
     if (rc) {
         zkml_ctx_destroy(ctx);

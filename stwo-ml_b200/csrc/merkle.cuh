@@ -9,7 +9,8 @@
 
 namespace zk {
 
-cudaError_t upload_hades_constants(const void* rc107_mont, const void* r2_mont, const void* two_mont);
+cudaError_t upload_hades_constants(const void* rc107_mont, const void* r2_mont, const void* two_mont,
+                                   const void* one_mont);
 size_t merkle_padded_leaves(size_t n);
 size_t merkle_node_count(size_t n);
 int merkle_tree_launches(size_t n);

@@ -7,7 +7,10 @@
 // Montgomery form (identical bytes on host and device).
 #include <cuda_runtime.h>
 
+#include <cstring>
+
 #include "felt252.cuh"
+#include "felt26.cuh"
 #include "merkle.cuh"
 #include "qm31.cuh"
 
@@ -17,7 +20,7 @@ __constant__ dfelt c_mont_r2;  // 2^512 mod p: Montgomery conversion factor
 __constant__ dfelt c_mont_two; // Montgomery form of 2 (poseidon_hash capacity)
 
 // securefield_to_felt(v) in Montgomery form.
-__device__ __forceinline__ dfelt leaf_felt(uint4 v) {
+__device__ __forceinline__ dfelt leaf_int(uint4 v) {
     // canonical integer 2^124 | a << 93 | b << 62 | c << 31 | d, as 8 x u32
     dfelt x;
     x.w[0] = v.w | (v.z << 31);
@@ -25,13 +28,61 @@ __device__ __forceinline__ dfelt leaf_felt(uint4 v) {
     x.w[2] = (v.y >> 2) | (v.x << 29);
     x.w[3] = (v.x >> 3) | (1u << 28);
     x.w[4] = x.w[5] = x.w[6] = x.w[7] = 0;
-    return dmul(x, c_mont_r2);
+    return x;
+}
+
+__device__ __forceinline__ dfelt leaf_felt(uint4 v) { return dmul(leaf_int(v), c_mont_r2); }
+
+
+// 256-bit value in 8 x 32-bit words <-> 10 limbs of 26 bits.
+__device__ __forceinline__ f26 f26_from_words(const dfelt& x) {
+    f26 a;
+#pragma unroll
+    for (int i = 0; i < 10; i++) {
+        const int b = 26 * i, w = b >> 5, sh = b & 31;
+        uint64_t win = x.w[w];
+        if (w + 1 < 8) win |= (uint64_t)x.w[w + 1] << 32;
+        a.l[i] = (uint32_t)(win >> sh) & F26_MASK;
+    }
+    return a;
+}
+
+__device__ __forceinline__ dfelt f26_to_words(const f26& a) {  // 26-bit limbs, value < 2^256
+    dfelt x;
+#pragma unroll
+    for (int w = 0; w < 8; w++) {
+        const int b = 32 * w, i = b / 26, sh = b % 26;
+        uint64_t win = (uint64_t)a.l[i] >> sh;
+        if (i + 1 < 10) win |= (uint64_t)a.l[i + 1] << (26 - sh);
+        if (i + 2 < 10) win |= (uint64_t)a.l[i + 2] << (52 - sh);
+        x.w[w] = (uint32_t)win;
+    }
+    return x;
+}
+
+// Montgomery (2^256) node value -> Montgomery (2^260) lane: times 16.
+__device__ __forceinline__ f26 m256_to_m260(const dfelt& m) {
+    f26 a = f26_from_words(m);
+#pragma unroll
+    for (int i = 0; i < 10; i++) a.l[i] <<= 4;
+    return norm26(a);
+}
+
+// Montgomery (2^260) lane below 2p -> canonical Montgomery (2^256) node value.
+__device__ __forceinline__ dfelt m260_to_m256(const f26& x) {
+    const f26 r = mul26(x, c26.one256);  // < 1.01 p, 26-bit limbs
+    f26 d = r;
+    d.l[0] -= 1;
+    d.l[7] -= F26_P7;
+    d.l[9] -= F26_P9;
+    d = norm26(d);
+    return f26_to_words((int32_t)d.l[9] < 0 ? r : d);
 }
 
 __device__ __forceinline__ dfelt hash2(const dfelt& l, const dfelt& r) {
-    dfelt s[3] = {l, r, c_mont_two};
-    dhades(s);
-    return s[0];
+    f26 s[3] = {m256_to_m260(l), m256_to_m260(r), c26.two};
+    hades26(s);
+    return m260_to_m256(s[0]);
 }
 
 __device__ __forceinline__ dfelt ld_f(const dfelt* p) {
@@ -49,14 +100,19 @@ __device__ __forceinline__ void st_f(dfelt* p, const dfelt& f) {
     q[1] = make_uint4(f.w[4], f.w[5], f.w[6], f.w[7]);
 }
 
+// securefield_to_felt(v) as a Montgomery (2^260) lane.
+__device__ __forceinline__ f26 leaf26(uint4 v) { return mul26(f26_from_words(leaf_int(v)), c26.r2); }
+
 __global__ void __launch_bounds__(128) merkle_leaf_level_kernel(const uint4* __restrict__ leaves, size_t n_leaves,
                                                                 size_t n_pairs, dfelt* __restrict__ out) {
-    const dfelt zero = {{0, 0, 0, 0, 0, 0, 0, 0}};
+    f26 zero;
+#pragma unroll
+    for (int i = 0; i < 10; i++) zero.l[i] = 0;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_pairs; i += (size_t)gridDim.x * blockDim.x) {
         const size_t l = 2 * i, r = 2 * i + 1;
-        dfelt fl = l < n_leaves ? leaf_felt(leaves[l]) : zero;
-        dfelt fr = r < n_leaves ? leaf_felt(leaves[r]) : zero;
-        st_f(out + i, hash2(fl, fr));
+        f26 s[3] = {l < n_leaves ? leaf26(leaves[l]) : zero, r < n_leaves ? leaf26(leaves[r]) : zero, c26.two};
+        hades26(s);
+        st_f(out + i, m260_to_m256(s[0]));
     }
 }
 
@@ -97,11 +153,69 @@ static unsigned blocks_for(size_t n, int threads, int num_sms) {
     return (unsigned)b;
 }
 
-cudaError_t upload_hades_constants(const void* rc107_mont, const void* r2_mont, const void* two_mont) {
+// ---- host: the radix-2^26 constants -------------------------------------------
+namespace {
+const uint64_t kP64[4] = {1, 0, 0, 0x0800000000000011ull};
+
+bool geq_p(const uint64_t v[4]) {
+    for (int i = 3; i >= 0; i--)
+        if (v[i] != kP64[i]) return v[i] > kP64[i];
+    return true;
+}
+void sub_p(uint64_t v[4]) {
+    unsigned __int128 br = 0;
+    for (int i = 0; i < 4; i++) {
+        const unsigned __int128 d = (unsigned __int128)v[i] - kP64[i] - br;
+        v[i] = (uint64_t)d;
+        br = (d >> 64) & 1;
+    }
+}
+void dbl_modp(uint64_t v[4]) {  // v < p -> 2v mod p
+    uint64_t c = 0;
+    for (int i = 0; i < 4; i++) {
+        const uint64_t n = (v[i] << 1) | c;
+        c = v[i] >> 63;
+        v[i] = n;
+    }
+    if (geq_p(v)) sub_p(v);
+}
+f26 limbs26(const uint64_t v[4]) {
+    f26 a;
+    for (int i = 0; i < 10; i++) {
+        const int b = 26 * i, w = b / 64, sh = b % 64;
+        unsigned __int128 win = v[w];
+        if (w + 1 < 4) win |= (unsigned __int128)v[w + 1] << 64;
+        a.l[i] = (uint32_t)(win >> sh) & F26_MASK;
+    }
+    return a;
+}
+f26 times_2k(const void* mont256, int k) {  // value * 2^k mod p, as limbs
+    uint64_t v[4];
+    memcpy(v, mont256, 32);
+    for (int i = 0; i < k; i++) dbl_modp(v);
+    return limbs26(v);
+}
+}  // namespace
+
+cudaError_t upload_hades_constants(const void* rc107_mont, const void* r2_mont, const void* two_mont,
+                                   const void* one_mont) {
     cudaError_t e = cudaMemcpyToSymbol(c_hades_rc, rc107_mont, sizeof(dfelt) * 107);
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(c_mont_r2, r2_mont, sizeof(dfelt));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(c_mont_two, two_mont, sizeof(dfelt));
-    return e;
+    if (e != cudaSuccess) return e;
+    static F26Consts h;  // Montgomery (2^256) x -> x * 2^260 = value * 16
+    const uint64_t* rc = static_cast<const uint64_t*>(rc107_mont);
+    for (int i = 0; i < 107; i++) h.rc[i] = times_2k(rc + 4 * i, 4);
+    h.two = times_2k(two_mont, 4);
+    h.r2 = times_2k(r2_mont, 8);          // 2^512 * 2^8 = 2^520 mod p
+    h.one256 = times_2k(one_mont, 0);     // 2^256 mod p
+    const uint64_t p4[4] = {4, 0, 0, 4 * 0x0800000000000011ull};
+    f26 k = limbs26(p4);                  // 4p < 2^256, then lend 2^28 to every lower limb
+    k.l[0] += 1u << 28;
+    for (int i = 1; i < 9; i++) k.l[i] += (1u << 28) - 4;
+    k.l[9] -= 4;
+    h.kp4 = k;
+    return cudaMemcpyToSymbol(c26, &h, sizeof(h));
 }
 
 size_t merkle_padded_leaves(size_t n) {

@@ -311,7 +311,6 @@ def run_product(args):
     import torch.distributed as dist
 
     import zkml_b200 as Z
-    from zkml_b200.distributed import GpuSumcheckSession, TorchCollective, prove_product_sharded
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -324,16 +323,17 @@ def run_product(args):
     stream = torch.cuda.current_stream()
     ctx = Z.Context(dev)
     ctx.set_stream(stream.cuda_stream)
-    session = GpuSumcheckSession(ctx)
-    col = TorchCollective()
+    from zkml_b200.distributed import ShmExchange, prove_product_sharded_native
+    port = os.environ.get("MASTER_PORT", "0")
+    ex = ShmExchange(f"zkml_bench_{port}_{world}", world, rank, max_gather_bytes=32 << 16)
     n = 1 << args.log_n
     n_loc = n // world
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
     a = torch.randint(0, 2**31 - 1, (n_loc,), dtype=torch.int32, device="cuda", generator=g)
     b = torch.randint(0, 2**31 - 1, (n_loc,), dtype=torch.int32, device="cuda", generator=g)
 
-    def step():
-        return prove_product_sharded(a, b, n, Z.PoseidonChannel(), session=session, collective=col)
+    def step():  # the library's round loop; round words and the final gather go through shared memory
+        return prove_product_sharded_native(a, b, n, Z.PoseidonChannel(), ex, gather_local=1 << 16, ctx=ctx)
 
     for _ in range(args.warmup):
         step()
@@ -353,6 +353,26 @@ def run_product(args):
     ms = float(t.item())
     launches = ctx.kernel_launches() - l0
     dist.barrier()
+    merkle = None
+    if world == 1:
+        # config 5's commitment: Poseidon-252 Merkle root of the first MLE (QM31 leaves (a, 0, 0, 0)),
+        # 2^min(L, 26) leaves
+        lg = min(args.log_n, 26)
+        leaves = torch.zeros((1 << lg, 4), dtype=torch.int32, device="cuda")
+        leaves[:, 0] = a[: 1 << lg]
+        Z.commit_mle_root(leaves)
+        torch.cuda.synchronize()
+        m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 2
+        m0.record(stream)
+        for _ in range(reps):
+            Z.commit_mle_root(leaves)
+        m1.record(stream)
+        torch.cuda.synchronize()
+        mms = m0.elapsed_time(m1) / reps
+        merkle = {"leaves": 1 << lg, "ms": mms, "hashes_per_s": ((1 << lg) - 1) / (mms * 1e-3),
+                  "bound": "integer pipe (Hades, radix-2^26 Montgomery multiply-add columns)"}
+        del leaves
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
         # per-GPU bytes until the gather, then one GPU's share of the tail
@@ -365,6 +385,7 @@ def run_product(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "u32 (M31/QM31 integer)", "data": "synthetic (torch-seeded M31)",
             "config": {"workload": "C5 degree-2 product sumcheck, MLE split by low index bits",
+                       "exchange": "host shared memory between the ranks (12 words per round, one gather)",
                        "log_n": args.log_n, "gathered_at": proof.gathered_at,
                        "l2": "inputs larger than L2" if 8 * n_loc > 126e6 else "inputs fit in L2"},
             "gpu_launches": launches,
@@ -372,7 +393,9 @@ def run_product(args):
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": None, "algorithmic_bytes_per_gpu": per_gpu},
             "clocks": clk.summary(),
+            **({"merkle_commitment": merkle} if merkle else {}),
         }), flush=True)
+    ex.close()
     dist.destroy_process_group()
 
 

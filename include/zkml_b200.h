@@ -218,6 +218,41 @@ int zkml_sumcheck_export(zkml_ctx *ctx, uint32_t *out_a, uint32_t *out_b);
 /* Fold length-2 vectors with alpha into the final values. */
 int zkml_sumcheck_finalize(zkml_ctx *ctx, const uint32_t alpha[4], uint32_t out_a[4], uint32_t out_b[4]);
 
+/* ---- Sharded product sumcheck, native round loop ------------------------------
+ * One degree-2 product sumcheck over M31 vectors of global length n split across
+ * `world` ranks (one process and context per GPU): rank g holds the elements
+ * whose index is g (mod world), in order.  Per round the ranks all-reduce the
+ * 12 round words through `ex`, every rank runs the same host transcript (no
+ * challenge broadcast), and once the local length is at most gather_local the
+ * folded vectors are all-gathered, interleaved back to global order and the
+ * remaining rounds run on every rank's GPU.  The proof (round polynomials,
+ * challenges, final values) is identical on every rank and equal to
+ * zkml_reduce_matmul_layer on the 1 x n and n x 1 matrices.  The round loop of
+ * engine/src/backend.rs:141-178, split as the north star's multi-GPU plan asks. */
+typedef struct zkml_exchange {
+    void *user;
+    /* element-wise sum of n u64 words over all ranks, in place */
+    int (*allreduce_u64)(void *user, uint64_t *words, int n);
+    /* every rank's `bytes` from `local` into out, rank-major */
+    int (*allgather)(void *user, const void *local, void *out, size_t bytes);
+    int world;
+    int rank;
+} zkml_exchange;
+
+/* A zkml_exchange over a POSIX shared-memory segment for the ranks of one node
+ * (name unique per job; rank 0 creates it).  max_gather_bytes bounds one rank's
+ * allgather contribution.  All waits are bounded (60 s -> ZKML_ERR_TIMEOUT). */
+int zkml_shm_exchange_open(const char *name, int world, int rank, size_t max_gather_bytes, zkml_exchange *out);
+int zkml_shm_exchange_close(zkml_exchange *ex);
+
+/* a_local, b_local: this rank's n / world M31 elements (host or device).
+ * out_round_polys: log2(n) x 12 words, out_challenges: log2(n) x 4 words;
+ * *out_gathered_at: global length at which the vectors were gathered. */
+int zkml_prove_product_sharded(zkml_ctx *ctx, const uint32_t *a_local, const uint32_t *b_local, size_t n,
+                               size_t gather_local, const zkml_exchange *ex, zkml_channel *ch,
+                               uint32_t *out_round_polys, uint32_t *out_challenges, uint32_t out_final_a[4],
+                               uint32_t out_final_b[4], size_t *out_gathered_at);
+
 /* Self-test of the bounded waits: queues one round kernel whose challenge is
  * never posted; *status_out = 1 when its wait ran out and it flagged the
  * timeout instead of hanging.  Takes a few seconds; no GPU fault is involved. */

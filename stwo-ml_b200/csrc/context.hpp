@@ -49,6 +49,12 @@ int reduce_matmul_internal(::zkml_ctx* ctx, const uint32_t* a, size_t a_rows, si
                            uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
                            const ClaimHook* hook);
 
+// The sumcheck round loop (matmul_api.cu): M31 inputs (A32, B32) or QM31 (A, B)
+// of length len; writes log2(len) round polynomials and challenges.
+int run_sumcheck(::zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const uint32_t* B32, size_t len,
+                 zkml_channel* chs, uint32_t* out_rp, uint32_t* out_ch, uint32_t* fa_out, uint32_t* fb_out,
+                 const ClaimHook* hook);
+
 // Shared host helpers (matmul_api.cu).
 // device_view: `p` itself if it is device memory of the context's GPU, else a copy in `stage`.
 int device_view(::zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const void** out);

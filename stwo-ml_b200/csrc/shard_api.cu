@@ -12,6 +12,9 @@
 #include <cstring>
 #include <string>
 
+#include <vector>
+
+#include "channel.hpp"
 #include "context.hpp"
 
 namespace zk {
@@ -81,6 +84,30 @@ int load(zkml_ctx* ctx, const uint32_t* a, const uint32_t* b, size_t n, bool m31
     return ZKML_OK;
 }
 
+// Round coefficients from (s0, s1, s2 = s(2)): c0 = s0, c2 = (s2 - 2 s1 + s0) / 2, c1 = s1 - s0 - c2.
+void round_coeffs(const uint32_t* s12, qm31& c0, qm31& c1, qm31& c2) {
+    static const uint32_t inv2 = minv(2);
+    const qm31 s0 = qm(s12[0], s12[1], s12[2], s12[3]), s1 = qm(s12[4], s12[5], s12[6], s12[7]);
+    const qm31 s2 = qm(s12[8], s12[9], s12[10], s12[11]);
+    c0 = s0;
+    c2 = qmul_m(qadd(qsub(qsub(s2, s1), s1), s0), inv2);
+    c1 = qsub(qsub(s1, s0), c2);
+}
+
+void st4(uint32_t* p, const qm31& x) {
+    p[0] = x.a;
+    p[1] = x.b;
+    p[2] = x.c;
+    p[3] = x.d;
+}
+
+// Copies n words of a host or device buffer to the host.
+int to_host(const uint32_t* src, size_t n, std::vector<uint32_t>& dst) {
+    dst.resize(n);
+    ZK_CUDA(cudaMemcpy(dst.data(), src, n * 4, cudaMemcpyDefault));
+    return ZKML_OK;
+}
+
 }  // namespace
 }  // namespace zk
 
@@ -135,6 +162,126 @@ int zkml_sumcheck_finalize(zkml_ctx* ctx, const uint32_t alpha[4], uint32_t out_
     memcpy(out_b, w + 4, 16);
     ctx->sc_len = 1;
     return ZKML_OK;
+}
+
+int zkml_prove_product_sharded(zkml_ctx* ctx, const uint32_t* a_local, const uint32_t* b_local, size_t n,
+                               size_t gather_local, const zkml_exchange* ex, zkml_channel* chs,
+                               uint32_t* out_rp, uint32_t* out_ch, uint32_t out_final_a[4], uint32_t out_final_b[4],
+                               size_t* out_gathered_at) {
+    if (!ctx || !a_local || !b_local || !ex || !ex->allreduce_u64 || !ex->allgather || !chs || !out_rp || !out_ch ||
+        !out_final_a || !out_final_b)
+        return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    const size_t G = (size_t)ex->world;
+    if (!is_pow2(n) || n < 2) return set_error(ZKML_ERR_INVALID_ARG, "n must be a power of two >= 2");
+    if (G < 1 || !is_pow2(G) || n % G || ex->rank < 0 || (size_t)ex->rank >= G)
+        return set_error(ZKML_ERR_INVALID_ARG, "world size must be a power of two dividing n");
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    const size_t nl = n / G;
+    cudaStream_t s = ctx->stream;
+    int rc;
+    if (G == 1) {  // one rank: the plain product sumcheck on this GPU
+        const void *A = nullptr, *B = nullptr;
+        if ((rc = device_view(ctx, a_local, n * 4, ctx->sc_a, &A)) || (rc = device_view(ctx, b_local, n * 4, ctx->sc_b, &B)))
+            return rc;
+        if ((rc = ctx->fa.ensure(n / 2 * 16)) || (rc = ctx->fb.ensure(n / 2 * 16))) return rc;
+        ctx->sc_len = 0;
+        if (out_gathered_at) *out_gathered_at = n;
+        return run_sumcheck(ctx, nullptr, nullptr, static_cast<const uint32_t*>(A), static_cast<const uint32_t*>(B), n,
+                            chs, out_rp, out_ch, out_final_a, out_final_b, nullptr);
+    }
+    if (nl < 4 || nl <= gather_local) {
+        // too small to split: every rank proves the whole product
+        std::vector<uint32_t> la, lb, ga(n), gb(n), tmp(n);
+        if ((rc = to_host(a_local, nl, la)) || (rc = to_host(b_local, nl, lb))) return rc;
+        if ((rc = ex->allgather(ex->user, la.data(), tmp.data(), nl * 4))) return rc;
+        for (size_t g = 0; g < G; g++)
+            for (size_t j = 0; j < nl; j++) ga[j * G + g] = tmp[g * nl + j];
+        if ((rc = ex->allgather(ex->user, lb.data(), tmp.data(), nl * 4))) return rc;
+        for (size_t g = 0; g < G; g++)
+            for (size_t j = 0; j < nl; j++) gb[j * G + g] = tmp[g * nl + j];
+        if ((rc = ctx->sc_a.ensure(n * 4)) || (rc = ctx->sc_b.ensure(n * 4)) || (rc = ctx->fa.ensure(n * 16)) ||
+            (rc = ctx->fb.ensure(n * 16)))
+            return rc;
+        ZK_CUDA(cudaMemcpyAsync(ctx->sc_a.ptr, ga.data(), n * 4, cudaMemcpyHostToDevice, s));
+        ZK_CUDA(cudaMemcpyAsync(ctx->sc_b.ptr, gb.data(), n * 4, cudaMemcpyHostToDevice, s));
+        ctx->sc_len = 0;
+        if (out_gathered_at) *out_gathered_at = n;
+        return run_sumcheck(ctx, nullptr, nullptr, ctx->sc_a.as<uint32_t>(), ctx->sc_b.as<uint32_t>(), n, chs, out_rp,
+                            out_ch, out_final_a, out_final_b, nullptr);
+    }
+    // Split phase: round 0 over the local M31 elements, then fused fold + round per challenge.
+    const void *A = nullptr, *B = nullptr;
+    if ((rc = device_view(ctx, a_local, nl * 4, ctx->sc_a, &A)) || (rc = device_view(ctx, b_local, nl * 4, ctx->sc_b, &B)))
+        return rc;
+    if ((rc = ctx->fa.ensure(nl / 2 * 16)) || (rc = ctx->fb.ensure(nl / 2 * 16))) return rc;
+    ctx->sc_len = 0;
+    const uint32_t* A32 = static_cast<const uint32_t*>(A);
+    const uint32_t* B32 = static_cast<const uint32_t*>(B);
+    Channel ch(chs);
+    RoundScratch rs = ctx->round_scratch();
+    rs.sig = ctx->d_sig;
+    rs.seq = ++ctx->sig_seq;
+    {
+        KTimer t(ctx, KC_ROUND);
+        launch_round_m31(A32, B32, nl, rs, ctx->err_flag(), s);
+    }
+    ZK_CUDA(cudaGetLastError());
+    ctx->launches++;
+    size_t len = nl;
+    unsigned r = 0;
+    uint32_t words[12];
+    for (;; r++) {
+        if ((rc = wait_signal(ctx, rs.seq, words, 12))) return rc;
+        uint64_t w64[12];
+        for (int i = 0; i < 12; i++) w64[i] = words[i];
+        if ((rc = ex->allreduce_u64(ex->user, w64, 12))) return rc;
+        uint32_t s12[12];
+        for (int i = 0; i < 12; i++) s12[i] = (uint32_t)(w64[i] % P);
+        qm31 c0, c1, c2, alpha;
+        round_coeffs(s12, c0, c1, c2);
+        ch.mix_poly_coeffs(c0, c1, c2);
+        alpha = ch.draw_qm31();
+        st4(out_rp + 12 * r, c0);
+        st4(out_rp + 12 * r + 4, c1);
+        st4(out_rp + 12 * r + 8, c2);
+        st4(out_ch + 4 * r, alpha);
+        rs.seq = ++ctx->sig_seq;
+        {
+            KTimer t(ctx, KC_ROUND);
+            if (len == nl)
+                launch_fold_round_m31(A32, B32, len, alpha, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), rs, s);
+            else
+                launch_fold_round_qm31(ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), len, alpha, rs, s);
+        }
+        ZK_CUDA(cudaGetLastError());
+        ctx->launches++;
+        len /= 2;
+        if (len <= gather_local || len < 4) break;
+    }
+    // The local sums of the fold just launched are not needed: the gathered
+    // vectors' first round recomputes them globally.
+    if ((rc = wait_signal(ctx, rs.seq, words, 12))) return rc;
+    if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "prove_product_sharded"))) return rc;
+    const size_t glen = len * G;
+    std::vector<uint32_t> la(len * 8), all(glen * 8), ga(glen * 4), gb(glen * 4);
+    ZK_CUDA(cudaMemcpyAsync(la.data(), ctx->fa.ptr, len * 16, cudaMemcpyDeviceToHost, s));
+    ZK_CUDA(cudaMemcpyAsync(la.data() + len * 4, ctx->fb.ptr, len * 16, cudaMemcpyDeviceToHost, s));
+    ZK_CUDA(cudaStreamSynchronize(s));
+    if ((rc = ex->allgather(ex->user, la.data(), all.data(), len * 32))) return rc;
+    for (size_t g = 0; g < G; g++) {
+        const uint32_t* src = all.data() + g * len * 8;
+        for (size_t j = 0; j < len; j++) {
+            memcpy(&ga[(j * G + g) * 4], src + 4 * j, 16);
+            memcpy(&gb[(j * G + g) * 4], src + len * 4 + 4 * j, 16);
+        }
+    }
+    if ((rc = ctx->fa.ensure(glen * 16)) || (rc = ctx->fb.ensure(glen * 16))) return rc;
+    ZK_CUDA(cudaMemcpyAsync(ctx->fa.ptr, ga.data(), glen * 16, cudaMemcpyHostToDevice, s));
+    ZK_CUDA(cudaMemcpyAsync(ctx->fb.ptr, gb.data(), glen * 16, cudaMemcpyHostToDevice, s));
+    if (out_gathered_at) *out_gathered_at = glen;
+    const unsigned done = r + 1;
+    return run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, glen, chs, out_rp + 12 * done,
+                        out_ch + 4 * done, out_final_a, out_final_b, nullptr);
 }
 
 // Queues one look-ahead round kernel that waits for a challenge nobody posts and

@@ -113,6 +113,10 @@ _SIGS = {
     "zkml_sumcheck_export": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "zkml_sumcheck_finalize": (C.c_int, [C.c_void_p, _u32, _u32, _u32]),
     "zkml_selftest_wait_timeout": (C.c_int, [C.c_void_p, _u32]),
+    "zkml_shm_exchange_open": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p]),
+    "zkml_shm_exchange_close": (C.c_int, [C.c_void_p]),
+    "zkml_prove_product_sharded": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p,
+                                             C.c_void_p, _u32, _u32, _u32, _u32, C.POINTER(C.c_size_t)]),
     "zkml_prove_gkr_matmul": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                         C.c_void_p, C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t), _u64,
                                         _u64]),

@@ -28,6 +28,107 @@ import numpy as np
 
 from . import (M31_P as P, PoseidonChannel, RoundPoly, Context, _Buf, _check, context, lib)
 
+ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_uint64), C.c_int)
+ALLGATHER_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t)
+
+
+class ExchangeStruct(C.Structure):
+    """`zkml_exchange` of the C ABI."""
+    _fields_ = [("user", C.c_void_p), ("allreduce_u64", ALLREDUCE_FN), ("allgather", ALLGATHER_FN),
+                ("world", C.c_int), ("rank", C.c_int)]
+
+
+class ShmExchange:
+    """The library's shared-memory exchange between the ranks (processes) of one node."""
+
+    def __init__(self, name: str, world: int, rank: int, max_gather_bytes: int = 64 << 20):
+        self.struct = ExchangeStruct()
+        _check(lib().zkml_shm_exchange_open(name.encode(), world, rank, max_gather_bytes, C.byref(self.struct)))
+        self.world, self.rank = world, rank
+
+    def allreduce(self, words) -> np.ndarray:
+        buf = np.ascontiguousarray(words, np.uint64).copy()
+        _check(self.struct.allreduce_u64(self.struct.user, buf.ctypes.data_as(C.POINTER(C.c_uint64)), len(buf)))
+        return buf
+
+    def allgather(self, local: np.ndarray) -> np.ndarray:
+        local = np.ascontiguousarray(local)
+        out = np.empty((self.world,) + local.shape, local.dtype)
+        _check(self.struct.allgather(self.struct.user, local.ctypes.data_as(C.c_void_p),
+                                     out.ctypes.data_as(C.c_void_p), local.nbytes))
+        return out
+
+    def close(self) -> None:
+        if self.struct.user:
+            lib().zkml_shm_exchange_close(C.byref(self.struct))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class TorchExchange:
+    """A zkml_exchange whose two collectives are torch.distributed calls (NCCL or gloo)."""
+
+    def __init__(self, group=None):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist, self.group = torch, dist, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = (torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl"
+                       else torch.device("cpu"))
+
+        def allreduce(_user, words, n):
+            try:
+                arr = np.ctypeslib.as_array(words, shape=(n,))
+                t = torch.from_numpy(arr.astype(np.int64)).to(self.device)
+                dist.all_reduce(t, group=self.group)
+                arr[:] = t.cpu().numpy().astype(np.uint64)
+                return 0
+            except Exception:
+                return 4
+
+        def allgather(_user, local, out, nbytes):
+            try:
+                src = np.ctypeslib.as_array(C.cast(local, C.POINTER(C.c_uint8)), shape=(nbytes,))
+                t = torch.from_numpy(src.copy()).to(self.device)
+                parts = [torch.empty_like(t) for _ in range(self.world)]
+                dist.all_gather(parts, t, group=self.group)
+                dst = np.ctypeslib.as_array(C.cast(out, C.POINTER(C.c_uint8)), shape=(nbytes * self.world,))
+                for r, part in enumerate(parts):
+                    dst[r * nbytes:(r + 1) * nbytes] = part.cpu().numpy()
+                return 0
+            except Exception:
+                return 4
+
+        self._fns = (ALLREDUCE_FN(allreduce), ALLGATHER_FN(allgather))  # keep alive
+        self.struct = ExchangeStruct(None, self._fns[0], self._fns[1], self.world, self.rank)
+
+    def close(self) -> None:
+        pass
+
+
+def prove_product_sharded_native(a_local, b_local, n: int, channel: PoseidonChannel, exchange,
+                                 gather_local: int = 1 << 16, ctx: Optional[Context] = None) -> "ShardedSumcheckProof":
+    """The same proof as prove_product_sharded, with the round loop inside the library
+    (zkml_prove_product_sharded); `exchange` is a ShmExchange or a TorchExchange."""
+    ctx = ctx or context()
+    ab, bb = _Buf(a_local), _Buf(b_local)
+    log_n = n.bit_length() - 1
+    rp = np.zeros((max(log_n, 1), 12), np.uint32)
+    ch = np.zeros((max(log_n, 1), 4), np.uint32)
+    fa = np.zeros(4, np.uint32)
+    fb = np.zeros(4, np.uint32)
+    gathered = C.c_size_t(0)
+    _check(lib().zkml_prove_product_sharded(ctx.handle, ab.ptr, bb.ptr, n, gather_local, C.byref(exchange.struct),
+                                            C.byref(channel.state), rp.reshape(-1), ch.reshape(-1), fa, fb,
+                                            C.byref(gathered)))
+    polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_n)]
+    return ShardedSumcheckProof(polys, ch[:log_n].copy(), fa, fb, int(gathered.value))
+
 INV2 = (P + 1) // 2
 
 

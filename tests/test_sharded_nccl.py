@@ -26,7 +26,7 @@ def _port():
     return p
 
 
-def _worker(rank, world, port, n, gather_local, out_dir):
+def _worker(rank, world, port, n, gather_local, out_dir, mode="python"):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "stwo-ml_b200")]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
@@ -40,8 +40,17 @@ def _worker(rank, world, port, n, gather_local, out_dir):
         b = uniform_m31(n, 22)
         la = torch.from_numpy(shard_of(a, rank, world).view(np.int32)).cuda()
         lb = torch.from_numpy(shard_of(b, rank, world).view(np.int32)).cuda()
-        proof = prove_product_sharded(la, lb, n, PoseidonChannel(), session=GpuSumcheckSession(device=rank),
-                                      gather_local=gather_local)
+        if mode == "python":
+            proof = prove_product_sharded(la, lb, n, PoseidonChannel(), session=GpuSumcheckSession(device=rank),
+                                          gather_local=gather_local)
+        else:
+            from zkml_b200 import context
+            from zkml_b200.distributed import ShmExchange, TorchExchange, prove_product_sharded_native
+            ex = (ShmExchange(f"zkml_nccl_t_{port}", world, rank, max_gather_bytes=32 * (n // world)) if mode == "shm"
+                  else TorchExchange())
+            proof = prove_product_sharded_native(la, lb, n, PoseidonChannel(), ex, gather_local=gather_local,
+                                                 ctx=context(rank))
+            ex.close()
         np.savez(os.path.join(out_dir, f"r{rank}.npz"), ch=proof.challenges, fa=proof.final_a, fb=proof.final_b,
                  gathered=proof.gathered_at)
     finally:
@@ -50,10 +59,12 @@ def _worker(rank, world, port, n, gather_local, out_dir):
 
 @pytest.mark.gpu
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("n,gather_local", [(1 << 20, 1 << 12), (1 << 16, 1 << 16)])
-def test_nccl_sharded_equals_single_gpu(n, gather_local, tmp_path):
+@pytest.mark.parametrize("n,gather_local,mode", [(1 << 20, 1 << 12, "python"), (1 << 16, 1 << 16, "python"),
+                                                 (1 << 20, 1 << 12, "shm"), (1 << 20, 1 << 12, "nccl"),
+                                                 (1 << 12, 1 << 16, "shm")])
+def test_nccl_sharded_equals_single_gpu(n, gather_local, mode, tmp_path):
     world = 2
-    mp.start_processes(_worker, args=(world, _port(), n, gather_local, str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _port(), n, gather_local, str(tmp_path), mode), nprocs=world, join=True,
                        start_method="spawn")
     sys.path[:0] = [str(ROOT / "stwo-ml_b200"), str(ROOT / "tests")]
     import zkml_b200 as Z

@@ -53,6 +53,53 @@ def _worker(rank, world, port, n, gather_local, use_gpu, out_dir):
         dist.destroy_process_group()
 
 
+def _native_worker(rank, world, name, n, gather_local, out_dir):
+    sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "stwo-ml_b200")]
+    from zkml_b200 import PoseidonChannel
+    from zkml_b200.distributed import ShmExchange, prove_product_sharded_native, shard_of
+    ex = ShmExchange(name, world, rank, max_gather_bytes=max(1 << 16, 32 * (n // world)))
+    try:
+        a = uniform_m31(n, 11)
+        b = uniform_m31(n, 12)
+        proof = prove_product_sharded_native(shard_of(a, rank, world), shard_of(b, rank, world), n, PoseidonChannel(),
+                                             ex, gather_local=gather_local)
+        rp = np.stack([np.concatenate([p.c0, p.c1, p.c2]) for p in proof.round_polys])
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), rp=rp, ch=proof.challenges, fa=proof.final_a,
+                 fb=proof.final_b, gathered=proof.gathered_at)
+    finally:
+        ex.close()
+
+
+def _check_against_oracle(world, n, tmp_path):
+    a = uniform_m31(n, 11)
+    b = uniform_m31(n, 12)
+    ref = oracle_lib.reduce_matmul_layer(a.reshape(1, n), b.reshape(n, 1), np.zeros((0, 4), np.uint32),
+                                         np.zeros((0, 4), np.uint32), oracle_lib.new_channel(), mode=0, nthreads=4)
+    gathered = []
+    for r in range(world):
+        got = np.load(tmp_path / f"r{r}.npz")
+        np.testing.assert_array_equal(got["rp"], ref["round_polys"])
+        np.testing.assert_array_equal(got["ch"], ref["challenges"])
+        np.testing.assert_array_equal(got["fa"], ref["final_a"])
+        np.testing.assert_array_equal(got["fb"], ref["final_b"])
+        gathered.append(int(got["gathered"]))
+    return gathered
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,n,gather_local", [(2, 1 << 16, 1 << 8), (2, 1 << 12, 2), (4, 1 << 14, 1 << 6),
+                                                  (2, 1 << 6, 1 << 16)])
+def test_native_sharded_matches_oracle_gpu(world, n, gather_local, tmp_path):
+    """The library's round loop (zkml_prove_product_sharded) with the shared-memory exchange, ranks on one GPU."""
+    import uuid
+    name = "zkml_t_" + uuid.uuid4().hex[:12]
+    mp.start_processes(_native_worker, args=(world, name, n, gather_local, str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    gathered = _check_against_oracle(world, n, tmp_path)
+    if n // world > max(gather_local, 2):
+        assert gathered[0] < n
+
+
 def _run(world, n, gather_local, use_gpu, tmp_path):
     mp.start_processes(_worker, args=(world, _free_port(), n, gather_local, use_gpu, str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")

@@ -325,7 +325,7 @@ def run_product(args):
     ctx.set_stream(stream.cuda_stream)
     from zkml_b200.distributed import ShmExchange, prove_product_sharded_native
     port = os.environ.get("MASTER_PORT", "0")
-    ex = ShmExchange(f"zkml_bench_{port}_{world}", world, rank, max_gather_bytes=32 << 16)
+    ex = ShmExchange(f"zkml_bench_{port}_{world}", world, rank, max_gather_bytes=32 << 17)
     n = 1 << args.log_n
     n_loc = n // world
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)
@@ -333,7 +333,7 @@ def run_product(args):
     b = torch.randint(0, 2**31 - 1, (n_loc,), dtype=torch.int32, device="cuda", generator=g)
 
     def step():  # the library's round loop; round words and the final gather go through shared memory
-        return prove_product_sharded_native(a, b, n, Z.PoseidonChannel(), ex, gather_local=1 << 16, ctx=ctx)
+        return prove_product_sharded_native(a, b, n, Z.PoseidonChannel(), ex, ctx=ctx)
 
     for _ in range(args.warmup):
         step()

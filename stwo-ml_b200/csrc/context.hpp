@@ -90,7 +90,10 @@ struct zkml_ctx {
     zk::DevBuf partials;            // per-block round partials
     zk::DevBuf small;               // ticket + out words + error flag
     zk::DevBuf act_tables[6];
-    zk::DevBuf rc_table;            // byte-plane eq table of the tensor-pipe column restriction
+    zk::DevBuf rc_table;
+    zk::DevBuf gather_dev;          // gathered shards of the sharded product sumcheck
+    uint8_t* h_stage = nullptr;     // pinned host staging for the sharded gather
+    size_t h_stage_bytes = 0;            // byte-plane eq table of the tensor-pipe column restriction
     // stepwise product-sumcheck session (zkml_sumcheck_*)
     zk::DevBuf sc_a, sc_b;          // staged M31 inputs
     const uint32_t* sc_a32 = nullptr;

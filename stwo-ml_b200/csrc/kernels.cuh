@@ -93,6 +93,9 @@ constexpr size_t LA_TAIL_MAX = 2048;
 int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0, bool wait0, qm31 alpha0,
                           uint32_t* sig, uint32_t seq_base, const uint32_t* msg, uint32_t tag_base, int slots,
                           uint32_t* status, cudaStream_t s);
+// Rank-major gathered shards [g][A: len | B: len] -> fa, fb in global order
+// (global[j * G + g] = local_g[j]).
+void launch_interleave_gather(const uint4* in, size_t len, size_t G, uint4* fa, uint4* fb, cudaStream_t s);
 // Final fold of length-2 vectors to one value each: out[0..4) = a, out[4..8) = b.
 // src_m31 selects M31 inputs (A32, B32) instead of QM31 (A, B).
 void launch_final_fold(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,

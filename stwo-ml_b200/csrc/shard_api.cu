@@ -9,6 +9,9 @@
 // global round sums: the only exchange per round is those 12 words.  Below a
 // size threshold the caller gathers the local vectors (zkml_sumcheck_export)
 // and continues on one GPU (zkml_sumcheck_load_qm31).
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -209,6 +212,14 @@ int zkml_prove_product_sharded(zkml_ctx* ctx, const uint32_t* a_local, const uin
         return run_sumcheck(ctx, nullptr, nullptr, ctx->sc_a.as<uint32_t>(), ctx->sc_b.as<uint32_t>(), n, chs, out_rp,
                             out_ch, out_final_a, out_final_b, nullptr);
     }
+    // ZKML_SHARD_TRACE=1 prints the phase times of each call to stderr.
+    static const bool trace = getenv("ZKML_SHARD_TRACE") && getenv("ZKML_SHARD_TRACE")[0] == '1';
+    const auto t_start = std::chrono::steady_clock::now();
+    double t_wait = 0, t_ex = 0, t_hash = 0;
+    auto now = [] { return std::chrono::steady_clock::now(); };
+    auto us = [](std::chrono::steady_clock::time_point a, std::chrono::steady_clock::time_point b) {
+        return std::chrono::duration<double, std::micro>(b - a).count();
+    };
     // Split phase: round 0 over the local M31 elements, then fused fold + round per challenge.
     const void *A = nullptr, *B = nullptr;
     if ((rc = device_view(ctx, a_local, nl * 4, ctx->sc_a, &A)) || (rc = device_view(ctx, b_local, nl * 4, ctx->sc_b, &B)))
@@ -231,16 +242,22 @@ int zkml_prove_product_sharded(zkml_ctx* ctx, const uint32_t* a_local, const uin
     unsigned r = 0;
     uint32_t words[12];
     for (;; r++) {
+        auto t0 = now();
         if ((rc = wait_signal(ctx, rs.seq, words, 12))) return rc;
+        auto t1 = now();
         uint64_t w64[12];
         for (int i = 0; i < 12; i++) w64[i] = words[i];
         if ((rc = ex->allreduce_u64(ex->user, w64, 12))) return rc;
+        auto t2 = now();
+        t_wait += us(t0, t1);
+        t_ex += us(t1, t2);
         uint32_t s12[12];
         for (int i = 0; i < 12; i++) s12[i] = (uint32_t)(w64[i] % P);
         qm31 c0, c1, c2, alpha;
         round_coeffs(s12, c0, c1, c2);
         ch.mix_poly_coeffs(c0, c1, c2);
         alpha = ch.draw_qm31();
+        t_hash += us(t2, now());
         st4(out_rp + 12 * r, c0);
         st4(out_rp + 12 * r + 4, c1);
         st4(out_rp + 12 * r + 8, c2);
@@ -263,25 +280,38 @@ int zkml_prove_product_sharded(zkml_ctx* ctx, const uint32_t* a_local, const uin
     if ((rc = wait_signal(ctx, rs.seq, words, 12))) return rc;
     if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "prove_product_sharded"))) return rc;
     const size_t glen = len * G;
-    std::vector<uint32_t> la(len * 8), all(glen * 8), ga(glen * 4), gb(glen * 4);
-    ZK_CUDA(cudaMemcpyAsync(la.data(), ctx->fa.ptr, len * 16, cudaMemcpyDeviceToHost, s));
-    ZK_CUDA(cudaMemcpyAsync(la.data() + len * 4, ctx->fb.ptr, len * 16, cudaMemcpyDeviceToHost, s));
-    ZK_CUDA(cudaStreamSynchronize(s));
-    if ((rc = ex->allgather(ex->user, la.data(), all.data(), len * 32))) return rc;
-    for (size_t g = 0; g < G; g++) {
-        const uint32_t* src = all.data() + g * len * 8;
-        for (size_t j = 0; j < len; j++) {
-            memcpy(&ga[(j * G + g) * 4], src + 4 * j, 16);
-            memcpy(&gb[(j * G + g) * 4], src + len * 4 + 4 * j, 16);
-        }
+    const size_t local_bytes = len * 32, need = local_bytes * (1 + G);
+    if (ctx->h_stage_bytes < need) {
+        if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
+        ctx->h_stage = nullptr;
+        ctx->h_stage_bytes = 0;
+        ZK_CUDA(cudaMallocHost(&ctx->h_stage, need));
+        ctx->h_stage_bytes = need;
     }
-    if ((rc = ctx->fa.ensure(glen * 16)) || (rc = ctx->fb.ensure(glen * 16))) return rc;
-    ZK_CUDA(cudaMemcpyAsync(ctx->fa.ptr, ga.data(), glen * 16, cudaMemcpyHostToDevice, s));
-    ZK_CUDA(cudaMemcpyAsync(ctx->fb.ptr, gb.data(), glen * 16, cudaMemcpyHostToDevice, s));
+    uint8_t* hl = ctx->h_stage;                // this rank: A part then B part
+    uint8_t* hall = ctx->h_stage + local_bytes;  // every rank, rank-major
+    ZK_CUDA(cudaMemcpyAsync(hl, ctx->fa.ptr, len * 16, cudaMemcpyDeviceToHost, s));
+    ZK_CUDA(cudaMemcpyAsync(hl + len * 16, ctx->fb.ptr, len * 16, cudaMemcpyDeviceToHost, s));
+    ZK_CUDA(cudaStreamSynchronize(s));
+    if ((rc = ex->allgather(ex->user, hl, hall, local_bytes))) return rc;
+    if ((rc = ctx->gather_dev.ensure(G * local_bytes)) || (rc = ctx->fa.ensure(glen * 16)) ||
+        (rc = ctx->fb.ensure(glen * 16)))
+        return rc;
+    ZK_CUDA(cudaMemcpyAsync(ctx->gather_dev.ptr, hall, G * local_bytes, cudaMemcpyHostToDevice, s));
+    launch_interleave_gather(ctx->gather_dev.as<uint4>(), len, G, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), s);
+    ZK_CUDA(cudaGetLastError());
+    ctx->launches++;
     if (out_gathered_at) *out_gathered_at = glen;
     const unsigned done = r + 1;
-    return run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, glen, chs, out_rp + 12 * done,
-                        out_ch + 4 * done, out_final_a, out_final_b, nullptr);
+    const auto t_gather = now();
+    rc = run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, glen, chs, out_rp + 12 * done,
+                      out_ch + 4 * done, out_final_a, out_final_b, nullptr);
+    if (trace)
+        fprintf(stderr,
+                "[zkml shard rank %d] split rounds %u: gpu wait %.1f us, exchange %.1f us, transcript %.1f us; "
+                "until gather end %.1f us; gathered tail (%zu) %.1f us\n",
+                ex->rank, done, t_wait, t_ex, t_hash, us(t_start, t_gather), glen, us(t_gather, now()));
+    return rc;
 }
 
 // Queues one look-ahead round kernel that waits for a challenge nobody posts and

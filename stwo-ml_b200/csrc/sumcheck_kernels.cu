@@ -1148,6 +1148,25 @@ int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0,
     return 0;
 }
 
+// Gathered shards (rank-major: rank g's A part then B part, `len` elements each)
+// -> global order, global[j * G + g] = local_g[j].
+__global__ void interleave_gather_kernel(const uint4* __restrict__ in, size_t len, size_t G, uint4* __restrict__ fa,
+                                        uint4* __restrict__ fb) {
+    const size_t glen = len * G;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < glen; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t j = i / G, g = i % G;
+        fa[i] = in[g * 2 * len + j];
+        fb[i] = in[g * 2 * len + len + j];
+    }
+}
+
+void launch_interleave_gather(const uint4* in, size_t len, size_t G, uint4* fa, uint4* fb, cudaStream_t s) {
+    size_t blocks = (len * G + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    if (blocks == 0) blocks = 1;
+    interleave_gather_kernel<<<(unsigned)blocks, 256, 0, s>>>(in, len, G, fa, fb);
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 static unsigned round_blocks(size_t work, int max_blocks) {

@@ -168,6 +168,23 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def bind_to_gpu_cpus(dev):
+    """Pin this rank's process to the CPUs NVML reports as local to its GPU: the round loop
+    spins on mapped host memory and its pinned buffers are allocated near the running CPU."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(dev)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, 16)
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:
+        return None
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -183,6 +200,7 @@ def run_b200(args):
     else:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
+    bind_to_gpu_cpus(dev)
     stream = torch.cuda.current_stream()
     ctx = Z.Context(dev)
     ctx.set_stream(stream.cuda_stream)
@@ -232,17 +250,22 @@ def run_b200(args):
         kt = ctx.kernel_time("restrict_cols") if profile else (0.0, 0)
         if profile:
             ctx.enable_timing(False)
+        rank_ms = [ms]
         if world > 1:
             t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
+            parts = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            rank_ms = [float(p.item()) for p in parts]
+            ms = max(rank_ms)
             lt = torch.tensor([launches], device="cuda", dtype=torch.int64)
             dist.all_reduce(lt)
             launches = int(lt.item())
         barrier()
+        timed.rank_ms = rank_ms
         return ms, launches, kt, clk.summary()
 
     ms, launches, (rc_ms, rc_n), clocks = timed(A_dev, B_dev, profile=True)
+    rank_ms = timed.rank_ms
     ms_e2e, _, _, _ = timed(A_host, B_host, profile=False)
 
     # CPU baseline: rank 0 at N=1 only, one full layer through the oracle
@@ -272,6 +295,7 @@ def run_b200(args):
         "data": "synthetic (SplitMix64-seeded int8 embedded in M31)",
         "config": {"workload": WORKLOAD, "m": M, "k": K, "n": N, "padded": [PM, PK, PN],
                    "layers_per_step": world, "parallelism": f"independent layer per GPU x{world}",
+                   "ms_per_step_by_rank": [round(x, 4) for x in rank_ms],
                    "l2": "inputs larger than L2 (B = 283 MB > 126 MB L2)"},
         "e2e": {"value": ms_e2e / 1e3 / world, "unit": "s/layer",
                 "h2d_bytes_per_step": 4 * (M * K + K * N),

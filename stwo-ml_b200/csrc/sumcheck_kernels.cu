@@ -41,31 +41,70 @@ __device__ __forceinline__ unsigned long long lazy2(unsigned long long x) {
 // ---------------------------------------------------------------------------
 // eq table
 // ---------------------------------------------------------------------------
-__global__ void eq_table_kernel(EqChallenges ch, uint4* __restrict__ table, size_t len) {
-    const size_t n = (size_t)1 << ch.v;
-    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < len;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        qm31 w = qzero();
-        if (idx < n) {
-            w = qone();
-            for (int l = 0; l < ch.v; l++) {
-                const int bit = (idx >> (ch.v - 1 - l)) & 1;
+// eq(idx, c) = prod_l (bit_l ? c_l : 1 - c_l), variable l on bit v - 1 - l (MSB first).
+// The product is split at k = min(v, 10) low bits: a block builds the 2^k-entry
+// table of the low variables in shared memory once (by doubling, one product per
+// entry; the product order only regroups field multiplications), then for each high prefix
+// h (one QM31 product chain of v - k factors, by one thread) writes the 2^k
+// entries h * 2^k + t as one product each.  Entries in [2^v, len) are zero.
+constexpr int EQ_LO_MAX = 10;
+
+__global__ void __launch_bounds__(256) eq_table_kernel(EqChallenges ch, uint4* __restrict__ table, size_t len) {
+    __shared__ uint4 buf[2][1 << EQ_LO_MAX];
+    __shared__ uint4 hi_s;
+    const int v = ch.v, k = v < EQ_LO_MAX ? v : EQ_LO_MAX;
+    const size_t n = (size_t)1 << v, nlo = (size_t)1 << k, nh = n >> k;
+    // low table by doubling, most significant low variable first: one product per entry
+    if (threadIdx.x == 0) st_q(&buf[0][0], qone());
+    int cur = 0;
+    for (int j = 0; j < k; j++) {
+        __syncthreads();
+        const qm31 c = ch.c[v - k + j], c1 = qsub(qone(), c);
+        const size_t sz = (size_t)1 << j;
+        for (size_t e = threadIdx.x; e < sz; e += blockDim.x) {
+            const qm31 w = ld_q(&buf[cur][e]);
+            st_q(&buf[cur ^ 1][2 * e], qmul(w, c1));
+            st_q(&buf[cur ^ 1][2 * e + 1], qmul(w, c));
+        }
+        cur ^= 1;
+    }
+    const uint4* lo = buf[cur];
+    for (size_t h = blockIdx.x; h < nh; h += gridDim.x) {
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            qm31 w = qone();
+            for (int l = 0; l < v - k; l++) {
+                const int bit = (int)((h >> (v - k - 1 - l)) & 1);
                 w = qmul(w, bit ? ch.c[l] : qsub(qone(), ch.c[l]));
             }
+            st_q(&hi_s, w);
         }
-        st_q(table + idx, w);
+        __syncthreads();
+        const qm31 hv = ld_q(&hi_s);
+        for (size_t t = threadIdx.x; t < nlo; t += blockDim.x) {
+            const size_t idx = h * nlo + t;
+            if (idx < len) st_q(table + idx, qmul(hv, ld_q(lo + t)));
+        }
     }
+    for (size_t idx = n + blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < len;
+         idx += (size_t)gridDim.x * blockDim.x)
+        st_q(table + idx, qzero());
 }
 
 void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaStream_t s) {
     EqChallenges ch;
     ch.v = v;
     for (int i = 0; i < v; i++) ch.c[i] = c[i];
-    const int threads = 256;
-    size_t blocks = (table_len + threads - 1) / threads;
-    if (blocks > 4096) blocks = 4096;
+    const int k = v < EQ_LO_MAX ? v : EQ_LO_MAX;
+    size_t blocks = ((size_t)1 << v) >> k;  // high prefixes; each block loops over several
+    if (blocks > 296) blocks = 296;
+    if (table_len > ((size_t)1 << v)) {
+        const size_t tail = (table_len - ((size_t)1 << v) + 255) / 256;
+        if (tail > blocks) blocks = tail;
+    }
+    if (blocks > 2048) blocks = 2048;
     if (blocks == 0) blocks = 1;
-    eq_table_kernel<<<(unsigned)blocks, threads, 0, s>>>(ch, table, table_len);
+    eq_table_kernel<<<(unsigned)blocks, 256, 0, s>>>(ch, table, table_len);
 }
 
 // ---------------------------------------------------------------------------

@@ -594,9 +594,17 @@ def activation_table(tag: int) -> np.ndarray:
 
 @dataclass
 class ActivationLogUpProof:
-    calldata: List[int]     # LayerProof::Activation record (serialize_gkr_model_proof)
-    input_eval: np.ndarray  # next claim value
+    """LayerProof::Activation record (serialize_gkr_model_proof).  `raw` holds the calldata as
+    4 x u64 limbs per felt; `calldata` converts it to Python integers on first use (the record
+    carries the 2^16 table multiplicities, so the conversion costs far more than the proof)."""
     raw: np.ndarray
+    input_eval: np.ndarray  # next claim value
+
+    @property
+    def calldata(self) -> List[int]:
+        if not hasattr(self, "_calldata"):
+            self._calldata = _felts(self.raw, self.raw.size // 4)
+        return self._calldata
 
 
 def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_type: int,
@@ -613,7 +621,7 @@ def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_t
     _check(lib().zkml_reduce_activation_logup(context(device).handle, buf.ptr, inp.rows, inp.cols, activation_type,
                                               pt_ptr, n_point, np.ascontiguousarray(output_claim.value, np.uint32),
                                               C.byref(channel.state), out, cap, C.byref(ln), ie))
-    proof = ActivationLogUpProof(_felts(out, ln.value), ie, out[:4 * ln.value].copy())
+    proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
     return proof, GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
 
 

@@ -76,6 +76,25 @@ struct KTimer {
 
 }  // namespace zk
 
+namespace zk {
+// Device scratch of the LogUp activation reduction, kept by the context (grown on demand).
+struct LogupScratch {
+    DevBuf x, m_in, m_out, mult, eq, d, w, mv;
+    void release() {
+        DevBuf* all[] = {&x, &m_in, &m_out, &mult, &eq, &d, &w, &mv};
+        for (DevBuf* b : all) b->release();
+    }
+};
+// Device scratch of the Merkle commitment and the MLE opening (grown on demand).
+struct OpeningScratch {
+    DevBuf layers, trees, idx, gathered, qvals, nodes, cbuf, bmle;
+    void release() {
+        DevBuf* all[] = {&layers, &trees, &idx, &gathered, &qvals, &nodes, &cbuf, &bmle};
+        for (DevBuf* b : all) b->release();
+    }
+};
+}  // namespace zk
+
 struct zkml_ctx {
     int device = 0;
     int num_sms = 148;
@@ -91,6 +110,8 @@ struct zkml_ctx {
     zk::DevBuf small;               // ticket + out words + error flag
     zk::DevBuf act_tables[6];
     zk::DevBuf rc_table;
+    zk::LogupScratch lu;
+    zk::OpeningScratch op;  // kept across calls: cudaMalloc/cudaFree would synchronise the device each call
     zk::DevBuf gather_dev;          // gathered shards of the sharded product sumcheck
     uint8_t* h_stage = nullptr;     // pinned host staging for the sharded gather
     size_t h_stage_bytes = 0;            // byte-plane eq table of the tensor-pipe column restriction

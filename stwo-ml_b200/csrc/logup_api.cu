@@ -54,14 +54,6 @@ struct Out {
     }
 };
 
-struct LogupBufs {
-    DevBuf x, m_in, m_out, mult, eq, d, w, mv;
-    ~LogupBufs() {
-        DevBuf* all[] = {&x, &m_in, &m_out, &mult, &eq, &d, &w, &mv};
-        for (DevBuf* b : all) b->release();
-    }
-};
-
 }  // namespace
 }  // namespace zk
 
@@ -95,7 +87,7 @@ extern "C" int zkml_reduce_activation_logup(zkml_ctx* ctx, const uint32_t* input
         if ((rc = tbuf.ensure(tsize * 4))) return rc;
         ZK_CUDA(cudaMemcpy(tbuf.ptr, t.data(), tsize * 4, cudaMemcpyHostToDevice));
     }
-    LogupBufs b;
+    LogupScratch& b = ctx->lu;  // kept across calls: allocation would synchronise the device every call
     if ((rc = b.x.ensure(n * 4)) || (rc = b.m_in.ensure(n * 4)) || (rc = b.m_out.ensure(n * 4)) ||
         (rc = b.mult.ensure(tsize * 4)) || (rc = b.eq.ensure(n * 16)) || (rc = b.d.ensure(n * 16)) ||
         (rc = b.w.ensure(n * 16)) || (rc = b.mv.ensure(tsize / 2 * 16)))

@@ -78,18 +78,6 @@ struct FeltOut {
     }
 };
 
-// Device buffers owned by one opening proof (released on return).
-struct OpeningBufs {
-    DevBuf layers, trees, idx, gathered, qvals;
-    ~OpeningBufs() {
-        layers.release();
-        trees.release();
-        idx.release();
-        gathered.release();
-        qvals.release();
-    }
-};
-
 // Proves the opening of the MLE `evals` (device, 2^n_vars QM31) at `point`,
 // appending the serialized MleOpeningProof to `out`.  Advances `chs`.
 int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const qm31* point, zkml_channel* chs,
@@ -97,7 +85,7 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
     Channel ch(chs);
     cudaStream_t s = ctx->stream;
     const size_t N = (size_t)1 << n_vars;
-    OpeningBufs ob;
+    OpeningScratch& ob = ctx->op;
     int rc;
     // layer r (r >= 1) of size N >> r lives at offset N - (N >> (r - 1)) in `layers`.
     if ((rc = ob.layers.ensure(N * 16))) return rc;
@@ -248,7 +236,7 @@ int zkml_commit_mle_root(zkml_ctx* ctx, const uint32_t* evals, size_t n, uint64_
     const void* E = nullptr;
     int rc = dev_view(ctx, evals, n * 16, ctx->a_in, &E);
     if (rc) return rc;
-    DevBuf nodes;
+    DevBuf& nodes = ctx->op.nodes;
     if ((rc = nodes.ensure(merkle_node_count(n) * 32))) return rc;
     {
         KTimer t(ctx, KC_MERKLE);
@@ -259,7 +247,6 @@ int zkml_commit_mle_root(zkml_ctx* ctx, const uint32_t* evals, size_t n, uint64_
     cudaError_t e = cudaMemcpyAsync(root, nodes.as<char>() + 32 * (merkle_node_count(n) - 1), 32,
                                     cudaMemcpyDeviceToHost, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
-    nodes.release();
     if (e != cudaSuccess) return cuda_error(e, "commit_mle_root");
     mont_to_canon(root, out_root);
     return ZKML_OK;
@@ -340,7 +327,8 @@ int zkml_prove_gkr_matmul(zkml_ctx* ctx, const uint32_t* input, size_t m, size_t
     std::vector<qm31> r_out(log_m + log_n + 1);
     for (unsigned i = 0; i < log_m + log_n; i++) r_out[i] = ch.draw_qm31();
     // output matrix for the IO commitment (forward pass on the GPU)
-    DevBuf cbuf, bmle;
+    DevBuf& cbuf = ctx->op.cbuf;
+    DevBuf& bmle = ctx->op.bmle;
     if ((rc = cbuf.ensure(m * n * 4))) return rc;
     launch_m31_gemm(A, B, cbuf.as<uint32_t>(), (uint32_t)m, (uint32_t)k, (uint32_t)n, s);
     ctx->launches++;
@@ -412,7 +400,6 @@ int zkml_prove_gkr_matmul(zkml_ctx* ctx, const uint32_t* input, size_t m, size_t
         KTimer t(ctx, KC_MERKLE);
         rc = prove_opening_dev(ctx, bmle.as<uint4>(), nv, wpt.data(), &chs, n_queries, commitment, opening, nullptr);
     }
-    bmle.release();
     if (rc) return rc;
     out.u64(1);  // weight commitments
     out.push(commitment);
@@ -426,7 +413,6 @@ int zkml_prove_gkr_matmul(zkml_ctx* ctx, const uint32_t* input, size_t m, size_t
     for (size_t i = 0; i < opening.len; i++) out.push(&obuf[4 * i]);
     // IO commitment (aggregation.rs:235-254)
     ZK_CUDA(cudaStreamSynchronize(s));
-    cbuf.release();
     std::vector<uint32_t> in_host(m * k);
     ZK_CUDA(cudaMemcpy(in_host.data(), A, m * k * 4, cudaMemcpyDeviceToHost));
     zkml_io_commitment(in_host.data(), m, k, out_host.data(), m, n, out_io);

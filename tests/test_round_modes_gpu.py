@@ -39,7 +39,8 @@ def check(a, b, r_i, r_j):
 for lg in (1, 2, 5, 11, 12, 17):
     n = 1 << lg
     check(uniform_m31(n, lg).reshape(1, n), uniform_m31(n, lg + 50).reshape(n, 1), np.zeros((0, 4), np.uint32), np.zeros((0, 4), np.uint32))
-for (m, k, n) in ((4, 96, 80), (8, 3000, 64), (2, 8192, 16), (3, 37, 1028), (16, 300, 2052), (5, 17, 6)):
+for (m, k, n) in ((4, 96, 80), (8, 3000, 64), (2, 8192, 16), (3, 37, 1028), (16, 300, 2052), (5, 17, 6),
+                  (2, 33, 4100), (4, 1000, 3072)):
     a = int_matrix_m31(m, k, 1)
     b = int_matrix_m31(k, n, 2)
     lm = (m - 1).bit_length()
@@ -54,6 +55,7 @@ MODES = {
     "unqueued": {"ZKML_LA_QUEUE": "0"},
     "plain_rounds": {"ZKML_LOOKAHEAD_MAX": "0"},
     "generic_restriction": {"ZKML_RESTRICT_TC": "0"},
+    "tensor_restriction_register_loads": {"ZKML_RESTRICT_TC": "1"},
 }
 
 

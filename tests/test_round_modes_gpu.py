@@ -55,7 +55,6 @@ MODES = {
     "unqueued": {"ZKML_LA_QUEUE": "0"},
     "plain_rounds": {"ZKML_LOOKAHEAD_MAX": "0"},
     "generic_restriction": {"ZKML_RESTRICT_TC": "0"},
-    "tensor_restriction_register_loads": {"ZKML_RESTRICT_TC": "1"},
 }
 
 

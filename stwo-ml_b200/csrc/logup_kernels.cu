@@ -4,6 +4,7 @@
 // LogUp sums, eq-weighted dot products, and the degree-3 eq-sumcheck rounds
 // (s(t) = sum eq_t w_t d_t at t = 0..3) with the fold of eq, w and d fused in.
 #include "logup.cuh"
+#include "round_arith.cuh"
 
 namespace zk {
 
@@ -100,7 +101,10 @@ __global__ void logup_prepare_kernel(const uint32_t* __restrict__ input, uint32_
         x_out[idx] = x;
         m_in[idx] = mi;
         m_out[idx] = __ldg(table + mi);
-        atomicAdd(mult + mi, 1u);
+        // lanes of a warp that hit the same table entry add once (inputs cluster on few entries)
+        const unsigned active = __activemask();
+        const unsigned peers = __match_any_sync(active, mi);
+        if ((__ffs(peers) - 1) == (int)(threadIdx.x & 31)) atomicAdd(mult + mi, (uint32_t)__popc(peers));
     }
     if (bad & 0x80000000u) atomicOr(err, 1u);
 }
@@ -112,25 +116,73 @@ void launch_logup_prepare(const uint32_t* input, uint32_t rows, uint32_t cols, s
                                                                       m_in, m_out, mult, err);
 }
 
-// d = gamma - in - beta * out, w = 1 / d, and trace_sum = sum w  (4 words)
+// d = gamma - in - beta * out, w = 1 / d, and trace_sum = sum w  (4 words).
+// Each thread inverts its DW_BATCH elements (grid-strided, so loads stay
+// coalesced) with one QM31 inversion: prefix products, one inverse, and a
+// backward pass (three products per element).  A batch containing d = 0 is
+// inverted element by element, so the result is the same as qinv of each d.
+constexpr int DW_BATCH = 8;
+
+__device__ __forceinline__ qm31 qmul_f(const qm31& x, const qm31& y) {
+    QAcc s;
+    qacc_zero(s);
+    qacc_mul(s, x, y);
+    return qacc_value(s);
+}
+
 __global__ void __launch_bounds__(256) logup_dw_kernel(const uint32_t* __restrict__ m_in,
                                                        const uint32_t* __restrict__ m_out, size_t n, qm31 gamma,
                                                        qm31 beta, uint4* __restrict__ d, uint4* __restrict__ w,
                                                        ReduceScratch rs) {
     unsigned long long acc[4] = {0, 0, 0, 0};
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const qm31 di = qsub(qsub(gamma, qm(m_in[i], 0, 0, 0)), qmul_m(beta, m_out[i]));
-        const qm31 wi = qinv(di);
-        stq4(d + i, di);
-        stq4(w + i, wi);
-        acc_q<4>(acc, 0, wi);
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i0 < n; i0 += stride * DW_BATCH) {
+        qm31 dv[DW_BATCH], pre[DW_BATCH];
+        bool zero = false;
+        qm31 run = qone();
+#pragma unroll
+        for (int e = 0; e < DW_BATCH; e++) {
+            const size_t i = i0 + e * stride;
+            dv[e] = qone();
+            if (i < n) {
+                dv[e] = qsub(qsub(gamma, qm(m_in[i], 0, 0, 0)), qmul_m(beta, m_out[i]));
+                stq4(d + i, dv[e]);
+                zero |= (dv[e].a | dv[e].b | dv[e].c | dv[e].d) == 0;
+            }
+            pre[e] = run;  // product of dv[0..e)
+            run = qmul_f(run, dv[e]);
+        }
+        if (!zero) {
+            qm31 inv = qinv(run);  // 1 / prod dv
+#pragma unroll
+            for (int e = DW_BATCH - 1; e >= 0; e--) {
+                const size_t i = i0 + e * stride;
+                const qm31 we = qmul_f(inv, pre[e]);
+                inv = qmul_f(inv, dv[e]);
+                if (i < n) {
+                    stq4(w + i, we);
+                    acc_q<4>(acc, 0, we);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < DW_BATCH; e++) {
+                const size_t i = i0 + e * stride;
+                if (i < n) {
+                    const qm31 we = qinv(dv[e]);
+                    stq4(w + i, we);
+                    acc_q<4>(acc, 0, we);
+                }
+            }
+        }
     }
     grid_reduce<4>(acc, rs);
 }
 
 void launch_logup_dw(const uint32_t* m_in, const uint32_t* m_out, size_t n, qm31 gamma, qm31 beta, uint4* d,
                      uint4* w, const ReduceScratch& rs, cudaStream_t s) {
-    logup_dw_kernel<<<grid_for(n, rs.max_blocks), 256, 0, s>>>(m_in, m_out, n, gamma, beta, d, w, rs);
+    logup_dw_kernel<<<grid_for((n + DW_BATCH - 1) / DW_BATCH, rs.max_blocks), 256, 0, s>>>(m_in, m_out, n, gamma,
+                                                                                           beta, d, w, rs);
 }
 
 // table_sum = sum_{j : mult_j > 0} mult_j / (gamma - j - beta * table_j)  (4 words)
@@ -180,12 +232,12 @@ void launch_eq_dot(const uint4* eq, const uint32_t* x0, const uint32_t* x1, size
 // t = 0, 1, 2, 3 over pairs (i, i + q), q = h / 2 (16 words).
 template <bool FOLD>
 __global__ void __launch_bounds__(256) logup_round_kernel(uint4* __restrict__ E, uint4* __restrict__ W,
-                                                          uint4* __restrict__ D, size_t h, qm31 alpha,
+                                                          uint4* __restrict__ D, size_t h, const AlphaRows m,
                                                           ReduceScratch rs) {
     const size_t q = h / 2;
-    unsigned long long acc[16];
+    QAcc acc[4];
 #pragma unroll
-    for (int i = 0; i < 16; i++) acc[i] = 0;
+    for (int t = 0; t < 4; t++) qacc_zero(acc[t]);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
         qm31 v[3][2];  // [vector][lo/hi]
         uint4* vec[3] = {E, W, D};
@@ -194,8 +246,8 @@ __global__ void __launch_bounds__(256) logup_round_kernel(uint4* __restrict__ E,
             if (FOLD) {
                 const qm31 a0 = ldq4(vec[k] + i), a1 = ldq4(vec[k] + i + q);
                 const qm31 a2 = ldq4(vec[k] + i + h), a3 = ldq4(vec[k] + i + q + h);
-                v[k][0] = qadd(a0, qmul(alpha, qsub(a2, a0)));
-                v[k][1] = qadd(a1, qmul(alpha, qsub(a3, a1)));
+                v[k][0] = fold_qq(a0, a2, m);
+                v[k][1] = fold_qq(a1, a3, m);
                 stq4(vec[k] + i, v[k][0]);
                 stq4(vec[k] + i + q, v[k][1]);
             } else {
@@ -211,21 +263,31 @@ __global__ void __launch_bounds__(256) logup_round_kernel(uint4* __restrict__ E,
         }
 #pragma unroll
         for (int t = 0; t < 4; t++) {
-            acc_q<16>(acc, 4 * t, qmul(qmul(x[0], x[1]), x[2]));
+            qacc_mul(acc[t], qmul_f(x[0], x[1]), x[2]);
 #pragma unroll
             for (int k = 0; k < 3; k++) x[k] = qadd(x[k], dlt[k]);
         }
     }
-    grid_reduce<16>(acc, rs);
+    unsigned long long words[16];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        const qm31 r = qacc_value(acc[t]);
+        words[4 * t] = r.a;
+        words[4 * t + 1] = r.b;
+        words[4 * t + 2] = r.c;
+        words[4 * t + 3] = r.d;
+    }
+    grid_reduce<16>(words, rs);
 }
 
 void launch_logup_round(uint4* E, uint4* W, uint4* D, size_t len, bool fold, qm31 alpha, const ReduceScratch& rs,
                         cudaStream_t s) {
     if (fold) {
         const size_t h = len / 2;
-        logup_round_kernel<true><<<grid_for(h / 2, rs.max_blocks), 256, 0, s>>>(E, W, D, h, alpha, rs);
+        logup_round_kernel<true><<<grid_for(h / 2, rs.max_blocks), 256, 0, s>>>(E, W, D, h, alpha_rows(alpha), rs);
     } else {
-        logup_round_kernel<false><<<grid_for(len / 2, rs.max_blocks), 256, 0, s>>>(E, W, D, len, alpha, rs);
+        logup_round_kernel<false><<<grid_for(len / 2, rs.max_blocks), 256, 0, s>>>(E, W, D, len, alpha_rows(alpha),
+                                                                                   rs);
     }
 }
 
@@ -270,8 +332,9 @@ __global__ void __launch_bounds__(256) mult_round_kernel(const uint32_t* __restr
                 a2 = ldq4(V + i + h);
                 a3 = ldq4(V + i + q + h);
             }
-            lo = qadd(a0, qmul(alpha, qsub(a2, a0)));
-            hi = qadd(a1, qmul(alpha, qsub(a3, a1)));
+            const AlphaRows m = alpha_rows(alpha);
+            lo = fold_qq(a0, a2, m);
+            hi = fold_qq(a1, a3, m);
             stq4(V + i, lo);
             stq4(V + i + q, hi);
         } else {

@@ -48,10 +48,10 @@ __device__ __forceinline__ unsigned long long lazy2(unsigned long long x) {
 // h (one QM31 product chain of v - k factors, by one thread) writes the 2^k
 // entries h * 2^k + t as one product each.  Entries in [2^v, len) are zero.
 constexpr int EQ_LO_MAX = 10;
+constexpr int EQ_HI_BATCH = 8;
 
 __global__ void __launch_bounds__(256) eq_table_kernel(EqChallenges ch, uint4* __restrict__ table, size_t len) {
     __shared__ uint4 buf[2][1 << EQ_LO_MAX];
-    __shared__ uint4 hi_s;
     const int v = ch.v, k = v < EQ_LO_MAX ? v : EQ_LO_MAX;
     const size_t n = (size_t)1 << v, nlo = (size_t)1 << k, nh = n >> k;
     // low table by doubling, most significant low variable first: one product per entry
@@ -69,21 +69,24 @@ __global__ void __launch_bounds__(256) eq_table_kernel(EqChallenges ch, uint4* _
         cur ^= 1;
     }
     const uint4* lo = buf[cur];
-    for (size_t h = blockIdx.x; h < nh; h += gridDim.x) {
+    // high prefixes in batches of EQ_HI_BATCH, one thread per prefix
+    __shared__ uint4 hs[EQ_HI_BATCH];
+    for (size_t hb = blockIdx.x * (size_t)EQ_HI_BATCH; hb < nh; hb += (size_t)gridDim.x * EQ_HI_BATCH) {
         __syncthreads();
-        if (threadIdx.x == 0) {
+        if (threadIdx.x < EQ_HI_BATCH && hb + threadIdx.x < nh) {
+            const size_t h = hb + threadIdx.x;
             qm31 w = qone();
             for (int l = 0; l < v - k; l++) {
                 const int bit = (int)((h >> (v - k - 1 - l)) & 1);
                 w = qmul(w, bit ? ch.c[l] : qsub(qone(), ch.c[l]));
             }
-            st_q(&hi_s, w);
+            st_q(&hs[threadIdx.x], w);
         }
         __syncthreads();
-        const qm31 hv = ld_q(&hi_s);
-        for (size_t t = threadIdx.x; t < nlo; t += blockDim.x) {
-            const size_t idx = h * nlo + t;
-            if (idx < len) st_q(table + idx, qmul(hv, ld_q(lo + t)));
+        const size_t nb = nh - hb < (size_t)EQ_HI_BATCH ? nh - hb : (size_t)EQ_HI_BATCH;
+        for (size_t u = threadIdx.x; u < nb * nlo; u += blockDim.x) {
+            const size_t hh = u / nlo, t = u % nlo, idx = (hb + hh) * nlo + t;
+            if (idx < len) st_q(table + idx, qmul(ld_q(&hs[hh]), ld_q(lo + t)));
         }
     }
     for (size_t idx = n + blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < len;
@@ -96,8 +99,7 @@ void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaS
     ch.v = v;
     for (int i = 0; i < v; i++) ch.c[i] = c[i];
     const int k = v < EQ_LO_MAX ? v : EQ_LO_MAX;
-    size_t blocks = ((size_t)1 << v) >> k;  // high prefixes; each block loops over several
-    if (blocks > 296) blocks = 296;
+    size_t blocks = ((((size_t)1 << v) >> k) + EQ_HI_BATCH - 1) / EQ_HI_BATCH;  // batches of high prefixes
     if (table_len > ((size_t)1 << v)) {
         const size_t tail = (table_len - ((size_t)1 << v) + 255) / 256;
         if (tail > blocks) blocks = tail;

@@ -197,6 +197,14 @@ int zkml_reduce_activation_logup(zkml_ctx *ctx, const uint32_t *input, size_t ro
                                  zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                  uint32_t out_input_eval[4]);
 
+/* ---- Forward pass --------------------------------------------------------------
+ * C = A * B mod p for M31 matrices (m x k times k x n, row major): the forward
+ * GEMM that produces a layer's output (gpu_matmul_m31_full,
+ * engine/src/gpu_sumcheck.rs:3104-3196).  Exact, on the integer tensor pipe
+ * (byte planes, u8 MMAs) when k % 4 == 0 and A is 16-byte aligned, else on CUDA
+ * cores.  c may be host memory or device memory of the context's GPU. */
+int zkml_matmul_m31(zkml_ctx *ctx, const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n, uint32_t *c);
+
 /* ---- Stepwise product sumcheck (multi-GPU building block) -------------------
  * The round loop of ZkmlOps::reduce_matmul_layer (backend.rs:141-178) one round
  * at a time, so that a caller can split one sumcheck across GPUs: rank g of G

@@ -111,7 +111,8 @@ struct zkml_ctx {
     zk::DevBuf act_tables[6];
     zk::DevBuf rc_table;
     zk::LogupScratch lu;
-    zk::OpeningScratch op;  // kept across calls: cudaMalloc/cudaFree would synchronise the device each call
+    zk::OpeningScratch op;
+    zk::DevBuf gemm_planes;         // byte planes of the forward GEMM's right operand  // kept across calls: cudaMalloc/cudaFree would synchronise the device each call
     zk::DevBuf gather_dev;          // gathered shards of the sharded product sumcheck
     uint8_t* h_stage = nullptr;     // pinned host staging for the sharded gather
     size_t h_stage_bytes = 0;            // byte-plane eq table of the tensor-pipe column restriction

@@ -113,6 +113,8 @@ _SIGS = {
     "zkml_sumcheck_export": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "zkml_sumcheck_finalize": (C.c_int, [C.c_void_p, _u32, _u32, _u32]),
     "zkml_selftest_wait_timeout": (C.c_int, [C.c_void_p, _u32]),
+    "zkml_matmul_m31": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                                  C.c_void_p]),
     "zkml_shm_exchange_open": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p]),
     "zkml_shm_exchange_close": (C.c_int, [C.c_void_p]),
     "zkml_prove_product_sharded": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p,
@@ -491,6 +493,32 @@ def mle_n_queries() -> int:
 
 def _felts(buf: np.ndarray, n: int) -> List[int]:
     return [limbs_to_felt(buf[4 * i:4 * i + 4]) for i in range(n)]
+
+
+def matmul_m31(a, b, out=None, device: int = 0):
+    """C = A * B mod p (forward pass, gpu_matmul_m31_full).  a: (m, k), b: (k, n) M31 as numpy
+    arrays or CUDA tensors; returns a numpy (m, n) uint32 array, or writes `out` (a CUDA int32
+    tensor of m * n elements) in place."""
+    am, bm = as_matrix(a), as_matrix(b)
+    if am.cols != bm.rows:
+        raise InvalidArgument(1, "A.cols must equal B.rows")
+    ab, bb = _Buf(am.data), _Buf(bm.data)
+    if out is None:
+        res = np.zeros((am.rows, bm.cols), np.uint32)
+        _check(lib().zkml_matmul_m31(context(device).handle, ab.ptr, am.rows, am.cols, bb.ptr, bm.cols,
+                                     res.ctypes.data_as(C.c_void_p)))
+        return res
+    ob = _Buf(out)
+    _check(lib().zkml_matmul_m31(context(device).handle, ab.ptr, am.rows, am.cols, bb.ptr, bm.cols, ob.ptr))
+    return out
+
+
+def as_matrix(x) -> "M31Matrix":
+    if isinstance(x, M31Matrix):
+        return x
+    if hasattr(x, "is_cuda"):
+        return M31Matrix(int(x.shape[0]), int(x.shape[1]), x.reshape(-1))
+    return M31Matrix.from_numpy(np.asarray(x))
 
 
 def commit_mle_root(evals, device: int = 0) -> int:

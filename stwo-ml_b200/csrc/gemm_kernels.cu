@@ -6,8 +6,8 @@
 // A_a B_b, each A_a B_b an exact u8 GEMM on mma.m16n8k32.  A (m x k, row major)
 // is read as is: four consecutive k of a row are one 16-byte load whose byte
 // planes are A fragments.  B (k x n, row major) is first packed into four
-// planes of n rows x kpad bytes (K contiguous, as the B fragments want) by a
-// shared-memory transpose.  The sixteen plane pairs share seven accumulators
+// planes (in the order the B fragments are read, bp_offset) by a shared-memory
+// transpose.  The sixteen plane pairs share seven accumulators
 // by weight w = a + b (at most four pairs per weight, each below
 // 255^2 * 8192 per K chunk, so a chunk of 8192 stays below 2^31); every K
 // chunk ends with sum_w 256^w acc_w mod P added to 64-bit lazy sums.
@@ -24,12 +24,20 @@ namespace zk {
 
 constexpr uint32_t GEMM_KCHUNK = 8192;
 
-// Bp[b][j][t] = byte b of B[t][j] (t < k; zero for k <= t < kpad).
+// Packed right operand, laid out in the order the B fragments are read: for
+// column j, K step s (32 values of t) and fragment lane tg (0..3), 32 bytes =
+// for each plane b the two fragment words (t = 32 s + 4 tg + [0, 4) and
+// t = 32 s + 16 + 4 tg + [0, 4)), so a lane fetches all four planes of one K
+// step with two 16-byte loads.  Entries with t >= k are zero.
+__device__ __forceinline__ size_t bp_offset(uint32_t j, uint32_t s, uint32_t tg, uint32_t ksteps) {
+    return (((size_t)j * ksteps + s) * 4 + tg) * 32;
+}
+
 __global__ void __launch_bounds__(256) pack_b_planes_kernel(const uint32_t* __restrict__ B, uint32_t k, uint32_t n,
                                                             uint32_t kpad, uint8_t* __restrict__ Bp,
                                                             uint32_t* __restrict__ err) {
     __shared__ uint32_t tile[32][33];
-    const uint32_t j0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+    const uint32_t j0 = blockIdx.x * 32, s = blockIdx.y, t0 = s * 32;
     const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     uint32_t bad = 0;
     for (uint32_t r = ty; r < 32; r += 8) {
@@ -40,17 +48,19 @@ __global__ void __launch_bounds__(256) pack_b_planes_kernel(const uint32_t* __re
         tile[r][tx] = v;
     }
     __syncthreads();
-    // thread -> (column j0 + jl, four consecutive t starting at t0 + 4 t4)
-    const uint32_t jl = threadIdx.x >> 3, t4 = threadIdx.x & 7;
-    const uint32_t j = j0 + jl;
-    if (j < n) {
-        const uint4 e = make_uint4(tile[4 * t4][jl], tile[4 * t4 + 1][jl], tile[4 * t4 + 2][jl], tile[4 * t4 + 3][jl]);
-        uint32_t p[4];
-        byte_planes(e, p[0], p[1], p[2], p[3]);
-        const size_t plane = (size_t)n * kpad;
-#pragma unroll
-        for (int b = 0; b < 4; b++)
-            *reinterpret_cast<uint32_t*>(Bp + b * plane + (size_t)j * kpad + t0 + 4 * t4) = p[b];
+    if (threadIdx.x < 128) {  // thread -> (column j0 + jl, fragment lane tg)
+        const uint32_t jl = threadIdx.x >> 2, tg = threadIdx.x & 3, j = j0 + jl;
+        if (j < n) {
+            uint32_t p0[4], p1[4];
+            byte_planes(make_uint4(tile[4 * tg][jl], tile[4 * tg + 1][jl], tile[4 * tg + 2][jl], tile[4 * tg + 3][jl]),
+                        p0[0], p0[1], p0[2], p0[3]);
+            byte_planes(make_uint4(tile[16 + 4 * tg][jl], tile[17 + 4 * tg][jl], tile[18 + 4 * tg][jl],
+                                   tile[19 + 4 * tg][jl]),
+                        p1[0], p1[1], p1[2], p1[3]);
+            uint4* dst = reinterpret_cast<uint4*>(Bp + bp_offset(j, s, tg, kpad / 32));
+            dst[0] = make_uint4(p0[0], p1[0], p0[1], p1[1]);
+            dst[1] = make_uint4(p0[2], p1[2], p0[3], p1[3]);
+        }
     }
     if (bad & 0x80000000u) atomicOr(err, 1u);
 }
@@ -67,7 +77,7 @@ __global__ void __launch_bounds__(128) m31_gemm_tc_kernel(const uint32_t* __rest
     const bool v0 = r0 < m, v1 = r1 < m;
     const uint4* a0p = reinterpret_cast<const uint4*>(A + (size_t)(v0 ? r0 : 0) * k);
     const uint4* a1p = reinterpret_cast<const uint4*>(A + (size_t)(v1 ? r1 : 0) * k);
-    const size_t plane = (size_t)n * kpad;
+    const uint32_t ksteps = kpad / 32;
     const uint32_t jb0 = j0 + g, jb1 = j0 + 8 + g;  // B fragment columns of the two N-tiles
     const bool w0 = jb0 < n, w1 = jb1 < n;
     uint64_t tot[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
@@ -96,14 +106,18 @@ __global__ void __launch_bounds__(128) m31_gemm_tc_kernel(const uint32_t* __rest
                 byte_planes(x[f], pa[0][f], pa[1][f], pa[2][f], pa[3][f]);
             }
             uint32_t bb[2][4][2];
+            const uint32_t ks = t / 32;
 #pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const uint8_t* p0 = Bp + b * plane + (size_t)jb0 * kpad + ta;
-                const uint8_t* p1 = Bp + b * plane + (size_t)jb1 * kpad + ta;
-                bb[0][b][0] = w0 ? __ldg(reinterpret_cast<const uint32_t*>(p0)) : 0u;
-                bb[0][b][1] = w0 ? __ldg(reinterpret_cast<const uint32_t*>(p0 + 16)) : 0u;
-                bb[1][b][0] = w1 ? __ldg(reinterpret_cast<const uint32_t*>(p1)) : 0u;
-                bb[1][b][1] = w1 ? __ldg(reinterpret_cast<const uint32_t*>(p1 + 16)) : 0u;
+            for (int q = 0; q < 2; q++) {
+                const bool ok = q ? w1 : w0;
+                uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
+                if (ok) {
+                    const uint4* src = reinterpret_cast<const uint4*>(Bp + bp_offset(q ? jb1 : jb0, ks, tg, ksteps));
+                    u0 = __ldg(src);
+                    u1 = __ldg(src + 1);
+                }
+                bb[q][0][0] = u0.x; bb[q][0][1] = u0.y; bb[q][1][0] = u0.z; bb[q][1][1] = u0.w;
+                bb[q][2][0] = u1.x; bb[q][2][1] = u1.y; bb[q][3][0] = u1.z; bb[q][3][1] = u1.w;
             }
 #pragma unroll
             for (int q = 0; q < 2; q++)

@@ -5,9 +5,8 @@
 // Both operands are split into byte planes (imma.cuh): C = sum_{a,b} 256^(a+b)
 // A_a B_b, each A_a B_b an exact u8 GEMM on mma.m16n8k32.  A (m x k, row major)
 // is read as is: four consecutive k of a row are one 16-byte load whose byte
-// planes are A fragments.  B (k x n, row major) is first packed into four
-// planes (in the order the B fragments are read, bp_offset) by a shared-memory
-// transpose.  The sixteen plane pairs share seven accumulators
+// planes are A fragments; B (k x n, row major) is read in place, four rows at a
+// time, and split into planes in registers.  The sixteen plane pairs share seven accumulators
 // by weight w = a + b (at most four pairs per weight, each below
 // 255^2 * 8192 per K chunk, so a chunk of 8192 stays below 2^31); every K
 // chunk ends with sum_w 256^w acc_w mod P added to 64-bit lazy sums.
@@ -24,127 +23,112 @@ namespace zk {
 
 constexpr uint32_t GEMM_KCHUNK = 8192;
 
-// Packed right operand, laid out in the order the B fragments are read: for
-// column j, K step s (32 values of t) and fragment lane tg (0..3), 32 bytes =
-// for each plane b the two fragment words (t = 32 s + 4 tg + [0, 4) and
-// t = 32 s + 16 + 4 tg + [0, 4)), so a lane fetches all four planes of one K
-// step with two 16-byte loads.  Entries with t >= k are zero.
-__device__ __forceinline__ size_t bp_offset(uint32_t j, uint32_t s, uint32_t tg, uint32_t ksteps) {
-    return (((size_t)j * ksteps + s) * 4 + tg) * 32;
+// One block = 4 x NT x KS warps over a 64-row group and 8 NT output columns:
+// warp w takes row tile w % 4 (16 rows), N-tile (w / 4) % NT and K part
+// w / (4 NT); K parts meet in shared memory at the end.  B is read in place (row major): the four
+// values B[t .. t+3][j] a B-fragment word needs are four 4-byte loads whose
+// byte planes are the four planes' words; the lanes of a warp cover 8
+// consecutive columns x 4 rows per load, so every 32-byte sector is used.
+// The next K step's loads are issued before this step's MMAs.
+constexpr int GEMM_NT = 1;  // 8-column N-tiles per block
+constexpr int GEMM_KS = 2;  // K splits per block
+
+struct GemmLoads {
+    uint4 a[4];      // A: rows r0 / r1, k = t + 4 tg (+16)
+    uint32_t b[8];   // B: rows t + 4 tg + e (e < 4) and t + 16 + 4 tg + e, column j
+};
+
+__device__ __forceinline__ void gemm_load(GemmLoads& L, const uint4* a0p, const uint4* a1p, bool v0, bool v1,
+                                          const uint32_t* __restrict__ B, uint32_t k, uint32_t n, uint32_t j,
+                                          bool wj, uint32_t t, uint32_t tg) {
+    const uint32_t ta = t + 4 * tg, tb = ta + 16;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    L.a[0] = (v0 && ta < k) ? __ldg(a0p + ta / 4) : z;
+    L.a[1] = (v1 && ta < k) ? __ldg(a1p + ta / 4) : z;
+    L.a[2] = (v0 && tb < k) ? __ldg(a0p + tb / 4) : z;
+    L.a[3] = (v1 && tb < k) ? __ldg(a1p + tb / 4) : z;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        L.b[e] = (wj && ta + e < k) ? __ldg(B + (size_t)(ta + e) * n + j) : 0u;
+        L.b[4 + e] = (wj && tb + e < k) ? __ldg(B + (size_t)(tb + e) * n + j) : 0u;
+    }
 }
 
-__global__ void __launch_bounds__(256) pack_b_planes_kernel(const uint32_t* __restrict__ B, uint32_t k, uint32_t n,
-                                                            uint32_t kpad, uint8_t* __restrict__ Bp,
-                                                            uint32_t* __restrict__ err) {
-    __shared__ uint32_t tile[32][33];
-    const uint32_t j0 = blockIdx.x * 32, s = blockIdx.y, t0 = s * 32;
-    const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    uint32_t bad = 0;
-    for (uint32_t r = ty; r < 32; r += 8) {
-        const uint32_t t = t0 + r, j = j0 + tx;
-        uint32_t v = 0;
-        if (t < k && j < n) v = B[(size_t)t * n + j];
-        bad |= v;
-        tile[r][tx] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x < 128) {  // thread -> (column j0 + jl, fragment lane tg)
-        const uint32_t jl = threadIdx.x >> 2, tg = threadIdx.x & 3, j = j0 + jl;
-        if (j < n) {
-            uint32_t p0[4], p1[4];
-            byte_planes(make_uint4(tile[4 * tg][jl], tile[4 * tg + 1][jl], tile[4 * tg + 2][jl], tile[4 * tg + 3][jl]),
-                        p0[0], p0[1], p0[2], p0[3]);
-            byte_planes(make_uint4(tile[16 + 4 * tg][jl], tile[17 + 4 * tg][jl], tile[18 + 4 * tg][jl],
-                                   tile[19 + 4 * tg][jl]),
-                        p1[0], p1[1], p1[2], p1[3]);
-            uint4* dst = reinterpret_cast<uint4*>(Bp + bp_offset(j, s, tg, kpad / 32));
-            dst[0] = make_uint4(p0[0], p1[0], p0[1], p1[1]);
-            dst[1] = make_uint4(p0[2], p1[2], p0[3], p1[3]);
-        }
-    }
-    if (bad & 0x80000000u) atomicOr(err, 1u);
-}
-
-// One block: 4 warps x 16 rows (a 64-row group) by 16 columns; warp w takes
-// rows 64 * blockIdx.y + 16 w ...  All warps of a block read the same B plane
-// words, so B comes from DRAM once and from L1 for the other warps.
-__global__ void __launch_bounds__(128) m31_gemm_tc_kernel(const uint32_t* __restrict__ A, const uint8_t* __restrict__ Bp,
-                                                          uint32_t* __restrict__ Cm, uint32_t m, uint32_t k, uint32_t n,
-                                                          uint32_t kpad, uint32_t* __restrict__ err) {
+template <int NT, int KS>
+__global__ void __launch_bounds__(4 * NT * KS * 32) m31_gemm_tc_kernel(const uint32_t* __restrict__ A,
+                                                                     const uint32_t* __restrict__ B,
+                                                                     uint32_t* __restrict__ Cm, uint32_t m, uint32_t k,
+                                                                     uint32_t n, uint32_t* __restrict__ err) {
+    __shared__ uint64_t part[KS > 1 ? 4 * NT : 1][32][4];
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tg = lane & 3;
-    const uint32_t r0 = blockIdx.y * 64 + warp * 16 + g, r1 = r0 + 8;
-    const uint32_t j0 = blockIdx.x * 16;
-    const bool v0 = r0 < m, v1 = r1 < m;
+    const uint32_t rt = warp & 3, nt = (warp >> 2) % NT, half = warp / (4 * NT);
+    const uint32_t r0 = blockIdx.y * 64 + rt * 16 + g, r1 = r0 + 8;
+    const uint32_t j0 = blockIdx.x * 8 * NT + 8 * nt, j = j0 + g;
+    const bool v0 = r0 < m, v1 = r1 < m, wj = j < n;
     const uint4* a0p = reinterpret_cast<const uint4*>(A + (size_t)(v0 ? r0 : 0) * k);
     const uint4* a1p = reinterpret_cast<const uint4*>(A + (size_t)(v1 ? r1 : 0) * k);
-    const uint32_t ksteps = kpad / 32;
-    const uint32_t jb0 = j0 + g, jb1 = j0 + 8 + g;  // B fragment columns of the two N-tiles
-    const bool w0 = jb0 < n, w1 = jb1 < n;
-    uint64_t tot[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    // this warp's half of the K steps
+    const uint32_t steps = (k + 31) / 32, per = (steps + KS - 1) / KS;
+    const uint32_t s_begin = min(steps, half * per), s_end = min(steps, s_begin + per);
+    uint64_t tot[4] = {0, 0, 0, 0};
     uint32_t bad = 0;
-    for (uint32_t c0 = 0; c0 < kpad; c0 += GEMM_KCHUNK) {
-        const uint32_t c_end = min(kpad, c0 + GEMM_KCHUNK);
-        int acc[7][2][4];
+    GemmLoads cur, nxt;
+    if (s_begin < s_end) gemm_load(cur, a0p, a1p, v0, v1, B, k, n, j, wj, 32 * s_begin, tg);
+    for (uint32_t c0 = s_begin; c0 < s_end; c0 += GEMM_KCHUNK / 32) {
+        const uint32_t c_end = min(s_end, c0 + GEMM_KCHUNK / 32);
+        int acc[7][4];
 #pragma unroll
         for (int w = 0; w < 7; w++)
 #pragma unroll
-            for (int q = 0; q < 2; q++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) acc[w][q][e] = 0;
-        for (uint32_t t = c0; t < c_end; t += 32) {
-            const uint32_t ta = t + 4 * tg, tb = ta + 16;
-            const uint4 z = make_uint4(0, 0, 0, 0);
-            uint4 x[4];
-            x[0] = (v0 && ta < k) ? __ldg(a0p + ta / 4) : z;
-            x[1] = (v1 && ta < k) ? __ldg(a1p + ta / 4) : z;
-            x[2] = (v0 && tb < k) ? __ldg(a0p + tb / 4) : z;
-            x[3] = (v1 && tb < k) ? __ldg(a1p + tb / 4) : z;
-            uint32_t pa[4][4];
+            for (int e = 0; e < 4; e++) acc[w][e] = 0;
+        for (uint32_t st = c0; st < c_end; st++) {
+            if (st + 1 < s_end) gemm_load(nxt, a0p, a1p, v0, v1, B, k, n, j, wj, 32 * (st + 1), tg);
+            uint32_t pa[4][4], pb[4][2];
 #pragma unroll
             for (int f = 0; f < 4; f++) {
-                bad |= x[f].x | x[f].y | x[f].z | x[f].w;
-                byte_planes(x[f], pa[0][f], pa[1][f], pa[2][f], pa[3][f]);
-            }
-            uint32_t bb[2][4][2];
-            const uint32_t ks = t / 32;
-#pragma unroll
-            for (int q = 0; q < 2; q++) {
-                const bool ok = q ? w1 : w0;
-                uint4 u0 = make_uint4(0, 0, 0, 0), u1 = u0;
-                if (ok) {
-                    const uint4* src = reinterpret_cast<const uint4*>(Bp + bp_offset(q ? jb1 : jb0, ks, tg, ksteps));
-                    u0 = __ldg(src);
-                    u1 = __ldg(src + 1);
-                }
-                bb[q][0][0] = u0.x; bb[q][0][1] = u0.y; bb[q][1][0] = u0.z; bb[q][1][1] = u0.w;
-                bb[q][2][0] = u1.x; bb[q][2][1] = u1.y; bb[q][3][0] = u1.z; bb[q][3][1] = u1.w;
+                bad |= cur.a[f].x | cur.a[f].y | cur.a[f].z | cur.a[f].w;
+                byte_planes(cur.a[f], pa[0][f], pa[1][f], pa[2][f], pa[3][f]);
             }
 #pragma unroll
-            for (int q = 0; q < 2; q++)
+            for (int h = 0; h < 2; h++) {
+                const uint4 bw = make_uint4(cur.b[4 * h], cur.b[4 * h + 1], cur.b[4 * h + 2], cur.b[4 * h + 3]);
+                bad |= bw.x | bw.y | bw.z | bw.w;
+                byte_planes(bw, pb[0][h], pb[1][h], pb[2][h], pb[3][h]);
+            }
 #pragma unroll
-                for (int a = 0; a < 4; a++)
+            for (int a = 0; a < 4; a++)
 #pragma unroll
-                    for (int b = 0; b < 4; b++) mma_u8(acc[a + b][q], pa[a], bb[q][b][0], bb[q][b][1]);
+                for (int b = 0; b < 4; b++) mma_u8(acc[a + b], pa[a], pb[b][0], pb[b][1]);
+            cur = nxt;
         }
-#pragma unroll
-        for (int q = 0; q < 2; q++)
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                uint64_t sum = 0;
-#pragma unroll
-                for (int w = 0; w < 7; w++) sum = acc_fold(sum, mul_wide((uint32_t)acc[w][q][e], pow256(w)));
-                tot[q][e] = acc_fold(tot[q][e], (uint64_t)canon64(sum));
-            }
-    }
-    // C fragment: e = 0, 1 -> row r0, columns 2 tg, 2 tg + 1 of N-tile q; e = 2, 3 -> row r1
-#pragma unroll
-    for (int q = 0; q < 2; q++)
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-            const uint32_t row = e < 2 ? r0 : r1, col = j0 + 8 * q + 2 * tg + (e & 1);
-            if (row < m && col < n) Cm[(size_t)row * n + col] = canon64(tot[q][e]);
+            uint64_t sum = 0;
+#pragma unroll
+            for (int w = 0; w < 7; w++) sum = acc_fold(sum, mul_wide((uint32_t)acc[w][e], pow256(w)));
+            tot[e] = acc_fold(tot[e], (uint64_t)canon64(sum));
         }
+    }
+    static_assert(KS == 1 || KS == 2, "K split");
     if (bad & 0x80000000u) atomicOr(err, 1u);
+    if (KS > 1) {  // K halves meet in shared memory
+        if (half) {
+#pragma unroll
+            for (int e = 0; e < 4; e++) part[warp % (4 * NT)][lane][e] = tot[e];
+        }
+        __syncthreads();
+        if (half) return;
+#pragma unroll
+        for (int e = 0; e < 4; e++) tot[e] = acc_fold(tot[e], part[warp][lane][e]);
+    }
+    {
+        // C fragment: e = 0, 1 -> row r0, columns 2 tg, 2 tg + 1; e = 2, 3 -> row r1
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t row = e < 2 ? r0 : r1, col = j0 + 2 * tg + (e & 1);
+            if (row < m && col < n) Cm[(size_t)row * n + col] = canon64(tot[e]);
+        }
+    }
 }
 
 }  // namespace zk
@@ -178,15 +162,10 @@ extern "C" int zkml_matmul_m31(zkml_ctx* ctx, const uint32_t* a, size_t m, size_
     const uint32_t* Ad = static_cast<const uint32_t*>(A);
     static const bool tc_on = !(getenv("ZKML_GEMM_TC") && getenv("ZKML_GEMM_TC")[0] == '0');  // 0: CUDA cores
     if (tc_on && k % 4 == 0 && (reinterpret_cast<uintptr_t>(Ad) & 15) == 0) {
-        const size_t kpad = (k + 31) / 32 * 32;
-        if ((rc = ctx->gemm_planes.ensure(4 * n * kpad))) return rc;
-        dim3 pg((unsigned)((n + 31) / 32), (unsigned)(kpad / 32));
-        pack_b_planes_kernel<<<pg, 256, 0, s>>>(static_cast<const uint32_t*>(B), (uint32_t)k, (uint32_t)n,
-                                                 (uint32_t)kpad, ctx->gemm_planes.as<uint8_t>(), ctx->err_flag());
-        dim3 gg((unsigned)((n + 15) / 16), (unsigned)((m + 63) / 64));
-        m31_gemm_tc_kernel<<<gg, 128, 0, s>>>(Ad, ctx->gemm_planes.as<uint8_t>(), C, (uint32_t)m, (uint32_t)k,
-                                               (uint32_t)n, (uint32_t)kpad, ctx->err_flag());
-        ctx->launches += 2;
+        dim3 gg((unsigned)((n + 8 * GEMM_NT - 1) / (8 * GEMM_NT)), (unsigned)((m + 63) / 64));
+        m31_gemm_tc_kernel<GEMM_NT, GEMM_KS><<<gg, 4 * GEMM_NT * GEMM_KS * 32, 0, s>>>(Ad, static_cast<const uint32_t*>(B), C, (uint32_t)m,
+                                                           (uint32_t)k, (uint32_t)n, ctx->err_flag());
+        ctx->launches++;
     } else {
         launch_m31_gemm(Ad, static_cast<const uint32_t*>(B), C, (uint32_t)m, (uint32_t)k, (uint32_t)n, s);
         ctx->launches++;

@@ -712,7 +712,6 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
     ctx->rc_table.release();
     ctx->lu.release();
     ctx->op.release();
-    ctx->gemm_planes.release();
     ctx->gather_dev.release();
     if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
     ctx->sc_a.release();

@@ -1,5 +1,6 @@
-// Device felt252 arithmetic (Stark prime) and the Hades permutation for the
-// Poseidon Merkle kernels.  Integer-pipe bound: no tensor cores.
+// Device felt252 Montgomery multiplication (Stark prime) in 8 x 32-bit limbs,
+// used to bring securefield_to_felt leaves into the host's Montgomery form.
+// The Merkle kernels' Hades permutation itself runs in radix 2^26 (felt26.cuh).
 //
 // Representation: 8 x u32 little-endian limbs, Montgomery form with R = 2^256
 // (bit-identical to the host's 4 x u64 Montgomery limbs, so host and device
@@ -15,12 +16,6 @@ namespace zk {
 struct dfelt {
     uint32_t w[8];
 };
-
-// Compressed Hades round keys (Montgomery form): 12 full-round keys, 83
-// partial-round keys, 12 full-round keys.  Without relocatable device code each
-// translation unit that includes this header has its own copy, filled by that
-// unit's upload function (merkle_kernels.cu: upload_hades_constants()).
-static __constant__ dfelt c_hades_rc[107];
 
 __device__ __forceinline__ bool dgeq_p(const uint32_t t[8]) {
     // compare with p from the top limb down
@@ -40,56 +35,6 @@ __device__ __forceinline__ void dsub_p(uint32_t t[8]) {
         "subc.cc.u32 %6, %6, 0x11;\n\t"
         "subc.u32    %7, %7, 0x08000000;"
         : "+r"(t[0]), "+r"(t[1]), "+r"(t[2]), "+r"(t[3]), "+r"(t[4]), "+r"(t[5]), "+r"(t[6]), "+r"(t[7]));
-}
-
-__device__ __forceinline__ dfelt dadd(const dfelt& a, const dfelt& b) {
-    dfelt r;
-    asm("add.cc.u32  %0, %8, %16;\n\t"
-        "addc.cc.u32 %1, %9, %17;\n\t"
-        "addc.cc.u32 %2, %10, %18;\n\t"
-        "addc.cc.u32 %3, %11, %19;\n\t"
-        "addc.cc.u32 %4, %12, %20;\n\t"
-        "addc.cc.u32 %5, %13, %21;\n\t"
-        "addc.cc.u32 %6, %14, %22;\n\t"
-        "addc.u32    %7, %15, %23;"
-        : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]), "=r"(r.w[4]), "=r"(r.w[5]), "=r"(r.w[6]),
-          "=r"(r.w[7])
-        : "r"(a.w[0]), "r"(a.w[1]), "r"(a.w[2]), "r"(a.w[3]), "r"(a.w[4]), "r"(a.w[5]), "r"(a.w[6]), "r"(a.w[7]),
-          "r"(b.w[0]), "r"(b.w[1]), "r"(b.w[2]), "r"(b.w[3]), "r"(b.w[4]), "r"(b.w[5]), "r"(b.w[6]), "r"(b.w[7]));
-    if (dgeq_p(r.w)) dsub_p(r.w);
-    return r;
-}
-
-// a - b mod p
-__device__ __forceinline__ dfelt dsub(const dfelt& a, const dfelt& b) {
-    dfelt r;
-    uint32_t borrow;
-    asm("sub.cc.u32  %0, %9, %17;\n\t"
-        "subc.cc.u32 %1, %10, %18;\n\t"
-        "subc.cc.u32 %2, %11, %19;\n\t"
-        "subc.cc.u32 %3, %12, %20;\n\t"
-        "subc.cc.u32 %4, %13, %21;\n\t"
-        "subc.cc.u32 %5, %14, %22;\n\t"
-        "subc.cc.u32 %6, %15, %23;\n\t"
-        "subc.cc.u32 %7, %16, %24;\n\t"
-        "subc.u32    %8, 0, 0;"
-        : "=r"(r.w[0]), "=r"(r.w[1]), "=r"(r.w[2]), "=r"(r.w[3]), "=r"(r.w[4]), "=r"(r.w[5]), "=r"(r.w[6]),
-          "=r"(r.w[7]), "=r"(borrow)
-        : "r"(a.w[0]), "r"(a.w[1]), "r"(a.w[2]), "r"(a.w[3]), "r"(a.w[4]), "r"(a.w[5]), "r"(a.w[6]), "r"(a.w[7]),
-          "r"(b.w[0]), "r"(b.w[1]), "r"(b.w[2]), "r"(b.w[3]), "r"(b.w[4]), "r"(b.w[5]), "r"(b.w[6]), "r"(b.w[7]));
-    if (borrow) {
-        asm("add.cc.u32  %0, %0, 1;\n\t"
-            "addc.cc.u32 %1, %1, 0;\n\t"
-            "addc.cc.u32 %2, %2, 0;\n\t"
-            "addc.cc.u32 %3, %3, 0;\n\t"
-            "addc.cc.u32 %4, %4, 0;\n\t"
-            "addc.cc.u32 %5, %5, 0;\n\t"
-            "addc.cc.u32 %6, %6, 0x11;\n\t"
-            "addc.u32    %7, %7, 0x08000000;"
-            : "+r"(r.w[0]), "+r"(r.w[1]), "+r"(r.w[2]), "+r"(r.w[3]), "+r"(r.w[4]), "+r"(r.w[5]), "+r"(r.w[6]),
-              "+r"(r.w[7]));
-    }
-    return r;
 }
 
 // One CIOS step: t += a * bi, then t = (t + m p) / 2^32 with m = -t0.
@@ -154,42 +99,6 @@ __device__ __forceinline__ dfelt dmul(const dfelt& a, const dfelt& b) {
     for (int i = 0; i < 8; i++) r.w[i] = t[i];
     if (dgeq_p(r.w)) dsub_p(r.w);
     return r;
-}
-
-// Kept out of line: Hades calls it 107 times and inlining every call site
-// overflows the instruction cache (ncu showed "no instruction" stalls).
-__device__ __noinline__ dfelt dcube(const dfelt x) { return dmul(dmul(x, x), x); }
-
-__device__ __forceinline__ void dmds(dfelt s[3]) {
-    dfelt t = dadd(dadd(s[0], s[1]), s[2]);
-    dfelt n0 = dadd(t, dadd(s[0], s[0]));
-    dfelt n1 = dsub(t, dadd(s[1], s[1]));
-    dfelt n2 = dsub(t, dadd(dadd(s[2], s[2]), s[2]));
-    s[0] = n0;
-    s[1] = n1;
-    s[2] = n2;
-}
-
-__device__ __forceinline__ void dhades(dfelt s[3]) {
-#pragma unroll 1
-    for (int r = 0; r < 4; r++) {
-        s[0] = dcube(dadd(s[0], c_hades_rc[3 * r + 0]));
-        s[1] = dcube(dadd(s[1], c_hades_rc[3 * r + 1]));
-        s[2] = dcube(dadd(s[2], c_hades_rc[3 * r + 2]));
-        dmds(s);
-    }
-#pragma unroll 1
-    for (int r = 0; r < 83; r++) {
-        s[2] = dcube(dadd(s[2], c_hades_rc[12 + r]));
-        dmds(s);
-    }
-#pragma unroll 1
-    for (int r = 0; r < 4; r++) {
-        s[0] = dcube(dadd(s[0], c_hades_rc[95 + 3 * r + 0]));
-        s[1] = dcube(dadd(s[1], c_hades_rc[95 + 3 * r + 1]));
-        s[2] = dcube(dadd(s[2], c_hades_rc[95 + 3 * r + 2]));
-        dmds(s);
-    }
 }
 
 }  // namespace zk

@@ -17,7 +17,6 @@
 namespace zk {
 
 __constant__ dfelt c_mont_r2;  // 2^512 mod p: Montgomery conversion factor
-__constant__ dfelt c_mont_two; // Montgomery form of 2 (poseidon_hash capacity)
 
 // securefield_to_felt(v) in Montgomery form.
 __device__ __forceinline__ dfelt leaf_int(uint4 v) {
@@ -199,9 +198,7 @@ f26 times_2k(const void* mont256, int k) {  // value * 2^k mod p, as limbs
 
 cudaError_t upload_hades_constants(const void* rc107_mont, const void* r2_mont, const void* two_mont,
                                    const void* one_mont) {
-    cudaError_t e = cudaMemcpyToSymbol(c_hades_rc, rc107_mont, sizeof(dfelt) * 107);
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(c_mont_r2, r2_mont, sizeof(dfelt));
-    if (e == cudaSuccess) e = cudaMemcpyToSymbol(c_mont_two, two_mont, sizeof(dfelt));
+    cudaError_t e = cudaMemcpyToSymbol(c_mont_r2, r2_mont, sizeof(dfelt));
     if (e != cudaSuccess) return e;
     static F26Consts h;  // Montgomery (2^256) x -> x * 2^260 = value * 16
     const uint64_t* rc = static_cast<const uint64_t*>(rc107_mont);

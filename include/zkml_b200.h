@@ -197,6 +197,21 @@ int zkml_reduce_activation_logup(zkml_ctx *ctx, const uint32_t *input, size_t ro
                                  zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                  uint32_t out_input_eval[4]);
 
+/* reduce_rmsnorm_layer_with_gamma (gkr/prover.rs:8424-8790): the RMSNorm layer
+ * output = input * rsqrt(rms^2) (* gamma) over the rows x cols input (zero-padded to
+ * powers of two; rms^2 over the first min(dim, padded cols) columns of each row).
+ * Proves sum_x input(x)^2 (plain sumcheck; left out when STWO_SKIP_RMS_SQ_PROOF is
+ * set, as in the reference), output(r) = sum_x eq(r, x) input(x) scale(x)
+ * (degree-3 eq-sumcheck) and that every (rms^2, rsqrt) pair lies in the 2^16-entry
+ * rsqrt table (LogUp + multiplicity sumcheck).  gamma (gamma_len values, host or
+ * device memory) is the optional learned per-column scale, NULL for none.  Writes
+ * the LayerProof::RMSNorm record of serialize_gkr_model_proof
+ * (cairo_serde.rs:1648-1726) and the input evaluation (the next claim's value). */
+int zkml_reduce_rmsnorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_t cols, size_t dim,
+                        const uint32_t *gamma, size_t gamma_len, const uint32_t *claim_point, size_t n_point,
+                        const uint32_t claim_value[4], zkml_channel *ch, uint64_t *out_calldata, size_t cap,
+                        size_t *out_len, uint32_t out_input_eval[4]);
+
 /* ---- Forward pass --------------------------------------------------------------
  * C = A * B mod p for M31 matrices (m x k times k x n, row major): the forward
  * GEMM that produces a layer's output (gpu_matmul_m31_full,

@@ -1766,3 +1766,442 @@ int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint
     if (out_input_eval) q_store(out_input_eval, input_eval);
     return in.pos == len && !in.bad;
 }
+
+/* ---------------------------------------------------------------------------
+ * RMSNorm layer reduction.
+ * ------------------------------------------------------------------------- */
+
+/* floor(sqrt(v)) for v < 2^53 (floating estimate, then corrected to the exact floor). */
+static uint64_t isqrt_u64(uint64_t v) {
+    uint64_t s = (uint64_t)sqrt((double)v);
+    while (s * s > v) s--;
+    while ((s + 1) * (s + 1) <= v) s++;
+    return s;
+}
+
+/* rsqrt lookup table (components/layernorm.rs:116-136): 0 -> 2^16 - 1, x -> min(2^16 / isqrt(x), p - 1). */
+int orc_rsqrt_table(unsigned log_size, uint32_t *out) {
+    if (log_size > 24) return 1;
+    for (size_t x = 0; x < ((size_t)1 << log_size); x++) {
+        if (x == 0) {
+            out[x] = (1u << 16) - 1;
+            continue;
+        }
+        uint64_t s = isqrt_u64(x);
+        uint64_t r = ((uint64_t)1 << 16) / s;
+        const uint64_t lim = ((uint64_t)1 << 31) - 2;
+        out[x] = (uint32_t)(r < lim ? r : lim);
+    }
+    return 0;
+}
+
+/* build_multiplicity_sumcheck (gkr/prover.rs:9449-9515): degree-1 rounds over the
+ * multiplicity MLE; per round mix c0, c1 and draw.  Fills rounds (2 per round), final, claim. */
+static void mult_sumcheck(orc_channel *ch, const uint32_t *mult, unsigned log_t, q31 *mrp, q31 *m_final,
+                          q31 *m_claim) {
+    size_t tsize = (size_t)1 << log_t;
+    q31 *mv = (q31 *)malloc(sizeof(q31) * tsize);
+    q31 claim = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        mv[j] = q_from_m(mult[j] % MP);
+        claim = q_add(claim, mv[j]);
+    }
+    size_t msz = tsize;
+    for (unsigned r = 0; r < log_t; r++) {
+        size_t half = msz / 2;
+        q31 s0 = q_from_m(0), s1 = q_from_m(0);
+        for (size_t j = 0; j < half; j++) {
+            s0 = q_add(s0, mv[j]);
+            s1 = q_add(s1, mv[half + j]);
+        }
+        q31 c0 = s0, c1 = q_sub(s1, s0);
+        if (mrp) {
+            mrp[2 * r] = c0;
+            mrp[2 * r + 1] = c1;
+        }
+        ch_mix_sf(ch, c0);
+        ch_mix_sf(ch, c1);
+        fold_vec(mv, half, ch_draw_qm31(ch));
+        msz = half;
+    }
+    if (m_final) *m_final = mv[0];
+    if (m_claim) *m_claim = claim;
+    free(mv);
+}
+
+static void mix_deg3(orc_channel *ch, q31 c0, q31 c1, q31 c2, q31 c3) {
+    uint32_t coeffs[16];
+    q_store(coeffs, c0);
+    q_store(coeffs + 4, c1);
+    q_store(coeffs + 8, c2);
+    q_store(coeffs + 12, c3);
+    orc_ch_mix_poly_coeffs_deg3(ch, coeffs);
+}
+
+/* Degree-3 eq-sumcheck sum eq(r, x) a(x) b(x) (eq, a, b are consumed); rounds get
+ * (c0, c1, c2, c3) per round, chal the challenges. */
+static void eq_sumcheck_deg3(orc_channel *ch, q31 *eq, q31 *a, q31 *b, size_t n, unsigned num_vars, q31 *rps,
+                             q31 *chal) {
+    uint32_t inv2 = m_inv(2), inv6 = m_inv(6);
+    size_t cur = n;
+    for (unsigned r = 0; r < num_vars; r++) {
+        size_t mid = cur / 2;
+        q31 s0 = mul_eq_sum_at(eq, a, b, mid, 0), s1 = mul_eq_sum_at(eq, a, b, mid, 1);
+        q31 s2 = mul_eq_sum_at(eq, a, b, mid, 2), s3 = mul_eq_sum_at(eq, a, b, mid, 3);
+        q31 dd1 = q_sub(s1, s0);
+        q31 dd2 = q_mul_m(q_add(q_sub(q_sub(s2, s1), s1), s0), inv2);
+        q31 dd3 = q_mul_m(q_sub(q_sub(s3, s0), q_mul_m(q_sub(s2, s1), 3)), inv6);
+        q31 c0 = s0, c1 = q_add(q_sub(dd1, dd2), q_mul_m(dd3, 2)), c2 = q_sub(dd2, q_mul_m(dd3, 3)), c3 = dd3;
+        rps[4 * r] = c0;
+        rps[4 * r + 1] = c1;
+        rps[4 * r + 2] = c2;
+        rps[4 * r + 3] = c3;
+        mix_deg3(ch, c0, c1, c2, c3);
+        chal[r] = ch_draw_qm31(ch);
+        fold_vec(eq, mid, chal[r]);
+        fold_vec(a, mid, chal[r]);
+        fold_vec(b, mid, chal[r]);
+        cur = mid;
+    }
+}
+
+static q31 mle_eval_copy(const q31 *v, size_t n, const q31 *point, unsigned num_vars) {
+    q31 *tmp = (q31 *)malloc(sizeof(q31) * n);
+    memcpy(tmp, v, sizeof(q31) * n);
+    restrict_inplace(tmp, n, point, num_vars, 1);
+    q31 r = tmp[0];
+    free(tmp);
+    return r;
+}
+
+int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *gamma_aff,
+                       size_t gamma_len, int skip_rms_sq, const uint32_t *claim_point, size_t n_point,
+                       const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata, size_t cap,
+                       size_t *out_len, uint32_t out_input_eval[4]) {
+    oracle_init();
+    if (rows == 0 || cols == 0 || dim == 0 || (gamma_aff && gamma_len == 0)) return 1;
+    size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
+    unsigned num_vars = ilog2(n);
+    if (num_vars == 0 || n_point < num_vars) return 1;
+    const q31 *point = (const q31 *)claim_point;
+    const unsigned log_t = 16;
+    const size_t tsize = (size_t)1 << log_t;
+    const uint32_t mask = (uint32_t)tsize - 1;
+    uint32_t *table = (uint32_t *)malloc(4 * tsize);
+    orc_rsqrt_table(log_t, table);
+    size_t n_active = dim < pc ? dim : pc;
+    uint32_t inv_n = m_inv((uint32_t)(n_active % MP));
+    /* per-row rms^2 = (sum of squares of the first n_active columns) / n_active, masked to the table */
+    q31 *in_mle = mle_row_major(input, rows, cols);
+    q31 *rsq = (q31 *)malloc(sizeof(q31) * n), *rsq_raw = (q31 *)malloc(sizeof(q31) * n);
+    q31 *scale = (q31 *)malloc(sizeof(q31) * n), *outv = (q31 *)malloc(sizeof(q31) * n);
+    uint32_t *row_rms = (uint32_t *)malloc(4 * pr), *mult = (uint32_t *)calloc(tsize, 4);
+    for (size_t i = 0; i < pr; i++) {
+        uint32_t sq = 0;
+        for (size_t j = 0; j < n_active; j++) sq = m_add(sq, m_mul(in_mle[i * pc + j].a, in_mle[i * pc + j].a));
+        uint32_t rms = m_mul(sq, inv_n) & mask, rs = table[rms];
+        row_rms[i] = rms;
+        mult[rms] += (uint32_t)pc;
+        for (size_t j = 0; j < pc; j++) {
+            size_t idx = i * pc + j;
+            uint32_t x = in_mle[idx].a;
+            rsq[idx] = q_from_m(rms);
+            rsq_raw[idx] = q_from_m(rs);
+            if (j < n_active) {
+                uint32_t sc = gamma_aff ? m_mul(rs, gamma_aff[j < gamma_len - 1 ? j : gamma_len - 1] % MP) : rs;
+                scale[idx] = q_from_m(sc);
+                outv[idx] = q_from_m(m_mul(x, sc));
+            } else {
+                scale[idx] = q_from_m(rs);
+                outv[idx] = q_from_m(x);
+            }
+        }
+    }
+    q31 input_eval = mle_eval_copy(in_mle, n, point, num_vars);
+    q31 output_eval = mle_eval_copy(outv, n, point, num_vars);
+    q31 rsqrt_eval = mle_eval_copy(rsq_raw, n, point, num_vars);
+    q31 rms_sq_eval = mle_eval_copy(rsq, n, point, num_vars);
+    free(outv);
+    /* Part 0: plain sumcheck sum_x input(x)^2 = total (prover.rs:8500-8545) */
+    q31 *rq = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    q31 total_sq = q_from_m(0), rq_final = q_from_m(0);
+    for (size_t i = 0; i < n; i++) total_sq = q_add(total_sq, q_mul(in_mle[i], in_mle[i]));
+    if (!skip_rms_sq) {
+        orc_ch_mix_u64(ch, 0x5251);
+        orc_ch_mix_u64(ch, n_active);
+        ch_mix_sf(ch, total_sq);
+        q31 *v = (q31 *)malloc(sizeof(q31) * n);
+        memcpy(v, in_mle, sizeof(q31) * n);
+        uint32_t inv2 = m_inv(2);
+        size_t cur = n;
+        for (unsigned r = 0; r < num_vars; r++) {
+            size_t mid = cur / 2;
+            q31 s0 = q_from_m(0), s1 = q_from_m(0), s2 = q_from_m(0);
+            for (size_t j = 0; j < mid; j++) {
+                q31 lo = v[j], hi = v[mid + j], two = q_sub(q_add(hi, hi), lo);
+                s0 = q_add(s0, q_mul(lo, lo));
+                s1 = q_add(s1, q_mul(hi, hi));
+                s2 = q_add(s2, q_mul(two, two));
+            }
+            q31 dd1 = q_sub(s1, s0);
+            q31 dd2 = q_mul_m(q_sub(q_sub(s2, s1), dd1), inv2);
+            q31 c0 = s0, c1 = q_sub(dd1, dd2), c2 = dd2, c3 = q_from_m(0);
+            rq[4 * r] = c0;
+            rq[4 * r + 1] = c1;
+            rq[4 * r + 2] = c2;
+            rq[4 * r + 3] = c3;
+            mix_deg3(ch, c0, c1, c2, c3);
+            fold_vec(v, mid, ch_draw_qm31(ch));
+            cur = mid;
+        }
+        rq_final = v[0];
+        ch_mix_sf(ch, rq_final);
+        free(v);
+    }
+    /* Part 1: degree-3 eq-sumcheck output = input x scale (prover.rs:8560-8630) */
+    orc_ch_mix_u64(ch, 0x524E);
+    ch_mix_sf(ch, rms_sq_eval);
+    ch_mix_sf(ch, rsqrt_eval);
+    ch_mix_sf(ch, q_load(claim_value));
+    q31 *eq = lagrange_basis(point, num_vars);
+    q31 *a = (q31 *)malloc(sizeof(q31) * n);
+    memcpy(a, in_mle, sizeof(q31) * n);
+    q31 *lin = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    q31 *chal = (q31 *)malloc(sizeof(q31) * (num_vars + 1));
+    eq_sumcheck_deg3(ch, eq, a, scale, n, num_vars, lin, chal);
+    q31 input_final = a[0], rsqrt_final = scale[0];
+    ch_mix_sf(ch, input_final);
+    ch_mix_sf(ch, rsqrt_final);
+    free(eq);
+    free(a);
+    free(scale);
+    free(in_mle);
+    /* Part 2: LogUp of (rms^2, rsqrt) against the rsqrt table (prover.rs:8632-8720) */
+    orc_ch_mix_u64(ch, 0x4C4F47);
+    orc_ch_mix_u64(ch, 0x524E);
+    q31 gm = ch_draw_qm31(ch), bt = ch_draw_qm31(ch);
+    q31 *d = (q31 *)malloc(sizeof(q31) * n), *w = (q31 *)malloc(sizeof(q31) * n);
+    q31 trace_sum = q_from_m(0);
+    for (size_t i = 0; i < n; i++) {
+        d[i] = q_sub(q_sub(gm, rsq[i]), q_mul(bt, rsq_raw[i]));
+        w[i] = q_inv(d[i]);
+        trace_sum = q_add(trace_sum, w[i]);
+    }
+    q31 table_sum = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        if (!mult[j]) continue;
+        q31 dj = q_sub(q_sub(gm, q_from_m((uint32_t)j)), q_mul(bt, q_from_m(table[j])));
+        table_sum = q_add(table_sum, q_mul_m(q_inv(dj), mult[j] % MP));
+    }
+    int rc = q_eq(trace_sum, table_sum) ? 0 : 3;
+    ch_mix_sf(ch, trace_sum);
+    eq = lagrange_basis(point, num_vars);
+    q31 *lrp = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    eq_sumcheck_deg3(ch, eq, w, d, n, num_vars, lrp, chal);
+    q31 w_eval = w[0];
+    restrict_inplace(rsq, n, chal, num_vars, 1);
+    restrict_inplace(rsq_raw, n, chal, num_vars, 1);
+    q31 rms_s = rsq[0], rsqrt_s = rsq_raw[0];
+    mult_sumcheck(ch, mult, log_t, NULL, NULL, NULL);
+    fe tcom;
+    table_commitment(0x5253, log_t, &tcom);
+    ch_mix_sf(ch, input_eval);
+    ch_mix_sf(ch, output_eval);
+    /* LayerProof::RMSNorm as serialize_gkr_model_proof writes it (cairo_serde.rs:1648-1726) */
+    felt_out o = {calldata, 0, cap, 0};
+    out_u64(&o, 8);
+    out_qm31(&o, input_eval);
+    out_qm31(&o, output_eval);
+    out_qm31(&o, rms_sq_eval);
+    out_qm31(&o, rsqrt_eval);
+    out_push(&o, &tcom);
+    out_u64(&o, 0); /* not SIMD-combined */
+    if (skip_rms_sq) {
+        out_u64(&o, 0);
+    } else {
+        out_u64(&o, 1);
+        out_u64(&o, n_active);
+        out_qm31(&o, total_sq);
+        out_u64(&o, num_vars);
+        for (unsigned r = 0; r < num_vars; r++) {
+            out_qm31(&o, rq[4 * r]);
+            out_qm31(&o, rq[4 * r + 2]);
+            out_qm31(&o, rq[4 * r + 3]);
+        }
+        out_qm31(&o, rq_final);
+    }
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, lin[4 * r]);
+        out_qm31(&o, lin[4 * r + 2]);
+        out_qm31(&o, lin[4 * r + 3]);
+    }
+    out_qm31(&o, input_final);
+    out_qm31(&o, rsqrt_final);
+    out_u64(&o, 1); /* LogUp proof present */
+    out_qm31(&o, trace_sum);
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, lrp[4 * r]);
+        out_qm31(&o, lrp[4 * r + 2]);
+        out_qm31(&o, lrp[4 * r + 3]);
+    }
+    out_qm31(&o, w_eval);
+    out_qm31(&o, rms_s);
+    out_qm31(&o, rsqrt_s);
+    out_u64(&o, tsize);
+    for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
+    if (pr > 1) {
+        out_u64(&o, 1);
+        out_u64(&o, pr);
+        for (size_t i = 0; i < pr; i++) out_u64(&o, row_rms[i]);
+    } else {
+        out_u64(&o, 0);
+    }
+    *out_len = o.len;
+    if (out_input_eval) q_store(out_input_eval, input_eval);
+    free(lrp);
+    free(eq);
+    free(d);
+    free(w);
+    free(chal);
+    free(lin);
+    free(rq);
+    free(rsq);
+    free(rsq_raw);
+    free(row_rms);
+    free(mult);
+    free(table);
+    if (rc) return rc;
+    return o.overflow ? 2 : 0;
+}
+
+/* Replays a compressed deg-3 sumcheck: c1 = cur - 2 c0 - c2 - c3; returns the final sum. */
+static q31 replay_deg3(orc_channel *ch, felt_in *in, size_t rounds, q31 cur, q31 *chal) {
+    for (size_t r = 0; r < rounds; r++) {
+        q31 c0 = in_qm31(in), c2 = in_qm31(in), c3 = in_qm31(in);
+        q31 c1 = q_sub(q_sub(q_sub(cur, q_add(c0, c0)), c2), c3);
+        mix_deg3(ch, c0, c1, c2, c3);
+        q31 x = ch_draw_qm31(ch);
+        if (chal) chal[r] = x;
+        cur = q_add(c0, q_mul(x, q_add(c1, q_mul(x, q_add(c2, q_mul(x, c3))))));
+    }
+    return cur;
+}
+
+int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const uint32_t *claim_point,
+                       size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint32_t out_input_eval[4]) {
+    oracle_init();
+    felt_in in = {calldata, len, 0, 0};
+    if (in_u64(&in) != 8) return 0;
+    q31 input_eval = in_qm31(&in), output_eval = in_qm31(&in);
+    q31 rms_sq_eval = in_qm31(&in), rsqrt_eval = in_qm31(&in);
+    fe tcom, expect;
+    in_felt(&in, &tcom);
+    table_commitment(0x5253, 16, &expect);
+    if (memcmp(expect.v, tcom.v, 32) || in_u64(&in) != 0 || in.bad) return 0;
+    const q31 *point = (const q31 *)claim_point;
+    size_t has_rq = in_u64(&in);
+    size_t num_vars = 0;
+    if (has_rq == 1) {
+        /* Part 0 (verifier.rs:4755-4870) */
+        size_t n_active_s = in_u64(&in);
+        q31 total = in_qm31(&in);
+        num_vars = in_u64(&in);
+        if (num_vars == 0 || num_vars > 40 || num_vars > n_point || in.bad) return 0;
+        size_t n_active = dim < ((size_t)1 << num_vars) ? dim : ((size_t)1 << num_vars);
+        if (n_active_s != n_active) return 0;
+        orc_ch_mix_u64(ch, 0x5251);
+        orc_ch_mix_u64(ch, n_active);
+        ch_mix_sf(ch, total);
+        q31 cur = replay_deg3(ch, &in, num_vars, total, NULL);
+        q31 fin = in_qm31(&in);
+        ch_mix_sf(ch, fin);
+        if (!q_eq(q_mul(fin, fin), cur)) return 0;
+        size_t cols_p = next_pow2(dim), rows_p = ((size_t)1 << num_vars) / cols_p;
+        if (cols_p > ((size_t)1 << num_vars)) return 0;
+        if (rows_p == 1) {
+            uint32_t rms = m_mul(total.a, m_inv((uint32_t)(n_active % MP))) & 0xFFFFu;
+            if (!q_eq(rms_sq_eval, q_from_m(rms))) return 0;
+        }
+        /* multi-row binding is checked after the row values are read */
+    } else if (has_rq != 0) {
+        return 0;
+    } else {
+        return 0; /* a missing RMS^2 proof is rejected (no override) */
+    }
+    if (in_u64(&in) != num_vars) return 0;
+    /* Part 1 */
+    orc_ch_mix_u64(ch, 0x524E);
+    ch_mix_sf(ch, rms_sq_eval);
+    ch_mix_sf(ch, rsqrt_eval);
+    ch_mix_sf(ch, q_load(claim_value));
+    q31 chal[40];
+    q31 cur = replay_deg3(ch, &in, num_vars, q_load(claim_value), chal);
+    q31 input_final = in_qm31(&in), rsqrt_final = in_qm31(&in);
+    if (!q_eq(cur, q_mul(q_mul(eq_eval(point, chal, num_vars), input_final), rsqrt_final))) return 0;
+    ch_mix_sf(ch, input_final);
+    ch_mix_sf(ch, rsqrt_final);
+    /* Part 2 */
+    if (in_u64(&in) != 1) return 0;
+    orc_ch_mix_u64(ch, 0x4C4F47);
+    orc_ch_mix_u64(ch, 0x524E);
+    q31 gm = ch_draw_qm31(ch), bt = ch_draw_qm31(ch);
+    q31 claimed = in_qm31(&in);
+    if (in_u64(&in) != num_vars || in.bad) return 0;
+    size_t rounds_at = in.pos;
+    in.pos += 12 * num_vars; /* round polynomials are replayed after the sum check */
+    q31 w_eval = in_qm31(&in), rms_s = in_qm31(&in), rsqrt_s = in_qm31(&in);
+    const size_t tsize = (size_t)1 << 16;
+    if (in_u64(&in) != tsize || in.bad || in.pos + tsize > len) return 0;
+    uint32_t *table = (uint32_t *)malloc(4 * tsize), *mult = (uint32_t *)malloc(4 * tsize);
+    orc_rsqrt_table(16, table);
+    q31 table_sum = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        uint64_t m = in_u64(&in);
+        mult[j] = (uint32_t)m;
+        if (!m) continue;
+        q31 dj = q_sub(q_sub(gm, q_from_m((uint32_t)j)), q_mul(bt, q_from_m(table[j])));
+        table_sum = q_add(table_sum, q_mul(q_from_m((uint32_t)(m % MP)), q_inv(dj)));
+    }
+    free(table);
+    int ok = q_eq(table_sum, claimed);
+    if (ok) {
+        ch_mix_sf(ch, claimed);
+        felt_in rin = {calldata, len, rounds_at, 0};
+        q31 lsum = replay_deg3(ch, &rin, num_vars, q_from_m(1), chal);
+        q31 d_eval = q_sub(q_sub(gm, rms_s), q_mul(bt, rsqrt_s));
+        ok = q_eq(lsum, q_mul(q_mul(eq_eval(point, chal, num_vars), w_eval), d_eval));
+    }
+    /* the multiplicity sumcheck is not in the calldata; it is a function of the
+     * multiplicities and the transcript, so the verifier replays it */
+    if (ok) mult_sumcheck(ch, mult, 16, NULL, NULL, NULL);
+    free(mult);
+    if (!ok) return 0;
+    /* per-row rms^2 binding (verifier.rs:4830-4870) */
+    size_t has_rows = in_u64(&in);
+    if (has_rows == 1) {
+        size_t cols_p = next_pow2(dim), rows_p = ((size_t)1 << num_vars) / cols_p;
+        size_t nr = in_u64(&in);
+        if (nr != rows_p || in.bad) return 0;
+        unsigned log_rows = ilog2(rows_p);
+        q31 acc = q_from_m(0);
+        for (size_t r = 0; r < nr; r++) {
+            q31 e = q_from_m(1);
+            for (unsigned k = 0; k < log_rows; k++) {
+                size_t bit = (r >> (log_rows - 1 - k)) & 1;
+                e = q_mul(e, bit ? point[k] : q_sub(q_from_m(1), point[k]));
+            }
+            acc = q_add(acc, q_mul_m(e, (uint32_t)(in_u64(&in) % MP)));
+        }
+        if (!q_eq(acc, rms_sq_eval)) return 0;
+    } else if (has_rows != 0) {
+        return 0;
+    } else if (((size_t)1 << num_vars) / next_pow2(dim) > 1) {
+        return 0;
+    }
+    ch_mix_sf(ch, input_eval);
+    ch_mix_sf(ch, output_eval);
+    if (out_input_eval) q_store(out_input_eval, input_eval);
+    return in.pos == len && !in.bad;
+}

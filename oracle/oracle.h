@@ -137,6 +137,23 @@ int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint
                                 size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
                                 uint32_t out_input_eval[4]);
 
+/* rsqrt table of the RMSNorm / LayerNorm lookups (components/layernorm.rs:116-136). */
+int orc_rsqrt_table(unsigned log_size, uint32_t *out);
+/* reduce_rmsnorm_layer_with_gamma (gkr/prover.rs:8424-8790): RMS^2 plain sumcheck, the
+ * degree-3 eq-sumcheck output = input x scale, and the rsqrt LogUp, serialized as the
+ * LayerProof::RMSNorm record (cairo_serde.rs:1648-1726).  gamma (gamma_len values) is the
+ * optional affine scale (NULL for none); skip_rms_sq mirrors STWO_SKIP_RMS_SQ_PROOF. */
+int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t dim,
+                       const uint32_t *gamma, size_t gamma_len, int skip_rms_sq,
+                       const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                       orc_channel *ch, uint64_t *calldata, size_t cap, size_t *out_len,
+                       uint32_t out_input_eval[4]);
+/* verify_rmsnorm_reduction (gkr/verifier.rs:4693-5080) on such a record; the multiplicity
+ * sumcheck, absent from the calldata, is replayed from the multiplicities.  Returns 1 if accepted. */
+int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const uint32_t *claim_point,
+                       size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
+                       uint32_t out_input_eval[4]);
+
 /* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
 void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
                     uint32_t *c, int threads);

@@ -101,6 +101,24 @@ const std::vector<uint32_t>& activation_table(int tag) {
     return tables[tag];
 }
 
+// rsqrt table of the RMSNorm / LayerNorm lookups (components/layernorm.rs:116-136):
+// 0 -> 2^16 - 1, x -> min(2^16 / floor(sqrt(x)), p - 1); 2^16 entries, built once.
+const std::vector<uint32_t>& rsqrt_table16() {
+    static std::once_flag once;
+    static std::vector<uint32_t> t;
+    std::call_once(once, [] {
+        t.resize((size_t)1 << 16);
+        t[0] = (1u << 16) - 1;
+        uint64_t s = 1;
+        for (uint64_t x = 1; x < t.size(); x++) {
+            while ((s + 1) * (s + 1) <= x) s++;  // s = floor(sqrt(x)), non-decreasing in x
+            const uint64_t r = (1ull << 16) / s;
+            t[x] = (uint32_t)(r < kP - 1 ? r : kP - 1);
+        }
+    });
+    return t;
+}
+
 }  // namespace zk
 
 #include "../../include/zkml_b200.h"

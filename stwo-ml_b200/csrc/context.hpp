@@ -77,11 +77,12 @@ struct KTimer {
 }  // namespace zk
 
 namespace zk {
-// Device scratch of the LogUp activation reduction, kept by the context (grown on demand).
+// Device scratch of the LogUp activation and RMSNorm reductions, kept by the context (grown on demand).
 struct LogupScratch {
     DevBuf x, m_in, m_out, mult, eq, d, w, mv;
+    DevBuf outv, row_rms, pv, gam;  // RMSNorm: output, per-row rms^2, plain-sumcheck vector, affine scale
     void release() {
-        DevBuf* all[] = {&x, &m_in, &m_out, &mult, &eq, &d, &w, &mv};
+        DevBuf* all[] = {&x, &m_in, &m_out, &mult, &eq, &d, &w, &mv, &outv, &row_rms, &pv, &gam};
         for (DevBuf* b : all) b->release();
     }
 };
@@ -108,20 +109,20 @@ struct zkml_ctx {
     zk::DevBuf eq_a, eq_hi, eq_lo;  // eq tables
     zk::DevBuf partials;            // per-block round partials
     zk::DevBuf small;               // ticket + out words + error flag
-    zk::DevBuf act_tables[6];
+    zk::DevBuf act_tables[6];       // activation lookup tables by type tag (device copies)
+    zk::DevBuf rsqrt_table;         // RMSNorm rsqrt table (device copy)
     zk::DevBuf rc_table;
     zk::LogupScratch lu;
     zk::OpeningScratch op;
-    zk::DevBuf gemm_planes;         // byte planes of the forward GEMM's right operand  // kept across calls: cudaMalloc/cudaFree would synchronise the device each call
     zk::DevBuf gather_dev;          // gathered shards of the sharded product sumcheck
     uint8_t* h_stage = nullptr;     // pinned host staging for the sharded gather
-    size_t h_stage_bytes = 0;            // byte-plane eq table of the tensor-pipe column restriction
+    size_t h_stage_bytes = 0;
     // stepwise product-sumcheck session (zkml_sumcheck_*)
     zk::DevBuf sc_a, sc_b;          // staged M31 inputs
     const uint32_t* sc_a32 = nullptr;
     const uint32_t* sc_b32 = nullptr;
     size_t sc_len = 0;              // current vector length (0 = no session)
-    bool sc_m31 = false;            // vectors are still the M31 inputs       // activation lookup tables by type tag (device copies)
+    bool sc_m31 = false;            // vectors are still the M31 inputs
     uint32_t* h_small = nullptr;    // pinned host mirror of `small`
     uint32_t* h_sig = nullptr;      // mapped pinned host words the round kernels publish to
     uint32_t* d_sig = nullptr;      // device alias of h_sig

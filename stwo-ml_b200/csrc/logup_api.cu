@@ -9,6 +9,7 @@
 #include <string>
 #include <vector>
 
+#include "calldata.hpp"
 #include "channel.hpp"
 #include "context.hpp"
 #include "logup.cuh"
@@ -32,27 +33,6 @@ inline unsigned ilog2(size_t x) {
     return l;
 }
 inline qm31 ldq(const uint32_t* p) { return qm(p[0], p[1], p[2], p[3]); }
-
-struct Out {
-    uint64_t* buf;
-    size_t cap, len = 0;
-    bool overflow = false;
-    void push(const uint64_t f[4]) {
-        if (len < cap) memcpy(buf + 4 * len, f, 32);
-        else overflow = true;
-        len++;
-    }
-    void u64(uint64_t x) {
-        const uint64_t f[4] = {x, 0, 0, 0};
-        push(f);
-    }
-    void q(const qm31& v) {
-        u64(v.a);
-        u64(v.b);
-        u64(v.c);
-        u64(v.d);
-    }
-};
 
 }  // namespace
 }  // namespace zk

@@ -4,83 +4,9 @@
 // LogUp sums, eq-weighted dot products, and the degree-3 eq-sumcheck rounds
 // (s(t) = sum eq_t w_t d_t at t = 0..3) with the fold of eq, w and d fused in.
 #include "logup.cuh"
-#include "round_arith.cuh"
+#include "logup_device.cuh"
 
 namespace zk {
-
-__device__ __forceinline__ qm31 ldq4(const uint4* p) {
-    uint4 v = *p;
-    return qm(v.x, v.y, v.z, v.w);
-}
-__device__ __forceinline__ void stq4(uint4* p, qm31 x) { *p = make_uint4(x.a, x.b, x.c, x.d); }
-
-__device__ __forceinline__ void publish_words(uint32_t* sig, uint32_t seq, const uint32_t* words, int n) {
-    volatile uint32_t* v = sig;
-    for (int i = 0; i < n; i++) v[1 + i] = words[i];
-    // the release store orders the word stores before the sequence number
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig), "r"(seq) : "memory");
-}
-
-// Grid reduction of NW lazily accumulated words (each accumulator is a sum of
-// values < P): per-block partials, then the last block (atomic ticket) reduces
-// them, stores the NW reduced words to out and optionally publishes them.
-template <int NW>
-__device__ void grid_reduce(unsigned long long (&acc)[NW], const ReduceScratch& rs) {
-    __shared__ uint32_t sh[32][NW];
-    __shared__ uint32_t res[NW];
-    __shared__ bool is_last;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-#pragma unroll
-    for (int i = 0; i < NW; i++) {
-        uint32_t r = red64(acc[i]);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) r = madd(r, __shfl_xor_sync(0xffffffffu, r, off));
-        if (lane == 0) sh[warp][i] = r;
-    }
-    __syncthreads();
-    if (threadIdx.x < NW) {
-        uint32_t a = 0;
-        for (int w = 0; w < nw; w++) a = madd(a, sh[w][threadIdx.x]);
-        rs.partials[blockIdx.x * NW + threadIdx.x] = a;
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = (atomicAdd(rs.ticket, 1u) == gridDim.x - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    for (int i = warp; i < NW; i += nw) {
-        unsigned long long a = 0;
-        for (unsigned b = lane; b < gridDim.x; b += 32) a += __ldcg(rs.partials + b * NW + i);
-        uint32_t v = red64(a);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if (lane == 0) {
-            rs.out[i] = v;
-            res[i] = v;
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        *rs.ticket = 0;
-        if (rs.sig) publish_words(rs.sig, rs.seq, res, NW);
-    }
-}
-
-template <int NW>
-__device__ __forceinline__ void acc_q(unsigned long long (&acc)[NW], int at, const qm31& x) {
-    acc[at] += x.a;
-    acc[at + 1] += x.b;
-    acc[at + 2] += x.c;
-    acc[at + 3] += x.d;
-}
-
-static unsigned grid_for(size_t work, int max_blocks) {
-    size_t b = (work + 255) / 256;
-    if (b > (size_t)max_blocks) b = max_blocks;
-    if (b == 0) b = 1;
-    return (unsigned)b;
-}
 
 // ---------------------------------------------------------------------------
 __global__ void logup_prepare_kernel(const uint32_t* __restrict__ input, uint32_t rows, uint32_t cols, size_t pc,
@@ -122,13 +48,6 @@ void launch_logup_prepare(const uint32_t* input, uint32_t rows, uint32_t cols, s
 // backward pass (three products per element).  A batch containing d = 0 is
 // inverted element by element, so the result is the same as qinv of each d.
 constexpr int DW_BATCH = 8;
-
-__device__ __forceinline__ qm31 qmul_f(const qm31& x, const qm31& y) {
-    QAcc s;
-    qacc_zero(s);
-    qacc_mul(s, x, y);
-    return qacc_value(s);
-}
 
 __global__ void __launch_bounds__(256) logup_dw_kernel(const uint32_t* __restrict__ m_in,
                                                        const uint32_t* __restrict__ m_out, size_t n, qm31 gamma,
@@ -204,27 +123,42 @@ void launch_logup_table_sum(const uint32_t* mult, const uint32_t* table, size_t 
     logup_table_sum_kernel<<<grid_for(tsize, rs.max_blocks), 256, 0, s>>>(mult, table, tsize, gamma, beta, rs);
 }
 
-// sum_i eq[i] * x[i] for up to three M31 vectors (NV of them): 4 * NV words.
+// sum_i eq[i] * x_v[i] for NV (1..4) M31 vectors: 4 * NV words.
+struct EqDotSrc {
+    const uint32_t* x[4];
+};
+
 template <int NV>
-__global__ void __launch_bounds__(256) eq_dot_kernel(const uint4* __restrict__ eq, const uint32_t* __restrict__ x0,
-                                                     const uint32_t* __restrict__ x1, size_t n, ReduceScratch rs) {
+__global__ void __launch_bounds__(256) eq_dot_kernel(const uint4* __restrict__ eq, const EqDotSrc src, size_t n,
+                                                     ReduceScratch rs) {
     unsigned long long acc[4 * NV];
 #pragma unroll
     for (int i = 0; i < 4 * NV; i++) acc[i] = 0;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const qm31 e = ldq4(eq + i);
-        acc_q<4 * NV>(acc, 0, qmul_m(e, x0[i]));
-        if (NV > 1) acc_q<4 * NV>(acc, 4, qmul_m(e, x1[i]));
+#pragma unroll
+        for (int v = 0; v < NV; v++) acc_q<4 * NV>(acc, 4 * v, qmul_m(e, __ldg(src.x[v] + i)));
     }
     grid_reduce<4 * NV>(acc, rs);
 }
 
+void launch_eq_dot(const uint4* eq, const uint32_t* const* xs, int nv, size_t n, const ReduceScratch& rs,
+                   cudaStream_t s) {
+    EqDotSrc src{};
+    for (int v = 0; v < nv && v < 4; v++) src.x[v] = xs[v];
+    const unsigned g = grid_for(n, rs.max_blocks);
+    switch (nv) {
+        case 1: eq_dot_kernel<1><<<g, 256, 0, s>>>(eq, src, n, rs); break;
+        case 2: eq_dot_kernel<2><<<g, 256, 0, s>>>(eq, src, n, rs); break;
+        case 3: eq_dot_kernel<3><<<g, 256, 0, s>>>(eq, src, n, rs); break;
+        default: eq_dot_kernel<4><<<g, 256, 0, s>>>(eq, src, n, rs); break;
+    }
+}
+
 void launch_eq_dot(const uint4* eq, const uint32_t* x0, const uint32_t* x1, size_t n, const ReduceScratch& rs,
                    cudaStream_t s) {
-    if (x1)
-        eq_dot_kernel<2><<<grid_for(n, rs.max_blocks), 256, 0, s>>>(eq, x0, x1, n, rs);
-    else
-        eq_dot_kernel<1><<<grid_for(n, rs.max_blocks), 256, 0, s>>>(eq, x0, nullptr, n, rs);
+    const uint32_t* xs[2] = {x0, x1};
+    launch_eq_dot(eq, xs, x1 ? 2 : 1, n, rs, s);
 }
 
 // Degree-3 eq-sumcheck round.  With FOLD, first folds (eq, w, d) in place with
@@ -291,16 +225,16 @@ void launch_logup_round(uint4* E, uint4* W, uint4* D, size_t len, bool fold, qm3
     }
 }
 
-// Final fold of length-2 (eq, w, d) vectors: publishes w (4 words).
+// Final fold of length-2 (eq, w, d) vectors: publishes w and d (8 words).
 __global__ void logup_final_kernel(const uint4* E, const uint4* W, const uint4* D, qm31 alpha, ReduceScratch rs) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    const qm31 w0 = ldq4(W), w1 = ldq4(W + 1);
+    const qm31 w0 = ldq4(W), w1 = ldq4(W + 1), d0 = ldq4(D), d1 = ldq4(D + 1);
     const qm31 w = qadd(w0, qmul(alpha, qsub(w1, w0)));
-    const uint32_t words[4] = {w.a, w.b, w.c, w.d};
-    for (int i = 0; i < 4; i++) rs.out[i] = words[i];
-    if (rs.sig) publish_words(rs.sig, rs.seq, words, 4);
+    const qm31 d = qadd(d0, qmul(alpha, qsub(d1, d0)));
+    const uint32_t words[8] = {w.a, w.b, w.c, w.d, d.a, d.b, d.c, d.d};
+    for (int i = 0; i < 8; i++) rs.out[i] = words[i];
+    if (rs.sig) publish_words(rs.sig, rs.seq, words, 8);
     (void)E;
-    (void)D;
 }
 
 void launch_logup_final(const uint4* E, const uint4* W, const uint4* D, qm31 alpha, const ReduceScratch& rs,

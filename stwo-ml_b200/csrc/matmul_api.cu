@@ -710,6 +710,7 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
     for (DevBuf* b : bufs) b->release();
     for (DevBuf& t : ctx->act_tables) t.release();
     ctx->rc_table.release();
+    ctx->rsqrt_table.release();
     ctx->lu.release();
     ctx->op.release();
     ctx->gather_dev.release();

@@ -104,6 +104,9 @@ _SIGS = {
     "zkml_reduce_activation_logup": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int,
                                                C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                                C.c_size_t, C.POINTER(C.c_size_t), _u32]),
+    "zkml_reduce_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
+                                      C.c_size_t, C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
+                                      C.c_size_t, C.POINTER(C.c_size_t), _u32]),
     "zkml_restrict_cols_noalloc": (C.c_int, [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                              C.c_void_p, C.c_size_t, C.c_void_p]),
     "zkml_sumcheck_load_m31": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -651,6 +654,44 @@ def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_t
                                               C.byref(channel.state), out, cap, C.byref(ln), ie))
     proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
     return proof, GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
+
+
+@dataclass
+class RMSNormProof:
+    """LayerProof::RMSNorm record (serialize_gkr_model_proof).  `raw` holds the calldata as
+    4 x u64 limbs per felt; `calldata` converts it to Python integers on first use."""
+    raw: np.ndarray
+    input_eval: np.ndarray   # next claim value
+    output_eval: np.ndarray  # the RMSNorm output MLE at the claim point
+
+    @property
+    def calldata(self) -> List[int]:
+        if not hasattr(self, "_calldata"):
+            self._calldata = _felts(self.raw, self.raw.size // 4)
+        return self._calldata
+
+
+def reduce_rmsnorm_layer(output_claim: GKRClaim, inp: M31Matrix, dim: int, channel: PoseidonChannel,
+                         gamma=None, device: int = 0) -> Tuple[RMSNormProof, GKRClaim]:
+    """gkr/prover.rs:8424-8790 (reduce_rmsnorm_layer_with_gamma).  `gamma` is the optional
+    learned per-column scale (M31 values, numpy or a CUDA tensor); STWO_SKIP_RMS_SQ_PROOF in
+    the environment leaves out the RMS^2 sumcheck, as in the reference."""
+    buf = _Buf(inp.data)
+    gbuf = None if gamma is None else _Buf(gamma)
+    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
+    n_point = len(as_qm31_array(output_claim.point))
+    pr = 1 << max(0, (inp.rows - 1).bit_length())
+    cap = (1 << 16) + pr + 64 + 40 * (n_point + 2)
+    out = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    _check(lib().zkml_reduce_rmsnorm(context(device).handle, buf.ptr, inp.rows, inp.cols, dim,
+                                     None if gbuf is None else gbuf.ptr, 0 if gbuf is None else gbuf.nbytes // 4,
+                                     pt_ptr, n_point, np.ascontiguousarray(output_claim.value, np.uint32),
+                                     C.byref(channel.state), out, cap, C.byref(ln), ie))
+    raw = out[:4 * ln.value].copy()
+    oe = np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)
+    return RMSNormProof(raw, ie, oe), GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
 
 
 # ---------------------------------------------------------------------------

@@ -81,6 +81,10 @@ def lib():
         L.orc_reduce_activation_logup.argtypes = [u32p, sz, sz, C.c_int, u32p, sz, u32p, chp, u64p, sz,
                                                   C.POINTER(sz), u32p]
         L.orc_verify_activation_logup.argtypes = [u64p, sz, u32p, sz, u32p, chp, u32p]
+        L.orc_rsqrt_table.argtypes = [C.c_uint, u32p]
+        L.orc_reduce_rmsnorm.argtypes = [u32p, sz, sz, sz, C.c_void_p, sz, C.c_int, u32p, sz, u32p, chp, u64p,
+                                         sz, C.POINTER(sz), u32p]
+        L.orc_verify_rmsnorm.argtypes = [u64p, sz, sz, u32p, sz, u32p, chp, u32p]
         _lib = L
     return _lib
 
@@ -198,3 +202,37 @@ def verify_activation_logup(raw, point, value, ch):
     ok = lib().orc_verify_activation_logup(np.ascontiguousarray(raw, np.uint64), raw.size // 4, point.reshape(-1),
                                            len(point), np.ascontiguousarray(value, np.uint32), C.byref(ch), ie)
     return bool(ok), ie
+
+
+def rsqrt_table(log_size: int = 16) -> np.ndarray:
+    t = np.zeros(1 << log_size, np.uint32)
+    assert lib().orc_rsqrt_table(log_size, t) == 0
+    return t
+
+
+def reduce_rmsnorm(inp, dim, point, value, ch, gamma=None, skip_rms_sq=False, cap=1 << 18):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    rows, cols = inp.shape
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    g = None if gamma is None else np.ascontiguousarray(gamma, np.uint32)
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    rc = lib().orc_reduce_rmsnorm(inp.reshape(-1), rows, cols, dim,
+                                  None if g is None else g.ctypes.data_as(C.c_void_p), 0 if g is None else g.size,
+                                  int(skip_rms_sq), point.reshape(-1), len(point),
+                                  np.ascontiguousarray(value, np.uint32), C.byref(ch), buf, cap, C.byref(ln), ie)
+    return rc, buf[:4 * ln.value].copy(), ie
+
+
+def verify_rmsnorm(raw, dim, point, value, ch):
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    ie = np.zeros(4, np.uint32)
+    ok = lib().orc_verify_rmsnorm(np.ascontiguousarray(raw, np.uint64), raw.size // 4, dim, point.reshape(-1),
+                                  len(point), np.ascontiguousarray(value, np.uint32), C.byref(ch), ie)
+    return bool(ok), ie
+
+
+def rmsnorm_output_eval(raw) -> np.ndarray:
+    """output_eval of a LayerProof::RMSNorm record (felts 5..8)."""
+    return np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)

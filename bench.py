@@ -451,6 +451,15 @@ def run_case(name):
         pt, val = random_qm31(20, rng), random_qm31(1, rng)[0]
         for _ in range(2):
             Z.reduce_activation_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), 5, Z.PoseidonChannel())
+    elif name.startswith("rmsnorm_"):  # RMSNorm layer R x C (e.g. rmsnorm_64x5120) with an affine scale, twice
+        rows, cols = (int(v) for v in name.split("_")[1].split("x"))
+        x = int_matrix_m31(rows, cols, 3, bound=300)
+        nv = (rows - 1).bit_length() + (cols - 1).bit_length()
+        rng = np.random.default_rng(0)
+        pt, val = random_qm31(nv, rng), random_qm31(1, rng)[0]
+        g = (np.arange(cols, dtype=np.uint32) % 1000) + 1
+        for _ in range(2):
+            Z.reduce_rmsnorm_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), cols, Z.PoseidonChannel(), gamma=g)
     elif name.startswith("la_"):  # native 1 x 2^L . 2^L x 1 reduction (look-ahead rounds), four times
         lg = int(name.split("_")[1])
         be = Z.GpuBackend(0)

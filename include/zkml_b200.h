@@ -212,6 +212,35 @@ int zkml_reduce_rmsnorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_
                         const uint32_t claim_value[4], zkml_channel *ch, uint64_t *out_calldata, size_t cap,
                         size_t *out_len, uint32_t out_input_eval[4]);
 
+/* ---- Aggregated weight binding ------------------------------------------------ */
+
+/* A weight claim of the GKR walk (AggregatedWeightClaim, crypto/aggregated_opening.rs:99-112).
+ * The weight is rows x cols M31, row major, host or device memory; its MLE is the
+ * column-major padded one (matrix_to_mle_col_major_padded) with
+ * n = log2(padded rows * padded cols) variables; eval_point holds n QM31; commitment
+ * is that MLE's Poseidon Merkle root (zkml_weight_commitment), canonical limbs. */
+typedef struct {
+    const uint32_t *weight;
+    size_t rows, cols;
+    size_t matrix_index;
+    const uint32_t *eval_point;
+    uint32_t expected_value[4];
+    uint64_t commitment[4];
+} zkml_weight_claim;
+
+/* commit_mle_root_only(matrix_to_mle_col_major_padded(weight)) (gkr/prover.rs:1137-1139). */
+int zkml_weight_commitment(zkml_ctx *ctx, const uint32_t *weight, size_t rows, size_t cols, uint64_t out_root[4]);
+
+/* prove_aggregated_binding_streaming (crypto/aggregated_opening.rs:1647-1719): super-root
+ * of the claims' commitments, beta weights, the mismatch sumcheck over
+ * log2(next_pow2(n_claims)) + max n variables, the oracle value at the challenge point and
+ * one MLE opening (n_queries queries) of the virtual MLE against the super-root.  Writes
+ * serialize_aggregated_binding_proof (cairo_serde.rs:3884-3921).  Returns
+ * ZKML_ERR_INVALID_ARG if a commitment does not match its weight. */
+int zkml_prove_aggregated_binding(zkml_ctx *ctx, const zkml_weight_claim *claims, size_t n_claims,
+                                  zkml_channel *ch, size_t n_queries, uint64_t *out_calldata, size_t cap,
+                                  size_t *out_len);
+
 /* ---- Forward pass --------------------------------------------------------------
  * C = A * B mod p for M31 matrices (m x k times k x n, row major): the forward
  * GEMM that produces a layer's output (gpu_matmul_m31_full,

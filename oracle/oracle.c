@@ -2205,3 +2205,263 @@ int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const u
     if (out_input_eval) q_store(out_input_eval, input_eval);
     return in.pos == len && !in.bad;
 }
+
+/* ---------------------------------------------------------------------------
+ * Aggregated weight binding (crypto/aggregated_opening.rs).
+ * ------------------------------------------------------------------------- */
+
+typedef struct {
+    unsigned sb, n_max, n_global;
+    size_t m_padded;
+} agg_cfg;
+
+/* AggregatedBindingConfig::from_claims (aggregated_opening.rs:68-97) */
+static int agg_config(const orc_weight_claim *c, size_t m, agg_cfg *cfg, unsigned *nv) {
+    if (m == 0 || m > 256) return 1;
+    cfg->n_max = 0;
+    for (size_t i = 0; i < m; i++) {
+        if (!c[i].rows || !c[i].cols) return 1;
+        nv[i] = ilog2(next_pow2(c[i].rows) * next_pow2(c[i].cols));
+        if (nv[i] == 0 || nv[i] > 30) return 1;
+        if (nv[i] > cfg->n_max) cfg->n_max = nv[i];
+    }
+    cfg->m_padded = next_pow2(m);
+    cfg->sb = ilog2(cfg->m_padded);
+    cfg->n_global = cfg->sb + cfg->n_max;
+    return 0;
+}
+
+/* build_super_root (aggregated_opening.rs:181-227): per-matrix roots extended to n_max
+ * with zero-tree roots, zero-tree padding to m_padded, a Merkle tree on top. */
+static void agg_super_root(const orc_weight_claim *c, size_t m, const unsigned *nv, const agg_cfg *cfg,
+                           fe *subtree /* m_padded */, fe *root) {
+    fe zr[32];
+    felt_of_qm31(&zr[0], q_from_m(0));
+    for (unsigned l = 1; l <= cfg->n_max; l++) pos_hash(&zr[l], &zr[l - 1], &zr[l - 1]);
+    for (size_t i = 0; i < cfg->m_padded; i++) {
+        if (i >= m) {
+            subtree[i] = zr[cfg->n_max];
+            continue;
+        }
+        fe_from_canon(&subtree[i], c[i].commitment);
+        for (unsigned l = nv[i]; l < cfg->n_max; l++) pos_hash(&subtree[i], &subtree[i], &zr[l]);
+    }
+    size_t w = cfg->m_padded;
+    fe *cur = (fe *)malloc(sizeof(fe) * w);
+    memcpy(cur, subtree, sizeof(fe) * w);
+    while (w > 1) {
+        for (size_t i = 0; i < w / 2; i++) pos_hash(&cur[i], &cur[2 * i], &cur[2 * i + 1]);
+        w /= 2;
+    }
+    *root = cur[0];
+    free(cur);
+}
+
+/* global_point (aggregated_opening.rs:328-358): selector bits of matrix_index (MSB first),
+ * zeros up to n_max, then the claim's evaluation point. */
+static void agg_global_point(const orc_weight_claim *c, unsigned nv, const agg_cfg *cfg, q31 *g) {
+    for (unsigned j = 0; j < cfg->sb; j++) g[j] = q_from_m((uint32_t)((c->matrix_index >> (cfg->sb - 1 - j)) & 1));
+    for (unsigned j = 0; j < cfg->n_max - nv; j++) g[cfg->sb + j] = q_from_m(0);
+    for (unsigned j = 0; j < nv; j++) g[cfg->sb + cfg->n_max - nv + j] = q_load(c->eval_point + 4 * j);
+}
+
+/* eval_unified_oracle (aggregated_opening.rs:364-392): sum_k sel(k, t_sel) W_k(last n_k of t_local). */
+static q31 agg_oracle(const q31 *t, q31 *const *mles, const unsigned *nv, size_t m, const agg_cfg *cfg) {
+    q31 res = q_from_m(0), one = q_from_m(1);
+    for (size_t k = 0; k < m; k++) {
+        q31 w = one;
+        for (unsigned j = 0; j < cfg->sb; j++) {
+            int bit = (int)((k >> (cfg->sb - 1 - j)) & 1);
+            w = q_mul(w, bit ? t[j] : q_sub(one, t[j]));
+        }
+        if (q_eq(w, q_from_m(0))) continue;
+        q31 v = mle_eval_copy(mles[k], (size_t)1 << nv[k], t + cfg->sb + cfg->n_max - nv[k], nv[k]);
+        res = q_add(res, q_mul(w, v));
+    }
+    return res;
+}
+
+static q31 *weight_mle_col_major(const orc_weight_claim *c) {
+    size_t pr = next_pow2(c->rows), pc = next_pow2(c->cols);
+    q31 *v = (q31 *)calloc(pr * pc, sizeof(q31));
+    for (size_t i = 0; i < c->rows; i++)
+        for (size_t j = 0; j < c->cols; j++) v[j * pr + i] = q_from_m(m_red64(c->weight[i * c->cols + j]));
+    return v;
+}
+
+void orc_weight_commitment(const uint32_t *weight, size_t rows, size_t cols, uint64_t out[4], int threads) {
+    orc_weight_claim c = {weight, rows, cols, 0, NULL, {0, 0, 0, 0}, {0, 0, 0, 0}};
+    q31 *v = weight_mle_col_major(&c);
+    orc_merkle_root_qm31((const uint32_t *)v, next_pow2(rows) * next_pow2(cols), out, threads);
+    free(v);
+}
+
+int orc_prove_aggregated_binding(const orc_weight_claim *claims, size_t m, orc_channel *ch, size_t n_queries,
+                                 uint64_t *calldata, size_t cap, size_t *out_len, int threads) {
+    oracle_init();
+    agg_cfg cfg;
+    unsigned nv[256];
+    if (agg_config(claims, m, &cfg, nv)) return 1;
+    const unsigned n = cfg.n_global;
+    q31 *mles[256];
+    for (size_t k = 0; k < m; k++) mles[k] = weight_mle_col_major(&claims[k]);
+    fe *subtree = (fe *)malloc(sizeof(fe) * cfg.m_padded), root;
+    agg_super_root(claims, m, nv, &cfg, subtree, &root);
+    orc_ch_mix_felt(ch, root.v);
+    /* draw_beta_weights (aggregated_opening.rs:395-405) */
+    q31 rho = ch_draw_qm31(ch), *beta = (q31 *)malloc(sizeof(q31) * m), pw = q_from_m(1);
+    for (size_t i = 0; i < m; i++) {
+        beta[i] = pw;
+        pw = q_mul(pw, rho);
+    }
+    q31 *g = (q31 *)malloc(sizeof(q31) * m * n), *pre = (q31 *)malloc(sizeof(q31) * m);
+    for (size_t i = 0; i < m; i++) {
+        agg_global_point(&claims[i], nv[i], &cfg, g + i * n);
+        pre[i] = q_from_m(1);
+    }
+    /* mismatch_sumcheck (aggregated_opening.rs:412-510, 517-625) */
+    q31 *chal = (q31 *)malloc(sizeof(q31) * (n + 1)), *pt = (q31 *)malloc(sizeof(q31) * n);
+    q31 *rp = (q31 *)malloc(sizeof(q31) * 3 * n), one = q_from_m(1);
+    uint32_t inv2 = m_inv(2);
+    for (unsigned j = 0; j < n; j++) {
+        q31 s[3];
+        for (uint32_t x = 0; x < 3; x++) {
+            q31 tot = q_from_m(0), X = q_from_m(x);
+            for (size_t i = 0; i < m; i++) {
+                const q31 *gi = g + i * n;
+                q31 eqr = q_add(q_mul(gi[j], X), q_mul(q_sub(one, gi[j]), q_sub(one, X)));
+                memcpy(pt, chal, sizeof(q31) * j);
+                pt[j] = X;
+                memcpy(pt + j + 1, gi + j + 1, sizeof(q31) * (n - j - 1));
+                q31 mis = q_sub(agg_oracle(pt, mles, nv, m, &cfg), q_load(claims[i].expected_value));
+                tot = q_add(tot, q_mul(q_mul(q_mul(beta[i], pre[i]), eqr), mis));
+            }
+            s[x] = tot;
+        }
+        q31 c0 = s[0], c2 = q_mul_m(q_add(q_sub(s[0], q_add(s[1], s[1])), s[2]), inv2);
+        q31 c1 = q_sub(q_sub(s[1], s[0]), c2);
+        uint32_t cw[12];
+        q_store(cw, c0);
+        q_store(cw + 4, c1);
+        q_store(cw + 8, c2);
+        orc_ch_mix_poly_coeffs(ch, cw);
+        rp[3 * j] = c0;
+        rp[3 * j + 1] = c1;
+        rp[3 * j + 2] = c2;
+        chal[j] = ch_draw_qm31(ch);
+        for (size_t i = 0; i < m; i++) {
+            q31 gv = g[i * n + j];
+            pre[i] = q_mul(pre[i], q_add(q_mul(chal[j], gv), q_mul(q_sub(one, chal[j]), q_sub(one, gv))));
+        }
+    }
+    q31 oracle_eval = agg_oracle(chal, mles, nv, m, &cfg);
+    {
+        uint32_t w[4];
+        q_store(w, oracle_eval);
+        orc_ch_mix_felts(ch, w, 1);
+    }
+    /* serialize_aggregated_binding_proof (cairo_serde.rs:3884-3921) */
+    felt_out o = {calldata, 0, cap, 0};
+    out_u64(&o, cfg.sb);
+    out_u64(&o, cfg.n_max);
+    out_u64(&o, cfg.m_padded);
+    out_u64(&o, cfg.n_global);
+    out_u64(&o, m);
+    out_u64(&o, n);
+    for (unsigned j = 0; j < 3 * n; j++) out_qm31(&o, rp[j]);
+    out_qm31(&o, oracle_eval);
+    out_push(&o, &root);
+    out_u64(&o, cfg.m_padded);
+    for (size_t i = 0; i < cfg.m_padded; i++) out_push(&o, &subtree[i]);
+    /* virtual MLE (build_virtual_mle, aggregated_opening.rs:631-652) opened at the challenges */
+    size_t total = (size_t)1 << n, slot = (size_t)1 << cfg.n_max;
+    q31 *virt = (q31 *)calloc(total, sizeof(q31));
+    for (size_t k = 0; k < m; k++) memcpy(virt + k * slot, mles[k], sizeof(q31) << nv[k]);
+    uint64_t com[4];
+    size_t olen = 0;
+    int rc = orc_prove_mle_opening((const uint32_t *)virt, n, (const uint32_t *)chal, ch, n_queries, com,
+                                   calldata ? calldata + 4 * (o.len < cap ? o.len : cap) : NULL,
+                                   o.len < cap ? cap - o.len : 0, &olen, threads);
+    if (rc == 0 && memcmp(com, root.v, 32) != 0) rc = 4; /* commitments do not match the weights */
+    *out_len = o.len + olen;
+    free(virt);
+    free(rp);
+    free(pt);
+    free(chal);
+    free(pre);
+    free(g);
+    free(beta);
+    free(subtree);
+    for (size_t k = 0; k < m; k++) free(mles[k]);
+    if (rc) return rc;
+    return (o.overflow || *out_len > cap) ? 2 : 0;
+}
+
+int orc_verify_aggregated_binding(const orc_weight_claim *claims, size_t m, const uint64_t *calldata, size_t len,
+                                  orc_channel *ch, size_t n_queries) {
+    oracle_init();
+    agg_cfg cfg;
+    unsigned nv[256];
+    if (agg_config(claims, m, &cfg, nv)) return 0;
+    felt_in in = {calldata, len, 0, 0};
+    if (in_u64(&in) != cfg.sb || in_u64(&in) != cfg.n_max || in_u64(&in) != cfg.m_padded ||
+        in_u64(&in) != cfg.n_global || in_u64(&in) != m)
+        return 0;
+    const unsigned n = cfg.n_global;
+    if (in_u64(&in) != n || in.bad) return 0;
+    size_t rounds_at = in.pos;
+    in.pos += 12 * (size_t)n;
+    q31 oracle_eval = in_qm31(&in);
+    fe root_s, root, *subtree = (fe *)malloc(sizeof(fe) * cfg.m_padded);
+    in_felt(&in, &root_s);
+    agg_super_root(claims, m, nv, &cfg, subtree, &root);
+    int ok = !memcmp(root.v, root_s.v, 32) && in_u64(&in) == cfg.m_padded;
+    for (size_t i = 0; ok && i < cfg.m_padded; i++) {
+        fe f;
+        in_felt(&in, &f);
+        ok = !memcmp(f.v, subtree[i].v, 32);
+    }
+    free(subtree);
+    if (!ok || in.bad) return 0;
+    /* verify_aggregated_binding (aggregated_opening.rs:1774-1905), legacy single-opening path */
+    orc_ch_mix_felt(ch, root.v);
+    q31 rho = ch_draw_qm31(ch), *beta = (q31 *)malloc(sizeof(q31) * m), pw = q_from_m(1);
+    for (size_t i = 0; i < m; i++) {
+        beta[i] = pw;
+        pw = q_mul(pw, rho);
+    }
+    felt_in rin = {calldata, len, rounds_at, 0};
+    q31 cur = q_from_m(0), *chal = (q31 *)malloc(sizeof(q31) * (n + 1));
+    for (unsigned j = 0; j < n && ok; j++) {
+        q31 c0 = in_qm31(&rin), c1 = in_qm31(&rin), c2 = in_qm31(&rin);
+        if (!q_eq(q_add(c0, q_add(q_add(c0, c1), c2)), cur)) ok = 0;
+        uint32_t cw[12];
+        q_store(cw, c0);
+        q_store(cw + 4, c1);
+        q_store(cw + 8, c2);
+        orc_ch_mix_poly_coeffs(ch, cw);
+        chal[j] = ch_draw_qm31(ch);
+        cur = q_add(c0, q_mul(chal[j], q_add(c1, q_mul(chal[j], c2))));
+    }
+    if (ok) {
+        q31 *g = (q31 *)malloc(sizeof(q31) * n), vs = q_from_m(0);
+        for (size_t i = 0; i < m; i++) {
+            agg_global_point(&claims[i], nv[i], &cfg, g);
+            vs = q_add(vs, q_mul(q_mul(beta[i], eq_eval(g, chal, n)),
+                                 q_sub(oracle_eval, q_load(claims[i].expected_value))));
+        }
+        free(g);
+        ok = q_eq(vs, cur);
+    }
+    if (ok) {
+        uint32_t w[4];
+        q_store(w, oracle_eval);
+        orc_ch_mix_felts(ch, w, 1);
+        uint32_t fin[4];
+        ok = orc_verify_mle_opening(root.v, calldata + 4 * in.pos, len - in.pos, (const uint32_t *)chal, n, ch,
+                                    n_queries, fin);
+    }
+    free(chal);
+    free(beta);
+    return ok;
+}

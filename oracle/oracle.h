@@ -154,6 +154,29 @@ int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const u
                        size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
                        uint32_t out_input_eval[4]);
 
+/* A weight claim of the aggregated binding (crypto/aggregated_opening.rs:99-112): the
+ * weight matrix (rows x cols M31, row major; its MLE is the column-major padded one,
+ * local_n_vars = log2(padded rows * padded cols)), its index in the binding, the
+ * evaluation point (local_n_vars QM31), the claimed value and the Merkle commitment. */
+typedef struct {
+    const uint32_t *weight;
+    size_t rows, cols;
+    size_t matrix_index;
+    const uint32_t *eval_point;
+    uint32_t expected_value[4];
+    uint64_t commitment[4];
+} orc_weight_claim;
+/* commit_mle_root_only of matrix_to_mle_col_major_padded (gkr/prover.rs:1137-1139). */
+void orc_weight_commitment(const uint32_t *weight, size_t rows, size_t cols, uint64_t out[4], int threads);
+/* prove_aggregated_binding (aggregated_opening.rs:681-730), serialized by
+ * serialize_aggregated_binding_proof (cairo_serde.rs:3884-3921).  Returns 4 if the
+ * commitments do not match the weights. */
+int orc_prove_aggregated_binding(const orc_weight_claim *claims, size_t m, orc_channel *ch, size_t n_queries,
+                                 uint64_t *calldata, size_t cap, size_t *out_len, int threads);
+/* verify_aggregated_binding (aggregated_opening.rs:1774-1905) on such a record (weights unused). */
+int orc_verify_aggregated_binding(const orc_weight_claim *claims, size_t m, const uint64_t *calldata,
+                                  size_t len, orc_channel *ch, size_t n_queries);
+
 /* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
 void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
                     uint32_t *c, int threads);

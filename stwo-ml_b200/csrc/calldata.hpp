@@ -21,6 +21,9 @@ struct Out {
         const uint64_t f[4] = {x, 0, 0, 0};
         push(f);
     }
+    void qm(const uint32_t v[4]) {
+        for (int i = 0; i < 4; i++) u64(v[i]);
+    }
     void q(const qm31& v) {
         u64(v.a);
         u64(v.b);
@@ -28,5 +31,7 @@ struct Out {
         u64(v.d);
     }
 };
+
+typedef Out FeltOut;
 
 }  // namespace zk

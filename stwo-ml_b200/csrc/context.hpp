@@ -37,10 +37,15 @@ struct DevBuf {
 // `overlap`, if set, runs on the host right after the first GPU launches
 // (before the host waits for the first round), for transcript work that does
 // not depend on GPU results.
+// `adjust`, if set, edits round r's sums (s(0), s(1), s(2), 12 words) before they are
+// interpolated and mixed, and `challenge` receives round r's challenge: together they let a
+// caller run a sumcheck of (sum A B) - (a host-known polynomial of degree <= 2 per round).
 struct ClaimHook {
     void (*fn)(void* arg, const qm31& claimed_sum);
     void* arg;
     void (*overlap)(void* arg) = nullptr;
+    void (*adjust)(void* arg, unsigned r, uint32_t s12[12]) = nullptr;
+    void (*challenge)(void* arg, unsigned r, const qm31& alpha) = nullptr;
 };
 
 int reduce_matmul_internal(::zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size_t a_cols, const uint32_t* b,

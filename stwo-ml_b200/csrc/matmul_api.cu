@@ -263,6 +263,7 @@ static int run_sumcheck_persistent(zkml_ctx* ctx, uint4* A, uint4* B, const uint
     for (unsigned r = 0; r < log_k; r++) {
         if ((rc = wait_signal(ctx, pa.seq_base + r, words, 12))) break;
         if (r == 0 && hook && hook->fn) hook->fn(hook->arg, qadd(ldq(words), ldq(words + 4)));
+        if (hook && hook->adjust) hook->adjust(hook->arg, r, words);
         qm31 c0, c1, c2, alpha;
         {
             HostTimer ht(ctx, KC_HOST_CHANNEL);
@@ -270,6 +271,7 @@ static int run_sumcheck_persistent(zkml_ctx* ctx, uint4* A, uint4* B, const uint
             ch.mix_poly_coeffs(c0, c1, c2);
             alpha = ch.draw_qm31();
         }
+        if (hook && hook->challenge) hook->challenge(hook->arg, r, alpha);
         post_challenge(ctx, pa.seq_base + r, alpha, false);
         if (out_rp) {
             stq(out_rp + 12 * r, c0);
@@ -496,10 +498,14 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
         qm31 c0, c1, c2, alpha;
         {
             HostTimer ht(ctx, KC_HOST_CHANNEL);
-            interpolate(s12, c0, c1, c2);
+            uint32_t adj[12];  // s12 stays the raw sums: the look-ahead check compares them
+            memcpy(adj, s12, sizeof(adj));
+            if (hook && hook->adjust) hook->adjust(hook->arg, r, adj);
+            interpolate(adj, c0, c1, c2);
             ch.mix_poly_coeffs(c0, c1, c2);
             alpha = ch.draw_qm31();
         }
+        if (hook && hook->challenge) hook->challenge(hook->arg, r, alpha);
         if (out_rp) {
             stq(out_rp + 12 * r, c0);
             stq(out_rp + 12 * r + 4, c1);

@@ -11,10 +11,12 @@
 #include <string>
 #include <vector>
 
+#include "calldata.hpp"
 #include "channel.hpp"
 #include "context.hpp"
 #include "gkr.cuh"
 #include "merkle.cuh"
+#include "opening.hpp"
 
 namespace zk {
 
@@ -60,23 +62,7 @@ inline void canon_qm31_felt(const uint32_t v[4], uint64_t out[4]) {
     f_to_canon(felt_of_qm31(qm(v[0], v[1], v[2], v[3])), out);
 }
 
-struct FeltOut {
-    uint64_t* buf;
-    size_t cap, len = 0;
-    bool overflow = false;
-    void push(const uint64_t f[4]) {
-        if (len < cap) memcpy(buf + 4 * len, f, 32);
-        else overflow = true;
-        len++;
-    }
-    void u64(uint64_t x) {
-        uint64_t f[4] = {x, 0, 0, 0};
-        push(f);
-    }
-    void qm(const uint32_t v[4]) {
-        for (int i = 0; i < 4; i++) u64(v[i]);
-    }
-};
+}  // namespace
 
 // Proves the opening of the MLE `evals` (device, 2^n_vars QM31) at `point`,
 // appending the serialized MleOpeningProof to `out`.  Advances `chs`.
@@ -223,7 +209,6 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
     return ZKML_OK;
 }
 
-}  // namespace
 }  // namespace zk
 
 using namespace zk;

@@ -107,6 +107,9 @@ _SIGS = {
     "zkml_reduce_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
                                       C.c_size_t, C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                       C.c_size_t, C.POINTER(C.c_size_t), _u32]),
+    "zkml_weight_commitment": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, _u64]),
+    "zkml_prove_aggregated_binding": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(_Channel),
+                                                C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),
     "zkml_restrict_cols_noalloc": (C.c_int, [C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                              C.c_void_p, C.c_size_t, C.c_void_p]),
     "zkml_sumcheck_load_m31": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
@@ -692,6 +695,77 @@ def reduce_rmsnorm_layer(output_claim: GKRClaim, inp: M31Matrix, dim: int, chann
     raw = out[:4 * ln.value].copy()
     oe = np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)
     return RMSNormProof(raw, ie, oe), GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
+
+
+# ---------------------------------------------------------------------------
+# Aggregated weight binding
+# ---------------------------------------------------------------------------
+
+class _WeightClaim(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("rows", C.c_size_t), ("cols", C.c_size_t),
+                ("matrix_index", C.c_size_t), ("eval_point", C.c_void_p),
+                ("expected_value", C.c_uint32 * 4), ("commitment", C.c_uint64 * 4)]
+
+
+def weight_commitment(weight, device: int = 0) -> int:
+    """commit_mle_root_only(matrix_to_mle_col_major_padded(weight)) (gkr/prover.rs:1137-1139)."""
+    wm = as_matrix(weight)
+    buf = _Buf(wm.data)
+    out = np.zeros(4, np.uint64)
+    _check(lib().zkml_weight_commitment(context(device).handle, buf.ptr, wm.rows, wm.cols, out))
+    return limbs_to_felt(out)
+
+
+@dataclass
+class AggregatedWeightClaim:
+    """crypto/aggregated_opening.rs:99-112, carrying its weight matrix (the reference's
+    WeightSource supplies it separately)."""
+    weight: object            # M31Matrix, numpy (rows, cols) or a CUDA tensor
+    matrix_index: int
+    eval_point: object        # (n, 4) QM31, n = log2(padded rows * padded cols)
+    expected_value: object    # (4,) QM31
+    commitment: int           # weight_commitment(weight)
+
+
+@dataclass
+class AggregatedBindingProof:
+    """serialize_aggregated_binding_proof layout; `raw` is 4 x u64 limbs per felt."""
+    raw: np.ndarray
+
+    @property
+    def calldata(self) -> List[int]:
+        return _felts(self.raw, self.raw.size // 4)
+
+
+def prove_aggregated_binding(claims: List[AggregatedWeightClaim], channel: PoseidonChannel,
+                             n_queries: Optional[int] = None, device: int = 0) -> AggregatedBindingProof:
+    """prove_aggregated_binding_streaming (crypto/aggregated_opening.rs:1647-1719)."""
+    keep = []
+    arr = (_WeightClaim * len(claims))()
+    n_max = 0
+    for i, c in enumerate(claims):
+        wm = as_matrix(c.weight)
+        wb = _Buf(wm.data)
+        pt = np.ascontiguousarray(as_qm31_array(c.eval_point), np.uint32)
+        keep += [wb, pt]
+        arr[i].weight = wb.ptr.value
+        arr[i].rows, arr[i].cols = wm.rows, wm.cols
+        arr[i].matrix_index = c.matrix_index
+        arr[i].eval_point = pt.ctypes.data if pt.size else None
+        v = np.asarray(c.expected_value, np.uint32).reshape(4)
+        limbs = felt_to_limbs(c.commitment)
+        for j in range(4):
+            arr[i].expected_value[j] = int(v[j])
+            arr[i].commitment[j] = int(limbs[j])
+        n_max = max(n_max, _log2(_next_pow2(wm.rows)) + _log2(_next_pow2(wm.cols)))
+    nq = mle_n_queries() if n_queries is None else n_queries
+    ng = n_max + _log2(_next_pow2(len(claims)))
+    cap = 64 + 12 * ng + _next_pow2(len(claims)) + (nq + 1) * (2 + ng * (10 + 2 * (ng + 1)))
+    out = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    _check(lib().zkml_prove_aggregated_binding(context(device).handle, C.cast(arr, C.c_void_p), len(claims),
+                                               C.byref(channel.state), nq, out, cap, C.byref(ln)))
+    return AggregatedBindingProof(out[:4 * ln.value].copy())
 
 
 # ---------------------------------------------------------------------------

@@ -81,6 +81,9 @@ def lib():
         L.orc_reduce_activation_logup.argtypes = [u32p, sz, sz, C.c_int, u32p, sz, u32p, chp, u64p, sz,
                                                   C.POINTER(sz), u32p]
         L.orc_verify_activation_logup.argtypes = [u64p, sz, u32p, sz, u32p, chp, u32p]
+        L.orc_weight_commitment.argtypes = [u32p, sz, sz, u64p, C.c_int]
+        L.orc_prove_aggregated_binding.argtypes = [C.c_void_p, sz, chp, sz, u64p, sz, C.POINTER(sz), C.c_int]
+        L.orc_verify_aggregated_binding.argtypes = [C.c_void_p, sz, u64p, sz, chp, sz]
         L.orc_rsqrt_table.argtypes = [C.c_uint, u32p]
         L.orc_reduce_rmsnorm.argtypes = [u32p, sz, sz, sz, C.c_void_p, sz, C.c_int, u32p, sz, u32p, chp, u64p,
                                          sz, C.POINTER(sz), u32p]
@@ -236,3 +239,70 @@ def verify_rmsnorm(raw, dim, point, value, ch):
 def rmsnorm_output_eval(raw) -> np.ndarray:
     """output_eval of a LayerProof::RMSNorm record (felts 5..8)."""
     return np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)
+
+
+class WeightClaim(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("rows", C.c_size_t), ("cols", C.c_size_t),
+                ("matrix_index", C.c_size_t), ("eval_point", C.c_void_p),
+                ("expected_value", C.c_uint32 * 4), ("commitment", C.c_uint64 * 4)]
+
+
+def weight_commitment(w) -> np.ndarray:
+    w = np.ascontiguousarray(w, np.uint32)
+    out = np.zeros(4, np.uint64)
+    lib().orc_weight_commitment(w.reshape(-1), w.shape[0], w.shape[1], out, threads())
+    return out
+
+
+def make_claims(specs):
+    """specs: list of (weight matrix, matrix_index, eval_point (n, 4), value (4,), commitment (4,) u64).
+    Returns the ctypes array and the arrays it points into (keep both alive)."""
+    keep = []
+    arr = (WeightClaim * len(specs))()
+    for i, (w, idx, pt, val, com) in enumerate(specs):
+        w = np.ascontiguousarray(w, np.uint32)
+        pt = np.ascontiguousarray(pt, np.uint32).reshape(-1)
+        keep += [w, pt]
+        arr[i].weight = w.ctypes.data
+        arr[i].rows, arr[i].cols = w.shape
+        arr[i].matrix_index = idx
+        arr[i].eval_point = pt.ctypes.data if pt.size else None
+        for j in range(4):
+            arr[i].expected_value[j] = int(val[j])
+            arr[i].commitment[j] = int(com[j])
+    return arr, keep
+
+
+def prove_aggregated_binding(specs, ch, n_queries=10, cap=1 << 20):
+    arr, keep = make_claims(specs)
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    rc = lib().orc_prove_aggregated_binding(C.cast(arr, C.c_void_p), len(specs), C.byref(ch), n_queries, buf, cap,
+                                            C.byref(ln), threads())
+    return rc, buf[:4 * ln.value].copy()
+
+
+def verify_aggregated_binding(specs, raw, ch, n_queries=10):
+    arr, keep = make_claims(specs)
+    return bool(lib().orc_verify_aggregated_binding(C.cast(arr, C.c_void_p), len(specs),
+                                                    np.ascontiguousarray(raw, np.uint64), raw.size // 4,
+                                                    C.byref(ch), n_queries))
+
+
+def mle_col_major(w) -> np.ndarray:
+    """matrix_to_mle_col_major_padded as (n, 4) QM31 words."""
+    rows, cols = w.shape
+    pr, pc = 1 << max(0, (rows - 1).bit_length()), 1 << max(0, (cols - 1).bit_length())
+    v = np.zeros((pc, pr), np.uint32)
+    v[:cols, :rows] = np.asarray(w, np.uint32).T % np.uint32((1 << 31) - 1)
+    out = np.zeros((pr * pc, 4), np.uint32)
+    out[:, 0] = v.reshape(-1)
+    return out
+
+
+def evaluate_mle(evals, point) -> np.ndarray:
+    evals = np.ascontiguousarray(evals, np.uint32).reshape(-1, 4)
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    out = np.zeros(4, np.uint32)
+    lib().orc_evaluate_mle(evals.reshape(-1), len(point), point.reshape(-1), out)
+    return out

@@ -212,6 +212,18 @@ int zkml_reduce_rmsnorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_
                         const uint32_t claim_value[4], zkml_channel *ch, uint64_t *out_calldata, size_t cap,
                         size_t *out_len, uint32_t out_input_eval[4]);
 
+/* reduce_activation_layer_piecewise (gkr/prover.rs:7006-7228), the default proof of a
+ * non-ReLU activation layer (STWO_PIECEWISE_ACTIVATION unset): the activation as 16
+ * linear segments of the M31 domain (components/activation.rs:269-358), one degree-3
+ * eq-sumcheck over the combined segment constraints with eta powers.  Writes the
+ * LayerProof::Activation record with the piecewise proof (cairo_serde.rs:1355-1387,
+ * 1249-1300), the input evaluation and, if out_point is set, the next claim's point
+ * (log2(padded size) QM31: the sumcheck challenges). */
+int zkml_reduce_activation_piecewise(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_t cols, int tag,
+                                     const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                                     zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
+                                     uint32_t out_input_eval[4], uint32_t *out_point);
+
 /* ---- Aggregated weight binding ------------------------------------------------ */
 
 /* A weight claim of the GKR walk (AggregatedWeightClaim, crypto/aggregated_opening.rs:99-112).

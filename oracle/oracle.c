@@ -2465,3 +2465,240 @@ int orc_verify_aggregated_binding(const orc_weight_claim *claims, size_t m, cons
     free(beta);
     return ok;
 }
+
+/* ---------------------------------------------------------------------------
+ * Piecewise-linear algebraic activation (the default non-ReLU activation path).
+ * ------------------------------------------------------------------------- */
+
+/* sigmoid_integer (components/integer_math.rs:288-315), C integer division (truncating, as Rust). */
+static int64_t pw_sigmoid(int64_t x, int64_t scale) {
+    int64_t x5 = scale * 5, x25 = scale * 5 / 2;
+    if (x <= -x5) return 0;
+    if (x >= x5) return scale;
+    if (x <= -x25) {
+        int64_t dx = x + x5;
+        return (dx * 28) / (1000 * (x5 - x25) / scale);
+    }
+    if (x >= x25) {
+        int64_t dx = x - x25;
+        int64_t base = scale * 93 / 100;
+        return base + (dx * 7) / (100 * (x5 - x25) / scale);
+    }
+    return scale / 2 + x / 4;
+}
+
+/* apply_activation_integer (components/integer_math.rs:212-263); act: 0 ReLU, 1 GELU,
+ * 2 Sigmoid, 3 Softmax-exp, 4 SiLU. */
+uint32_t orc_activation_integer(int act, uint32_t val) {
+    const uint32_t P31 = 0x7FFFFFFFu, half_p = P31 / 2;
+    int64_t s = val <= half_p ? (int64_t)val : (int64_t)val - (int64_t)P31;
+    int64_t scale = half_p, r;
+    switch (act) {
+    case 0: r = s > 0 ? s : 0; break;
+    case 1: { /* gelu_integer, integer_math.rs:268-276 */
+        int64_t arg = (s * 1702) / 1000;
+        r = (s * pw_sigmoid(arg, scale)) / scale;
+        break;
+    }
+    case 2: r = pw_sigmoid(s, scale); break;
+    case 3: { /* exp_activation_integer, integer_math.rs:318-331 */
+        int64_t res = scale, term = s;
+        res += term;
+        for (int64_t k = 2; k <= 8; k++) {
+            term = (term * s) / (k * scale);
+            res += term;
+            if ((term < 0 ? -term : term) < 2) break;
+        }
+        r = res > 0 ? res : 0;
+        break;
+    }
+    case 4: r = (s * pw_sigmoid(s, scale)) / scale; break;
+    default: r = s;
+    }
+    return (uint32_t)(((r % (int64_t)P31) + (int64_t)P31) % (int64_t)P31);
+}
+
+/* PiecewiseLinearCoeffs::for_activation (components/activation.rs:269-316): 16 segments of
+ * width 2^27; type tag 1..5 (ReLU..SiLU). */
+int orc_piecewise_coeffs(int tag, uint32_t slopes[16], uint32_t intercepts[16]) {
+    if (tag < 1 || tag > 5) return 1;
+    const uint32_t w = 1u << 27;
+    for (uint32_t i = 0; i < 16; i++) {
+        uint32_t xs = i * w, xe = i == 15 ? MP - 1 : (i + 1) * w - 1;
+        uint32_t ys = orc_activation_integer(tag - 1, xs), ye = orc_activation_integer(tag - 1, xe);
+        uint32_t slope = m_mul(m_sub(ye, ys), m_inv(m_sub(xe, xs)));
+        slopes[i] = slope;
+        intercepts[i] = m_sub(ys, m_mul(slope, xs));
+    }
+    return 0;
+}
+
+#define PW_NV 23 /* eq, input, output, 16 indicators, 4 segment bits */
+
+/* compute_piecewise_eq_sum_at_t (gkr/prover.rs:6935-6998) */
+static q31 pw_sum_at(q31 *const *v, size_t mid, uint32_t t, const uint32_t *slopes, const uint32_t *icpt,
+                     const q31 *ep) {
+    q31 sum = q_from_m(0), one = q_from_m(1);
+    for (size_t j = 0; j < mid; j++) {
+        q31 x[PW_NV];
+        for (int k = 0; k < PW_NV; k++) x[k] = q_add(v[k][j], q_mul_m(q_sub(v[k][mid + j], v[k][j]), t));
+        q31 ind_sum = q_from_m(0), pv = q_from_m(0);
+        for (int i = 0; i < 16; i++) {
+            ind_sum = q_add(ind_sum, x[3 + i]);
+            pv = q_add(pv, q_mul(x[3 + i], q_add(q_mul_m(x[1], slopes[i]), q_from_m(icpt[i]))));
+        }
+        q31 h = q_mul(ep[0], q_sub(x[2], pv));
+        h = q_add(h, q_mul(ep[1], q_sub(ind_sum, one)));
+        for (int i = 0; i < 16; i++) h = q_add(h, q_mul(q_mul(ep[2 + i], x[3 + i]), q_sub(one, x[3 + i])));
+        q31 bs = q_from_m(0), is = q_from_m(0);
+        for (int k = 0; k < 4; k++) bs = q_add(bs, q_mul_m(x[19 + k], 1u << k));
+        for (int i = 0; i < 16; i++) is = q_add(is, q_mul_m(x[3 + i], (uint32_t)i));
+        h = q_add(h, q_mul(ep[18], q_sub(bs, is)));
+        for (int k = 0; k < 4; k++) h = q_add(h, q_mul(q_mul(ep[19 + k], x[19 + k]), q_sub(one, x[19 + k])));
+        sum = q_add(sum, q_mul(x[0], h));
+    }
+    return sum;
+}
+
+/* reduce_activation_layer_piecewise (gkr/prover.rs:7006-7228), serialized as the
+ * LayerProof::Activation record (cairo_serde.rs:1355-1387) with the piecewise proof. */
+int orc_reduce_activation_piecewise(const uint32_t *input, size_t rows, size_t cols, int tag,
+                                    const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                                    orc_channel *ch, uint64_t *calldata, size_t cap, size_t *out_len,
+                                    uint32_t out_input_eval[4], uint32_t *out_point) {
+    oracle_init();
+    uint32_t slopes[16], icpt[16];
+    if (orc_piecewise_coeffs(tag, slopes, icpt)) return 1;
+    size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
+    unsigned num_vars = ilog2(n);
+    if (num_vars == 0 || n_point < num_vars) return 1;
+    q31 *v[PW_NV];
+    for (int k = 0; k < PW_NV; k++) v[k] = (q31 *)calloc(n, sizeof(q31));
+    for (size_t i = 0; i < pr; i++)
+        for (size_t j = 0; j < pc; j++) {
+            size_t idx = i * pc + j;
+            uint32_t x = (i < rows && j < cols) ? m_red64(input[i * cols + j]) : 0;
+            uint32_t seg = x >> 27;
+            if (seg > 15) seg = 15;
+            v[1][idx] = q_from_m(x);
+            v[2][idx] = q_from_m(m_add(m_mul(slopes[seg], x), icpt[seg]));
+            v[3 + seg][idx] = q_from_m(1);
+            for (int k = 0; k < 4; k++) v[19 + k][idx] = q_from_m((seg >> k) & 1);
+        }
+    orc_ch_mix_u64(ch, 0x50575F414354ull);
+    orc_ch_mix_u64(ch, (uint64_t)tag);
+    orc_ch_mix_u64(ch, num_vars);
+    ch_mix_sf(ch, q_load(claim_value));
+    q31 eta = ch_draw_qm31(ch), ep[23];
+    ep[0] = q_from_m(1);
+    for (int i = 1; i < 23; i++) ep[i] = q_mul(ep[i - 1], eta);
+    q31 *eq = lagrange_basis((const q31 *)claim_point, num_vars);
+    memcpy(v[0], eq, sizeof(q31) * n);
+    free(eq);
+    q31 *rp = (q31 *)malloc(sizeof(q31) * 4 * num_vars), *chal = (q31 *)malloc(sizeof(q31) * num_vars);
+    uint32_t inv2 = m_inv(2), inv6 = m_inv(6);
+    size_t cur = n;
+    for (unsigned r = 0; r < num_vars; r++) {
+        size_t mid = cur / 2;
+        q31 s0 = pw_sum_at(v, mid, 0, slopes, icpt, ep), s1 = pw_sum_at(v, mid, 1, slopes, icpt, ep);
+        q31 s2 = pw_sum_at(v, mid, 2, slopes, icpt, ep), s3 = pw_sum_at(v, mid, 3, slopes, icpt, ep);
+        q31 d01 = q_sub(s1, s0), d12 = q_sub(s2, s1), d23 = q_sub(s3, s2);
+        q31 d012 = q_mul_m(q_sub(d12, d01), inv2);
+        q31 d0123 = q_mul_m(q_add(q_sub(q_sub(d23, d12), d12), d01), inv6);
+        q31 c0 = s0, c1 = q_add(q_sub(d01, d012), q_mul_m(d0123, 2)), c2 = q_sub(d012, q_mul_m(d0123, 3));
+        q31 c3 = d0123;
+        rp[4 * r] = c0;
+        rp[4 * r + 1] = c1;
+        rp[4 * r + 2] = c2;
+        rp[4 * r + 3] = c3;
+        mix_deg3(ch, c0, c1, c2, c3);
+        chal[r] = ch_draw_qm31(ch);
+        for (int k = 0; k < PW_NV; k++) fold_vec(v[k], mid, chal[r]);
+        cur = mid;
+    }
+    for (int k = 1; k < PW_NV; k++) ch_mix_sf(ch, v[k][0]);
+    felt_out o = {calldata, 0, cap, 0};
+    fe zero;
+    fe_u64(&zero, 0);
+    out_u64(&o, 3);
+    out_u64(&o, (uint64_t)tag);
+    out_qm31(&o, v[1][0]);
+    out_qm31(&o, q_load(claim_value));
+    out_push(&o, &zero);
+    out_u64(&o, 0); /* no LogUp proof */
+    out_u64(&o, 0); /* no multiplicity sumcheck */
+    out_u64(&o, 0); /* no activation product proof */
+    out_u64(&o, 1); /* piecewise proof */
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, rp[4 * r]);
+        out_qm31(&o, rp[4 * r + 2]);
+        out_qm31(&o, rp[4 * r + 3]);
+    }
+    out_qm31(&o, v[1][0]);
+    out_qm31(&o, v[2][0]);
+    for (int i = 0; i < 16; i++) out_qm31(&o, v[3 + i][0]);
+    out_u64(&o, 1); /* segment bits present */
+    for (int k = 0; k < 4; k++) out_qm31(&o, v[19 + k][0]);
+    *out_len = o.len;
+    if (out_input_eval) q_store(out_input_eval, v[1][0]);
+    if (out_point) memcpy(out_point, chal, sizeof(q31) * num_vars);
+    for (int k = 0; k < PW_NV; k++) free(v[k]);
+    free(rp);
+    free(chal);
+    return o.overflow ? 2 : 0;
+}
+
+/* verify_piecewise_activation_reduction (gkr/verifier.rs:3298-3480) on such a record. */
+int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const uint32_t *claim_point,
+                                    size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
+                                    uint32_t out_input_eval[4]) {
+    oracle_init();
+    felt_in in = {calldata, len, 0, 0};
+    if (in_u64(&in) != 3) return 0;
+    int tag = (int)in_u64(&in);
+    uint32_t slopes[16], icpt[16];
+    if (orc_piecewise_coeffs(tag, slopes, icpt)) return 0;
+    q31 input_eval = in_qm31(&in), output_eval = in_qm31(&in);
+    fe tcom;
+    in_felt(&in, &tcom);
+    if (tcom.v[0] | tcom.v[1] | tcom.v[2] | tcom.v[3]) return 0;
+    if (in_u64(&in) != 0 || in_u64(&in) != 0 || in_u64(&in) != 0 || in_u64(&in) != 1) return 0;
+    size_t nv = in_u64(&in);
+    if (nv == 0 || nv > 40 || nv > n_point || in.bad) return 0;
+    if (!q_eq(output_eval, q_load(claim_value))) return 0;
+    orc_ch_mix_u64(ch, 0x50575F414354ull);
+    orc_ch_mix_u64(ch, (uint64_t)tag);
+    orc_ch_mix_u64(ch, nv);
+    ch_mix_sf(ch, q_load(claim_value));
+    q31 eta = ch_draw_qm31(ch), ep[23], one = q_from_m(1);
+    ep[0] = one;
+    for (int i = 1; i < 23; i++) ep[i] = q_mul(ep[i - 1], eta);
+    q31 chal[40];
+    q31 cur = replay_deg3(ch, &in, nv, q_from_m(0), chal);
+    q31 inp = in_qm31(&in), out = in_qm31(&in), ind[16], sb[4];
+    for (int i = 0; i < 16; i++) ind[i] = in_qm31(&in);
+    if (in_u64(&in) != 1) return 0;
+    for (int k = 0; k < 4; k++) sb[k] = in_qm31(&in);
+    if (in.bad || !q_eq(inp, input_eval)) return 0;
+    q31 pv = q_from_m(0), isum = q_from_m(0);
+    for (int i = 0; i < 16; i++) {
+        isum = q_add(isum, ind[i]);
+        pv = q_add(pv, q_mul(ind[i], q_add(q_mul_m(inp, slopes[i]), q_from_m(icpt[i]))));
+    }
+    q31 h = q_mul(ep[0], q_sub(out, pv));
+    h = q_add(h, q_mul(ep[1], q_sub(isum, one)));
+    for (int i = 0; i < 16; i++) h = q_add(h, q_mul(q_mul(ep[2 + i], ind[i]), q_sub(one, ind[i])));
+    q31 bs = q_from_m(0), is = q_from_m(0);
+    for (int k = 0; k < 4; k++) bs = q_add(bs, q_mul_m(sb[k], 1u << k));
+    for (int i = 0; i < 16; i++) is = q_add(is, q_mul_m(ind[i], (uint32_t)i));
+    h = q_add(h, q_mul(ep[18], q_sub(bs, is)));
+    for (int k = 0; k < 4; k++) h = q_add(h, q_mul(q_mul(ep[19 + k], sb[k]), q_sub(one, sb[k])));
+    if (!q_eq(cur, q_mul(eq_eval((const q31 *)claim_point, chal, nv), h))) return 0;
+    ch_mix_sf(ch, inp);
+    ch_mix_sf(ch, out);
+    for (int i = 0; i < 16; i++) ch_mix_sf(ch, ind[i]);
+    for (int k = 0; k < 4; k++) ch_mix_sf(ch, sb[k]);
+    if (out_input_eval) q_store(out_input_eval, input_eval);
+    return in.pos == len;
+}

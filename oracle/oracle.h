@@ -177,6 +177,23 @@ int orc_prove_aggregated_binding(const orc_weight_claim *claims, size_t m, orc_c
 int orc_verify_aggregated_binding(const orc_weight_claim *claims, size_t m, const uint64_t *calldata,
                                   size_t len, orc_channel *ch, size_t n_queries);
 
+/* apply_activation_integer (components/integer_math.rs:212-263), act 0..4 = ReLU..SiLU. */
+uint32_t orc_activation_integer(int act, uint32_t val);
+/* PiecewiseLinearCoeffs::for_activation (components/activation.rs:269-316), tag 1..5. */
+int orc_piecewise_coeffs(int tag, uint32_t slopes[16], uint32_t intercepts[16]);
+/* reduce_activation_layer_piecewise (gkr/prover.rs:7006-7228), serialized as
+ * LayerProof::Activation with the piecewise proof (cairo_serde.rs:1355-1387, 1249-1300).
+ * out_point (num_vars QM31, may be NULL) receives the next claim's point. */
+int orc_reduce_activation_piecewise(const uint32_t *input, size_t rows, size_t cols, int tag,
+                                    const uint32_t *claim_point, size_t n_point,
+                                    const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                                    size_t cap, size_t *out_len, uint32_t out_input_eval[4],
+                                    uint32_t *out_point);
+/* verify_piecewise_activation_reduction (gkr/verifier.rs:3298-3480).  Returns 1 if accepted. */
+int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const uint32_t *claim_point,
+                                    size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
+                                    uint32_t out_input_eval[4]);
+
 /* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
 void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
                     uint32_t *c, int threads);

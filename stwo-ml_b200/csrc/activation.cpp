@@ -101,6 +101,68 @@ const std::vector<uint32_t>& activation_table(int tag) {
     return tables[tag];
 }
 
+// sigmoid_integer (components/integer_math.rs:288-315); C++ division truncates like Rust's.
+static int64_t sigmoid_int(int64_t x, int64_t scale) {
+    const int64_t x5 = scale * 5, x25 = scale * 5 / 2;
+    if (x <= -x5) return 0;
+    if (x >= x5) return scale;
+    if (x <= -x25) return ((x + x5) * 28) / (1000 * (x5 - x25) / scale);
+    if (x >= x25) return scale * 93 / 100 + ((x - x25) * 7) / (100 * (x5 - x25) / scale);
+    return scale / 2 + x / 4;
+}
+
+// apply_activation_integer (components/integer_math.rs:212-263) for type tag 1..5
+// (ReLU, GELU, Sigmoid, Softmax-exp, SiLU): M31 read as signed fixed point with scale
+// (p - 1) / 2, integer-only arithmetic, the result mapped back into [0, p).
+uint32_t activation_integer(int tag, uint32_t val) {
+    const int64_t P31 = 0x7FFFFFFF, half = P31 / 2;
+    const int64_t s = val <= (uint32_t)half ? (int64_t)val : (int64_t)val - P31;
+    int64_t r;
+    switch (tag) {
+        case 1: r = s > 0 ? s : 0; break;
+        case 2: r = (s * sigmoid_int((s * 1702) / 1000, half)) / half; break;
+        case 3: r = sigmoid_int(s, half); break;
+        case 4: {  // exp_activation_integer: Taylor terms until one is below 2 in magnitude
+            int64_t res = half + s, term = s;
+            for (int64_t k = 2; k <= 8; k++) {
+                term = (term * s) / (k * half);
+                res += term;
+                if ((term < 0 ? -term : term) < 2) break;
+            }
+            r = res > 0 ? res : 0;
+            break;
+        }
+        case 5: r = (s * sigmoid_int(s, half)) / half; break;
+        default: r = s;
+    }
+    return (uint32_t)(((r % P31) + P31) % P31);
+}
+
+namespace {
+uint64_t mpow_host(uint64_t b, uint64_t e) {
+    uint64_t r = 1;
+    b %= kP;
+    while (e) {
+        if (e & 1) r = r * b % kP;
+        b = b * b % kP;
+        e >>= 1;
+    }
+    return r;
+}
+}  // namespace
+
+// PiecewiseLinearCoeffs::for_activation (components/activation.rs:269-316): segment i of
+// width 2^27 (the last one ending at p - 1) is the line through its two end points.
+void piecewise_coeffs(int tag, uint32_t slopes[16], uint32_t intercepts[16]) {
+    for (uint32_t i = 0; i < 16; i++) {
+        const uint64_t xs = (uint64_t)i << 27, xe = i == 15 ? kP - 1 : (((uint64_t)i + 1) << 27) - 1;
+        const uint64_t ys = activation_integer(tag, (uint32_t)xs), ye = activation_integer(tag, (uint32_t)xe);
+        const uint64_t slope = (ye + kP - ys) % kP * mpow_host((xe + kP - xs) % kP, kP - 2) % kP;
+        slopes[i] = (uint32_t)slope;
+        intercepts[i] = (uint32_t)((ys + kP - slope * xs % kP) % kP);
+    }
+}
+
 // rsqrt table of the RMSNorm / LayerNorm lookups (components/layernorm.rs:116-136):
 // 0 -> 2^16 - 1, x -> min(2^16 / floor(sqrt(x)), p - 1); 2^16 entries, built once.
 const std::vector<uint32_t>& rsqrt_table16() {

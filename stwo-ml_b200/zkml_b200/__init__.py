@@ -107,6 +107,9 @@ _SIGS = {
     "zkml_reduce_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
                                       C.c_size_t, C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                       C.c_size_t, C.POINTER(C.c_size_t), _u32]),
+    "zkml_reduce_activation_piecewise": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int,
+                                                   C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
+                                                   C.c_size_t, C.POINTER(C.c_size_t), _u32, _u32]),
     "zkml_weight_commitment": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, _u64]),
     "zkml_prove_aggregated_binding": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(_Channel),
                                                 C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),
@@ -657,6 +660,37 @@ def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_t
                                               C.byref(channel.state), out, cap, C.byref(ln), ie))
     proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
     return proof, GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
+
+
+def piecewise_activation_enabled() -> bool:
+    """STWO_PIECEWISE_ACTIVATION (default on; 0/false/no/off select the LogUp path),
+    components/activation.rs:365-373."""
+    v = os.environ.get("STWO_PIECEWISE_ACTIVATION")
+    if v is None:
+        return True
+    return v.strip().lower() not in ("0", "false", "no", "off")
+
+
+def reduce_activation_layer_piecewise(output_claim: GKRClaim, inp: M31Matrix, activation_type: int,
+                                      channel: PoseidonChannel, device: int = 0
+                                      ) -> Tuple[ActivationLogUpProof, GKRClaim]:
+    """gkr/prover.rs:7006-7228.  Returns the LayerProof::Activation record (piecewise proof)
+    and the next claim (the sumcheck challenges, the input evaluation)."""
+    buf = _Buf(inp.data)
+    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
+    n_point = len(as_qm31_array(output_claim.point))
+    cap = 64 + 12 * n_point + 4 * 24
+    out = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    nxt = np.zeros((max(n_point, 1), 4), np.uint32)
+    _check(lib().zkml_reduce_activation_piecewise(context(device).handle, buf.ptr, inp.rows, inp.cols,
+                                                  activation_type, pt_ptr, n_point,
+                                                  np.ascontiguousarray(output_claim.value, np.uint32),
+                                                  C.byref(channel.state), out, cap, C.byref(ln), ie,
+                                                  nxt.reshape(-1)))
+    proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
+    return proof, GKRClaim(nxt[:n_point].copy(), ie.copy())
 
 
 @dataclass

@@ -84,6 +84,12 @@ def lib():
         L.orc_weight_commitment.argtypes = [u32p, sz, sz, u64p, C.c_int]
         L.orc_prove_aggregated_binding.argtypes = [C.c_void_p, sz, chp, sz, u64p, sz, C.POINTER(sz), C.c_int]
         L.orc_verify_aggregated_binding.argtypes = [C.c_void_p, sz, u64p, sz, chp, sz]
+        L.orc_activation_integer.argtypes = [C.c_int, C.c_uint32]
+        L.orc_activation_integer.restype = C.c_uint32
+        L.orc_piecewise_coeffs.argtypes = [C.c_int, u32p, u32p]
+        L.orc_reduce_activation_piecewise.argtypes = [u32p, sz, sz, C.c_int, u32p, sz, u32p, chp, u64p, sz,
+                                                      C.POINTER(sz), u32p, u32p]
+        L.orc_verify_activation_piecewise.argtypes = [u64p, sz, u32p, sz, u32p, chp, u32p]
         L.orc_rsqrt_table.argtypes = [C.c_uint, u32p]
         L.orc_reduce_rmsnorm.argtypes = [u32p, sz, sz, sz, C.c_void_p, sz, C.c_int, u32p, sz, u32p, chp, u64p,
                                          sz, C.POINTER(sz), u32p]
@@ -306,3 +312,33 @@ def evaluate_mle(evals, point) -> np.ndarray:
     out = np.zeros(4, np.uint32)
     lib().orc_evaluate_mle(evals.reshape(-1), len(point), point.reshape(-1), out)
     return out
+
+
+def piecewise_coeffs(tag):
+    sl, ic = np.zeros(16, np.uint32), np.zeros(16, np.uint32)
+    assert lib().orc_piecewise_coeffs(tag, sl, ic) == 0
+    return sl, ic
+
+
+def reduce_activation_piecewise(inp, tag, point, value, ch, cap=1 << 16):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    rows, cols = inp.shape
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    nxt = np.zeros((len(point), 4), np.uint32)
+    rc = lib().orc_reduce_activation_piecewise(inp.reshape(-1), rows, cols, tag, point.reshape(-1), len(point),
+                                               np.ascontiguousarray(value, np.uint32), C.byref(ch), buf, cap,
+                                               C.byref(ln), ie, nxt.reshape(-1))
+    nv = (rows - 1).bit_length() + (cols - 1).bit_length()
+    return rc, buf[:4 * ln.value].copy(), ie, nxt[:nv].copy()
+
+
+def verify_activation_piecewise(raw, point, value, ch):
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    ie = np.zeros(4, np.uint32)
+    ok = lib().orc_verify_activation_piecewise(np.ascontiguousarray(raw, np.uint64), raw.size // 4,
+                                               point.reshape(-1), len(point), np.ascontiguousarray(value, np.uint32),
+                                               C.byref(ch), ie)
+    return bool(ok), ie

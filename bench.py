@@ -277,6 +277,8 @@ def run_b200(args):
                "sample": "one full C2 layer through the C restatement of the reference CPU prover "
                          "(materialised restriction, backend.rs:110-197), all host threads"}
 
+    nxt = time_next_rows(Z, torch, ta, tb) if world == 1 else None
+
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -309,9 +311,52 @@ def run_b200(args):
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if nxt:
+        line["next_rows"] = nxt
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def time_next_rows(Z, torch, ta, tb, reps=5):
+    """Wall time per call (host transcript included, inputs resident in HBM) of the layer
+    reductions beside the matmul path, on config-2-shaped data: the forward GEMM, the SiLU
+    activation (LogUp and piecewise) and the RMSNorm of the C2 input, and the aggregated
+    binding of the C2 weight."""
+    import time
+
+    from helpers import random_qm31
+
+    rng = np.random.default_rng(7)
+    out = {}
+
+    def wall(fn, n):
+        fn()
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        for _ in range(n):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t) / n * 1e3
+
+    A, B = Z.M31Matrix(M, K, ta), Z.M31Matrix(K, N, tb)
+    tc = torch.empty(M * N, dtype=torch.int32, device="cuda")
+    out["forward_gemm_ms"] = wall(lambda: Z.matmul_m31(A, B, out=tc), reps)
+    C = Z.M31Matrix(M, N, tc)
+    pt_c = random_qm31(log2(PM) + log2(PN), rng)
+    val = random_qm31(1, rng)[0]
+    out["logup_silu_ms"] = wall(lambda: Z.reduce_activation_layer(Z.GKRClaim(pt_c, val), C, 5,
+                                                                  Z.PoseidonChannel()), reps)
+    out["piecewise_silu_ms"] = wall(lambda: Z.reduce_activation_layer_piecewise(Z.GKRClaim(pt_c, val), C, 5,
+                                                                                Z.PoseidonChannel()), reps)
+    pt_a = random_qm31(log2(PM) + log2(PK), rng)
+    out["rmsnorm_ms"] = wall(lambda: Z.reduce_rmsnorm_layer(Z.GKRClaim(pt_a, val), A, K, Z.PoseidonChannel()), reps)
+    com = Z.weight_commitment(tb)
+    out["weight_commitment_ms"] = wall(lambda: Z.weight_commitment(tb), 1)
+    claim = Z.AggregatedWeightClaim(B, 0, random_qm31(log2(PK) + log2(PN), rng), val, com)
+    out["aggregated_binding_ms"] = wall(lambda: Z.prove_aggregated_binding([claim], Z.PoseidonChannel()), 1)
+    out["shapes"] = {"gemm": [M, K, N], "activation": [M, N], "rmsnorm": [M, K], "binding_weight": [K, N]}
+    return {k: (round(v, 3) if isinstance(v, float) else v) for k, v in out.items()}
 
 
 def product_bytes(n):
@@ -460,6 +505,22 @@ def run_case(name):
         g = (np.arange(cols, dtype=np.uint32) % 1000) + 1
         for _ in range(2):
             Z.reduce_rmsnorm_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), cols, Z.PoseidonChannel(), gamma=g)
+    elif name.startswith("piecewise_"):  # piecewise SiLU layer R x C (e.g. piecewise_64x13824), twice
+        rows, cols = (int(v) for v in name.split("_")[1].split("x"))
+        x = int_matrix_m31(rows, cols, 3, bound=60000)
+        nv = (rows - 1).bit_length() + (cols - 1).bit_length()
+        rng = np.random.default_rng(0)
+        pt, val = random_qm31(nv, rng), random_qm31(1, rng)[0]
+        for _ in range(2):
+            Z.reduce_activation_layer_piecewise(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), 5,
+                                                Z.PoseidonChannel())
+    elif name.startswith("binding_"):  # aggregated binding of one R x C weight (e.g. binding_5120x13824)
+        rows, cols = (int(v) for v in name.split("_")[1].split("x"))
+        w = torch.randint(0, 255, (rows, cols), dtype=torch.int32, device="cuda")
+        nv = (rows - 1).bit_length() + (cols - 1).bit_length()
+        rng = np.random.default_rng(0)
+        claim = Z.AggregatedWeightClaim(w, 0, random_qm31(nv, rng), random_qm31(1, rng)[0], Z.weight_commitment(w))
+        Z.prove_aggregated_binding([claim], Z.PoseidonChannel())
     elif name.startswith("la_"):  # native 1 x 2^L . 2^L x 1 reduction (look-ahead rounds), four times
         lg = int(name.split("_")[1])
         be = Z.GpuBackend(0)

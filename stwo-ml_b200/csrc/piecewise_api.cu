@@ -9,7 +9,9 @@
 // at t = 0, 1, 2, 3 for every pair (prover.rs:6935-6998).  Here h is regrouped as
 //   h = L - in G - Q,  L = sum_i u_i I_i + sum_k w_k B_k + e0 out - e1,  G = sum_i g_i I_i,
 //   Q = sum_i e_{2+i} I_i^2 + sum_k e_{19+k} B_k^2
-// (u_i = e1 + e_{2+i} - i e18 - e0 b_i, g_i = e0 a_i, w_k = 2^k e18 + e_{19+k}), every vector
+// (u_i = e1 + e_{2+i} - i e18 - e0 b_i, g_i = e0 a_i, w_k = 2^k e18 + e_{19+k}), i.e.
+//   h = e0 out - e1 + sum_i I_i (u_i - g_i in - e_{2+i} I_i) + sum_k B_k (w_k - e_{19+k} B_k);
+// every vector
 // is linear in t over a pair, so each pair contributes the cubic eq(t) h(t) in coefficient
 // form and the kernel returns the round polynomial's coefficients (c0..c3) directly; they
 // equal the reference's Newton interpolation of s(0..3) because a cubic is determined by
@@ -41,124 +43,271 @@ struct PwConsts {
     uint32_t slope[16], icpt[16];
 };
 
-enum PwMode { PW_RAW = 0, PW_RAW_FOLD = 1, PW_FOLD = 2 };
+// Folded rounds with at least this many pairs run one thread per pair (throughput); shorter
+// ones one warp per pair (latency: a pair is ~10k dependent instructions for one thread).
+constexpr size_t PW_THREAD_MIN_PAIRS = (size_t)1 << 16;
 
 __device__ __forceinline__ uint32_t pw_seg(uint32_t x) { return min(x >> 27, 15u); }
 
-// Accumulates one vector's pair (lo at t = 0, d = hi - lo) into the lazy sums.
+// h(t) = h0 + h1 t + h2 t^2 accumulated lazily over one pair.
 struct PwAcc {
-    QAcc L0, LD, G0, GD, Q0, Q1, Q2;
+    QAcc H0, H1, H2;
 };
 
-__device__ __forceinline__ void pw_indicator(PwAcc& a, const qm31& x0, const qm31& xd, const qm31& u, const qm31* g,
-                                             const qm31& e) {
-    qacc_mul(a.L0, u, x0);
-    qacc_mul(a.LD, u, xd);
+// One indicator (or segment bit) with value x0 + t xd: adds x (u - g in - e x), where
+// in = in0 + t ind and g is null for a segment bit.
+__device__ __forceinline__ void pw_term(PwAcc& a, const qm31& x0, const qm31& xd, const qm31& u, const qm31* g,
+                                        const qm31& e, const qm31& in0, const qm31& ind) {
+    qm31 y0 = qsub(u, qmul_f(e, x0)), yd = qsub(qzero(), qmul_f(e, xd));
     if (g) {
-        qacc_mul(a.G0, *g, x0);
-        qacc_mul(a.GD, *g, xd);
+        y0 = qsub(y0, qmul_f(*g, in0));
+        yd = qsub(yd, qmul_f(*g, ind));
     }
-    const qm31 ex0 = qmul_f(e, x0), exd = qmul_f(e, xd);
-    qacc_mul(a.Q0, ex0, x0);
-    qacc_mul(a.Q1, ex0, xd);
-    qacc_mul(a.Q2, exd, xd);
+    qacc_mul(a.H0, x0, y0);
+    qacc_mul(a.H1, x0, yd);
+    qacc_mul(a.H1, xd, y0);
+    qacc_mul(a.H2, xd, yd);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(256) pw_round_kernel(const uint32_t* __restrict__ x32, const uint4* __restrict__ E,
-                                                       uint4* __restrict__ V, size_t stride, size_t h,
-                                                       const AlphaRows m, qm31 alpha, const PwConsts c,
-                                                       ReduceScratch rs) {
-    // MODE == PW_RAW: h is the current length (no fold); otherwise h is the length after
-    // folding a vector of 2h.  Pairs (i, i + q), q = h / 2.
+// Folded rounds (2 and later), one thread per pair: each of the 23 vectors is folded
+// 2h -> h in place and its pair (i, i + q), q = h / 2, is added to h(t).
+__global__ void __launch_bounds__(256, 2) pw_round_kernel(uint4* __restrict__ V, size_t stride, size_t h,
+                                                          const AlphaRows m, const PwConsts c, ReduceScratch rs) {
     const size_t q = h / 2;
-    unsigned long long words[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) words[i] = 0;
+    qm31 kacc[4] = {qzero(), qzero(), qzero(), qzero()};  // this thread's coefficient sums
     const qm31 one = qm(1, 0, 0, 0);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
-        // vector v at this pair: lo (index i) and hi (index i + q) after the optional fold
-        uint32_t xr[4] = {0, 0, 0, 0};  // raw inputs (raw modes)
-        if (MODE == PW_RAW) {
-            xr[0] = x32[i];
-            xr[1] = x32[i + q];
-        } else if (MODE == PW_RAW_FOLD) {
-            xr[0] = x32[i];
-            xr[1] = x32[i + q];
-            xr[2] = x32[i + h];
-            xr[3] = x32[i + q + h];
-        }
-        auto pair_of = [&](int v, auto raw_value, qm31& lo, qm31& hi) {
-            if (MODE == PW_RAW) {
-                lo = qm(raw_value(xr[0]), 0, 0, 0);
-                hi = qm(raw_value(xr[1]), 0, 0, 0);
-            } else if (MODE == PW_RAW_FOLD) {
-                lo = fold_mq(raw_value(xr[0]), raw_value(xr[2]), alpha);
-                hi = fold_mq(raw_value(xr[1]), raw_value(xr[3]), alpha);
-                stq4(V + v * stride + i, lo);
-                stq4(V + v * stride + i + q, hi);
-            } else {
-                uint4* b = V + v * stride;
-                lo = fold_qq(ldq4(b + i), ldq4(b + i + h), m);
-                hi = fold_qq(ldq4(b + i + q), ldq4(b + i + q + h), m);
-                stq4(b + i, lo);
-                stq4(b + i + q, hi);
-            }
+        auto pair_of = [&](int v, qm31& lo, qm31& hi) {
+            uint4* b = V + v * stride;
+            lo = fold_qq(ldq4(b + i), ldq4(b + i + h), m);
+            hi = fold_qq(ldq4(b + i + q), ldq4(b + i + q + h), m);
+            stq4(b + i, lo);
+            stq4(b + i + q, hi);
         };
-        // eq
-        qm31 e0, e1;
-        if (MODE == PW_RAW) {
-            e0 = ldq4(E + i);
-            e1 = ldq4(E + i + q);
-        } else if (MODE == PW_RAW_FOLD) {
-            e0 = fold_qq(ldq4(E + i), ldq4(E + i + h), m);
-            e1 = fold_qq(ldq4(E + i + q), ldq4(E + i + q + h), m);
-            stq4(V + i, e0);
-            stq4(V + i + q, e1);
-        } else {
-            pair_of(0, [](uint32_t) { return 0u; }, e0, e1);
-        }
-        const qm31 eD = qsub(e1, e0);
-        qm31 in0, in1, o0, o1;
-        pair_of(1, [](uint32_t x) { return x; }, in0, in1);
-        pair_of(2, [&](uint32_t x) { const uint32_t s = pw_seg(x); return madd(mmul(c.slope[s], x), c.icpt[s]); }, o0,
-                o1);
-        const qm31 inD = qsub(in1, in0);
+        qm31 e0, e1, in0, in1, o0, o1;
+        pair_of(0, e0, e1);
+        pair_of(1, in0, in1);
+        pair_of(2, o0, o1);
+        const qm31 eD = qsub(e1, e0), inD = qsub(in1, in0);
         PwAcc a;
-        qacc_zero(a.L0);
-        qacc_zero(a.LD);
-        qacc_zero(a.G0);
-        qacc_zero(a.GD);
-        qacc_zero(a.Q0);
-        qacc_zero(a.Q1);
-        qacc_zero(a.Q2);
-        qacc_mul(a.L0, c.eta0, o0);
-        qacc_mul(a.LD, c.eta0, qsub(o1, o0));
-        qacc_mul(a.L0, c.neg_eta1, one);
+        qacc_zero(a.H0);
+        qacc_zero(a.H1);
+        qacc_zero(a.H2);
+        qacc_mul(a.H0, c.eta0, o0);
+        qacc_mul(a.H1, c.eta0, qsub(o1, o0));
+        qacc_mul(a.H0, c.neg_eta1, one);
 #pragma unroll 1
         for (int s = 0; s < 16; s++) {
             qm31 x0, x1;
-            pair_of(3 + s, [s](uint32_t x) { return pw_seg(x) == (uint32_t)s ? 1u : 0u; }, x0, x1);
-            pw_indicator(a, x0, qsub(x1, x0), c.u[s], &c.g[s], c.e[s]);
+            pair_of(3 + s, x0, x1);
+            pw_term(a, x0, qsub(x1, x0), c.u[s], &c.g[s], c.e[s], in0, inD);
         }
 #pragma unroll 1
         for (int k = 0; k < 4; k++) {
             qm31 x0, x1;
-            pair_of(19 + k, [k](uint32_t x) { return (pw_seg(x) >> k) & 1u; }, x0, x1);
-            pw_indicator(a, x0, qsub(x1, x0), c.w[k], nullptr, c.f[k]);
+            pair_of(19 + k, x0, x1);
+            pw_term(a, x0, qsub(x1, x0), c.w[k], nullptr, c.f[k], in0, inD);
         }
-        const qm31 L0 = qacc_value(a.L0), LD = qacc_value(a.LD), G0 = qacc_value(a.G0), GD = qacc_value(a.GD);
-        const qm31 Q0 = qacc_value(a.Q0), Q1 = qacc_value(a.Q1), Q2 = qacc_value(a.Q2);
-        // h(t) = h0 + h1 t + h2 t^2
-        const qm31 h0 = qsub(qsub(L0, qmul_f(in0, G0)), Q0);
-        const qm31 h1 = qsub(qsub(LD, qadd(qmul_f(in0, GD), qmul_f(inD, G0))), qadd(Q1, Q1));
-        const qm31 h2 = qsub(qmul_f(qsub(qzero(), inD), GD), Q2);
-        const qm31 k0 = qmul_f(e0, h0), k1 = qadd(qmul_f(e0, h1), qmul_f(eD, h0));
-        const qm31 k2 = qadd(qmul_f(e0, h2), qmul_f(eD, h1)), k3 = qmul_f(eD, h2);
-        acc_q<16>(words, 0, k0);
-        acc_q<16>(words, 4, k1);
-        acc_q<16>(words, 8, k2);
-        acc_q<16>(words, 12, k3);
+        const qm31 h0 = qacc_value(a.H0), h1 = qacc_value(a.H1), h2 = qacc_value(a.H2);
+        kacc[0] = qadd(kacc[0], qmul_f(e0, h0));
+        kacc[1] = qadd(kacc[1], qadd(qmul_f(e0, h1), qmul_f(eD, h0)));
+        kacc[2] = qadd(kacc[2], qadd(qmul_f(e0, h2), qmul_f(eD, h1)));
+        kacc[3] = qadd(kacc[3], qmul_f(eD, h2));
+    }
+    unsigned long long words[16];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        words[4 * t] = kacc[t].a;
+        words[4 * t + 1] = kacc[t].b;
+        words[4 * t + 2] = kacc[t].c;
+        words[4 * t + 3] = kacc[t].d;
+    }
+    grid_reduce<16>(words, rs);
+}
+
+// Rounds 0 and 1 read the raw input: the indicators and segment bits are 0/1 there
+// (round 0) or fold two 0/1 values (round 1), so only the segments a pair touches (at
+// most 2 or 4 of the 16) contribute, and in round 0 every term is a signed sum of
+// constants and M31 multiples of constants (no QM31 products but the eq ones).
+__device__ __forceinline__ qm31 qneg(const qm31& x) { return qsub(qzero(), x); }
+__device__ __forceinline__ qm31 qsign(int s, const qm31& x) { return s > 0 ? x : (s < 0 ? qneg(x) : qzero()); }
+
+// Round 0 term of an indicator / segment bit with 0/1 values x0 (lo), x1 (hi).
+__device__ __forceinline__ void pw_term01(qm31 (&H)[3], int x0, int x1, const qm31& u, const qm31* g,
+                                          const qm31& e, uint32_t in0, uint32_t ind) {
+    const int xd = x1 - x0;
+    qm31 y0 = x0 ? qsub(u, e) : u;
+    qm31 yd = qsign(-xd, e);
+    if (g) {
+        y0 = qsub(y0, qmul_m(*g, in0));
+        yd = qsub(yd, qmul_m(*g, ind));
+    }
+    if (x0) {
+        H[0] = qadd(H[0], y0);
+        H[1] = qadd(H[1], yd);
+    }
+    H[1] = qadd(H[1], qsign(xd, y0));
+    H[2] = qadd(H[2], qsign(xd, yd));
+}
+
+__device__ __forceinline__ void pw_term_h(qm31 (&H)[3], const qm31& x0, const qm31& xd, const qm31& u, const qm31* g,
+                                        const qm31& e, const qm31& in0, const qm31& ind) {
+    qm31 y0 = qsub(u, qmul_f(e, x0)), yd = qneg(qmul_f(e, xd));
+    if (g) {
+        y0 = qsub(y0, qmul_f(*g, in0));
+        yd = qsub(yd, qmul_f(*g, ind));
+    }
+    H[0] = qadd(H[0], qmul_f(x0, y0));
+    H[1] = qadd(H[1], qadd(qmul_f(x0, yd), qmul_f(xd, y0)));
+    H[2] = qadd(H[2], qmul_f(xd, yd));
+}
+
+template <bool FOLD>
+__global__ void __launch_bounds__(256) pw_raw_kernel(const uint32_t* __restrict__ x32, const uint4* __restrict__ E,
+                                                     uint4* __restrict__ V, size_t stride, size_t h, const AlphaRows m,
+                                                     qm31 alpha, const PwConsts c, ReduceScratch rs) {
+    // !FOLD: pairs (i, i + h/2) of the raw length-h input; FOLD: the raw input has length 2h
+    // and is folded into V (length h) while the pairs (i, i + h/2) are summed.
+    const size_t q = h / 2;
+    qm31 kacc[4] = {qzero(), qzero(), qzero(), qzero()};
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x) {
+        qm31 H[3] = {qzero(), qzero(), qzero()};
+        qm31 e0, eD;
+        if (!FOLD) {
+            const uint32_t xa = x32[i], xb = x32[i + q];
+            const uint32_t sa = pw_seg(xa), sb = pw_seg(xb);
+            e0 = ldq4(E + i);
+            eD = qsub(ldq4(E + i + q), e0);
+            const uint32_t ind = csub(xb, xa);
+            const uint32_t oa = madd(mmul(c.slope[sa], xa), c.icpt[sa]), ob = madd(mmul(c.slope[sb], xb), c.icpt[sb]);
+            H[0] = qadd(qmul_m(c.eta0, oa), c.neg_eta1);
+            H[1] = qmul_m(c.eta0, csub(ob, oa));
+            pw_term01(H, 1, sa == sb, c.u[sa], &c.g[sa], c.e[sa], xa, ind);
+            if (sb != sa) pw_term01(H, 0, 1, c.u[sb], &c.g[sb], c.e[sb], xa, ind);
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                pw_term01(H, (sa >> k) & 1, (sb >> k) & 1, c.w[k], nullptr, c.f[k], xa, ind);
+        } else {
+            const uint32_t xr[4] = {x32[i], x32[i + q], x32[i + h], x32[i + q + h]};
+            uint32_t sg[4], o[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                sg[j] = pw_seg(xr[j]);
+                o[j] = madd(mmul(c.slope[sg[j]], xr[j]), c.icpt[sg[j]]);
+            }
+            e0 = fold_qq(ldq4(E + i), ldq4(E + i + h), m);
+            const qm31 e1 = fold_qq(ldq4(E + i + q), ldq4(E + i + q + h), m);
+            eD = qsub(e1, e0);
+            stq4(V + i, e0);
+            stq4(V + i + q, e1);
+            const qm31 in0 = fold_mq(xr[0], xr[2], alpha), in1 = fold_mq(xr[1], xr[3], alpha);
+            stq4(V + stride + i, in0);
+            stq4(V + stride + i + q, in1);
+            const qm31 inD = qsub(in1, in0);
+            const qm31 o0 = fold_mq(o[0], o[2], alpha), o1 = fold_mq(o[1], o[3], alpha);
+            stq4(V + 2 * stride + i, o0);
+            stq4(V + 2 * stride + i + q, o1);
+            H[0] = qadd(qmul_f(c.eta0, o0), c.neg_eta1);
+            H[1] = qmul_f(c.eta0, qsub(o1, o0));
+#pragma unroll 1
+            for (int sI = 0; sI < 16; sI++) {
+                const uint32_t su = (uint32_t)sI;
+                const bool l0 = sg[0] == su, l2 = sg[2] == su, h1 = sg[1] == su, h3 = sg[3] == su;
+                const qm31 lo = fold_mq(l0, l2, alpha), hi = fold_mq(h1, h3, alpha);
+                stq4(V + (3 + sI) * stride + i, lo);
+                stq4(V + (3 + sI) * stride + i + q, hi);
+                if (l0 | l2 | h1 | h3) pw_term_h(H, lo, qsub(hi, lo), c.u[sI], &c.g[sI], c.e[sI], in0, inD);
+            }
+#pragma unroll 1
+            for (int k = 0; k < 4; k++) {
+                const qm31 lo = fold_mq((sg[0] >> k) & 1, (sg[2] >> k) & 1, alpha);
+                const qm31 hi = fold_mq((sg[1] >> k) & 1, (sg[3] >> k) & 1, alpha);
+                stq4(V + (19 + k) * stride + i, lo);
+                stq4(V + (19 + k) * stride + i + q, hi);
+                pw_term_h(H, lo, qsub(hi, lo), c.w[k], nullptr, c.f[k], in0, inD);
+            }
+        }
+        kacc[0] = qadd(kacc[0], qmul_f(e0, H[0]));
+        kacc[1] = qadd(kacc[1], qadd(qmul_f(e0, H[1]), qmul_f(eD, H[0])));
+        kacc[2] = qadd(kacc[2], qadd(qmul_f(e0, H[2]), qmul_f(eD, H[1])));
+        kacc[3] = qadd(kacc[3], qmul_f(eD, H[2]));
+    }
+    unsigned long long words[16];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        words[4 * t] = kacc[t].a;
+        words[4 * t + 1] = kacc[t].b;
+        words[4 * t + 2] = kacc[t].c;
+        words[4 * t + 3] = kacc[t].d;
+    }
+    grid_reduce<16>(words, rs);
+}
+
+// Folded rounds with one warp per pair: lane v < 23 folds vector v (lo at index i, hi at
+// i + q) and adds its term of h; the eq and input values are broadcast from lanes 0 and 1,
+// and lane 0 combines the warp's h with eq into the cubic.  A pair's work is spread over 23
+// lanes, so the short rounds at the end (a few pairs) do not run one long dependent chain
+// per thread.
+__global__ void __launch_bounds__(256) pw_fold_warp_kernel(uint4* __restrict__ V, size_t stride, size_t h,
+                                                           const AlphaRows m, const PwConsts c, ReduceScratch rs) {
+    const size_t q = h / 2;
+    const int lane = threadIdx.x & 31;
+    const size_t w0 = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+    const size_t nw = ((size_t)gridDim.x * blockDim.x) >> 5;
+    qm31 kacc[4] = {qzero(), qzero(), qzero(), qzero()};
+    for (size_t i = w0; i < q; i += nw) {
+        qm31 lo = qzero(), hi = qzero();
+        if (lane < PW_NV) {
+            uint4* b = V + lane * stride;
+            lo = fold_qq(ldq4(b + i), ldq4(b + i + h), m);
+            hi = fold_qq(ldq4(b + i + q), ldq4(b + i + q + h), m);
+            stq4(b + i, lo);
+            stq4(b + i + q, hi);
+        }
+        const qm31 d = qsub(hi, lo);
+        auto bcast = [&](const qm31& v, int src) {
+            return qm(__shfl_sync(0xffffffffu, v.a, src), __shfl_sync(0xffffffffu, v.b, src),
+                      __shfl_sync(0xffffffffu, v.c, src), __shfl_sync(0xffffffffu, v.d, src));
+        };
+        const qm31 in0 = bcast(lo, 1), inD = bcast(d, 1);
+        qm31 H[3] = {qzero(), qzero(), qzero()};
+        if (lane == 2) {
+            H[0] = qadd(qmul_f(c.eta0, lo), c.neg_eta1);
+            H[1] = qmul_f(c.eta0, d);
+        } else if (lane >= 3 && lane < PW_NV) {
+            qm31 y0, yd;
+            if (lane < 19) {
+                const int s = lane - 3;
+                y0 = qsub(qsub(c.u[s], qmul_f(c.e[s], lo)), qmul_f(c.g[s], in0));
+                yd = qsub(qsub(qzero(), qmul_f(c.e[s], d)), qmul_f(c.g[s], inD));
+            } else {
+                const int k = lane - 19;
+                y0 = qsub(c.w[k], qmul_f(c.f[k], lo));
+                yd = qsub(qzero(), qmul_f(c.f[k], d));
+            }
+            H[0] = qmul_f(lo, y0);
+            H[1] = qadd(qmul_f(lo, yd), qmul_f(d, y0));
+            H[2] = qmul_f(d, yd);
+        }
+#pragma unroll
+        for (int t = 0; t < 3; t++)
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) H[t] = qadd(H[t], bcast(H[t], lane ^ off));
+        if (lane == 0) {
+            const qm31 e0 = lo, eD = d;
+            kacc[0] = qadd(kacc[0], qmul_f(e0, H[0]));
+            kacc[1] = qadd(kacc[1], qadd(qmul_f(e0, H[1]), qmul_f(eD, H[0])));
+            kacc[2] = qadd(kacc[2], qadd(qmul_f(e0, H[2]), qmul_f(eD, H[1])));
+            kacc[3] = qadd(kacc[3], qmul_f(eD, H[2]));
+        }
+    }
+    unsigned long long words[16];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+        words[4 * t] = kacc[t].a;
+        words[4 * t + 1] = kacc[t].b;
+        words[4 * t + 2] = kacc[t].c;
+        words[4 * t + 3] = kacc[t].d;
     }
     grid_reduce<16>(words, rs);
 }
@@ -296,8 +445,8 @@ extern "C" int zkml_reduce_activation_piecewise(zkml_ctx* ctx, const uint32_t* i
     std::vector<qm31> rps(4 * num_vars), chal(num_vars);
     size_t len = n;
     next();
-    pw_round_kernel<PW_RAW><<<grid(len / 2), 256, 0, s>>>(b.x.as<uint32_t>(), b.eq.as<uint4>(), b.pv.as<uint4>(),
-                                                          stride, len, alpha_rows(qzero()), qzero(), c, rs);
+    pw_raw_kernel<false><<<grid(len / 2), 256, 0, s>>>(b.x.as<uint32_t>(), b.eq.as<uint4>(), b.pv.as<uint4>(),
+                                                       stride, len, alpha_rows(qzero()), qzero(), c, rs);
     ctx->launches++;
     ZK_CUDA(cudaGetLastError());
     for (unsigned r = 0; r < num_vars; r++) {
@@ -316,13 +465,14 @@ extern "C" int zkml_reduce_activation_piecewise(zkml_ctx* ctx, const uint32_t* i
             next();
             const size_t h = len / 2;
             if (r == 0)
-                pw_round_kernel<PW_RAW_FOLD><<<grid(h / 2), 256, 0, s>>>(b.x.as<uint32_t>(), b.eq.as<uint4>(),
-                                                                         b.pv.as<uint4>(), stride, h,
-                                                                         alpha_rows(chal[r]), chal[r], c, rs);
+                pw_raw_kernel<true><<<grid(h / 2), 256, 0, s>>>(b.x.as<uint32_t>(), b.eq.as<uint4>(),
+                                                                b.pv.as<uint4>(), stride, h, alpha_rows(chal[r]),
+                                                                chal[r], c, rs);
+            else if (h / 2 >= PW_THREAD_MIN_PAIRS)
+                pw_round_kernel<<<grid(h / 2), 256, 0, s>>>(b.pv.as<uint4>(), stride, h, alpha_rows(chal[r]), c, rs);
             else
-                pw_round_kernel<PW_FOLD><<<grid(h / 2), 256, 0, s>>>(b.x.as<uint32_t>(), b.eq.as<uint4>(),
-                                                                     b.pv.as<uint4>(), stride, h, alpha_rows(chal[r]),
-                                                                     chal[r], c, rs);
+                pw_fold_warp_kernel<<<grid(h / 2 * 32), 256, 0, s>>>(b.pv.as<uint4>(), stride, h, alpha_rows(chal[r]),
+                                                                    c, rs);
         }
         ctx->launches++;
         ZK_CUDA(cudaGetLastError());

@@ -174,6 +174,21 @@ int zkml_prove_gkr_matmul(zkml_ctx *ctx, const uint32_t *input, size_t m, size_t
                           size_t n, const uint64_t *policy, size_t n_queries, uint64_t *out_calldata,
                           size_t cap, size_t *out_len, uint64_t out_digest[4], uint64_t out_io[4]);
 
+/* ---- Column-block sharded matmul layer -----------------------------------------
+ * The config-2/4 layer split by column blocks of B across ranks (one GPU each): rank g
+ * restricts its block B[:, col_offset .. col_offset + n_block) with the weights
+ * L_{col_offset + j}(r_j) of the full padded column space into 4 k canonical u64 words
+ * (out_words, device memory of the context's GPU); the ranks add their words (an int64
+ * SUM all-reduce, e.g. NCCL); every rank then runs the layer from the summed words
+ * (zkml_reduce_matmul_layer_gkr_fb), whose outputs equal zkml_reduce_matmul_layer_gkr's
+ * on the whole B.  col_offset must be a multiple of 64. */
+int zkml_restrict_cols_block(zkml_ctx *ctx, const uint32_t *b_block, size_t k, size_t n_block, size_t col_offset,
+                             const uint32_t *r_j, size_t n_rj, uint64_t *out_words);
+int zkml_reduce_matmul_layer_gkr_fb(zkml_ctx *ctx, const uint32_t *claim_point, size_t n_point,
+                                    const uint32_t claim_value[4], const uint32_t *a, size_t m, size_t k,
+                                    const uint64_t *fb_words, size_t n, zkml_channel *ch, uint32_t *out_round_polys,
+                                    uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t *out_next_point);
+
 /* ---- LogUp activation layer ------------------------------------------------- */
 
 /* reduce_activation_layer, LogUp path (gkr/prover.rs:6390-6600; reference GPU

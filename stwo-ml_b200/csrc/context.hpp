@@ -52,7 +52,7 @@ int reduce_matmul_internal(::zkml_ctx* ctx, const uint32_t* a, size_t a_rows, si
                            size_t b_rows, size_t b_cols, const uint32_t* r_i, size_t n_ri, const uint32_t* r_j,
                            size_t n_rj, size_t pk, zkml_channel* ch, uint32_t* out_round_polys,
                            uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
-                           const ClaimHook* hook);
+                           const ClaimHook* hook, const uint64_t* fb_words = nullptr);
 
 // The sumcheck round loop (matmul_api.cu): M31 inputs (A32, B32) or QM31 (A, B)
 // of length len; writes log2(len) round polynomials and challenges.

@@ -57,6 +57,8 @@ struct RoundScratch {
 };
 // Reduce n u32 words in place to [0, P) (the round kernels need canonical QM31 input).
 void launch_canon_words(uint32_t* w, size_t n, cudaStream_t s);
+// Reduce n u64 words in place to [0, P).
+void launch_canon_u64(unsigned long long* w, size_t n, cudaStream_t s);
 // Round sums over QM31 vectors of length len (no fold).
 void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s);
 // Fold A, B in place with alpha (len -> len/2) and emit the next round's sums.

@@ -581,7 +581,8 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
 
 // Restriction of A (rows by r_i) and B (columns by r_j) into ctx->fa / fb (length pk).
 static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, const uint32_t* B, size_t n,
-                       const qm31* r_i, unsigned n_ri, const qm31* r_j, unsigned n_rj, size_t pk) {
+                       const qm31* r_i, unsigned n_ri, const qm31* r_j, unsigned n_rj, size_t pk,
+                       const uint64_t* fb_words) {
     cudaStream_t s = ctx->stream;
     int rc;
     if ((rc = ctx->fa.ensure(pk * 16)) || (rc = ctx->fb.ensure(pk * 16))) return rc;
@@ -602,7 +603,10 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
         launch_acc_finalize(ctx->acc_a.as<unsigned long long>(), k, fa, pk, s);
         ctx->launches += 3;
     }
-    if (n_rj == 0) {  // n == 1: f_b is B's single column (contiguous)
+    if (fb_words) {  // f_b from column-block partial sums added across ranks (zkml_restrict_cols_block)
+        launch_acc_finalize(reinterpret_cast<const unsigned long long*>(fb_words), k, fb, pk, s);
+        ctx->launches++;
+    } else if (n_rj == 0) {  // n == 1: f_b is B's single column (contiguous)
         launch_m31_to_qm31(B, k, fb, pk, ctx->err_flag(), s);
         ctx->launches++;
     } else {
@@ -784,8 +788,8 @@ int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size
                            size_t b_rows, size_t b_cols, const uint32_t* r_i, size_t n_ri, const uint32_t* r_j,
                            size_t n_rj, size_t pk, zkml_channel* ch, uint32_t* out_round_polys,
                            uint32_t* out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
-                           const ClaimHook* hook) {
-    if (!ctx || !a || !b || !ch || !out_final_a || !out_final_b)
+                           const ClaimHook* hook, const uint64_t* fb_words) {
+    if (!ctx || !a || !(b || fb_words) || !ch || !out_final_a || !out_final_b)
         return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (a_rows == 0 || a_cols == 0 || b_cols == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty matrix");
     if (a_cols != b_rows) return set_error(ZKML_ERR_INVALID_ARG, "A.cols must equal B.rows");
@@ -802,18 +806,26 @@ int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size
     const void* A = nullptr;
     const void* B = nullptr;
     int rc = device_view(ctx, a, a_rows * a_cols * 4, ctx->a_in, &A);
-    if (!rc) rc = device_view(ctx, b, b_rows * b_cols * 4, ctx->b_in, &B);
+    if (!rc && !fb_words) rc = device_view(ctx, b, b_rows * b_cols * 4, ctx->b_in, &B);
     if (rc) return rc;
     const uint32_t* Ad = static_cast<const uint32_t*>(A);
     const uint32_t* Bd = static_cast<const uint32_t*>(B);
+    if (fb_words) {
+        cudaPointerAttributes attr;
+        if (cudaPointerGetAttributes(&attr, fb_words) != cudaSuccess || attr.type != cudaMemoryTypeDevice ||
+            attr.device != ctx->device) {
+            cudaGetLastError();
+            return set_error(ZKML_ERR_INVALID_ARG, "f_b partial words must be device memory of the context's GPU");
+        }
+    }
     // Product sumcheck (1 x k times k x 1, k a power of two): stay in M31 for round 0.
-    if (n_ri == 0 && n_rj == 0 && pk == a_cols && pk >= 4) {
+    if (!fb_words && n_ri == 0 && n_rj == 0 && pk == a_cols && pk >= 4) {
         if ((rc = ctx->fa.ensure(pk / 2 * 16)) || (rc = ctx->fb.ensure(pk / 2 * 16))) return rc;
         return run_sumcheck(ctx, nullptr, nullptr, Ad, Bd, pk, ch, out_round_polys, out_challenges, out_final_a,
                             out_final_b, hook);
     }
     rc = restrict_ab(ctx, Ad, a_rows, a_cols, Bd, b_cols, reinterpret_cast<const qm31*>(r_i), (unsigned)n_ri,
-                     reinterpret_cast<const qm31*>(r_j), (unsigned)n_rj, pk);
+                     reinterpret_cast<const qm31*>(r_j), (unsigned)n_rj, pk, fb_words);
     if (rc) return rc;
     rc = run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, pk, ch, out_round_polys,
                       out_challenges, out_final_a, out_final_b, hook);
@@ -822,12 +834,10 @@ int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size
 }
 }  // namespace zk
 
-extern "C" {
-
-int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n_point,
-                                 const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k,
-                                 const uint32_t* b, size_t n, zkml_channel* chs, uint32_t* out_round_polys,
-                                 uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t* out_next_point) {
+static int matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n_point,
+                            const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k, const uint32_t* b,
+                            size_t n, const uint64_t* fb_words, zkml_channel* chs, uint32_t* out_round_polys,
+                            uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t* out_next_point) {
     if (!ctx || !claim_value || !chs || (n_point && !claim_point)) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (m == 0 || k == 0 || n == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty matrix");
     const size_t pm = next_pow2(m), pk = next_pow2(k), pn = next_pow2(n);
@@ -854,7 +864,7 @@ int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, siz
     };
     std::vector<uint32_t> chal(4 * (log_k + 1));
     int rc = reduce_matmul_internal(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
-                                    chs, out_round_polys, chal.data(), out_final_a, out_final_b, &hook);
+                                    chs, out_round_polys, chal.data(), out_final_a, out_final_b, &hook, fb_words);
     if (rc) return rc;
     Channel ch(chs);
     ch.mix_qm31(ldq(out_final_a));
@@ -863,6 +873,75 @@ int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, siz
         memcpy(out_next_point, claim_point, 16 * log_m);
         memcpy(out_next_point + 4 * log_m, chal.data(), 16 * log_k);
     }
+    return ZKML_OK;
+}
+
+extern "C" {
+
+int zkml_reduce_matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n_point,
+                                 const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k,
+                                 const uint32_t* b, size_t n, zkml_channel* chs, uint32_t* out_round_polys,
+                                 uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t* out_next_point) {
+    if (!b) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    return matmul_layer_gkr(ctx, claim_point, n_point, claim_value, a, m, k, b, n, nullptr, chs, out_round_polys,
+                            out_final_a, out_final_b, out_next_point);
+}
+
+int zkml_reduce_matmul_layer_gkr_fb(zkml_ctx* ctx, const uint32_t* claim_point, size_t n_point,
+                                    const uint32_t claim_value[4], const uint32_t* a, size_t m, size_t k,
+                                    const uint64_t* fb_words, size_t n, zkml_channel* chs, uint32_t* out_round_polys,
+                                    uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t* out_next_point) {
+    if (!fb_words) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    return matmul_layer_gkr(ctx, claim_point, n_point, claim_value, a, m, k, nullptr, n, fb_words, chs,
+                            out_round_polys, out_final_a, out_final_b, out_next_point);
+}
+
+int zkml_restrict_cols_block(zkml_ctx* ctx, const uint32_t* b_block, size_t k, size_t n_block, size_t col_offset,
+                             const uint32_t* r_j, size_t n_rj, uint64_t* out_words) {
+    if (!ctx || !b_block || !out_words || (n_rj && !r_j)) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    if (k == 0 || n_block == 0 || k > (1u << 30) || k * n_block > ((size_t)1 << 34))
+        return set_error(ZKML_ERR_INVALID_ARG, "bad block shape");
+    if (n_rj > MAX_EQ_VARS || col_offset + n_block > ((size_t)1 << n_rj))
+        return set_error(ZKML_ERR_INVALID_ARG, "block exceeds the padded column space of r_j");
+    if (col_offset % 64 != 0) return set_error(ZKML_ERR_INVALID_ARG, "col_offset must be a multiple of 64");
+    ZK_CUDA(cudaSetDevice(ctx->device));
+    cudaStream_t s = ctx->stream;
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, out_words) != cudaSuccess || attr.type != cudaMemoryTypeDevice ||
+        attr.device != ctx->device) {
+        cudaGetLastError();
+        return set_error(ZKML_ERR_INVALID_ARG, "out_words must be device memory of the context's GPU");
+    }
+    const void* Bv = nullptr;
+    int rc = device_view(ctx, b_block, k * n_block * 4, ctx->b_in, &Bv);
+    if (rc) return rc;
+    const uint32_t* B = static_cast<const uint32_t*>(Bv);
+    // L_{col_offset + j} = eq_hi[(col_offset >> 6) + (j >> 6)] * eq_lo[j & 63]
+    const unsigned lo_vars = n_rj < 6 ? (unsigned)n_rj : 6u;
+    const unsigned hi_vars = (unsigned)n_rj - lo_vars;
+    const qm31* rj = reinterpret_cast<const qm31*>(r_j);
+    if ((rc = ctx->eq_hi.ensure(((size_t)16) << hi_vars)) || (rc = ctx->eq_lo.ensure(64 * 16))) return rc;
+    launch_eq_table(rj, (int)hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
+    launch_eq_table(rj + hi_vars, (int)lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
+    unsigned long long* acc = reinterpret_cast<unsigned long long*>(out_words);
+    ZK_CUDA(cudaMemsetAsync(acc, 0, k * 32, s));
+    const uint4* lhi = ctx->eq_hi.as<uint4>() + (col_offset >> 6);
+    const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n_block);
+    if (tc && (rc = ctx->rc_table.ensure(16 * ((n_block + 31) / 32 * 32)))) return rc;
+    {
+        KTimer t(ctx, KC_RESTRICT_COLS);
+        if (tc)
+            launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n_block, lhi, ctx->eq_lo.as<uint4>(),
+                                    ctx->rc_table.as<uint8_t>(), acc, ctx->err_flag(), ctx->num_sms, s);
+        else
+            launch_restrict_cols(B, (uint32_t)k, (uint32_t)n_block, lhi, ctx->eq_lo.as<uint4>(), acc, ctx->err_flag(),
+                                 ctx->num_sms, s);
+    }
+    // partial sums to canonical words (so that adding them across ranks cannot overflow)
+    launch_canon_u64(acc, 4 * k, s);
+    ctx->launches += tc ? 5 : 4;
+    ZK_CUDA(cudaGetLastError());
+    if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "restrict_cols_block"))) return rc;
     return ZKML_OK;
 }
 

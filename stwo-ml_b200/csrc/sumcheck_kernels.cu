@@ -486,6 +486,18 @@ void launch_acc_finalize(const unsigned long long* acc, size_t n_rows, uint4* ou
     acc_finalize_kernel<<<(unsigned)blocks, 256, 0, s>>>(acc, n_rows, out, out_len);
 }
 
+__global__ void canon_u64_kernel(unsigned long long* __restrict__ w, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        w[i] = red64(w[i]);
+}
+
+void launch_canon_u64(unsigned long long* w, size_t n, cudaStream_t s) {
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 8192) blocks = 8192;
+    if (blocks == 0) blocks = 1;
+    canon_u64_kernel<<<(unsigned)blocks, 256, 0, s>>>(w, n);
+}
+
 __global__ void canon_words_kernel(uint32_t* __restrict__ w, size_t n) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
         w[i] = red32(w[i]);

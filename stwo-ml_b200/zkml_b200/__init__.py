@@ -110,6 +110,11 @@ _SIGS = {
     "zkml_reduce_activation_piecewise": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int,
                                                    C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                                    C.c_size_t, C.POINTER(C.c_size_t), _u32, _u32]),
+    "zkml_restrict_cols_block": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
+                                           C.c_size_t, C.c_void_p]),
+    "zkml_reduce_matmul_layer_gkr_fb": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u32, C.c_void_p, C.c_size_t,
+                                                  C.c_size_t, C.c_void_p, C.c_size_t, C.POINTER(_Channel), _u32,
+                                                  _u32, _u32, _u32]),
     "zkml_weight_commitment": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, _u64]),
     "zkml_prove_aggregated_binding": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(_Channel),
                                                 C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),

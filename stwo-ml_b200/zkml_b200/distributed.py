@@ -26,7 +26,8 @@ from typing import List, Optional
 
 import numpy as np
 
-from . import (M31_P as P, PoseidonChannel, RoundPoly, Context, _Buf, _check, context, lib)
+from . import (M31_P as P, PoseidonChannel, RoundPoly, Context, GKRClaim, M31Matrix, MatMulReduction, _Buf, _check,
+               _log2, _next_pow2, _qm31_ptr, as_qm31_array, context, lib)
 
 ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_uint64), C.c_int)
 ALLGATHER_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t)
@@ -324,3 +325,78 @@ def prove_product_sharded(a_local, b_local, n: int, channel: PoseidonChannel, se
             gathered_at = glen
             sums = session.round(None)
     return ShardedSumcheckProof(polys, chals, final_a, final_b, gathered_at)
+
+
+# ---------------------------------------------------------------------------
+# One matmul layer split by column blocks of the weight
+# ---------------------------------------------------------------------------
+
+def column_block(n: int, rank: int, world: int):
+    """Columns [lo, hi) of B that `rank` holds: the padded column space next_pow2(n) cut into
+    `world` equal blocks (each a multiple of 64 columns), clipped to the n real columns
+    (a rank whose block is all padding holds none: lo == hi)."""
+    pn = _next_pow2(n)
+    block = pn // world
+    if block * world != pn or block % 64:
+        raise ValueError(f"next_pow2(n) = {pn} does not split into {world} blocks of a multiple of 64 columns")
+    lo = min(rank * block, n)
+    return lo, min(lo + block, n) if lo < n else lo
+
+
+def restrict_cols_block_words(b_block, k: int, col_offset: int, r_j, ctx: Optional[Context] = None):
+    """This rank's 4k partial words of f_b (a CUDA int64 tensor): its column block restricted
+    with the weights of the full padded column space (zkml_restrict_cols_block)."""
+    import torch
+    ctx = ctx or context(torch.cuda.current_device())
+    words = torch.zeros(4 * k, dtype=torch.int64, device=torch.device("cuda", ctx.device))
+    bm = b_block if isinstance(b_block, M31Matrix) else None
+    n_block = bm.cols if bm is not None else (int(b_block.shape[1]) if b_block is not None else 0)
+    if n_block:
+        bb = _Buf(bm.data if bm is not None else b_block)
+        rj = np.ascontiguousarray(as_qm31_array(r_j), np.uint32)
+        _check(lib().zkml_restrict_cols_block(ctx.handle, bb.ptr, k, n_block, col_offset,
+                                              rj.ctypes.data_as(C.c_void_p) if rj.size else None, len(rj),
+                                              C.c_void_p(words.data_ptr())))
+    return words
+
+
+def reduce_matmul_layer_from_words(output_claim: GKRClaim, a: M31Matrix, words, m: int, k: int, n: int,
+                                   channel: PoseidonChannel, ctx: Optional[Context] = None):
+    """The layer from the all-reduced partial words (zkml_reduce_matmul_layer_gkr_fb)."""
+    import torch
+    ctx = ctx or context(torch.cuda.current_device())
+    pm, pk, pn = _next_pow2(m), _next_pow2(k), _next_pow2(n)
+    log_m, log_k = _log2(pm), _log2(pk)
+    point = as_qm31_array(output_claim.point)
+    ab = _Buf(a.data)
+    pt_ptr, pt_keep = _qm31_ptr(point)
+    rp = np.zeros((max(log_k, 1), 12), np.uint32)
+    fa = np.zeros(4, np.uint32)
+    fb = np.zeros(4, np.uint32)
+    nxt = np.zeros((max(log_m + log_k, 1), 4), np.uint32)
+    _check(lib().zkml_reduce_matmul_layer_gkr_fb(ctx.handle, pt_ptr, len(point),
+                                                 np.ascontiguousarray(output_claim.value, np.uint32).reshape(4),
+                                                 ab.ptr, m, k, C.c_void_p(words.data_ptr()), n,
+                                                 C.byref(channel.state), rp.reshape(-1), fa, fb, nxt.reshape(-1)))
+    polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_k)]
+    red = MatMulReduction(polys, nxt[log_m:log_m + log_k].copy(), fa, fb)
+    return red, GKRClaim(nxt[:log_m + log_k].copy(), fa.copy())
+
+
+def reduce_matmul_layer_colsharded(output_claim: GKRClaim, a: M31Matrix, b_block, col_offset: int, m: int, k: int,
+                                   n: int, channel: PoseidonChannel, group=None, ctx: Optional[Context] = None):
+    """reduce_matmul_layer_with_backend (gkr/prover.rs:5959-6073) for a layer whose weight is
+    split by column blocks over the ranks of `group` (one GPU each; rank g holds
+    B[:, column_block(n, g, world)] as `b_block`, k x (hi - lo), device or host memory).
+    Each rank restricts its block; one NCCL all-reduce adds the 4k partial words; every rank
+    then runs the (small) sumcheck from the sum and returns the same reduction and next
+    claim as the unsplit layer."""
+    import torch.distributed as dist
+    pm, pn = _next_pow2(m), _next_pow2(n)
+    point = as_qm31_array(output_claim.point)
+    if len(point) != _log2(pm) + _log2(pn):
+        raise ValueError("output claim must have log2(pm) + log2(pn) variables")
+    words = restrict_cols_block_words(b_block, k, col_offset, point[_log2(pm):], ctx)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(words, group=group)
+    return reduce_matmul_layer_from_words(output_claim, a, words, m, k, n, channel, ctx)

@@ -318,6 +318,67 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+def run_colsharded(args):
+    """One C2 layer per step, B split by column blocks over the ranks: per rank the block
+    restriction, one NCCL all-reduce of the 4k partial words, and the (replicated) sumcheck."""
+    import torch
+    import torch.distributed as dist
+
+    import zkml_b200 as Z
+    from zkml_b200.distributed import column_block, reduce_matmul_layer_colsharded
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.cuda.current_device()
+    bind_to_gpu_cpus(dev)
+    ctx = Z.context(dev)
+    a, b = make_inputs(0)
+    lo, hi = column_block(N, rank, world)
+    A = Z.M31Matrix(M, K, torch.from_numpy(a.view(np.int32)).cuda().reshape(-1))
+    blk = torch.from_numpy(np.ascontiguousarray(b[:, lo:hi]).view(np.int32)).cuda() if hi > lo else None
+    ch0, point = seeded_channel_state(Z, 0)
+    claim = np.zeros(4, np.uint32)
+
+    def step():
+        return reduce_matmul_layer_colsharded(Z.GKRClaim(point, claim), A, blk, lo, M, K, N, ch0.clone(), ctx=ctx)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    t = torch.tensor([ms], device="cuda") if world > 1 else None
+    rank_ms = [ms]
+    if world > 1:
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        rank_ms = [float(x.item()) for x in parts]
+    ms = max(rank_ms)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC + " [one layer split by column blocks]", "value": ms / 1e3, "unit": "s/layer",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "u32 (M31/QM31 integer)",
+            "data": "synthetic (SplitMix64-seeded int8 embedded in M31)",
+            "config": {"workload": "C2 layer, B column blocks of next_pow2(n)/G columns, NCCL all-reduce of 4k words",
+                       "m": M, "k": K, "n": N, "ms_per_step_by_rank": [round(x, 4) for x in rank_ms]},
+            "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def time_next_rows(Z, torch, ta, tb, reps=5):
     """Wall time per call (host transcript included, inputs resident in HBM) of the layer
     reductions beside the matmul path, on config-2-shaped data: the forward GEMM, the SiLU
@@ -550,8 +611,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["c2", "product"], default="c2",
-                    help="c2: the headline matmul layer; product: the config-5 product sumcheck split across GPUs")
+    ap.add_argument("--workload", choices=["c2", "c2-colsharded", "product"], default="c2",
+                    help="c2: the headline matmul layer (one independent layer per GPU); c2-colsharded: one C2 "
+                         "layer with B split by column blocks across the GPUs (strong scaling); product: the "
+                         "config-5 product sumcheck split across GPUs")
     ap.add_argument("--log-n", type=int, default=28, help="product workload: log2 of the MLE length")
     args = ap.parse_args()
     if args.case:
@@ -561,6 +624,8 @@ def main():
         args.warmup = 3
     if args.workload == "product" and args.impl == "b200":
         run_product(args)
+    elif args.workload == "c2-colsharded" and args.impl == "b200":
+        run_colsharded(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -2702,3 +2702,255 @@ int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const 
     if (out_input_eval) q_store(out_input_eval, input_eval);
     return in.pos == len;
 }
+
+/* ---------------------------------------------------------------------------
+ * ReLU (algebraic product + bit decomposition) and the GKR walk over a chain of
+ * MatMul / ReLU layers.
+ * ------------------------------------------------------------------------- */
+
+#define RELU_BITS 30
+
+/* compute_combined_activation_eq_sum_at_t (gkr/prover.rs:6642-6690) */
+static q31 relu_sum_at(q31 *const *v, size_t mid, uint32_t t, const q31 *ep) {
+    q31 sum = q_from_m(0), one = q_from_m(1);
+    for (size_t i = 0; i < mid; i++) {
+        q31 x[3 + RELU_BITS];
+        for (int k = 0; k < 3 + RELU_BITS; k++) x[k] = q_add(v[k][i], q_mul_m(q_sub(v[k][mid + i], v[k][i]), t));
+        q31 eq = x[0], in = x[1], b = x[2];
+        q31 h = q_mul(q_mul(ep[0], b), in);
+        h = q_add(h, q_mul(q_mul(ep[1], b), q_sub(one, b)));
+        q31 bs = q_from_m(0);
+        uint32_t pw = 1;
+        for (int j = 0; j < RELU_BITS; j++) {
+            bs = q_add(bs, q_mul_m(x[3 + j], pw));
+            pw = m_add(pw, pw);
+        }
+        q31 dec = q_sub(q_sub(in, bs), q_mul_m(q_sub(one, b), pw));
+        h = q_add(h, q_mul(ep[2], dec));
+        for (int j = 0; j < RELU_BITS; j++) h = q_add(h, q_mul(q_mul(ep[3 + j], x[3 + j]), q_sub(one, x[3 + j])));
+        sum = q_add(sum, q_mul(eq, h));
+    }
+    return sum;
+}
+
+/* reduce_activation_layer_algebraic (gkr/prover.rs:6700-6890) on the rows x cols activation
+ * input; appends the LayerProof::Activation record (cairo_serde.rs:1355-1387, 1190-1235) to o
+ * and writes the next claim (point = challenges, value = input evaluation). */
+static int relu_reduce(const uint32_t *input, size_t rows, size_t cols, const q31 *point, q31 claim_value,
+                       orc_channel *ch, felt_out *o, q31 *next_point, q31 *next_value, int legacy) {
+    size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
+    unsigned nv = ilog2(n);
+    if (nv == 0) return 1;
+    const uint32_t half = 1073741823u;
+    q31 *v[3 + RELU_BITS];
+    for (int k = 0; k < 3 + RELU_BITS; k++) v[k] = (q31 *)calloc(n, sizeof(q31));
+    for (size_t i = 0; i < pr; i++)
+        for (size_t j = 0; j < pc; j++) {
+            size_t idx = i * pc + j;
+            uint32_t x = (i < rows && j < cols) ? m_red64(input[i * cols + j]) : 0;
+            v[1][idx] = q_from_m(x);
+            v[2][idx] = q_from_m(x <= half ? 1 : 0);
+            uint32_t low = x <= half ? x : x - (1u << 30);
+            for (int b = 0; b < RELU_BITS; b++) v[3 + b][idx] = q_from_m((low >> b) & 1);
+        }
+    orc_ch_mix_u64(ch, 0x414354);
+    ch_mix_sf(ch, claim_value);
+    q31 eta = ch_draw_qm31(ch), ep[3 + RELU_BITS];
+    ep[0] = q_from_m(1);
+    for (int i = 1; i < 3 + RELU_BITS; i++) ep[i] = q_mul(ep[i - 1], eta);
+    q31 *eq = lagrange_basis(point, nv);
+    memcpy(v[0], eq, sizeof(q31) * n);
+    free(eq);
+    q31 rp[64][4];
+    uint32_t inv2 = m_inv(2), inv6 = m_inv(6);
+    size_t cur = n;
+    for (unsigned r = 0; r < nv; r++) {
+        size_t mid = cur / 2;
+        q31 s0 = relu_sum_at(v, mid, 0, ep), s1 = relu_sum_at(v, mid, 1, ep);
+        q31 s2 = relu_sum_at(v, mid, 2, ep), s3 = relu_sum_at(v, mid, 3, ep);
+        q31 d1 = q_sub(s1, s0);
+        q31 d2 = q_mul_m(q_add(q_sub(q_sub(s2, s1), s1), s0), inv2);
+        q31 d3 = q_mul_m(q_sub(q_sub(s3, s0), q_mul_m(q_sub(s2, s1), 3)), inv6);
+        rp[r][0] = s0;
+        rp[r][1] = q_add(q_sub(d1, d2), q_mul_m(d3, 2));
+        rp[r][2] = q_sub(d2, q_mul_m(d3, 3));
+        rp[r][3] = d3;
+        mix_deg3(ch, rp[r][0], rp[r][1], rp[r][2], rp[r][3]);
+        next_point[r] = ch_draw_qm31(ch);
+        for (int k = 0; k < 3 + RELU_BITS; k++) fold_vec(v[k], mid, next_point[r]);
+        cur = mid;
+    }
+    for (int k = 1; k < 3 + RELU_BITS; k++) ch_mix_sf(ch, v[k][0]);
+    fe zero;
+    fe_u64(&zero, 0);
+    out_u64(o, 3);
+    out_u64(o, 1); /* ReLU type tag */
+    out_qm31(o, v[1][0]);
+    out_qm31(o, claim_value);
+    out_push(o, &zero);
+    out_u64(o, 0); /* no LogUp proof */
+    if (!legacy) out_u64(o, 0); /* no multiplicity sumcheck */
+    out_u64(o, 1); /* activation product proof */
+    out_u64(o, nv);
+    for (unsigned r = 0; r < nv; r++) {
+        out_qm31(o, rp[r][0]);
+        out_qm31(o, rp[r][2]);
+        out_qm31(o, rp[r][3]);
+    }
+    out_qm31(o, v[1][0]);
+    out_qm31(o, v[2][0]);
+    out_u64(o, 1);
+    out_u64(o, RELU_BITS);
+    for (int b = 0; b < RELU_BITS; b++) out_qm31(o, v[3 + b][0]);
+    if (!legacy) out_u64(o, 0); /* no piecewise proof */
+    *next_value = v[1][0];
+    for (int k = 0; k < 3 + RELU_BITS; k++) free(v[k]);
+    return 0;
+}
+
+/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for a chain GraphBuilder::new((m, k0))
+ * .linear(..)/.activation(ReLU).. in Sequential weight-binding mode, serialized by
+ * serialize_gkr_model_proof (cairo_serde.rs:1307-1772). */
+int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
+                        const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
+                        size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads) {
+    oracle_init();
+    if (n_layers == 0 || n_layers > 64) return 1;
+    /* forward pass: acts[l] is layer l's input (m x width[l]) */
+    uint32_t *acts[65];
+    size_t width[65];
+    acts[0] = (uint32_t *)malloc(4 * m * k0);
+    for (size_t i = 0; i < m * k0; i++) acts[0][i] = m_red64(input[i]);
+    width[0] = k0;
+    for (size_t l = 0; l < n_layers; l++) {
+        size_t w = width[l];
+        if (layers[l].type == 0) {
+            if (!layers[l].weight || layers[l].n == 0) return 1;
+            acts[l + 1] = (uint32_t *)malloc(4 * m * layers[l].n);
+            orc_matmul_m31(acts[l], m, w, layers[l].weight, layers[l].n, acts[l + 1], threads);
+            width[l + 1] = layers[l].n;
+        } else if (layers[l].type == 1) {
+            acts[l + 1] = (uint32_t *)malloc(4 * m * w);
+            for (size_t i = 0; i < m * w; i++) acts[l + 1][i] = acts[l][i] <= 1073741823u ? acts[l][i] : 0;
+            width[l + 1] = w;
+        } else {
+            return 1;
+        }
+    }
+    orc_channel ch;
+    orc_ch_init(&ch);
+    orc_ch_mix_u64(&ch, n_layers);
+    orc_ch_mix_u64(&ch, m);
+    orc_ch_mix_u64(&ch, k0);
+    if (policy && (policy[0] | policy[1] | policy[2] | policy[3])) orc_ch_mix_felt(&ch, policy);
+    size_t wout = width[n_layers];
+    unsigned log_m = ilog2(next_pow2(m));
+    unsigned nvo = log_m + ilog2(next_pow2(wout));
+    q31 point[64], value;
+    for (unsigned i = 0; i < nvo; i++) point[i] = ch_draw_qm31(&ch);
+    {
+        q31 *omle = mle_row_major(acts[n_layers], m, wout);
+        uint32_t val[4];
+        orc_evaluate_mle((const uint32_t *)omle, nvo, (const uint32_t *)point, val);
+        free(omle);
+        value = q_load(val);
+    }
+    ch_mix_sf(&ch, value);
+    unsigned npt = nvo;
+    felt_out o = {calldata, 0, cap, 0};
+    out_u64(&o, n_layers);
+    /* weight claims in walk order */
+    q31 *wpts[64];
+    unsigned wnv[64];
+    q31 wval[64];
+    size_t widx[64], nw = 0;
+    int rc = 0;
+    for (size_t li = n_layers; li-- > 0 && !rc;) {
+        size_t w = width[li];
+        if (layers[li].type == 0) {
+            size_t n = layers[li].n;
+            unsigned log_k = ilog2(next_pow2(w)), log_n = ilog2(next_pow2(n));
+            uint32_t *rp = (uint32_t *)malloc(48 * (log_k + 1));
+            uint32_t fa[4], fb[4];
+            q31 nxt[64];
+            uint32_t cv[4];
+            q_store(cv, value);
+            rc = orc_reduce_matmul_gkr((const uint32_t *)point, npt, cv, acts[li], m, w, layers[li].weight, n, &ch, rp,
+                                       fa, fb, (uint32_t *)nxt, 1, threads);
+            if (rc) {
+                free(rp);
+                break;
+            }
+            out_u64(&o, 0);
+            out_u64(&o, log_k);
+            for (unsigned r = 0; r < log_k; r++) {
+                out_qm31(&o, q_load(rp + 12 * r));
+                out_qm31(&o, q_load(rp + 12 * r + 8));
+            }
+            out_qm31(&o, q_load(fa));
+            out_qm31(&o, q_load(fb));
+            /* weight claim: r_j || sumcheck challenges (prover.rs:1465-1483) */
+            wnv[nw] = log_n + log_k;
+            wpts[nw] = (q31 *)malloc(sizeof(q31) * (wnv[nw] + 1));
+            memcpy(wpts[nw], point + log_m, sizeof(q31) * log_n);
+            memcpy(wpts[nw] + log_n, nxt + log_m, sizeof(q31) * log_k);
+            wval[nw] = q_load(fb);
+            widx[nw] = li;
+            nw++;
+            memcpy(point, nxt, sizeof(q31) * (log_m + log_k));
+            npt = log_m + log_k;
+            value = q_load(fa);
+            free(rp);
+        } else {
+            q31 nxt[64], nval;
+            rc = relu_reduce(acts[li], m, w, point, value, &ch, &o, nxt, &nval, flags & 1);
+            npt = ilog2(next_pow2(m) * next_pow2(w));
+            memcpy(point, nxt, sizeof(q31) * npt);
+            value = nval;
+        }
+    }
+    if (!rc) {
+        /* input claim */
+        out_u64(&o, npt);
+        for (unsigned i = 0; i < npt; i++) out_qm31(&o, point[i]);
+        out_qm31(&o, value);
+        /* Sequential weight openings on the main channel, in walk order */
+        fe coms[64];
+        uint64_t *obufs[64];
+        size_t olens[64];
+        for (size_t i = 0; i < nw; i++) {
+            size_t l = widx[i];
+            q31 *bmle = mle_col_major(layers[l].weight, width[l], layers[l].n, threads);
+            size_t ocap = 64 + (n_queries + 1) * (2 + (size_t)wnv[i] * (10 + 2 * (wnv[i] + 1)));
+            obufs[i] = (uint64_t *)malloc(32 * ocap);
+            felt_out oo = {obufs[i], 0, ocap, 0};
+            prove_opening(bmle, wnv[i], wpts[i], &ch, n_queries, &coms[i], &oo, NULL, threads);
+            olens[i] = oo.len;
+            free(bmle);
+        }
+        out_u64(&o, nw);
+        for (size_t i = 0; i < nw; i++) out_push(&o, &coms[i]);
+        out_u64(&o, nw);
+        for (size_t i = 0; i < nw; i++) {
+            out_u64(&o, wnv[i]);
+            for (unsigned j = 0; j < wnv[i]; j++) out_qm31(&o, wpts[i][j]);
+            out_qm31(&o, wval[i]);
+            for (size_t j = 0; j < olens[i]; j++) {
+                fe f;
+                fe_from_canon(&f, obufs[i] + 4 * j);
+                out_push(&o, &f);
+            }
+            free(obufs[i]);
+        }
+        orc_io_commitment(acts[0], m, k0, acts[n_layers], m, wout, io);
+        fe iof;
+        fe_from_canon(&iof, io);
+        out_push(&o, &iof);
+        memcpy(digest, ch.digest, 32);
+        *out_len = o.len;
+    }
+    for (size_t i = 0; i < nw; i++) free(wpts[i]);
+    for (size_t l = 0; l <= n_layers; l++) free(acts[l]);
+    if (rc) return rc;
+    return o.overflow ? 2 : 0;
+}

@@ -194,6 +194,22 @@ int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const 
                                     size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
                                     uint32_t out_input_eval[4]);
 
+/* One layer of a sequential GKR chain: type 0 = Linear (weight: rows = the layer's input
+ * width, n columns, row major), type 1 = ReLU. */
+typedef struct {
+    int type;
+    const uint32_t *weight;
+    size_t n;
+} orc_chain_layer;
+/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for GraphBuilder::new((m, k0)) followed by
+ * the given Linear / ReLU layers, Sequential weight binding, serialized by
+ * serialize_gkr_model_proof (cairo_serde.rs:1307-1772).  Writes the final digest and the
+ * io commitment.  flags bit 0: the earlier Activation record layout without the
+ * multiplicity-sumcheck and piecewise flags (the layout of engine/tests/artifacts/sp3_mlp_proof.json). */
+int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
+                        const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
+                        size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads);
+
 /* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
 void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
                     uint32_t *c, int threads);

@@ -8,6 +8,11 @@ reference's own known answers for the matmul-sumcheck path:
   produced by engine/tests/e2e_cairo_verify.rs:1093-1180 (1x4 input [1,2,3,4],
   weight W[i][j] = 2i+j+1, 4x2) -- full GKR calldata, weight commitment,
   weight claims, weight-opening calldata, io commitment, final channel digest.
+* ``sp3_mlp``: engine/tests/artifacts/sp3_mlp_proof.json, produced by
+  engine/tests/e2e_cairo_verify.rs:978-1040 from build_gkr_mlp_relu (272-304): 1x4 input
+  [1,2,3,4] -> Linear(4) with W0[i][j] = (i+j)%7+1 -> ReLU -> Linear(2) with
+  W2[i][j] = i+j+1 -- full GKR calldata (780 felts), weight commitments, io commitment,
+  final channel digest.
 * ``poseidon_kats``: engine/src/crypto/poseidon_channel.rs:1619-1637
   (poseidon_hash_many([0, pack(QM31(1,2,3,4))])) and
   stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs:230-241
@@ -22,6 +27,7 @@ from pathlib import Path
 
 ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
 art = json.loads((ref / "engine/tests/artifacts/sp3_matmul_only_proof.json").read_text())
+mlp = json.loads((ref / "engine/tests/artifacts/sp3_mlp_proof.json").read_text())
 out = {
     "sp3_matmul_only": {
         "source": "engine/tests/artifacts/sp3_matmul_only_proof.json",
@@ -35,6 +41,19 @@ out = {
         "weight_opening_calldata_hex": art["weight_opening_calldata_hex"],
         "io_commitment": art["io_commitment"],
         "final_channel_digest": art["verification"]["final_channel_digest"],
+    },
+    "sp3_mlp": {
+        "source": "engine/tests/artifacts/sp3_mlp_proof.json",
+        "input": mlp["input_data"],
+        "input_shape": mlp["model"]["input_shape"],
+        "layers": mlp["model"]["layers"],
+        "weights": [[[(i + j) % 7 + 1 for j in range(4)] for i in range(4)],
+                    [[i + j + 1 for j in range(2)] for i in range(4)]],
+        "output": mlp["output_data"],
+        "calldata_hex": mlp["calldata_hex"],
+        "weight_commitments": mlp["weight_commitments"],
+        "io_commitment": mlp["io_commitment"],
+        "final_channel_digest": mlp["verification"]["final_channel_digest"],
     },
     "poseidon_kats": [
         {
@@ -56,6 +75,9 @@ src1 = (ref / "engine/src/crypto/poseidon_channel.rs").read_text()
 src2 = (ref / "stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs").read_text()
 assert out["poseidon_kats"][0]["expect"] in src1
 assert out["poseidon_kats"][1]["expect"] in src2
+# Sanity: the MLP weights are the ones build_gkr_mlp_relu sets.
+src3 = (ref / "engine/tests/e2e_cairo_verify.rs").read_text()
+assert "M31::from(((i + j) % 7 + 1) as u32)" in src3 and "M31::from((i + j + 1) as u32)" in src3
 dst = Path(__file__).with_name("reference_vectors.json")
 dst.write_text(json.dumps(out, indent=1) + "\n")
 print("wrote", dst)

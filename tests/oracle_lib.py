@@ -90,6 +90,8 @@ def lib():
         L.orc_reduce_activation_piecewise.argtypes = [u32p, sz, sz, C.c_int, u32p, sz, u32p, chp, u64p, sz,
                                                       C.POINTER(sz), u32p, u32p]
         L.orc_verify_activation_piecewise.argtypes = [u64p, sz, u32p, sz, u32p, chp, u32p]
+        L.orc_prove_gkr_chain.argtypes = [u32p, sz, sz, C.c_void_p, sz, C.c_void_p, sz, C.c_int, u64p, sz,
+                                          C.POINTER(sz), u64p, u64p, C.c_int]
         L.orc_rsqrt_table.argtypes = [C.c_uint, u32p]
         L.orc_reduce_rmsnorm.argtypes = [u32p, sz, sz, sz, C.c_void_p, sz, C.c_int, u32p, sz, u32p, chp, u64p,
                                          sz, C.POINTER(sz), u32p]
@@ -342,3 +344,32 @@ def verify_activation_piecewise(raw, point, value, ch):
                                                point.reshape(-1), len(point), np.ascontiguousarray(value, np.uint32),
                                                C.byref(ch), ie)
     return bool(ok), ie
+
+
+class ChainLayer(C.Structure):
+    _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t)]
+
+
+def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, cap=1 << 18):
+    """layers: list of ("linear", weight (rows, n)) or ("relu", None)."""
+    inp = np.ascontiguousarray(inp, np.uint32)
+    m, k0 = inp.shape
+    keep = []
+    arr = (ChainLayer * len(layers))()
+    for i, (kind, w) in enumerate(layers):
+        if kind == "linear":
+            w = np.ascontiguousarray(w, np.uint32)
+            keep.append(w)
+            arr[i].type, arr[i].weight, arr[i].n = 0, w.ctypes.data, w.shape[1]
+        else:
+            arr[i].type, arr[i].weight, arr[i].n = 1, None, 0
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    dig = np.zeros(4, np.uint64)
+    io = np.zeros(4, np.uint64)
+    pol = None if policy is None else felt(policy)
+    rc = lib().orc_prove_gkr_chain(inp.reshape(-1), m, k0, C.cast(arr, C.c_void_p), len(layers),
+                                   None if pol is None else pol.ctypes.data_as(C.c_void_p), n_queries,
+                                   int(legacy_layout), buf, cap,
+                                   C.byref(ln), dig, io, threads())
+    return rc, buf[:4 * ln.value].copy(), felt_int(dig), felt_int(io)

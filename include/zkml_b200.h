@@ -239,6 +239,40 @@ int zkml_reduce_activation_piecewise(zkml_ctx *ctx, const uint32_t *input, size_
                                      zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                      uint32_t out_input_eval[4], uint32_t *out_point);
 
+/* reduce_activation_layer_algebraic (gkr/prover.rs:6700-6890), the proof of a ReLU layer:
+ * product + indicator + 30-bit decomposition constraints in one degree-3 eq-sumcheck.
+ * Writes the LayerProof::Activation record with the activation product proof
+ * (cairo_serde.rs:1355-1387, 1190-1235), the input evaluation and, if out_point is set,
+ * the next claim's point (the sumcheck challenges). */
+int zkml_reduce_activation_relu(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_t cols,
+                                const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                                zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
+                                uint32_t out_input_eval[4], uint32_t *out_point);
+
+/* ---- GKR proof of a Linear / ReLU chain ------------------------------------------ */
+
+#define ZKML_LAYER_LINEAR 0
+#define ZKML_LAYER_RELU 1
+/* flags: the Activation record without the multiplicity-sumcheck and piecewise flags, the
+ * layout of the reference's engine/tests/artifacts/sp3_mlp_proof.json */
+#define ZKML_CHAIN_LEGACY_ACTIVATION_RECORD 1
+
+typedef struct {
+    int type;               /* ZKML_LAYER_LINEAR or ZKML_LAYER_RELU */
+    const uint32_t *weight; /* Linear: (input width) x n, row major, host or device memory */
+    size_t n;               /* Linear: output width */
+} zkml_chain_layer;
+
+/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for GraphBuilder::new((m, k0)) followed by
+ * the given layers, from a fresh PoseidonChannel, Sequential weight binding (one MLE opening
+ * per weight, n_queries queries, on the main channel), serialized by
+ * serialize_gkr_model_proof (cairo_serde.rs:1307-1772).  The forward pass runs on the GPU.
+ * policy may be NULL (no policy mix).  Writes the final channel digest and the io commitment. */
+int zkml_prove_gkr_chain(zkml_ctx *ctx, const uint32_t *input, size_t m, size_t k0, const zkml_chain_layer *layers,
+                         size_t n_layers, const uint64_t *policy, size_t n_queries, int flags,
+                         uint64_t *out_calldata, size_t cap, size_t *out_len, uint64_t out_digest[4],
+                         uint64_t out_io[4]);
+
 /* ---- Aggregated weight binding ------------------------------------------------ */
 
 /* A weight claim of the GKR walk (AggregatedWeightClaim, crypto/aggregated_opening.rs:99-112).

@@ -2954,3 +2954,19 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     if (rc) return rc;
     return o.overflow ? 2 : 0;
 }
+
+int orc_reduce_activation_relu(const uint32_t *input, size_t rows, size_t cols, const uint32_t *claim_point,
+                               size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                               size_t cap, size_t *out_len, uint32_t out_input_eval[4], uint32_t *out_point) {
+    oracle_init();
+    unsigned nv = ilog2(next_pow2(rows) * next_pow2(cols));
+    if (n_point < nv || nv == 0 || nv > 40) return 1;
+    felt_out o = {calldata, 0, cap, 0};
+    q31 nxt[64], val;
+    int rc = relu_reduce(input, rows, cols, (const q31 *)claim_point, q_load(claim_value), ch, &o, nxt, &val, 0);
+    if (rc) return rc;
+    *out_len = o.len;
+    if (out_input_eval) q_store(out_input_eval, val);
+    if (out_point) memcpy(out_point, nxt, sizeof(q31) * nv);
+    return o.overflow ? 2 : 0;
+}

@@ -210,6 +210,13 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
                         const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
                         size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads);
 
+/* reduce_activation_layer_algebraic (gkr/prover.rs:6700-6890), the ReLU proof, serialized as
+ * LayerProof::Activation with the activation product proof (cairo_serde.rs:1355-1387,
+ * 1190-1235).  out_point receives the next claim's point (the sumcheck challenges). */
+int orc_reduce_activation_relu(const uint32_t *input, size_t rows, size_t cols, const uint32_t *claim_point,
+                               size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                               size_t cap, size_t *out_len, uint32_t out_input_eval[4], uint32_t *out_point);
+
 /* M31 matmul C = A.B mod p (components/matmul.rs:572-627) */
 void orc_matmul_m31(const uint32_t *a, size_t m, size_t k, const uint32_t *b, size_t n,
                     uint32_t *c, int threads);

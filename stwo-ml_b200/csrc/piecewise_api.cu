@@ -25,6 +25,7 @@
 #include "calldata.hpp"
 #include "channel.hpp"
 #include "context.hpp"
+#include "deg3_terms.cuh"
 #include "logup_device.cuh"
 
 namespace zk {
@@ -48,26 +49,6 @@ struct PwConsts {
 constexpr size_t PW_THREAD_MIN_PAIRS = (size_t)1 << 16;
 
 __device__ __forceinline__ uint32_t pw_seg(uint32_t x) { return min(x >> 27, 15u); }
-
-// h(t) = h0 + h1 t + h2 t^2 accumulated lazily over one pair.
-struct PwAcc {
-    QAcc H0, H1, H2;
-};
-
-// One indicator (or segment bit) with value x0 + t xd: adds x (u - g in - e x), where
-// in = in0 + t ind and g is null for a segment bit.
-__device__ __forceinline__ void pw_term(PwAcc& a, const qm31& x0, const qm31& xd, const qm31& u, const qm31* g,
-                                        const qm31& e, const qm31& in0, const qm31& ind) {
-    qm31 y0 = qsub(u, qmul_f(e, x0)), yd = qsub(qzero(), qmul_f(e, xd));
-    if (g) {
-        y0 = qsub(y0, qmul_f(*g, in0));
-        yd = qsub(yd, qmul_f(*g, ind));
-    }
-    qacc_mul(a.H0, x0, y0);
-    qacc_mul(a.H1, x0, yd);
-    qacc_mul(a.H1, xd, y0);
-    qacc_mul(a.H2, xd, yd);
-}
 
 // Folded rounds (2 and later), one thread per pair: each of the 23 vectors is folded
 // 2h -> h in place and its pair (i, i + q), q = h / 2, is added to h(t).

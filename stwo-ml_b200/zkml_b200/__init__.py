@@ -115,6 +115,12 @@ _SIGS = {
     "zkml_reduce_matmul_layer_gkr_fb": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u32, C.c_void_p, C.c_size_t,
                                                   C.c_size_t, C.c_void_p, C.c_size_t, C.POINTER(_Channel), _u32,
                                                   _u32, _u32, _u32]),
+    "zkml_reduce_activation_relu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p,
+                                              C.c_size_t, _u32, C.POINTER(_Channel), _u64, C.c_size_t,
+                                              C.POINTER(C.c_size_t), _u32, _u32]),
+    "zkml_prove_gkr_chain": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
+                                       C.c_void_p, C.c_size_t, C.c_int, _u64, C.c_size_t, C.POINTER(C.c_size_t),
+                                       _u64, _u64]),
     "zkml_weight_commitment": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, _u64]),
     "zkml_prove_aggregated_binding": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(_Channel),
                                                 C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),
@@ -696,6 +702,78 @@ def reduce_activation_layer_piecewise(output_claim: GKRClaim, inp: M31Matrix, ac
                                                   nxt.reshape(-1)))
     proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
     return proof, GKRClaim(nxt[:n_point].copy(), ie.copy())
+
+
+def reduce_activation_layer_relu(output_claim: GKRClaim, inp: M31Matrix, channel: PoseidonChannel,
+                                 device: int = 0) -> Tuple[ActivationLogUpProof, GKRClaim]:
+    """gkr/prover.rs:6700-6890 (ReLU, algebraic).  Returns the LayerProof::Activation record and
+    the next claim (the sumcheck challenges, the input evaluation)."""
+    buf = _Buf(inp.data)
+    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
+    n_point = len(as_qm31_array(output_claim.point))
+    cap = 256 + 12 * n_point
+    out = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    nxt = np.zeros((max(n_point, 1), 4), np.uint32)
+    _check(lib().zkml_reduce_activation_relu(context(device).handle, buf.ptr, inp.rows, inp.cols, pt_ptr, n_point,
+                                             np.ascontiguousarray(output_claim.value, np.uint32),
+                                             C.byref(channel.state), out, cap, C.byref(ln), ie, nxt.reshape(-1)))
+    return ActivationLogUpProof(out[:4 * ln.value].copy(), ie), GKRClaim(nxt[:n_point].copy(), ie.copy())
+
+
+class _ChainLayer(C.Structure):
+    _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t)]
+
+
+@dataclass
+class GKRChainProof:
+    raw: np.ndarray       # serialize_gkr_model_proof, 4 x u64 limbs per felt
+    final_digest: int
+    io_commitment: int
+
+    @property
+    def calldata(self) -> List[int]:
+        return _felts(self.raw, self.raw.size // 4)
+
+
+def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_queries: Optional[int] = None,
+                    legacy_activation_record: bool = False, device: int = 0) -> GKRChainProof:
+    """prove_gkr (gkr/prover.rs:1500-2251) for GraphBuilder::new(inp.shape) followed by `layers`,
+    each ("linear", weight) with weight (in_width, n) or ("relu", None); Sequential weight
+    binding."""
+    im = as_matrix(inp)
+    ib = _Buf(im.data)
+    keep = [ib]
+    arr = (_ChainLayer * len(layers))()
+    width, nv_max, n_lin = im.cols, 0, 0
+    for i, (kind, w) in enumerate(layers):
+        if kind == "linear":
+            wm = as_matrix(w)
+            if wm.rows != width:
+                raise InvalidArgument(1, f"layer {i}: weight rows {wm.rows} != input width {width}")
+            wb = _Buf(wm.data)
+            keep.append(wb)
+            arr[i].type, arr[i].weight, arr[i].n = 0, wb.ptr.value, wm.cols
+            nv_max = max(nv_max, _log2(_next_pow2(wm.rows)) + _log2(_next_pow2(wm.cols)))
+            width = wm.cols
+            n_lin += 1
+        elif kind == "relu":
+            arr[i].type, arr[i].weight, arr[i].n = 1, None, 0
+        else:
+            raise InvalidArgument(1, f"layer {i}: unknown kind {kind}")
+    nq = mle_n_queries() if n_queries is None else n_queries
+    nv_all = _log2(_next_pow2(im.rows)) + max(nv_max, _log2(_next_pow2(width)) + 1)
+    cap = 256 + len(layers) * (200 + 12 * nv_all) + n_lin * (64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1))))
+    out = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    dig = np.zeros(4, np.uint64)
+    io = np.zeros(4, np.uint64)
+    pol = felt_to_limbs(policy_commitment) if policy_commitment else None
+    _check(lib().zkml_prove_gkr_chain(context(device).handle, ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
+                                      len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq,
+                                      1 if legacy_activation_record else 0, out, cap, C.byref(ln), dig, io))
+    return GKRChainProof(out[:4 * ln.value].copy(), limbs_to_felt(dig), limbs_to_felt(io))
 
 
 @dataclass

@@ -92,6 +92,8 @@ def lib():
         L.orc_verify_activation_piecewise.argtypes = [u64p, sz, u32p, sz, u32p, chp, u32p]
         L.orc_prove_gkr_chain.argtypes = [u32p, sz, sz, C.c_void_p, sz, C.c_void_p, sz, C.c_int, u64p, sz,
                                           C.POINTER(sz), u64p, u64p, C.c_int]
+        L.orc_reduce_activation_relu.argtypes = [u32p, sz, sz, u32p, sz, u32p, chp, u64p, sz, C.POINTER(sz), u32p,
+                                                 u32p]
         L.orc_rsqrt_table.argtypes = [C.c_uint, u32p]
         L.orc_reduce_rmsnorm.argtypes = [u32p, sz, sz, sz, C.c_void_p, sz, C.c_int, u32p, sz, u32p, chp, u64p,
                                          sz, C.POINTER(sz), u32p]
@@ -373,3 +375,18 @@ def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False,
                                    int(legacy_layout), buf, cap,
                                    C.byref(ln), dig, io, threads())
     return rc, buf[:4 * ln.value].copy(), felt_int(dig), felt_int(io)
+
+
+def reduce_activation_relu(inp, point, value, ch, cap=1 << 14):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    rows, cols = inp.shape
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    nxt = np.zeros((max(len(point), 1), 4), np.uint32)
+    rc = lib().orc_reduce_activation_relu(inp.reshape(-1), rows, cols, point.reshape(-1), len(point),
+                                          np.ascontiguousarray(value, np.uint32), C.byref(ch), buf, cap, C.byref(ln),
+                                          ie, nxt.reshape(-1))
+    nv = (rows - 1).bit_length() + (cols - 1).bit_length()
+    return rc, buf[:4 * ln.value].copy(), ie, nxt[:nv].copy()

@@ -566,6 +566,15 @@ def run_case(name):
         g = (np.arange(cols, dtype=np.uint32) % 1000) + 1
         for _ in range(2):
             Z.reduce_rmsnorm_layer(Z.GKRClaim(pt, val), Z.M31Matrix.from_numpy(x), cols, Z.PoseidonChannel(), gamma=g)
+    elif name.startswith("gemm_"):  # forward M31 GEMM M x K x N (e.g. gemm_64x5120x13824), three times
+        m_, k_, n_ = (int(v) for v in name.split("_")[1].split("x"))
+        a = torch.randint(-127, 128, (m_, k_), dtype=torch.int32, device="cuda")
+        b = torch.randint(-127, 128, (k_, n_), dtype=torch.int32, device="cuda")
+        a = torch.where(a < 0, a + (2**31 - 1), a)
+        b = torch.where(b < 0, b + (2**31 - 1), b)
+        c = torch.empty(m_ * n_, dtype=torch.int32, device="cuda")
+        for _ in range(3):
+            Z.matmul_m31(Z.M31Matrix(m_, k_, a.reshape(-1)), Z.M31Matrix(k_, n_, b.reshape(-1)), out=c)
     elif name.startswith("piecewise_"):  # piecewise SiLU layer R x C (e.g. piecewise_64x13824), twice
         rows, cols = (int(v) for v in name.split("_")[1].split("x"))
         x = int_matrix_m31(rows, cols, 3, bound=60000)

@@ -94,8 +94,10 @@ struct LogupScratch {
 // Device scratch of the Merkle commitment and the MLE opening (grown on demand).
 struct OpeningScratch {
     DevBuf layers, trees, idx, gathered, qvals, nodes, cbuf, bmle;
+    DevBuf adig;   // signed byte digits of the forward GEMM's left operand
+    DevBuf gpart;  // the forward GEMM's per-K-split partial products
     void release() {
-        DevBuf* all[] = {&layers, &trees, &idx, &gathered, &qvals, &nodes, &cbuf, &bmle};
+        DevBuf* all[] = {&layers, &trees, &idx, &gathered, &qvals, &nodes, &cbuf, &bmle, &adig, &gpart};
         for (DevBuf* b : all) b->release();
     }
 };

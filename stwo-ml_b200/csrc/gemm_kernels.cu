@@ -12,6 +12,7 @@
 // chunk ends with sum_w 256^w acc_w mod P added to 64-bit lazy sums.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
 
 #include "context.hpp"
@@ -131,6 +132,201 @@ __global__ void __launch_bounds__(4 * NT * KS * 32) m31_gemm_tc_kernel(const uin
     }
 }
 
+// ---------------------------------------------------------------------------
+// Narrow-value path.  Quantised layers carry small signed values (int8 weights, int16
+// activations embedded in M31 as v or p - |v|).  Read as signed integers, an A value is
+// a = 256 a_1 + a_0 with a_0 in [0, 256) and a_1 in [-128, 128) (every int16), a B value
+// is one signed byte, so C = A_0 B + 256 A_1 B takes one u8 x s8 and one s8 x s8 MMA per
+// element pair instead of the 16 u8 byte-plane pairs.  A value that does not fit sets a
+// flag and the caller recomputes with the full kernel, so the result is the same exact
+// product for every input.
+constexpr int GEMM_GA = 2;        // byte digits of A
+
+// A (m x k, row major) -> GA digit planes, each m x kp int8 (kp = k rounded up to 32,
+// zero padded); sets *narrow_bad if a value needs more digits.
+__global__ void gemm_a_digits_kernel(const uint32_t* __restrict__ A, uint32_t m, uint32_t k, uint32_t kp,
+                                     int8_t* __restrict__ D, uint32_t* __restrict__ narrow_bad) {
+    uint32_t bad = 0;
+    const size_t total = (size_t)m * kp;
+    for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (size_t)gridDim.x * blockDim.x) {
+        const uint32_t r = (uint32_t)(idx / kp), c = (uint32_t)(idx % kp);
+        const int q = c < k ? m31_signed(A[(size_t)r * k + c]) : 0;
+        const int d0 = q & 0xff, d1 = (q - d0) >> 8;  // q = 256 d1 + d0, d0 unsigned
+        D[idx] = (int8_t)(uint8_t)d0;
+        D[total + idx] = (int8_t)d1;
+        bad |= (uint32_t)(d1 < -128 || d1 > 127);
+    }
+    if (bad) atomicOr(narrow_bad, 1u);
+}
+
+// One block: 64 rows (4 row tiles) x GN_COLS columns, 8 warps = 4 row tiles x 2 column
+// halves (4 N-tiles each).  Per stage of GN_BK rows of K, the block loads the B tile
+// (GN_BK rows x GN_COLS columns, 16-byte coalesced loads along the rows), converts it once
+// to signed bytes and stores it transposed ([column][k], pitch GN_BK + 4 bytes) in shared
+// memory, where each B fragment is one 4-byte read; the block's A digit tile (64 rows x
+// GN_BK, both digits) is staged beside it.  The next stage's tiles are loaded into registers
+// while this stage's MMAs run.
+// gridDim.z splits K: each split writes its partial products (mod p) to its own plane of
+// `part`, added by gemm_combine_kernel.
+constexpr int GN_COLS = 64;
+constexpr int GN_BK = 64;
+constexpr int GN_PITCH = GN_BK + 4;
+constexpr int GN_PIECES = GN_BK * GN_COLS / 4 / 256;  // 4-column pieces per thread and stage
+constexpr int GN_APITCH = GN_BK + 16;                  // A tile row pitch (bytes)
+constexpr int GN_APIECES = GEMM_GA * 64 * GN_BK / 16 / 256;  // 16-byte A pieces per thread and stage
+
+__global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __restrict__ D,
+                                                              const uint32_t* __restrict__ B,
+                                                              uint32_t* __restrict__ part, uint32_t m, uint32_t k,
+                                                              uint32_t kp, uint32_t n,
+                                                              uint32_t* __restrict__ narrow_bad) {
+    __shared__ __align__(16) uint8_t bs[2][GN_COLS * GN_PITCH];
+    __shared__ __align__(16) uint8_t as[2][GEMM_GA * 64 * GN_APITCH];
+    const uint32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tg = lane & 3;
+    const uint32_t rt = warp & 3, ch = warp >> 2;  // row tile, column half
+    const uint32_t r0 = blockIdx.y * 64 + rt * 16 + g, r1 = r0 + 8;
+    const uint32_t col0 = blockIdx.x * GN_COLS;
+    const size_t plane = (size_t)m * kp;
+    const bool vec_ok = (n % 4 == 0) && ((reinterpret_cast<uintptr_t>(B) & 15) == 0);
+    // this block's stages (of GN_BK rows) of the K range
+    const uint32_t stages = (kp + GN_BK - 1) / GN_BK, per = (stages + gridDim.z - 1) / gridDim.z;
+    const uint32_t s_begin = min(stages, blockIdx.z * per), s_end = min(stages, s_begin + per);
+    uint32_t raw[GN_PIECES][4];
+    uint4 araw[GN_APIECES];
+    auto load_tile = [&](uint32_t sg) {
+#pragma unroll
+        for (int h = 0; h < GN_APIECES; h++) {
+            const uint32_t idx = tid + 256 * h, per_row = GN_BK / 16, dg = idx / (64 * per_row);
+            const uint32_t row = (idx / per_row) % 64, c16 = idx % per_row;
+            const uint32_t grow = blockIdx.y * 64 + row, kk = GN_BK * sg + 16 * c16;
+            araw[h] = (grow < m && kk < kp)
+                          ? __ldg(reinterpret_cast<const uint4*>(D + dg * plane + (size_t)grow * kp + kk))
+                          : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int h = 0; h < GN_PIECES; h++) {
+            const uint32_t idx = tid + 256 * h, tr = idx >> 4, c4 = (idx & 15) * 4;
+            const uint32_t row = GN_BK * sg + tr, col = col0 + c4;
+            if (row < k && vec_ok && col + 3 < n) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(B + (size_t)row * n + col));
+                raw[h][0] = v.x;
+                raw[h][1] = v.y;
+                raw[h][2] = v.z;
+                raw[h][3] = v.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    raw[h][e] = (row < k && col + e < n) ? __ldg(B + (size_t)row * n + col + e) : 0u;
+            }
+        }
+    };
+    uint32_t bad = 0;
+    auto store_tile = [&](int buf) {
+#pragma unroll
+        for (int h = 0; h < GN_APIECES; h++) {
+            const uint32_t idx = tid + 256 * h, per_row = GN_BK / 16, dg = idx / (64 * per_row);
+            const uint32_t row = (idx / per_row) % 64, c16 = idx % per_row;
+            *reinterpret_cast<uint4*>(as[buf] + (dg * 64 + row) * GN_APITCH + 16 * c16) = araw[h];
+        }
+#pragma unroll
+        for (int h = 0; h < GN_PIECES; h++) {
+            const uint32_t idx = tid + 256 * h, tr = idx >> 4, c4 = (idx & 15) * 4;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const uint32_t v = raw[h][e];
+                const int sv = m31_signed(v);
+                bad |= (uint32_t)(sv < -128 || sv > 127) | (v >> 31);
+                bs[buf][(c4 + e) * GN_PITCH + tr] = (uint8_t)sv;
+            }
+        }
+    };
+    uint64_t tot[4][4];
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) tot[t][e] = 0;
+    if (s_begin < s_end) {
+        load_tile(s_begin);
+        store_tile(0);
+    }
+    __syncthreads();
+    int buf = 0;
+    constexpr uint32_t CHUNK = GEMM_KCHUNK / GN_BK;  // stages per s32 accumulation chunk
+    for (uint32_t c0 = s_begin; c0 < s_end; c0 += CHUNK) {
+        const uint32_t c_end = min(s_end, c0 + CHUNK);
+        int acc[4][GEMM_GA][4];
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+#pragma unroll
+            for (int a = 0; a < GEMM_GA; a++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[t][a][e] = 0;
+        for (uint32_t sg = c0; sg < c_end; sg++) {
+            if (sg + 1 < s_end) load_tile(sg + 1);
+#pragma unroll
+            for (int ks = 0; ks < GN_BK / 32; ks++) {
+                const uint32_t ta = 32 * ks + 4 * tg, tb = ta + 16;
+                uint32_t af[GEMM_GA][4];
+#pragma unroll
+                for (int a = 0; a < GEMM_GA; a++) {
+                    const uint8_t* p0 = as[buf] + (a * 64 + rt * 16 + g) * GN_APITCH;
+                    const uint8_t* p1 = p0 + 8 * GN_APITCH;
+                    af[a][0] = *reinterpret_cast<const uint32_t*>(p0 + ta);
+                    af[a][1] = *reinterpret_cast<const uint32_t*>(p1 + ta);
+                    af[a][2] = *reinterpret_cast<const uint32_t*>(p0 + tb);
+                    af[a][3] = *reinterpret_cast<const uint32_t*>(p1 + tb);
+                }
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const uint8_t* col = bs[buf] + (ch * 32 + t * 8 + g) * GN_PITCH + 32 * ks;
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(col + 4 * tg);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(col + 16 + 4 * tg);
+                    mma_u8s8(acc[t][0], af[0], b0, b1);
+                    mma_s8(acc[t][1], af[1], b0, b1);
+                }
+            }
+            if (sg + 1 < s_end) {
+                store_tile(buf ^ 1);
+                __syncthreads();
+                buf ^= 1;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; t++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                uint64_t sum = 0;
+#pragma unroll
+                for (int a = 0; a < GEMM_GA; a++) {
+                    const int v = acc[t][a][e];
+                    const uint32_t u = v < 0 ? (uint32_t)(v + 0x7fffffff) : (uint32_t)v;  // v mod P, <= P
+                    sum = acc_fold(sum, mul_wide(u, pow256(a)));
+                }
+                tot[t][e] = acc_fold(tot[t][e], (uint64_t)canon64(sum));
+            }
+    }
+    if (bad) atomicOr(narrow_bad, 1u);
+    uint32_t* out = part + (size_t)blockIdx.z * m * n;
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t row = e < 2 ? r0 : r1, col = col0 + ch * 32 + t * 8 + 2 * tg + (e & 1);
+            if (row < m && col < n) out[(size_t)row * n + col] = canon64(tot[t][e]);
+        }
+}
+
+// C = sum of the K splits' partial products mod p.
+__global__ void gemm_combine_kernel(const uint32_t* __restrict__ part, uint32_t splits, size_t mn,
+                                    uint32_t* __restrict__ C) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < mn; i += (size_t)gridDim.x * blockDim.x) {
+        uint64_t s = 0;
+        for (uint32_t z = 0; z < splits; z++) s += part[z * mn + i];
+        C[i] = red64(s);
+    }
+}
+
 }  // namespace zk
 
 using namespace zk;
@@ -161,7 +357,47 @@ extern "C" int zkml_matmul_m31(zkml_ctx* ctx, const uint32_t* a, size_t m, size_
     }
     const uint32_t* Ad = static_cast<const uint32_t*>(A);
     static const bool tc_on = !(getenv("ZKML_GEMM_TC") && getenv("ZKML_GEMM_TC")[0] == '0');  // 0: CUDA cores
-    if (tc_on && k % 4 == 0 && (reinterpret_cast<uintptr_t>(Ad) & 15) == 0) {
+    static const bool narrow_on = !(getenv("ZKML_GEMM_NARROW") && getenv("ZKML_GEMM_NARROW")[0] == '0');
+    bool done = false;
+    if (tc_on && narrow_on) {
+        // narrow-value path; falls through to the full kernel if a value does not fit
+        const uint32_t kp = (uint32_t)((k + 31) / 32 * 32);
+        if ((rc = ctx->op.adig.ensure((size_t)GEMM_GA * m * kp + 16))) return rc;
+        uint32_t* flag = ctx->err_flag() + 2;  // spare word of the error-flag block
+        ZK_CUDA(cudaMemsetAsync(flag, 0, 4, s));
+        {
+            const size_t total = (size_t)m * kp;
+            const unsigned g = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);
+            gemm_a_digits_kernel<<<g, 256, 0, s>>>(Ad, (uint32_t)m, (uint32_t)k, kp, ctx->op.adig.as<int8_t>(), flag);
+        }
+        // K splits so that the grid is about four blocks per SM
+        const unsigned bx = (unsigned)((n + GN_COLS - 1) / GN_COLS), by = (unsigned)((m + 63) / 64);
+        const unsigned stages = (kp + GN_BK - 1) / GN_BK;
+        const size_t want = (size_t)4 * ctx->num_sms, have = (size_t)bx * by;
+        unsigned splits = (unsigned)std::max<size_t>(1, (want + have - 1) / have);
+        splits = std::min(splits, std::min(stages, 8u));
+        uint32_t* target = C;
+        if (splits > 1) {
+            if ((rc = ctx->op.gpart.ensure((size_t)splits * m * n * 4))) return rc;
+            target = ctx->op.gpart.as<uint32_t>();
+        }
+        m31_gemm_narrow_kernel<<<dim3(bx, by, splits), 256, 0, s>>>(ctx->op.adig.as<int8_t>(),
+                                                                    static_cast<const uint32_t*>(B), target,
+                                                                    (uint32_t)m, (uint32_t)k, kp, (uint32_t)n, flag);
+        if (splits > 1) {
+            const unsigned g = (unsigned)std::min<size_t>((m * n + 255) / 256, (size_t)ctx->num_sms * 8);
+            gemm_combine_kernel<<<g, 256, 0, s>>>(target, splits, m * n, C);
+            ctx->launches++;
+        }
+        ctx->launches += 2;
+        ZK_CUDA(cudaGetLastError());
+        uint32_t hflag = 0;
+        ZK_CUDA(cudaMemcpyAsync(&hflag, flag, 4, cudaMemcpyDeviceToHost, s));
+        ZK_CUDA(cudaStreamSynchronize(s));
+        done = hflag == 0;
+    }
+    if (done) {
+    } else if (tc_on && k % 4 == 0 && (reinterpret_cast<uintptr_t>(Ad) & 15) == 0) {
         dim3 gg((unsigned)((n + 8 * GEMM_NT - 1) / (8 * GEMM_NT)), (unsigned)((m + 63) / 64));
         m31_gemm_tc_kernel<GEMM_NT, GEMM_KS><<<gg, 4 * GEMM_NT * GEMM_KS * 32, 0, s>>>(Ad, static_cast<const uint32_t*>(B), C, (uint32_t)m,
                                                            (uint32_t)k, (uint32_t)n, ctx->err_flag());

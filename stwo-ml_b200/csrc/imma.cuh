@@ -18,6 +18,34 @@ __device__ __forceinline__ void mma_u8(int (&d)[4], const uint32_t (&a)[4], uint
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// D += A (16 x 32, s8, row) * B (32 x 8, s8, col), s32 accumulators.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// D += A (16 x 32, u8, row) * B (32 x 8, s8, col), s32 accumulators.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Signed value of an M31 element v < 2^31 read as v (v <= (P-1)/2) or v - P.
+__device__ __forceinline__ int m31_signed(uint32_t v) {
+    const uint32_t r = (v & 0x7fffffffu) + (v >> 31);
+    const uint32_t c = r >= 0x7fffffffu ? r - 0x7fffffffu : r;
+    return c <= 0x3fffffffu ? (int)c : (int)c - 0x7fffffff;
+}
+
+// Balanced signed byte digit: the low byte of s sign-extended; s - digit is a multiple of 256.
+__device__ __forceinline__ int sdigit(int s) { return (int)(int8_t)(s & 0xff); }
+
 // Byte planes of four consecutive u32 elements: plane b = [e0.b, e1.b, e2.b, e3.b].
 __device__ __forceinline__ void byte_planes(const uint4& e, uint32_t& p0, uint32_t& p1, uint32_t& p2,
                                             uint32_t& p3) {

@@ -58,3 +58,27 @@ def test_matmul_m31_device_output_and_bad_values():
     with pytest.raises(Z.InvalidArgument):
         Z.matmul_m31(a, bad)
     np.testing.assert_array_equal(Z.matmul_m31(a, b), oracle_matmul(a, b))  # context still usable
+
+
+def signed_m31(v):
+    v = np.asarray(v, np.int64)
+    return np.where(v >= 0, v, P + v).astype(np.uint32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,k,n,arange,brange", [
+    (64, 5120, 1536, 32767, 127),       # int16 activations x int8 weights: the signed-digit path
+    (7, 33, 19, 32000, 127),            # k not a multiple of 4 or 32
+    (64, 5120, 96, 32768, 128),         # ranges just past the digits: full-kernel fallback
+    (32, 1000, 64, 40000, 127),
+    (16, 300, 40, 100, 127),
+])
+def test_matmul_m31_narrow_values(m, k, n, arange, brange):
+    import zkml_b200 as Z
+    rng = np.random.default_rng(m + k + n)
+    a = signed_m31(rng.integers(-arange, arange + 1, (m, k)))
+    b = signed_m31(rng.integers(-brange, brange + 1, (k, n)))
+    # the digit boundaries themselves
+    a.flat[0], a.flat[1] = signed_m31(-32768), signed_m31(min(arange, 32767))
+    b.flat[0] = signed_m31(-128)
+    np.testing.assert_array_equal(Z.matmul_m31(a, b), oracle_matmul(a, b))

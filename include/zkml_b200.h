@@ -253,12 +253,13 @@ int zkml_reduce_activation_relu(zkml_ctx *ctx, const uint32_t *input, size_t row
 
 #define ZKML_LAYER_LINEAR 0
 #define ZKML_LAYER_RELU 1
+#define ZKML_LAYER_RMSNORM 2 /* RMSNorm over the full layer width, no affine scale */
 /* flags: the Activation record without the multiplicity-sumcheck and piecewise flags, the
  * layout of the reference's engine/tests/artifacts/sp3_mlp_proof.json */
 #define ZKML_CHAIN_LEGACY_ACTIVATION_RECORD 1
 
 typedef struct {
-    int type;               /* ZKML_LAYER_LINEAR or ZKML_LAYER_RELU */
+    int type;               /* ZKML_LAYER_LINEAR, ZKML_LAYER_RELU or ZKML_LAYER_RMSNORM */
     const uint32_t *weight; /* Linear: (input width) x n, row major, host or device memory */
     size_t n;               /* Linear: output width */
 } zkml_chain_layer;

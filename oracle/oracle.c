@@ -2833,6 +2833,20 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             acts[l + 1] = (uint32_t *)malloc(4 * m * w);
             for (size_t i = 0; i < m * w; i++) acts[l + 1][i] = acts[l][i] <= 1073741823u ? acts[l][i] : 0;
             width[l + 1] = w;
+        } else if (layers[l].type == 2) {
+            /* apply_rmsnorm_detailed (compiler/prove.rs:1115-1180), dim = the layer width */
+            uint32_t *tab = (uint32_t *)malloc(4u << 16);
+            orc_rsqrt_table(16, tab);
+            uint32_t inv_n = m_inv((uint32_t)(w % MP));
+            acts[l + 1] = (uint32_t *)malloc(4 * m * w);
+            for (size_t i = 0; i < m; i++) {
+                uint32_t sq = 0;
+                for (size_t j = 0; j < w; j++) sq = m_add(sq, m_mul(acts[l][i * w + j], acts[l][i * w + j]));
+                uint32_t rs = tab[m_mul(sq, inv_n) & 0xFFFF];
+                for (size_t j = 0; j < w; j++) acts[l + 1][i * w + j] = m_mul(acts[l][i * w + j], rs);
+            }
+            free(tab);
+            width[l + 1] = w;
         } else {
             return 1;
         }
@@ -2901,6 +2915,20 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             npt = log_m + log_k;
             value = q_load(fa);
             free(rp);
+        } else if (layers[li].type == 2) {
+            size_t tcap = (1 << 16) + 64 + next_pow2(m) + 40 * (npt + 2), tlen = 0;
+            uint64_t *tbuf = (uint64_t *)malloc(32 * tcap);
+            uint32_t cv[4], ie[4];
+            q_store(cv, value);
+            rc = orc_reduce_rmsnorm(acts[li], m, w, w, NULL, 0, 0, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap,
+                                    &tlen, ie);
+            for (size_t i = 0; i < tlen && !rc; i++) {
+                fe f;
+                fe_from_canon(&f, tbuf + 4 * i);
+                out_push(&o, &f);
+            }
+            free(tbuf);
+            value = q_load(ie);
         } else {
             q31 nxt[64], nval;
             rc = relu_reduce(acts[li], m, w, point, value, &ch, &o, nxt, &nval, flags & 1);

@@ -195,7 +195,7 @@ int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const 
                                     uint32_t out_input_eval[4]);
 
 /* One layer of a sequential GKR chain: type 0 = Linear (weight: rows = the layer's input
- * width, n columns, row major), type 1 = ReLU. */
+ * width, n columns, row major), type 1 = ReLU, type 2 = RMSNorm over the full width. */
 typedef struct {
     int type;
     const uint32_t *weight;

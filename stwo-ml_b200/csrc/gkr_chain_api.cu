@@ -1,4 +1,4 @@
-// C-ABI: the GKR proof of a sequential chain of Linear and ReLU layers
+// C-ABI: the GKR proof of a sequential chain of Linear, ReLU and RMSNorm layers
 // (prove_gkr_with_cache, gkr/prover.rs:1500-2251, for GraphBuilder::new((m, k0)) followed
 // by .linear(n) / .activation(ReLU) layers) in Sequential weight-binding mode, serialized
 // by serialize_gkr_model_proof (cairo_serde.rs:1307-1772).
@@ -6,7 +6,8 @@
 // Forward pass on the GPU (tensor-pipe M31 GEMM, ReLU), then the transcript: depth, input
 // shape, optional policy commitment, the output claim at a drawn point, the walk from the
 // output layer to the input (matmul layers through zkml_reduce_matmul_layer_gkr, ReLU
-// layers through the algebraic reduction), the input claim, one MLE opening per weight on
+// layers through the algebraic reduction, RMSNorm layers through the RMSNorm reduction),
+// the input claim, one MLE opening per weight on
 // the main channel in walk order, and the io commitment.
 #include <algorithm>
 #include <array>
@@ -23,6 +24,9 @@
 #include "relu.hpp"
 
 namespace zk {
+
+const std::vector<uint32_t>& rsqrt_table16();
+
 namespace {
 
 __global__ void relu_forward_kernel(const uint32_t* __restrict__ x, size_t n, uint32_t* __restrict__ y) {
@@ -38,6 +42,37 @@ __global__ void pad_rows_cols_kernel(const uint32_t* __restrict__ x, size_t rows
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < n; idx += (size_t)gridDim.x * blockDim.x) {
         const size_t i = idx / pc, j = idx % pc;
         y[idx] = (i < rows && j < cols) ? red32(x[i * cols + j]) : 0u;
+    }
+}
+
+// apply_rmsnorm_detailed (compiler/prove.rs:1115-1180) with dim = cols: one block per
+// row, rms^2 = sum x^2 / cols masked to 16 bits, out = x * rsqrt(rms^2).
+__global__ void __launch_bounds__(256) rmsnorm_forward_kernel(const uint32_t* __restrict__ x, uint32_t rows,
+                                                              uint32_t cols, uint32_t inv_n,
+                                                              const uint32_t* __restrict__ table,
+                                                              uint32_t* __restrict__ y) {
+    __shared__ unsigned long long part[8];
+    __shared__ uint32_t s_rs;
+    for (uint32_t i = blockIdx.x; i < rows; i += gridDim.x) {
+        const uint32_t* row = x + (size_t)i * cols;
+        unsigned long long sq = 0;
+        for (uint32_t j = threadIdx.x; j < cols; j += blockDim.x) {
+            const uint32_t v = red32(row[j]);
+            sq += red64((uint64_t)v * v);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = sq;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long t = 0;
+            for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += part[w];
+            s_rs = table[mmul(red64(t), inv_n) & 0xFFFFu];
+        }
+        __syncthreads();
+        const uint32_t rs = s_rs;
+        for (uint32_t j = threadIdx.x; j < cols; j += blockDim.x) y[(size_t)i * cols + j] = mmul(red32(row[j]), rs);
+        __syncthreads();
     }
 }
 
@@ -77,7 +112,7 @@ extern "C" int zkml_prove_gkr_chain(zkml_ctx* ctx, const uint32_t* input, size_t
             if (!layers[l].weight || layers[l].n == 0 || layers[l].n > (1u << 30))
                 return set_error(ZKML_ERR_INVALID_ARG, "layer " + std::to_string(l) + ": bad Linear layer");
             width[l + 1] = layers[l].n;
-        } else if (layers[l].type == ZKML_LAYER_RELU) {
+        } else if (layers[l].type == ZKML_LAYER_RELU || layers[l].type == ZKML_LAYER_RMSNORM) {
             width[l + 1] = width[l];
         } else {
             return set_error(ZKML_ERR_INVALID_ARG, "layer " + std::to_string(l) + ": unsupported layer type");
@@ -104,6 +139,15 @@ extern "C" int zkml_prove_gkr_chain(zkml_ctx* ctx, const uint32_t* input, size_t
             if ((rc = zkml_matmul_m31(ctx, acts[l].as<uint32_t>(), m, width[l], layers[l].weight, width[l + 1],
                                       acts[l + 1].as<uint32_t>())))
                 return rc;
+        } else if (layers[l].type == ZKML_LAYER_RMSNORM) {
+            if (!ctx->rsqrt_table.ptr) {
+                if ((rc = ctx->rsqrt_table.ensure(4u << 16))) return rc;
+                ZK_CUDA(cudaMemcpy(ctx->rsqrt_table.ptr, rsqrt_table16().data(), 4u << 16, cudaMemcpyHostToDevice));
+            }
+            rmsnorm_forward_kernel<<<(unsigned)std::min<size_t>(m, 8192), 256, 0, s>>>(
+                acts[l].as<uint32_t>(), (uint32_t)m, (uint32_t)width[l], minv((uint32_t)(width[l] % P)),
+                ctx->rsqrt_table.as<uint32_t>(), acts[l + 1].as<uint32_t>());
+            ctx->launches++;
         } else {
             relu_forward_kernel<<<blocks_for(m * width[l]), 256, 0, s>>>(acts[l].as<uint32_t>(), m * width[l],
                                                                          acts[l + 1].as<uint32_t>());
@@ -179,6 +223,12 @@ extern "C" int zkml_prove_gkr_chain(zkml_ctx* ctx, const uint32_t* input, size_t
             memcpy(point.data(), nxt.data(), 16 * (log_m + log_k));
             npt = log_m + log_k;
             value = qm(fa[0], fa[1], fa[2], fa[3]);
+        } else if (layers[li].type == ZKML_LAYER_RMSNORM) {
+            uint32_t cv[4] = {value.a, value.b, value.c, value.d}, ie[4];
+            if ((rc = rmsnorm_reduce_dev(ctx, acts[li].as<uint32_t>(), m, w, w, nullptr, 0,
+                                         reinterpret_cast<const uint32_t*>(point.data()), npt, cv, &chs, o, ie)))
+                return rc;
+            value = qm(ie[0], ie[1], ie[2], ie[3]);  // the point is unchanged
         } else {
             std::vector<qm31> nxt(64);
             qm31 nval;

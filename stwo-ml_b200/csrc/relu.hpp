@@ -1,4 +1,5 @@
-// The algebraic ReLU reduction on the device (relu_api.cu), shared with the GKR chain driver.
+// Layer reductions on the device shared with the GKR chain driver: the algebraic ReLU
+// (relu_api.cu) and the RMSNorm reduction (rmsnorm_api.cu).
 #pragma once
 #include "calldata.hpp"
 #include "context.hpp"
@@ -12,5 +13,12 @@ namespace zk {
 int relu_reduce_dev(::zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, const qm31* point,
                     const qm31& claim_value, zkml_channel* chs, Out& o, qm31* next_point, qm31* next_value,
                     bool legacy_record);
+
+// reduce_rmsnorm_layer_with_gamma (gkr/prover.rs:8424-8790) on the rows x cols input;
+// appends the LayerProof::RMSNorm record to `o` (rmsnorm_api.cu).  The next claim keeps the
+// point; its value is written to out_input_eval.
+int rmsnorm_reduce_dev(::zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
+                       const uint32_t* gamma, size_t gamma_len, const uint32_t* claim_point, size_t n_point,
+                       const uint32_t claim_value[4], zkml_channel* chs, Out& o, uint32_t out_input_eval[4]);
 
 }  // namespace zk

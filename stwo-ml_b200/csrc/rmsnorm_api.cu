@@ -22,6 +22,7 @@
 #include "channel.hpp"
 #include "context.hpp"
 #include "logup.cuh"
+#include "relu.hpp"
 
 namespace zk {
 
@@ -46,11 +47,10 @@ inline qm31 ldw(const uint32_t* p) { return qm(p[0], p[1], p[2], p[3]); }
 
 using namespace zk;
 
-extern "C" int zkml_reduce_rmsnorm(zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
-                                   const uint32_t* gamma, size_t gamma_len, const uint32_t* claim_point,
-                                   size_t n_point, const uint32_t claim_value[4], zkml_channel* chs,
-                                   uint64_t* out_calldata, size_t cap, size_t* out_len, uint32_t out_input_eval[4]) {
-    if (!ctx || !input || !claim_value || !chs || !out_len) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+int zk::rmsnorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
+                           const uint32_t* gamma, size_t gamma_len, const uint32_t* claim_point, size_t n_point,
+                           const uint32_t claim_value[4], zkml_channel* chs, Out& o, uint32_t out_input_eval[4]) {
+    if (!ctx || !input || !claim_value || !chs) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (rows == 0 || cols == 0 || dim == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty RMSNorm input or dim 0");
     if (gamma && gamma_len == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty gamma");
     const size_t pr = np2(rows), pc = np2(cols), n = pr * pc;
@@ -257,7 +257,6 @@ extern "C" int zkml_reduce_rmsnorm(zkml_ctx* ctx, const uint32_t* input, size_t 
     ch.mix_qm31(output_eval);
 
     // LayerProof::RMSNorm as serialize_gkr_model_proof writes it (cairo_serde.rs:1648-1726)
-    Out o{out_calldata, out_calldata ? cap : 0};
     o.u64(8);
     o.q(input_eval);
     o.q(output_eval);
@@ -299,13 +298,25 @@ extern "C" int zkml_reduce_rmsnorm(zkml_ctx* ctx, const uint32_t* input, size_t 
     } else {
         o.u64(0);
     }
-    *out_len = o.len;
     if (out_input_eval) {
         out_input_eval[0] = input_eval.a;
         out_input_eval[1] = input_eval.b;
         out_input_eval[2] = input_eval.c;
         out_input_eval[3] = input_eval.d;
     }
+    return ZKML_OK;
+}
+
+extern "C" int zkml_reduce_rmsnorm(zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
+                                   const uint32_t* gamma, size_t gamma_len, const uint32_t* claim_point,
+                                   size_t n_point, const uint32_t claim_value[4], zkml_channel* chs,
+                                   uint64_t* out_calldata, size_t cap, size_t* out_len, uint32_t out_input_eval[4]) {
+    if (!out_len) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
+    Out o{out_calldata, out_calldata ? cap : 0};
+    int rc = rmsnorm_reduce_dev(ctx, input, rows, cols, dim, gamma, gamma_len, claim_point, n_point, claim_value, chs,
+                                o, out_input_eval);
+    if (rc) return rc;
+    *out_len = o.len;
     if (o.overflow)
         return set_error(ZKML_ERR_INVALID_ARG, "calldata buffer too small: need " + std::to_string(o.len) + " felts");
     return ZKML_OK;

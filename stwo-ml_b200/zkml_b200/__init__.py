@@ -740,8 +740,8 @@ class GKRChainProof:
 def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_queries: Optional[int] = None,
                     legacy_activation_record: bool = False, device: int = 0) -> GKRChainProof:
     """prove_gkr (gkr/prover.rs:1500-2251) for GraphBuilder::new(inp.shape) followed by `layers`,
-    each ("linear", weight) with weight (in_width, n) or ("relu", None); Sequential weight
-    binding."""
+    each ("linear", weight) with weight (in_width, n), ("relu", None) or ("rmsnorm", None);
+    Sequential weight binding."""
     im = as_matrix(inp)
     ib = _Buf(im.data)
     keep = [ib]
@@ -760,11 +760,15 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
             n_lin += 1
         elif kind == "relu":
             arr[i].type, arr[i].weight, arr[i].n = 1, None, 0
+        elif kind == "rmsnorm":
+            arr[i].type, arr[i].weight, arr[i].n = 2, None, 0
         else:
             raise InvalidArgument(1, f"layer {i}: unknown kind {kind}")
     nq = mle_n_queries() if n_queries is None else n_queries
     nv_all = _log2(_next_pow2(im.rows)) + max(nv_max, _log2(_next_pow2(width)) + 1)
+    n_norm = sum(1 for kind, _ in layers if kind == "rmsnorm")
     cap = 256 + len(layers) * (200 + 12 * nv_all) + n_lin * (64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1))))
+    cap += n_norm * ((1 << 16) + _next_pow2(im.rows) + 40 * (nv_all + 2))
     out = np.zeros(4 * cap, np.uint64)
     ln = C.c_size_t(0)
     dig = np.zeros(4, np.uint64)

@@ -352,7 +352,7 @@ class ChainLayer(C.Structure):
     _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t)]
 
 
-def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, cap=1 << 18):
+def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, cap=1 << 20):
     """layers: list of ("linear", weight (rows, n)) or ("relu", None)."""
     inp = np.ascontiguousarray(inp, np.uint32)
     m, k0 = inp.shape
@@ -363,6 +363,8 @@ def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False,
             w = np.ascontiguousarray(w, np.uint32)
             keep.append(w)
             arr[i].type, arr[i].weight, arr[i].n = 0, w.ctypes.data, w.shape[1]
+        elif kind == "rmsnorm":
+            arr[i].type, arr[i].weight, arr[i].n = 2, None, 0
         else:
             arr[i].type, arr[i].weight, arr[i].n = 1, None, 0
     buf = np.zeros(4 * cap, np.uint64)

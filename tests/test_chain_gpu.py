@@ -62,3 +62,24 @@ def test_gpu_chain_matches_oracle(m, dims):
     proof = Z.prove_gkr_chain(x, layers, n_queries=6)
     assert proof.raw.size == raw.size and (proof.raw == raw).all()
     assert proof.final_digest == dig and proof.io_commitment == io
+
+
+def norm_chain_case(m, d, d_ff, seed):
+    """One SmolLM-style block of the reference recipe (hf_loader.rs:770-813) with the gated FFN
+    replaced by Linear -> ReLU -> Linear: RMSNorm, q, o, RMSNorm, up, ReLU, down, final RMSNorm."""
+    x = int_matrix_m31(m, d, seed, bound=100)
+    w = [int_matrix_m31(a, b, seed * 10 + i, bound=20) for i, (a, b) in enumerate([(d, d), (d, d), (d, d_ff),
+                                                                                     (d_ff, d)])]
+    layers = [("rmsnorm", None), ("linear", w[0]), ("linear", w[1]), ("rmsnorm", None), ("linear", w[2]),
+              ("relu", None), ("linear", w[3]), ("rmsnorm", None)]
+    return x, layers
+
+
+@pytest.mark.parametrize("m,d,d_ff", [(2, 8, 16), (3, 12, 20), (1, 576, 1536)], ids=lambda x: str(x))
+def test_gpu_chain_with_rmsnorm_matches_oracle(m, d, d_ff):
+    x, layers = norm_chain_case(m, d, d_ff, m + d)
+    rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=4)
+    assert rc == 0
+    proof = Z.prove_gkr_chain(x, layers, n_queries=4)
+    assert proof.raw.size == raw.size and (proof.raw == raw).all()
+    assert proof.final_digest == dig and proof.io_commitment == io

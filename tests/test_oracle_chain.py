@@ -51,3 +51,14 @@ def test_chain_reproduces_sp3_matmul_only_artifact():
     assert rc == 0
     assert felts(raw) == [int(h, 16) for h in g["calldata_hex"]]
     assert dig == int(g["final_channel_digest"], 16) and io == int(g["io_commitment"], 16)
+
+
+def test_chain_with_rmsnorm_runs_and_is_deterministic():
+    rng_w = [np.arange(64, dtype=np.uint32).reshape(8, 8) % 13, np.arange(32, dtype=np.uint32).reshape(8, 4) % 7]
+    x = (np.arange(16, dtype=np.uint32).reshape(2, 8) * 37) % 200
+    layers = [("rmsnorm", None), ("linear", rng_w[0]), ("relu", None), ("linear", rng_w[1]), ("rmsnorm", None)]
+    rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=3)
+    rc2, raw2, dig2, io2 = O.prove_gkr_chain(x, layers, n_queries=3)
+    assert rc == rc2 == 0 and (raw == raw2).all() and dig == dig2
+    f = [O.felt_int(raw[4 * i:4 * i + 4]) for i in range(raw.size // 4)]
+    assert f[0] == len(layers) and f[1] == 8  # first record is the output RMSNorm (tag 8)

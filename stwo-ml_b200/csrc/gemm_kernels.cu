@@ -172,11 +172,11 @@ __global__ void gemm_a_digits_kernel(const uint32_t* __restrict__ A, uint32_t m,
 constexpr int GN_COLS = 64;
 constexpr int GN_BK = 64;
 constexpr int GN_PITCH = GN_BK + 4;
-constexpr int GN_PIECES = GN_BK * GN_COLS / 4 / 256;  // 4-column pieces per thread and stage
+static_assert(GN_BK * GN_COLS == 256 * 16, "one 4 x 4 block of the B tile per thread and stage");
 constexpr int GN_APITCH = GN_BK + 16;                  // A tile row pitch (bytes)
 constexpr int GN_APIECES = GEMM_GA * 64 * GN_BK / 16 / 256;  // 16-byte A pieces per thread and stage
 
-__global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __restrict__ D,
+__global__ void __launch_bounds__(256, 3) m31_gemm_narrow_kernel(const int8_t* __restrict__ D,
                                                               const uint32_t* __restrict__ B,
                                                               uint32_t* __restrict__ part, uint32_t m, uint32_t k,
                                                               uint32_t kp, uint32_t n,
@@ -192,7 +192,9 @@ __global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __re
     // this block's stages (of GN_BK rows) of the K range
     const uint32_t stages = (kp + GN_BK - 1) / GN_BK, per = (stages + gridDim.z - 1) / gridDim.z;
     const uint32_t s_begin = min(stages, blockIdx.z * per), s_end = min(stages, s_begin + per);
-    uint32_t raw[GN_PIECES][4];
+    // this thread's 4 x 4 block of the B tile: rows 4 br .. 4 br + 3, columns 4 bc .. 4 bc + 3
+    const uint32_t br = tid >> 4, bc = tid & 15;
+    uint32_t raw[4][4];  // [row][column]
     uint4 araw[GN_APIECES];
     auto load_tile = [&](uint32_t sg) {
 #pragma unroll
@@ -205,19 +207,18 @@ __global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __re
                           : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
-        for (int h = 0; h < GN_PIECES; h++) {
-            const uint32_t idx = tid + 256 * h, tr = idx >> 4, c4 = (idx & 15) * 4;
-            const uint32_t row = GN_BK * sg + tr, col = col0 + c4;
+        for (int rr = 0; rr < 4; rr++) {
+            const uint32_t row = GN_BK * sg + 4 * br + rr, col = col0 + 4 * bc;
             if (row < k && vec_ok && col + 3 < n) {
                 const uint4 v = __ldg(reinterpret_cast<const uint4*>(B + (size_t)row * n + col));
-                raw[h][0] = v.x;
-                raw[h][1] = v.y;
-                raw[h][2] = v.z;
-                raw[h][3] = v.w;
+                raw[rr][0] = v.x;
+                raw[rr][1] = v.y;
+                raw[rr][2] = v.z;
+                raw[rr][3] = v.w;
             } else {
 #pragma unroll
                 for (int e = 0; e < 4; e++)
-                    raw[h][e] = (row < k && col + e < n) ? __ldg(B + (size_t)row * n + col + e) : 0u;
+                    raw[rr][e] = (row < k && col + e < n) ? __ldg(B + (size_t)row * n + col + e) : 0u;
             }
         }
     };
@@ -229,19 +230,24 @@ __global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __re
             const uint32_t row = (idx / per_row) % 64, c16 = idx % per_row;
             *reinterpret_cast<uint4*>(as[buf] + (dg * 64 + row) * GN_APITCH + 16 * c16) = araw[h];
         }
+        // signed bytes, transposed: column 4 bc + e gets the 4 bytes of rows 4 br .. 4 br + 3
+        uint32_t sb[4][4];
 #pragma unroll
-        for (int h = 0; h < GN_PIECES; h++) {
-            const uint32_t idx = tid + 256 * h, tr = idx >> 4, c4 = (idx & 15) * 4;
+        for (int rr = 0; rr < 4; rr++)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const uint32_t v = raw[h][e];
+                const uint32_t v = raw[rr][e];
                 const int sv = m31_signed(v);
                 bad |= (uint32_t)(sv < -128 || sv > 127) | (v >> 31);
-                bs[buf][(c4 + e) * GN_PITCH + tr] = (uint8_t)sv;
+                sb[rr][e] = (uint32_t)sv & 0xffu;
             }
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t w = sb[0][e] | (sb[1][e] << 8) | (sb[2][e] << 16) | (sb[3][e] << 24);
+            *reinterpret_cast<uint32_t*>(bs[buf] + (4 * bc + e) * GN_PITCH + 4 * br) = w;
         }
     };
-    uint64_t tot[4][4];
+    uint32_t tot[4][4];  // canonical partial sums
 #pragma unroll
     for (int t = 0; t < 4; t++)
 #pragma unroll
@@ -303,7 +309,7 @@ __global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __re
                     const uint32_t u = v < 0 ? (uint32_t)(v + 0x7fffffff) : (uint32_t)v;  // v mod P, <= P
                     sum = acc_fold(sum, mul_wide(u, pow256(a)));
                 }
-                tot[t][e] = acc_fold(tot[t][e], (uint64_t)canon64(sum));
+                tot[t][e] = canon64((uint64_t)tot[t][e] + canon64(sum));
             }
     }
     if (bad) atomicOr(narrow_bad, 1u);
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(256) m31_gemm_narrow_kernel(const int8_t* __re
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const uint32_t row = e < 2 ? r0 : r1, col = col0 + ch * 32 + t * 8 + 2 * tg + (e & 1);
-            if (row < m && col < n) out[(size_t)row * n + col] = canon64(tot[t][e]);
+            if (row < m && col < n) out[(size_t)row * n + col] = tot[t][e];
         }
 }
 

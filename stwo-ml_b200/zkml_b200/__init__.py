@@ -566,7 +566,7 @@ def prove_mle_opening(evals, point, channel: PoseidonChannel, n_queries: Optiona
     p_ptr, p_keep = _qm31_ptr(point)
     nq = mle_n_queries() if n_queries is None else n_queries
     cap = 64 + (nq + 1) * (2 + n_vars * (10 + 2 * (n_vars + 1)))
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     com = np.zeros(4, np.uint64)
     ln = C.c_size_t(0)
     _check(lib().zkml_prove_mle_opening(context(device).handle, buf.ptr, n_vars, p_ptr, C.byref(channel.state), nq,
@@ -663,13 +663,13 @@ def reduce_activation_layer(output_claim: GKRClaim, inp: M31Matrix, activation_t
     n_point = len(as_qm31_array(output_claim.point))
     tsize = 1 << ActivationType.table_log_size(activation_type)
     cap = tsize + 64 + 16 * (n_point + 40)
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     ie = np.zeros(4, np.uint32)
     _check(lib().zkml_reduce_activation_logup(context(device).handle, buf.ptr, inp.rows, inp.cols, activation_type,
                                               pt_ptr, n_point, np.ascontiguousarray(output_claim.value, np.uint32),
                                               C.byref(channel.state), out, cap, C.byref(ln), ie))
-    proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
+    proof = ActivationLogUpProof(out[:4 * ln.value], ie)
     return proof, GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
 
 
@@ -691,7 +691,7 @@ def reduce_activation_layer_piecewise(output_claim: GKRClaim, inp: M31Matrix, ac
     pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
     n_point = len(as_qm31_array(output_claim.point))
     cap = 64 + 12 * n_point + 4 * 24
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     ie = np.zeros(4, np.uint32)
     nxt = np.zeros((max(n_point, 1), 4), np.uint32)
@@ -700,7 +700,7 @@ def reduce_activation_layer_piecewise(output_claim: GKRClaim, inp: M31Matrix, ac
                                                   np.ascontiguousarray(output_claim.value, np.uint32),
                                                   C.byref(channel.state), out, cap, C.byref(ln), ie,
                                                   nxt.reshape(-1)))
-    proof = ActivationLogUpProof(out[:4 * ln.value].copy(), ie)
+    proof = ActivationLogUpProof(out[:4 * ln.value], ie)
     return proof, GKRClaim(nxt[:n_point].copy(), ie.copy())
 
 
@@ -712,14 +712,14 @@ def reduce_activation_layer_relu(output_claim: GKRClaim, inp: M31Matrix, channel
     pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
     n_point = len(as_qm31_array(output_claim.point))
     cap = 256 + 12 * n_point
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     ie = np.zeros(4, np.uint32)
     nxt = np.zeros((max(n_point, 1), 4), np.uint32)
     _check(lib().zkml_reduce_activation_relu(context(device).handle, buf.ptr, inp.rows, inp.cols, pt_ptr, n_point,
                                              np.ascontiguousarray(output_claim.value, np.uint32),
                                              C.byref(channel.state), out, cap, C.byref(ln), ie, nxt.reshape(-1)))
-    return ActivationLogUpProof(out[:4 * ln.value].copy(), ie), GKRClaim(nxt[:n_point].copy(), ie.copy())
+    return ActivationLogUpProof(out[:4 * ln.value], ie), GKRClaim(nxt[:n_point].copy(), ie.copy())
 
 
 class _ChainLayer(C.Structure):
@@ -769,7 +769,7 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
     n_norm = sum(1 for kind, _ in layers if kind == "rmsnorm")
     cap = 256 + len(layers) * (200 + 12 * nv_all) + n_lin * (64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1))))
     cap += n_norm * ((1 << 16) + _next_pow2(im.rows) + 40 * (nv_all + 2))
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     dig = np.zeros(4, np.uint64)
     io = np.zeros(4, np.uint64)
@@ -777,7 +777,7 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
     _check(lib().zkml_prove_gkr_chain(context(device).handle, ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
                                       len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq,
                                       1 if legacy_activation_record else 0, out, cap, C.byref(ln), dig, io))
-    return GKRChainProof(out[:4 * ln.value].copy(), limbs_to_felt(dig), limbs_to_felt(io))
+    return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
 
 
 @dataclass
@@ -806,14 +806,14 @@ def reduce_rmsnorm_layer(output_claim: GKRClaim, inp: M31Matrix, dim: int, chann
     n_point = len(as_qm31_array(output_claim.point))
     pr = 1 << max(0, (inp.rows - 1).bit_length())
     cap = (1 << 16) + pr + 64 + 40 * (n_point + 2)
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     ie = np.zeros(4, np.uint32)
     _check(lib().zkml_reduce_rmsnorm(context(device).handle, buf.ptr, inp.rows, inp.cols, dim,
                                      None if gbuf is None else gbuf.ptr, 0 if gbuf is None else gbuf.nbytes // 4,
                                      pt_ptr, n_point, np.ascontiguousarray(output_claim.value, np.uint32),
                                      C.byref(channel.state), out, cap, C.byref(ln), ie))
-    raw = out[:4 * ln.value].copy()
+    raw = out[:4 * ln.value]
     oe = np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)
     return RMSNormProof(raw, ie, oe), GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
 
@@ -882,11 +882,11 @@ def prove_aggregated_binding(claims: List[AggregatedWeightClaim], channel: Posei
     nq = mle_n_queries() if n_queries is None else n_queries
     ng = n_max + _log2(_next_pow2(len(claims)))
     cap = 64 + 12 * ng + _next_pow2(len(claims)) + (nq + 1) * (2 + ng * (10 + 2 * (ng + 1)))
-    out = np.zeros(4 * cap, np.uint64)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     _check(lib().zkml_prove_aggregated_binding(context(device).handle, C.cast(arr, C.c_void_p), len(claims),
                                                C.byref(channel.state), nq, out, cap, C.byref(ln)))
-    return AggregatedBindingProof(out[:4 * ln.value].copy())
+    return AggregatedBindingProof(out[:4 * ln.value])
 
 
 # ---------------------------------------------------------------------------

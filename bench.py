@@ -325,7 +325,8 @@ def run_colsharded(args):
     import torch.distributed as dist
 
     import zkml_b200 as Z
-    from zkml_b200.distributed import column_block, reduce_matmul_layer_colsharded
+    from zkml_b200.distributed import (P2PInbox, column_block, reduce_matmul_layer_colsharded,
+                                       reduce_matmul_layer_colsharded_p2p)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -342,8 +343,12 @@ def run_colsharded(args):
     blk = torch.from_numpy(np.ascontiguousarray(b[:, lo:hi]).view(np.int32)).cuda() if hi > lo else None
     ch0, point = seeded_channel_state(Z, 0)
     claim = np.zeros(4, np.uint32)
+    inbox = P2PInbox(K, ctx=ctx) if (args.p2p and world > 1) else None
 
     def step():
+        if inbox is not None:
+            return reduce_matmul_layer_colsharded_p2p(Z.GKRClaim(point, claim), A, blk, lo, M, K, N, ch0.clone(),
+                                                      inbox)
         return reduce_matmul_layer_colsharded(Z.GKRClaim(point, claim), A, blk, lo, M, K, N, ch0.clone(), ctx=ctx)
 
     for _ in range(args.warmup):
@@ -372,9 +377,15 @@ def run_colsharded(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "u32 (M31/QM31 integer)",
             "data": "synthetic (SplitMix64-seeded int8 embedded in M31)",
-            "config": {"workload": "C2 layer, B column blocks of next_pow2(n)/G columns, NCCL all-reduce of 4k words",
+            "config": {"workload": "C2 layer, B column blocks of next_pow2(n)/G columns, " +
+                       ("peer-memory exchange of the 4k partial words" if inbox is not None else
+                        "NCCL all-reduce of the 4k partial words"),
                        "m": M, "k": K, "n": N, "ms_per_step_by_rank": [round(x, 4) for x in rank_ms]},
             "clocks": clk.summary()}), flush=True)
+    if inbox is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        inbox.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -625,6 +636,8 @@ def main():
                          "layer with B split by column blocks across the GPUs (strong scaling); product: the "
                          "config-5 product sumcheck split across GPUs")
     ap.add_argument("--log-n", type=int, default=28, help="product workload: log2 of the MLE length")
+    ap.add_argument("--p2p", action="store_true",
+                    help="c2-colsharded: exchange the partial words over peer memory instead of NCCL")
     args = ap.parse_args()
     if args.case:
         run_case(args.case)

@@ -189,6 +189,25 @@ int zkml_reduce_matmul_layer_gkr_fb(zkml_ctx *ctx, const uint32_t *claim_point, 
                                     const uint64_t *fb_words, size_t n, zkml_channel *ch, uint32_t *out_round_polys,
                                     uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t *out_next_point);
 
+/* The same split layer with the partial-word exchange over peer memory (NVLink) instead
+ * of a collective library.  Each rank (one process per GPU, distinct GPUs of one node)
+ * creates an inbox for a given k and exports its CUDA IPC handle (64 bytes); after the
+ * ranks have exchanged the handles, each opens the others'.  Per layer call, with an
+ * epoch that increases by one per call: zkml_restrict_cols_block_p2p restricts the block
+ * and stores the canonical partial words straight into every rank's inbox, then publishes
+ * the epoch there; zkml_reduce_matmul_layer_gkr_p2p waits (bounded: ZKML_ERR_TIMEOUT after
+ * about two seconds) for every rank's words, adds them and runs the layer.  Two ranks
+ * must not share a GPU (their kernels would wait on each other). */
+int zkml_p2p_inbox_create(zkml_ctx *ctx, size_t k, int world, int rank, uint8_t out_handle[64]);
+int zkml_p2p_open(zkml_ctx *ctx, const uint8_t *handles /* world x 64 bytes */, int world);
+int zkml_p2p_close(zkml_ctx *ctx);
+int zkml_restrict_cols_block_p2p(zkml_ctx *ctx, const uint32_t *b_block, size_t k, size_t n_block, size_t col_offset,
+                                 const uint32_t *r_j, size_t n_rj, uint32_t epoch);
+int zkml_reduce_matmul_layer_gkr_p2p(zkml_ctx *ctx, const uint32_t *claim_point, size_t n_point,
+                                     const uint32_t claim_value[4], const uint32_t *a, size_t m, size_t k, size_t n,
+                                     uint32_t epoch, zkml_channel *ch, uint32_t *out_round_polys,
+                                     uint32_t out_final_a[4], uint32_t out_final_b[4], uint32_t *out_next_point);
+
 /* ---- LogUp activation layer ------------------------------------------------- */
 
 /* reduce_activation_layer, LogUp path (gkr/prover.rs:6390-6600; reference GPU

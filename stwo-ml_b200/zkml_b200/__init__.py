@@ -121,6 +121,14 @@ _SIGS = {
     "zkml_prove_gkr_chain": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                        C.c_void_p, C.c_size_t, C.c_int, _u64, C.c_size_t, C.POINTER(C.c_size_t),
                                        _u64, _u64]),
+    "zkml_p2p_inbox_create": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]),
+    "zkml_p2p_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "zkml_p2p_close": (C.c_int, [C.c_void_p]),
+    "zkml_restrict_cols_block_p2p": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
+                                               C.c_void_p, C.c_size_t, C.c_uint32]),
+    "zkml_reduce_matmul_layer_gkr_p2p": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u32, C.c_void_p,
+                                                   C.c_size_t, C.c_size_t, C.c_size_t, C.c_uint32,
+                                                   C.POINTER(_Channel), _u32, _u32, _u32, _u32]),
     "zkml_weight_commitment": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, _u64]),
     "zkml_prove_aggregated_binding": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(_Channel),
                                                 C.c_size_t, _u64, C.c_size_t, C.POINTER(C.c_size_t)]),

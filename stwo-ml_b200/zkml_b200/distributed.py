@@ -400,3 +400,67 @@ def reduce_matmul_layer_colsharded(output_claim: GKRClaim, a: M31Matrix, b_block
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(words, group=group)
     return reduce_matmul_layer_from_words(output_claim, a, words, m, k, n, channel, ctx)
+
+
+class P2PInbox:
+    """The peer-memory exchange of the split layer (zkml_p2p_*): this rank's inbox for the
+    layer's k, mapped by every rank of `group` (CUDA IPC handles exchanged through the
+    process group).  The ranks must be on distinct GPUs of one node."""
+
+    def __init__(self, k: int, group=None, ctx: Optional[Context] = None):
+        import torch
+        import torch.distributed as dist
+        self.ctx = ctx or context(torch.cuda.current_device())
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.k = k
+        self.epoch = 0
+        h = (C.c_uint8 * 64)()
+        _check(lib().zkml_p2p_inbox_create(self.ctx.handle, k, self.world, self.rank, h))
+        devs = [None] * self.world
+        dist.all_gather_object(devs, str(torch.cuda.get_device_properties(self.ctx.device).uuid), group=group)
+        if len(set(str(d) for d in devs)) != self.world:
+            lib().zkml_p2p_close(self.ctx.handle)
+            raise ValueError("P2PInbox ranks must be on distinct GPUs")
+        hs = [None] * self.world
+        dist.all_gather_object(hs, bytes(h), group=group)
+        allh = (C.c_uint8 * (64 * self.world)).from_buffer_copy(b"".join(hs))
+        _check(lib().zkml_p2p_open(self.ctx.handle, allh, self.world))
+        dist.barrier(group=group)
+
+    def close(self) -> None:
+        lib().zkml_p2p_close(self.ctx.handle)
+
+
+def reduce_matmul_layer_colsharded_p2p(output_claim: GKRClaim, a: M31Matrix, b_block, col_offset: int, m: int, k: int,
+                                       n: int, channel: PoseidonChannel, inbox: P2PInbox):
+    """reduce_matmul_layer_colsharded with the exchange over peer memory: the block
+    restriction's partial words go straight into every rank's inbox (no collective library,
+    no host step between the two kernels)."""
+    pm, pn = _next_pow2(m), _next_pow2(n)
+    log_m, log_k = _log2(pm), _log2(_next_pow2(k))
+    point = as_qm31_array(output_claim.point)
+    if len(point) != log_m + _log2(pn):
+        raise ValueError("output claim must have log2(pm) + log2(pn) variables")
+    ctx = inbox.ctx
+    inbox.epoch += 1
+    bm = b_block if isinstance(b_block, M31Matrix) else None
+    n_block = bm.cols if bm is not None else (int(b_block.shape[1]) if b_block is not None else 0)
+    bb = _Buf(bm.data if bm is not None else b_block) if n_block else None
+    rj = np.ascontiguousarray(point[log_m:], np.uint32)
+    _check(lib().zkml_restrict_cols_block_p2p(ctx.handle, bb.ptr if bb else None, k, n_block, col_offset,
+                                              rj.ctypes.data_as(C.c_void_p) if rj.size else None, len(rj),
+                                              inbox.epoch))
+    ab = _Buf(a.data)
+    pt_ptr, pt_keep = _qm31_ptr(point)
+    rp = np.zeros((max(log_k, 1), 12), np.uint32)
+    fa = np.zeros(4, np.uint32)
+    fb = np.zeros(4, np.uint32)
+    nxt = np.zeros((max(log_m + log_k, 1), 4), np.uint32)
+    _check(lib().zkml_reduce_matmul_layer_gkr_p2p(ctx.handle, pt_ptr, len(point),
+                                                  np.ascontiguousarray(output_claim.value, np.uint32).reshape(4),
+                                                  ab.ptr, m, k, n, inbox.epoch, C.byref(channel.state),
+                                                  rp.reshape(-1), fa, fb, nxt.reshape(-1)))
+    polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_k)]
+    red = MatMulReduction(polys, nxt[log_m:log_m + log_k].copy(), fa, fb)
+    return red, GKRClaim(nxt[:log_m + log_k].copy(), fa.copy())

@@ -268,30 +268,58 @@ int zkml_reduce_activation_relu(zkml_ctx *ctx, const uint32_t *input, size_t row
                                 zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                 uint32_t out_input_eval[4], uint32_t *out_point);
 
-/* ---- GKR proof of a Linear / ReLU chain ------------------------------------------ */
+/* ---- GKR proof of a layered circuit (Linear / ReLU / RMSNorm / Add / Mul) ------- */
 
 #define ZKML_LAYER_LINEAR 0
 #define ZKML_LAYER_RELU 1
 #define ZKML_LAYER_RMSNORM 2 /* RMSNorm over the full layer width, no affine scale */
+#define ZKML_LAYER_ADD 3     /* element-wise lhs + rhs (GraphBuilder::add_from) */
+#define ZKML_LAYER_MUL 4     /* element-wise lhs * rhs (GraphBuilder::mul_from) */
+/* zkml_chain_layer.src: the previous layer's output (the model input for layer 0) */
+#define ZKML_CHAIN_PREV (-2)
 /* flags: the Activation record without the multiplicity-sumcheck and piecewise flags, the
  * layout of the reference's engine/tests/artifacts/sp3_mlp_proof.json */
 #define ZKML_CHAIN_LEGACY_ACTIVATION_RECORD 1
+/* flags: emit the verify_model_gkr calldata (starknet.rs:3143-3345, layout V1) from
+ * proof_data on, instead of serialize_gkr_model_proof */
+#define ZKML_CHAIN_V1_CALLDATA 2
 
+/* One layer of the circuit (LayeredCircuit::from_graph, gkr/circuit.rs:140-225); layer i's
+ * index is its circuit layer index. */
 typedef struct {
-    int type;               /* ZKML_LAYER_LINEAR, ZKML_LAYER_RELU or ZKML_LAYER_RMSNORM */
+    int type;               /* ZKML_LAYER_* */
     const uint32_t *weight; /* Linear: (input width) x n, row major, host or device memory */
     size_t n;               /* Linear: output width */
+    long long src;          /* the layer whose output feeds this one (Add / Mul: the rhs operand);
+                               ZKML_CHAIN_PREV, -1 = the model input, or a lower layer index */
+    long long lhs;          /* Add / Mul: the layer whose output is the lhs operand (the fork) */
 } zkml_chain_layer;
 
-/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for GraphBuilder::new((m, k0)) followed by
- * the given layers, from a fresh PoseidonChannel, Sequential weight binding (one MLE opening
- * per weight, n_queries queries, on the main channel), serialized by
- * serialize_gkr_model_proof (cairo_serde.rs:1307-1772).  The forward pass runs on the GPU.
- * policy may be NULL (no policy mix).  Writes the final channel digest and the io commitment. */
+/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for such a circuit on an m x k0 input, from
+ * a fresh PoseidonChannel: the walk from the output layer (Add layers defer their skip branch,
+ * prover.rs:1424-1463; Mul layers run the degree-3 eq-sumcheck of reduce_mul_layer,
+ * prover.rs:6172-6280, and defer and skip theirs, prover.rs:1719-1760), the deferred MatMul
+ * proofs (prover.rs:1918-2047), Sequential weight binding (one MLE opening per weight,
+ * n_queries queries, deferred openings first, all on the main channel).  The forward pass runs
+ * on the GPU.  Output: serialize_gkr_model_proof (cairo_serde.rs:1307-1772; it carries no
+ * deferred proofs), or with ZKML_CHAIN_V1_CALLDATA the verify_model_gkr calldata from
+ * proof_data on.  policy may be NULL (no policy mix).  Writes the final channel digest and the
+ * io commitment.  A deferred branch that is not a Linear layer fails with
+ * ZKML_ERR_INVALID_ARG, as the reference's prover does. */
 int zkml_prove_gkr_chain(zkml_ctx *ctx, const uint32_t *input, size_t m, size_t k0, const zkml_chain_layer *layers,
                          size_t n_layers, const uint64_t *policy, size_t n_queries, int flags,
                          uint64_t *out_calldata, size_t cap, size_t *out_len, uint64_t out_digest[4],
                          uint64_t out_io[4]);
+
+/* build_verify_model_gkr_calldata (starknet.rs:2837-2852, 3143-3345; layout V1, Sequential
+ * weight binding) for the same circuit: model_id, raw_io_data (serialize_raw_io of the input
+ * and the GPU forward pass's output), circuit depth, proof layer count, matmul dims in walk
+ * order, dequantize bits (none), proof_data, weight commitments and opening proofs. */
+int zkml_build_verify_model_gkr_calldata(zkml_ctx *ctx, const uint64_t model_id[4], const uint32_t *input, size_t m,
+                                         size_t k0, const zkml_chain_layer *layers, size_t n_layers,
+                                         const uint64_t *policy, size_t n_queries, int flags,
+                                         uint64_t *out_calldata, size_t cap, size_t *out_len,
+                                         uint64_t out_digest[4], uint64_t out_io[4]);
 
 /* ---- Aggregated weight binding ------------------------------------------------ */
 

@@ -2811,45 +2811,80 @@ static int relu_reduce(const uint32_t *input, size_t rows, size_t cols, const q3
 /* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for a chain GraphBuilder::new((m, k0))
  * .linear(..)/.activation(ReLU).. in Sequential weight-binding mode, serialized by
  * serialize_gkr_model_proof (cairo_serde.rs:1307-1772). */
+typedef struct {
+    q31 point[64];
+    unsigned npt;
+    q31 value;
+    size_t layer;
+} chain_deferred;
+
 int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
                         const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
                         size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads) {
     oracle_init();
     if (n_layers == 0 || n_layers > 64) return 1;
-    /* forward pass: acts[l] is layer l's input (m x width[l]) */
-    uint32_t *acts[65];
+    /* forward pass: outs[0] is the model input, outs[l + 1] layer l's output (m x width[.]) */
+    uint32_t *outs[65];
     size_t width[65];
-    acts[0] = (uint32_t *)malloc(4 * m * k0);
-    for (size_t i = 0; i < m * k0; i++) acts[0][i] = m_red64(input[i]);
+    long long src[64];
+    outs[0] = (uint32_t *)malloc(4 * m * k0);
+    for (size_t i = 0; i < m * k0; i++) outs[0][i] = m_red64(input[i]);
     width[0] = k0;
-    for (size_t l = 0; l < n_layers; l++) {
-        size_t w = width[l];
+    size_t built = 0;
+    int rc = 0;
+    for (size_t l = 0; l < n_layers && !rc; l++) {
+        src[l] = layers[l].src == ORC_CHAIN_PREV ? (long long)l - 1 : layers[l].src;
+        if (src[l] < -1 || src[l] >= (long long)l) {
+            rc = 1;
+            break;
+        }
+        const uint32_t *x = outs[src[l] + 1];
+        size_t w = width[src[l] + 1];
+        size_t wo = w;
         if (layers[l].type == 0) {
-            if (!layers[l].weight || layers[l].n == 0) return 1;
-            acts[l + 1] = (uint32_t *)malloc(4 * m * layers[l].n);
-            orc_matmul_m31(acts[l], m, w, layers[l].weight, layers[l].n, acts[l + 1], threads);
-            width[l + 1] = layers[l].n;
+            if (!layers[l].weight || layers[l].n == 0) {
+                rc = 1;
+                break;
+            }
+            wo = layers[l].n;
+        } else if (layers[l].type == 3 || layers[l].type == 4) {
+            if (layers[l].lhs < 0 || layers[l].lhs >= (long long)l || width[layers[l].lhs + 1] != w) {
+                rc = 1;
+                break;
+            }
+        } else if (layers[l].type != 1 && layers[l].type != 2) {
+            rc = 1;
+            break;
+        }
+        uint32_t *y = (uint32_t *)malloc(4 * m * wo);
+        outs[l + 1] = y;
+        width[l + 1] = wo;
+        built = l + 1;
+        if (layers[l].type == 0) {
+            orc_matmul_m31(x, m, w, layers[l].weight, wo, y, threads);
         } else if (layers[l].type == 1) {
-            acts[l + 1] = (uint32_t *)malloc(4 * m * w);
-            for (size_t i = 0; i < m * w; i++) acts[l + 1][i] = acts[l][i] <= 1073741823u ? acts[l][i] : 0;
-            width[l + 1] = w;
+            for (size_t i = 0; i < m * w; i++) y[i] = x[i] <= 1073741823u ? x[i] : 0;
         } else if (layers[l].type == 2) {
             /* apply_rmsnorm_detailed (compiler/prove.rs:1115-1180), dim = the layer width */
             uint32_t *tab = (uint32_t *)malloc(4u << 16);
             orc_rsqrt_table(16, tab);
             uint32_t inv_n = m_inv((uint32_t)(w % MP));
-            acts[l + 1] = (uint32_t *)malloc(4 * m * w);
             for (size_t i = 0; i < m; i++) {
                 uint32_t sq = 0;
-                for (size_t j = 0; j < w; j++) sq = m_add(sq, m_mul(acts[l][i * w + j], acts[l][i * w + j]));
+                for (size_t j = 0; j < w; j++) sq = m_add(sq, m_mul(x[i * w + j], x[i * w + j]));
                 uint32_t rs = tab[m_mul(sq, inv_n) & 0xFFFF];
-                for (size_t j = 0; j < w; j++) acts[l + 1][i * w + j] = m_mul(acts[l][i * w + j], rs);
+                for (size_t j = 0; j < w; j++) y[i * w + j] = m_mul(x[i * w + j], rs);
             }
             free(tab);
-            width[l + 1] = w;
         } else {
-            return 1;
+            /* elementwise_add / elementwise_mul (compiler/prove.rs:875-925), lhs op rhs */
+            const uint32_t *a = outs[layers[l].lhs + 1];
+            for (size_t i = 0; i < m * w; i++) y[i] = layers[l].type == 3 ? m_add(a[i], x[i]) : m_mul(a[i], x[i]);
         }
+    }
+    if (rc) {
+        for (size_t l = 0; l <= built; l++) free(outs[l]);
+        return rc;
     }
     orc_channel ch;
     orc_ch_init(&ch);
@@ -2863,7 +2898,7 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     q31 point[64], value;
     for (unsigned i = 0; i < nvo; i++) point[i] = ch_draw_qm31(&ch);
     {
-        q31 *omle = mle_row_major(acts[n_layers], m, wout);
+        q31 *omle = mle_row_major(outs[n_layers], m, wout);
         uint32_t val[4];
         orc_evaluate_mle((const uint32_t *)omle, nvo, (const uint32_t *)point, val);
         free(omle);
@@ -2871,16 +2906,22 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     }
     ch_mix_sf(&ch, value);
     unsigned npt = nvo;
-    felt_out o = {calldata, 0, cap, 0};
-    out_u64(&o, n_layers);
-    /* weight claims in walk order */
+    const int v1 = (flags & 2) != 0;
+    felt_out lay = {(uint64_t *)malloc(32 * cap), 0, cap, 0};
+    size_t n_proofs = 0;
+    /* weight claims: the walk's, in walk order */
     q31 *wpts[64];
     unsigned wnv[64];
     q31 wval[64];
     size_t widx[64], nw = 0;
-    int rc = 0;
+    chain_deferred *defs = (chain_deferred *)calloc(64, sizeof(chain_deferred));
+    size_t nd = 0;
+    unsigned char skip[64] = {0};
     for (size_t li = n_layers; li-- > 0 && !rc;) {
-        size_t w = width[li];
+        if (skip[li]) continue;
+        n_proofs++;
+        const uint32_t *x = outs[src[li] + 1];
+        size_t w = width[src[li] + 1];
         if (layers[li].type == 0) {
             size_t n = layers[li].n;
             unsigned log_k = ilog2(next_pow2(w)), log_n = ilog2(next_pow2(n));
@@ -2889,20 +2930,20 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             q31 nxt[64];
             uint32_t cv[4];
             q_store(cv, value);
-            rc = orc_reduce_matmul_gkr((const uint32_t *)point, npt, cv, acts[li], m, w, layers[li].weight, n, &ch, rp,
-                                       fa, fb, (uint32_t *)nxt, 1, threads);
+            rc = orc_reduce_matmul_gkr((const uint32_t *)point, npt, cv, x, m, w, layers[li].weight, n, &ch, rp, fa, fb,
+                                       (uint32_t *)nxt, 1, threads);
             if (rc) {
                 free(rp);
                 break;
             }
-            out_u64(&o, 0);
-            out_u64(&o, log_k);
+            out_u64(&lay, 0);
+            out_u64(&lay, log_k);
             for (unsigned r = 0; r < log_k; r++) {
-                out_qm31(&o, q_load(rp + 12 * r));
-                out_qm31(&o, q_load(rp + 12 * r + 8));
+                out_qm31(&lay, q_load(rp + 12 * r));
+                out_qm31(&lay, q_load(rp + 12 * r + 8));
             }
-            out_qm31(&o, q_load(fa));
-            out_qm31(&o, q_load(fb));
+            out_qm31(&lay, q_load(fa));
+            out_qm31(&lay, q_load(fb));
             /* weight claim: r_j || sumcheck challenges (prover.rs:1465-1483) */
             wnv[nw] = log_n + log_k;
             wpts[nw] = (q31 *)malloc(sizeof(q31) * (wnv[nw] + 1));
@@ -2920,35 +2961,152 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             uint64_t *tbuf = (uint64_t *)malloc(32 * tcap);
             uint32_t cv[4], ie[4];
             q_store(cv, value);
-            rc = orc_reduce_rmsnorm(acts[li], m, w, w, NULL, 0, 0, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap,
-                                    &tlen, ie);
+            rc = orc_reduce_rmsnorm(x, m, w, w, NULL, 0, 0, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen,
+                                    ie);
             for (size_t i = 0; i < tlen && !rc; i++) {
                 fe f;
                 fe_from_canon(&f, tbuf + 4 * i);
-                out_push(&o, &f);
+                out_push(&lay, &f);
             }
             free(tbuf);
             value = q_load(ie);
-        } else {
+        } else if (layers[li].type == 1) {
             q31 nxt[64], nval;
-            rc = relu_reduce(acts[li], m, w, point, value, &ch, &o, nxt, &nval, flags & 1);
+            rc = relu_reduce(x, m, w, point, value, &ch, &lay, nxt, &nval, flags & 1);
             npt = ilog2(next_pow2(m) * next_pow2(w));
             memcpy(point, nxt, sizeof(q31) * npt);
             value = nval;
+        } else {
+            /* binary op: input_layers = [lhs, rhs]; the trunk is the higher layer index */
+            const long long il0 = layers[li].lhs, il1 = src[li];
+            const uint32_t *lv = outs[il0 + 1];
+            q31 *la = mle_row_major(lv, m, w), *ra = mle_row_major(x, m, w);
+            size_t n = next_pow2(m) * next_pow2(w);
+            unsigned nv = ilog2(n);
+            q31 le, re;
+            if (npt < nv) {
+                rc = 1;
+            } else if (layers[li].type == 3) {
+                /* reduce_add_layer (prover.rs:6103-6146) + process_add_deferred (prover.rs:1424-1463) */
+                le = mle_eval_copy(la, n, point, nv);
+                re = mle_eval_copy(ra, n, point, nv);
+                ch_mix_sf(&ch, le);
+                ch_mix_sf(&ch, re);
+                (void)ch_draw_qm31(&ch);
+                const int rhs_trunk = il1 > il0;
+                out_u64(&lay, 1);
+                out_qm31(&lay, le);
+                out_qm31(&lay, re);
+                out_u64(&lay, rhs_trunk ? 1 : 0);
+                chain_deferred *d = &defs[nd++];
+                memcpy(d->point, point, sizeof(q31) * npt);
+                d->npt = npt;
+                d->value = rhs_trunk ? le : re;
+                d->layer = (size_t)(rhs_trunk ? il0 : il1);
+                value = rhs_trunk ? re : le;
+            } else {
+                /* reduce_mul_layer (prover.rs:6172-6280) and the branched-Mul claim
+                 * (prover.rs:1719-1760): the deferred claim carries rhs_eval, the walk goes on
+                 * at the same point with the trunk's evaluation */
+                q31 *eq = lagrange_basis(point, nv);
+                q31 *rps = (q31 *)malloc(sizeof(q31) * 4 * (nv + 1)), chal[64];
+                orc_ch_mix_u64(&ch, 0x4D554C);
+                ch_mix_sf(&ch, value);
+                eq_sumcheck_deg3(&ch, eq, la, ra, n, nv, rps, chal);
+                le = la[0];
+                re = ra[0];
+                ch_mix_sf(&ch, le);
+                ch_mix_sf(&ch, re);
+                (void)ch_draw_qm31(&ch);
+                out_u64(&lay, 2);
+                out_u64(&lay, nv);
+                for (unsigned r = 0; r < nv; r++) {
+                    out_qm31(&lay, rps[4 * r]);
+                    out_qm31(&lay, rps[4 * r + 2]);
+                    out_qm31(&lay, rps[4 * r + 3]);
+                }
+                out_qm31(&lay, le);
+                out_qm31(&lay, re);
+                free(rps);
+                free(eq);
+                const int rhs_trunk = il1 > il0;
+                const long long sk = rhs_trunk ? il0 : il1;
+                chain_deferred *d = &defs[nd++];
+                memcpy(d->point, point, sizeof(q31) * npt);
+                d->npt = npt;
+                d->value = re;
+                d->layer = (size_t)sk;
+                skip[sk] = 1;
+                value = rhs_trunk ? re : le;
+            }
+            free(la);
+            free(ra);
         }
     }
+    /* deferred proofs of the skip branches, then their Sequential openings (prover.rs:1918-2047) */
+    felt_out dsec = {(uint64_t *)malloc(32 * cap), 0, cap, 0};
+    fe dcoms[64];
+    uint64_t *dobufs[64] = {0};
+    size_t dolens[64];
+    out_u64(&dsec, nd);
+    for (size_t i = 0; i < nd && !rc; i++) {
+        chain_deferred *d = &defs[i];
+        size_t L = d->layer;
+        if (layers[L].type != 0) {
+            rc = 4;
+            break;
+        }
+        const uint32_t *x = outs[src[L] + 1];
+        size_t w = width[src[L] + 1], n = layers[L].n;
+        unsigned log_k = ilog2(next_pow2(w)), log_n = ilog2(next_pow2(n));
+        ch_mix_sf(&ch, d->value);
+        uint32_t *rp = (uint32_t *)malloc(48 * (log_k + 1));
+        uint32_t fa[4], fb[4], cv[4];
+        q31 nxt[64];
+        q_store(cv, d->value);
+        rc = orc_reduce_matmul_gkr((const uint32_t *)d->point, d->npt, cv, x, m, w, layers[L].weight, n, &ch, rp, fa,
+                                   fb, (uint32_t *)nxt, 1, threads);
+        if (rc) {
+            free(rp);
+            break;
+        }
+        q31 wp[64];
+        memcpy(wp, d->point + log_m, sizeof(q31) * log_n);
+        memcpy(wp + log_n, nxt + log_m, sizeof(q31) * log_k);
+        q31 *bmle = mle_col_major(layers[L].weight, w, n, threads);
+        unsigned nv = log_n + log_k;
+        size_t ocap = 64 + (n_queries + 1) * (2 + (size_t)nv * (10 + 2 * (nv + 1)));
+        dobufs[i] = (uint64_t *)malloc(32 * ocap);
+        felt_out oo = {dobufs[i], 0, ocap, 0};
+        prove_opening(bmle, nv, wp, &ch, n_queries, &dcoms[i], &oo, NULL, threads);
+        dolens[i] = oo.len;
+        free(bmle);
+        /* serialize_gkr_proof_data_only's deferred record (cairo_serde.rs:2238-2276) */
+        out_qm31(&dsec, d->value);
+        out_u64(&dsec, 0);
+        out_u64(&dsec, m);
+        out_u64(&dsec, w);
+        out_u64(&dsec, n);
+        out_u64(&dsec, log_k);
+        for (unsigned r = 0; r < log_k; r++) {
+            out_qm31(&dsec, q_load(rp + 12 * r));
+            out_qm31(&dsec, q_load(rp + 12 * r + 8));
+        }
+        out_qm31(&dsec, q_load(fa));
+        out_qm31(&dsec, q_load(fb));
+        out_push(&dsec, &dcoms[i]);
+        free(rp);
+    }
+    felt_out o = {calldata, 0, cap, 0};
     if (!rc) {
-        /* input claim */
-        out_u64(&o, npt);
-        for (unsigned i = 0; i < npt; i++) out_qm31(&o, point[i]);
-        out_qm31(&o, value);
-        /* Sequential weight openings on the main channel, in walk order */
+        /* Sequential weight openings of the walk on the main channel, in walk order */
         fe coms[64];
         uint64_t *obufs[64];
         size_t olens[64];
         for (size_t i = 0; i < nw; i++) {
             size_t l = widx[i];
-            q31 *bmle = mle_col_major(layers[l].weight, width[l], layers[l].n, threads);
+            size_t w = width[src[l] + 1];
+            q31 *bmle = mle_col_major(layers[l].weight, w, layers[l].n, threads);
             size_t ocap = 64 + (n_queries + 1) * (2 + (size_t)wnv[i] * (10 + 2 * (wnv[i] + 1)));
             obufs[i] = (uint64_t *)malloc(32 * ocap);
             felt_out oo = {obufs[i], 0, ocap, 0};
@@ -2956,31 +3114,54 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             olens[i] = oo.len;
             free(bmle);
         }
-        out_u64(&o, nw);
-        for (size_t i = 0; i < nw; i++) out_push(&o, &coms[i]);
-        out_u64(&o, nw);
-        for (size_t i = 0; i < nw; i++) {
-            out_u64(&o, wnv[i]);
-            for (unsigned j = 0; j < wnv[i]; j++) out_qm31(&o, wpts[i][j]);
-            out_qm31(&o, wval[i]);
-            for (size_t j = 0; j < olens[i]; j++) {
-                fe f;
-                fe_from_canon(&f, obufs[i] + 4 * j);
-                out_push(&o, &f);
+        if (v1) {
+            out_u64(&o, lay.len + dsec.len);
+            for (size_t j = 0; j < lay.len && j < lay.cap; j++) out_push(&o, (const fe *)(lay.buf + 4 * j));
+            for (size_t j = 0; j < dsec.len && j < dsec.cap; j++) out_push(&o, (const fe *)(dsec.buf + 4 * j));
+            out_u64(&o, nw + nd);
+            for (size_t i = 0; i < nw; i++) out_push(&o, &coms[i]);
+            for (size_t i = 0; i < nd; i++) out_push(&o, &dcoms[i]);
+            out_u64(&o, nw + nd);
+            for (size_t i = 0; i < nw; i++)
+                for (size_t j = 0; j < olens[i]; j++) out_push(&o, (const fe *)(obufs[i] + 4 * j));
+            for (size_t i = 0; i < nd; i++)
+                for (size_t j = 0; j < dolens[i]; j++) out_push(&o, (const fe *)(dobufs[i] + 4 * j));
+        } else {
+            out_u64(&o, n_proofs);
+            for (size_t j = 0; j < lay.len && j < lay.cap; j++) out_push(&o, (const fe *)(lay.buf + 4 * j));
+            /* input claim */
+            out_u64(&o, npt);
+            for (unsigned i = 0; i < npt; i++) out_qm31(&o, point[i]);
+            out_qm31(&o, value);
+            out_u64(&o, nw);
+            for (size_t i = 0; i < nw; i++) out_push(&o, &coms[i]);
+            out_u64(&o, nw);
+            for (size_t i = 0; i < nw; i++) {
+                out_u64(&o, wnv[i]);
+                for (unsigned j = 0; j < wnv[i]; j++) out_qm31(&o, wpts[i][j]);
+                out_qm31(&o, wval[i]);
+                for (size_t j = 0; j < olens[i]; j++) out_push(&o, (const fe *)(obufs[i] + 4 * j));
             }
-            free(obufs[i]);
         }
-        orc_io_commitment(acts[0], m, k0, acts[n_layers], m, wout, io);
-        fe iof;
-        fe_from_canon(&iof, io);
-        out_push(&o, &iof);
+        for (size_t i = 0; i < nw; i++) free(obufs[i]);
+        orc_io_commitment(outs[0], m, k0, outs[n_layers], m, wout, io);
+        if (!v1) {
+            fe iof;
+            fe_from_canon(&iof, io);
+            out_push(&o, &iof);
+        }
         memcpy(digest, ch.digest, 32);
         *out_len = o.len;
     }
+    for (size_t i = 0; i < nd; i++) free(dobufs[i]);
     for (size_t i = 0; i < nw; i++) free(wpts[i]);
-    for (size_t l = 0; l <= n_layers; l++) free(acts[l]);
+    for (size_t l = 0; l <= n_layers; l++) free(outs[l]);
+    const int overflow = o.overflow || lay.overflow || dsec.overflow;
+    free(lay.buf);
+    free(dsec.buf);
+    free(defs);
     if (rc) return rc;
-    return o.overflow ? 2 : 0;
+    return overflow ? 2 : 0;
 }
 
 int orc_reduce_activation_relu(const uint32_t *input, size_t rows, size_t cols, const uint32_t *claim_point,

@@ -194,18 +194,34 @@ int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const 
                                     size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
                                     uint32_t out_input_eval[4]);
 
-/* One layer of a sequential GKR chain: type 0 = Linear (weight: rows = the layer's input
- * width, n columns, row major), type 1 = ReLU, type 2 = RMSNorm over the full width. */
+/* One layer of a GKR circuit (LayeredCircuit::from_graph, gkr/circuit.rs:140-225, for the
+ * GraphBuilder ops linear / activation(ReLU) / rms_norm / add_from / mul_from):
+ * type 0 = Linear (weight: rows = the layer's input width, n columns, row major), 1 = ReLU,
+ * 2 = RMSNorm over the full width, 3 = Add, 4 = Mul (element-wise, M31).
+ * src: the layer whose output is this layer's input (for Add / Mul the rhs operand);
+ * ORC_CHAIN_PREV = the previous layer (the model input for layer 0), -1 = the model input.
+ * lhs: Add / Mul only, the layer whose output is the lhs operand (the saved fork). */
+#define ORC_CHAIN_PREV (-2)
 typedef struct {
     int type;
     const uint32_t *weight;
     size_t n;
+    long long src;
+    long long lhs;
 } orc_chain_layer;
-/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for GraphBuilder::new((m, k0)) followed by
- * the given Linear / ReLU layers, Sequential weight binding, serialized by
- * serialize_gkr_model_proof (cairo_serde.rs:1307-1772).  Writes the final digest and the
- * io commitment.  flags bit 0: the earlier Activation record layout without the
- * multiplicity-sumcheck and piecewise flags (the layout of engine/tests/artifacts/sp3_mlp_proof.json). */
+/* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for such a circuit on an m x k0 input:
+ * the walk from the output with DAG Add / Mul layers (prover.rs:1424-1463, 1705-1760), the
+ * deferred MatMul proofs of their skip branches (prover.rs:1918-2047), Sequential weight
+ * binding (deferred openings first, then the walk's, all on the main channel).  Output:
+ *   flags bit 1 clear: serialize_gkr_model_proof (cairo_serde.rs:1307-1772), which carries
+ *     neither the deferred proofs nor their openings;
+ *   flags bit 1 set: the verify_model_gkr calldata (starknet.rs:3143-3345, layout V1) from
+ *     proof_data on: proof_data (serialize_gkr_proof_data_only, cairo_serde.rs:1816-2277,
+ *     deferred proofs included), weight commitments (walk, then deferred), opening proofs.
+ * flags bit 0: the earlier Activation record layout without the multiplicity-sumcheck and
+ * piecewise flags (the layout of engine/tests/artifacts/sp3_mlp_proof.json).
+ * Writes the final digest and the io commitment.  Returns 4 for a deferred branch that is
+ * not a Linear layer (the reference's "deferred proof not yet supported"). */
 int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
                         const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
                         size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads);

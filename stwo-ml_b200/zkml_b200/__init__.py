@@ -121,6 +121,9 @@ _SIGS = {
     "zkml_prove_gkr_chain": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                        C.c_void_p, C.c_size_t, C.c_int, _u64, C.c_size_t, C.POINTER(C.c_size_t),
                                        _u64, _u64]),
+    "zkml_build_verify_model_gkr_calldata": (C.c_int, [C.c_void_p, _u64, C.c_void_p, C.c_size_t, C.c_size_t,
+                                                       C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int,
+                                                       _u64, C.c_size_t, C.POINTER(C.c_size_t), _u64, _u64]),
     "zkml_p2p_inbox_create": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]),
     "zkml_p2p_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "zkml_p2p_close": (C.c_int, [C.c_void_p]),
@@ -731,12 +734,17 @@ def reduce_activation_layer_relu(output_claim: GKRClaim, inp: M31Matrix, channel
 
 
 class _ChainLayer(C.Structure):
-    _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t)]
+    _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t), ("src", C.c_longlong),
+                ("lhs", C.c_longlong)]
+
+
+CHAIN_PREV = -2
+_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4}
 
 
 @dataclass
 class GKRChainProof:
-    raw: np.ndarray       # serialize_gkr_model_proof, 4 x u64 limbs per felt
+    raw: np.ndarray       # serialize_gkr_model_proof (or verify_model_gkr calldata), 4 x u64 limbs per felt
     final_digest: int
     io_commitment: int
 
@@ -745,46 +753,86 @@ class GKRChainProof:
         return _felts(self.raw, self.raw.size // 4)
 
 
-def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_queries: Optional[int] = None,
-                    legacy_activation_record: bool = False, device: int = 0) -> GKRChainProof:
-    """prove_gkr (gkr/prover.rs:1500-2251) for GraphBuilder::new(inp.shape) followed by `layers`,
-    each ("linear", weight) with weight (in_width, n), ("relu", None) or ("rmsnorm", None);
-    Sequential weight binding."""
+def _chain_args(inp, layers, n_queries):
+    """ctypes layer array, buffers to keep alive and a calldata capacity for `layers`, each
+    (kind, arg[, src]): ("linear", weight (in_width, n)), ("relu", None), ("rmsnorm", None),
+    ("add", lhs_layer), ("mul", lhs_layer); src = the layer feeding this one (None: the
+    previous layer, -1: the model input).  The Add / Mul rhs operand is src's output."""
     im = as_matrix(inp)
     ib = _Buf(im.data)
     keep = [ib]
     arr = (_ChainLayer * len(layers))()
-    width, nv_max, n_lin = im.cols, 0, 0
-    for i, (kind, w) in enumerate(layers):
+    widths = [im.cols]  # widths[l + 1]: layer l's output width; widths[0]: the input's
+    nv_max, n_lin, n_bin = 0, 0, 0
+    for i, spec in enumerate(layers):
+        kind, arg = spec[0], spec[1]
+        src = spec[2] if len(spec) > 2 and spec[2] is not None else CHAIN_PREV
+        if kind not in _CHAIN_KINDS:
+            raise InvalidArgument(1, f"layer {i}: unknown kind {kind}")
+        s_eff = i - 1 if src == CHAIN_PREV else src
+        if not -1 <= s_eff < i:
+            raise InvalidArgument(1, f"layer {i}: input layer {src} is not a lower layer")
+        width = widths[s_eff + 1]
+        arr[i].type, arr[i].weight, arr[i].n, arr[i].src, arr[i].lhs = _CHAIN_KINDS[kind], None, 0, src, -1
         if kind == "linear":
-            wm = as_matrix(w)
+            wm = as_matrix(arg)
             if wm.rows != width:
                 raise InvalidArgument(1, f"layer {i}: weight rows {wm.rows} != input width {width}")
             wb = _Buf(wm.data)
             keep.append(wb)
-            arr[i].type, arr[i].weight, arr[i].n = 0, wb.ptr.value, wm.cols
+            arr[i].weight, arr[i].n = wb.ptr.value, wm.cols
             nv_max = max(nv_max, _log2(_next_pow2(wm.rows)) + _log2(_next_pow2(wm.cols)))
             width = wm.cols
             n_lin += 1
-        elif kind == "relu":
-            arr[i].type, arr[i].weight, arr[i].n = 1, None, 0
-        elif kind == "rmsnorm":
-            arr[i].type, arr[i].weight, arr[i].n = 2, None, 0
-        else:
-            raise InvalidArgument(1, f"layer {i}: unknown kind {kind}")
+        elif kind in ("add", "mul"):
+            arr[i].lhs = int(arg)
+            n_bin += 1
+        widths.append(width)
     nq = mle_n_queries() if n_queries is None else n_queries
-    nv_all = _log2(_next_pow2(im.rows)) + max(nv_max, _log2(_next_pow2(width)) + 1)
-    n_norm = sum(1 for kind, _ in layers if kind == "rmsnorm")
-    cap = 256 + len(layers) * (200 + 12 * nv_all) + n_lin * (64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1))))
+    nv_all = _log2(_next_pow2(im.rows)) + max(nv_max, max(_log2(_next_pow2(w)) for w in widths) + 1)
+    n_norm = sum(1 for spec in layers if spec[0] == "rmsnorm")
+    per_open = 64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1)))
+    cap = 256 + len(layers) * (200 + 12 * nv_all) + (n_lin + n_bin) * per_open + n_bin * (60 + 16 * nv_all)
     cap += n_norm * ((1 << 16) + _next_pow2(im.rows) + 40 * (nv_all + 2))
+    cap += 2 * im.rows * max(widths)
+    return im, ib, arr, keep, nq, cap
+
+
+def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_queries: Optional[int] = None,
+                    legacy_activation_record: bool = False, v1_layout: bool = False,
+                    device: int = 0) -> GKRChainProof:
+    """prove_gkr (gkr/prover.rs:1500-2251) for GraphBuilder::new(inp.shape) followed by `layers`
+    (see _chain_args; Add / Mul layers defer their skip branch), Sequential weight binding.
+    raw: serialize_gkr_model_proof, or with v1_layout the verify_model_gkr calldata from
+    proof_data on (deferred proofs and their openings included)."""
+    im, ib, arr, keep, nq, cap = _chain_args(inp, layers, n_queries)
     out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
     dig = np.zeros(4, np.uint64)
     io = np.zeros(4, np.uint64)
     pol = felt_to_limbs(policy_commitment) if policy_commitment else None
+    flags = (1 if legacy_activation_record else 0) | (2 if v1_layout else 0)
     _check(lib().zkml_prove_gkr_chain(context(device).handle, ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
                                       len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq,
-                                      1 if legacy_activation_record else 0, out, cap, C.byref(ln), dig, io))
+                                      flags, out, cap, C.byref(ln), dig, io))
+    return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
+
+
+def build_verify_model_gkr_calldata(model_id: int, inp, layers, policy_commitment: Optional[int] = None,
+                                    n_queries: Optional[int] = None, device: int = 0) -> GKRChainProof:
+    """build_verify_model_gkr_calldata (starknet.rs:2837-2852): the proof of the circuit and the
+    whole verify_model_gkr(model_id, raw_io_data, circuit_depth, num_layers, matmul_dims,
+    dequantize_bits, proof_data, weight_commitments, weight_opening_proofs) calldata."""
+    im, ib, arr, keep, nq, cap = _chain_args(inp, layers, n_queries)
+    out = np.empty(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    dig = np.zeros(4, np.uint64)
+    io = np.zeros(4, np.uint64)
+    pol = felt_to_limbs(policy_commitment) if policy_commitment else None
+    _check(lib().zkml_build_verify_model_gkr_calldata(
+        context(device).handle, felt_to_limbs(model_id), ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
+        len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq, 0, out, cap, C.byref(ln), dig,
+        io))
     return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
 
 

@@ -13,6 +13,18 @@ reference's own known answers for the matmul-sumcheck path:
   [1,2,3,4] -> Linear(4) with W0[i][j] = (i+j)%7+1 -> ReLU -> Linear(2) with
   W2[i][j] = i+j+1 -- full GKR calldata (780 felts), weight commitments, io commitment,
   final channel digest.
+* ``d9_verify_calldata``: engine/tests/artifacts/d9_verify_gkr_calldata.txt, written by
+  engine/tests/e2e_cairo_verify.rs:1375-1470 (build_verify_model_gkr_calldata, layout V1, for
+  the sp3_mlp model with model id 0xd9) -- the whole verify_model_gkr calldata (754 felts).
+  The artifact was generated with 5 MLE-opening queries (its opening proofs carry 5) and
+  predates the Activation record's trailing piecewise flag (cairo_serde.rs:1881).
+* ``d11_residual``: engine/tests/artifacts/d11_verify_gkr_calldata.txt and
+  d11_onchain_summary.json, written by e2e_cairo_verify.rs:1549-1660 for
+  Linear(identity 4x4) -> fork -> ReLU -> Linear(W2[i][j] = (i+j)%3+1) -> add_from(fork) on the
+  input [1,2,3,4] (model id 0xdb).  The calldata file predates the compressed round
+  polynomials (it carries c0, c1, c2) and the algebraic ReLU proof, so only its leading Add
+  record and the first round of the next MatMul are pinned, with the io commitment and the
+  walk's weight commitments.
 * ``poseidon_kats``: engine/src/crypto/poseidon_channel.rs:1619-1637
   (poseidon_hash_many([0, pack(QM31(1,2,3,4))])) and
   stwo-gpu/crates/stwo/src/core/channel/poseidon252.rs:230-241
@@ -28,6 +40,23 @@ from pathlib import Path
 ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
 art = json.loads((ref / "engine/tests/artifacts/sp3_matmul_only_proof.json").read_text())
 mlp = json.loads((ref / "engine/tests/artifacts/sp3_mlp_proof.json").read_text())
+d11_summary = json.loads((ref / "engine/tests/artifacts/d11_onchain_summary.json").read_text())
+
+
+def _calldata(name):
+    """The artifact's felts as hex strings (decimal tokens converted)."""
+    toks = (ref / f"engine/tests/artifacts/{name}_verify_gkr_calldata.txt").read_text().split()
+    return [t if t.startswith("0x") else hex(int(t)) for t in toks]
+
+
+def _d11_proof_data():
+    """proof_data of the d11 calldata: after model_id, raw io, depth, layer count, matmul
+    dims (6) and dequantize bits (0) comes its length, then the felts."""
+    v = [int(t, 16) for t in _calldata("d11")]
+    i = 2 + v[1] + 2 + 1 + v[2 + v[1] + 2] + 1
+    n = v[i]
+    return [int(x) for x in v[i + 1:i + 1 + n]]
+
 out = {
     "sp3_matmul_only": {
         "source": "engine/tests/artifacts/sp3_matmul_only_proof.json",
@@ -55,6 +84,24 @@ out = {
         "io_commitment": mlp["io_commitment"],
         "final_channel_digest": mlp["verification"]["final_channel_digest"],
     },
+    "d9_verify_calldata": {
+        "source": "engine/tests/artifacts/d9_verify_gkr_calldata.txt",
+        "model_id": "0xd9",
+        "n_queries": 5,
+        "calldata": _calldata("d9"),
+    },
+    "d11_residual": {
+        "source": "engine/tests/artifacts/d11_verify_gkr_calldata.txt, d11_onchain_summary.json",
+        "model_id": "0xdb",
+        "input": [[1, 2, 3, 4]],
+        "w0": [[1 if i == j else 0 for j in range(4)] for i in range(4)],
+        "w2": [[(i + j) % 3 + 1 for j in range(4)] for i in range(4)],
+        "add_record": _d11_proof_data()[:10],
+        "matmul_round0_c0": _d11_proof_data()[12:16],
+        "matmul_round0_c2": _d11_proof_data()[20:24],
+        "io_commitment": d11_summary["io_commitment"],
+        "weight_commitments": d11_summary["weight_commitments"],
+    },
     "poseidon_kats": [
         {
             "op": "poseidon_hash_many",
@@ -78,6 +125,8 @@ assert out["poseidon_kats"][1]["expect"] in src2
 # Sanity: the MLP weights are the ones build_gkr_mlp_relu sets.
 src3 = (ref / "engine/tests/e2e_cairo_verify.rs").read_text()
 assert "M31::from(((i + j) % 7 + 1) as u32)" in src3 and "M31::from((i + j + 1) as u32)" in src3
+# Sanity: the d11 residual model's weights are the ones its test sets.
+assert "w2.set(i, j, M31::from(((i + j) % 3 + 1) as u32));" in src3 and "w0.set(i, i, M31::from(1u32));" in src3
 dst = Path(__file__).with_name("reference_vectors.json")
 dst.write_text(json.dumps(out, indent=1) + "\n")
 print("wrote", dst)

@@ -349,24 +349,38 @@ def verify_activation_piecewise(raw, point, value, ch):
 
 
 class ChainLayer(C.Structure):
-    _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t)]
+    _fields_ = [("type", C.c_int), ("weight", C.c_void_p), ("n", C.c_size_t), ("src", C.c_longlong),
+                ("lhs", C.c_longlong)]
 
 
-def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, cap=1 << 20):
-    """layers: list of ("linear", weight (rows, n)) or ("relu", None)."""
-    inp = np.ascontiguousarray(inp, np.uint32)
-    m, k0 = inp.shape
+CHAIN_PREV = -2
+_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4}
+
+
+def chain_layers(layers):
+    """ctypes array for layers given as (kind, arg[, src]): ("linear", weight (rows, n)),
+    ("relu", None), ("rmsnorm", None), ("add", lhs layer), ("mul", lhs layer); src is the
+    layer feeding this one (None = the previous layer, -1 = the model input)."""
     keep = []
     arr = (ChainLayer * len(layers))()
-    for i, (kind, w) in enumerate(layers):
+    for i, spec in enumerate(layers):
+        kind, arg = spec[0], spec[1]
+        src = spec[2] if len(spec) > 2 and spec[2] is not None else CHAIN_PREV
+        arr[i].type, arr[i].weight, arr[i].n, arr[i].src, arr[i].lhs = _CHAIN_KINDS[kind], None, 0, src, -1
         if kind == "linear":
-            w = np.ascontiguousarray(w, np.uint32)
+            w = np.ascontiguousarray(arg, np.uint32)
             keep.append(w)
-            arr[i].type, arr[i].weight, arr[i].n = 0, w.ctypes.data, w.shape[1]
-        elif kind == "rmsnorm":
-            arr[i].type, arr[i].weight, arr[i].n = 2, None, 0
-        else:
-            arr[i].type, arr[i].weight, arr[i].n = 1, None, 0
+            arr[i].weight, arr[i].n = w.ctypes.data, w.shape[1]
+        elif kind in ("add", "mul"):
+            arr[i].lhs = int(arg)
+    return arr, keep
+
+
+def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, v1_layout=False, cap=1 << 20):
+    """layers: see chain_layers.  v1_layout: the verify_model_gkr calldata from proof_data on."""
+    inp = np.ascontiguousarray(inp, np.uint32)
+    m, k0 = inp.shape
+    arr, keep = chain_layers(layers)
     buf = np.zeros(4 * cap, np.uint64)
     ln = C.c_size_t(0)
     dig = np.zeros(4, np.uint64)
@@ -374,7 +388,7 @@ def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False,
     pol = None if policy is None else felt(policy)
     rc = lib().orc_prove_gkr_chain(inp.reshape(-1), m, k0, C.cast(arr, C.c_void_p), len(layers),
                                    None if pol is None else pol.ctypes.data_as(C.c_void_p), n_queries,
-                                   int(legacy_layout), buf, cap,
+                                   int(legacy_layout) | (2 if v1_layout else 0), buf, cap,
                                    C.byref(ln), dig, io, threads())
     return rc, buf[:4 * ln.value].copy(), felt_int(dig), felt_int(io)
 

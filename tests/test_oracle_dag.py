@@ -1,0 +1,140 @@
+"""The oracle's DAG circuits (Add / Mul layers with deferred skip-branch proofs) and the
+verify_model_gkr calldata layout, pinned against the reference's artifacts:
+
+* d9_verify_gkr_calldata.txt (sp3_mlp model, model id 0xd9): every felt of the V1 calldata,
+  after removing the Activation record's trailing piecewise flag, which the artifact predates;
+* d11 (Linear -> fork -> ReLU -> Linear -> add_from(fork)): the Add record, the first
+  round of the next MatMul sumcheck, the io commitment and the weight commitments.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle_lib as O
+from helpers import int_matrix_m31
+
+GOLD = json.loads((Path(__file__).parent / "golden" / "reference_vectors.json").read_text())
+
+
+def felts(raw):
+    b = raw.reshape(-1, 4)
+    return [sum(int(r[i]) << (64 * i) for i in range(4)) for r in b]
+
+
+def v1_envelope(model_id, x, y, layers, n_proofs):
+    """verify_model_gkr's leading arguments (starknet.rs:3168-3200) for a chain proof."""
+    m, k0 = x.shape
+    out = [model_id, 6 + x.size + y.size, m, k0, x.size, *map(int, x.reshape(-1)), y.shape[0], y.shape[1], y.size,
+           *map(int, y.reshape(-1)), len(layers), n_proofs]
+    widths, dims = [k0], []
+    for spec in layers:
+        widths.append(spec[1].shape[1] if spec[0] == "linear" else widths[-1])
+    for i in reversed(range(len(layers))):
+        if layers[i][0] == "linear":
+            dims += [m, widths[i], widths[i + 1]]
+    return out + [len(dims), *dims, 0]
+
+
+def sp3_model():
+    g = GOLD["sp3_mlp"]
+    x = np.array([g["input"]], np.uint32)
+    w0, w2 = (np.array(w, np.uint32) for w in g["weights"])
+    return x, [("linear", w0), ("relu", None), ("linear", w2)], np.array([g["output"]], np.uint32)
+
+
+def drop_piecewise_flag(tail, relu_at=26, walk_tail=26 + 1):
+    """The V1 tail without the ReLU record's last felt (its piecewise flag); the ReLU record sits
+    between the first MatMul record (26 felts) and the last MatMul record + deferred count."""
+    pd_len = tail[0]
+    idx = 1 + pd_len - walk_tail - 1
+    assert tail[idx] == 0
+    return [pd_len - 1] + tail[1:idx] + tail[idx + 1:]
+
+
+def test_d9_verify_calldata_reproduced():
+    g = GOLD["d9_verify_calldata"]
+    x, layers, y = sp3_model()
+    rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=g["n_queries"], v1_layout=True)
+    assert rc == 0
+    tail = drop_piecewise_flag(felts(raw))
+    mine = v1_envelope(int(g["model_id"], 16), x, y, layers, 3) + tail
+    assert mine == [int(h, 16) for h in g["calldata"]]
+
+
+def d11_model():
+    g = GOLD["d11_residual"]
+    x = np.array(g["input"], np.uint32)
+    w0, w2 = np.array(g["w0"], np.uint32), np.array(g["w2"], np.uint32)
+    return x, [("linear", w0), ("relu", None), ("linear", w2), ("add", 0)]
+
+
+def test_d11_residual_pins():
+    g = GOLD["d11_residual"]
+    x, layers = d11_model()
+    rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=5, v1_layout=True)
+    assert rc == 0
+    tail = felts(raw)
+    pd = tail[1:1 + tail[0]]
+    assert pd[:10] == g["add_record"]
+    assert pd[10:12] == [0, 2]  # MatMul tag, 2 rounds
+    assert pd[12:16] == g["matmul_round0_c0"] and pd[16:20] == g["matmul_round0_c2"]
+    assert io == int(g["io_commitment"], 16)
+    coms = tail[1 + tail[0]:]
+    assert coms[0] == 3  # the walk's two weights, then the deferred branch's (W0 again)
+    assert coms[1:3] == [int(c, 16) for c in g["weight_commitments"]] and coms[3] == coms[2]
+    # the deferred record: count 1, the skip claim (the Add's lhs), kind MatMul, m k n
+    dstart = len(pd) - (4 + 1 + 3 + 1 + 2 * 8 + 8 + 1) - 1
+    assert pd[dstart] == 1 and pd[dstart + 1:dstart + 5] == g["add_record"][1:5]
+    assert pd[dstart + 5:dstart + 9] == [0, 1, 4, 4]
+
+
+def test_model_proof_layout_omits_deferred():
+    x, layers = d11_model()
+    rc, raw, _, io = O.prove_gkr_chain(x, layers, n_queries=5)
+    assert rc == 0
+    f = felts(raw)
+    assert f[0] == 4 and f[1:11] == GOLD["d11_residual"]["add_record"]
+    assert f[-1] == io
+
+
+def mul_circuit(seed, m=2, d=8, e=4):
+    x = int_matrix_m31(m, d, seed, bound=30)
+    return x, [("linear", int_matrix_m31(d, 2 * d, seed + 1, bound=9)),      # 0: gate branch
+               ("linear", int_matrix_m31(2 * d, 2 * d, seed + 2, bound=9)),  # 1
+               ("relu", None),                                              # 2
+               ("mul", 0),                                                  # 3: lhs = layer 0
+               ("linear", int_matrix_m31(2 * d, e, seed + 3, bound=9))]     # 4
+
+
+def test_mul_circuit_structure():
+    x, layers = mul_circuit(3)
+    rc, raw, _, _ = O.prove_gkr_chain(x, layers, n_queries=4, v1_layout=True)
+    assert rc == 0
+    tail = felts(raw)
+    pd = tail[1:1 + tail[0]]
+    # walk: Linear 4, Mul 3 (skips layer 0), ReLU 2, Linear 1; then one deferred MatMul (layer 0)
+    nv = 1 + 4  # log2(2) + log2(16)
+    assert pd[0] == 0
+    off = 2 + 8 * 4 + 8  # after Linear 4's record (k = 16: 4 rounds)
+    assert pd[off] == 2 and pd[off + 1] == nv
+    rc2, raw2, _, _ = O.prove_gkr_chain(x, layers, n_queries=4)
+    f = felts(raw2)
+    assert f[0] == 4  # four layer records: the skipped layer has none
+    assert tail[1 + tail[0]] == 3  # commitments: Linear 4, Linear 1, deferred Linear 0
+
+
+def test_deferred_branch_must_be_linear():
+    x = int_matrix_m31(2, 8, 5, bound=30)
+    layers = [("linear", int_matrix_m31(8, 8, 6, bound=9)), ("relu", None),
+              ("linear", int_matrix_m31(8, 8, 7, bound=9)), ("mul", 1)]
+    rc, _, _, _ = O.prove_gkr_chain(x, layers, n_queries=4)
+    assert rc == 4
+
+
+def test_bad_dag_rejected():
+    x = int_matrix_m31(2, 8, 5, bound=30)
+    w = int_matrix_m31(8, 4, 6, bound=9)
+    assert O.prove_gkr_chain(x, [("linear", w), ("add", 1)], n_queries=4)[0] == 1  # lhs must be lower
+    assert O.prove_gkr_chain(x, [("linear", w), ("relu", None), ("add", 0, -1)], n_queries=4)[0] == 1  # widths

@@ -818,6 +818,56 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
     return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
 
 
+_DESCRIPTOR_TAGS = {"linear": 0, "add": 1, "mul": 2, "relu": 3, "rmsnorm": 8}
+
+
+def circuit_descriptor(layers) -> List[int]:
+    """build_circuit_descriptor (starknet.rs:1591-1617): [layer count, tag of each layer from
+    the output to the input] with MatMul 0, Add 1, Mul 2, Activation 3, RMSNorm 8."""
+    return [len(layers)] + [_DESCRIPTOR_TAGS[spec[0]] for spec in reversed(layers)]
+
+
+def build_register_gkr_calldata(model_id: int, weight_commitments: Sequence[int], layers) -> List[str]:
+    """build_register_gkr_calldata (starknet.rs:1619-1640): the sncast calldata of
+    register_model_gkr(model_id, weight_commitments, circuit_descriptor)."""
+    desc = circuit_descriptor(layers)
+    return ([f"0x{model_id:x}", str(len(weight_commitments))] + [f"0x{c:x}" for c in weight_commitments]
+            + [str(len(desc))] + [str(t) for t in desc])
+
+
+def verify_calldata_weight_commitments(calldata: Sequence[int]) -> List[int]:
+    """The walk's weight commitments (GKRProof::weight_commitments, without the deferred
+    branches') of a verify_model_gkr calldata built by build_verify_model_gkr_calldata."""
+    i = 2 + calldata[1]
+    n_proofs = calldata[i + 1]
+    i += 2
+    n_dims = calldata[i]
+    i += 1 + n_dims
+    i += 1 + calldata[i]  # dequantize bits
+    pd_len = calldata[i]
+    pd = calldata[i + 1:i + 1 + pd_len]
+    coms = calldata[i + 1 + pd_len:]
+    n_deferred = _deferred_count(pd, n_proofs)
+    return list(coms[1:1 + coms[0] - n_deferred])
+
+
+def _deferred_count(pd: Sequence[int], n_proofs: int) -> int:
+    """The deferred-proof count of a proof_data of Linear / Add / Mul / ReLU records (walks the
+    tagged records; serialize_gkr_proof_data_only)."""
+    j = 0
+    for _ in range(n_proofs):
+        tag = pd[j]
+        if tag == 0:
+            j += 2 + 8 * pd[j + 1] + 8
+        elif tag == 1:
+            j += 10
+        elif tag == 2:
+            j += 2 + 12 * pd[j + 1] + 8
+        else:
+            raise InvalidArgument(1, "only Linear / Add / Mul records can be walked here")
+    return pd[j]
+
+
 def build_verify_model_gkr_calldata(model_id: int, inp, layers, policy_commitment: Optional[int] = None,
                                     n_queries: Optional[int] = None, device: int = 0) -> GKRChainProof:
     """build_verify_model_gkr_calldata (starknet.rs:2837-2852): the proof of the circuit and the

@@ -18,6 +18,11 @@ reference's own known answers for the matmul-sumcheck path:
   the sp3_mlp model with model id 0xd9) -- the whole verify_model_gkr calldata (754 felts).
   The artifact was generated with 5 MLE-opening queries (its opening proofs carry 5) and
   predates the Activation record's trailing piecewise flag (cairo_serde.rs:1881).
+* ``d7_verify_calldata``: engine/tests/artifacts/d7_verify_gkr_calldata.txt, written by
+  e2e_cairo_verify.rs:1294-1370 for the sp3_matmul_only model (model id 0xd7): the whole V1
+  verify_model_gkr calldata (236 felts).
+* ``register_calldata``: the d7 / d9 / d11 register_model_gkr calldata (build_register_gkr_calldata,
+  starknet.rs:1619-1640: model id, the walk's weight commitments, the circuit descriptor).
 * ``d11_residual``: engine/tests/artifacts/d11_verify_gkr_calldata.txt and
   d11_onchain_summary.json, written by e2e_cairo_verify.rs:1549-1660 for
   Linear(identity 4x4) -> fork -> ReLU -> Linear(W2[i][j] = (i+j)%3+1) -> add_from(fork) on the
@@ -89,6 +94,15 @@ out = {
         "model_id": "0xd9",
         "n_queries": 5,
         "calldata": _calldata("d9"),
+    },
+    "d7_verify_calldata": {
+        "source": "engine/tests/artifacts/d7_verify_gkr_calldata.txt",
+        "model_id": "0xd7",
+        "calldata": _calldata("d7"),
+    },
+    "register_calldata": {
+        name: (ref / f"engine/tests/artifacts/{name}_register_gkr_calldata.txt").read_text().split()
+        for name in ("d7", "d9", "d11")
     },
     "d11_residual": {
         "source": "engine/tests/artifacts/d11_verify_gkr_calldata.txt, d11_onchain_summary.json",

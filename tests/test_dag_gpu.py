@@ -70,3 +70,21 @@ def test_gpu_deferred_non_linear_rejected():
               ("linear", int_matrix_m31(8, 8, 7, bound=9)), ("mul", 1)]
     with pytest.raises(Z.InvalidArgument):
         Z.prove_gkr_chain(x, layers, n_queries=4)
+
+
+def test_gpu_verify_calldata_reproduces_d7():
+    g = GOLD["d7_verify_calldata"]
+    x = np.array([[1, 2, 3, 4]], np.uint32)
+    w = np.array([[2 * i + j + 1 for j in range(2)] for i in range(4)], np.uint32)
+    proof = Z.build_verify_model_gkr_calldata(int(g["model_id"], 16), x, [("linear", w)], n_queries=10)
+    assert proof.calldata == [int(h, 16) for h in g["calldata"]]
+
+
+@pytest.mark.parametrize("name", ["d9", "d11"])
+def test_gpu_register_calldata_reproduced(name):
+    """register_model_gkr calldata from the GPU proof's own weight commitments."""
+    ref = GOLD["register_calldata"][name]
+    x, layers = (sp3_model()[:2] if name == "d9" else d11_model())
+    proof = Z.build_verify_model_gkr_calldata(int(ref[0], 16), x, layers, n_queries=5)
+    coms = Z.verify_calldata_weight_commitments(proof.calldata)
+    assert Z.build_register_gkr_calldata(int(ref[0], 16), coms, layers) == ref

@@ -138,3 +138,29 @@ def test_bad_dag_rejected():
     w = int_matrix_m31(8, 4, 6, bound=9)
     assert O.prove_gkr_chain(x, [("linear", w), ("add", 1)], n_queries=4)[0] == 1  # lhs must be lower
     assert O.prove_gkr_chain(x, [("linear", w), ("relu", None), ("add", 0, -1)], n_queries=4)[0] == 1  # widths
+
+
+def test_d7_verify_calldata_reproduced():
+    g = GOLD["d7_verify_calldata"]
+    a = GOLD["sp3_matmul_only"]
+    x = np.array([[1, 2, 3, 4]], np.uint32)
+    w = np.array([[2 * i + j + 1 for j in range(2)] for i in range(4)], np.uint32)
+    rc, raw, _, io = O.prove_gkr_chain(x, [("linear", w)], n_queries=10, v1_layout=True)
+    assert rc == 0
+    mine = v1_envelope(int(g["model_id"], 16), x, np.array([[50, 60]], np.uint32), [("linear", w)], 1) + felts(raw)
+    assert mine == [int(h, 16) for h in g["calldata"]]
+    assert io == int(a["io_commitment"], 16)
+
+
+@pytest.mark.parametrize("name", ["d7", "d9", "d11"])
+def test_register_calldata(name):
+    import zkml_b200 as Z
+    ref = GOLD["register_calldata"][name]
+    if name == "d7":
+        layers = [("linear", None)]
+    elif name == "d9":
+        layers = sp3_model()[1]
+    else:
+        layers = d11_model()[1]
+    coms = [int(c, 16) for c in ref[2:2 + int(ref[1])]]
+    assert Z.build_register_gkr_calldata(int(ref[0], 16), coms, layers) == ref

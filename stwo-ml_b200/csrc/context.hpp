@@ -118,7 +118,6 @@ struct zkml_ctx {
     zk::DevBuf small;               // ticket + out words + error flag
     zk::DevBuf act_tables[6];       // activation lookup tables by type tag (device copies)
     zk::DevBuf rsqrt_table;         // RMSNorm rsqrt table (device copy)
-    zk::DevBuf rc_table;
     zk::LogupScratch lu;
     zk::OpeningScratch op;
     zk::DevBuf gather_dev;          // gathered shards of the sharded product sumcheck

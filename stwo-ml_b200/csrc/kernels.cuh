@@ -23,11 +23,10 @@ void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaS
 // Column restriction of a row-major k x n M31 matrix: acc[i] += sum_j B[i][j] L_j,
 // with L_j = lhi[j >> 6] * llo[j & 63] (llo zero-padded to 64 entries); acc is 4 x u64
 // per row, zeroed by the caller.
-// Tensor-pipe column restriction (see restrict_cols_tc_kernel); needs
-// restrict_cols_tc_ok(B, n) and a 16 * roundup(n, 32)-byte table scratch.
+// Tensor-pipe column restriction (see restrict_cols_tc_kernel); needs restrict_cols_tc_ok(B, n).
 bool restrict_cols_tc_ok(const uint32_t* B, uint32_t n);
 void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
-                             uint8_t* table, unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s);
+                             unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s);
 void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
                           unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s);
 // Row restriction of a row-major m x k M31 matrix: acc[j] += sum_i A[i][j] L_i.

@@ -619,18 +619,16 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
         launch_eq_table(r_j + hi_vars, lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
         ZK_CUDA(cudaMemsetAsync(ctx->acc_b.ptr, 0, k * 32, s));
         const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n);
-        if (tc && (rc = ctx->rc_table.ensure(16 * ((n + 31) / 32 * 32)))) return rc;
         {
             KTimer t(ctx, KC_RESTRICT_COLS);
             if (tc)
                 launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
-                                        ctx->rc_table.as<uint8_t>(), ctx->acc_b.as<unsigned long long>(),
+                                        ctx->acc_b.as<unsigned long long>(),
                                         ctx->err_flag(), ctx->num_sms, s);
             else
                 launch_restrict_cols(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
                                      ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
         }
-        if (tc) ctx->launches++;
         launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
         ctx->launches += 4;
     }
@@ -719,7 +717,6 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
                       &ctx->eq_a, &ctx->eq_hi, &ctx->eq_lo, &ctx->partials, &ctx->small};
     for (DevBuf* b : bufs) b->release();
     for (DevBuf& t : ctx->act_tables) t.release();
-    ctx->rc_table.release();
     ctx->rsqrt_table.release();
     ctx->lu.release();
     ctx->op.release();
@@ -927,19 +924,18 @@ int zkml_restrict_cols_block(zkml_ctx* ctx, const uint32_t* b_block, size_t k, s
     ZK_CUDA(cudaMemsetAsync(acc, 0, k * 32, s));
     const uint4* lhi = ctx->eq_hi.as<uint4>() + (col_offset >> 6);
     const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n_block);
-    if (tc && (rc = ctx->rc_table.ensure(16 * ((n_block + 31) / 32 * 32)))) return rc;
     {
         KTimer t(ctx, KC_RESTRICT_COLS);
         if (tc)
             launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n_block, lhi, ctx->eq_lo.as<uint4>(),
-                                    ctx->rc_table.as<uint8_t>(), acc, ctx->err_flag(), ctx->num_sms, s);
+                                    acc, ctx->err_flag(), ctx->num_sms, s);
         else
             launch_restrict_cols(B, (uint32_t)k, (uint32_t)n_block, lhi, ctx->eq_lo.as<uint4>(), acc, ctx->err_flag(),
                                  ctx->num_sms, s);
     }
     // partial sums to canonical words (so that adding them across ranks cannot overflow)
     launch_canon_u64(acc, 4 * k, s);
-    ctx->launches += tc ? 5 : 4;
+    ctx->launches += 4;
     ZK_CUDA(cudaGetLastError());
     if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "restrict_cols_block"))) return rc;
     return ZKML_OK;

@@ -294,9 +294,10 @@ void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4
 // at most 1024 * 255^2 < 2^31).  A warp takes 16 rows at a time; each 16 x 32
 // tile of B arrives as four 16-byte loads per thread whose byte planes (three
 // PRMTs per plane register) are exactly the A fragments of mma.m16n8k32, with
-// K running over consecutive columns.  The eq side is a 16 x n byte-plane table
-// (row c * 4 + l, built once per call by restrict_table_kernel), staged per
-// block chunk in shared memory.  Per 16 x 32 tile: 8 MMAs (4 byte planes x 2
+// K running over consecutive columns.  The eq side is a 16 x chunk byte-plane
+// table (row c * 4 + l) that each block computes for its chunk straight into
+// shared memory.  Each warp's loads for the next 64 columns are in flight while
+// it runs the MMAs of the current 64 (register double buffering).  Per 16 x 32 tile: 8 MMAs (4 byte planes x 2
 // N-tiles of 8 (c, l) columns), ~1.5 PRMT per element, no 64-bit integer work:
 // the kernel is left with the HBM stream.
 // ---------------------------------------------------------------------------
@@ -304,34 +305,40 @@ constexpr int TC_CH = 1024;                 // columns per block chunk
 constexpr int TC_TROW = TC_CH + 16;         // padded table row (bytes): conflict-free fragment loads
 constexpr int TC_WARPS = 8;
 constexpr int TC_MINB = 2;   // launch-bounds minimum blocks per SM
-constexpr int TC_STEPS = 2;  // 32-column steps loaded per iteration
-
-__global__ void restrict_table_kernel(const uint4* __restrict__ lhi, const uint4* __restrict__ llo, uint32_t n,
-                                      uint32_t npad, uint8_t* __restrict__ T) {
-    for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < npad; j += gridDim.x * blockDim.x) {
-        qm31 L = qzero();
-        if (j < n) L = qmul(ld_q(lhi + (j >> 6)), ld_q(llo + (j & 63)));
-        const uint32_t w[4] = {L.a, L.b, L.c, L.d};
-#pragma unroll
-        for (int c = 0; c < 4; c++)
-#pragma unroll
-            for (int l = 0; l < 4; l++) T[(size_t)(c * 4 + l) * npad + j] = (uint8_t)(w[c] >> (8 * l));
-    }
-}
+constexpr int TC_STEPS = 2;  // 32-column steps loaded per iteration (one iteration ahead of the MMAs)
 
 template <int MINB, int STEPS>
 __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(const uint32_t* __restrict__ B, uint32_t k,
-                                                                         uint32_t n, const uint8_t* __restrict__ T,
-                                                                         uint32_t npad,
+                                                                         uint32_t n, const uint4* __restrict__ lhi,
+                                                                         const uint4* __restrict__ llo, uint32_t npad,
                                                                          unsigned long long* __restrict__ acc_out,
                                                                          uint32_t* __restrict__ err) {
     __shared__ __align__(16) uint8_t tb[16 * TC_TROW];
     const uint32_t c0 = blockIdx.x * TC_CH;
     const uint32_t cw = min((uint32_t)TC_CH, npad - c0);  // chunk width (multiple of 32)
-    for (uint32_t i = threadIdx.x; i < 16 * (cw / 16); i += blockDim.x) {
-        const uint32_t r = i / (cw / 16), q = i % (cw / 16);
-        *reinterpret_cast<uint4*>(tb + r * TC_TROW + 16 * q) =
-            *reinterpret_cast<const uint4*>(T + (size_t)r * npad + c0 + 16 * q);
+    // the chunk's eq byte planes: row c * 4 + l holds byte l of component c of
+    // L_j = lhi[j / 64] * llo[j % 64] (zero past n), four columns per thread and row word
+    for (uint32_t j4 = threadIdx.x; j4 < cw / 4; j4 += blockDim.x) {
+        uint32_t w[4][4];  // [column][component]
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const uint32_t col = c0 + 4 * j4 + u;
+            qm31 L = qzero();
+            if (col < n) L = qmul(ld_q(lhi + (col >> 6)), ld_q(llo + (col & 63)));
+            w[u][0] = L.a;
+            w[u][1] = L.b;
+            w[u][2] = L.c;
+            w[u][3] = L.d;
+        }
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+#pragma unroll
+            for (int l = 0; l < 4; l++) {
+                uint32_t v = 0;
+#pragma unroll
+                for (int u = 0; u < 4; u++) v |= ((w[u][c] >> (8 * l)) & 0xFFu) << (8 * u);
+                *reinterpret_cast<uint32_t*>(tb + (c * 4 + l) * TC_TROW + 4 * j4) = v;
+            }
     }
     __syncthreads();
     const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tg = lane & 3;
@@ -350,9 +357,9 @@ __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(c
             for (int t = 0; t < 2; t++)
 #pragma unroll
                 for (int e = 0; e < 4; e++) acc[b][t][e] = 0;
-        // STEPS 32-column steps per iteration: all their 16-byte loads issue before any MMA
-        for (uint32_t j0 = c0; j0 < c_end; j0 += 32 * STEPS) {
-            uint4 x[STEPS][4];
+        // STEPS 32-column steps per iteration: all their 16-byte loads issue before any MMA,
+        // and the next iteration's loads are issued before this iteration's MMAs
+        auto load = [&](uint4 (&x)[STEPS][4], uint32_t j0) {
 #pragma unroll
             for (int h = 0; h < STEPS; h++) {
                 const uint32_t ja = j0 + 32 * h + 4 * tg, jb = ja + 16;
@@ -362,6 +369,16 @@ __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(c
                 x[h][2] = (v0 && jb < c_end) ? __ldcs(p0 + jb / 4) : z;
                 x[h][3] = (v1 && jb < c_end) ? __ldcs(p1 + jb / 4) : z;
             }
+        };
+        uint4 xn[STEPS][4];
+        load(xn, c0);
+        for (uint32_t j0 = c0; j0 < c_end; j0 += 32 * STEPS) {
+            uint4 x[STEPS][4];
+#pragma unroll
+            for (int h = 0; h < STEPS; h++)
+#pragma unroll
+                for (int f = 0; f < 4; f++) x[h][f] = xn[h][f];
+            load(xn, j0 + 32 * STEPS);  // past c_end: zeros, no loads
 #pragma unroll
             for (int h = 0; h < STEPS; h++) {
                 const uint32_t jj = j0 + 32 * h - c0;
@@ -412,13 +429,8 @@ bool restrict_cols_tc_ok(const uint32_t* B, uint32_t n) {
 }
 
 void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
-                             uint8_t* table, unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s) {
+                             unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s) {
     const uint32_t npad = (n + 31) / 32 * 32;
-    {
-        uint32_t blocks = (npad + 255) / 256;
-        if (blocks > 4096) blocks = 4096;
-        restrict_table_kernel<<<blocks, 256, 0, s>>>(lhi, llo, n, npad, table);
-    }
     const uint32_t chunks = (npad + TC_CH - 1) / TC_CH;
     const uint32_t row_tiles = (k + 15) / 16;
     // one wave of TC_MINB resident 8-warp blocks per SM
@@ -426,7 +438,8 @@ void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const ui
     const uint32_t gy_max = (row_tiles + TC_WARPS - 1) / TC_WARPS;
     if (gy > gy_max) gy = gy_max;
     if (gy == 0) gy = 1;
-    restrict_cols_tc_kernel<TC_MINB, TC_STEPS><<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, table, npad, acc, err);
+    restrict_cols_tc_kernel<TC_MINB, TC_STEPS><<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, lhi, llo,
+                                                                                          npad, acc, err);
 }
 
 // ---------------------------------------------------------------------------

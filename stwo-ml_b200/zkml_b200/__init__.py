@@ -835,37 +835,22 @@ def build_register_gkr_calldata(model_id: int, weight_commitments: Sequence[int]
             + [str(len(desc))] + [str(t) for t in desc])
 
 
-def verify_calldata_weight_commitments(calldata: Sequence[int]) -> List[int]:
+def verify_calldata_weight_commitments(calldata: Sequence[int], layers) -> List[int]:
     """The walk's weight commitments (GKRProof::weight_commitments, without the deferred
-    branches') of a verify_model_gkr calldata built by build_verify_model_gkr_calldata."""
-    i = 2 + calldata[1]
-    n_proofs = calldata[i + 1]
-    i += 2
-    n_dims = calldata[i]
-    i += 1 + n_dims
+    branches') of a verify_model_gkr calldata that build_verify_model_gkr_calldata built for
+    `layers`: one per Linear layer the walk reaches (a Mul layer takes its lower input out of
+    the walk, prover.rs:1740-1750)."""
+    skipped = set()
+    for i, spec in enumerate(layers):
+        if spec[0] == "mul":
+            src = i - 1 if len(spec) < 3 or spec[2] is None or spec[2] == CHAIN_PREV else spec[2]
+            skipped.add(min(int(spec[1]), src))
+    n_walk = sum(1 for i, spec in enumerate(layers) if spec[0] == "linear" and i not in skipped)
+    i = 2 + calldata[1] + 2
+    i += 1 + calldata[i]  # matmul dims
     i += 1 + calldata[i]  # dequantize bits
-    pd_len = calldata[i]
-    pd = calldata[i + 1:i + 1 + pd_len]
-    coms = calldata[i + 1 + pd_len:]
-    n_deferred = _deferred_count(pd, n_proofs)
-    return list(coms[1:1 + coms[0] - n_deferred])
-
-
-def _deferred_count(pd: Sequence[int], n_proofs: int) -> int:
-    """The deferred-proof count of a proof_data of Linear / Add / Mul / ReLU records (walks the
-    tagged records; serialize_gkr_proof_data_only)."""
-    j = 0
-    for _ in range(n_proofs):
-        tag = pd[j]
-        if tag == 0:
-            j += 2 + 8 * pd[j + 1] + 8
-        elif tag == 1:
-            j += 10
-        elif tag == 2:
-            j += 2 + 12 * pd[j + 1] + 8
-        else:
-            raise InvalidArgument(1, "only Linear / Add / Mul records can be walked here")
-    return pd[j]
+    i += 1 + calldata[i]  # proof_data
+    return list(calldata[i + 1:i + 1 + n_walk])
 
 
 def build_verify_model_gkr_calldata(model_id: int, inp, layers, policy_commitment: Optional[int] = None,

@@ -86,5 +86,5 @@ def test_gpu_register_calldata_reproduced(name):
     ref = GOLD["register_calldata"][name]
     x, layers = (sp3_model()[:2] if name == "d9" else d11_model())
     proof = Z.build_verify_model_gkr_calldata(int(ref[0], 16), x, layers, n_queries=5)
-    coms = Z.verify_calldata_weight_commitments(proof.calldata)
+    coms = Z.verify_calldata_weight_commitments(proof.calldata, layers)
     assert Z.build_register_gkr_calldata(int(ref[0], 16), coms, layers) == ref

@@ -164,3 +164,22 @@ def test_register_calldata(name):
         layers = d11_model()[1]
     coms = [int(c, 16) for c in ref[2:2 + int(ref[1])]]
     assert Z.build_register_gkr_calldata(int(ref[0], 16), coms, layers) == ref
+
+
+@pytest.mark.parametrize("name", ["d9", "d11"])
+def test_register_calldata_from_proof_commitments(name):
+    """register_model_gkr calldata from the weight commitments of an oracle-built verify calldata."""
+    import zkml_b200 as Z
+    ref = GOLD["register_calldata"][name]
+    if name == "d9":
+        x, layers, y = sp3_model()
+    else:
+        x, layers = d11_model()
+        y = np.array([[19, 21, 26, 22]], np.uint32)
+    rc, raw, _, _ = O.prove_gkr_chain(x, layers, n_queries=5, v1_layout=True)
+    assert rc == 0
+    tail = felts(raw)
+    n_proofs = 3 if name == "d9" else 4
+    cd = v1_envelope(int(ref[0], 16), x, y, layers, n_proofs) + tail
+    coms = Z.verify_calldata_weight_commitments(cd, layers)
+    assert Z.build_register_gkr_calldata(int(ref[0], 16), coms, layers) == ref

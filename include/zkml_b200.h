@@ -268,13 +268,25 @@ int zkml_reduce_activation_relu(zkml_ctx *ctx, const uint32_t *input, size_t row
                                 zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                                 uint32_t out_input_eval[4], uint32_t *out_point);
 
-/* ---- GKR proof of a layered circuit (Linear / ReLU / RMSNorm / Add / Mul) ------- */
+/* reduce_layernorm_layer (gkr/prover.rs:7944-8354) on a rows x cols M31 input over its
+ * first dim columns: the batched mean / variance plain sumcheck, the eq-sumcheck of
+ * centered x rsqrt with the centered binding, the LogUp of (variance, rsqrt) against the
+ * 2^16 rsqrt table and its multiplicity sumcheck, advancing ch; writes the
+ * LayerProof::LayerNorm record (cairo_serde.rs:1389-1483).  The next claim is the claim
+ * point with value out_input_eval. */
+int zkml_reduce_layernorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, size_t cols, size_t dim,
+                          const uint32_t *claim_point, size_t n_point, const uint32_t claim_value[4],
+                          zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
+                          uint32_t out_input_eval[4]);
+
+/* ---- GKR proof of a layered circuit (Linear / ReLU / RMSNorm / LayerNorm / Add / Mul) */
 
 #define ZKML_LAYER_LINEAR 0
 #define ZKML_LAYER_RELU 1
 #define ZKML_LAYER_RMSNORM 2 /* RMSNorm over the full layer width, no affine scale */
 #define ZKML_LAYER_ADD 3     /* element-wise lhs + rhs (GraphBuilder::add_from) */
 #define ZKML_LAYER_MUL 4     /* element-wise lhs * rhs (GraphBuilder::mul_from) */
+#define ZKML_LAYER_LAYERNORM 5 /* LayerNorm over the full layer width (GraphBuilder::layer_norm) */
 /* zkml_chain_layer.src: the previous layer's output (the model input for layer 0) */
 #define ZKML_CHAIN_PREV (-2)
 /* flags: the Activation record without the multiplicity-sumcheck and piecewise flags, the

@@ -2811,6 +2811,258 @@ static int relu_reduce(const uint32_t *input, size_t rows, size_t cols, const q3
 /* prove_gkr_with_cache (gkr/prover.rs:1500-2251) for a chain GraphBuilder::new((m, k0))
  * .linear(..)/.activation(ReLU).. in Sequential weight-binding mode, serialized by
  * serialize_gkr_model_proof (cairo_serde.rs:1307-1772). */
+/* LayerNorm forward (apply_layernorm_detailed, compiler/prove.rs:977-1060) of one padded row:
+ * mean over the first n_active columns, variance masked to the table, rsqrt from the table;
+ * centered = x - mean and out = centered * rsqrt over every column. */
+static void layernorm_row(const uint32_t *x, size_t pc, size_t n_active, uint32_t inv_n, const uint32_t *table,
+                          uint32_t mask, uint32_t *mean_o, uint32_t *var_o, uint32_t *rs_o) {
+    uint32_t sum = 0;
+    for (size_t j = 0; j < n_active; j++) sum = m_add(sum, x[j]);
+    uint32_t mean = m_mul(sum, inv_n), vs = 0;
+    for (size_t j = 0; j < n_active; j++) {
+        uint32_t d = m_sub(x[j], mean);
+        vs = m_add(vs, m_mul(d, d));
+    }
+    uint32_t var = m_mul(vs, inv_n) & mask;
+    *mean_o = mean;
+    *var_o = var;
+    *rs_o = table[var];
+}
+
+int orc_reduce_layernorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *claim_point,
+                         size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                         size_t cap, size_t *out_len, uint32_t out_input_eval[4]) {
+    oracle_init();
+    if (rows == 0 || cols == 0 || dim == 0) return 1;
+    size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
+    unsigned num_vars = ilog2(n);
+    if (num_vars == 0 || n_point < num_vars) return 1;
+    const q31 *point = (const q31 *)claim_point;
+    const unsigned log_t = 16;
+    const size_t tsize = (size_t)1 << log_t;
+    uint32_t *table = (uint32_t *)malloc(4 * tsize);
+    orc_rsqrt_table(log_t, table);
+    size_t n_active = dim < pc ? dim : pc;
+    uint32_t inv_n = m_inv((uint32_t)(n_active % MP));
+    q31 *in_mle = mle_row_major(input, rows, cols);
+    q31 *mean_v = (q31 *)malloc(sizeof(q31) * n), *var_v = (q31 *)malloc(sizeof(q31) * n);
+    q31 *rs_v = (q31 *)malloc(sizeof(q31) * n), *cen = (q31 *)malloc(sizeof(q31) * n);
+    q31 *outv = (q31 *)malloc(sizeof(q31) * n);
+    uint32_t *row_mean = (uint32_t *)malloc(4 * pr), *row_var = (uint32_t *)malloc(4 * pr);
+    uint32_t *mult = (uint32_t *)calloc(tsize, 4), *xrow = (uint32_t *)malloc(4 * pc);
+    for (size_t i = 0; i < pr; i++) {
+        for (size_t j = 0; j < pc; j++) xrow[j] = in_mle[i * pc + j].a;
+        uint32_t mean, var, rs;
+        layernorm_row(xrow, pc, n_active, inv_n, table, (uint32_t)tsize - 1, &mean, &var, &rs);
+        row_mean[i] = mean;
+        row_var[i] = var;
+        mult[var] += (uint32_t)pc;
+        for (size_t j = 0; j < pc; j++) {
+            size_t idx = i * pc + j;
+            uint32_t c = m_sub(xrow[j], mean);
+            mean_v[idx] = q_from_m(mean);
+            var_v[idx] = q_from_m(var);
+            rs_v[idx] = q_from_m(rs);
+            cen[idx] = q_from_m(c);
+            outv[idx] = q_from_m(m_mul(c, rs));
+        }
+    }
+    free(xrow);
+    q31 input_eval = mle_eval_copy(in_mle, n, point, num_vars);
+    q31 output_eval = mle_eval_copy(outv, n, point, num_vars);
+    q31 mean_eval = mle_eval_copy(mean_v, n, point, num_vars);
+    q31 rsqrt_eval = mle_eval_copy(rs_v, n, point, num_vars);
+    q31 var_eval = mle_eval_copy(var_v, n, point, num_vars);
+    free(outv);
+    /* Part 0: batched mean / variance plain sumcheck (prover.rs:8040-8090) */
+    q31 tot_in = q_from_m(0), tot_c2 = q_from_m(0);
+    for (size_t i = 0; i < n; i++) {
+        tot_in = q_add(tot_in, in_mle[i]);
+        tot_c2 = q_add(tot_c2, q_mul(cen[i], cen[i]));
+    }
+    orc_ch_mix_u64(ch, 0x4D56);
+    orc_ch_mix_u64(ch, n_active);
+    ch_mix_sf(ch, tot_in);
+    ch_mix_sf(ch, tot_c2);
+    q31 eta0 = ch_draw_qm31(ch), eta1 = q_mul(eta0, eta0);
+    q31 *mvp = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    q31 *pin = (q31 *)malloc(sizeof(q31) * n), *pc_ = (q31 *)malloc(sizeof(q31) * n), *pm = (q31 *)malloc(sizeof(q31) * n);
+    memcpy(pin, in_mle, sizeof(q31) * n);
+    memcpy(pc_, cen, sizeof(q31) * n);
+    memcpy(pm, mean_v, sizeof(q31) * n);
+    {
+        uint32_t inv2 = m_inv(2);
+        size_t cur = n;
+        for (unsigned r = 0; r < num_vars; r++) {
+            size_t mid = cur / 2;
+            q31 s[3];
+            for (uint32_t t = 0; t < 3; t++) {
+                q31 acc = q_from_m(0);
+                for (size_t j = 0; j < mid; j++) {
+                    q31 it = q_add(pin[j], q_mul_m(q_sub(pin[mid + j], pin[j]), t));
+                    q31 ct = q_add(pc_[j], q_mul_m(q_sub(pc_[mid + j], pc_[j]), t));
+                    acc = q_add(acc, q_add(q_mul(eta0, it), q_mul(eta1, q_mul(ct, ct))));
+                }
+                s[t] = acc;
+            }
+            q31 dd1 = q_sub(s[1], s[0]);
+            q31 dd2 = q_mul_m(q_sub(q_sub(s[2], s[1]), dd1), inv2);
+            q31 c0 = s[0], c1 = q_sub(dd1, dd2), c2 = dd2, c3 = q_from_m(0);
+            mvp[4 * r] = c0;
+            mvp[4 * r + 1] = c1;
+            mvp[4 * r + 2] = c2;
+            mvp[4 * r + 3] = c3;
+            mix_deg3(ch, c0, c1, c2, c3);
+            q31 x = ch_draw_qm31(ch);
+            fold_vec(pin, mid, x);
+            fold_vec(pc_, mid, x);
+            fold_vec(pm, mid, x);
+            cur = mid;
+        }
+    }
+    q31 mv_in_final = pin[0], mv_mean_final = pm[0];
+    ch_mix_sf(ch, mv_in_final);
+    ch_mix_sf(ch, mv_mean_final);
+    free(pin);
+    free(pc_);
+    free(pm);
+    /* Part 1: eq-sumcheck output = centered x rsqrt, with the centered binding (prover.rs:8092-8170) */
+    orc_ch_mix_u64(ch, 0x4C4E);
+    ch_mix_sf(ch, mean_eval);
+    ch_mix_sf(ch, rsqrt_eval);
+    ch_mix_sf(ch, q_load(claim_value));
+    q31 *eq = lagrange_basis(point, num_vars);
+    q31 *a = (q31 *)malloc(sizeof(q31) * n), *b = (q31 *)malloc(sizeof(q31) * n);
+    memcpy(a, cen, sizeof(q31) * n);
+    memcpy(b, rs_v, sizeof(q31) * n);
+    q31 *lin = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    q31 *chal = (q31 *)malloc(sizeof(q31) * (num_vars + 1));
+    eq_sumcheck_deg3(ch, eq, a, b, n, num_vars, lin, chal);
+    q31 cen_final = a[0], rs_final = b[0];
+    q31 cb_in = mle_eval_copy(in_mle, n, chal, num_vars), cb_mean = mle_eval_copy(mean_v, n, chal, num_vars);
+    ch_mix_sf(ch, cen_final);
+    ch_mix_sf(ch, rs_final);
+    ch_mix_sf(ch, cb_in);
+    ch_mix_sf(ch, cb_mean);
+    free(eq);
+    free(a);
+    free(b);
+    /* Part 2: LogUp of (variance, rsqrt) against the rsqrt table (prover.rs:8172-8300) */
+    orc_ch_mix_u64(ch, 0x4C4F47);
+    orc_ch_mix_u64(ch, 0x5253);
+    q31 gm = ch_draw_qm31(ch), bt = ch_draw_qm31(ch);
+    q31 *d = (q31 *)malloc(sizeof(q31) * n), *w = (q31 *)malloc(sizeof(q31) * n);
+    q31 trace_sum = q_from_m(0);
+    for (size_t i = 0; i < n; i++) {
+        d[i] = q_sub(q_sub(gm, var_v[i]), q_mul(bt, rs_v[i]));
+        w[i] = q_inv(d[i]);
+        trace_sum = q_add(trace_sum, w[i]);
+    }
+    q31 table_sum = q_from_m(0);
+    for (size_t j = 0; j < tsize; j++) {
+        if (!mult[j]) continue;
+        q31 dj = q_sub(q_sub(gm, q_from_m((uint32_t)j)), q_mul(bt, q_from_m(table[j])));
+        table_sum = q_add(table_sum, q_mul_m(q_inv(dj), mult[j] % MP));
+    }
+    int rc = q_eq(trace_sum, table_sum) ? 0 : 3;
+    ch_mix_sf(ch, trace_sum);
+    eq = lagrange_basis(point, num_vars);
+    q31 *lrp = (q31 *)malloc(sizeof(q31) * 4 * (num_vars + 1));
+    eq_sumcheck_deg3(ch, eq, w, d, n, num_vars, lrp, chal);
+    q31 w_eval = w[0];
+    q31 var_s = mle_eval_copy(var_v, n, chal, num_vars), rs_s = mle_eval_copy(rs_v, n, chal, num_vars);
+    q31 *mrp = (q31 *)malloc(sizeof(q31) * 2 * log_t), m_final, m_claim;
+    mult_sumcheck(ch, mult, log_t, mrp, &m_final, &m_claim);
+    fe tcom;
+    table_commitment(0x5253, log_t, &tcom);
+    ch_mix_sf(ch, input_eval);
+    ch_mix_sf(ch, output_eval);
+    /* LayerProof::LayerNorm as serialize_gkr_model_proof writes it (cairo_serde.rs:1389-1483) */
+    felt_out o = {calldata, 0, cap, 0};
+    out_u64(&o, 4);
+    out_qm31(&o, input_eval);
+    out_qm31(&o, output_eval);
+    out_qm31(&o, mean_eval);
+    out_qm31(&o, rsqrt_eval);
+    out_push(&o, &tcom);
+    out_u64(&o, 0); /* not SIMD-combined */
+    out_u64(&o, 1); /* mean / variance sumcheck present */
+    out_u64(&o, n_active);
+    out_qm31(&o, tot_in);
+    out_qm31(&o, tot_c2);
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, mvp[4 * r]);
+        out_qm31(&o, mvp[4 * r + 2]);
+        out_qm31(&o, mvp[4 * r + 3]);
+    }
+    out_qm31(&o, mv_in_final);
+    out_qm31(&o, mv_mean_final);
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, lin[4 * r]);
+        out_qm31(&o, lin[4 * r + 2]);
+        out_qm31(&o, lin[4 * r + 3]);
+    }
+    out_qm31(&o, cen_final);
+    out_qm31(&o, rs_final);
+    out_qm31(&o, cb_in);
+    out_qm31(&o, cb_mean);
+    out_u64(&o, 1); /* LogUp proof present, with its multiplicities */
+    out_qm31(&o, trace_sum);
+    out_u64(&o, num_vars);
+    for (unsigned r = 0; r < num_vars; r++) {
+        out_qm31(&o, lrp[4 * r]);
+        out_qm31(&o, lrp[4 * r + 2]);
+        out_qm31(&o, lrp[4 * r + 3]);
+    }
+    out_qm31(&o, w_eval);
+    out_qm31(&o, var_s);
+    out_qm31(&o, rs_s);
+    out_u64(&o, tsize);
+    for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
+    out_u64(&o, 1); /* multiplicity sumcheck (serialize_multiplicity_sumcheck, cairo_serde.rs:1138-1156) */
+    out_u64(&o, log_t);
+    for (unsigned r = 0; r < log_t; r++) {
+        out_qm31(&o, mrp[2 * r]);
+        out_qm31(&o, mrp[2 * r + 1]);
+    }
+    out_qm31(&o, m_final);
+    out_qm31(&o, m_claim);
+    out_qm31(&o, var_eval);
+    for (int pass = 0; pass < 2; pass++) {
+        const uint32_t *rv = pass ? row_var : row_mean;
+        if (pr > 1) {
+            out_u64(&o, 1);
+            out_u64(&o, pr);
+            for (size_t i = 0; i < pr; i++) out_u64(&o, rv[i]);
+        } else {
+            out_u64(&o, 0);
+        }
+    }
+    *out_len = o.len;
+    if (out_input_eval) q_store(out_input_eval, input_eval);
+    free(mrp);
+    free(lrp);
+    free(eq);
+    free(d);
+    free(w);
+    free(chal);
+    free(lin);
+    free(mvp);
+    free(in_mle);
+    free(mean_v);
+    free(var_v);
+    free(rs_v);
+    free(cen);
+    free(row_mean);
+    free(row_var);
+    free(mult);
+    free(table);
+    if (rc) return rc;
+    return o.overflow ? 2 : 0;
+}
+
 typedef struct {
     q31 point[64];
     unsigned npt;
@@ -2852,7 +3104,7 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
                 rc = 1;
                 break;
             }
-        } else if (layers[l].type != 1 && layers[l].type != 2) {
+        } else if (layers[l].type != 1 && layers[l].type != 2 && layers[l].type != 5) {
             rc = 1;
             break;
         }
@@ -2874,6 +3126,17 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
                 for (size_t j = 0; j < w; j++) sq = m_add(sq, m_mul(x[i * w + j], x[i * w + j]));
                 uint32_t rs = tab[m_mul(sq, inv_n) & 0xFFFF];
                 for (size_t j = 0; j < w; j++) y[i * w + j] = m_mul(x[i * w + j], rs);
+            }
+            free(tab);
+        } else if (layers[l].type == 5) {
+            /* apply_layernorm_detailed (compiler/prove.rs:977-1060), dim = the layer width */
+            uint32_t *tab = (uint32_t *)malloc(4u << 16);
+            orc_rsqrt_table(16, tab);
+            uint32_t inv_n = m_inv((uint32_t)(w % MP));
+            for (size_t i = 0; i < m; i++) {
+                uint32_t mean, var, rs;
+                layernorm_row(x + i * w, w, w, inv_n, tab, 0xFFFF, &mean, &var, &rs);
+                for (size_t j = 0; j < w; j++) y[i * w + j] = m_mul(m_sub(x[i * w + j], mean), rs);
             }
             free(tab);
         } else {
@@ -2963,6 +3226,19 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             q_store(cv, value);
             rc = orc_reduce_rmsnorm(x, m, w, w, NULL, 0, 0, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen,
                                     ie);
+            for (size_t i = 0; i < tlen && !rc; i++) {
+                fe f;
+                fe_from_canon(&f, tbuf + 4 * i);
+                out_push(&lay, &f);
+            }
+            free(tbuf);
+            value = q_load(ie);
+        } else if (layers[li].type == 5) {
+            size_t tcap = (1 << 16) + 400 + 2 * next_pow2(m) + 60 * (npt + 2), tlen = 0;
+            uint64_t *tbuf = (uint64_t *)malloc(32 * tcap);
+            uint32_t cv[4], ie[4];
+            q_store(cv, value);
+            rc = orc_reduce_layernorm(x, m, w, w, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen, ie);
             for (size_t i = 0; i < tlen && !rc; i++) {
                 fe f;
                 fe_from_canon(&f, tbuf + 4 * i);

@@ -194,10 +194,19 @@ int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const 
                                     size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
                                     uint32_t out_input_eval[4]);
 
+/* reduce_layernorm_layer (gkr/prover.rs:7944-8354): the batched mean / variance plain
+ * sumcheck, the eq-sumcheck of centered x rsqrt with the centered binding, the LogUp of
+ * (variance, rsqrt) against the 2^16 rsqrt table and its multiplicity sumcheck; serialized as
+ * LayerProof::LayerNorm (cairo_serde.rs:1389-1483).  The next claim is (point, input eval). */
+int orc_reduce_layernorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *claim_point,
+                         size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                         size_t cap, size_t *out_len, uint32_t out_input_eval[4]);
+
 /* One layer of a GKR circuit (LayeredCircuit::from_graph, gkr/circuit.rs:140-225, for the
  * GraphBuilder ops linear / activation(ReLU) / rms_norm / add_from / mul_from):
  * type 0 = Linear (weight: rows = the layer's input width, n columns, row major), 1 = ReLU,
- * 2 = RMSNorm over the full width, 3 = Add, 4 = Mul (element-wise, M31).
+ * 2 = RMSNorm over the full width, 3 = Add, 4 = Mul (element-wise, M31), 5 = LayerNorm over
+ * the full width.
  * src: the layer whose output is this layer's input (for Add / Mul the rhs operand);
  * ORC_CHAIN_PREV = the previous layer (the model input for layer 0), -1 = the model input.
  * lhs: Add / Mul only, the layer whose output is the lhs operand (the saved fork). */

@@ -86,8 +86,9 @@ namespace zk {
 struct LogupScratch {
     DevBuf x, m_in, m_out, mult, eq, d, w, mv;
     DevBuf outv, row_rms, pv, gam;  // RMSNorm: output, per-row rms^2, plain-sumcheck vector, affine scale
+    DevBuf cen, meanv, row_var;     // LayerNorm: centered input, per-element mean, per-row variance
     void release() {
-        DevBuf* all[] = {&x, &m_in, &m_out, &mult, &eq, &d, &w, &mv, &outv, &row_rms, &pv, &gam};
+        DevBuf* all[] = {&x, &m_in, &m_out, &mult, &eq, &d, &w, &mv, &outv, &row_rms, &pv, &gam, &cen, &meanv, &row_var};
         for (DevBuf* b : all) b->release();
     }
 };

@@ -139,7 +139,7 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
             if (!layers[l].weight || layers[l].n == 0 || layers[l].n > (1u << 30))
                 return set_error(ZKML_ERR_INVALID_ARG, at + "bad Linear layer");
             width[l + 1] = layers[l].n;
-        } else if (t == ZKML_LAYER_RELU || t == ZKML_LAYER_RMSNORM) {
+        } else if (t == ZKML_LAYER_RELU || t == ZKML_LAYER_RMSNORM || t == ZKML_LAYER_LAYERNORM) {
             width[l + 1] = w;
         } else if (t == ZKML_LAYER_ADD || t == ZKML_LAYER_MUL) {
             if (layers[l].lhs < 0 || layers[l].lhs >= (long long)l || width[layers[l].lhs + 1] != w)
@@ -180,6 +180,14 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
             rmsnorm_forward_kernel<<<(unsigned)std::min<size_t>(m, 8192), 256, 0, s>>>(
                 in_of(l), (uint32_t)m, (uint32_t)w, minv((uint32_t)(w % P)), ctx->rsqrt_table.as<uint32_t>(),
                 outs[l + 1].as<uint32_t>());
+            ctx->launches++;
+        } else if (t == ZKML_LAYER_LAYERNORM) {
+            if (!ctx->rsqrt_table.ptr) {
+                if ((rc = ctx->rsqrt_table.ensure(4u << 16))) return rc;
+                ZK_CUDA(cudaMemcpy(ctx->rsqrt_table.ptr, rsqrt_table16().data(), 4u << 16, cudaMemcpyHostToDevice));
+            }
+            launch_layernorm_forward(in_of(l), (uint32_t)m, (uint32_t)w, minv((uint32_t)(w % P)),
+                                     ctx->rsqrt_table.as<uint32_t>(), outs[l + 1].as<uint32_t>(), s);
             ctx->launches++;
         } else if (t == ZKML_LAYER_RELU) {
             relu_forward_kernel<<<blocks_for(m * w), 256, 0, s>>>(in_of(l), m * w, outs[l + 1].as<uint32_t>());
@@ -277,6 +285,12 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
             uint32_t cv[4] = {value.a, value.b, value.c, value.d}, ie[4];
             if ((rc = rmsnorm_reduce_dev(ctx, in_of(li), m, w, w, nullptr, 0,
                                          reinterpret_cast<const uint32_t*>(point.data()), npt, cv, &chs, lay, ie)))
+                return rc;
+            value = qm(ie[0], ie[1], ie[2], ie[3]);  // the point is unchanged
+        } else if (t == ZKML_LAYER_LAYERNORM) {
+            uint32_t cv[4] = {value.a, value.b, value.c, value.d}, ie[4];
+            if ((rc = layernorm_reduce_dev(ctx, in_of(li), m, w, w, reinterpret_cast<const uint32_t*>(point.data()),
+                                           npt, cv, &chs, lay, ie)))
                 return rc;
             value = qm(ie[0], ie[1], ie[2], ie[3]);  // the point is unchanged
         } else if (t == ZKML_LAYER_RELU) {

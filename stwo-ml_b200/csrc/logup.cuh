@@ -53,4 +53,24 @@ void launch_rmsnorm_prepare(const uint32_t* input, uint32_t rows, uint32_t cols,
 void launch_sq_round(const uint32_t* src32, uint4* V, size_t len, bool first, bool fold, qm31 alpha,
                      const ReduceScratch& rs, cudaStream_t s);
 
+// LayerNorm (layernorm_kernels.cu).  Per padded row: mean, variance masked to the table,
+// rsqrt, the multiplicity histogram (pc per row), row_mean / row_var; per element: x,
+// centered, mean, variance, rsqrt (M31) and the output centered * rsqrt.
+void launch_layernorm_prepare(const uint32_t* input, uint32_t rows, uint32_t cols, uint32_t pr, uint32_t pc,
+                              uint32_t n_active, uint32_t inv_n, const uint32_t* table, uint32_t mask,
+                              uint32_t* x_out, uint32_t* cen, uint32_t* mean_v, uint32_t* var_v, uint32_t* rs_v,
+                              uint32_t* outv, uint32_t* row_mean, uint32_t* row_var, uint32_t* mult, uint32_t* err,
+                              int max_blocks, cudaStream_t s);
+// Batched mean / variance round: s(0..2) of sum eta0 in + eta1 c^2 (12 words); len is the
+// current length before the optional fold of the input, centered and mean vectors.
+void launch_mv_round(const uint32_t* x32, const uint32_t* c32, const uint32_t* m32, uint4* IN, uint4* C, uint4* M,
+                     size_t len, bool first, bool fold, qm31 alpha, qm31 eta0, qm31 eta1, const ReduceScratch& rs,
+                     cudaStream_t s);
+// Last fold of the length-2 input and mean vectors (M31 sources when non-null): 8 words.
+void launch_mv_final(const uint32_t* x32, const uint32_t* m32, const uint4* IN, const uint4* M, qm31 alpha,
+                     const ReduceScratch& rs, cudaStream_t s);
+void launch_lift2(const uint32_t* a, const uint32_t* b, size_t n, uint4* W, uint4* D, cudaStream_t s);
+void launch_layernorm_forward(const uint32_t* x, uint32_t rows, uint32_t cols, uint32_t inv_n, const uint32_t* table,
+                              uint32_t* y, cudaStream_t s);
+
 }  // namespace zk

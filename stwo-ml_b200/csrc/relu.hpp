@@ -21,4 +21,11 @@ int rmsnorm_reduce_dev(::zkml_ctx* ctx, const uint32_t* input, size_t rows, size
                        const uint32_t* gamma, size_t gamma_len, const uint32_t* claim_point, size_t n_point,
                        const uint32_t claim_value[4], zkml_channel* chs, Out& o, uint32_t out_input_eval[4]);
 
+// reduce_layernorm_layer (gkr/prover.rs:7944-8354) on the rows x cols input; appends the
+// LayerProof::LayerNorm record to `o` (layernorm_api.cu).  The next claim keeps the point;
+// its value is written to out_input_eval.
+int layernorm_reduce_dev(::zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
+                         const uint32_t* claim_point, size_t n_point, const uint32_t claim_value[4],
+                         zkml_channel* chs, Out& o, uint32_t out_input_eval[4]);
+
 }  // namespace zk

@@ -107,6 +107,9 @@ _SIGS = {
     "zkml_reduce_rmsnorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
                                       C.c_size_t, C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                       C.c_size_t, C.POINTER(C.c_size_t), _u32]),
+    "zkml_reduce_layernorm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
+                                        C.c_size_t, _u32, C.POINTER(_Channel), _u64, C.c_size_t,
+                                        C.POINTER(C.c_size_t), _u32]),
     "zkml_reduce_activation_piecewise": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_int,
                                                    C.c_void_p, C.c_size_t, _u32, C.POINTER(_Channel), _u64,
                                                    C.c_size_t, C.POINTER(C.c_size_t), _u32, _u32]),
@@ -739,7 +742,7 @@ class _ChainLayer(C.Structure):
 
 
 CHAIN_PREV = -2
-_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4}
+_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layernorm": 5}
 
 
 @dataclass
@@ -755,7 +758,7 @@ class GKRChainProof:
 
 def _chain_args(inp, layers, n_queries):
     """ctypes layer array, buffers to keep alive and a calldata capacity for `layers`, each
-    (kind, arg[, src]): ("linear", weight (in_width, n)), ("relu", None), ("rmsnorm", None),
+    (kind, arg[, src]): ("linear", weight (in_width, n)), ("relu", None), ("rmsnorm", None), ("layernorm", None),
     ("add", lhs_layer), ("mul", lhs_layer); src = the layer feeding this one (None: the
     previous layer, -1: the model input).  The Add / Mul rhs operand is src's output."""
     im = as_matrix(inp)
@@ -790,10 +793,10 @@ def _chain_args(inp, layers, n_queries):
         widths.append(width)
     nq = mle_n_queries() if n_queries is None else n_queries
     nv_all = _log2(_next_pow2(im.rows)) + max(nv_max, max(_log2(_next_pow2(w)) for w in widths) + 1)
-    n_norm = sum(1 for spec in layers if spec[0] == "rmsnorm")
+    n_norm = sum(1 for spec in layers if spec[0] in ("rmsnorm", "layernorm"))
     per_open = 64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1)))
     cap = 256 + len(layers) * (200 + 12 * nv_all) + (n_lin + n_bin) * per_open + n_bin * (60 + 16 * nv_all)
-    cap += n_norm * ((1 << 16) + _next_pow2(im.rows) + 40 * (nv_all + 2))
+    cap += n_norm * ((1 << 16) + 2 * _next_pow2(im.rows) + 200 + 60 * (nv_all + 2))
     cap += 2 * im.rows * max(widths)
     return im, ib, arr, keep, nq, cap
 
@@ -818,12 +821,12 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
     return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
 
 
-_DESCRIPTOR_TAGS = {"linear": 0, "add": 1, "mul": 2, "relu": 3, "rmsnorm": 8}
+_DESCRIPTOR_TAGS = {"linear": 0, "add": 1, "mul": 2, "relu": 3, "layernorm": 4, "rmsnorm": 8}
 
 
 def circuit_descriptor(layers) -> List[int]:
     """build_circuit_descriptor (starknet.rs:1591-1617): [layer count, tag of each layer from
-    the output to the input] with MatMul 0, Add 1, Mul 2, Activation 3, RMSNorm 8."""
+    the output to the input] with MatMul 0, Add 1, Mul 2, Activation 3, LayerNorm 4, RMSNorm 8."""
     return [len(layers)] + [_DESCRIPTOR_TAGS[spec[0]] for spec in reversed(layers)]
 
 
@@ -904,6 +907,26 @@ def reduce_rmsnorm_layer(output_claim: GKRClaim, inp: M31Matrix, dim: int, chann
                                      None if gbuf is None else gbuf.ptr, 0 if gbuf is None else gbuf.nbytes // 4,
                                      pt_ptr, n_point, np.ascontiguousarray(output_claim.value, np.uint32),
                                      C.byref(channel.state), out, cap, C.byref(ln), ie))
+    raw = out[:4 * ln.value]
+    oe = np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)
+    return RMSNormProof(raw, ie, oe), GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())
+
+
+def reduce_layernorm_layer(output_claim: GKRClaim, inp: M31Matrix, dim: int, channel: PoseidonChannel,
+                           device: int = 0) -> Tuple[RMSNormProof, GKRClaim]:
+    """gkr/prover.rs:7944-8354 (reduce_layernorm_layer): the LayerProof::LayerNorm record and
+    the next claim (same point, the input's evaluation)."""
+    buf = _Buf(inp.data)
+    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
+    n_point = len(as_qm31_array(output_claim.point))
+    pr = 1 << max(0, (inp.rows - 1).bit_length())
+    cap = (1 << 16) + 2 * pr + 200 + 60 * (n_point + 2)
+    out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    _check(lib().zkml_reduce_layernorm(context(device).handle, buf.ptr, inp.rows, inp.cols, dim, pt_ptr, n_point,
+                                       np.ascontiguousarray(output_claim.value, np.uint32), C.byref(channel.state),
+                                       out, cap, C.byref(ln), ie))
     raw = out[:4 * ln.value]
     oe = np.array([raw[4 * (5 + i)] for i in range(4)], np.uint32)
     return RMSNormProof(raw, ie, oe), GKRClaim(as_qm31_array(output_claim.point).copy(), ie.copy())

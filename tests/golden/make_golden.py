@@ -23,6 +23,9 @@ reference's own known answers for the matmul-sumcheck path:
   verify_model_gkr calldata (236 felts).
 * ``register_calldata``: the d7 / d9 / d11 register_model_gkr calldata (build_register_gkr_calldata,
   starknet.rs:1619-1640: model id, the walk's weight commitments, the circuit descriptor).
+* ``d10_weight_commitments``: d10_onchain_summary.json (Linear(identity) -> LayerNorm ->
+  Linear(4->2) on [[7,9,11,13],[17,19,21,23]], e2e_cairo_verify.rs:312-352); the rest of the
+  d10 artifacts predate the current rsqrt table, so only the weight commitments are pinned.
 * ``d11_residual``: engine/tests/artifacts/d11_verify_gkr_calldata.txt and
   d11_onchain_summary.json, written by e2e_cairo_verify.rs:1549-1660 for
   Linear(identity 4x4) -> fork -> ReLU -> Linear(W2[i][j] = (i+j)%3+1) -> add_from(fork) on the
@@ -104,6 +107,8 @@ out = {
         name: (ref / f"engine/tests/artifacts/{name}_register_gkr_calldata.txt").read_text().split()
         for name in ("d7", "d9", "d11")
     },
+    "d10_weight_commitments": json.loads(
+        (ref / "engine/tests/artifacts/d10_onchain_summary.json").read_text())["weight_commitments"],
     "d11_residual": {
         "source": "engine/tests/artifacts/d11_verify_gkr_calldata.txt, d11_onchain_summary.json",
         "model_id": "0xdb",

@@ -98,6 +98,7 @@ def lib():
         L.orc_reduce_rmsnorm.argtypes = [u32p, sz, sz, sz, C.c_void_p, sz, C.c_int, u32p, sz, u32p, chp, u64p,
                                          sz, C.POINTER(sz), u32p]
         L.orc_verify_rmsnorm.argtypes = [u64p, sz, sz, u32p, sz, u32p, chp, u32p]
+        L.orc_reduce_layernorm.argtypes = [u32p, sz, sz, sz, u32p, sz, u32p, chp, u64p, sz, C.POINTER(sz), u32p]
         _lib = L
     return _lib
 
@@ -238,6 +239,18 @@ def reduce_rmsnorm(inp, dim, point, value, ch, gamma=None, skip_rms_sq=False, ca
     return rc, buf[:4 * ln.value].copy(), ie
 
 
+def reduce_layernorm(inp, dim, point, value, ch, cap=1 << 18):
+    inp = np.ascontiguousarray(inp, np.uint32)
+    rows, cols = inp.shape
+    point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
+    buf = np.zeros(4 * cap, np.uint64)
+    ln = C.c_size_t(0)
+    ie = np.zeros(4, np.uint32)
+    rc = lib().orc_reduce_layernorm(inp.reshape(-1), rows, cols, dim, point.reshape(-1), len(point),
+                                    np.ascontiguousarray(value, np.uint32), C.byref(ch), buf, cap, C.byref(ln), ie)
+    return rc, buf[:4 * ln.value].copy(), ie
+
+
 def verify_rmsnorm(raw, dim, point, value, ch):
     point = np.ascontiguousarray(point, np.uint32).reshape(-1, 4)
     ie = np.zeros(4, np.uint32)
@@ -354,12 +367,12 @@ class ChainLayer(C.Structure):
 
 
 CHAIN_PREV = -2
-_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4}
+_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layernorm": 5}
 
 
 def chain_layers(layers):
     """ctypes array for layers given as (kind, arg[, src]): ("linear", weight (rows, n)),
-    ("relu", None), ("rmsnorm", None), ("add", lhs layer), ("mul", lhs layer); src is the
+    ("relu", None), ("rmsnorm", None), ("layernorm", None), ("add", lhs layer), ("mul", lhs layer); src is the
     layer feeding this one (None = the previous layer, -1 = the model input)."""
     keep = []
     arr = (ChainLayer * len(layers))()

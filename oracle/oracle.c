@@ -1874,10 +1874,24 @@ static q31 mle_eval_copy(const q31 *v, size_t n, const q31 *point, unsigned num_
     return r;
 }
 
-int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *gamma_aff,
-                       size_t gamma_len, int skip_rms_sq, const uint32_t *claim_point, size_t n_point,
-                       const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata, size_t cap,
-                       size_t *out_len, uint32_t out_input_eval[4]) {
+/* serialize_multiplicity_sumcheck (cairo_serde.rs:1138-1156) of a present proof. */
+static void out_mult_sumcheck(felt_out *o, const q31 *mrp, unsigned log_t, q31 m_final, q31 m_claim) {
+    out_u64(o, 1);
+    out_u64(o, log_t);
+    for (unsigned r = 0; r < log_t; r++) {
+        out_qm31(o, mrp[2 * r]);
+        out_qm31(o, mrp[2 * r + 1]);
+    }
+    out_qm31(o, m_final);
+    out_qm31(o, m_claim);
+}
+
+/* v1: the record as serialize_gkr_proof_data_only writes it (cairo_serde.rs:2145-2222): the
+ * LogUp proof without multiplicities, then the multiplicity sumcheck. */
+static int rmsnorm_impl(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *gamma_aff,
+                        size_t gamma_len, int skip_rms_sq, const uint32_t *claim_point, size_t n_point,
+                        const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata, size_t cap,
+                        size_t *out_len, uint32_t out_input_eval[4], int v1) {
     oracle_init();
     if (rows == 0 || cols == 0 || dim == 0 || (gamma_aff && gamma_len == 0)) return 1;
     size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
@@ -2002,7 +2016,8 @@ int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t d
     restrict_inplace(rsq, n, chal, num_vars, 1);
     restrict_inplace(rsq_raw, n, chal, num_vars, 1);
     q31 rms_s = rsq[0], rsqrt_s = rsq_raw[0];
-    mult_sumcheck(ch, mult, log_t, NULL, NULL, NULL);
+    q31 *mrp = (q31 *)malloc(sizeof(q31) * 2 * log_t), m_final, m_claim;
+    mult_sumcheck(ch, mult, log_t, mrp, &m_final, &m_claim);
     fe tcom;
     table_commitment(0x5253, log_t, &tcom);
     ch_mix_sf(ch, input_eval);
@@ -2049,8 +2064,14 @@ int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t d
     out_qm31(&o, w_eval);
     out_qm31(&o, rms_s);
     out_qm31(&o, rsqrt_s);
-    out_u64(&o, tsize);
-    for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
+    if (v1) {
+        out_u64(&o, 0); /* no multiplicities on chain */
+        out_mult_sumcheck(&o, mrp, log_t, m_final, m_claim);
+    } else {
+        out_u64(&o, tsize);
+        for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
+    }
+    free(mrp);
     if (pr > 1) {
         out_u64(&o, 1);
         out_u64(&o, pr);
@@ -2074,6 +2095,14 @@ int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t d
     free(table);
     if (rc) return rc;
     return o.overflow ? 2 : 0;
+}
+
+int orc_reduce_rmsnorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *gamma_aff,
+                       size_t gamma_len, int skip_rms_sq, const uint32_t *claim_point, size_t n_point,
+                       const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata, size_t cap,
+                       size_t *out_len, uint32_t out_input_eval[4]) {
+    return rmsnorm_impl(input, rows, cols, dim, gamma_aff, gamma_len, skip_rms_sq, claim_point, n_point, claim_value,
+                        ch, calldata, cap, out_len, out_input_eval, 0);
 }
 
 /* Replays a compressed deg-3 sumcheck: c1 = cur - 2 c0 - c2 - c3; returns the final sum. */
@@ -2829,9 +2858,11 @@ static void layernorm_row(const uint32_t *x, size_t pc, size_t n_active, uint32_
     *rs_o = table[var];
 }
 
-int orc_reduce_layernorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *claim_point,
-                         size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
-                         size_t cap, size_t *out_len, uint32_t out_input_eval[4]) {
+/* v1: the record as serialize_gkr_proof_data_only writes it (cairo_serde.rs:1886-1985): the
+ * LogUp proof without multiplicities. */
+static int layernorm_impl(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *claim_point,
+                          size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                          size_t cap, size_t *out_len, uint32_t out_input_eval[4], int v1) {
     oracle_init();
     if (rows == 0 || cols == 0 || dim == 0) return 1;
     size_t pr = next_pow2(rows), pc = next_pow2(cols), n = pr * pc;
@@ -3019,16 +3050,13 @@ int orc_reduce_layernorm(const uint32_t *input, size_t rows, size_t cols, size_t
     out_qm31(&o, w_eval);
     out_qm31(&o, var_s);
     out_qm31(&o, rs_s);
-    out_u64(&o, tsize);
-    for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
-    out_u64(&o, 1); /* multiplicity sumcheck (serialize_multiplicity_sumcheck, cairo_serde.rs:1138-1156) */
-    out_u64(&o, log_t);
-    for (unsigned r = 0; r < log_t; r++) {
-        out_qm31(&o, mrp[2 * r]);
-        out_qm31(&o, mrp[2 * r + 1]);
+    if (v1) {
+        out_u64(&o, 0); /* no multiplicities on chain */
+    } else {
+        out_u64(&o, tsize);
+        for (size_t j = 0; j < tsize; j++) out_u64(&o, mult[j]);
     }
-    out_qm31(&o, m_final);
-    out_qm31(&o, m_claim);
+    out_mult_sumcheck(&o, mrp, log_t, m_final, m_claim);
     out_qm31(&o, var_eval);
     for (int pass = 0; pass < 2; pass++) {
         const uint32_t *rv = pass ? row_var : row_mean;
@@ -3061,6 +3089,13 @@ int orc_reduce_layernorm(const uint32_t *input, size_t rows, size_t cols, size_t
     free(table);
     if (rc) return rc;
     return o.overflow ? 2 : 0;
+}
+
+int orc_reduce_layernorm(const uint32_t *input, size_t rows, size_t cols, size_t dim, const uint32_t *claim_point,
+                         size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint64_t *calldata,
+                         size_t cap, size_t *out_len, uint32_t out_input_eval[4]) {
+    return layernorm_impl(input, rows, cols, dim, claim_point, n_point, claim_value, ch, calldata, cap, out_len,
+                          out_input_eval, 0);
 }
 
 typedef struct {
@@ -3224,8 +3259,8 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             uint64_t *tbuf = (uint64_t *)malloc(32 * tcap);
             uint32_t cv[4], ie[4];
             q_store(cv, value);
-            rc = orc_reduce_rmsnorm(x, m, w, w, NULL, 0, 0, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen,
-                                    ie);
+            rc = rmsnorm_impl(x, m, w, w, NULL, 0, 0, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen, ie,
+                              v1);
             for (size_t i = 0; i < tlen && !rc; i++) {
                 fe f;
                 fe_from_canon(&f, tbuf + 4 * i);
@@ -3238,7 +3273,7 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             uint64_t *tbuf = (uint64_t *)malloc(32 * tcap);
             uint32_t cv[4], ie[4];
             q_store(cv, value);
-            rc = orc_reduce_layernorm(x, m, w, w, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen, ie);
+            rc = layernorm_impl(x, m, w, w, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap, &tlen, ie, v1);
             for (size_t i = 0; i < tlen && !rc; i++) {
                 fe f;
                 fe_from_canon(&f, tbuf + 4 * i);

@@ -284,13 +284,13 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
         } else if (t == ZKML_LAYER_RMSNORM) {
             uint32_t cv[4] = {value.a, value.b, value.c, value.d}, ie[4];
             if ((rc = rmsnorm_reduce_dev(ctx, in_of(li), m, w, w, nullptr, 0,
-                                         reinterpret_cast<const uint32_t*>(point.data()), npt, cv, &chs, lay, ie)))
+                                         reinterpret_cast<const uint32_t*>(point.data()), npt, cv, &chs, lay, ie, v1)))
                 return rc;
             value = qm(ie[0], ie[1], ie[2], ie[3]);  // the point is unchanged
         } else if (t == ZKML_LAYER_LAYERNORM) {
             uint32_t cv[4] = {value.a, value.b, value.c, value.d}, ie[4];
             if ((rc = layernorm_reduce_dev(ctx, in_of(li), m, w, w, reinterpret_cast<const uint32_t*>(point.data()),
-                                           npt, cv, &chs, lay, ie)))
+                                           npt, cv, &chs, lay, ie, v1)))
                 return rc;
             value = qm(ie[0], ie[1], ie[2], ie[3]);  // the point is unchanged
         } else if (t == ZKML_LAYER_RELU) {

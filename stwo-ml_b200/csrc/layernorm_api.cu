@@ -46,7 +46,7 @@ using namespace zk;
 
 int zk::layernorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
                              const uint32_t* claim_point, size_t n_point, const uint32_t claim_value[4],
-                             zkml_channel* chs, Out& o, uint32_t out_input_eval[4]) {
+                             zkml_channel* chs, Out& o, uint32_t out_input_eval[4], bool v1_record) {
     if (!ctx || !input || !claim_value || !chs) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (rows == 0 || cols == 0 || dim == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty LayerNorm input or dim 0");
     const size_t pr = np2(rows), pc = np2(cols), n = pr * pc;
@@ -324,8 +324,12 @@ int zk::layernorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, 
     o.q(w_eval);
     o.q(var_s);
     o.q(rs_s);
-    o.u64(tsize);
-    for (size_t j = 0; j < tsize; j++) o.u64(mult[j]);
+    if (v1_record) {
+        o.u64(0);  // no multiplicities on chain
+    } else {
+        o.u64(tsize);
+        for (size_t j = 0; j < tsize; j++) o.u64(mult[j]);
+    }
     o.u64(1);  // multiplicity sumcheck
     o.u64(log_t);
     for (unsigned r = 0; r < 2 * log_t; r++) o.q(mrp[r]);

@@ -49,7 +49,8 @@ using namespace zk;
 
 int zk::rmsnorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, size_t cols, size_t dim,
                            const uint32_t* gamma, size_t gamma_len, const uint32_t* claim_point, size_t n_point,
-                           const uint32_t claim_value[4], zkml_channel* chs, Out& o, uint32_t out_input_eval[4]) {
+                           const uint32_t claim_value[4], zkml_channel* chs, Out& o, uint32_t out_input_eval[4],
+                           bool v1_record) {
     if (!ctx || !input || !claim_value || !chs) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     if (rows == 0 || cols == 0 || dim == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty RMSNorm input or dim 0");
     if (gamma && gamma_len == 0) return set_error(ZKML_ERR_INVALID_ARG, "empty gamma");
@@ -223,7 +224,9 @@ int zk::rmsnorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, si
     if ((rc = wait_signal(ctx, rs.seq, words, 8))) return rc;
     const qm31 rms_s = ldw(words), rsqrt_s = ldw(words + 4);
 
-    // multiplicity sumcheck (prover.rs:9449-9515): transcript only
+    // multiplicity sumcheck (prover.rs:9449-9515): in the record only in the V1 layout
+    std::vector<qm31> mrp(2 * log_t);
+    qm31 m_claim = qzero();
     size_t mlen = tsize;
     next();
     launch_mult_round(b.mult.as<uint32_t>(), b.mv.as<uint4>(), mlen, true, false, qzero(), rs, s);
@@ -231,6 +234,9 @@ int zk::rmsnorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, si
     for (unsigned r = 0; r < log_t; r++) {
         if ((rc = wait_signal(ctx, rs.seq, words, 8))) return rc;
         const qm31 lo = ldw(words), hi = ldw(words + 4);
+        if (r == 0) m_claim = qadd(lo, hi);
+        mrp[2 * r] = lo;
+        mrp[2 * r + 1] = qsub(hi, lo);
         ch.mix_qm31(lo);
         ch.mix_qm31(qsub(hi, lo));
         const qm31 x = ch.draw_qm31();
@@ -243,6 +249,7 @@ int zk::rmsnorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, si
         mlen /= 2;
     }
     if ((rc = wait_signal(ctx, rs.seq, words, 4))) return rc;
+    const qm31 m_final = ldw(words);
     std::vector<uint32_t> mult(tsize), row_rms(pr);
     ZK_CUDA(cudaMemcpyAsync(mult.data(), b.mult.ptr, tsize * 4, cudaMemcpyDeviceToHost, s));
     ZK_CUDA(cudaMemcpyAsync(row_rms.data(), b.row_rms.ptr, pr * 4, cudaMemcpyDeviceToHost, s));
@@ -289,8 +296,17 @@ int zk::rmsnorm_reduce_dev(zkml_ctx* ctx, const uint32_t* input, size_t rows, si
     o.q(w_eval);
     o.q(rms_s);
     o.q(rsqrt_s);
-    o.u64(tsize);
-    for (size_t j = 0; j < tsize; j++) o.u64(mult[j]);
+    if (v1_record) {
+        o.u64(0);  // no multiplicities on chain
+        o.u64(1);  // multiplicity sumcheck (serialize_multiplicity_sumcheck, cairo_serde.rs:1138-1156)
+        o.u64(log_t);
+        for (unsigned r = 0; r < 2 * log_t; r++) o.q(mrp[r]);
+        o.q(m_final);
+        o.q(m_claim);
+    } else {
+        o.u64(tsize);
+        for (size_t j = 0; j < tsize; j++) o.u64(mult[j]);
+    }
     if (pr > 1) {
         o.u64(1);
         o.u64(pr);

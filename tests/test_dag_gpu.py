@@ -34,12 +34,20 @@ def residual_gated_block(seed, m=4, d=64, f=128):
                ("linear", w(d, f, 4)), ("linear", w(d, f, 5), 3), ("mul", 4), ("linear", w(f, d, 7))]
 
 
+def norms_block(seed, m=4, d=32):
+    """Linear -> RMSNorm -> Linear -> LayerNorm -> add_from(layer 0)."""
+    x = int_matrix_m31(m, d, seed, bound=60)
+    w = lambda i: int_matrix_m31(d, d, seed * 10 + i, bound=5)  # noqa: E731
+    return x, [("linear", w(0)), ("rmsnorm", None), ("linear", w(2)), ("layernorm", None), ("add", 0)]
+
+
 CASES = {
     "d11": lambda: d11_model(),
     "mul": lambda: mul_circuit(3),
     "mul_wide": lambda: mul_circuit(11, m=8, d=32, e=16),
     "residual_gated": lambda: residual_gated_block(5),
     "residual_gated_ragged": lambda: residual_gated_block(6, m=3, d=40, f=72),
+    "norms": lambda: norms_block(7),
 }
 
 

@@ -16,6 +16,7 @@ import oracle_lib as O
 from helpers import int_matrix_m31
 
 GOLD = json.loads((Path(__file__).parent / "golden" / "reference_vectors.json").read_text())
+P = (1 << 31) - 1
 
 
 def felts(raw):
@@ -183,3 +184,91 @@ def test_register_calldata_from_proof_commitments(name):
     cd = v1_envelope(int(ref[0], 16), x, y, layers, n_proofs) + tail
     coms = Z.verify_calldata_weight_commitments(cd, layers)
     assert Z.build_register_gkr_calldata(int(ref[0], 16), coms, layers) == ref
+
+
+# --- verifier-side replay of the Add and Mul records (gkr/verifier.rs Add / Mul arms) --------------
+
+def _cm(a, b):  # CM31 product, i^2 = -1
+    return ((a[0] * b[0] - a[1] * b[1]) % P, (a[0] * b[1] + a[1] * b[0]) % P)
+
+
+def qmul(x, y):
+    """QM31 product: (a + b u)(c + d u) with u^2 = 2 + i."""
+    a, b, c, d = (x[0], x[1]), (x[2], x[3]), (y[0], y[1]), (y[2], y[3])
+    ac, bd = _cm(a, c), _cm(b, d)
+    bdu = _cm(bd, (2, 1))
+    ad, bc = _cm(a, d), _cm(b, c)
+    return [(ac[0] + bdu[0]) % P, (ac[1] + bdu[1]) % P, (ad[0] + bc[0]) % P, (ad[1] + bc[1]) % P]
+
+
+def qadd(x, y):
+    return [(u + v) % P for u, v in zip(x, y)]
+
+
+def qsub(x, y):
+    return [(u - v) % P for u, v in zip(x, y)]
+
+
+def mle_point_eval(vals, point):
+    """MLE of M31 values (index bit n-1 = the first variable) at a QM31 point."""
+    cur = [[int(v) % P, 0, 0, 0] for v in vals]
+    for r in point:
+        h = len(cur) // 2
+        cur = [qadd(cur[i], qmul(r, qsub(cur[h + i], cur[i]))) for i in range(h)]
+    return cur[0]
+
+
+def test_add_and_mul_records_verify():
+    """Replays the transcript up to a Mul record and checks the degree-3 eq-sumcheck the way the
+    reference verifier does: c1 from the running claim, the final claim = eq(r, s) lhs(s) rhs(s);
+    then the Add record: lhs + rhs equals the claim on its output."""
+    import zkml_b200 as Z
+    m, d = 2, 8
+    x = int_matrix_m31(m, d, 21, bound=30)
+    wa, wb = int_matrix_m31(d, d, 22, bound=9), int_matrix_m31(d, d, 23, bound=9)
+    layers = [("linear", wa), ("linear", wb, -1), ("mul", 0), ("add", 1)]
+    rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=4)
+    assert rc == 0
+    f = felts(raw)
+    ya = (x.astype(object) @ wa.astype(object)) % P
+    yb = (x.astype(object) @ wb.astype(object)) % P
+    ymul = (ya * yb) % P
+    yout = (ymul + yb) % P
+    nv = (m - 1).bit_length() + (d - 1).bit_length()
+    ch = Z.PoseidonChannel()
+    for v in (4, m, d):
+        ch.mix_u64(v)
+    point = [list(map(int, ch.draw_qm31())) for _ in range(nv)]
+    claim = mle_point_eval(yout.reshape(-1), point)
+    ch.mix_felt(Z.securefield_to_felt(np.array(claim, np.uint32)))
+    # Add record (walk starts at layer 3): tag, lhs, rhs, trunk
+    assert f[1] == 1
+    lhs, rhs = f[2:6], f[6:10]
+    assert qadd(lhs, rhs) == claim
+    assert lhs == mle_point_eval(yb.reshape(-1), point) and rhs == mle_point_eval(ymul.reshape(-1), point)
+    assert f[10] == 1  # rhs (layer 2) is the trunk
+    ch.mix_felt(Z.securefield_to_felt(np.array(lhs, np.uint32)))
+    ch.mix_felt(Z.securefield_to_felt(np.array(rhs, np.uint32)))
+    ch.draw_qm31()
+    claim = rhs
+    # Mul record: tag 2, rounds, (c0, c2, c3) per round, lhs, rhs
+    at = 11
+    assert f[at] == 2 and f[at + 1] == nv
+    ch.mix_u64(0x4D554C)
+    ch.mix_felt(Z.securefield_to_felt(np.array(claim, np.uint32)))
+    cur, chal = claim, []
+    for r in range(nv):
+        base = at + 2 + 12 * r
+        c0, c2, c3 = f[base:base + 4], f[base + 4:base + 8], f[base + 8:base + 12]
+        c1 = qsub(qsub(qsub(cur, qadd(c0, c0)), c2), c3)
+        ch.mix_poly_coeffs_deg3(*(np.array(c, np.uint32) for c in (c0, c1, c2, c3)))
+        s = list(map(int, ch.draw_qm31()))
+        chal.append(s)
+        cur = qadd(qadd(c0, qmul(c1, s)), qmul(qadd(c2, qmul(c3, s)), qmul(s, s)))
+    ml, mr = f[at + 2 + 12 * nv:at + 6 + 12 * nv], f[at + 6 + 12 * nv:at + 10 + 12 * nv]
+    eq = [1, 0, 0, 0]
+    for r, s in zip(point, chal):
+        one_r, one_s = qsub([1, 0, 0, 0], r), qsub([1, 0, 0, 0], s)
+        eq = qmul(eq, qadd(qmul(r, s), qmul(one_r, one_s)))
+    assert cur == qmul(qmul(eq, ml), mr)
+    assert ml == mle_point_eval(ya.reshape(-1), chal) and mr == mle_point_eval(yb.reshape(-1), chal)

@@ -25,8 +25,11 @@ void launch_eq_table(const qm31* c, int v, uint4* table, size_t table_len, cudaS
 // per row, zeroed by the caller.
 // Tensor-pipe column restriction (see restrict_cols_tc_kernel); needs restrict_cols_tc_ok(B, n).
 bool restrict_cols_tc_ok(const uint32_t* B, uint32_t n);
-void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
-                             unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s);
+// The eq weights come straight from r_j (hi_vars high + lo_vars low challenges, lo_vars <= 6);
+// hi_base is the first 64-column stripe of B within the full column range.
+void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const qm31* r_j, unsigned hi_vars,
+                             unsigned lo_vars, uint32_t hi_base, unsigned long long* acc, uint32_t* err, int num_sms,
+                             cudaStream_t s);
 void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
                           unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s);
 // Row restriction of a row-major m x k M31 matrix: acc[j] += sum_i A[i][j] L_i.

@@ -612,25 +612,26 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
     } else {
         const unsigned lo_vars = n_rj < 6 ? n_rj : 6;
         const unsigned hi_vars = n_rj - lo_vars;
-        if ((rc = ctx->eq_hi.ensure(((size_t)16) << hi_vars)) || (rc = ctx->eq_lo.ensure(64 * 16)) ||
-            (rc = ctx->acc_b.ensure(k * 32)))
-            return rc;
-        launch_eq_table(r_j, hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
-        launch_eq_table(r_j + hi_vars, lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
-        ZK_CUDA(cudaMemsetAsync(ctx->acc_b.ptr, 0, k * 32, s));
         const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n);
+        if ((rc = ctx->acc_b.ensure(k * 32))) return rc;
+        if (!tc) {  // the tensor-pipe kernel forms its eq weights from r_j itself
+            if ((rc = ctx->eq_hi.ensure(((size_t)16) << hi_vars)) || (rc = ctx->eq_lo.ensure(64 * 16))) return rc;
+            launch_eq_table(r_j, hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
+            launch_eq_table(r_j + hi_vars, lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
+            ctx->launches += 2;
+        }
+        ZK_CUDA(cudaMemsetAsync(ctx->acc_b.ptr, 0, k * 32, s));
         {
             KTimer t(ctx, KC_RESTRICT_COLS);
             if (tc)
-                launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
-                                        ctx->acc_b.as<unsigned long long>(),
-                                        ctx->err_flag(), ctx->num_sms, s);
+                launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n, r_j, hi_vars, lo_vars, 0,
+                                        ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
             else
                 launch_restrict_cols(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
                                      ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
         }
         launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
-        ctx->launches += 4;
+        ctx->launches += 2;
     }
     return ZKML_OK;
 }
@@ -917,25 +918,27 @@ int zkml_restrict_cols_block(zkml_ctx* ctx, const uint32_t* b_block, size_t k, s
     const unsigned lo_vars = n_rj < 6 ? (unsigned)n_rj : 6u;
     const unsigned hi_vars = (unsigned)n_rj - lo_vars;
     const qm31* rj = reinterpret_cast<const qm31*>(r_j);
-    if ((rc = ctx->eq_hi.ensure(((size_t)16) << hi_vars)) || (rc = ctx->eq_lo.ensure(64 * 16))) return rc;
-    launch_eq_table(rj, (int)hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
-    launch_eq_table(rj + hi_vars, (int)lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
+    const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n_block);
+    if (!tc) {  // the tensor-pipe kernel forms its eq weights from r_j itself
+        if ((rc = ctx->eq_hi.ensure(((size_t)16) << hi_vars)) || (rc = ctx->eq_lo.ensure(64 * 16))) return rc;
+        launch_eq_table(rj, (int)hi_vars, ctx->eq_hi.as<uint4>(), (size_t)1 << hi_vars, s);
+        launch_eq_table(rj + hi_vars, (int)lo_vars, ctx->eq_lo.as<uint4>(), 64, s);
+        ctx->launches += 2;
+    }
     unsigned long long* acc = reinterpret_cast<unsigned long long*>(out_words);
     ZK_CUDA(cudaMemsetAsync(acc, 0, k * 32, s));
-    const uint4* lhi = ctx->eq_hi.as<uint4>() + (col_offset >> 6);
-    const bool tc = ctx->restrict_tc && restrict_cols_tc_ok(B, (uint32_t)n_block);
     {
         KTimer t(ctx, KC_RESTRICT_COLS);
         if (tc)
-            launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n_block, lhi, ctx->eq_lo.as<uint4>(),
-                                    acc, ctx->err_flag(), ctx->num_sms, s);
+            launch_restrict_cols_tc(B, (uint32_t)k, (uint32_t)n_block, rj, hi_vars, lo_vars,
+                                    (uint32_t)(col_offset >> 6), acc, ctx->err_flag(), ctx->num_sms, s);
         else
-            launch_restrict_cols(B, (uint32_t)k, (uint32_t)n_block, lhi, ctx->eq_lo.as<uint4>(), acc, ctx->err_flag(),
-                                 ctx->num_sms, s);
+            launch_restrict_cols(B, (uint32_t)k, (uint32_t)n_block, ctx->eq_hi.as<uint4>() + (col_offset >> 6),
+                                 ctx->eq_lo.as<uint4>(), acc, ctx->err_flag(), ctx->num_sms, s);
     }
     // partial sums to canonical words (so that adding them across ranks cannot overflow)
     launch_canon_u64(acc, 4 * k, s);
-    ctx->launches += 4;
+    ctx->launches += 2;
     ZK_CUDA(cudaGetLastError());
     if ((rc = read_err_flag(ctx)) || (rc = check_err_flag(ctx, "restrict_cols_block"))) return rc;
     return ZKML_OK;

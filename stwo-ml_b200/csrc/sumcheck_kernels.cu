@@ -301,6 +301,16 @@ void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4
 // N-tiles of 8 (c, l) columns), ~1.5 PRMT per element, no 64-bit integer work:
 // the kernel is left with the HBM stream.
 // ---------------------------------------------------------------------------
+// One eq-table entry: prod_l (bit_{v-1-l}(idx) ? c_l : 1 - c_l), first challenge on the MSB.
+__device__ __forceinline__ qm31 eq_entry(const EqChallenges& ch, uint32_t idx) {
+    qm31 r = qm(1, 0, 0, 0);
+    for (int l = 0; l < ch.v; l++) {
+        const qm31 c = ch.c[l];
+        r = qmul(r, ((idx >> (ch.v - 1 - l)) & 1u) ? c : qsub(qm(1, 0, 0, 0), c));
+    }
+    return r;
+}
+
 constexpr int TC_CH = 1024;                 // columns per block chunk
 constexpr int TC_TROW = TC_CH + 16;         // padded table row (bytes): conflict-free fragment loads
 constexpr int TC_WARPS = 8;
@@ -309,22 +319,33 @@ constexpr int TC_STEPS = 2;  // 32-column steps loaded per iteration (one iterat
 
 template <int MINB, int STEPS>
 __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(const uint32_t* __restrict__ B, uint32_t k,
-                                                                         uint32_t n, const uint4* __restrict__ lhi,
-                                                                         const uint4* __restrict__ llo, uint32_t npad,
+                                                                         uint32_t n, const EqChallenges hi,
+                                                                         const EqChallenges lo, uint32_t hi_base,
+                                                                         uint32_t npad,
                                                                          unsigned long long* __restrict__ acc_out,
                                                                          uint32_t* __restrict__ err) {
     __shared__ __align__(16) uint8_t tb[16 * TC_TROW];
+    __shared__ qm31 s_hi[TC_CH / 64], s_lo[64];
     const uint32_t c0 = blockIdx.x * TC_CH;
     const uint32_t cw = min((uint32_t)TC_CH, npad - c0);  // chunk width (multiple of 32)
-    // the chunk's eq byte planes: row c * 4 + l holds byte l of component c of
-    // L_j = lhi[j / 64] * llo[j % 64] (zero past n), four columns per thread and row word
+    // eq(r_j, j) = lhi[j / 64] * llo[j % 64]: the chunk's 16 high factors (stripe hi_base + j / 64 of
+    // the high challenges) and the 64 low ones (zero past 2^lo.v), straight from the challenges
+    if (threadIdx.x < 64) {
+        const uint32_t u = threadIdx.x;
+        s_lo[u] = u < (1u << lo.v) ? eq_entry(lo, u) : qzero();
+    } else if (threadIdx.x < 64 + TC_CH / 64) {
+        s_hi[threadIdx.x - 64] = eq_entry(hi, hi_base + (c0 >> 6) + (threadIdx.x - 64));
+    }
+    __syncthreads();
+    // the chunk's eq byte planes: row c * 4 + l holds byte l of component c of L_j (zero past
+    // n), four columns per thread and row word
     for (uint32_t j4 = threadIdx.x; j4 < cw / 4; j4 += blockDim.x) {
         uint32_t w[4][4];  // [column][component]
 #pragma unroll
         for (int u = 0; u < 4; u++) {
             const uint32_t col = c0 + 4 * j4 + u;
             qm31 L = qzero();
-            if (col < n) L = qmul(ld_q(lhi + (col >> 6)), ld_q(llo + (col & 63)));
+            if (col < n) L = qmul(s_hi[(col - c0) >> 6], s_lo[col & 63]);
             w[u][0] = L.a;
             w[u][1] = L.b;
             w[u][2] = L.c;
@@ -428,8 +449,14 @@ bool restrict_cols_tc_ok(const uint32_t* B, uint32_t n) {
     return n % 4 == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0;
 }
 
-void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const uint4* lhi, const uint4* llo,
-                             unsigned long long* acc, uint32_t* err, int num_sms, cudaStream_t s) {
+void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const qm31* r_j, unsigned hi_vars,
+                             unsigned lo_vars, uint32_t hi_base, unsigned long long* acc, uint32_t* err, int num_sms,
+                             cudaStream_t s) {
+    EqChallenges hi, lo;
+    hi.v = (int)hi_vars;
+    lo.v = (int)lo_vars;
+    for (unsigned i = 0; i < hi_vars; i++) hi.c[i] = r_j[i];
+    for (unsigned i = 0; i < lo_vars; i++) lo.c[i] = r_j[hi_vars + i];
     const uint32_t npad = (n + 31) / 32 * 32;
     const uint32_t chunks = (npad + TC_CH - 1) / TC_CH;
     const uint32_t row_tiles = (k + 15) / 16;
@@ -438,8 +465,8 @@ void launch_restrict_cols_tc(const uint32_t* B, uint32_t k, uint32_t n, const ui
     const uint32_t gy_max = (row_tiles + TC_WARPS - 1) / TC_WARPS;
     if (gy > gy_max) gy = gy_max;
     if (gy == 0) gy = 1;
-    restrict_cols_tc_kernel<TC_MINB, TC_STEPS><<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, lhi, llo,
-                                                                                          npad, acc, err);
+    restrict_cols_tc_kernel<TC_MINB, TC_STEPS><<<dim3(chunks, gy), TC_WARPS * 32, 0, s>>>(B, k, n, hi, lo,
+                                                                                          hi_base, npad, acc, err);
 }
 
 // ---------------------------------------------------------------------------

@@ -502,9 +502,10 @@ def reduce_matmul_layer_with_backend(output_claim: GKRClaim, a: M31Matrix, b: M3
                                               np.ascontiguousarray(output_claim.value, np.uint32).reshape(4),
                                               abuf.ptr, m, k, bbuf.ptr, n, C.byref(channel.state),
                                               rp.reshape(-1), fa, fb, nxt.reshape(-1)))
-    polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_k)]
-    red = MatMulReduction(polys, nxt[log_m:log_m + log_k].copy(), fa, fb)
-    return red, GKRClaim(nxt[:log_m + log_k].copy(), fa.copy())
+    # views of this call's own fresh arrays (no per-round copies)
+    polys = [RoundPoly(row[0:4], row[4:8], row[8:12]) for row in rp[:log_k]]
+    red = MatMulReduction(polys, nxt[log_m:log_m + log_k], fa, fb)
+    return red, GKRClaim(nxt[:log_m + log_k], fa.copy())
 
 
 # ---------------------------------------------------------------------------

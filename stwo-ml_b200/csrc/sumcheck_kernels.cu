@@ -328,6 +328,27 @@ __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(c
     __shared__ qm31 s_hi[TC_CH / 64], s_lo[64];
     const uint32_t c0 = blockIdx.x * TC_CH;
     const uint32_t cw = min((uint32_t)TC_CH, npad - c0);  // chunk width (multiple of 32)
+    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tg = lane & 3;
+    const uint32_t row_tiles = (k + 15) / 16;
+    const uint32_t c_end = min(n, c0 + cw);
+    const uint32_t rt0 = blockIdx.y * TC_WARPS + warp;
+    // the first row tile's first loads go out before the eq weights are formed
+    uint4 xn[STEPS][4];
+    {
+        const uint32_t r0 = rt0 * 16 + g, r1 = r0 + 8;
+        const bool v0 = rt0 < row_tiles && r0 < k, v1 = rt0 < row_tiles && r1 < k;
+        const uint4* p0 = reinterpret_cast<const uint4*>(B + (size_t)(v0 ? r0 : 0) * n);
+        const uint4* p1 = reinterpret_cast<const uint4*>(B + (size_t)(v1 ? r1 : 0) * n);
+#pragma unroll
+        for (int h = 0; h < STEPS; h++) {
+            const uint32_t ja = c0 + 32 * h + 4 * tg, jb = ja + 16;
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            xn[h][0] = (v0 && ja < c_end) ? __ldcs(p0 + ja / 4) : z;
+            xn[h][1] = (v1 && ja < c_end) ? __ldcs(p1 + ja / 4) : z;
+            xn[h][2] = (v0 && jb < c_end) ? __ldcs(p0 + jb / 4) : z;
+            xn[h][3] = (v1 && jb < c_end) ? __ldcs(p1 + jb / 4) : z;
+        }
+    }
     // eq(r_j, j) = lhi[j / 64] * llo[j % 64]: the chunk's 16 high factors (stripe hi_base + j / 64 of
     // the high challenges) and the 64 low ones (zero past 2^lo.v), straight from the challenges
     if (threadIdx.x < 64) {
@@ -362,11 +383,8 @@ __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(c
             }
     }
     __syncthreads();
-    const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g = lane >> 2, tg = lane & 3;
-    const uint32_t row_tiles = (k + 15) / 16;
-    const uint32_t c_end = min(n, c0 + cw);
     uint32_t bad = 0;
-    for (uint32_t rt = blockIdx.y * TC_WARPS + warp; rt < row_tiles; rt += gridDim.y * TC_WARPS) {
+    for (uint32_t rt = rt0; rt < row_tiles; rt += gridDim.y * TC_WARPS) {
         const uint32_t r0 = rt * 16 + g, r1 = r0 + 8;
         const bool v0 = r0 < k, v1 = r1 < k;
         const uint4* p0 = reinterpret_cast<const uint4*>(B + (size_t)(v0 ? r0 : 0) * n);
@@ -391,8 +409,7 @@ __global__ void __launch_bounds__(TC_WARPS * 32, MINB) restrict_cols_tc_kernel(c
                 x[h][3] = (v1 && jb < c_end) ? __ldcs(p1 + jb / 4) : z;
             }
         };
-        uint4 xn[STEPS][4];
-        load(xn, c0);
+        if (rt != rt0) load(xn, c0);
         for (uint32_t j0 = c0; j0 < c_end; j0 += 32 * STEPS) {
             uint4 x[STEPS][4];
 #pragma unroll

@@ -95,6 +95,12 @@ inline felt mul_adx(const felt& a, const felt& b) {
     zk_felt_mont_mul_adx(r.l, a.l, b.l);
     return r;
 }
+// x^3 (in Montgomery form: x^3 / R^2), both multiplications in one call.
+inline felt cube_adx(const felt& a) {
+    felt r;
+    zk_felt_mont_cube_adx(r.l, a.l);
+    return r;
+}
 // 256-bit add / subtract without reduction (callers keep results in range).
 // Early-clobber outputs: the carry chains write limbs before reading later inputs.
 inline felt add4(const felt& a, const felt& b) {
@@ -141,9 +147,9 @@ const felt kP = {{1, 0, 0, FP3}};
 
 inline void full_round_fast(felt s[3], const felt* rc, const felt& p2, const felt& p3) {
     felt y0 = add4(s[0], rc[0]), y1 = add4(s[1], rc[1]), y2 = add4(s[2], rc[2]);
-    y0 = mul_adx(mul_adx(y0, y0), y0);
-    y1 = mul_adx(mul_adx(y1, y1), y1);
-    y2 = mul_adx(mul_adx(y2, y2), y2);
+    y0 = cube_adx(y0);
+    y1 = cube_adx(y1);
+    y2 = cube_adx(y2);
     const felt t = add4(add4(y0, y1), y2);                             // < 3p
     s[0] = red_full(add4(t, dbl4(y0)));                                // < 5p
     s[1] = red_full(sub4(add4(t, p2), dbl4(y1)));                      // < 5p
@@ -157,7 +163,7 @@ void hades_fast(felt s[3]) {
     felt s0 = s[0], s1 = s[1];
     felt x = add4(s[2], rc[0]);
     for (int r = 0; r < 83; r++) {
-        const felt y = mul_adx(mul_adx(x, x), x);                      // < p
+        const felt y = cube_adx(x);                                    // < p
         const felt u = add4(s0, s1);                                   // < 2p
         const felt t = add4(u, y);                                     // < 3p
         const felt n0 = red_full(add4(t, dbl4(s0)));

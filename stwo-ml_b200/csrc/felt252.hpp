@@ -113,6 +113,7 @@ inline felt f_redc(uint64_t t[8]) {
 
 // BMI2 + ADX assembly multiply (felt252_x86.S) and whether this CPU can run it.
 extern "C" void zk_felt_mont_mul_adx(uint64_t r[4], const uint64_t a[4], const uint64_t b[4]);
+extern "C" void zk_felt_mont_cube_adx(uint64_t r[4], const uint64_t a[4]);
 extern bool g_felt_use_adx;
 
 // Montgomery product a * b / 2^256 mod p for a, b < p (CIOS, one limb of b per step).

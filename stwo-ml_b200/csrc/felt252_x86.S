@@ -5,24 +5,19 @@
  *
  * void zk_felt_mont_mul_adx(uint64_t r[4], const uint64_t a[4], const uint64_t b[4]);
  *
- * 4x4 schoolbook product with the two ADX carry chains (adcx / adox), then a
- * separate reduction: for each low limb t_i, m = -t_i (p = 1 mod 2^64), adding
- * m * p clears t_i (carry iff t_i != 0) and adds m * 0x0800000000000011 at
- * limbs i+3, i+4.  The result is < 2p and is reduced once with cmov.
+ * 4x4 schoolbook product with the two ADX carry chains (adcx / adox), then the
+ * reduction in two steps.  p = 1 mod 2^192, so M = -t[0..2] mod 2^192 clears the
+ * three low limbs at once: t + M p = t + M + (M * 0x0800000000000011) 2^192, the
+ * three 64 x 64 products of M * p3 independent of one another; then the usual
+ * word step m = -t3 clears limb 3.  This is the same Montgomery quotient as the
+ * word-by-word form (the unique m < 2^256 with t + m p = 0 mod 2^256), with a
+ * shorter dependency chain.  The result is < 2p and is reduced once with cmov.
+ *
+ * void zk_felt_mont_cube_adx(uint64_t r[4], const uint64_t a[4]);
+ *   r = a^3 / R^2 mod p (two multiplications without a second call).
  */
-    .text
-    .globl  zk_felt_mont_mul_adx
-    .type   zk_felt_mont_mul_adx, @function
-    .p2align 4
-zk_felt_mont_mul_adx:
-    pushq   %rbx
-    pushq   %rbp
-    pushq   %r12
-    pushq   %r13
-    pushq   %r14
-    pushq   %r15
-    movq    %rdx, %rcx                  /* rcx = b */
-
+/* (rdi) = (rsi) * (rcx) / R mod p; clobbers rax, rbx, rbp, rdx, r8-r15; keeps rdi, rsi, rcx */
+.macro MONT_MUL
     /* row 0: t[0..4] = a * b0 */
     movq    (%rcx), %rdx
     mulxq   (%rsi), %r8, %r9
@@ -85,47 +80,47 @@ zk_felt_mont_mul_adx:
     adoxq   %rbp, %r15
     adcxq   %rbp, %r15
 
-    /* reduction, p3 in rcx */
-    movabsq $0x0800000000000011, %rcx
-
+    /* reduction step 1: M = -t[0..2] mod 2^192 in rax, rbx, rbp; CF: t[0..2] != 0 */
+    xorl    %eax, %eax
+    xorl    %ebx, %ebx
+    xorl    %ebp, %ebp
+    subq    %r8, %rax
+    sbbq    %r9, %rbx
+    sbbq    %r10, %rbp
     movq    %r8, %rdx
-    negq    %rdx                        /* m0 = -t0, CF = (t0 != 0) */
-    adcq    $0, %r9
-    adcq    $0, %r10
-    mulxq   %rcx, %rax, %rbx
-    adcq    %rax, %r11
-    adcq    %rbx, %r12
-    adcq    $0, %r13
-    adcq    $0, %r14
-    adcq    $0, %r15
-
-    movq    %r9, %rdx
-    negq    %rdx
-    adcq    $0, %r10
-    adcq    $0, %r11
-    mulxq   %rcx, %rax, %rbx
-    adcq    %rax, %r12
-    adcq    %rbx, %r13
-    adcq    $0, %r14
-    adcq    $0, %r15
-
-    movq    %r10, %rdx
+    orq     %r9, %rdx
+    orq     %r10, %rdx
     negq    %rdx
     adcq    $0, %r11
     adcq    $0, %r12
-    mulxq   %rcx, %rax, %rbx
-    adcq    %rax, %r13
-    adcq    %rbx, %r14
+    adcq    $0, %r13
+    adcq    $0, %r14
     adcq    $0, %r15
-
+    /* t[3..7] += M * p3 */
+    movabsq $0x0800000000000011, %rdx
+    mulxq   %rax, %r8, %r9
+    mulxq   %rbx, %r10, %rax
+    mulxq   %rbp, %rbx, %rbp
+    addq    %r8, %r11
+    adcq    %r9, %r12
+    adcq    %rax, %r13
+    adcq    %rbp, %r14
+    adcq    $0, %r15
+    addq    %r10, %r12
+    adcq    %rbx, %r13
+    adcq    $0, %r14
+    adcq    $0, %r15
+    /* reduction step 2: m = -t3 clears limb 3, m * p3 lands on limbs 6, 7 */
     movq    %r11, %rdx
     negq    %rdx
     adcq    $0, %r12
     adcq    $0, %r13
-    mulxq   %rcx, %rax, %rbx
-    adcq    %rax, %r14
+    adcq    $0, %r14
+    adcq    $0, %r15
+    movabsq $0x0800000000000011, %r8
+    mulxq   %r8, %rax, %rbx
+    addq    %rax, %r14
     adcq    %rbx, %r15
-
     /* r = t[4..7] - p if t >= p (branch-free) */
     movq    %r12, %rax
     subq    $1, %rax
@@ -134,7 +129,7 @@ zk_felt_mont_mul_adx:
     movq    %r14, %rdx
     sbbq    $0, %rdx
     movq    %r15, %rbp
-    sbbq    %rcx, %rbp
+    sbbq    %r8, %rbp
     cmovncq %rax, %r12
     cmovncq %rbx, %r13
     cmovncq %rdx, %r14
@@ -143,7 +138,21 @@ zk_felt_mont_mul_adx:
     movq    %r13, 8(%rdi)
     movq    %r14, 16(%rdi)
     movq    %r15, 24(%rdi)
+.endm
 
+    .text
+    .globl  zk_felt_mont_mul_adx
+    .type   zk_felt_mont_mul_adx, @function
+    .p2align 4
+zk_felt_mont_mul_adx:
+    pushq   %rbx
+    pushq   %rbp
+    pushq   %r12
+    pushq   %r13
+    pushq   %r14
+    pushq   %r15
+    movq    %rdx, %rcx                  /* rcx = b */
+    MONT_MUL
     popq    %r15
     popq    %r14
     popq    %r13
@@ -152,4 +161,32 @@ zk_felt_mont_mul_adx:
     popq    %rbx
     ret
     .size   zk_felt_mont_mul_adx, .-zk_felt_mont_mul_adx
+
+    .globl  zk_felt_mont_cube_adx
+    .type   zk_felt_mont_cube_adx, @function
+    .p2align 4
+zk_felt_mont_cube_adx:
+    pushq   %rbx
+    pushq   %rbp
+    pushq   %r12
+    pushq   %r13
+    pushq   %r14
+    pushq   %r15
+    subq    $40, %rsp
+    movq    %rdi, 32(%rsp)              /* the result pointer */
+    movq    %rsi, %rcx                  /* b = a */
+    movq    %rsp, %rdi                  /* a^2 into the stack slot */
+    MONT_MUL
+    movq    %rsp, %rcx                  /* b = a^2 */
+    movq    32(%rsp), %rdi
+    MONT_MUL
+    addq    $40, %rsp
+    popq    %r15
+    popq    %r14
+    popq    %r13
+    popq    %r12
+    popq    %rbp
+    popq    %rbx
+    ret
+    .size   zk_felt_mont_cube_adx, .-zk_felt_mont_cube_adx
     .section .note.GNU-stack,"",@progbits

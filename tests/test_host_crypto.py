@@ -128,3 +128,40 @@ def test_activation_tables_match_oracle(tag):
     ref = np.zeros(1 << lg, np.uint32)
     O.lib().orc_activation_table(tag, lg, ref)
     assert (Z.activation_table(tag) == ref).all()
+
+
+def test_montgomery_multiply_and_cube_edges():
+    """The x86 Montgomery multiply and cube (felt252_x86.S) against big-integer arithmetic, on
+    inputs up to 4p (the lazy-reduction range) and on products whose low 192 bits are zero
+    (the reduction's no-carry path)."""
+    import ctypes as C
+    import random
+    p = Z.STARK_P
+    R = 1 << 256
+    rinv = pow(R, -1, p)
+    L = Z.lib()
+    try:
+        flags = open("/proc/cpuinfo").read()
+    except OSError:
+        flags = ""
+    if not hasattr(L, "zk_felt_mont_mul_adx") or " adx" not in flags or " bmi2" not in flags:
+        pytest.skip("no x86 ADX / BMI2 multiply on this host")
+    u64x4 = C.c_uint64 * 4
+
+    def limbs(x):
+        return u64x4(*[(x >> (64 * i)) & (2**64 - 1) for i in range(4)])
+
+    def val(a):
+        return sum(int(a[i]) << (64 * i) for i in range(4))
+
+    rng = random.Random(7)
+    cases = [(0, 0), (1, 1), (p - 1, p - 1), (4 * p - 1, 4 * p - 1), (1 << 192, 1 << 64), (1 << 128, 1 << 128),
+             (1 << 250, 1 << 6), (p, p), (2 * p + 5, 3 * p + 7)]
+    cases += [(rng.randrange(4 * p), rng.randrange(4 * p)) for _ in range(3000)]
+    for a, b in cases:
+        r = u64x4()
+        L.zk_felt_mont_mul_adx(r, limbs(a), limbs(b))
+        assert val(r) == a * b * rinv % p
+        if a == b or a < 4 * p:
+            L.zk_felt_mont_cube_adx(r, limbs(a))
+            assert val(r) == a * a * a * rinv * rinv % p

@@ -464,9 +464,9 @@ def run_product(args):
     stream = torch.cuda.current_stream()
     ctx = Z.Context(dev)
     ctx.set_stream(stream.cuda_stream)
-    from zkml_b200.distributed import ShmExchange, prove_product_sharded_native
+    from zkml_b200.distributed import ShmExchange, job_nonce, prove_product_sharded_native
     port = os.environ.get("MASTER_PORT", "0")
-    ex = ShmExchange(f"zkml_bench_{port}_{world}", world, rank, max_gather_bytes=32 << 17)
+    ex = ShmExchange(f"zkml_bench_{port}_{world}", world, rank, max_gather_bytes=32 << 17, nonce=job_nonce())
     n = 1 << args.log_n
     n_loc = n // world
     g = torch.Generator(device="cuda").manual_seed(1234 + rank)

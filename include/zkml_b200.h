@@ -193,7 +193,10 @@ int zkml_reduce_matmul_layer_gkr_fb(zkml_ctx *ctx, const uint32_t *claim_point, 
  * of a collective library.  Each rank (one process per GPU, distinct GPUs of one node)
  * creates an inbox for a given k and exports its CUDA IPC handle (64 bytes); after the
  * ranks have exchanged the handles, each opens the others'.  Per layer call, with an
- * epoch that increases by one per call: zkml_restrict_cols_block_p2p restricts the block
+ * epoch that starts at 1 and increases by one per call (epoch 0, a skipped or repeated
+ * epoch, and a scatter before the previous call's gather return ZKML_ERR_INVALID_ARG;
+ * both calls go on the context's stream, gather(e) before scatter(e + 1), which is what
+ * makes the inbox's double buffer safe): zkml_restrict_cols_block_p2p restricts the block
  * and stores the canonical partial words straight into every rank's inbox, then publishes
  * the epoch there; zkml_reduce_matmul_layer_gkr_p2p waits (bounded: ZKML_ERR_TIMEOUT after
  * about two seconds) for every rank's words, adds them and runs the layer.  Two ranks
@@ -279,7 +282,8 @@ int zkml_reduce_layernorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, siz
                           zkml_channel *ch, uint64_t *out_calldata, size_t cap, size_t *out_len,
                           uint32_t out_input_eval[4]);
 
-/* ---- GKR proof of a layered circuit (Linear / ReLU / RMSNorm / LayerNorm / Add / Mul) */
+/* ---- GKR proof of a layered circuit (Linear / ReLU / Activation / RMSNorm / LayerNorm /
+ *      Add / Mul) */
 
 #define ZKML_LAYER_LINEAR 0
 #define ZKML_LAYER_RELU 1
@@ -287,6 +291,10 @@ int zkml_reduce_layernorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, siz
 #define ZKML_LAYER_ADD 3     /* element-wise lhs + rhs (GraphBuilder::add_from) */
 #define ZKML_LAYER_MUL 4     /* element-wise lhs * rhs (GraphBuilder::mul_from) */
 #define ZKML_LAYER_LAYERNORM 5 /* LayerNorm over the full layer width (GraphBuilder::layer_norm) */
+/* GraphBuilder::activation(GELU / Sigmoid / Softmax / SiLU): zkml_chain_layer.n holds the type
+ * tag (2 GELU, 3 Sigmoid, 4 Softmax, 5 SiLU); the forward pass applies ActivationType::as_fn
+ * to the full M31 values (compiler/prove.rs:1893-1899) */
+#define ZKML_LAYER_ACTIVATION 6
 /* zkml_chain_layer.src: the previous layer's output (the model input for layer 0) */
 #define ZKML_CHAIN_PREV (-2)
 /* flags: the Activation record without the multiplicity-sumcheck and piecewise flags, the
@@ -295,6 +303,10 @@ int zkml_reduce_layernorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, siz
 /* flags: emit the verify_model_gkr calldata (starknet.rs:3143-3345, layout V1) from
  * proof_data on, instead of serialize_gkr_model_proof */
 #define ZKML_CHAIN_V1_CALLDATA 2
+/* flags: Activation layers take the LogUp reduction (gkr/prover.rs:6400-6600), as the
+ * reference does under STWO_PIECEWISE_ACTIVATION=0; without it the piecewise-algebraic
+ * reduction (prover.rs:7006-7228), the reference's default (prover.rs:1765-1790) */
+#define ZKML_CHAIN_ACTIVATION_LOGUP 4
 
 /* One layer of the circuit (LayeredCircuit::from_graph, gkr/circuit.rs:140-225); layer i's
  * index is its circuit layer index. */
@@ -413,10 +425,36 @@ typedef struct zkml_exchange {
 } zkml_exchange;
 
 /* A zkml_exchange over a POSIX shared-memory segment for the ranks of one node
- * (name unique per job; rank 0 creates it).  max_gather_bytes bounds one rank's
- * allgather contribution.  All waits are bounded (60 s -> ZKML_ERR_TIMEOUT). */
-int zkml_shm_exchange_open(const char *name, int world, int rank, size_t max_gather_bytes, zkml_exchange *out);
+ * (rank 0 creates it under `name`).  job_nonce must be the same on every rank and
+ * differ between jobs (rank 0 draws it and broadcasts it): a segment an earlier,
+ * crashed job left under the same name carries another nonce and is never joined.
+ * max_gather_bytes bounds one rank's allgather contribution.  All waits are
+ * bounded (60 s -> ZKML_ERR_TIMEOUT). */
+int zkml_shm_exchange_open(const char *name, int world, int rank, size_t max_gather_bytes, uint64_t job_nonce,
+                           zkml_exchange *out);
 int zkml_shm_exchange_close(zkml_exchange *ex);
+
+/* The same sharded proof with the exchange on the GPUs' own data path: a peer-memory mesh
+ * over NVLink / NVSwitch between the ranks of one node, one process per distinct GPU.
+ * zkml_mesh_create allocates this rank's inbox (max_gather_bytes bounds one rank's share of
+ * the gather: 32 x gather_local bytes for the folded vectors, 8 x n / world when the vectors
+ * are too short to split) and returns its CUDA IPC handle; once the ranks have exchanged the
+ * handles (e.g. an all-gather over their process group), zkml_mesh_open maps every peer's
+ * inbox.  zkml_prove_product_sharded_mesh then runs the loop of zkml_prove_product_sharded
+ * with each split round's 12 words added across the ranks inside the round kernel (peer
+ * stores, a release flag per rank, a bounded acquire wait in the grid's last block) and the
+ * folded vectors gathered by peer stores into every inbox, with no host step and no
+ * collective library.  Every rank must make the same sequence of calls on its context's
+ * stream.  A rank that does not arrive within about two seconds makes the others' calls
+ * return ZKML_ERR_TIMEOUT with the GPU usable; the mesh must then be closed and re-created.
+ * No TMA and no multicast touch peer memory. */
+int zkml_mesh_create(zkml_ctx *ctx, int world, int rank, size_t max_gather_bytes, uint8_t out_handle[64]);
+int zkml_mesh_open(zkml_ctx *ctx, const uint8_t *handles /* world x 64 bytes */, int world);
+int zkml_mesh_close(zkml_ctx *ctx);
+int zkml_prove_product_sharded_mesh(zkml_ctx *ctx, const uint32_t *a_local, const uint32_t *b_local, size_t n,
+                                    size_t gather_local, zkml_channel *ch, uint32_t *out_round_polys,
+                                    uint32_t *out_challenges, uint32_t out_final_a[4], uint32_t out_final_b[4],
+                                    size_t *out_gathered_at);
 
 /* a_local, b_local: this rank's n / world M31 elements (host or device).
  * out_round_polys: log2(n) x 12 words, out_challenges: log2(n) x 4 words;

@@ -3105,15 +3105,17 @@ typedef struct {
     size_t layer;
 } chain_deferred;
 
+#define CHAIN_MAX 1024
+
 int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
                         const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
                         size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads) {
     oracle_init();
-    if (n_layers == 0 || n_layers > 64) return 1;
+    if (n_layers == 0 || n_layers > CHAIN_MAX) return 1;
     /* forward pass: outs[0] is the model input, outs[l + 1] layer l's output (m x width[.]) */
-    uint32_t *outs[65];
-    size_t width[65];
-    long long src[64];
+    uint32_t **outs = (uint32_t **)calloc(n_layers + 1, sizeof(uint32_t *));
+    size_t *width = (size_t *)calloc(n_layers + 1, sizeof(size_t));
+    long long *src = (long long *)calloc(n_layers, sizeof(long long));
     outs[0] = (uint32_t *)malloc(4 * m * k0);
     for (size_t i = 0; i < m * k0; i++) outs[0][i] = m_red64(input[i]);
     width[0] = k0;
@@ -3139,6 +3141,11 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
                 rc = 1;
                 break;
             }
+        } else if (layers[l].type == 6) {
+            if (layers[l].n < 2 || layers[l].n > 5) {
+                rc = 1;
+                break;
+            }
         } else if (layers[l].type != 1 && layers[l].type != 2 && layers[l].type != 5) {
             rc = 1;
             break;
@@ -3151,6 +3158,9 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             orc_matmul_m31(x, m, w, layers[l].weight, wo, y, threads);
         } else if (layers[l].type == 1) {
             for (size_t i = 0; i < m * w; i++) y[i] = x[i] <= 1073741823u ? x[i] : 0;
+        } else if (layers[l].type == 6) {
+            /* apply_activation with ActivationType::as_fn (compiler/prove.rs:1893-1899) */
+            for (size_t i = 0; i < m * w; i++) y[i] = act_fn((int)layers[l].n, x[i]);
         } else if (layers[l].type == 2) {
             /* apply_rmsnorm_detailed (compiler/prove.rs:1115-1180), dim = the layer width */
             uint32_t *tab = (uint32_t *)malloc(4u << 16);
@@ -3182,6 +3192,9 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     }
     if (rc) {
         for (size_t l = 0; l <= built; l++) free(outs[l]);
+        free(outs);
+        free(width);
+        free(src);
         return rc;
     }
     orc_channel ch;
@@ -3208,13 +3221,13 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     felt_out lay = {(uint64_t *)malloc(32 * cap), 0, cap, 0};
     size_t n_proofs = 0;
     /* weight claims: the walk's, in walk order */
-    q31 *wpts[64];
-    unsigned wnv[64];
-    q31 wval[64];
-    size_t widx[64], nw = 0;
-    chain_deferred *defs = (chain_deferred *)calloc(64, sizeof(chain_deferred));
+    q31 **wpts = (q31 **)calloc(n_layers, sizeof(q31 *));
+    unsigned *wnv = (unsigned *)calloc(n_layers, sizeof(unsigned));
+    q31 *wval = (q31 *)calloc(n_layers, sizeof(q31));
+    size_t *widx = (size_t *)calloc(n_layers, sizeof(size_t)), nw = 0;
+    chain_deferred *defs = (chain_deferred *)calloc(n_layers, sizeof(chain_deferred));
     size_t nd = 0;
-    unsigned char skip[64] = {0};
+    unsigned char *skip = (unsigned char *)calloc(n_layers, 1);
     for (size_t li = n_layers; li-- > 0 && !rc;) {
         if (skip[li]) continue;
         n_proofs++;
@@ -3281,6 +3294,41 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             }
             free(tbuf);
             value = q_load(ie);
+        } else if (layers[li].type == 6) {
+            /* Activation (prover.rs:1765-1790): LogUp when flags bit 2 is set (the reference's
+             * STWO_PIECEWISE_ACTIVATION=0), else the piecewise-algebraic reduction */
+            const int tag = (int)layers[li].n, logup = (flags & 4) != 0;
+            const unsigned nv = ilog2(next_pow2(m) * next_pow2(w));
+            size_t tcap = (1 << 21) + 200 + 40 * (size_t)(nv + 2), tlen = 0;
+            uint64_t *tbuf = (uint64_t *)malloc(32 * tcap);
+            uint32_t cv[4], ie[4];
+            q31 nxt[64];
+            q_store(cv, value);
+            if (npt != nv)
+                rc = 1;
+            else if (logup)
+                rc = orc_reduce_activation_logup(x, m, w, tag, (const uint32_t *)point, npt, cv, &ch, tbuf, tcap,
+                                                 &tlen, ie);
+            else
+                rc = orc_reduce_activation_piecewise(x, m, w, tag, (const uint32_t *)point, npt, cv, &ch, tbuf,
+                                                     tcap, &tlen, ie, (uint32_t *)nxt);
+            /* on-chain layout (cairo_serde.rs:1862-1890): the LogUp proof without multiplicities */
+            const size_t mpos = 29 + 12 * (size_t)nv;
+            for (size_t i = 0; i < tlen && !rc; i++) {
+                if (v1 && logup && i == mpos) {
+                    out_u64(&lay, 0);
+                    i += (size_t)tbuf[4 * i];  /* skip the count's multiplicities */
+                    continue;
+                }
+                fe f;
+                fe_from_canon(&f, tbuf + 4 * i);
+                out_push(&lay, &f);
+            }
+            free(tbuf);
+            if (!rc) {
+                if (!logup) memcpy(point, nxt, sizeof(q31) * nv);
+                value = q_load(ie);
+            }
         } else if (layers[li].type == 1) {
             q31 nxt[64], nval;
             rc = relu_reduce(x, m, w, point, value, &ch, &lay, nxt, &nval, flags & 1);
@@ -3356,9 +3404,9 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     }
     /* deferred proofs of the skip branches, then their Sequential openings (prover.rs:1918-2047) */
     felt_out dsec = {(uint64_t *)malloc(32 * cap), 0, cap, 0};
-    fe dcoms[64];
-    uint64_t *dobufs[64] = {0};
-    size_t dolens[64];
+    fe *dcoms = (fe *)calloc(n_layers, sizeof(fe));
+    uint64_t **dobufs = (uint64_t **)calloc(n_layers, sizeof(uint64_t *));
+    size_t *dolens = (size_t *)calloc(n_layers, sizeof(size_t));
     out_u64(&dsec, nd);
     for (size_t i = 0; i < nd && !rc; i++) {
         chain_deferred *d = &defs[i];
@@ -3411,9 +3459,9 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     felt_out o = {calldata, 0, cap, 0};
     if (!rc) {
         /* Sequential weight openings of the walk on the main channel, in walk order */
-        fe coms[64];
-        uint64_t *obufs[64];
-        size_t olens[64];
+        fe *coms = (fe *)calloc(nw + 1, sizeof(fe));
+        uint64_t **obufs = (uint64_t **)calloc(nw + 1, sizeof(uint64_t *));
+        size_t *olens = (size_t *)calloc(nw + 1, sizeof(size_t));
         for (size_t i = 0; i < nw; i++) {
             size_t l = widx[i];
             size_t w = width[src[l] + 1];
@@ -3455,6 +3503,9 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
             }
         }
         for (size_t i = 0; i < nw; i++) free(obufs[i]);
+        free(coms);
+        free(obufs);
+        free(olens);
         orc_io_commitment(outs[0], m, k0, outs[n_layers], m, wout, io);
         if (!v1) {
             fe iof;
@@ -3471,6 +3522,17 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
     free(lay.buf);
     free(dsec.buf);
     free(defs);
+    free(outs);
+    free(width);
+    free(src);
+    free(wpts);
+    free(wnv);
+    free(wval);
+    free(widx);
+    free(skip);
+    free(dcoms);
+    free(dobufs);
+    free(dolens);
     if (rc) return rc;
     return overflow ? 2 : 0;
 }

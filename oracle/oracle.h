@@ -229,6 +229,9 @@ typedef struct {
  *     deferred proofs included), weight commitments (walk, then deferred), opening proofs.
  * flags bit 0: the earlier Activation record layout without the multiplicity-sumcheck and
  * piecewise flags (the layout of engine/tests/artifacts/sp3_mlp_proof.json).
+ * flags bit 2: Activation layers (type 6, tag in .n: 2 GELU, 3 Sigmoid, 4 Softmax, 5 SiLU)
+ * take the LogUp reduction (STWO_PIECEWISE_ACTIVATION=0); clear: the piecewise reduction
+ * (the reference's default), gkr/prover.rs:1765-1790.  At most 1024 layers.
  * Writes the final digest and the io commitment.  Returns 4 for a deferred branch that is
  * not a Linear layer (the reference's "deferred proof not yet supported"). */
 int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,

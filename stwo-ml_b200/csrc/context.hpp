@@ -122,6 +122,7 @@ struct zkml_ctx {
     zk::LogupScratch lu;
     zk::OpeningScratch op;
     zk::DevBuf gather_dev;          // gathered shards of the sharded product sumcheck
+    zk::DevBuf mesh_stage;          // this rank's contribution to a mesh gather
     uint8_t* h_stage = nullptr;     // pinned host staging for the sharded gather
     size_t h_stage_bytes = 0;
     // stepwise product-sumcheck session (zkml_sumcheck_*)

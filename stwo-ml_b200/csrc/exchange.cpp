@@ -8,8 +8,12 @@
 // sequence number with a release store, and reads the other slots once their
 // sequence numbers have arrived.  Slots are double-buffered by sequence parity,
 // which is enough because no rank can start exchange s + 2 before every rank
-// has finished exchange s + 1 (and so finished reading exchange s).  Every wait
-// is bounded.
+// has finished exchange s + 1 (and so finished reading exchange s): while a
+// rank waits for exchange s, a peer's slot holds either s - 2 or s, so the waits
+// test for equality.  A segment left behind by an earlier job under the same
+// name is told apart by the job nonce every rank passes in: rank 0 recreates the
+// segment and writes the nonce before marking it ready, and the other ranks
+// re-open the name until they see their own nonce.  Every wait is bounded.
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -42,6 +46,7 @@ struct alignas(64) ReduceSlot {
 struct Header {
     std::atomic<uint32_t> ready;  // set by rank 0 once the segment is initialised
     uint32_t world;
+    uint64_t nonce;               // the job's nonce, written by rank 0 before ready
     uint64_t gather_bytes;        // per rank per buffer
     std::atomic<uint64_t> gather_seq[2][kMaxRanks];
     std::atomic<uint32_t> closed[kMaxRanks];
@@ -65,7 +70,7 @@ struct Shm {
 
 bool wait_until(const std::atomic<uint64_t>& v, uint64_t want) {
     const auto t0 = std::chrono::steady_clock::now();
-    for (uint64_t it = 0; v.load(std::memory_order_acquire) < want; it++) {
+    for (uint64_t it = 0; v.load(std::memory_order_acquire) != want; it++) {
         if ((it & 255) == 255) {
             if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kTimeoutS)
                 return false;
@@ -112,7 +117,8 @@ int shm_allgather(void* user, const void* local, void* out, size_t bytes) {
 
 extern "C" {
 
-int zkml_shm_exchange_open(const char* name, int world, int rank, size_t max_gather_bytes, zkml_exchange* out) {
+int zkml_shm_exchange_open(const char* name, int world, int rank, size_t max_gather_bytes, uint64_t job_nonce,
+                           zkml_exchange* out) {
     if (!name || !out || world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
         return zk::set_error(ZKML_ERR_INVALID_ARG, "exchange: bad name, world or rank");
     Shm* s = new Shm;
@@ -121,58 +127,71 @@ int zkml_shm_exchange_open(const char* name, int world, int rank, size_t max_gat
     s->rank = rank;
     const size_t gb = (max_gather_bytes + 63) / 64 * 64;
     s->bytes = 4096 + 2 * kMaxRanks * sizeof(ReduceSlot) + 2 * (size_t)world * gb;
-    int fd = -1;
+    auto elapsed = [](std::chrono::steady_clock::time_point t) {
+        return std::chrono::duration<double>(std::chrono::steady_clock::now() - t).count();
+    };
+    const auto t0 = std::chrono::steady_clock::now();
     if (rank == 0) {
         shm_unlink(s->name.c_str());  // a stale segment of an earlier job
-        fd = shm_open(s->name.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
+        int fd = shm_open(s->name.c_str(), O_CREAT | O_EXCL | O_RDWR, 0600);
         if (fd >= 0 && ftruncate(fd, (off_t)s->bytes) != 0) {
             close(fd);
             fd = -1;
         }
-    } else {
-        const auto t0 = std::chrono::steady_clock::now();
-        while ((fd = shm_open(s->name.c_str(), O_RDWR, 0600)) < 0) {
-            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kTimeoutS) break;
-            std::this_thread::sleep_for(std::chrono::milliseconds(1));
+        void* p = fd >= 0 ? mmap(nullptr, s->bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0) : MAP_FAILED;
+        if (fd >= 0) close(fd);
+        if (p == MAP_FAILED) {
+            delete s;
+            return zk::set_error(ZKML_ERR_UNSUPPORTED, "exchange: cannot create the shared-memory segment");
         }
-        struct stat st;
-        // wait until rank 0 has sized the segment
-        const auto t1 = std::chrono::steady_clock::now();
-        while (fd >= 0 && fstat(fd, &st) == 0 && (size_t)st.st_size < s->bytes) {
-            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t1).count() > kTimeoutS) break;
-            std::this_thread::sleep_for(std::chrono::milliseconds(1));
-        }
-    }
-    if (fd < 0) {
-        delete s;
-        return zk::set_error(ZKML_ERR_UNSUPPORTED, "exchange: cannot open the shared-memory segment");
-    }
-    void* p = mmap(nullptr, s->bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
-    close(fd);
-    if (p == MAP_FAILED) {
-        delete s;
-        return zk::set_error(ZKML_ERR_UNSUPPORTED, "exchange: mmap failed");
-    }
-    s->base = static_cast<uint8_t*>(p);
-    Header* h = s->hdr();
-    if (rank == 0) {
+        s->base = static_cast<uint8_t*>(p);
+        Header* h = s->hdr();
         h->world = (uint32_t)world;
         h->gather_bytes = gb;
+        h->nonce = job_nonce;
         h->ready.store(1, std::memory_order_release);
     } else {
-        const auto t0 = std::chrono::steady_clock::now();
-        while (h->ready.load(std::memory_order_acquire) != 1) {
-            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > kTimeoutS) {
-                munmap(p, s->bytes);
+        // Open the name until it holds this job's initialised segment: a segment of an
+        // earlier job (other nonce) is unmapped and the name opened again.
+        for (;;) {
+            if (elapsed(t0) > kTimeoutS) {
                 delete s;
-                return zk::set_error(ZKML_ERR_TIMEOUT, "exchange: rank 0 did not initialise the segment");
+                return zk::set_error(ZKML_ERR_TIMEOUT, "exchange: rank 0 did not create this job's segment");
             }
+            int fd = shm_open(s->name.c_str(), O_RDWR, 0600);
+            if (fd < 0) {
+                std::this_thread::sleep_for(std::chrono::milliseconds(1));
+                continue;
+            }
+            struct stat st;
+            if (fstat(fd, &st) != 0 || (size_t)st.st_size < s->bytes) {
+                close(fd);
+                std::this_thread::sleep_for(std::chrono::milliseconds(1));
+                continue;
+            }
+            void* p = mmap(nullptr, s->bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+            close(fd);
+            if (p == MAP_FAILED) {
+                delete s;
+                return zk::set_error(ZKML_ERR_UNSUPPORTED, "exchange: mmap failed");
+            }
+            Header* h = reinterpret_cast<Header*>(p);
+            // give rank 0 a moment to finish initialising a fresh segment
+            const auto t1 = std::chrono::steady_clock::now();
+            while (h->ready.load(std::memory_order_acquire) != 1 && elapsed(t1) < 0.05)
+                std::this_thread::sleep_for(std::chrono::microseconds(200));
+            if (h->ready.load(std::memory_order_acquire) == 1 && h->nonce == job_nonce) {
+                if (h->world != (uint32_t)world || h->gather_bytes != gb) {
+                    munmap(p, s->bytes);
+                    delete s;
+                    return zk::set_error(ZKML_ERR_INVALID_ARG,
+                                         "exchange: ranks disagree on world size or gather size");
+                }
+                s->base = static_cast<uint8_t*>(p);
+                break;
+            }
+            munmap(p, s->bytes);  // not (yet) this job's segment
             std::this_thread::sleep_for(std::chrono::milliseconds(1));
-        }
-        if (h->world != (uint32_t)world || h->gather_bytes != gb) {
-            munmap(p, s->bytes);
-            delete s;
-            return zk::set_error(ZKML_ERR_INVALID_ARG, "exchange: ranks disagree on world size or gather size");
         }
     }
     out->user = s;

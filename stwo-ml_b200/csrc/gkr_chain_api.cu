@@ -39,6 +39,63 @@ __global__ void relu_forward_kernel(const uint32_t* __restrict__ x, size_t n, ui
     }
 }
 
+// ActivationType::as_fn (gadgets/lookup_table.rs:193-345) applied to full M31 values, as the
+// reference's forward pass does (compiler/prove.rs:1893-1899): fixed point with scale 2^16,
+// values above (P - 1) / 2 read as negative; GELU (tanh form) and SiLU in binary64, rounded
+// half away from zero and clamped to [0, P - 1] / [-(P - 1), 0]; Sigmoid a step; Softmax-exp a
+// shift.  The binary64 evaluation uses the device exp / tanh; they round to nearest within an
+// ulp of the host libm's, which decides a result only when x * 2^16 lands within ~1e-9 of a
+// half-integer.
+__device__ __forceinline__ double act_real(uint32_t v) {
+    return v <= 0x3FFFFFFFu ? (double)v / 65536.0 : -((double)((uint64_t)P - v)) / 65536.0;
+}
+__device__ __forceinline__ uint32_t act_from_real(double r) {
+    const uint64_t pm1 = (uint64_t)P - 1;
+    if (r >= 0.0) {
+        const uint64_t u = (uint64_t)round(r * 65536.0);
+        return (uint32_t)(u < pm1 ? u : pm1);
+    }
+    uint64_t neg = (uint64_t)round(-r * 65536.0);
+    if (neg > pm1) neg = pm1;
+    return (uint32_t)((uint64_t)P - neg);
+}
+__device__ uint32_t act_value(int tag, uint32_t v) {
+    switch (tag) {
+        case 2: {  // GELU
+            if (v == 0) return 0;
+            const double x = act_real(v);
+            const double c = sqrt(2.0 / 3.14159265358979311599796346854);
+            const double inner = __dmul_rn(c, __dadd_rn(x, __dmul_rn(__dmul_rn(__dmul_rn(0.044715, x), x), x)));
+            return act_from_real(__dmul_rn(__dmul_rn(0.5, x), __dadd_rn(1.0, tanh(inner))));
+        }
+        case 3:  // Sigmoid step
+            if (v > 0x3FFFFFFFu) return 0;
+            return v == 0 ? 32768u : 65536u;
+        case 4: {  // Softmax exp
+            if (v > 0x3FFFFFFFu) {
+                uint32_t decay = (((1u << 31) - 2) - v) / 65536u;
+                if (decay > 20) decay = 20;
+                const uint32_t r = 65536u >> decay;
+                return r > 1 ? r : 1;
+            }
+            if (v == 0) return 65536u;
+            uint32_t growth = v / 65536u;
+            if (growth > 10) growth = 10;
+            const uint64_t r = (uint64_t)65536u << growth, cap = (1ull << 31) - 2;
+            return (uint32_t)(r < cap ? r : cap);
+        }
+        default: {  // SiLU
+            if (v == 0) return 0;
+            const double x = act_real(v);
+            return act_from_real(__ddiv_rn(x, __dadd_rn(1.0, exp(-x))));
+        }
+    }
+}
+__global__ void act_forward_kernel(const uint32_t* __restrict__ x, size_t n, int tag, uint32_t* __restrict__ y) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = act_value(tag, red32(x[i]));
+}
+
 // Zero-padded row-major copy (rows x cols -> pr x pc) of an M31 matrix.
 __global__ void pad_rows_cols_kernel(const uint32_t* __restrict__ x, size_t rows, size_t cols, size_t pc, size_t n,
                                      uint32_t* __restrict__ y) {
@@ -141,6 +198,11 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
             width[l + 1] = layers[l].n;
         } else if (t == ZKML_LAYER_RELU || t == ZKML_LAYER_RMSNORM || t == ZKML_LAYER_LAYERNORM) {
             width[l + 1] = w;
+        } else if (t == ZKML_LAYER_ACTIVATION) {
+            if (layers[l].n < 2 || layers[l].n > 5)
+                return set_error(ZKML_ERR_INVALID_ARG, at + "Activation tag must be 2 (GELU), 3 (Sigmoid), 4 (Softmax) "
+                                                            "or 5 (SiLU); ReLU is ZKML_LAYER_RELU");
+            width[l + 1] = w;
         } else if (t == ZKML_LAYER_ADD || t == ZKML_LAYER_MUL) {
             if (layers[l].lhs < 0 || layers[l].lhs >= (long long)l || width[layers[l].lhs + 1] != w)
                 return set_error(ZKML_ERR_INVALID_ARG, at + "bad lhs layer (a lower layer of the same width)");
@@ -191,6 +253,10 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
             ctx->launches++;
         } else if (t == ZKML_LAYER_RELU) {
             relu_forward_kernel<<<blocks_for(m * w), 256, 0, s>>>(in_of(l), m * w, outs[l + 1].as<uint32_t>());
+            ctx->launches++;
+        } else if (t == ZKML_LAYER_ACTIVATION) {
+            act_forward_kernel<<<blocks_for(m * w), 256, 0, s>>>(in_of(l), m * w, (int)layers[l].n,
+                                                                 outs[l + 1].as<uint32_t>());
             ctx->launches++;
         } else {
             elementwise_kernel<<<blocks_for(m * w), 256, 0, s>>>(outs[layers[l].lhs + 1].as<uint32_t>(), in_of(l),
@@ -293,6 +359,40 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
                                            npt, cv, &chs, lay, ie, v1)))
                 return rc;
             value = qm(ie[0], ie[1], ie[2], ie[3]);  // the point is unchanged
+        } else if (t == ZKML_LAYER_ACTIVATION) {
+            // prover.rs:1765-1790: piecewise by default, LogUp under STWO_PIECEWISE_ACTIVATION=0
+            const bool logup = (flags & ZKML_CHAIN_ACTIVATION_LOGUP) != 0;
+            const int tag = (int)layers[li].n;
+            const unsigned nv = lg2(pm * np2(w));
+            if (npt != nv)
+                return set_error(ZKML_ERR_INVALID_ARG, "layer " + std::to_string(li) + ": claim point size mismatch");
+            const size_t tcap = (logup ? ((size_t)1 << (tag == 4 ? 20 : 16)) : 0) + 200 + 40 * (size_t)(nv + 2);
+            std::vector<uint64_t> tbuf(4 * tcap);
+            size_t tlen = 0;
+            uint32_t cv[4] = {value.a, value.b, value.c, value.d}, ie[4];
+            std::vector<qm31> nxt(64);
+            if (logup)
+                rc = zkml_reduce_activation_logup(ctx, in_of(li), m, w, tag,
+                                                  reinterpret_cast<const uint32_t*>(point.data()), npt, cv, &chs,
+                                                  tbuf.data(), tcap, &tlen, ie);
+            else
+                rc = zkml_reduce_activation_piecewise(ctx, in_of(li), m, w, tag,
+                                                      reinterpret_cast<const uint32_t*>(point.data()), npt, cv, &chs,
+                                                      tbuf.data(), tcap, &tlen, ie,
+                                                      reinterpret_cast<uint32_t*>(nxt.data()));
+            if (rc) return rc;
+            // the on-chain record (cairo_serde.rs:1862-1890) drops the LogUp multiplicities
+            const size_t mpos = 29 + 12 * (size_t)nv;
+            for (size_t i = 0; i < tlen; i++) {
+                if (v1 && logup && i == mpos) {
+                    lay.u64(0);
+                    i += (size_t)tbuf[4 * i];
+                    continue;
+                }
+                lay.push(&tbuf[4 * i]);
+            }
+            if (!logup) memcpy(point.data(), nxt.data(), 16 * nv);
+            value = qm(ie[0], ie[1], ie[2], ie[3]);
         } else if (t == ZKML_LAYER_RELU) {
             std::vector<qm31> nxt(64);
             qm31 nval;

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "mesh.cuh"
 #include "qm31.cuh"
 
 namespace zk {
@@ -56,6 +57,9 @@ struct RoundScratch {
     // spin on sig[0] instead of synchronising the stream.
     uint32_t* sig;
     uint32_t seq;
+    // Optional peer mesh (launch_round_m31, launch_fold_round_m31 / _qm31, launch_round_qm31):
+    // the last block adds every rank's 12 words before it stores or publishes them.
+    MeshArg mesh{nullptr, 0};
 };
 // Reduce n u32 words in place to [0, P) (the round kernels need canonical QM31 input).
 void launch_canon_words(uint32_t* w, size_t n, cudaStream_t s);

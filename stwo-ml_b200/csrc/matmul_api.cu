@@ -722,6 +722,7 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
     ctx->lu.release();
     ctx->op.release();
     ctx->gather_dev.release();
+    ctx->mesh_stage.release();
     if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
     ctx->sc_a.release();
     ctx->sc_b.release();

@@ -28,6 +28,8 @@ struct P2PState {
     size_t words = 0;                // u64 words per slot (4 k)
     void* own = nullptr;             // this rank's inbox allocation
     std::vector<uint8_t*> peers;     // every rank's inbox (own included), as mapped here
+    uint32_t scattered = 0;          // epoch of this rank's last scatter
+    uint32_t gathered = 0;           // epoch of this rank's last gather
 };
 
 std::vector<P2PState>& states() {
@@ -167,6 +169,13 @@ int zkml_restrict_cols_block_p2p(zkml_ctx* ctx, const uint32_t* b_block, size_t 
     if (!st.own || st.words != 4 * k) return set_error(ZKML_ERR_INVALID_ARG, "p2p inbox not created for this k");
     for (int r = 0; r < st.world; r++)
         if (!st.peers[r]) return set_error(ZKML_ERR_INVALID_ARG, "p2p peers not opened");
+    // The flags start at 0, so epoch 0 would pass every wait at once; and the parity double
+    // buffer is safe only if call e + 1's scatter follows call e's gather on this context.
+    if (epoch == 0 || epoch != st.gathered + 1 || st.scattered != st.gathered)
+        return set_error(ZKML_ERR_INVALID_ARG, "p2p scatter: epochs start at 1 and go up by one per call, each "
+                                               "call's scatter after the previous call's gather (expected " +
+                                                   std::to_string(st.gathered + 1) + ", got " +
+                                                   std::to_string(epoch) + ")");
     int rc;
     if ((rc = ctx->acc_b.ensure(k * 32))) return rc;
     unsigned long long* acc = ctx->acc_b.as<unsigned long long>();
@@ -185,6 +194,7 @@ int zkml_restrict_cols_block_p2p(zkml_ctx* ctx, const uint32_t* b_block, size_t 
     p2p_scatter_kernel<<<g, 256, 0, ctx->stream>>>(acc, words, pp, st.world, st.rank, epoch, ticket, flags_off);
     ctx->launches++;
     ZK_CUDA(cudaGetLastError());
+    st.scattered = epoch;
     return ZKML_OK;
 }
 
@@ -195,6 +205,10 @@ int zkml_reduce_matmul_layer_gkr_p2p(zkml_ctx* ctx, const uint32_t* claim_point,
     if (!ctx) return set_error(ZKML_ERR_INVALID_ARG, "NULL argument");
     P2PState& st = states()[ctx->device % 64];
     if (!st.own || st.words != 4 * k) return set_error(ZKML_ERR_INVALID_ARG, "p2p inbox not created for this k");
+    if (epoch == 0 || epoch != st.scattered || st.gathered + 1 != epoch)
+        return set_error(ZKML_ERR_INVALID_ARG, "p2p gather: epoch must be the one this rank scattered last (" +
+                                                   std::to_string(st.scattered) + "), got " + std::to_string(epoch));
+    st.gathered = epoch;
     int rc;
     if ((rc = ctx->acc_a.ensure(k * 32))) return rc;  // acc_a is free until the layer's row restriction
     DevBuf& words = ctx->op.gpart;

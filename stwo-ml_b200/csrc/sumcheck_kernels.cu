@@ -611,8 +611,9 @@ __device__ __forceinline__ void publish(uint32_t* sig, uint32_t seq, const uint3
 }
 
 // Block-reduce the 12 lazily accumulated words and finish the grid reduction.
+// With a peer mesh, the grid's result is summed over the ranks before it is stored.
 __device__ void finish_sums(Sums& s, uint32_t* __restrict__ partials, unsigned int* __restrict__ ticket,
-                            uint32_t* __restrict__ out, uint32_t* sig, uint32_t seq) {
+                            uint32_t* __restrict__ out, uint32_t* sig, uint32_t seq, MeshArg mesh = {nullptr, 0}) {
     __shared__ uint32_t sh[32][12];
     __shared__ uint32_t res[12];
     __shared__ bool is_last;
@@ -645,14 +646,13 @@ __device__ void finish_sums(Sums& s, uint32_t* __restrict__ partials, unsigned i
         uint32_t v = red64(acc);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if (lane == 0) {
-            out[i] = v;
-            res[i] = v;
-        }
+        if (lane == 0) res[i] = v;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         *ticket = 0;
+        if (mesh.desc) mesh_allreduce12(res, mesh);
+        for (int i = 0; i < 12; i++) out[i] = res[i];
         if (sig) publish(sig, seq, res, 12);
     }
 }
@@ -671,14 +671,14 @@ __device__ __forceinline__ void racc_to_sums(const RoundAcc& r, Sums& s) {
 
 __global__ void __launch_bounds__(256) round_qm31_kernel(const uint4* __restrict__ A, const uint4* __restrict__ B,
                                                          size_t q, uint32_t* partials, unsigned int* ticket,
-                                                         uint32_t* out, uint32_t* sig, uint32_t seq) {
+                                                         uint32_t* out, uint32_t* sig, uint32_t seq, MeshArg mesh) {
     RoundAcc acc;
     racc_zero(acc);
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < q; i += (size_t)gridDim.x * blockDim.x)
         racc_add(acc, ld_q(A + i), ld_q(A + i + q), ld_q(B + i), ld_q(B + i + q));
     Sums s;
     racc_to_sums(acc, s);
-    finish_sums(s, partials, ticket, out, sig, seq);
+    finish_sums(s, partials, ticket, out, sig, seq, mesh);
 }
 
 // In-place fold with alpha fused with the next round's sums.  Thread i reads
@@ -709,7 +709,7 @@ __device__ __forceinline__ qm31 u2q(const uint4& v) { return qm(v.x, v.y, v.z, v
 __global__ void __launch_bounds__(256, 2) fold_round_qm31_kernel(uint4* __restrict__ A, uint4* __restrict__ B,
                                                                  size_t h, const AlphaRows m, uint32_t* partials,
                                                                  unsigned int* ticket, uint32_t* out, uint32_t* sig,
-                                                                 uint32_t seq) {
+                                                                 uint32_t seq, MeshArg mesh) {
     const size_t q = h / 2, stride = (size_t)gridDim.x * blockDim.x;
     RoundAcc acc;
     racc_zero(acc);
@@ -732,7 +732,7 @@ __global__ void __launch_bounds__(256, 2) fold_round_qm31_kernel(uint4* __restri
     }
     Sums s;
     racc_to_sums(acc, s);
-    finish_sums(s, partials, ticket, out, sig, seq);
+    finish_sums(s, partials, ticket, out, sig, seq, mesh);
 }
 
 // Base-field round: products of M31 values accumulate lazily (acc_fold).  Any
@@ -742,7 +742,8 @@ __global__ void __launch_bounds__(256, 2) fold_round_qm31_kernel(uint4* __restri
 template <int VEC>
 __global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restrict__ A, const uint32_t* __restrict__ B,
                                                         size_t q, uint32_t* partials, unsigned int* ticket,
-                                                        uint32_t* out, uint32_t* err, uint32_t* sig, uint32_t seq) {
+                                                        uint32_t* out, uint32_t* err, uint32_t* sig, uint32_t seq,
+                                                        MeshArg mesh) {
     uint64_t s0 = 0, s1 = 0, s2 = 0;
     uint32_t bad = 0;
     const size_t nq = q / VEC;
@@ -774,7 +775,7 @@ __global__ void __launch_bounds__(256) round_m31_kernel(const uint32_t* __restri
     s.v[0] = canon64(s0);
     s.v[4] = canon64(s1);
     s.v[8] = canon64(s2);
-    finish_sums(s, partials, ticket, out, sig, seq);
+    finish_sums(s, partials, ticket, out, sig, seq, mesh);
 }
 
 // lo + alpha (hi - lo) with lo, hi in M31.
@@ -794,7 +795,7 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
                                                              const uint32_t* __restrict__ B, size_t h, qm31 alpha,
                                                              uint4* __restrict__ Ao, uint4* __restrict__ Bo,
                                                              uint32_t* partials, unsigned int* ticket, uint32_t* out,
-                                                             uint32_t* sig, uint32_t seq) {
+                                                             uint32_t* sig, uint32_t seq, MeshArg mesh) {
     const size_t q = h / 2;
     const size_t tile = (size_t)FR_UNROLL * blockDim.x;
     RoundAcc acc;
@@ -826,7 +827,7 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
     }
     Sums s;
     racc_to_sums(acc, s);
-    finish_sums(s, partials, ticket, out, sig, seq);
+    finish_sums(s, partials, ticket, out, sig, seq, mesh);
 }
 
 // ---------------------------------------------------------------------------
@@ -1268,14 +1269,14 @@ static unsigned round_blocks(size_t work, int max_blocks) {
 void launch_round_qm31(uint4* A, uint4* B, size_t len, const RoundScratch& rs, cudaStream_t s) {
     const size_t q = len / 2;
     round_qm31_kernel<<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out, rs.sig,
-                                                                                  rs.seq);
+                                                                      rs.seq, rs.mesh);
 }
 
 void launch_fold_round_qm31(uint4* A, uint4* B, size_t len, qm31 alpha, const RoundScratch& rs, cudaStream_t s) {
     const size_t h = len / 2;
     fold_round_qm31_kernel<<<round_blocks(h / 2, rs.max_blocks), 256, 0, s>>>(A, B, h, alpha_rows(alpha),
                                                                                 rs.partials, rs.ticket, rs.out,
-                                                                                rs.sig, rs.seq);
+                                                                                rs.sig, rs.seq, rs.mesh);
 }
 
 void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const RoundScratch& rs, uint32_t* err,
@@ -1283,17 +1284,17 @@ void launch_round_m31(const uint32_t* A, const uint32_t* B, size_t len, const Ro
     const size_t q = len / 2;
     if (q % 4 == 0 && aligned16(A) && aligned16(B))
         round_m31_kernel<4><<<round_blocks(q / 4, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket,
-                                                                               rs.out, err, rs.sig, rs.seq);
+                                                                               rs.out, err, rs.sig, rs.seq, rs.mesh);
     else
         round_m31_kernel<1><<<round_blocks(q, rs.max_blocks), 256, 0, s>>>(A, B, q, rs.partials, rs.ticket, rs.out,
-                                                                           err, rs.sig, rs.seq);
+                                                                           err, rs.sig, rs.seq, rs.mesh);
 }
 
 void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm31 alpha, uint4* Ao, uint4* Bo,
                            const RoundScratch& rs, cudaStream_t s) {
     const size_t h = len / 2;
     fold_round_m31_kernel<<<round_blocks((h / 2 + FR_UNROLL - 1) / FR_UNROLL, rs.max_blocks), 256, 0, s>>>(
-        A, B, h, alpha, Ao, Bo, rs.partials, rs.ticket, rs.out, rs.sig, rs.seq);
+        A, B, h, alpha, Ao, Bo, rs.partials, rs.ticket, rs.out, rs.sig, rs.seq, rs.mesh);
 }
 
 __global__ void final_fold_kernel(const uint4* A, const uint4* B, const uint32_t* A32, const uint32_t* B32,

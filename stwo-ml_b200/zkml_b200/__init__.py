@@ -130,6 +130,12 @@ _SIGS = {
     "zkml_p2p_inbox_create": (C.c_int, [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_void_p]),
     "zkml_p2p_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     "zkml_p2p_close": (C.c_int, [C.c_void_p]),
+    "zkml_mesh_create": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p]),
+    "zkml_mesh_open": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "zkml_mesh_close": (C.c_int, [C.c_void_p]),
+    "zkml_prove_product_sharded_mesh": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
+                                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                  C.c_void_p]),
     "zkml_restrict_cols_block_p2p": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t,
                                                C.c_void_p, C.c_size_t, C.c_uint32]),
     "zkml_reduce_matmul_layer_gkr_p2p": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, _u32, C.c_void_p,
@@ -149,7 +155,7 @@ _SIGS = {
     "zkml_selftest_wait_timeout": (C.c_int, [C.c_void_p, _u32]),
     "zkml_matmul_m31": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t,
                                   C.c_void_p]),
-    "zkml_shm_exchange_open": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_size_t, C.c_void_p]),
+    "zkml_shm_exchange_open": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_size_t, C.c_uint64, C.c_void_p]),
     "zkml_shm_exchange_close": (C.c_int, [C.c_void_p]),
     "zkml_prove_product_sharded": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t, C.c_void_p,
                                              C.c_void_p, _u32, _u32, _u32, _u32, C.POINTER(C.c_size_t)]),
@@ -743,7 +749,19 @@ class _ChainLayer(C.Structure):
 
 
 CHAIN_PREV = -2
-_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layernorm": 5}
+_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layernorm": 5, "activation": 6}
+# ActivationType::type_tag (components/activation.rs:50-60) of the non-ReLU activations
+ACTIVATION_TAGS = {"gelu": 2, "sigmoid": 3, "softmax": 4, "silu": 5}
+CHAIN_ACTIVATION_LOGUP = 4
+
+
+def piecewise_activation_enabled() -> bool:
+    """STWO_PIECEWISE_ACTIVATION as the reference reads it (components/activation.rs:365-373):
+    on unless set to 0 / false / no / off."""
+    v = os.environ.get("STWO_PIECEWISE_ACTIVATION")
+    if v is None:
+        return True
+    return v.strip().lower() not in ("0", "false", "no", "off")
 
 
 @dataclass
@@ -759,15 +777,16 @@ class GKRChainProof:
 
 def _chain_args(inp, layers, n_queries):
     """ctypes layer array, buffers to keep alive and a calldata capacity for `layers`, each
-    (kind, arg[, src]): ("linear", weight (in_width, n)), ("relu", None), ("rmsnorm", None), ("layernorm", None),
-    ("add", lhs_layer), ("mul", lhs_layer); src = the layer feeding this one (None: the
-    previous layer, -1: the model input).  The Add / Mul rhs operand is src's output."""
+    (kind, arg[, src]): ("linear", weight (in_width, n)), ("relu", None), ("activation", type: "silu" /
+    "gelu" / "sigmoid" / "softmax" or its tag), ("rmsnorm", None), ("layernorm", None), ("add", lhs_layer),
+    ("mul", lhs_layer); src = the layer feeding this one (None: the previous layer, -1: the model
+    input).  The Add / Mul rhs operand is src's output."""
     im = as_matrix(inp)
     ib = _Buf(im.data)
     keep = [ib]
     arr = (_ChainLayer * len(layers))()
     widths = [im.cols]  # widths[l + 1]: layer l's output width; widths[0]: the input's
-    nv_max, n_lin, n_bin = 0, 0, 0
+    nv_max, n_lin, n_bin, n_act_mult = 0, 0, 0, 0
     for i, spec in enumerate(layers):
         kind, arg = spec[0], spec[1]
         src = spec[2] if len(spec) > 2 and spec[2] is not None else CHAIN_PREV
@@ -791,6 +810,12 @@ def _chain_args(inp, layers, n_queries):
         elif kind in ("add", "mul"):
             arr[i].lhs = int(arg)
             n_bin += 1
+        elif kind == "activation":
+            tag = ACTIVATION_TAGS[arg.lower()] if isinstance(arg, str) else int(arg)
+            if tag not in ACTIVATION_TAGS.values():
+                raise InvalidArgument(1, f"layer {i}: activation must be GELU, Sigmoid, Softmax or SiLU")
+            arr[i].n = tag
+            n_act_mult += 1 << (20 if tag == 4 else 16)
         widths.append(width)
     nq = mle_n_queries() if n_queries is None else n_queries
     nv_all = _log2(_next_pow2(im.rows)) + max(nv_max, max(_log2(_next_pow2(w)) for w in widths) + 1)
@@ -798,17 +823,21 @@ def _chain_args(inp, layers, n_queries):
     per_open = 64 + (nq + 1) * (2 + nv_max * (10 + 2 * (nv_max + 1)))
     cap = 256 + len(layers) * (200 + 12 * nv_all) + (n_lin + n_bin) * per_open + n_bin * (60 + 16 * nv_all)
     cap += n_norm * ((1 << 16) + 2 * _next_pow2(im.rows) + 200 + 60 * (nv_all + 2))
-    cap += 2 * im.rows * max(widths)
+    cap += 2 * im.rows * max(widths) + n_act_mult
     return im, ib, arr, keep, nq, cap
 
 
 def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_queries: Optional[int] = None,
                     legacy_activation_record: bool = False, v1_layout: bool = False,
-                    device: int = 0) -> GKRChainProof:
+                    device: int = 0, activation_logup: Optional[bool] = None) -> GKRChainProof:
     """prove_gkr (gkr/prover.rs:1500-2251) for GraphBuilder::new(inp.shape) followed by `layers`
     (see _chain_args; Add / Mul layers defer their skip branch), Sequential weight binding.
     raw: serialize_gkr_model_proof, or with v1_layout the verify_model_gkr calldata from
-    proof_data on (deferred proofs and their openings included)."""
+    proof_data on (deferred proofs and their openings included).  Activation layers take the
+    LogUp reduction when activation_logup is true, the piecewise one when false; None follows
+    STWO_PIECEWISE_ACTIVATION as the reference does (prover.rs:1765-1790)."""
+    if activation_logup is None:
+        activation_logup = not piecewise_activation_enabled()
     im, ib, arr, keep, nq, cap = _chain_args(inp, layers, n_queries)
     out = np.empty(4 * cap, np.uint64)  # the library writes every reported felt
     ln = C.c_size_t(0)
@@ -816,13 +845,14 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
     io = np.zeros(4, np.uint64)
     pol = felt_to_limbs(policy_commitment) if policy_commitment else None
     flags = (1 if legacy_activation_record else 0) | (2 if v1_layout else 0)
+    flags |= CHAIN_ACTIVATION_LOGUP if activation_logup else 0
     _check(lib().zkml_prove_gkr_chain(context(device).handle, ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
                                       len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq,
                                       flags, out, cap, C.byref(ln), dig, io))
     return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
 
 
-_DESCRIPTOR_TAGS = {"linear": 0, "add": 1, "mul": 2, "relu": 3, "layernorm": 4, "rmsnorm": 8}
+_DESCRIPTOR_TAGS = {"linear": 0, "add": 1, "mul": 2, "relu": 3, "activation": 3, "layernorm": 4, "rmsnorm": 8}
 
 
 def circuit_descriptor(layers) -> List[int]:
@@ -858,10 +888,13 @@ def verify_calldata_weight_commitments(calldata: Sequence[int], layers) -> List[
 
 
 def build_verify_model_gkr_calldata(model_id: int, inp, layers, policy_commitment: Optional[int] = None,
-                                    n_queries: Optional[int] = None, device: int = 0) -> GKRChainProof:
+                                    n_queries: Optional[int] = None, device: int = 0,
+                                    activation_logup: Optional[bool] = None) -> GKRChainProof:
     """build_verify_model_gkr_calldata (starknet.rs:2837-2852): the proof of the circuit and the
     whole verify_model_gkr(model_id, raw_io_data, circuit_depth, num_layers, matmul_dims,
     dequantize_bits, proof_data, weight_commitments, weight_opening_proofs) calldata."""
+    if activation_logup is None:
+        activation_logup = not piecewise_activation_enabled()
     im, ib, arr, keep, nq, cap = _chain_args(inp, layers, n_queries)
     out = np.empty(4 * cap, np.uint64)
     ln = C.c_size_t(0)
@@ -870,8 +903,8 @@ def build_verify_model_gkr_calldata(model_id: int, inp, layers, policy_commitmen
     pol = felt_to_limbs(policy_commitment) if policy_commitment else None
     _check(lib().zkml_build_verify_model_gkr_calldata(
         context(device).handle, felt_to_limbs(model_id), ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
-        len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq, 0, out, cap, C.byref(ln), dig,
-        io))
+        len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq,
+        CHAIN_ACTIVATION_LOGUP if activation_logup else 0, out, cap, C.byref(ln), dig, io))
     return GKRChainProof(out[:4 * ln.value], limbs_to_felt(dig), limbs_to_felt(io))
 
 

@@ -39,12 +39,31 @@ class ExchangeStruct(C.Structure):
                 ("world", C.c_int), ("rank", C.c_int)]
 
 
-class ShmExchange:
-    """The library's shared-memory exchange between the ranks (processes) of one node."""
+def job_nonce(group=None) -> int:
+    """A 64-bit value that is the same on every rank of the process group and new for each
+    call: rank 0 draws it and broadcasts it (a single process draws its own)."""
+    import secrets
+    import torch
+    import torch.distributed as dist
+    v = secrets.randbits(63)
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dev = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
+        t = torch.tensor([v], dtype=torch.int64, device=dev)
+        dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        v = int(t.item())
+    return v
 
-    def __init__(self, name: str, world: int, rank: int, max_gather_bytes: int = 64 << 20):
+
+class ShmExchange:
+    """The library's shared-memory exchange between the ranks (processes) of one node.
+
+    `nonce` must be equal on all ranks and new per job (see `job_nonce`); it keeps a rank
+    from joining a segment that an earlier job left under the same name."""
+
+    def __init__(self, name: str, world: int, rank: int, max_gather_bytes: int = 64 << 20, *, nonce: int):
         self.struct = ExchangeStruct()
-        _check(lib().zkml_shm_exchange_open(name.encode(), world, rank, max_gather_bytes, C.byref(self.struct)))
+        _check(lib().zkml_shm_exchange_open(name.encode(), world, rank, max_gather_bytes, nonce & (2**64 - 1),
+                                            C.byref(self.struct)))
         self.world, self.rank = world, rank
 
     def allreduce(self, words) -> np.ndarray:
@@ -134,6 +153,64 @@ def prove_product_sharded_native(a_local, b_local, n: int, channel: PoseidonChan
                                             C.byref(gathered)))
     polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_n)]
     return ShardedSumcheckProof(polys, ch[:log_n].copy(), fa, fb, int(gathered.value))
+
+class PeerMesh:
+    """The library's peer-memory mesh (zkml_mesh_*): this rank's inbox in HBM, mapped by every
+    rank of `group` through CUDA IPC handles exchanged over the process group.  The round words
+    and the gather of the sharded product sumcheck then travel as peer stores over NVLink
+    inside the library's kernels.  The ranks must be on distinct GPUs of one node.
+    max_gather_bytes bounds one rank's share of a gather (32 x gather_local bytes)."""
+
+    def __init__(self, group=None, ctx: Optional[Context] = None, max_gather_bytes: int = 32 << 17):
+        import torch
+        import torch.distributed as dist
+        self.ctx = ctx or context(torch.cuda.current_device())
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        h = (C.c_uint8 * 64)()
+        _check(lib().zkml_mesh_create(self.ctx.handle, self.world, self.rank, max_gather_bytes, h))
+        hs, devs = [bytes(h)], [str(torch.cuda.get_device_properties(self.ctx.device).uuid)]
+        if self.world > 1:
+            devs = [None] * self.world
+            dist.all_gather_object(devs, str(torch.cuda.get_device_properties(self.ctx.device).uuid), group=group)
+            if len(set(devs)) != self.world:
+                lib().zkml_mesh_close(self.ctx.handle)
+                raise ValueError("PeerMesh ranks must be on distinct GPUs")
+            hs = [None] * self.world
+            dist.all_gather_object(hs, bytes(h), group=group)
+        allh = (C.c_uint8 * (64 * self.world)).from_buffer_copy(b"".join(hs))
+        _check(lib().zkml_mesh_open(self.ctx.handle, allh, self.world))
+        if self.world > 1:
+            dist.barrier(group=group)
+        self.closed = False
+
+    def close(self) -> None:
+        if not self.closed:
+            lib().zkml_mesh_close(self.ctx.handle)
+            self.closed = True
+
+
+def prove_product_sharded_mesh(a_local, b_local, n: int, channel: PoseidonChannel, mesh: PeerMesh,
+                               gather_local: Optional[int] = None) -> "ShardedSumcheckProof":
+    """prove_product_sharded_native with the exchange over the peer mesh
+    (zkml_prove_product_sharded_mesh): each split round's words are added across the ranks
+    inside the round kernel and the folded vectors are gathered by peer stores."""
+    if gather_local is None:
+        gather_local = max(2, (1 << 17) // mesh.world)
+    ab, bb = _Buf(a_local), _Buf(b_local)
+    log_n = n.bit_length() - 1
+    rp = np.zeros((max(log_n, 1), 12), np.uint32)
+    ch = np.zeros((max(log_n, 1), 4), np.uint32)
+    fa = np.zeros(4, np.uint32)
+    fb = np.zeros(4, np.uint32)
+    gathered = C.c_size_t(0)
+    _check(lib().zkml_prove_product_sharded_mesh(mesh.ctx.handle, ab.ptr, bb.ptr, n, gather_local,
+                                                 C.byref(channel.state), rp.ctypes.data, ch.ctypes.data,
+                                                 fa.ctypes.data, fb.ctypes.data, C.byref(gathered)))
+    polys = [RoundPoly(rp[r, 0:4].copy(), rp[r, 4:8].copy(), rp[r, 8:12].copy()) for r in range(log_n)]
+    return ShardedSumcheckProof(polys, ch[:log_n].copy(), fa, fb, int(gathered.value))
+
 
 INV2 = (P + 1) // 2
 

@@ -39,13 +39,15 @@ reference's own known answers for the matmul-sumcheck path:
   (Poseidon252Channel::mix_u64(0x1111222233334444) from the zero digest,
   i.e. poseidon_hash(0, 0x1111222233334444)).
 
-Usage: python tests/golden/make_golden.py [reference root]
+Usage: python tests/golden/make_golden.py <reference root>
 """
 import json
 import sys
 from pathlib import Path
 
-ref = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) != 2:
+    sys.exit("usage: make_golden.py <reference checkout root>")
+ref = Path(sys.argv[1])
 art = json.loads((ref / "engine/tests/artifacts/sp3_matmul_only_proof.json").read_text())
 mlp = json.loads((ref / "engine/tests/artifacts/sp3_mlp_proof.json").read_text())
 d11_summary = json.loads((ref / "engine/tests/artifacts/d11_onchain_summary.json").read_text())

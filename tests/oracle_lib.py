@@ -331,6 +331,15 @@ def evaluate_mle(evals, point) -> np.ndarray:
     return out
 
 
+def restrict_mle(evals, assign) -> np.ndarray:
+    """restrict_mle (backend.rs:199-215): fix the first len(assign) variables."""
+    evals = np.ascontiguousarray(evals, np.uint32).reshape(-1, 4)
+    assign = np.ascontiguousarray(assign, np.uint32).reshape(-1, 4)
+    out = np.zeros((len(evals) >> len(assign), 4), np.uint32)
+    lib().orc_restrict_mle(evals.reshape(-1), len(evals), assign.reshape(-1), len(assign), out.reshape(-1))
+    return out
+
+
 def piecewise_coeffs(tag):
     sl, ic = np.zeros(16, np.uint32), np.zeros(16, np.uint32)
     assert lib().orc_piecewise_coeffs(tag, sl, ic) == 0
@@ -367,7 +376,8 @@ class ChainLayer(C.Structure):
 
 
 CHAIN_PREV = -2
-_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layernorm": 5}
+_CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layernorm": 5, "activation": 6}
+_ACT_TAGS = {"gelu": 2, "sigmoid": 3, "softmax": 4, "silu": 5}
 
 
 def chain_layers(layers):
@@ -386,10 +396,13 @@ def chain_layers(layers):
             arr[i].weight, arr[i].n = w.ctypes.data, w.shape[1]
         elif kind in ("add", "mul"):
             arr[i].lhs = int(arg)
+        elif kind == "activation":
+            arr[i].n = _ACT_TAGS[arg.lower()] if isinstance(arg, str) else int(arg)
     return arr, keep
 
 
-def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, v1_layout=False, cap=1 << 20):
+def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False, v1_layout=False, cap=1 << 20,
+                    activation_logup=False):
     """layers: see chain_layers.  v1_layout: the verify_model_gkr calldata from proof_data on."""
     inp = np.ascontiguousarray(inp, np.uint32)
     m, k0 = inp.shape
@@ -401,7 +414,8 @@ def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False,
     pol = None if policy is None else felt(policy)
     rc = lib().orc_prove_gkr_chain(inp.reshape(-1), m, k0, C.cast(arr, C.c_void_p), len(layers),
                                    None if pol is None else pol.ctypes.data_as(C.c_void_p), n_queries,
-                                   int(legacy_layout) | (2 if v1_layout else 0), buf, cap,
+                                   int(legacy_layout) | (2 if v1_layout else 0) | (4 if activation_logup else 0),
+                                   buf, cap,
                                    C.byref(ln), dig, io, threads())
     return rc, buf[:4 * ln.value].copy(), felt_int(dig), felt_int(io)
 

@@ -45,8 +45,9 @@ def _worker(rank, world, port, n, gather_local, out_dir, mode="python"):
                                           gather_local=gather_local)
         else:
             from zkml_b200 import context
-            from zkml_b200.distributed import ShmExchange, TorchExchange, prove_product_sharded_native
-            ex = (ShmExchange(f"zkml_nccl_t_{port}", world, rank, max_gather_bytes=32 * (n // world)) if mode == "shm"
+            from zkml_b200.distributed import ShmExchange, TorchExchange, job_nonce, prove_product_sharded_native
+            ex = (ShmExchange(f"zkml_nccl_t_{port}", world, rank, max_gather_bytes=32 * (n // world),
+                              nonce=job_nonce()) if mode == "shm"
                   else TorchExchange())
             proof = prove_product_sharded_native(la, lb, n, PoseidonChannel(), ex, gather_local=gather_local,
                                                  ctx=context(rank))

@@ -57,7 +57,7 @@ def _native_worker(rank, world, name, n, gather_local, out_dir):
     sys.path[:0] = [str(ROOT), str(ROOT / "tests"), str(ROOT / "stwo-ml_b200")]
     from zkml_b200 import PoseidonChannel
     from zkml_b200.distributed import ShmExchange, prove_product_sharded_native, shard_of
-    ex = ShmExchange(name, world, rank, max_gather_bytes=max(1 << 16, 32 * (n // world)))
+    ex = ShmExchange(name, world, rank, max_gather_bytes=max(1 << 16, 32 * (n // world)), nonce=int(name[-12:], 16))
     try:
         a = uniform_m31(n, 11)
         b = uniform_m31(n, 12)

@@ -2,15 +2,19 @@
 
 It exists for callers that cannot allocate GPU memory; its scratch is a fixed
 array inside the library.  Checked through the C ABI against the existing
-ZkmlOps::restrict_mle entry point applied to the column-major padded MLE of
-the same matrix -- the same f_b, bit for bit -- on two calls in a row (the
-shared array keeps the first call's contents, which the second must not see).
+ZkmlOps::restrict_mle entry point and against the CPU oracle's restrict_mle
+(backend.rs:199-215), both applied to the column-major padded MLE of the same
+matrix -- the same f_b, bit for bit -- on two calls in a row (the shared array
+keeps the first call's contents, which the second must not see).  The shapes
+cover a column count below 64 (no high eq variables) and one above 65536 (the
+high eq table no longer fits the kernel's shared-memory copy).
 Collected last so that a run stopping at the first failure has run everything
 else first.
 """
 import numpy as np
 import pytest
 
+import oracle_lib as O
 import zkml_b200 as Z
 from helpers import int_matrix_m31, log2, next_pow2, random_qm31, uniform_m31
 
@@ -28,6 +32,10 @@ def colmajor_padded_mle(b):
 def reference_restriction(b, r_j):
     # existing entry point: ZkmlOps::restrict_mle on the column-major MLE
     return Z.GpuBackend(0).restrict_mle(colmajor_padded_mle(b), r_j)
+
+
+def oracle_restriction(b, r_j):
+    return O.restrict_mle(colmajor_padded_mle(b), r_j)
 
 
 def run_noalloc(b, r_j):
@@ -48,8 +56,19 @@ def test_noalloc_restriction_matches_existing_entry_twice():
     r2 = random_qm31(log2(next_pow2(1000)), rng)
     got1 = run_noalloc(b1, r1)
     got2 = run_noalloc(b2, r2)
-    assert (got1 == reference_restriction(b1, r1)).all()
-    assert (got2 == reference_restriction(b2, r2)).all()
+    for b, r, got in ((b1, r1, got1), (b2, r2, got2)):
+        want = oracle_restriction(b, r)
+        assert (got == want).all()
+        assert (got == reference_restriction(b, r)).all()
+
+
+@pytest.mark.parametrize("rows,cols,seed", [(5, 37, 81), (4, 70000, 82), (3, 1, 83)])
+def test_noalloc_narrow_and_wide_columns(rows, cols, seed):
+    rng = np.random.default_rng(seed)
+    b = uniform_m31(rows * cols, seed).reshape(rows, cols)
+    r = random_qm31(log2(next_pow2(cols)), rng)
+    for _ in range(2):
+        assert (run_noalloc(b, r) == oracle_restriction(b, r)).all()
 
 
 def test_noalloc_rejects_oversize_and_bad_values():
@@ -65,4 +84,4 @@ def test_noalloc_rejects_oversize_and_bad_values():
     rng = np.random.default_rng(3)
     b = int_matrix_m31(8, 64, 5)
     r = random_qm31(6, rng)
-    assert (run_noalloc(b, r) == reference_restriction(b, r)).all()
+    assert (run_noalloc(b, r) == oracle_restriction(b, r)).all()

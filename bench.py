@@ -7,10 +7,19 @@ padded to 64 x 8192 and 8192 x 16384.  One step = one
 seeding, the W.eq(r) restrictions, 13 sumcheck rounds with the Poseidon
 channel on the host, and the final evaluation mixes.
 
-Multi-GPU: one process per GPU (torchrun), each rank proves its own
-independent layer (different seeded weights), no data-path collective; the
-timed region is bracketed by barriers and the max over ranks is reported
-("scaling": "weak").  The reference arm (--impl reference) times the CPU
+Multi-GPU: one process per GPU (torchrun).  The headline value keeps N = 1
+comparable: each rank proves its own independent C2 layer (different seeded
+weights), the timed region is bracketed by barriers and the max over ranks is
+reported ("scaling": "weak").  The same JSON line carries, under "sharded",
+the splits of one proof across the N GPUs, each timed the same way:
+  c5           one 2^30-element product sumcheck (config 5) with the MLEs split by
+               the low index bits; the 12 round words are added across the GPUs
+               inside the round kernels and the folded vectors are gathered by
+               peer stores (the peer mesh); strong scaling;
+  c2_colsplit  one C2 layer with B split by column blocks, the partial words
+               exchanged by peer stores; strong scaling;
+and "parity_vs_1gpu": rank 0 recomputes both proofs on one GPU (untimed) and
+compares them bit for bit.  The reference arm (--impl reference) times the CPU
 restatement of the reference prover (the oracle, materialised restriction as
 in engine/src/backend.rs:110-197) on the host cores, rank 0 only.
 """
@@ -43,9 +52,9 @@ def npow2(x):
 
 
 PM, PK, PN = npow2(M), npow2(K), npow2(N)
-# MLE elements folded per layer: every element of the padded A and B MLEs is
-# folded by the restriction, plus both length-pk vectors through the rounds.
-ELEMS_FOLDED = PM * PK + PN * PK + 2 * (2 * PK - 2)
+# MLE elements folded per layer: the restriction folds every real (unpadded) element of A
+# and B -- the zero padding is never read -- and the rounds fold both length-pk vectors.
+ELEMS_FOLDED = M * K + K * N + 2 * (2 * PK - 2)
 
 
 def make_inputs(rank):
@@ -131,8 +140,17 @@ def ncu_traffic_per_launch():
     return None
 
 
+def host_cores():
+    """Every host core this process may run on, before any narrowing to the GPU-local CPUs."""
+    return len(HOST_AFFINITY) if HOST_AFFINITY else (os.cpu_count() or 1)
+
+
+HOST_AFFINITY = set(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else set()
+
+
 def cpu_reference_layer(threads):
-    """One C2 layer through the oracle's materialised (reference) CPU path."""
+    """One C2 layer through the oracle's materialised (reference) CPU path, its threads spread
+    over all host cores (the process affinity is widened back for the call)."""
     import oracle_lib as O
 
     a, b = make_inputs(0)
@@ -140,16 +158,23 @@ def cpu_reference_layer(threads):
     r_i = rng.integers(0, (1 << 31) - 1, (log2(PM), 4), dtype=np.uint32)
     r_j = rng.integers(0, (1 << 31) - 1, (log2(PN), 4), dtype=np.uint32)
     ch = O.new_channel()
-    t0 = time.perf_counter()
-    O.reduce_matmul_layer(a, b, r_i, r_j, ch, mode=0, nthreads=threads)
-    return time.perf_counter() - t0
+    narrowed = set(os.sched_getaffinity(0)) if HOST_AFFINITY else set()
+    if HOST_AFFINITY and narrowed != HOST_AFFINITY:
+        os.sched_setaffinity(0, HOST_AFFINITY)
+    try:
+        t0 = time.perf_counter()
+        O.reduce_matmul_layer(a, b, r_i, r_j, ch, mode=0, nthreads=threads)
+        return time.perf_counter() - t0
+    finally:
+        if HOST_AFFINITY and narrowed != HOST_AFFINITY:
+            os.sched_setaffinity(0, narrowed)
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
+    threads = host_cores()
     for _ in range(args.warmup):
         cpu_reference_layer(threads)
     times = [cpu_reference_layer(threads) for _ in range(args.steps)]
@@ -271,13 +296,14 @@ def run_b200(args):
     # CPU baseline: rank 0 at N=1 only, one full layer through the oracle
     cpu = None
     if world == 1:
-        threads = os.cpu_count() or 1
+        threads = host_cores()
         t = cpu_reference_layer(threads)
         cpu = {"value": t, "unit": "s/layer", "cores": threads, "kind": "port",
                "sample": "one full C2 layer through the C restatement of the reference CPU prover "
                          "(materialised restriction, backend.rs:110-197), all host threads"}
 
     nxt = time_next_rows(Z, torch, ta, tb) if world == 1 else None
+    sharded = measure_sharded(Z, torch, dist, world, rank, ctx, stream) if not args.no_sharded else None
 
     if rank != 0:
         if world > 1:
@@ -311,11 +337,131 @@ def run_b200(args):
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if sharded:
+        line["parity_vs_1gpu"] = sharded.pop("parity_vs_1gpu")
+        line["sharded"] = sharded
     if nxt:
         line["next_rows"] = nxt
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+C5_LOG_N = 30
+
+
+def c5_inputs(torch, n, world, rank):
+    """The config-5 MLEs: uniform M31 from a fixed torch generator on the GPU; every rank
+    draws the same global vectors and keeps the elements with index = rank mod world."""
+    g = torch.Generator(device="cuda").manual_seed(0xC5)
+    a = torch.randint(0, 2**31 - 1, (n,), dtype=torch.int32, device="cuda", generator=g)
+    b = torch.randint(0, 2**31 - 1, (n,), dtype=torch.int32, device="cuda", generator=g)
+    if world == 1:
+        return a, b, a, b
+    return a, b, a[rank::world].contiguous(), b[rank::world].contiguous()
+
+
+def timed_steps(torch, dist, world, stream, fn, steps, warmup):
+    """fn() `steps` times between barriers, CUDA events on `stream`; the max over ranks (ms)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    out = None
+    for _ in range(steps):
+        out = fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms, out
+
+
+def proof_words(round_polys, final_a, final_b):
+    return np.concatenate([np.concatenate([p.c0, p.c1, p.c2]) for p in round_polys] +
+                          [np.asarray(final_a, np.uint32), np.asarray(final_b, np.uint32)])
+
+
+def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3):
+    """The north star's splits of one proof over the `world` GPUs (see the module docstring),
+    with rank 0's one-GPU recomputation of both proofs for the parity check."""
+    from zkml_b200.distributed import (P2PInbox, PeerMesh, ShmExchange, column_block, prove_product_sharded_mesh,
+                                       prove_product_sharded_native, reduce_matmul_layer_colsharded_p2p)
+    out, parity = {}, True
+    peak, _ = measured_peak_hbm()
+    # ---- C5: 2^30-element product sumcheck split by the low index bits -----------------
+    n = 1 << C5_LOG_N
+    ga, gb, la, lb = c5_inputs(torch, n, world, rank)
+    mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None
+    # one GPU: the same library loop with a one-rank exchange (no split, no exchange)
+    solo = ShmExchange(f"zkml_solo_{os.getpid()}", 1, 0, max_gather_bytes=64, nonce=os.getpid()) \
+        if (world == 1 or rank == 0) else None
+    backend = Z.GpuBackend.__new__(Z.GpuBackend)
+    backend.ctx = ctx
+    if mesh is not None:
+        def c5():
+            return prove_product_sharded_mesh(la, lb, n, Z.PoseidonChannel(), mesh)
+    else:
+        def c5():
+            return prove_product_sharded_native(la, lb, n, Z.PoseidonChannel(), solo, ctx=ctx)
+    l0 = ctx.kernel_launches()
+    ms, proof = timed_steps(torch, dist, world, stream, c5, steps, warmup)
+    launches = (ctx.kernel_launches() - l0) // (steps + warmup)
+    n_loc = n // world
+    per_gpu = product_bytes(n_loc)
+    out["c5"] = {"log_n": C5_LOG_N, "ms": round(ms, 4), "elems_folded_per_s_per_gpu": 2 * (2 * n - 2) / (ms * 1e-3) / world,
+                 "hbm_frac_per_gpu": per_gpu / (ms * 1e-3) / 1e9 / peak, "algorithmic_bytes_per_gpu": per_gpu,
+                 "launches_per_proof": launches,
+                 "exchange": "peer mesh (round words reduced in the round kernels, gather by peer stores)"
+                 if world > 1 else "none (one GPU)"}
+    if world > 1:
+        out["c5"]["gathered_at"] = proof.gathered_at
+        got = proof_words(proof.round_polys, proof.final_a, proof.final_b)
+        if rank == 0:
+            ref = prove_product_sharded_native(ga, gb, n, Z.PoseidonChannel(), solo, ctx=ctx)
+            parity &= bool((proof_words(ref.round_polys, ref.final_a, ref.final_b) == got).all())
+        mesh.close()
+    if solo is not None:
+        solo.close()
+    del ga, gb, la, lb
+    torch.cuda.empty_cache()
+    # ---- C2 layer split by column blocks ---------------------------------------------------
+    if world > 1:
+        a, b = make_inputs(0)
+        lo, hi = column_block(N, rank, world)
+        A = Z.M31Matrix(M, K, torch.from_numpy(a.view(np.int32)).cuda().reshape(-1))
+        blk = torch.from_numpy(np.ascontiguousarray(b[:, lo:hi]).view(np.int32)).cuda() if hi > lo else None
+        ch0, point = seeded_channel_state(Z, 0)
+        claim = np.zeros(4, np.uint32)
+        inbox = P2PInbox(K, ctx=ctx)
+
+        def c2():
+            ch = ch0.clone()
+            red, nxt = reduce_matmul_layer_colsharded_p2p(Z.GKRClaim(point, claim), A, blk, lo, M, K, N, ch, inbox)
+            return red, nxt, ch
+
+        ms2, (red, nxt, ch) = timed_steps(torch, dist, world, stream, c2, 10, warmup)
+        out["c2_colsplit"] = {"ms": round(ms2, 4), "columns_per_gpu": hi - lo,
+                              "exchange": "peer stores of the 4k partial words into every rank's inbox"}
+        if rank == 0:
+            chr_ = ch0.clone()
+            ref, rnxt = Z.reduce_matmul_layer_with_backend(Z.GKRClaim(point, claim), A,
+                                                           Z.M31Matrix(K, N, torch.from_numpy(b.view(np.int32)).cuda()),
+                                                           M, K, N, chr_, backend)
+            parity &= bool((proof_words(ref.round_polys, ref.final_a_eval, ref.final_b_eval) ==
+                            proof_words(red.round_polys, red.final_a_eval, red.final_b_eval)).all())
+            parity &= chr_.digest() == ch.digest() and bool((rnxt.point == nxt.point).all())
+        torch.cuda.synchronize()
+        dist.barrier()
+        inbox.close()
+    out["parity_vs_1gpu"] = parity if world > 1 else None
+    return out
 
 
 def run_colsharded(args):
@@ -636,6 +782,7 @@ def main():
                          "layer with B split by column blocks across the GPUs (strong scaling); product: the "
                          "config-5 product sumcheck split across GPUs")
     ap.add_argument("--log-n", type=int, default=28, help="product workload: log2 of the MLE length")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the split-proof measurements")
     ap.add_argument("--p2p", action="store_true",
                     help="c2-colsharded: exchange the partial words over peer memory instead of NCCL")
     args = ap.parse_args()

@@ -573,8 +573,49 @@ def time_next_rows(Z, torch, ta, tb, reps=5):
     out["weight_commitment_ms"] = wall(lambda: Z.weight_commitment(tb), 1)
     claim = Z.AggregatedWeightClaim(B, 0, random_qm31(log2(PK) + log2(PN), rng), val, com)
     out["aggregated_binding_ms"] = wall(lambda: Z.prove_aggregated_binding([claim], Z.PoseidonChannel()), 1)
+    out["merkle_2e24"] = time_merkle_vs_reference(Z, torch)
     out["shapes"] = {"gemm": [M, K, N], "activation": [M, N], "rmsnorm": [M, K], "binding_weight": [K, N]}
     return {k: (round(v, 3) if isinstance(v, float) else v) for k, v in out.items()}
+
+
+def time_merkle_vs_reference(Z, torch, log_n=24, reps=3):
+    """Poseidon-252 Merkle commitment of 2^log_n QM31 leaves: this library's kernels against the
+    reference's own layer kernel compiled from its source (oracle/_ref, a measuring stick; leaf
+    felts precomputed for it, as the reference converts leaves on the CPU), both on this GPU,
+    CUDA events, after one warm-up each; the roots are compared."""
+    import ref_merkle as R
+    n = 1 << log_n
+    g = torch.Generator(device="cuda").manual_seed(24)
+    leaves = torch.randint(0, 2**31 - 1, (n, 4), dtype=torch.int32, device="cuda", generator=g)
+
+    def events(fn):
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, r
+
+    ms, root = events(lambda: Z.commit_mle_root(leaves))
+    res = {"leaves": n, "ms": round(ms, 3), "hashes_per_s": (n - 1) / (ms * 1e-3)}
+    if R.available():
+        felts = torch.from_numpy(R.leaf_felts(leaves.cpu().numpy().view(np.uint32)).view(np.int64)).cuda()
+        rc = torch.from_numpy(R.limbs(R.compressed_round_keys()).view(np.int64)).cuda()
+        scratch = torch.zeros((n, 4), dtype=torch.int64, device="cuda")
+
+        def ref():
+            R.lib().ref_merkle_root(felts.data_ptr(), n, scratch.data_ptr(), rc.data_ptr(),
+                                    torch.cuda.current_stream().cuda_stream)
+            return scratch[0]
+        rms, rroot = events(ref)
+        rroot = rroot.cpu().numpy().view(np.uint64)
+        res.update({"reference_kernel_ms": round(rms, 3), "reference_kernel_hashes_per_s": (n - 1) / (rms * 1e-3),
+                    "speedup_vs_reference_kernel": rms / ms,
+                    "roots_equal": sum(int(rroot[j]) << (64 * j) for j in range(4)) == root})
+    return res
 
 
 def product_bytes(n):

@@ -348,6 +348,22 @@ def run_b200(args):
 
 
 C5_LOG_N = 30
+# config 4: Qwen2.5-14B decoder layer at 64 tokens (hidden 5120, 40 x 128 query width, SwiGLU 13824)
+C4_M, C4_D, C4_Q, C4_FF = 64, 5120, 5120, 13824
+
+
+def c4_inputs(torch, Z):
+    """16-bit activations and int8 weights embedded in M31, drawn on the GPU from fixed seeds;
+    the layer list of the reference recipe for one block (zkml_b200.circuits)."""
+    from zkml_b200.circuits import hf_transformer_layers
+    g = torch.Generator(device="cuda").manual_seed(0xC4)
+
+    def m31(rows, cols, bound):
+        v = torch.randint(-bound, bound + 1, (rows, cols), dtype=torch.int64, device="cuda", generator=g)
+        return torch.where(v < 0, v + Z.M31_P, v).to(torch.int32)
+
+    x = m31(C4_M, C4_D, 32767)
+    return x, hf_transformer_layers(C4_D, C4_Q, C4_FF, 1, lambda i, r, c: m31(r, c, 127), "silu")
 
 
 def c5_inputs(torch, n, world, rank):
@@ -460,6 +476,27 @@ def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3)
         torch.cuda.synchronize()
         dist.barrier()
         inbox.close()
+    # ---- C4: one Qwen2.5-14B decoder layer, weight openings' Merkle hashing split over the mesh ----
+    x, layers = c4_inputs(torch, Z)
+    mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None
+
+    def c4():
+        return Z.prove_gkr_chain(x, layers, mesh=mesh, device=ctx.device, activation_logup=True)
+
+    ms4, proof = timed_steps(torch, dist, world, stream, c4, 2, 1)
+    out["c4_layer"] = {"s": round(ms4 / 1e3, 4), "m": C4_M, "d": C4_D, "q_dim": C4_Q, "d_ff": C4_FF,
+                       "felts": int(proof.raw.size // 4),
+                       "activation": "SiLU through LogUp (the STWO_PIECEWISE_ACTIVATION=0 pin)",
+                       "split": "weight-opening Merkle hashing over the peer mesh" if world > 1 else "none (one GPU)"}
+    if world > 1:
+        if rank == 0:
+            ref = Z.prove_gkr_chain(x, layers, device=ctx.device, activation_logup=True)
+            parity &= ref.raw.size == proof.raw.size and bool((ref.raw == proof.raw).all())
+        torch.cuda.synchronize()
+        dist.barrier()
+        mesh.close()
+    del x, layers
+    torch.cuda.empty_cache()
     out["parity_vs_1gpu"] = parity if world > 1 else None
     return out
 

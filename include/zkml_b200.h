@@ -307,6 +307,11 @@ int zkml_reduce_layernorm(zkml_ctx *ctx, const uint32_t *input, size_t rows, siz
  * reference does under STWO_PIECEWISE_ACTIVATION=0; without it the piecewise-algebraic
  * reduction (prover.rs:7006-7228), the reference's default (prover.rs:1765-1790) */
 #define ZKML_CHAIN_ACTIVATION_LOGUP 4
+/* flags: split the weight openings' Merkle hashing across the ranks of the peer mesh open on
+ * the context's device (zkml_mesh_create / zkml_mesh_open): every rank of the mesh makes the
+ * same call with the same inputs and gets the same proof, equal to the one-GPU proof; each
+ * hashes 1/world of every large tree (see zkml_prove_product_sharded_mesh for the mesh) */
+#define ZKML_CHAIN_MESH 8
 
 /* One layer of the circuit (LayeredCircuit::from_graph, gkr/circuit.rs:140-225); layer i's
  * index is its circuit layer index. */

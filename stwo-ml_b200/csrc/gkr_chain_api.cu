@@ -23,6 +23,7 @@
 #include "context.hpp"
 #include "gkr.cuh"
 #include "logup.cuh"
+#include "mesh.hpp"
 #include "opening.hpp"
 #include "relu.hpp"
 
@@ -182,6 +183,11 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
     ZK_CUDA(cudaSetDevice(ctx->device));
     cudaStream_t s = ctx->stream;
     int rc;
+    MeshState* mesh = nullptr;
+    if (flags & ZKML_CHAIN_MESH) {
+        mesh = mesh_of(ctx);
+        if (!mesh) return set_error(ZKML_ERR_INVALID_ARG, "ZKML_CHAIN_MESH: no peer mesh is open on this device");
+    }
     // outs[0] is the model input, outs[l + 1] layer l's output (m x width[l + 1]), in device memory
     std::vector<size_t> width(n_layers + 1);
     std::vector<long long> src(n_layers);
@@ -517,7 +523,7 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
         obuf.resize(qcap * 4);
         Out oo{obuf.data(), qcap};
         KTimer tm(ctx, KC_MERKLE);
-        if ((e = prove_opening_dev(ctx, bmle.as<uint4>(), nv, wpt.data(), &chs, n_queries, com, oo, nullptr)))
+        if ((e = prove_opening_dev(ctx, bmle.as<uint4>(), nv, wpt.data(), &chs, n_queries, com, oo, nullptr, mesh)))
             return e;
         *olen = oo.len;
         return 0;

@@ -16,6 +16,16 @@ size_t merkle_node_count(size_t n);
 int merkle_tree_launches(size_t n);
 // Full tree over QM31 leaves; nodes must hold merkle_node_count(n) felts.
 void launch_merkle_tree(const uint4* leaves, size_t n, void* nodes, int num_sms, cudaStream_t s);
+// The subtree over leaves [lo, lo + cnt) of a tree over S leaves (S, cnt powers of two >= 2,
+// lo a multiple of cnt): levels 1 .. log2(cnt), written to their places in the full tree's
+// level-major node array.
+void launch_merkle_subtree(const uint4* leaves, size_t S, size_t lo, size_t cnt, void* nodes, int num_sms,
+                           cudaStream_t s);
+int merkle_subtree_launches(size_t cnt);
+// Levels from_level + 1 .. root of a tree over S leaves (S a power of two), from level from_level.
+void launch_merkle_upper_levels(void* nodes, size_t S, unsigned from_level, int num_sms, cudaStream_t s);
+// base[idx[i]] = src[i] (felts).
+void launch_scatter_felts(const void* src, const unsigned long long* idx, size_t n, void* base, cudaStream_t s);
 // securefield_to_felt of each leaf (Montgomery form).
 void launch_leaf_felts(const uint4* leaves, size_t n, void* out, int num_sms, cudaStream_t s);
 // out[i] = poseidon_hash(a[i], b[i]).

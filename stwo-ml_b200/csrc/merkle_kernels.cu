@@ -138,6 +138,12 @@ __global__ void gather_felts_kernel(const dfelt* __restrict__ base, const unsign
         st_f(out + i, ld_f(base + idx[i]));
 }
 
+__global__ void scatter_felts_kernel(const dfelt* __restrict__ src, const unsigned long long* __restrict__ idx,
+                                     size_t n, dfelt* __restrict__ base) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        st_f(base + idx[i], ld_f(src + i));
+}
+
 __global__ void gather_qm31_kernel(const uint4* __restrict__ base, const unsigned long long* __restrict__ idx,
                                    size_t n, uint4* __restrict__ out) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -236,6 +242,47 @@ void launch_merkle_tree(const uint4* leaves, size_t n, void* nodes_v, int num_sm
         in = out;
         pairs = np;
     }
+}
+
+// Level-major offset (in felts) of level l >= 1 of a tree over S = 2^k >= 2 leaves.
+static inline size_t level_base(size_t S, unsigned l) { return S - (S >> (l - 1)); }
+
+void launch_merkle_subtree(const uint4* leaves, size_t S, size_t lo, size_t cnt, void* nodes_v, int num_sms,
+                           cudaStream_t s) {
+    dfelt* nodes = static_cast<dfelt*>(nodes_v);
+    size_t pairs = cnt / 2;
+    dfelt* out = nodes + level_base(S, 1) + lo / 2;
+    merkle_leaf_level_kernel<<<blocks_for(pairs, 128, num_sms), 128, 0, s>>>(leaves + lo, cnt, pairs, out);
+    unsigned l = 1;
+    while (pairs > 1) {
+        const dfelt* in = out;
+        l++;
+        out = nodes + level_base(S, l) + (lo >> l);
+        const size_t np = pairs / 2;
+        merkle_node_level_kernel<<<blocks_for(np, 128, num_sms), 128, 0, s>>>(in, np, out);
+        pairs = np;
+    }
+}
+
+int merkle_subtree_launches(size_t cnt) {
+    int c = 0;
+    for (size_t p = cnt / 2; p >= 1; p /= 2) c++;
+    return c;
+}
+
+void launch_merkle_upper_levels(void* nodes_v, size_t S, unsigned from_level, int num_sms, cudaStream_t s) {
+    dfelt* nodes = static_cast<dfelt*>(nodes_v);
+    for (unsigned l = from_level + 1; (S >> l) >= 1; l++) {
+        const size_t np = S >> l;
+        merkle_node_level_kernel<<<blocks_for(np, 128, num_sms), 128, 0, s>>>(nodes + level_base(S, l - 1), np,
+                                                                               nodes + level_base(S, l));
+        if (np == 1) break;
+    }
+}
+
+void launch_scatter_felts(const void* src, const unsigned long long* idx, size_t n, void* base, cudaStream_t s) {
+    scatter_felts_kernel<<<blocks_for(n, 128, 148), 128, 0, s>>>(static_cast<const dfelt*>(src), idx, n,
+                                                                  static_cast<dfelt*>(base));
 }
 
 int merkle_tree_launches(size_t n) {

@@ -16,6 +16,7 @@
 #include "context.hpp"
 #include "gkr.cuh"
 #include "merkle.cuh"
+#include "mesh.hpp"
 #include "opening.hpp"
 
 namespace zk {
@@ -66,9 +67,19 @@ inline void canon_qm31_felt(const uint32_t v[4], uint64_t out[4]) {
 
 // Proves the opening of the MLE `evals` (device, 2^n_vars QM31) at `point`,
 // appending the serialized MleOpeningProof to `out`.  Advances `chs`.
+//
+// With a peer mesh of G ranks (G a power of two), every rank folds all layers, but the hashing
+// of each layer with at least G x 1024 leaves is split: rank g hashes the subtree over the g-th
+// 1/G of the leaves, the G subtree roots of every such layer are all-gathered over the mesh,
+// and every rank hashes the top log2(G) levels itself; the auth-path nodes below the subtree
+// roots are gathered from their owners the same way.  Every rank ends with the same proof.
 int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const qm31* point, zkml_channel* chs,
-                      size_t n_queries_cfg, uint64_t commitment[4], FeltOut& out, uint32_t final_out[4]) {
+                      size_t n_queries_cfg, uint64_t commitment[4], FeltOut& out, uint32_t final_out[4],
+                      MeshState* mesh) {
     Channel ch(chs);
+    const size_t G = (mesh && mesh->world > 1 && !(mesh->world & (mesh->world - 1))) ? (size_t)mesh->world : 1;
+    const size_t grank = G > 1 ? (size_t)mesh->rank : 0;
+    constexpr size_t kSplitMinLeaves = 1024;
     cudaStream_t s = ctx->stream;
     const size_t N = (size_t)1 << n_vars;
     OpeningScratch& ob = ctx->op;
@@ -88,15 +99,57 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
     };
     auto root_index = [&](unsigned r) { return tree_off[r] + merkle_node_count(layer_size[r]) - 1; };
     // All folds and trees are independent of the transcript: launch them all.
-    launch_merkle_tree(layer_ptr(0), N, ob.trees.as<char>() + 32 * tree_off[0], ctx->num_sms, s);
-    ctx->launches += merkle_tree_launches(N);
+    auto is_split = [&](unsigned r) { return G > 1 && layer_size[r] >= G * kSplitMinLeaves; };
+    auto sub_level = [&](unsigned r) { return ilog2(layer_size[r] / G); };  // level of the subtree roots
+    auto build_tree = [&](unsigned r) {
+        char* tree = ob.trees.as<char>() + 32 * tree_off[r];
+        const size_t S = layer_size[r];
+        if (is_split(r)) {
+            launch_merkle_subtree(layer_ptr(r), S, grank * (S / G), S / G, tree, ctx->num_sms, s);
+            ctx->launches += merkle_subtree_launches(S / G);
+        } else {
+            launch_merkle_tree(layer_ptr(r), S, tree, ctx->num_sms, s);
+            ctx->launches += merkle_tree_launches(S);
+        }
+    };
+    build_tree(0);
     for (unsigned r = 0; r < n_vars; r++) {
         launch_mle_fold(layer_ptr(r), const_cast<uint4*>(layer_ptr(r + 1)), layer_size[r] / 2, point[r], s);
         ctx->launches++;
-        if (layer_size[r + 1] > 1) {
-            launch_merkle_tree(layer_ptr(r + 1), layer_size[r + 1], ob.trees.as<char>() + 32 * tree_off[r + 1],
-                               ctx->num_sms, s);
-            ctx->launches += merkle_tree_launches(layer_size[r + 1]);
+        if (layer_size[r + 1] > 1) build_tree(r + 1);
+    }
+    if (G > 1 && is_split(0)) {
+        // the subtree roots of every split layer, all-gathered, then the top levels on every rank
+        std::vector<unsigned> split_layers;
+        for (unsigned r = 0; r <= n_vars; r++)
+            if (layer_size[r] > 1 && is_split(r)) split_layers.push_back(r);
+        const size_t ne = split_layers.size();
+        std::vector<unsigned long long> own_idx(ne), dst_idx(G * ne);
+        for (size_t e = 0; e < ne; e++) {
+            const unsigned r = split_layers[e];
+            const size_t base = tree_off[r] + (layer_size[r] - (layer_size[r] >> (sub_level(r) - 1)));
+            own_idx[e] = base + grank;
+            for (size_t q = 0; q < G; q++) dst_idx[q * ne + e] = base + q;
+        }
+        const size_t stage_felts = (ne + 1) & ~(size_t)1;  // a multiple of 16 bytes
+        if ((rc = ob.idx.ensure((ne + G * ne) * 8)) || (rc = ob.gathered.ensure((stage_felts + G * stage_felts) * 32)))
+            return rc;
+        ZK_CUDA(cudaMemcpyAsync(ob.idx.ptr, own_idx.data(), ne * 8, cudaMemcpyHostToDevice, s));
+        ZK_CUDA(cudaMemcpyAsync(ob.idx.as<unsigned long long>() + ne, dst_idx.data(), G * ne * 8,
+                                cudaMemcpyHostToDevice, s));
+        char* stage = ob.gathered.as<char>();
+        char* all = stage + 32 * stage_felts;
+        launch_gather_felts(ob.trees.ptr, ob.idx.as<unsigned long long>(), ne, stage, s);
+        if ((rc = mesh_allgather(ctx, mesh, stage, stage_felts * 32, all))) return rc;
+        // rank q's roots sit at all[q * stage_felts + e]: scatter them layer by layer
+        for (size_t q = 0; q < G; q++)
+            launch_scatter_felts(all + 32 * q * stage_felts, ob.idx.as<unsigned long long>() + ne + q * ne, ne,
+                                 ob.trees.ptr, s);
+        ctx->launches += 1 + G;
+        for (unsigned r : split_layers) {
+            launch_merkle_upper_levels(ob.trees.as<char>() + 32 * tree_off[r], layer_size[r], sub_level(r),
+                                       ctx->num_sms, s);
+            ctx->launches += ilog2(G);
         }
     }
     // roots (and the final value) to the host
@@ -129,6 +182,7 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
     // gather values and siblings: per (q, r): left/right values and their sibling leaves,
     // then the internal-node siblings of both paths.
     std::vector<unsigned long long> node_idx;
+    std::vector<int> node_owner;  // the rank whose subtree holds the node, -1: every rank has it
     std::vector<std::vector<unsigned long long>> val_idx(n_vars);
     std::vector<size_t> cur(qidx);
     for (unsigned r = 0; r < n_vars; r++) {
@@ -140,8 +194,11 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
             val_idx[r].push_back(li ^ 1);
             val_idx[r].push_back(ri ^ 1);
             for (size_t x : {li, ri})
-                for (size_t l = 1; l < depth; l++)
-                    node_idx.push_back(tree_off[r] + (S - (S >> (l - 1))) + ((x >> l) ^ 1));
+                for (size_t l = 1; l < depth; l++) {
+                    const size_t xi = (x >> l) ^ 1;
+                    node_idx.push_back(tree_off[r] + (S - (S >> (l - 1))) + xi);
+                    node_owner.push_back(is_split(r) && l < sub_level(r) ? (int)(xi / ((S / G) >> l)) : -1);
+                }
             const size_t next_half = mid / 2 > 0 ? mid / 2 : 1;
             cur[q] %= next_half;
         }
@@ -169,9 +226,28 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
         off += val_idx[r].size();
     }
     std::vector<uint32_t> nodes_m(n_nodes * 8 + 8), vals(n_vals * 4 + 4);
-    if (n_nodes) ZK_CUDA(cudaMemcpyAsync(nodes_m.data(), ob.gathered.ptr, n_nodes * 32, cudaMemcpyDeviceToHost, s));
-    if (n_vals) ZK_CUDA(cudaMemcpyAsync(vals.data(), ob.qvals.ptr, n_vals * 16, cudaMemcpyDeviceToHost, s));
-    ZK_CUDA(cudaStreamSynchronize(s));
+    bool foreign = false;
+    for (int o : node_owner) foreign |= o >= 0 && (size_t)o != grank;
+    if (foreign) {
+        // every rank's gathered nodes over the mesh; each node is taken from its owner
+        const size_t padded = (n_nodes + 1) & ~(size_t)1;
+        DevBuf& allb = ob.nodes;
+        if ((rc = allb.ensure(G * padded * 32))) return rc;
+        if ((rc = mesh_allgather(ctx, mesh, ob.gathered.ptr, padded * 32, allb.ptr))) return rc;
+        std::vector<uint32_t> all(G * padded * 8);
+        ZK_CUDA(cudaMemcpyAsync(all.data(), allb.ptr, G * padded * 32, cudaMemcpyDeviceToHost, s));
+        if (n_vals) ZK_CUDA(cudaMemcpyAsync(vals.data(), ob.qvals.ptr, n_vals * 16, cudaMemcpyDeviceToHost, s));
+        ZK_CUDA(cudaStreamSynchronize(s));
+        for (size_t i = 0; i < n_nodes; i++) {
+            const size_t from = node_owner[i] >= 0 ? (size_t)node_owner[i] : grank;
+            memcpy(&nodes_m[8 * i], &all[8 * (from * padded + i)], 32);
+        }
+    } else {
+        if (n_nodes) ZK_CUDA(cudaMemcpyAsync(nodes_m.data(), ob.gathered.ptr, n_nodes * 32, cudaMemcpyDeviceToHost, s));
+        if (n_vals) ZK_CUDA(cudaMemcpyAsync(vals.data(), ob.qvals.ptr, n_vals * 16, cudaMemcpyDeviceToHost, s));
+        ZK_CUDA(cudaStreamSynchronize(s));
+    }
+    if (G > 1 && (rc = mesh_check(ctx))) return rc;
     // serialize (cairo_serde::serialize_mle_opening_proof): query-major
     out.u64(n_roots - 1);
     for (size_t i = 1; i < n_roots; i++) out.push(&roots[4 * i]);

@@ -753,6 +753,7 @@ _CHAIN_KINDS = {"linear": 0, "relu": 1, "rmsnorm": 2, "add": 3, "mul": 4, "layer
 # ActivationType::type_tag (components/activation.rs:50-60) of the non-ReLU activations
 ACTIVATION_TAGS = {"gelu": 2, "sigmoid": 3, "softmax": 4, "silu": 5}
 CHAIN_ACTIVATION_LOGUP = 4
+CHAIN_MESH = 8
 
 
 def piecewise_activation_enabled() -> bool:
@@ -829,13 +830,15 @@ def _chain_args(inp, layers, n_queries):
 
 def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_queries: Optional[int] = None,
                     legacy_activation_record: bool = False, v1_layout: bool = False,
-                    device: int = 0, activation_logup: Optional[bool] = None) -> GKRChainProof:
+                    device: int = 0, activation_logup: Optional[bool] = None, mesh=None) -> GKRChainProof:
     """prove_gkr (gkr/prover.rs:1500-2251) for GraphBuilder::new(inp.shape) followed by `layers`
     (see _chain_args; Add / Mul layers defer their skip branch), Sequential weight binding.
     raw: serialize_gkr_model_proof, or with v1_layout the verify_model_gkr calldata from
     proof_data on (deferred proofs and their openings included).  Activation layers take the
     LogUp reduction when activation_logup is true, the piecewise one when false; None follows
-    STWO_PIECEWISE_ACTIVATION as the reference does (prover.rs:1765-1790)."""
+    STWO_PIECEWISE_ACTIVATION as the reference does (prover.rs:1765-1790).  With a
+    distributed.PeerMesh, every rank of the mesh makes this call and the weight openings'
+    Merkle hashing is split across them (same proof on every rank)."""
     if activation_logup is None:
         activation_logup = not piecewise_activation_enabled()
     im, ib, arr, keep, nq, cap = _chain_args(inp, layers, n_queries)
@@ -846,6 +849,9 @@ def prove_gkr_chain(inp, layers, policy_commitment: Optional[int] = None, n_quer
     pol = felt_to_limbs(policy_commitment) if policy_commitment else None
     flags = (1 if legacy_activation_record else 0) | (2 if v1_layout else 0)
     flags |= CHAIN_ACTIVATION_LOGUP if activation_logup else 0
+    if mesh is not None:
+        flags |= CHAIN_MESH
+        device = mesh.ctx.device
     _check(lib().zkml_prove_gkr_chain(context(device).handle, ib.ptr, im.rows, im.cols, C.cast(arr, C.c_void_p),
                                       len(layers), C.c_void_p(pol.ctypes.data) if pol is not None else None, nq,
                                       flags, out, cap, C.byref(ln), dig, io))

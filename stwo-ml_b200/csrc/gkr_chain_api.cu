@@ -16,6 +16,7 @@
 #include <array>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "calldata.hpp"
@@ -272,6 +273,26 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
         }
     }
     ZK_CUDA(cudaGetLastError());
+
+    // io commitment (aggregation.rs:235-254) of the model input and output: a sequential
+    // Poseidon sponge over every element (one permutation per two elements), known as soon as
+    // the forward pass is done, so it runs on a host thread of its own beside the proof
+    const size_t wout0 = width[n_layers];
+    std::vector<uint32_t> hin(m * k0), hout(m * wout0);
+    ZK_CUDA(cudaMemcpyAsync(hin.data(), outs[0].ptr, m * k0 * 4, cudaMemcpyDeviceToHost, s));
+    ZK_CUDA(cudaMemcpyAsync(hout.data(), outs[n_layers].ptr, m * wout0 * 4, cudaMemcpyDeviceToHost, s));
+    ZK_CUDA(cudaStreamSynchronize(s));
+    felt_init();
+    int io_rc = ZKML_OK;
+    std::thread io_thread(
+        [&] { io_rc = zkml_io_commitment(hin.data(), m, k0, hout.data(), m, wout0, out_io); });
+    // the thread must be joined on every return path
+    struct Joiner {
+        std::thread& t;
+        ~Joiner() {
+            if (t.joinable()) t.join();
+        }
+    } joiner{io_thread};
 
     zkml_channel chs;
     zkml_channel_init(&chs);
@@ -577,12 +598,8 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
     for (size_t i = 0; i < wclaims.size(); i++)
         if ((rc = open_weight(wclaims[i].layer, wclaims[i].point, coms[i].data(), obufs[i], &olens[i]))) return rc;
 
-    // io commitment (aggregation.rs:235-254) of the model input and output
-    std::vector<uint32_t> hin(m * k0), hout(m * wout);
-    ZK_CUDA(cudaMemcpyAsync(hin.data(), outs[0].ptr, m * k0 * 4, cudaMemcpyDeviceToHost, s));
-    ZK_CUDA(cudaMemcpyAsync(hout.data(), outs[n_layers].ptr, m * wout * 4, cudaMemcpyDeviceToHost, s));
-    ZK_CUDA(cudaStreamSynchronize(s));
-    if ((rc = zkml_io_commitment(hin.data(), m, k0, hout.data(), m, wout, out_io))) return rc;
+    io_thread.join();
+    if ((rc = io_rc)) return rc;
 
     Out o{out_calldata, out_calldata ? cap : 0};
     if (v1 && model_id) {

@@ -291,18 +291,22 @@ def run_b200(args):
 
     ms, launches, (rc_ms, rc_n), clocks = timed(A_dev, B_dev, profile=True)
     rank_ms = timed.rank_ms
-    ms_e2e, _, _, _ = timed(A_host, B_host, profile=False)
+    if args.headline_only:
+        args.no_sharded = True
+        ms_e2e = float("nan")
+    else:
+        ms_e2e, _, _, _ = timed(A_host, B_host, profile=False)
 
     # CPU baseline: rank 0 at N=1 only, one full layer through the oracle
     cpu = None
-    if world == 1:
+    if world == 1 and not args.headline_only:
         threads = host_cores()
         t = cpu_reference_layer(threads)
         cpu = {"value": t, "unit": "s/layer", "cores": threads, "kind": "port",
                "sample": "one full C2 layer through the C restatement of the reference CPU prover "
                          "(materialised restriction, backend.rs:110-197), all host threads"}
 
-    nxt = time_next_rows(Z, torch, ta, tb) if world == 1 else None
+    nxt = time_next_rows(Z, torch, ta, tb) if world == 1 and not args.headline_only else None
     sharded = measure_sharded(Z, torch, dist, world, rank, ctx, stream) if not args.no_sharded else None
 
     if rank != 0:
@@ -861,6 +865,8 @@ def main():
                          "config-5 product sumcheck split across GPUs")
     ap.add_argument("--log-n", type=int, default=28, help="product workload: log2 of the MLE length")
     ap.add_argument("--no-sharded", action="store_true", help="skip the split-proof measurements")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="only the headline C2 layer (no e2e leg, CPU baseline, next rows or splits): for launch lists")
     ap.add_argument("--p2p", action="store_true",
                     help="c2-colsharded: exchange the partial words over peer memory instead of NCCL")
     args = ap.parse_args()

@@ -230,21 +230,27 @@ __global__ void __launch_bounds__(256, 3) m31_gemm_narrow_kernel(const int8_t* _
             const uint32_t row = (idx / per_row) % 64, c16 = idx % per_row;
             *reinterpret_cast<uint4*>(as[buf] + (dg * 64 + row) * GN_APITCH + 16 * c16) = araw[h];
         }
-        // signed bytes, transposed: column 4 bc + e gets the 4 bytes of rows 4 br .. 4 br + 3
-        uint32_t sb[4][4];
+        // signed bytes, transposed: column 4 bc + e gets the 4 bytes of rows 4 br .. 4 br + 3.
+        // For v < 2^31, t = v + (v >> 30) has the signed value's byte as its low byte when v
+        // is in [0, 127] or in [P - 128, P] (t = 2^31 + s there); every other v leaves a bit of
+        // 8..30 set in t + 128.  Inputs with bit 31 set are caught by vor.
+        uint32_t tb[4][4], vor = 0;
 #pragma unroll
         for (int rr = 0; rr < 4; rr++)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const uint32_t v = raw[rr][e];
-                const int sv = m31_signed(v);
-                bad |= (uint32_t)(sv < -128 || sv > 127) | (v >> 31);
-                sb[rr][e] = (uint32_t)sv & 0xffu;
+                const uint32_t t = v + (v >> 30);
+                bad |= (t + 128u) & 0x7fffff00u;
+                vor |= v;
+                tb[rr][e] = t;
             }
+        bad |= vor >> 31;
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-            const uint32_t w = sb[0][e] | (sb[1][e] << 8) | (sb[2][e] << 16) | (sb[3][e] << 24);
-            *reinterpret_cast<uint32_t*>(bs[buf] + (4 * bc + e) * GN_PITCH + 4 * br) = w;
+            const uint32_t lo = __byte_perm(tb[0][e], tb[1][e], 0x0040);
+            const uint32_t hi = __byte_perm(tb[2][e], tb[3][e], 0x0040);
+            *reinterpret_cast<uint32_t*>(bs[buf] + (4 * bc + e) * GN_PITCH + 4 * br) = __byte_perm(lo, hi, 0x5410);
         }
     };
     uint32_t tot[4][4];  // canonical partial sums
@@ -376,11 +382,18 @@ extern "C" int zkml_matmul_m31(zkml_ctx* ctx, const uint32_t* a, size_t m, size_
             const unsigned g = (unsigned)std::min<size_t>((total + 255) / 256, (size_t)ctx->num_sms * 8);
             gemm_a_digits_kernel<<<g, 256, 0, s>>>(Ad, (uint32_t)m, (uint32_t)k, kp, ctx->op.adig.as<int8_t>(), flag);
         }
-        // K splits so that the grid is about four blocks per SM
+        // K splits so that the whole grid is resident at once (one wave): as many splits as
+        // fit in the resident block slots, rounded down
         const unsigned bx = (unsigned)((n + GN_COLS - 1) / GN_COLS), by = (unsigned)((m + 63) / 64);
         const unsigned stages = (kp + GN_BK - 1) / GN_BK;
-        const size_t want = (size_t)4 * ctx->num_sms, have = (size_t)bx * by;
-        unsigned splits = (unsigned)std::max<size_t>(1, (want + have - 1) / have);
+        static int per_sm = 0;
+        if (!per_sm && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, m31_gemm_narrow_kernel, 256, 0) !=
+                           cudaSuccess) {
+            cudaGetLastError();
+            per_sm = 3;
+        }
+        const size_t want = (size_t)std::max(per_sm, 1) * ctx->num_sms, have = (size_t)bx * by;
+        unsigned splits = (unsigned)std::max<size_t>(1, want / have);
         splits = std::min(splits, std::min(stages, 8u));
         uint32_t* target = C;
         if (splits > 1) {

@@ -307,7 +307,8 @@ def run_b200(args):
                          "(materialised restriction, backend.rs:110-197), all host threads"}
 
     nxt = time_next_rows(Z, torch, ta, tb) if world == 1 and not args.headline_only else None
-    sharded = measure_sharded(Z, torch, dist, world, rank, ctx, stream) if not args.no_sharded else None
+    sharded = (measure_sharded(Z, torch, dist, world, rank, ctx, stream, cpu_sample=(world == 1))
+               if not args.no_sharded else None)
 
     if rank != 0:
         if world > 1:
@@ -354,6 +355,44 @@ def run_b200(args):
 C5_LOG_N = 30
 # config 4: Qwen2.5-14B decoder layer at 64 tokens (hidden 5120, 40 x 128 query width, SwiGLU 13824)
 C4_M, C4_D, C4_Q, C4_FF = 64, 5120, 5120, 13824
+
+
+# config 3: SmolLM2-135M, 30 blocks (hidden 576, 9 x 64 query width, SwiGLU 1536), one token
+C3_D, C3_Q, C3_FF, C3_BLOCKS = 576, 576, 1536, 30
+
+
+def c3_inputs(torch, Z, blocks=C3_BLOCKS):
+    """int8 input and weights in M31 from fixed seeds on the GPU, the reference recipe's layers."""
+    from zkml_b200.circuits import hf_transformer_layers
+    g = torch.Generator(device="cuda").manual_seed(0xC3)
+
+    def m31(rows, cols):
+        v = torch.randint(-127, 128, (rows, cols), dtype=torch.int64, device="cuda", generator=g)
+        return torch.where(v < 0, v + Z.M31_P, v).to(torch.int32)
+
+    x = m31(1, C3_D)
+    return x, hf_transformer_layers(C3_D, C3_Q, C3_FF, blocks, lambda i, r, c: m31(r, c), "silu")
+
+
+def c3_cpu_sample(torch, Z):
+    """The oracle (the C restatement of the reference prover) on the first block of the same
+    recipe, all host cores: the CPU baseline's bounded sample, scaled by the block count."""
+    import oracle_lib as O
+    x, layers = c3_inputs(torch, Z, blocks=1)
+    xh = x.cpu().numpy().view(np.uint32)
+    lh = [(k, a.cpu().numpy().view(np.uint32) if k == "linear" else a) for k, a in layers]
+    narrowed = set(os.sched_getaffinity(0)) if HOST_AFFINITY else set()
+    if HOST_AFFINITY:
+        os.sched_setaffinity(0, HOST_AFFINITY)
+    try:
+        t0 = time.perf_counter()
+        rc, _, _, _ = O.prove_gkr_chain(xh, lh, n_queries=10, activation_logup=True, cap=1 << 22)
+        dt = time.perf_counter() - t0
+    finally:
+        if HOST_AFFINITY:
+            os.sched_setaffinity(0, narrowed)
+    assert rc == 0
+    return dt
 
 
 def c4_inputs(torch, Z):
@@ -408,7 +447,7 @@ def proof_words(round_polys, final_a, final_b):
                           [np.asarray(final_a, np.uint32), np.asarray(final_b, np.uint32)])
 
 
-def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3):
+def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3, cpu_sample=False):
     """The north star's splits of one proof over the `world` GPUs (see the module docstring),
     with rank 0's one-GPU recomputation of both proofs for the parity check."""
     from zkml_b200.distributed import (P2PInbox, PeerMesh, ShmExchange, column_block, prove_product_sharded_mesh,
@@ -480,6 +519,35 @@ def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3)
         torch.cuda.synchronize()
         dist.barrier()
         inbox.close()
+    # ---- C3: the 30-block SmolLM2-135M proof (one token), openings split over the mesh ---------
+    x, layers = c3_inputs(torch, Z)
+    mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None
+
+    def c3():
+        return Z.prove_gkr_chain(x, layers, mesh=mesh, device=ctx.device, activation_logup=True)
+
+    ms3, proof = timed_steps(torch, dist, world, stream, c3, 2, 1)
+    out["c3_30_layer"] = {"s": round(ms3 / 1e3, 4), "blocks": C3_BLOCKS, "d": C3_D, "d_ff": C3_FF,
+                          "felts": int(proof.raw.size // 4),
+                          "activation": "SiLU through LogUp (the STWO_PIECEWISE_ACTIVATION=0 pin)",
+                          "recipe": "build_hf_transformer_graph: RMSNorm, q, o, RMSNorm, gate, SiLU, down per "
+                                    "block, final RMSNorm (no K/V, attention, RoPE, embedding or lm_head, as the "
+                                    "reference graph)",
+                          "split": "weight-opening Merkle hashing over the peer mesh" if world > 1 else "none"}
+    if world > 1:
+        if rank == 0:
+            ref = Z.prove_gkr_chain(x, layers, device=ctx.device, activation_logup=True)
+            parity &= ref.raw.size == proof.raw.size and bool((ref.raw == proof.raw).all())
+        torch.cuda.synchronize()
+        dist.barrier()
+        mesh.close()
+    elif cpu_sample:
+        t1 = c3_cpu_sample(torch, Z)
+        out["c3_30_layer"]["cpu_baseline"] = {
+            "value": round(t1 * C3_BLOCKS, 2), "unit": "s", "cores": host_cores(), "kind": "port",
+            "sample": f"the first of the 30 blocks through the oracle chain prover ({t1:.1f} s), times 30"}
+    del x, layers, proof
+    torch.cuda.empty_cache()
     # ---- C4: one Qwen2.5-14B decoder layer, weight openings' Merkle hashing split over the mesh ----
     x, layers = c4_inputs(torch, Z)
     mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None

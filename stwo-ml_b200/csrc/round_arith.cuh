@@ -126,6 +126,12 @@ __device__ __forceinline__ qm31 fold_mq(uint32_t lo, uint32_t hi, const qm31& al
               canon64(mul_wide(d, alpha.d)));
 }
 
+// lo + alpha d for canonical M31 lo and difference d; canonical QM31 result.
+__device__ __forceinline__ qm31 fold_md(uint32_t lo, uint32_t d, const qm31& alpha) {
+    return qm(canon64(mad_wide(d, alpha.a, lo)), canon64(mul_wide(d, alpha.b)), canon64(mul_wide(d, alpha.c)),
+              canon64(mul_wide(d, alpha.d)));
+}
+
 // Per-thread accumulators of one degree-2 product round over QM31 vectors:
 // s0 = sum a_lo b_lo, s1 = sum a_hi b_hi, s2 = sum (2 a_hi - a_lo)(2 b_hi - b_lo).
 struct RoundAcc {

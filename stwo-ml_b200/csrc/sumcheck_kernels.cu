@@ -789,7 +789,24 @@ __device__ __forceinline__ qm31 fold_m31(uint32_t lo, uint32_t hi, const qm31& a
 // tile + t + 256 e (e < FR_UNROLL), so every load (4 bytes a thread) and every
 // 16-byte store of a warp is one contiguous run, and all FR_UNROLL x 8 loads of
 // a tile are issued before its arithmetic.
+//
+// The round sums need no QM31 product: every folded value is x0 + alpha x1 with
+// base-field x0 (the low input) and x1 (high - low), so a product of two folded
+// values is x0 y0 + alpha (x0 y1 + x1 y0) + alpha^2 x1 y1.  Each of the three sums
+// (s0, s1 and s2, whose factors 2 hi - lo are again of that form) is kept as three
+// lazily reduced base-field sums, and alpha, alpha^2 are applied once per thread.
 constexpr int FR_UNROLL = 4;
+
+struct BaseSums {  // [sum][x0 y0, x0 y1 + x1 y0, x1 y1]
+    uint64_t v[3][3];
+};
+
+__device__ __forceinline__ void base_sums_add(BaseSums& s, int k, uint32_t x0, uint32_t x1, uint32_t y0,
+                                              uint32_t y1) {
+    s.v[k][0] = acc_fold(s.v[k][0], mul_wide(x0, y0));
+    s.v[k][1] = acc_fold(s.v[k][1], mad_wide(x0, y1, mul_wide(x1, y0)));
+    s.v[k][2] = acc_fold(s.v[k][2], mul_wide(x1, y1));
+}
 
 __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __restrict__ A,
                                                              const uint32_t* __restrict__ B, size_t h, qm31 alpha,
@@ -798,8 +815,11 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
                                                              uint32_t* sig, uint32_t seq, MeshArg mesh) {
     const size_t q = h / 2;
     const size_t tile = (size_t)FR_UNROLL * blockDim.x;
-    RoundAcc acc;
-    racc_zero(acc);
+    BaseSums bs;
+#pragma unroll
+    for (int k = 0; k < 3; k++)
+#pragma unroll
+        for (int j = 0; j < 3; j++) bs.v[k][j] = 0;
     for (size_t base = blockIdx.x * tile; base < q; base += (size_t)gridDim.x * tile) {
         uint32_t a0[FR_UNROLL], a1[FR_UNROLL], a2[FR_UNROLL], a3[FR_UNROLL];
         uint32_t b0[FR_UNROLL], b1[FR_UNROLL], b2[FR_UNROLL], b3[FR_UNROLL];
@@ -815,18 +835,33 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
         for (int e = 0; e < FR_UNROLL; e++) {
             const size_t j = base + threadIdx.x + (size_t)e * blockDim.x;
             if (j < q) {
-                const qm31 alo = fold_mq(a0[e], a2[e], alpha), ahi = fold_mq(a1[e], a3[e], alpha);
-                const qm31 blo = fold_mq(b0[e], b2[e], alpha), bhi = fold_mq(b1[e], b3[e], alpha);
-                st_q(Ao + j, alo);
-                st_q(Ao + j + q, ahi);
-                st_q(Bo + j, blo);
-                st_q(Bo + j + q, bhi);
-                racc_add(acc, alo, ahi, blo, bhi);
+                // canonical base-field lows and differences (inputs <= P)
+                const uint32_t la = red32(a0[e]), ha = red32(a1[e]), lb = red32(b0[e]), hb = red32(b1[e]);
+                const uint32_t da = csub(red32(a2[e]), la), ea = csub(red32(a3[e]), ha);
+                const uint32_t db = csub(red32(b2[e]), lb), eb = csub(red32(b3[e]), hb);
+                st_q(Ao + j, fold_md(la, da, alpha));
+                st_q(Ao + j + q, fold_md(ha, ea, alpha));
+                st_q(Bo + j, fold_md(lb, db, alpha));
+                st_q(Bo + j + q, fold_md(hb, eb, alpha));
+                base_sums_add(bs, 0, la, da, lb, db);
+                base_sums_add(bs, 1, ha, ea, hb, eb);
+                base_sums_add(bs, 2, csub(cdbl(ha), la), csub(cdbl(ea), da), csub(cdbl(hb), lb), csub(cdbl(eb), db));
             }
         }
     }
+    // s_k = S_k0 + alpha S_k1 + alpha^2 S_k2, once per thread
+    const qm31 alpha2 = qmul(alpha, alpha);
     Sums s;
-    racc_to_sums(acc, s);
+    sums_zero(s);
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const uint32_t c0 = canon64(bs.v[k][0]), c1 = canon64(bs.v[k][1]), c2 = canon64(bs.v[k][2]);
+        const qm31 v = qadd(qadd(qm(c0, 0, 0, 0), qmul_m(alpha, c1)), qmul_m(alpha2, c2));
+        s.v[4 * k] = v.a;
+        s.v[4 * k + 1] = v.b;
+        s.v[4 * k + 2] = v.c;
+        s.v[4 * k + 3] = v.d;
+    }
     finish_sums(s, partials, ticket, out, sig, seq, mesh);
 }
 

@@ -488,6 +488,20 @@ class GpuBackend:
         return out[:n_evals >> n_assign]
 
 
+_fast_fns = {}
+
+
+def _fast_fn(name: str, nargs: int):
+    """The C entry point `name` with every argument passed as a plain integer (pointer or
+    size): no per-call ctypes array validation on the hot path."""
+    f = _fast_fns.get(name)
+    if f is None:
+        addr = C.cast(getattr(lib(), name), C.c_void_p).value
+        f = C.CFUNCTYPE(C.c_int, *([C.c_void_p] * nargs))(addr)
+        _fast_fns[name] = f
+    return f
+
+
 def reduce_matmul_layer_with_backend(output_claim: GKRClaim, a: M31Matrix, b: M31Matrix, m: int, k: int, n: int,
                                      channel: PoseidonChannel, backend: Optional[GpuBackend] = None
                                      ) -> Tuple[MatMulReduction, GKRClaim]:
@@ -495,20 +509,25 @@ def reduce_matmul_layer_with_backend(output_claim: GKRClaim, a: M31Matrix, b: M3
     backend = backend or GpuBackend()
     pm, pk, pn = _next_pow2(a.rows), _next_pow2(a.cols), _next_pow2(b.cols)
     log_m, log_k, log_n = _log2(pm), _log2(pk), _log2(pn)
-    pt_ptr, pt_keep = _qm31_ptr(output_claim.point)
-    n_point = len(as_qm31_array(output_claim.point))
+    point = as_qm31_array(output_claim.point)
+    value = np.ascontiguousarray(output_claim.value, np.uint32)
     abuf, bbuf = _Buf(a.data), _Buf(b.data)
-    rp = np.zeros((max(log_k, 1), 12), np.uint32)
-    fa = np.zeros(4, np.uint32)
-    fb = np.zeros(4, np.uint32)
-    nxt = np.zeros((max(log_m + log_k, 1), 4), np.uint32)
     if (a.rows, a.cols, b.cols) != (m, k, n) or b.rows != k:
         raise InvalidArgument(1, "matrix shapes do not match (m, k, n)")
-    _check(lib().zkml_reduce_matmul_layer_gkr(backend.ctx.handle, pt_ptr, n_point,
-                                              np.ascontiguousarray(output_claim.value, np.uint32).reshape(4),
-                                              abuf.ptr, m, k, bbuf.ptr, n, C.byref(channel.state),
-                                              rp.reshape(-1), fa, fb, nxt.reshape(-1)))
-    # views of this call's own fresh arrays (no per-round copies)
+    # one allocation for every output: round polynomials, final a / b, next point
+    outw = np.empty(12 * max(log_k, 1) + 8 + 4 * max(log_m + log_k, 1), np.uint32)
+    base = outw.ctypes.data
+    o_fa = 4 * 12 * max(log_k, 1)
+    o_nx = o_fa + 32
+    _check(_fast_fn("zkml_reduce_matmul_layer_gkr", 14)(
+        backend.ctx.handle.value,
+        point.ctypes.data if point.size else None, len(point), value.ctypes.data, abuf.ptr.value, m, k,
+        bbuf.ptr.value, n, C.addressof(channel.state), base, base + o_fa, base + o_fa + 16, base + o_nx))
+    rp = outw[:12 * max(log_k, 1)].reshape(-1, 12)
+    fa = outw[o_fa // 4:o_fa // 4 + 4]
+    fb = outw[o_fa // 4 + 4:o_fa // 4 + 8]
+    nxt = outw[o_nx // 4:].reshape(-1, 4)
+    # views of this call's own fresh array (no per-round copies)
     polys = [RoundPoly(row[0:4], row[4:8], row[8:12]) for row in rp[:log_k]]
     red = MatMulReduction(polys, nxt[log_m:log_m + log_k], fa, fb)
     return red, GKRClaim(nxt[:log_m + log_k], fa.copy())

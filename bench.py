@@ -519,6 +519,29 @@ def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3,
         torch.cuda.synchronize()
         dist.barrier()
         inbox.close()
+    # ---- C2 full layer: prove_gkr of the one-layer circuit, Sequential weight opening included ----
+    a, b = make_inputs(0)
+    xa = torch.from_numpy(a.view(np.int32)).cuda()
+    wb = torch.from_numpy(b.view(np.int32)).cuda()
+    mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None
+
+    def full():
+        return Z.prove_gkr_chain(xa, [("linear", wb)], mesh=mesh, device=ctx.device)
+
+    msf, proof = timed_steps(torch, dist, world, stream, full, 2, 1)
+    out["c2_full_layer"] = {"s": round(msf / 1e3, 4), "felts": int(proof.raw.size // 4),
+                            "includes": "forward GEMM, output claim, matmul sumcheck, Sequential weight opening "
+                                        "(2^27-leaf Merkle trees of every folded layer), io commitment",
+                            "split": "weight-opening Merkle hashing over the peer mesh" if world > 1 else "none"}
+    if world > 1:
+        if rank == 0:
+            ref = Z.prove_gkr_chain(xa, [("linear", wb)], device=ctx.device)
+            parity &= ref.raw.size == proof.raw.size and bool((ref.raw == proof.raw).all())
+        torch.cuda.synchronize()
+        dist.barrier()
+        mesh.close()
+    del xa, wb, proof
+    torch.cuda.empty_cache()
     # ---- C3: the 30-block SmolLM2-135M proof (one token), openings split over the mesh ---------
     x, layers = c3_inputs(torch, Z)
     mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None

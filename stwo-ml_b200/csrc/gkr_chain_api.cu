@@ -15,6 +15,9 @@
 #include <algorithm>
 #include <array>
 #include <cstring>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <string>
 #include <thread>
 #include <vector>
@@ -184,6 +187,14 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
     ZK_CUDA(cudaSetDevice(ctx->device));
     cudaStream_t s = ctx->stream;
     int rc;
+    // ZKML_CHAIN_TRACE=1 prints the host wall time of each phase and layer kind to stderr.
+    static const bool trace = getenv("ZKML_CHAIN_TRACE") && getenv("ZKML_CHAIN_TRACE")[0] == '1';
+    auto now = [] { return std::chrono::steady_clock::now(); };
+    auto ms_since = [](std::chrono::steady_clock::time_point t) {
+        return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t).count();
+    };
+    const auto t_call = now();
+    double t_kind[8] = {0, 0, 0, 0, 0, 0, 0, 0}, t_forward = 0, t_open = 0, t_io_wait = 0;
     MeshState* mesh = nullptr;
     if (flags & ZKML_CHAIN_MESH) {
         mesh = mesh_of(ctx);
@@ -294,6 +305,7 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
         }
     } joiner{io_thread};
 
+    t_forward = ms_since(t_call);
     zkml_channel chs;
     zkml_channel_init(&chs);
     Channel ch(&chs);
@@ -349,6 +361,15 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
         n_proofs++;
         const size_t w = width[src[li] + 1];
         const int t = layers[li].type;
+        const auto t_layer = now();
+        struct KindTimer {
+            double* acc;
+            std::chrono::steady_clock::time_point t0;
+            bool on;
+            ~KindTimer() {
+                if (on) *acc += std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+            }
+        } kind_timer{&t_kind[t & 7], t_layer, trace};
         if (t == ZKML_LAYER_LINEAR) {
             const size_t n = width[li + 1];
             const unsigned log_k = lg2(np2(w)), log_n = lg2(np2(n));
@@ -591,6 +612,7 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
         dsec.qm(fb);
         dsec.push(dcoms[i].data());
     }
+    const auto t_open0 = now();
     // the walk's Sequential weight openings on the main channel, in walk order (prover.rs:2140-2171)
     std::vector<std::array<uint64_t, 4>> coms(wclaims.size());
     std::vector<std::vector<uint64_t>> obufs(wclaims.size());
@@ -598,8 +620,17 @@ static int prove_chain(zkml_ctx* ctx, const uint64_t* model_id, const uint32_t* 
     for (size_t i = 0; i < wclaims.size(); i++)
         if ((rc = open_weight(wclaims[i].layer, wclaims[i].point, coms[i].data(), obufs[i], &olens[i]))) return rc;
 
+    t_open = ms_since(t_open0);
+    const auto t_join = now();
     io_thread.join();
+    t_io_wait = ms_since(t_join);
     if ((rc = io_rc)) return rc;
+    if (trace)
+        fprintf(stderr,
+                "[zkml chain] forward %.2f ms; walk: linear %.2f, relu %.2f, rmsnorm %.2f, add %.2f, mul %.2f, "
+                "layernorm %.2f, activation %.2f ms; deferred+openings %.2f ms; io wait %.2f ms; total %.2f ms\n",
+                t_forward, t_kind[0], t_kind[1], t_kind[2], t_kind[3], t_kind[4], t_kind[5], t_kind[6], t_open,
+                t_io_wait, ms_since(t_call));
 
     Out o{out_calldata, out_calldata ? cap : 0};
     if (v1 && model_id) {

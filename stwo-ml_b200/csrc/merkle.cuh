@@ -24,6 +24,20 @@ void launch_merkle_subtree(const uint4* leaves, size_t S, size_t lo, size_t cnt,
 int merkle_subtree_launches(size_t cnt);
 // Levels from_level + 1 .. root of a tree over S leaves (S a power of two), from level from_level.
 void launch_merkle_upper_levels(void* nodes, size_t S, unsigned from_level, int num_sms, cudaStream_t s);
+// One level of up to MERKLE_MAX_JOBS trees in one launch: job j hashes start[j + 1] - start[j]
+// nodes into out from in (QM31 leaves when leaf_level, else node felts of the level below);
+// every leaf count is even (no padding).
+constexpr int MERKLE_MAX_JOBS = 48;
+struct MerkleLevelJob {
+    const void* in;
+    void* out;
+};
+struct MerkleLevelJobs {  // a kernel parameter
+    MerkleLevelJob job[MERKLE_MAX_JOBS];
+    unsigned long long start[MERKLE_MAX_JOBS + 1];
+    int count;
+};
+void launch_merkle_level_batch(const MerkleLevelJobs& jobs, bool leaf_level, int num_sms, cudaStream_t s);
 // base[idx[i]] = src[i] (felts).
 void launch_scatter_felts(const void* src, const unsigned long long* idx, size_t n, void* base, cudaStream_t s);
 // securefield_to_felt of each leaf (Montgomery form).

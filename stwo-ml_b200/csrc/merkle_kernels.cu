@@ -138,6 +138,36 @@ __global__ void gather_felts_kernel(const dfelt* __restrict__ base, const unsign
         st_f(out + i, ld_f(base + idx[i]));
 }
 
+// One level of many trees in one launch: job j hashes n_j nodes of its tree from its level
+// below (QM31 leaves for level 1, node felts above).  Thread-per-node over the concatenated
+// node ranges, so the small levels of small trees share the GPU instead of each paying a
+// launch and a full permutation latency of its own.
+template <bool LEAF>
+__global__ void __launch_bounds__(128) merkle_level_batch_kernel(const MerkleLevelJobs jobs) {
+    const unsigned long long total = jobs.start[jobs.count];
+    for (unsigned long long idx = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (unsigned long long)gridDim.x * blockDim.x) {
+        int lo = 0, hi = jobs.count - 1;  // the job with start[j] <= idx < start[j + 1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (jobs.start[mid] <= idx) lo = mid;
+            else hi = mid - 1;
+        }
+        const MerkleLevelJob& jb = jobs.job[lo];
+        const unsigned long long i = idx - jobs.start[lo];
+        dfelt* out = static_cast<dfelt*>(jb.out);
+        if (LEAF) {
+            const uint4* leaves = static_cast<const uint4*>(jb.in);
+            f26 st[3] = {leaf26(leaves[2 * i]), leaf26(leaves[2 * i + 1]), c26.two};
+            hades26(st);
+            st_f(out + i, m260_to_m256(st[0]));
+        } else {
+            const dfelt* in = static_cast<const dfelt*>(jb.in);
+            st_f(out + i, hash2(ld_f(in + 2 * i), ld_f(in + 2 * i + 1)));
+        }
+    }
+}
+
 __global__ void scatter_felts_kernel(const dfelt* __restrict__ src, const unsigned long long* __restrict__ idx,
                                      size_t n, dfelt* __restrict__ base) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
@@ -278,6 +308,15 @@ void launch_merkle_upper_levels(void* nodes_v, size_t S, unsigned from_level, in
                                                                                nodes + level_base(S, l));
         if (np == 1) break;
     }
+}
+
+void launch_merkle_level_batch(const MerkleLevelJobs& jobs, bool leaf_level, int num_sms, cudaStream_t s) {
+    const unsigned long long total = jobs.start[jobs.count];
+    if (total == 0) return;
+    if (leaf_level)
+        merkle_level_batch_kernel<true><<<blocks_for(total, 128, num_sms), 128, 0, s>>>(jobs);
+    else
+        merkle_level_batch_kernel<false><<<blocks_for(total, 128, num_sms), 128, 0, s>>>(jobs);
 }
 
 void launch_scatter_felts(const void* src, const unsigned long long* idx, size_t n, void* base, cudaStream_t s) {

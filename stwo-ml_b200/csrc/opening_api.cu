@@ -7,6 +7,7 @@
 // tree is kept in HBM from the first pass (about 64 N bytes, 8 GB at N = 2^27),
 // so each node is hashed once (about 2N hashes) and the auth paths are gathered
 // with one kernel; the proof bytes are identical.
+#include <algorithm>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -22,6 +23,10 @@
 namespace zk {
 
 namespace {
+
+struct dfelt_t {  // a 32-byte node felt, for pointer arithmetic on the tree buffer
+    uint32_t w[8];
+};
 
 inline size_t next_pow2(size_t x) {
     size_t p = 1;
@@ -80,6 +85,7 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
     const size_t G = (mesh && mesh->world > 1 && !(mesh->world & (mesh->world - 1))) ? (size_t)mesh->world : 1;
     const size_t grank = G > 1 ? (size_t)mesh->rank : 0;
     constexpr size_t kSplitMinLeaves = 1024;
+    if (n_vars + 1 > (unsigned)MERKLE_MAX_JOBS) return set_error(ZKML_ERR_INVALID_ARG, "MLE opening: too many variables");
     cudaStream_t s = ctx->stream;
     const size_t N = (size_t)1 << n_vars;
     OpeningScratch& ob = ctx->op;
@@ -98,25 +104,48 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
         return r == 0 ? evals : ob.layers.as<uint4>() + (N - (N >> (r - 1)));
     };
     auto root_index = [&](unsigned r) { return tree_off[r] + merkle_node_count(layer_size[r]) - 1; };
-    // All folds and trees are independent of the transcript: launch them all.
+    // All folds and trees are independent of the transcript.  The folds run first (each layer
+    // from the previous one); then the trees are hashed level by level, one launch per level
+    // for all layers together, so the many small levels do not each pay a launch and a full
+    // permutation latency.
     auto is_split = [&](unsigned r) { return G > 1 && layer_size[r] >= G * kSplitMinLeaves; };
     auto sub_level = [&](unsigned r) { return ilog2(layer_size[r] / G); };  // level of the subtree roots
-    auto build_tree = [&](unsigned r) {
-        char* tree = ob.trees.as<char>() + 32 * tree_off[r];
-        const size_t S = layer_size[r];
-        if (is_split(r)) {
-            launch_merkle_subtree(layer_ptr(r), S, grank * (S / G), S / G, tree, ctx->num_sms, s);
-            ctx->launches += merkle_subtree_launches(S / G);
-        } else {
-            launch_merkle_tree(layer_ptr(r), S, tree, ctx->num_sms, s);
-            ctx->launches += merkle_tree_launches(S);
-        }
+    auto level_base = [&](unsigned r, unsigned l) -> size_t {  // felt offset of level l >= 1 of tree r
+        return tree_off[r] + (layer_size[r] - (layer_size[r] >> (l - 1)));
     };
-    build_tree(0);
     for (unsigned r = 0; r < n_vars; r++) {
         launch_mle_fold(layer_ptr(r), const_cast<uint4*>(layer_ptr(r + 1)), layer_size[r] / 2, point[r], s);
         ctx->launches++;
-        if (layer_size[r + 1] > 1) build_tree(r + 1);
+    }
+    dfelt_t* trees = ob.trees.as<dfelt_t>();
+    if (N == 1) {  // a single value: its tree is the leaf and a zero pad
+        launch_merkle_tree(layer_ptr(0), 1, ob.trees.as<char>() + 32 * tree_off[0], ctx->num_sms, s);
+        ctx->launches += merkle_tree_launches(1);
+    }
+    unsigned max_levels = 0;
+    for (unsigned r = 0; r <= n_vars; r++)
+        if (layer_size[r] > 1) max_levels = std::max(max_levels, is_split(r) ? sub_level(r) : ilog2(layer_size[r]));
+    for (unsigned l = 1; l <= max_levels; l++) {
+        MerkleLevelJobs jobs;
+        jobs.count = 0;
+        jobs.start[0] = 0;
+        for (unsigned r = 0; r <= n_vars; r++) {
+            const size_t S = layer_size[r];
+            if (S < 2) continue;
+            const unsigned top = is_split(r) ? sub_level(r) : ilog2(S);
+            if (l > top) continue;
+            // this rank's range of the layer: all of it, or its 1/G share when split
+            const size_t lo = is_split(r) ? grank * (S / G) : 0;
+            const size_t cnt = is_split(r) ? S / G : S;
+            MerkleLevelJob& jb = jobs.job[jobs.count];
+            jb.in = l == 1 ? static_cast<const void*>(layer_ptr(r) + lo)
+                           : static_cast<const void*>(trees + level_base(r, l - 1) + (lo >> (l - 1)));
+            jb.out = trees + level_base(r, l) + (lo >> l);
+            jobs.start[jobs.count + 1] = jobs.start[jobs.count] + (cnt >> l);
+            jobs.count++;
+        }
+        launch_merkle_level_batch(jobs, l == 1, ctx->num_sms, s);
+        ctx->launches++;
     }
     if (G > 1 && is_split(0)) {
         // the subtree roots of every split layer, all-gathered, then the top levels on every rank
@@ -127,7 +156,7 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
         std::vector<unsigned long long> own_idx(ne), dst_idx(G * ne);
         for (size_t e = 0; e < ne; e++) {
             const unsigned r = split_layers[e];
-            const size_t base = tree_off[r] + (layer_size[r] - (layer_size[r] >> (sub_level(r) - 1)));
+            const size_t base = level_base(r, sub_level(r));
             own_idx[e] = base + grank;
             for (size_t q = 0; q < G; q++) dst_idx[q * ne + e] = base + q;
         }
@@ -146,10 +175,21 @@ int prove_opening_dev(zkml_ctx* ctx, const uint4* evals, unsigned n_vars, const 
             launch_scatter_felts(all + 32 * q * stage_felts, ob.idx.as<unsigned long long>() + ne + q * ne, ne,
                                  ob.trees.ptr, s);
         ctx->launches += 1 + G;
-        for (unsigned r : split_layers) {
-            launch_merkle_upper_levels(ob.trees.as<char>() + 32 * tree_off[r], layer_size[r], sub_level(r),
-                                       ctx->num_sms, s);
-            ctx->launches += ilog2(G);
+        // the top log2(G) levels of every split tree, one launch per level
+        for (unsigned u = 1; (size_t(1) << u) <= G; u++) {
+            MerkleLevelJobs jobs;
+            jobs.count = 0;
+            jobs.start[0] = 0;
+            for (unsigned r : split_layers) {
+                const unsigned l = sub_level(r) + u;
+                MerkleLevelJob& jb = jobs.job[jobs.count];
+                jb.in = trees + level_base(r, l - 1);
+                jb.out = trees + level_base(r, l);
+                jobs.start[jobs.count + 1] = jobs.start[jobs.count] + (layer_size[r] >> l);
+                jobs.count++;
+            }
+            launch_merkle_level_batch(jobs, false, ctx->num_sms, s);
+            ctx->launches++;
         }
     }
     // roots (and the final value) to the host

@@ -82,11 +82,11 @@ void felt_init() {
 }
 
 // ---------------------------------------------------------------------------
-// Fast path (BMI2 + ADX): lazy reduction.  The multiply accepts inputs < 4p
-// and returns values < p, so additions in front of a multiply need no
-// reduction; in the 83 partial rounds the S-box lane carries x = s2 + key
-// (< 3p) and its critical path is x -> x^2 -> x^3 -> (w + 2p - 2 x^3), where
-// w = (s0 + s1 + next key) mod p is computed off that path.
+// Fast path (BMI2 + ADX): lazy reduction.  The cube accepts inputs < 5p and
+// returns values < 1.3p, so additions in front of it need no reduction; in the
+// 83 partial rounds the S-box lane carries x = s2 + key (< 5p) and its critical
+// path is x -> x^2 -> x^3 -> (w + 3p - 2 x^3), where w = (s0 + s1 + next key)
+// mod p is computed off that path.
 // ---------------------------------------------------------------------------
 namespace {
 
@@ -95,7 +95,8 @@ inline felt mul_adx(const felt& a, const felt& b) {
     zk_felt_mont_mul_adx(r.l, a.l, b.l);
     return r;
 }
-// x^3 (in Montgomery form: x^3 / R^2), both multiplications in one call.
+// x^3 (in Montgomery form: x^3 / R^2) for x < 5p, both multiplications in one call; the
+// result is below 1.3 p (not reduced).
 inline felt cube_adx(const felt& a) {
     felt r;
     zk_felt_mont_cube_adx(r.l, a.l);
@@ -150,10 +151,10 @@ inline void full_round_fast(felt s[3], const felt* rc, const felt& p2, const fel
     y0 = cube_adx(y0);
     y1 = cube_adx(y1);
     y2 = cube_adx(y2);
-    const felt t = add4(add4(y0, y1), y2);                             // < 3p
-    s[0] = red_full(add4(t, dbl4(y0)));                                // < 5p
-    s[1] = red_full(sub4(add4(t, p2), dbl4(y1)));                      // < 5p
-    s[2] = red_full(sub4(add4(t, p3), add4(dbl4(y2), y2)));            // < 6p
+    const felt t = add4(add4(y0, y1), y2);                             // < 3.9p
+    s[0] = red_full(add4(t, dbl4(y0)));                                // < 6.5p
+    s[1] = red_full(sub4(add4(t, p2), dbl4(y1)));                      // t >= y1: >= 0, < 5.9p
+    s[2] = red_full(sub4(add4(t, p3), add4(dbl4(y2), y2)));            // t >= y2: >= 0, < 6.9p
 }
 
 void hades_fast(felt s[3]) {
@@ -163,16 +164,16 @@ void hades_fast(felt s[3]) {
     felt s0 = s[0], s1 = s[1];
     felt x = add4(s[2], rc[0]);
     for (int r = 0; r < 83; r++) {
-        const felt y = cube_adx(x);                                    // < p
+        const felt y = cube_adx(x);                                    // < 1.3p
         const felt u = add4(s0, s1);                                   // < 2p
-        const felt t = add4(u, y);                                     // < 3p
+        const felt t = add4(u, y);                                     // < 3.3p
         const felt n0 = red_full(add4(t, dbl4(s0)));
         const felt n1 = red_full(sub4(add4(t, p2), dbl4(s1)));
         if (r + 1 < 83) {
             const felt w = red_full(add4(u, rc[r + 1]));               // s0 + s1 + next key
-            x = sub4(add4(w, p2), dbl4(y));                            // next s2 + key, < 3p
+            x = sub4(add4(w, p3), dbl4(y));                            // next s2 + key, in (0.4p, 4p)
         } else {
-            x = red_full(sub4(add4(u, p2), dbl4(y)));                  // s2 after the last partial round
+            x = red_full(sub4(add4(u, p3), dbl4(y)));                  // s2 after the last partial round
         }
         s0 = n0;
         s1 = n1;

@@ -14,10 +14,13 @@
  * shorter dependency chain.  The result is < 2p and is reduced once with cmov.
  *
  * void zk_felt_mont_cube_adx(uint64_t r[4], const uint64_t a[4]);
- *   r = a^3 / R^2 mod p (two multiplications without a second call).
+ *   r = a^3 / R^2 mod p (two multiplications without a second call), for a < 5p, left
+ *   unreduced: the product (a < 5p) * (b < 5p) / R is below p + 25 p^2 / 2^256 < 1.8 p, so a^2 is
+ *   below 1.8 p and a^3 below 1.3 p; skipping the final conditional subtraction takes it off the
+ *   S-box's latency chain.
  */
 /* (rdi) = (rsi) * (rcx) / R mod p; clobbers rax, rbx, rbp, rdx, r8-r15; keeps rdi, rsi, rcx */
-.macro MONT_MUL
+.macro MONT_MUL reduce=1
     /* row 0: t[0..4] = a * b0 */
     movq    (%rcx), %rdx
     mulxq   (%rsi), %r8, %r9
@@ -121,6 +124,7 @@
     mulxq   %r8, %rax, %rbx
     addq    %rax, %r14
     adcq    %rbx, %r15
+    .if \reduce
     /* r = t[4..7] - p if t >= p (branch-free) */
     movq    %r12, %rax
     subq    $1, %rax
@@ -134,6 +138,7 @@
     cmovncq %rbx, %r13
     cmovncq %rdx, %r14
     cmovncq %rbp, %r15
+    .endif
     movq    %r12, (%rdi)
     movq    %r13, 8(%rdi)
     movq    %r14, 16(%rdi)
@@ -175,11 +180,11 @@ zk_felt_mont_cube_adx:
     subq    $40, %rsp
     movq    %rdi, 32(%rsp)              /* the result pointer */
     movq    %rsi, %rcx                  /* b = a */
-    movq    %rsp, %rdi                  /* a^2 into the stack slot */
-    MONT_MUL
+    movq    %rsp, %rdi                  /* a^2 into the stack slot, left below 1.5 p (not reduced) */
+    MONT_MUL 0
     movq    %rsp, %rcx                  /* b = a^2 */
     movq    32(%rsp), %rdi
-    MONT_MUL
+    MONT_MUL 0                          /* a^3 below 1.3 p (not reduced) */
     addq    $40, %rsp
     popq    %r15
     popq    %r14

@@ -132,7 +132,7 @@ def test_activation_tables_match_oracle(tag):
 
 def test_montgomery_multiply_and_cube_edges():
     """The x86 Montgomery multiply and cube (felt252_x86.S) against big-integer arithmetic, on
-    inputs up to 4p (the lazy-reduction range) and on products whose low 192 bits are zero
+    inputs up to 4p (5p for the cube: the lazy-reduction ranges) and on products whose low 192 bits are zero
     (the reduction's no-carry path)."""
     import ctypes as C
     import random
@@ -163,5 +163,7 @@ def test_montgomery_multiply_and_cube_edges():
         L.zk_felt_mont_mul_adx(r, limbs(a), limbs(b))
         assert val(r) == a * b * rinv % p
         if a == b or a < 4 * p:
-            L.zk_felt_mont_cube_adx(r, limbs(a))
-            assert val(r) == a * a * a * rinv * rinv % p
+            # the cube is left unreduced, below 1.3 p, for inputs below 5 p
+            for x in (a, a + p):
+                L.zk_felt_mont_cube_adx(r, limbs(x))
+                assert val(r) % p == x * x * x * rinv * rinv % p and val(r) < 13 * p // 10

@@ -19,7 +19,7 @@
  *   below 1.8 p and a^3 below 1.3 p; skipping the final conditional subtraction takes it off the
  *   S-box's latency chain.
  */
-/* (rdi) = (rsi) * (rcx) / R mod p; clobbers rax, rbx, rbp, rdx, r8-r15; keeps rdi, rsi, rcx */
+/* (rdi) = (rsi) * (rcx) / R mod p; clobbers rax, rbx, rcx, rbp, rdx, r8-r15; keeps rdi, rsi */
 .macro MONT_MUL reduce=1
     /* row 0: t[0..4] = a * b0 */
     movq    (%rcx), %rdx
@@ -90,21 +90,17 @@
     subq    %r8, %rax
     sbbq    %r9, %rbx
     sbbq    %r10, %rbp
-    movq    %r8, %rdx
-    orq     %r9, %rdx
-    orq     %r10, %rdx
-    negq    %rdx
-    adcq    $0, %r11
-    adcq    $0, %r12
-    adcq    $0, %r13
-    adcq    $0, %r14
-    adcq    $0, %r15
-    /* t[3..7] += M * p3 */
+    movq    %r8, %rcx                   /* rcx = t[0] | t[1] | t[2] (b is no longer needed) */
+    orq     %r9, %rcx
+    orq     %r10, %rcx
+    /* t[3..7] += M * p3, and the carry of t[0..2] + M (set iff t[0..2] != 0) enters with the
+     * first addition instead of rippling through its own chain */
     movabsq $0x0800000000000011, %rdx
     mulxq   %rax, %r8, %r9
     mulxq   %rbx, %r10, %rax
     mulxq   %rbp, %rbx, %rbp
-    addq    %r8, %r11
+    negq    %rcx
+    adcq    %r8, %r11
     adcq    %r9, %r12
     adcq    %rax, %r13
     adcq    %rbp, %r14
@@ -115,14 +111,12 @@
     adcq    $0, %r15
     /* reduction step 2: m = -t3 clears limb 3, m * p3 lands on limbs 6, 7 */
     movq    %r11, %rdx
-    negq    %rdx
-    adcq    $0, %r12
-    adcq    $0, %r13
-    adcq    $0, %r14
-    adcq    $0, %r15
+    negq    %rdx                        /* CF: t3 != 0 (mov and mulx keep the flags) */
     movabsq $0x0800000000000011, %r8
     mulxq   %r8, %rax, %rbx
-    addq    %rax, %r14
+    adcq    $0, %r12
+    adcq    $0, %r13
+    adcq    %rax, %r14
     adcq    %rbx, %r15
     .if \reduce
     /* r = t[4..7] - p if t >= p (branch-free) */

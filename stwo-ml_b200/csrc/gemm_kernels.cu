@@ -282,12 +282,16 @@ __global__ void __launch_bounds__(256, 3) m31_gemm_narrow_kernel(const int8_t* _
                 uint32_t af[GEMM_GA][4];
 #pragma unroll
                 for (int a = 0; a < GEMM_GA; a++) {
-                    const uint8_t* p0 = as[buf] + (a * 64 + rt * 16 + g) * GN_APITCH;
-                    const uint8_t* p1 = p0 + 8 * GN_APITCH;
-                    af[a][0] = *reinterpret_cast<const uint32_t*>(p0 + ta);
-                    af[a][1] = *reinterpret_cast<const uint32_t*>(p1 + ta);
-                    af[a][2] = *reinterpret_cast<const uint32_t*>(p0 + tb);
-                    af[a][3] = *reinterpret_cast<const uint32_t*>(p1 + tb);
+                    // the four 8 x 16-byte pieces of the 16 x 32 A fragment in one ldmatrix: lane l
+                    // gives row (l & 7) of piece l >> 3 (rows +8 for odd pieces, bytes +16 for the
+                    // upper two); the 80-byte row pitch keeps the eight rows of a piece on distinct banks
+                    const uint32_t mi = lane >> 3;
+                    const uint8_t* rowp = as[buf] + (a * 64 + rt * 16 + (mi & 1) * 8 + (lane & 7)) * GN_APITCH +
+                                          32 * ks + (mi >> 1) * 16;
+                    const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(rowp));
+                    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                                 : "=r"(af[a][0]), "=r"(af[a][1]), "=r"(af[a][2]), "=r"(af[a][3])
+                                 : "r"(addr));
                 }
 #pragma unroll
                 for (int t = 0; t < 4; t++) {

@@ -20,7 +20,7 @@
  *   S-box's latency chain.
  */
 /* (rdi) = (rsi) * (rcx) / R mod p; clobbers rax, rbx, rcx, rbp, rdx, r8-r15; keeps rdi, rsi */
-.macro MONT_MUL reduce=1
+.macro MONT_ROWS
     /* row 0: t[0..4] = a * b0 */
     movq    (%rcx), %rdx
     mulxq   (%rsi), %r8, %r9
@@ -83,6 +83,11 @@
     adoxq   %rbp, %r15
     adcxq   %rbp, %r15
 
+.endm
+
+/* (rdi) = t[0..7] (r8-r15) / R mod p, reduced below p when reduce=1; clobbers rax, rbx, rcx, rbp,
+ * rdx, r8-r15 */
+.macro MONT_REDUCE reduce=1
     /* reduction step 1: M = -t[0..2] mod 2^192 in rax, rbx, rbp; CF: t[0..2] != 0 */
     xorl    %eax, %eax
     xorl    %ebx, %ebx
@@ -139,6 +144,62 @@
     movq    %r15, 24(%rdi)
 .endm
 
+/* (rdi) = (rsi) * (rcx) / R mod p; clobbers rax, rbx, rcx, rbp, rdx, r8-r15; keeps rdi, rsi */
+.macro MONT_MUL reduce=1
+    MONT_ROWS
+    MONT_REDUCE \reduce
+.endm
+
+/* t[0..7] (r8-r15) = (rsi)^2: the six cross products once, doubled with one shift chain, then
+ * the four squares on the diagonal; mov and mulx leave the flags, so the final carry chain runs
+ * through the diagonal products as they arrive.  Clobbers rax, rbx, rcx, rdx. */
+.macro SQR_ROWS
+    movq    (%rsi), %rdx
+    mulxq   8(%rsi), %r9, %r10          /* a0 a1 -> t1, t2 */
+    mulxq   16(%rsi), %rax, %r11        /* a0 a2 -> t2, t3 */
+    addq    %rax, %r10
+    mulxq   24(%rsi), %rax, %r12        /* a0 a3 -> t3, t4 */
+    adcq    %rax, %r11
+    adcq    $0, %r12
+    movq    8(%rsi), %rdx
+    mulxq   16(%rsi), %rax, %rbx        /* a1 a2 -> t3, t4 */
+    mulxq   24(%rsi), %rcx, %r13        /* a1 a3 -> t4, t5 */
+    addq    %rax, %r11
+    adcq    %rbx, %r12
+    adcq    $0, %r13
+    addq    %rcx, %r12
+    adcq    $0, %r13
+    movq    16(%rsi), %rdx
+    mulxq   24(%rsi), %rax, %r14        /* a2 a3 -> t5, t6 */
+    addq    %rax, %r13
+    adcq    $0, %r14
+    /* double t1..t6 into t1..t7 */
+    xorl    %r15d, %r15d
+    shldq   $1, %r14, %r15
+    shldq   $1, %r13, %r14
+    shldq   $1, %r12, %r13
+    shldq   $1, %r11, %r12
+    shldq   $1, %r10, %r11
+    shldq   $1, %r9, %r10
+    addq    %r9, %r9
+    /* + a_i^2 at t[2i], t[2i+1] */
+    movq    (%rsi), %rdx
+    mulxq   %rdx, %r8, %rax
+    movq    8(%rsi), %rdx
+    mulxq   %rdx, %rbx, %rcx
+    addq    %rax, %r9
+    adcq    %rbx, %r10
+    adcq    %rcx, %r11
+    movq    16(%rsi), %rdx
+    mulxq   %rdx, %rax, %rbx
+    adcq    %rax, %r12
+    adcq    %rbx, %r13
+    movq    24(%rsi), %rdx
+    mulxq   %rdx, %rax, %rbx
+    adcq    %rax, %r14
+    adcq    %rbx, %r15
+.endm
+
     .text
     .globl  zk_felt_mont_mul_adx
     .type   zk_felt_mont_mul_adx, @function
@@ -173,9 +234,9 @@ zk_felt_mont_cube_adx:
     pushq   %r15
     subq    $40, %rsp
     movq    %rdi, 32(%rsp)              /* the result pointer */
-    movq    %rsi, %rcx                  /* b = a */
-    movq    %rsp, %rdi                  /* a^2 into the stack slot, left below 1.5 p (not reduced) */
-    MONT_MUL 0
+    movq    %rsp, %rdi                  /* a^2 into the stack slot, left below 1.8 p (not reduced) */
+    SQR_ROWS
+    MONT_REDUCE 0
     movq    %rsp, %rcx                  /* b = a^2 */
     movq    32(%rsp), %rdi
     MONT_MUL 0                          /* a^3 below 1.3 p (not reduced) */

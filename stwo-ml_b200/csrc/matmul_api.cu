@@ -16,6 +16,32 @@
 #include "context.hpp"
 #include "merkle.cuh"
 
+// ZKML_LAYER_TRACE=1: the host timeline of each matmul layer reduction, printed to stderr
+// (microseconds since the call entered the library).
+namespace {
+struct LayerTrace {
+    bool on = getenv("ZKML_LAYER_TRACE") && getenv("ZKML_LAYER_TRACE")[0] == '1';
+    std::chrono::steady_clock::time_point t0;
+    std::vector<std::pair<const char*, double>> marks;
+    void start() {
+        if (!on) return;
+        marks.clear();
+        t0 = std::chrono::steady_clock::now();
+    }
+    void mark(const char* what) {
+        if (on)
+            marks.emplace_back(what, std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - t0).count());
+    }
+    void print() {
+        if (!on) return;
+        fprintf(stderr, "[zkml layer]");
+        for (auto& m : marks) fprintf(stderr, " %s %.1f", m.first, m.second);
+        fprintf(stderr, "\n");
+    }
+};
+LayerTrace g_trace;
+}  // namespace
+
 namespace zk {
 
 static thread_local std::string g_last_error;
@@ -474,7 +500,9 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
         ZK_CUDA(cudaGetLastError());
         ctx->launches++;
     }
+    g_trace.mark("queued");
     if (hook && hook->overlap) hook->overlap(hook->arg);  // host transcript work while the GPU runs
+    g_trace.mark("overlap");
     uint32_t words[LA_WORDS_HOST];
     uint32_t s12[12];
     uint32_t la_w[LA_WORDS_HOST];  // the previous look-ahead words (this round's sums as a quadratic)
@@ -485,6 +513,7 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             la_next_sums(la_w, alpha_prev, s12);  // this round's kernel may still be running
         } else {
             rc = wait_signal(ctx, la ? laq.seq[0] : rs.seq, words, la ? LA_WORDS_HOST : 12);
+            g_trace.mark("w0");
             if (rc) {
                 laq.abort_rest();
                 return rc;
@@ -505,6 +534,7 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
             ch.mix_poly_coeffs(c0, c1, c2);
             alpha = ch.draw_qm31();
         }
+        g_trace.mark("r");
         if (hook && hook->challenge) hook->challenge(hook->arg, r, alpha);
         if (out_rp) {
             stq(out_rp + 12 * r, c0);
@@ -531,6 +561,7 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
                 const qm31 a0 = ldq(words + 12), a1 = ldq(words + 16), b0 = ldq(words + 20), b1 = ldq(words + 24);
                 stq(fa_out, qadd(a0, qmul(alpha, qsub(a1, a0))));
                 stq(fb_out, qadd(b0, qmul(alpha, qsub(b1, b0))));
+                g_trace.mark("last");
                 if ((rc = read_err_flag(ctx))) return rc;
                 return check_err_flag(ctx, "reduce_matmul_layer");
             }
@@ -823,12 +854,15 @@ int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size
         return run_sumcheck(ctx, nullptr, nullptr, Ad, Bd, pk, ch, out_round_polys, out_challenges, out_final_a,
                             out_final_b, hook);
     }
+    g_trace.mark("views");
     rc = restrict_ab(ctx, Ad, a_rows, a_cols, Bd, b_cols, reinterpret_cast<const qm31*>(r_i), (unsigned)n_ri,
                      reinterpret_cast<const qm31*>(r_j), (unsigned)n_rj, pk, fb_words);
     if (rc) return rc;
+    g_trace.mark("restrict");
     rc = run_sumcheck(ctx, ctx->fa.as<uint4>(), ctx->fb.as<uint4>(), nullptr, nullptr, pk, ch, out_round_polys,
                       out_challenges, out_final_a, out_final_b, hook);
     if (rc) return rc;
+    g_trace.mark("rounds");
     return check_err_flag(ctx, "reduce_matmul_layer");
 }
 }  // namespace zk
@@ -862,12 +896,16 @@ static int matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n
         c.mix_qm31(ldq(sd->value));
     };
     std::vector<uint32_t> chal(4 * (log_k + 1));
+    g_trace.start();
     int rc = reduce_matmul_internal(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
                                     chs, out_round_polys, chal.data(), out_final_a, out_final_b, &hook, fb_words);
     if (rc) return rc;
+    g_trace.mark("sumcheck");
     Channel ch(chs);
     ch.mix_qm31(ldq(out_final_a));
     ch.mix_qm31(ldq(out_final_b));
+    g_trace.mark("final");
+    g_trace.print();
     if (out_next_point) {
         memcpy(out_next_point, claim_point, 16 * log_m);
         memcpy(out_next_point + 4 * log_m, chal.data(), 16 * log_k);

@@ -172,6 +172,7 @@ struct zkml_ctx {
     bool restrict_tc = true;  // tensor-pipe column restriction when the layout allows (ZKML_RESTRICT_TC=0: off)
     bool la_queue = true;  // queue look-ahead kernels up front (ZKML_LA_QUEUE=0 turns it off)
     bool la_tail = true;  // single-block tail for the last look-ahead rounds (ZKML_LOOKAHEAD_TAIL=0 turns it off)
+    size_t la_tail_max = zk::LA_TAIL_MAX;  // vectors up to this length go to the tail (ZKML_LOOKAHEAD_TAIL_MAX)
     uint32_t* h_msg() const { return h_sig + 64; }  // host -> GPU words (own cache lines)
     uint32_t* d_msg() const { return d_sig + 64; }
     zk::RoundScratch round_scratch() const {

@@ -390,7 +390,7 @@ struct LaQueue {
             }
         }
         for (int j = 0; j < n; j++) {
-            if (ctx->la_tail && len[j] <= LA_TAIL_MAX) {  // the remaining rounds in one resident block
+            if (ctx->la_tail && len[j] <= ctx->la_tail_max) {  // the remaining rounds in one resident block
                 const bool wait0 = j > 0;
                 const bool f0 = wait0 || fold0;
                 const uint32_t tag_base = wait0 ? tag[j] : (n > 1 ? tag[1] - 1 : 0);
@@ -619,21 +619,8 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
     if ((rc = ctx->fa.ensure(pk * 16)) || (rc = ctx->fb.ensure(pk * 16))) return rc;
     uint4* fa = ctx->fa.as<uint4>();
     uint4* fb = ctx->fb.as<uint4>();
-    if (n_ri == 0) {  // m == 1: f_a is A's single row
-        launch_m31_to_qm31(A, k, fa, pk, ctx->err_flag(), s);
-        ctx->launches++;
-    } else {
-        if ((rc = ctx->eq_a.ensure(((size_t)16) << n_ri)) || (rc = ctx->acc_a.ensure(k * 32))) return rc;
-        launch_eq_table(r_i, n_ri, ctx->eq_a.as<uint4>(), (size_t)1 << n_ri, s);
-        ZK_CUDA(cudaMemsetAsync(ctx->acc_a.ptr, 0, k * 32, s));
-        {
-            KTimer t(ctx, KC_RESTRICT_ROWS);
-            launch_restrict_rows(A, (uint32_t)m, (uint32_t)k, ctx->eq_a.as<uint4>(),
-                                 ctx->acc_a.as<unsigned long long>(), ctx->err_flag(), s);
-        }
-        launch_acc_finalize(ctx->acc_a.as<unsigned long long>(), k, fa, pk, s);
-        ctx->launches += 3;
-    }
+    // f_b first: the column restriction streams the whole weight and is the long kernel, so it
+    // goes to the GPU before the host spends time launching the row side
     if (fb_words) {  // f_b from column-block partial sums added across ranks (zkml_restrict_cols_block)
         launch_acc_finalize(reinterpret_cast<const unsigned long long*>(fb_words), k, fb, pk, s);
         ctx->launches++;
@@ -663,6 +650,21 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
         }
         launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
         ctx->launches += 2;
+    }
+    if (n_ri == 0) {  // m == 1: f_a is A's single row
+        launch_m31_to_qm31(A, k, fa, pk, ctx->err_flag(), s);
+        ctx->launches++;
+    } else {
+        if ((rc = ctx->eq_a.ensure(((size_t)16) << n_ri)) || (rc = ctx->acc_a.ensure(k * 32))) return rc;
+        launch_eq_table(r_i, n_ri, ctx->eq_a.as<uint4>(), (size_t)1 << n_ri, s);
+        ZK_CUDA(cudaMemsetAsync(ctx->acc_a.ptr, 0, k * 32, s));
+        {
+            KTimer t(ctx, KC_RESTRICT_ROWS);
+            launch_restrict_rows(A, (uint32_t)m, (uint32_t)k, ctx->eq_a.as<uint4>(),
+                                 ctx->acc_a.as<unsigned long long>(), ctx->err_flag(), s);
+        }
+        launch_acc_finalize(ctx->acc_a.as<unsigned long long>(), k, fa, pk, s);
+        ctx->launches += 3;
     }
     return ZKML_OK;
 }
@@ -701,6 +703,11 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
         if (lv) ctx->lookahead_max = strtoull(lv, nullptr, 10);
         const char* tv = getenv("ZKML_LOOKAHEAD_TAIL");
         if (tv) ctx->la_tail = tv[0] != '0';
+        const char* tm = getenv("ZKML_LOOKAHEAD_TAIL_MAX");  // a power of two in [2, LA_TAIL_MAX]
+        if (tm) {
+            const size_t v = strtoull(tm, nullptr, 10);
+            if (v >= 2 && v <= LA_TAIL_MAX && !(v & (v - 1))) ctx->la_tail_max = v;
+        }
         const char* rv = getenv("ZKML_RESTRICT_TC");
         if (rv) ctx->restrict_tc = rv[0] != '0';
         const char* qv = getenv("ZKML_LA_QUEUE");

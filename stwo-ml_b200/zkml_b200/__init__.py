@@ -24,6 +24,7 @@ context's device (used in place).
 """
 from __future__ import annotations
 
+import collections.abc as _abc
 import ctypes as C
 import os
 import threading
@@ -336,6 +337,23 @@ class RoundPoly:
     c2: np.ndarray
 
 
+class RoundPolys(_abc.Sequence):
+    """The round polynomials of a reduction as a sequence of RoundPoly, built on access from the
+    (rounds x 12) coefficient array the library wrote (views, no copies)."""
+
+    def __init__(self, coeffs: np.ndarray):
+        self.coeffs = coeffs
+
+    def __len__(self) -> int:
+        return len(self.coeffs)
+
+    def __getitem__(self, i):
+        if isinstance(i, slice):
+            return [self[j] for j in range(*i.indices(len(self)))]
+        row = self.coeffs[i]
+        return RoundPoly(row[0:4], row[4:8], row[8:12])
+
+
 @dataclass
 class MatMulReduction:
     round_polys: List[RoundPoly]
@@ -510,26 +528,30 @@ def reduce_matmul_layer_with_backend(output_claim: GKRClaim, a: M31Matrix, b: M3
     pm, pk, pn = _next_pow2(a.rows), _next_pow2(a.cols), _next_pow2(b.cols)
     log_m, log_k, log_n = _log2(pm), _log2(pk), _log2(pn)
     point = as_qm31_array(output_claim.point)
-    value = np.ascontiguousarray(output_claim.value, np.uint32)
     abuf, bbuf = _Buf(a.data), _Buf(b.data)
     if (a.rows, a.cols, b.cols) != (m, k, n) or b.rows != k:
         raise InvalidArgument(1, "matrix shapes do not match (m, k, n)")
-    # one allocation for every output: round polynomials, final a / b, next point
-    outw = np.empty(12 * max(log_k, 1) + 8 + 4 * max(log_m + log_k, 1), np.uint32)
-    base = outw.ctypes.data
-    o_fa = 4 * 12 * max(log_k, 1)
-    o_nx = o_fa + 32
+    # one allocation (and one pointer lookup) for the point, the claimed value and every output:
+    # round polynomials, final a / b, next point
+    npw = point.size
+    n_rp = 12 * max(log_k, 1)
+    buf = np.empty(npw + 4 + n_rp + 8 + 4 * max(log_m + log_k, 1), np.uint32)
+    buf[:npw] = point.reshape(-1)
+    buf[npw:npw + 4] = np.asarray(output_claim.value, np.uint32).reshape(4)
+    base = buf.ctypes.data
+    o_rp = npw + 4
+    o_fa = o_rp + n_rp
+    o_nx = o_fa + 8
     _check(_fast_fn("zkml_reduce_matmul_layer_gkr", 14)(
-        backend.ctx.handle.value,
-        point.ctypes.data if point.size else None, len(point), value.ctypes.data, abuf.ptr.value, m, k,
-        bbuf.ptr.value, n, C.addressof(channel.state), base, base + o_fa, base + o_fa + 16, base + o_nx))
-    rp = outw[:12 * max(log_k, 1)].reshape(-1, 12)
-    fa = outw[o_fa // 4:o_fa // 4 + 4]
-    fb = outw[o_fa // 4 + 4:o_fa // 4 + 8]
-    nxt = outw[o_nx // 4:].reshape(-1, 4)
+        backend.ctx.handle.value, base if npw else None, len(point), base + 4 * npw, abuf.ptr.value, m, k,
+        bbuf.ptr.value, n, C.addressof(channel.state), base + 4 * o_rp, base + 4 * o_fa, base + 4 * o_fa + 16,
+        base + 4 * o_nx))
+    fa = buf[o_fa:o_fa + 4]
+    fb = buf[o_fa + 4:o_fa + 8]
+    nxt = buf[o_nx:].reshape(-1, 4)
     # views of this call's own fresh array (no per-round copies)
-    polys = [RoundPoly(row[0:4], row[4:8], row[8:12]) for row in rp[:log_k]]
-    red = MatMulReduction(polys, nxt[log_m:log_m + log_k], fa, fb)
+    red = MatMulReduction(RoundPolys(buf[o_rp:o_rp + n_rp].reshape(-1, 12)[:log_k]), nxt[log_m:log_m + log_k],
+                          fa, fb)
     return red, GKRClaim(nxt[:log_m + log_k], fa.copy())
 
 

@@ -1679,7 +1679,7 @@ static q31 eq_eval(const q31 *r, const q31 *s, size_t n) {
     return acc;
 }
 
-int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint32_t *claim_point, size_t n_point,
+static int orc_verify_activation_logup_impl(size_t *consumed, uint32_t *out_point, int exact, const uint64_t *calldata, size_t len, const uint32_t *claim_point, size_t n_point,
                                 const uint32_t claim_value[4], orc_channel *ch, uint32_t out_input_eval[4]) {
     oracle_init();
     felt_in in = {calldata, len, 0, 0};
@@ -1764,7 +1764,13 @@ int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint
     ch_mix_sf(ch, input_eval);
     ch_mix_sf(ch, output_eval);
     if (out_input_eval) q_store(out_input_eval, input_eval);
-    return in.pos == len && !in.bad;
+    if (consumed) *consumed = in.pos;
+    return (exact ? in.pos == len : in.pos <= len) && !in.bad;
+}
+
+int orc_verify_activation_logup(const uint64_t *calldata, size_t len, const uint32_t *claim_point, size_t n_point,
+                                const uint32_t claim_value[4], orc_channel *ch, uint32_t out_input_eval[4]) {
+    return orc_verify_activation_logup_impl(NULL, NULL, 1, calldata, len, claim_point, n_point, claim_value, ch, out_input_eval);
 }
 
 /* ---------------------------------------------------------------------------
@@ -2118,7 +2124,7 @@ static q31 replay_deg3(orc_channel *ch, felt_in *in, size_t rounds, q31 cur, q31
     return cur;
 }
 
-int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const uint32_t *claim_point,
+static int orc_verify_rmsnorm_impl(size_t *consumed, uint32_t *out_point, int exact, const uint64_t *calldata, size_t len, size_t dim, const uint32_t *claim_point,
                        size_t n_point, const uint32_t claim_value[4], orc_channel *ch, uint32_t out_input_eval[4]) {
     oracle_init();
     felt_in in = {calldata, len, 0, 0};
@@ -2232,7 +2238,14 @@ int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const u
     ch_mix_sf(ch, input_eval);
     ch_mix_sf(ch, output_eval);
     if (out_input_eval) q_store(out_input_eval, input_eval);
-    return in.pos == len && !in.bad;
+    if (consumed) *consumed = in.pos;
+    return (exact ? in.pos == len : in.pos <= len) && !in.bad;
+}
+
+int orc_verify_rmsnorm(const uint64_t *calldata, size_t len, size_t dim, const uint32_t *claim_point,
+                       size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
+                       uint32_t out_input_eval[4]) {
+    return orc_verify_rmsnorm_impl(NULL, NULL, 1, calldata, len, dim, claim_point, n_point, claim_value, ch, out_input_eval);
 }
 
 /* ---------------------------------------------------------------------------
@@ -2679,7 +2692,7 @@ int orc_reduce_activation_piecewise(const uint32_t *input, size_t rows, size_t c
 }
 
 /* verify_piecewise_activation_reduction (gkr/verifier.rs:3298-3480) on such a record. */
-int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const uint32_t *claim_point,
+static int orc_verify_activation_piecewise_impl(size_t *consumed, uint32_t *out_point, int exact, const uint64_t *calldata, size_t len, const uint32_t *claim_point,
                                     size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
                                     uint32_t out_input_eval[4]) {
     oracle_init();
@@ -2729,7 +2742,15 @@ int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const 
     for (int i = 0; i < 16; i++) ch_mix_sf(ch, ind[i]);
     for (int k = 0; k < 4; k++) ch_mix_sf(ch, sb[k]);
     if (out_input_eval) q_store(out_input_eval, input_eval);
-    return in.pos == len;
+    if (out_point) memcpy(out_point, chal, sizeof(q31) * nv);
+    if (consumed) *consumed = in.pos;
+    return (exact ? in.pos == len : in.pos <= len) && !in.bad;
+}
+
+int orc_verify_activation_piecewise(const uint64_t *calldata, size_t len, const uint32_t *claim_point,
+                                    size_t n_point, const uint32_t claim_value[4], orc_channel *ch,
+                                    uint32_t out_input_eval[4]) {
+    return orc_verify_activation_piecewise_impl(NULL, NULL, 1, calldata, len, claim_point, n_point, claim_value, ch, out_input_eval);
 }
 
 /* ---------------------------------------------------------------------------
@@ -3107,15 +3128,13 @@ typedef struct {
 
 #define CHAIN_MAX 1024
 
-int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
-                        const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
-                        size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads) {
-    oracle_init();
-    if (n_layers == 0 || n_layers > CHAIN_MAX) return 1;
+/* The chain's forward pass (compiler/prove.rs:1893-1899 and the layer functions it calls):
+ * outs[0] = the model input, outs[l + 1] = layer l's output (m x width[l + 1]); src[l] = the
+ * layer feeding layer l.  outs, width and src have n_layers + 1 entries; on failure every
+ * allocated output is freed.  Returns 0 or 1 (a bad layer list). */
+static int chain_forward(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
+                         int threads, uint32_t **outs, size_t *width, long long *src) {
     /* forward pass: outs[0] is the model input, outs[l + 1] layer l's output (m x width[.]) */
-    uint32_t **outs = (uint32_t **)calloc(n_layers + 1, sizeof(uint32_t *));
-    size_t *width = (size_t *)calloc(n_layers + 1, sizeof(size_t));
-    long long *src = (long long *)calloc(n_layers, sizeof(long long));
     outs[0] = (uint32_t *)malloc(4 * m * k0);
     for (size_t i = 0; i < m * k0; i++) outs[0][i] = m_red64(input[i]);
     width[0] = k0;
@@ -3191,7 +3210,24 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
         }
     }
     if (rc) {
-        for (size_t l = 0; l <= built; l++) free(outs[l]);
+        for (size_t l = 0; l <= built; l++) {
+            free(outs[l]);
+            outs[l] = NULL;
+        }
+    }
+    return rc;
+}
+
+int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
+                        const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
+                        size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads) {
+    oracle_init();
+    if (n_layers == 0 || n_layers > CHAIN_MAX) return 1;
+    uint32_t **outs = (uint32_t **)calloc(n_layers + 1, sizeof(uint32_t *));
+    size_t *width = (size_t *)calloc(n_layers + 1, sizeof(size_t));
+    long long *src = (long long *)calloc(n_layers + 1, sizeof(long long));
+    int rc = chain_forward(input, m, k0, layers, n_layers, threads, outs, width, src);
+    if (rc) {
         free(outs);
         free(width);
         free(src);
@@ -3551,4 +3587,189 @@ int orc_reduce_activation_relu(const uint32_t *input, size_t rows, size_t cols, 
     if (out_input_eval) q_store(out_input_eval, val);
     if (out_point) memcpy(out_point, nxt, sizeof(q31) * nv);
     return o.overflow ? 2 : 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Verifier of a chain proof (gkr/verifier.rs: verify_gkr's layer walk)      */
+/* ------------------------------------------------------------------------ */
+
+/* verify_gkr for a chain of Linear, Activation (LogUp or piecewise) and RMSNorm layers, proven
+ * by orc_prove_gkr_chain / zkml_prove_gkr_chain and serialized by serialize_gkr_model_proof.
+ * The verifier recomputes the model output from the input and the weights (the claimed io), then
+ * replays the transcript: the prefix and output claim (prover.rs:1516-1561), each layer record
+ * from the output to the input with the layer verifiers of this file (the matmul reduction as
+ * verifier.rs:2675-2788 checks it), the input claim against the input MLE, every weight's
+ * commitment against its column-major MLE, every Sequential opening
+ * (mle_opening.rs:1918-2029) at the point the walk produced, and the io commitment.  Returns 1
+ * if the proof is accepted; layer kinds other than these three are not handled (returns 0). */
+int orc_verify_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
+                         const uint64_t *policy, size_t n_queries, int flags, const uint64_t *calldata, size_t len,
+                         uint64_t digest[4], int threads) {
+    oracle_init();
+    if (n_layers == 0 || n_layers > CHAIN_MAX) return 0;
+    for (size_t l = 0; l < n_layers; l++) {
+        const int t = layers[l].type;
+        if ((t != 0 && t != 2 && t != 6) || layers[l].src != ORC_CHAIN_PREV) return 0;
+    }
+    uint32_t **outs = (uint32_t **)calloc(n_layers + 1, sizeof(uint32_t *));
+    size_t *width = (size_t *)calloc(n_layers + 1, sizeof(size_t));
+    long long *src = (long long *)calloc(n_layers + 1, sizeof(long long));
+    int ok = chain_forward(input, m, k0, layers, n_layers, threads, outs, width, src) == 0;
+    const int logup = (flags & 4) != 0;
+    felt_in in = {calldata, len, 0, 0};
+    orc_channel ch;
+    orc_ch_init(&ch);
+    const size_t wout = width[n_layers];
+    const unsigned log_m = ilog2(next_pow2(m));
+    const unsigned nvo = log_m + ilog2(next_pow2(wout));
+    q31 point[64], value = q_from_m(0);
+    unsigned npt = nvo;
+    /* weight claims in walk order */
+    size_t *wl = (size_t *)calloc(n_layers, sizeof(size_t));
+    q31 (*wpt)[64] = (q31(*)[64])calloc(n_layers, sizeof(q31[64]));
+    unsigned *wnv = (unsigned *)calloc(n_layers, sizeof(unsigned));
+    q31 *wval = (q31 *)calloc(n_layers, sizeof(q31));
+    size_t nw = 0;
+    if (ok) {
+        orc_ch_mix_u64(&ch, n_layers);
+        orc_ch_mix_u64(&ch, m);
+        orc_ch_mix_u64(&ch, k0);
+        if (policy && (policy[0] | policy[1] | policy[2] | policy[3])) orc_ch_mix_felt(&ch, policy);
+        for (unsigned i = 0; i < nvo; i++) point[i] = ch_draw_qm31(&ch);
+        q31 *omle = mle_row_major(outs[n_layers], m, wout);
+        uint32_t val[4];
+        orc_evaluate_mle((const uint32_t *)omle, nvo, (const uint32_t *)point, val);
+        free(omle);
+        value = q_load(val);
+        ch_mix_sf(&ch, value);
+        if (in_u64(&in) != n_layers) ok = 0;
+    }
+    for (size_t li = n_layers; li-- > 0 && ok;) {
+        const size_t w = width[li];
+        const int t = layers[li].type;
+        if (t == 0) {
+            /* verify_matmul_reduction: mix m, k, n and the claim, the compressed rounds, the final product */
+            const size_t n = layers[li].n;
+            const unsigned log_k = ilog2(next_pow2(w)), log_n = ilog2(next_pow2(n));
+            if (in_u64(&in) != 0 || in_u64(&in) != log_k || npt != log_m + log_n) {
+                ok = 0;
+                break;
+            }
+            orc_ch_mix_u64(&ch, m);
+            orc_ch_mix_u64(&ch, w);
+            orc_ch_mix_u64(&ch, n);
+            ch_mix_sf(&ch, value);
+            q31 cur = value, chal[64];
+            for (unsigned r = 0; r < log_k; r++) {
+                q31 c0 = in_qm31(&in), c2 = in_qm31(&in);
+                q31 c1 = q_sub(q_sub(cur, q_add(c0, c0)), c2);
+                uint32_t coeffs[12];
+                q_store(coeffs, c0);
+                q_store(coeffs + 4, c1);
+                q_store(coeffs + 8, c2);
+                orc_ch_mix_poly_coeffs(&ch, coeffs);
+                chal[r] = ch_draw_qm31(&ch);
+                cur = q_add(c0, q_add(q_mul(c1, chal[r]), q_mul(c2, q_mul(chal[r], chal[r]))));
+            }
+            q31 fa = in_qm31(&in), fb = in_qm31(&in);
+            if (!q_eq(cur, q_mul(fa, fb))) ok = 0;
+            ch_mix_sf(&ch, fa);
+            ch_mix_sf(&ch, fb);
+            /* weight claim r_j || challenges (prover.rs:1465-1483) */
+            wl[nw] = li;
+            wnv[nw] = log_n + log_k;
+            memcpy(wpt[nw], point + log_m, sizeof(q31) * log_n);
+            memcpy(wpt[nw] + log_n, chal, sizeof(q31) * log_k);
+            wval[nw] = fb;
+            nw++;
+            memcpy(point + log_m, chal, sizeof(q31) * log_k);
+            npt = log_m + log_k;
+            value = fa;
+        } else {
+            /* activation / RMSNorm records: the record's own verifier on the rest of the calldata */
+            size_t used = 0;
+            uint32_t cv[4], ie[4];
+            q31 nxt[64];
+            q_store(cv, value);
+            const uint64_t *rec = calldata + 4 * in.pos;
+            const size_t rest = len - in.pos;
+            if (t == 2)
+                ok = orc_verify_rmsnorm_impl(&used, NULL, 0, rec, rest, w, (const uint32_t *)point, npt, cv, &ch, ie);
+            else if (logup)
+                ok = orc_verify_activation_logup_impl(&used, NULL, 0, rec, rest, (const uint32_t *)point, npt, cv, &ch,
+                                                      ie);
+            else
+                ok = orc_verify_activation_piecewise_impl(&used, (uint32_t *)nxt, 0, rec, rest,
+                                                          (const uint32_t *)point, npt, cv, &ch, ie);
+            if (ok && t == 6 && !logup) memcpy(point, nxt, sizeof(q31) * npt);
+            in.pos += used;
+            value = q_load(ie);
+        }
+    }
+    /* the input claim: the walk's point and value, and the input MLE there */
+    if (ok) {
+        if (in_u64(&in) != npt) ok = 0;
+        for (unsigned i = 0; i < npt && ok; i++)
+            if (!q_eq(in_qm31(&in), point[i])) ok = 0;
+        if (ok && !q_eq(in_qm31(&in), value)) ok = 0;
+        if (ok) {
+            q31 *imle = mle_row_major(outs[0], m, k0);
+            uint32_t ev[4];
+            orc_evaluate_mle((const uint32_t *)imle, npt, (const uint32_t *)point, ev);
+            free(imle);
+            if (!q_eq(q_load(ev), value)) ok = 0;
+        }
+    }
+    /* weight commitments, then the Sequential openings in walk order on the main channel */
+    fe *coms = (fe *)calloc(nw + 1, sizeof(fe));
+    if (ok && in_u64(&in) != nw) ok = 0;
+    for (size_t i = 0; i < nw && ok; i++) {
+        in_felt(&in, &coms[i]);
+        const size_t l = wl[i];
+        q31 *bmle = mle_col_major(layers[l].weight, width[l], layers[l].n, threads);
+        fe expect;
+        merkle_root(bmle, next_pow2(width[l]) * next_pow2(layers[l].n), &expect, threads);
+        free(bmle);
+        if (memcmp(expect.v, coms[i].v, 32)) ok = 0;
+    }
+    if (ok && in_u64(&in) != nw) ok = 0;
+    for (size_t i = 0; i < nw && ok; i++) {
+        if (in_u64(&in) != wnv[i]) ok = 0;
+        for (unsigned j = 0; j < wnv[i] && ok; j++)
+            if (!q_eq(in_qm31(&in), wpt[i][j])) ok = 0;
+        if (ok && !q_eq(in_qm31(&in), wval[i])) ok = 0;
+        if (!ok) break;
+        const size_t start = in.pos;
+        felt_in sub = {calldata + 4 * start, len - start, 0, 0};
+        orc_channel probe = ch;
+        q31 fv;
+        ok = verify_opening(&coms[i], &sub, wpt[i], wnv[i], &probe, n_queries, &fv);
+        if (ok) {
+            uint32_t fvv[4];
+            ok = orc_verify_mle_opening(coms[i].v, calldata + 4 * start, sub.pos, (const uint32_t *)wpt[i], wnv[i],
+                                        &ch, n_queries, fvv);
+            if (ok && !q_eq(q_load(fvv), wval[i])) ok = 0;
+        }
+        in.pos = start + sub.pos;
+    }
+    /* io commitment */
+    if (ok) {
+        fe iof;
+        in_felt(&in, &iof);
+        uint64_t io[4];
+        orc_io_commitment(outs[0], m, k0, outs[n_layers], m, wout, io);
+        if (memcmp(io, iof.v, 32)) ok = 0;
+        if (in.pos != len || in.bad) ok = 0;
+    }
+    if (digest) memcpy(digest, ch.digest, 32);
+    for (size_t l = 0; l <= n_layers; l++) free(outs[l]);
+    free(outs);
+    free(width);
+    free(src);
+    free(wl);
+    free(wpt);
+    free(wnv);
+    free(wval);
+    free(coms);
+    return ok;
 }

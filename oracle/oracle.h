@@ -238,6 +238,15 @@ int orc_prove_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_ch
                         const uint64_t *policy, size_t n_queries, int flags, uint64_t *calldata, size_t cap,
                         size_t *out_len, uint64_t digest[4], uint64_t io[4], int threads);
 
+/* verify_gkr (gkr/verifier.rs) on a chain proof of Linear, Activation (GELU / Sigmoid / Softmax /
+ * SiLU; flags bit 2 as for orc_prove_gkr_chain) and RMSNorm layers, each fed by the previous
+ * one: the output recomputed from the input and weights, every layer record replayed with its
+ * verifier, the input claim, the weight commitments and Sequential openings, the io commitment.
+ * Writes the verifier channel's final digest.  Returns 1 if accepted. */
+int orc_verify_gkr_chain(const uint32_t *input, size_t m, size_t k0, const orc_chain_layer *layers, size_t n_layers,
+                         const uint64_t *policy, size_t n_queries, int flags, const uint64_t *calldata, size_t len,
+                         uint64_t digest[4], int threads);
+
 /* reduce_activation_layer_algebraic (gkr/prover.rs:6700-6890), the ReLU proof, serialized as
  * LayerProof::Activation with the activation product proof (cairo_serde.rs:1355-1387,
  * 1190-1235).  out_point receives the next claim's point (the sumcheck challenges). */

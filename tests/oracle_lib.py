@@ -420,6 +420,24 @@ def prove_gkr_chain(inp, layers, n_queries=10, policy=None, legacy_layout=False,
     return rc, buf[:4 * ln.value].copy(), felt_int(dig), felt_int(io)
 
 
+def verify_gkr_chain(inp, layers, raw, n_queries=10, policy=None, activation_logup=False):
+    """orc_verify_gkr_chain on a serialize_gkr_model_proof of a Linear / Activation / RMSNorm
+    chain: (accepted, verifier digest)."""
+    inp = np.ascontiguousarray(inp, np.uint32)
+    m, k0 = inp.shape
+    arr, keep = chain_layers(layers)
+    raw = np.ascontiguousarray(raw, np.uint64)
+    dig = np.zeros(4, np.uint64)
+    pol = None if policy is None else felt(policy)
+    L = lib()
+    L.orc_verify_gkr_chain.argtypes = [u32p, C.c_size_t, C.c_size_t, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t,
+                                       C.c_int, u64p, C.c_size_t, u64p, C.c_int]
+    ok = L.orc_verify_gkr_chain(inp.reshape(-1), m, k0, C.cast(arr, C.c_void_p), len(layers),
+                                None if pol is None else pol.ctypes.data_as(C.c_void_p), n_queries,
+                                4 if activation_logup else 0, raw, raw.size // 4, dig, threads())
+    return bool(ok), felt_int(dig)
+
+
 def reduce_activation_relu(inp, point, value, ch, cap=1 << 14):
     inp = np.ascontiguousarray(inp, np.uint32)
     rows, cols = inp.shape

@@ -62,3 +62,24 @@ def test_chain_with_rmsnorm_runs_and_is_deterministic():
     assert rc == rc2 == 0 and (raw == raw2).all() and dig == dig2
     f = [O.felt_int(raw[4 * i:4 * i + 4]) for i in range(raw.size // 4)]
     assert f[0] == len(layers) and f[1] == 8  # first record is the output RMSNorm (tag 8)
+
+
+def test_oracle_transformer_chain_verifies_and_rejects_tampering():
+    """The oracle's chain verifier (verify_gkr's walk, restated) accepts the oracle's transformer
+    proofs with both SiLU reductions and ends on the prover's digest; a flipped felt is rejected."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "stwo-ml_b200"))
+    from helpers import int_matrix_m31
+    from zkml_b200.circuits import hf_transformer_layers
+    x = int_matrix_m31(2, 8, 1)
+    for act, logup in (("silu", False), ("silu", True), ("gelu", False), ("sigmoid", True)):
+        layers = hf_transformer_layers(8, 8, 16, 2, lambda i, r, c: int_matrix_m31(r, c, 100 + i), act)
+        rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=4, activation_logup=logup, cap=1 << 22)
+        assert rc == 0
+        ok, vdig = O.verify_gkr_chain(x, layers, raw, n_queries=4, activation_logup=logup)
+        assert ok and vdig == dig
+        for pos in (4 * 3, 4 * 150, raw.size - 8):
+            bad = raw.copy()
+            bad[pos] ^= 1
+            assert not O.verify_gkr_chain(x, layers, bad, n_queries=4, activation_logup=logup)[0]

@@ -30,6 +30,8 @@ def test_small_transformer_chain_matches_oracle(m, d, q_dim, d_ff, blocks, act, 
     proof = Z.prove_gkr_chain(x, layers, n_queries=4, activation_logup=logup)
     assert proof.raw.size == raw.size and (proof.raw == raw).all()
     assert proof.final_digest == dig and proof.io_commitment == io
+    ok, vdig = O.verify_gkr_chain(x, layers, proof.raw, n_queries=4, activation_logup=logup)
+    assert ok and vdig == proof.final_digest
 
 
 @pytest.mark.parametrize("mode", ["piecewise", "logup"])
@@ -48,6 +50,9 @@ def test_smollm2_two_blocks_matches_oracle_fixture(mode):
     assert hashlib.sha256(proof.raw.astype("<u8").tobytes()).hexdigest() == want["sha256"]
     assert proof.final_digest == int(want["final_digest"], 16)
     assert proof.io_commitment == int(want["io_commitment"], 16)
+    if mode == "piecewise":  # the oracle's verifier replays the whole GPU proof (the default reduction)
+        ok, vdig = O.verify_gkr_chain(x, layers, proof.raw, n_queries=fx["n_queries"], activation_logup=False)
+        assert ok and vdig == proof.final_digest
 
 
 def test_transformer_chain_v1_calldata_matches_oracle():

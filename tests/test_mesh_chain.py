@@ -1,6 +1,6 @@
 """The GKR chain prover with the weight openings' Merkle hashing split over the peer mesh, on 2
-and 4 GPUs: every rank's proof equals the one-GPU proof byte for byte, for a transformer block
-whose weight MLEs are large enough to split (skipped with fewer GPUs)."""
+and 4 GPUs: every rank's proof equals the one-GPU proof byte for byte, and the oracle's chain verifier accepts
+it, for transformer blocks whose weight MLEs are large enough to split (skipped with fewer GPUs)."""
 import os
 import socket
 import sys
@@ -45,7 +45,7 @@ def _worker(rank, world, port, out_dir):
     try:
         for i in range(len(SHAPES)):
             x, layers = _case(i)
-            proof = Z.prove_gkr_chain(x, layers, n_queries=6, mesh=mesh)
+            proof = Z.prove_gkr_chain(x, layers, n_queries=6, mesh=mesh, activation_logup=False)
             np.save(os.path.join(out_dir, f"r{rank}_c{i}.npy"), proof.raw)
         torch.cuda.synchronize()
         dist.barrier()
@@ -60,11 +60,13 @@ def test_mesh_chain_equals_one_gpu(world, tmp_path):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     mp.start_processes(_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True, start_method="spawn")
-    sys.path[:0] = [str(ROOT / "stwo-ml_b200")]
+    sys.path[:0] = [str(ROOT / "stwo-ml_b200"), str(ROOT / "tests")]
+    import oracle_lib as O
     import zkml_b200 as Z
     for i in range(len(SHAPES)):
         x, layers = _case(i)
-        ref = Z.prove_gkr_chain(x, layers, n_queries=6).raw
+        ref = Z.prove_gkr_chain(x, layers, n_queries=6, activation_logup=False).raw
+        assert O.verify_gkr_chain(x, layers, ref, n_queries=6, activation_logup=False)[0]
         for r in range(world):
             got = np.load(tmp_path / f"r{r}_c{i}.npy")
             assert got.size == ref.size and (got == ref).all(), (i, r)

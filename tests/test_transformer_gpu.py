@@ -79,3 +79,19 @@ def test_activation_forward_matches_oracle_on_full_range():
         assert rc == 0
         proof = Z.prove_gkr_chain(v, layers, n_queries=2, activation_logup=True)
         assert proof.io_commitment == io and proof.final_digest == dig
+
+
+def test_qwen_decoder_layer_reduced_width_matches_oracle_and_verifies():
+    """The config-4 layer (Qwen2.5-14B recipe: 64 tokens, 16-bit activations, SwiGLU ratio
+    13824 / 5120) at a reduced width: bit-exact against the oracle with the LogUp SiLU (the
+    STWO_PIECEWISE_ACTIVATION=0 pin) and accepted by the oracle's chain verifier."""
+    m, d, d_ff = 64, 128, 346
+    x = int_matrix_m31(m, d, 414, bound=32767)
+    layers = hf_transformer_layers(d, d, d_ff, 1, lambda i, r, c: int_matrix_m31(r, c, 41400 + i, bound=127), "silu")
+    rc, raw, dig, io = O.prove_gkr_chain(x, layers, n_queries=10, activation_logup=True, cap=1 << 22)
+    assert rc == 0
+    proof = Z.prove_gkr_chain(x, layers, n_queries=10, activation_logup=True)
+    assert proof.raw.size == raw.size and (proof.raw == raw).all()
+    assert proof.final_digest == dig and proof.io_commitment == io
+    ok, vdig = O.verify_gkr_chain(x, layers, proof.raw, n_queries=10, activation_logup=True)
+    assert ok and vdig == dig

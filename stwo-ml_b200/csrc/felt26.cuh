@@ -110,10 +110,14 @@ __device__ __forceinline__ f26 norm26(const f26& a) {
 }
 
 // Value below 2^256 (limbs up to 2^30, as left by a few additions) -> a
-// representative below 2p with 26-bit limbs: q = floor(v / 2^251) is floor(v / p)
-// or one more, so v - max(q - 1, 0) p lies in [0, 2p).
+// representative below 3p with 26-bit limbs, with one carry pass.  The carry the
+// lower limbs would bring into limb 9 is below 2^4, so q = l9 >> 17 of the
+// unnormalised top limb is floor(v / 2^251) or one less, floor(v / 2^251) is
+// floor(v / p) or one more, and subtracting max(q - 1, 0) p limb-wise (limbs may
+// go negative; the value does not) leaves v - q' p in [0, 3p).  Every lane the
+// permutation keeps below 3p keeps its sums below 2^256 (bounds at each use).
 __device__ __forceinline__ f26 red26(const f26& a) {
-    f26 n = norm26(a);
+    f26 n = a;
     uint32_t q = n.l[9] >> 17;
     q -= (q != 0);
     n.l[0] -= q;
@@ -133,8 +137,9 @@ struct F26Consts {
 static __constant__ F26Consts c26;
 
 // Full rounds: every lane through the S-box, then the MDS matrix
-// [[3,1,1],[1,-1,1],[1,1,-2]].  Inputs below 2p keep every intermediate below
-// 2^256; outputs are reduced below 2p.
+// [[3,1,1],[1,-1,1],[1,1,-2]].  Inputs below 3p keep every intermediate below
+// 2^256 (S-box inputs below 4p, outputs below 1.2p, sums below 7.6p); outputs are
+// reduced below 3p.
 __device__ __forceinline__ void full_round26(f26 s[3], const f26* rc) {
     const f26 y0 = cube26(add26(s[0], rc[0]));
     const f26 y1 = cube26(add26(s[1], rc[1]));
@@ -152,27 +157,27 @@ __device__ __forceinline__ void full_round26(f26 s[3], const f26* rc) {
     s[2] = red26(n2);
 }
 
-// Hades on Montgomery (2^260) lanes below 2p; the result lanes are below 2p.
+// Hades on Montgomery (2^260) lanes below 3p; the result lanes are below 3p.
 // The 83 partial rounds keep lane 2 as x = s2 + key (compressed schedule: one
 // key per partial round).
 __device__ __forceinline__ void hades26(f26 s[3]) {
 #pragma unroll 1
     for (int r = 0; r < 4; r++) full_round26(s, c26.rc + 3 * r);
     f26 s0 = s[0], s1 = s[1];
-    f26 x = add26(s[2], c26.rc[12]);  // < 3p
+    f26 x = add26(s[2], c26.rc[12]);  // < 4p
 #pragma unroll 1
     for (int r = 0; r < 83; r++) {
         const f26 y = cube26(x);                    // < 1.2p
-        const f26 u = add26(s0, s1);                // < 4p
-        const f26 t = add26(u, y);                  // < 5.2p
-        f26 n0 = add26(add26(t, s0), s0);           // < 9.2p
+        const f26 u = add26(s0, s1);                // < 6p
+        const f26 t = add26(u, y);                  // < 7.2p
+        f26 n0 = add26(add26(t, s0), s0);           // < 13.2p
         f26 n1, xn;
         // w = s0 + s1 (+ the next round's key): the next lane-2 value is w - 2y
-        const f26 w = red26(r + 1 < 83 ? add26(u, c26.rc[13 + r]) : u);  // < 2p
+        const f26 w = red26(r + 1 < 83 ? add26(u, c26.rc[13 + r]) : u);  // < 3p
 #pragma unroll
         for (int i = 0; i < 10; i++) {
-            n1.l[i] = t.l[i] + c26.kp4.l[i] - 2 * s1.l[i];               // < 9.2p
-            xn.l[i] = w.l[i] + c26.kp4.l[i] - 2 * y.l[i];                // < 6p, limbs >= 0
+            n1.l[i] = t.l[i] + c26.kp4.l[i] - 2 * s1.l[i];               // t >= s1: in (0, 11.2p)
+            xn.l[i] = w.l[i] + c26.kp4.l[i] - 2 * y.l[i];                // 2y < 2.4p: in (0, 7p), limbs >= 0
         }
         s0 = red26(n0);
         s1 = red26(n1);

@@ -67,7 +67,7 @@ __device__ __forceinline__ f26 m256_to_m260(const dfelt& m) {
     return norm26(a);
 }
 
-// Montgomery (2^260) lane below 2p -> canonical Montgomery (2^256) node value.
+// Montgomery (2^260) lane below 3p -> canonical Montgomery (2^256) node value.
 __device__ __forceinline__ dfelt m260_to_m256(const f26& x) {
     const f26 r = mul26(x, c26.one256);  // < 1.01 p, 26-bit limbs
     f26 d = r;

@@ -164,7 +164,7 @@ __device__ __forceinline__ void hades26(f26 s[3]) {
 #pragma unroll 1
     for (int r = 0; r < 4; r++) full_round26(s, c26.rc + 3 * r);
     f26 s0 = s[0], s1 = s[1];
-    f26 x = add26(s[2], c26.rc[12]);  // < 4p
+    f26 x = add26(s[2], c26.rc[12]);  // < 4p (lane 2 stays below 11p)
 #pragma unroll 1
     for (int r = 0; r < 83; r++) {
         const f26 y = cube26(x);                    // < 1.2p
@@ -172,12 +172,13 @@ __device__ __forceinline__ void hades26(f26 s[3]) {
         const f26 t = add26(u, y);                  // < 7.2p
         f26 n0 = add26(add26(t, s0), s0);           // < 13.2p
         f26 n1, xn;
-        // w = s0 + s1 (+ the next round's key): the next lane-2 value is w - 2y
-        const f26 w = red26(r + 1 < 83 ? add26(u, c26.rc[13 + r]) : u);  // < 3p
+        // w = s0 + s1 (+ the next round's key), left unreduced: the next lane-2
+        // value is w - 2y, below 11p with limbs below 2^29, which the S-box takes
+        const f26 w = r + 1 < 83 ? add26(u, c26.rc[13 + r]) : u;  // < 7p, limbs < 3 * 2^26
 #pragma unroll
         for (int i = 0; i < 10; i++) {
             n1.l[i] = t.l[i] + c26.kp4.l[i] - 2 * s1.l[i];               // t >= s1: in (0, 11.2p)
-            xn.l[i] = w.l[i] + c26.kp4.l[i] - 2 * y.l[i];                // 2y < 2.4p: in (0, 7p), limbs >= 0
+            xn.l[i] = w.l[i] + c26.kp4.l[i] - 2 * y.l[i];                // 2y < 2.4p: in (0, 11p), limbs >= 0
         }
         s0 = red26(n0);
         s1 = red26(n1);

@@ -109,6 +109,14 @@ struct zkml_ctx {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     cudaStream_t own_stream = nullptr;
+    // The row side of a restriction runs on side_stream under the column side
+    // (fork / join events; off with ZKML_ROW_SIDE_STREAM=0 or while kernel timing is on).
+    cudaStream_t side_stream = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    bool row_side_stream = true;
+    // Queued look-ahead kernels that wait for a challenge launch as programmatic
+    // dependents of the kernel before them (ZKML_LA_PDL=0: plain launches).
+    bool la_pdl = true;
     uint64_t launches = 0;
     // scratch
     zk::DevBuf a_in, b_in;          // device copies of host inputs
@@ -163,6 +171,8 @@ struct zkml_ctx {
     uint32_t* persist_status() const { return small.as<uint32_t>() + 60; }
     uint32_t* la_mailbox() const { return small.as<uint32_t>() + 4; }  // words 4-9
     uint32_t* la_status() const { return small.as<uint32_t>() + 61; }  // look-ahead wait timed out
+    // 40 u64 look-ahead accumulators, words 64-143 (zero between kernels)
+    unsigned long long* la_acc() const { return reinterpret_cast<unsigned long long*>(small.as<uint32_t>() + 64); }
     // challenge slots of the pre-queued look-ahead kernels: LA_SLOTS x 8 words
     // (sequence tag, 4 challenge words, abort) from word 256 of the mapped page
     static constexpr int LA_SLOTS = 32;
@@ -183,6 +193,7 @@ struct zkml_ctx {
         r.max_blocks = max_round_blocks;
         r.sig = nullptr;
         r.seq = 0;
+        r.la_acc = la_acc();
         return r;
     }
 };

@@ -60,6 +60,9 @@ struct RoundScratch {
     // Optional peer mesh (launch_round_m31, launch_fold_round_m31 / _qm31, launch_round_qm31):
     // the last block adds every rank's 12 words before it stores or publishes them.
     MeshArg mesh{nullptr, 0};
+    // Look-ahead rounds: LA_WORDS zero-initialised 64-bit accumulators (left zero
+    // by every launch_round_lookahead kernel).
+    unsigned long long* la_acc = nullptr;
 };
 // Reduce n u32 words in place to [0, P) (the round kernels need canonical QM31 input).
 void launch_canon_words(uint32_t* w, size_t n, cudaStream_t s);
@@ -87,20 +90,30 @@ void launch_fold_round_m31(const uint32_t* A, const uint32_t* B, size_t len, qm3
 // or a poll that runs past its limit skips the arithmetic (the latter also sets
 // *status), and the kernel still publishes so that the queue drains.  Only
 // block 0 polls host memory; it forwards the slot to the other blocks through
-// `mailbox` (6 words of device memory).
+// `mailbox` (6 words of device memory).  With err_word, the last round (L = 2)
+// also publishes *err_word and *status as words 40-41.  pdl launches it as a
+// programmatic dependent of the stream's previous kernel (resident early): only
+// for a kernel that waits for a challenge the host posts after the previous
+// kernel published, since the vectors are read after that challenge is seen.
 void launch_round_lookahead(uint4* A, uint4* B, size_t L, bool fold, qm31 alpha, const RoundScratch& rs,
                             cudaStream_t s, const uint32_t* wait_msg = nullptr, uint32_t wait_seq = 0,
-                            uint32_t* status = nullptr, uint32_t* mailbox = nullptr);
+                            uint32_t* status = nullptr, uint32_t* mailbox = nullptr,
+                            const uint32_t* err_word = nullptr, bool pdl = false);
 // All remaining look-ahead rounds in one single-block launch (vectors in shared
 // memory).  The L0 input elements (L0 <= 2 * LA_TAIL_MAX) are folded first when
 // fold0 is set, with alpha0 or, if wait0, with the challenge posted to round
 // 0's slot.  Round j publishes sequence seq_base + j and (j > 0, or j = 0 with
 // wait0) waits for tag tag_base + j in the 8-word slot (tag_base + j) % slots
-// of msg.  Returns nonzero if the launch could not be configured.
+// of msg.  With err_word, the last round also publishes *err_word and *status
+// as words 40-41.  pdl as for launch_round_lookahead (wait0 set).  Returns
+// nonzero if the launch could not be configured.
 constexpr size_t LA_TAIL_MAX = 2048;
+void la_stamps_enable(bool on);
+void la_stamps_print(uint32_t lo, uint32_t hi);
 int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0, bool wait0, qm31 alpha0,
                           uint32_t* sig, uint32_t seq_base, const uint32_t* msg, uint32_t tag_base, int slots,
-                          uint32_t* status, cudaStream_t s);
+                          uint32_t* status, cudaStream_t s, const uint32_t* err_word = nullptr,
+                          bool pdl = false);
 // Rank-major gathered shards [g][A: len | B: len] -> fa, fb in global order
 // (global[j * G + g] = local_g[j]).
 void launch_interleave_gather(const uint4* in, size_t len, size_t G, uint4* fa, uint4* fb, cudaStream_t s);

@@ -326,7 +326,7 @@ static int run_sumcheck_persistent(zkml_ctx* ctx, uint4* A, uint4* B, const uint
 // The sumcheck round loop over (A, B).  In M31 mode A32/B32 hold the base-field
 // vectors (length len) and the first fold writes QM31 into ctx->fa / fb.
 // Host side of the look-ahead rounds (launch_round_lookahead).
-constexpr int LA_WORDS_HOST = 40;
+constexpr int LA_WORDS_HOST = 42;  // 40 words + the last round's two error words
 
 // Round r's own sums from its look-ahead words (len = |V_r|).
 static void la_round_sums(const uint32_t* w, size_t len, uint32_t s12[12]) {
@@ -395,7 +395,8 @@ struct LaQueue {
                 const bool f0 = wait0 || fold0;
                 const uint32_t tag_base = wait0 ? tag[j] : (n > 1 ? tag[1] - 1 : 0);
                 if (launch_lookahead_tail(A, B, f0 ? 2 * len[j] : len[j], f0, wait0, alpha0, rs.sig, seq[j],
-                                          ctx->d_la_msg(), tag_base, zkml_ctx::LA_SLOTS, ctx->la_status(), s))
+                                          ctx->d_la_msg(), tag_base, zkml_ctx::LA_SLOTS, ctx->la_status(), s,
+                                          ctx->err_flag(), wait0 && ctx->la_pdl))
                     return set_error(ZKML_ERR_CUDA, "cannot configure the look-ahead tail kernel");
                 ZK_CUDA(cudaGetLastError());
                 ctx->launches++;
@@ -413,7 +414,7 @@ struct LaQueue {
         {
             KTimer t(ctx, KC_ROUND, wait_msg == nullptr);
             launch_round_lookahead(A, B, len[j], fold, alpha, rs, stream, wait_msg, wait_tag, ctx->la_status(),
-                                   ctx->la_mailbox());
+                                   ctx->la_mailbox(), ctx->err_flag(), queued && wait_msg && ctx->la_pdl);
         }
         ZK_CUDA(cudaGetLastError());
         ctx->launches++;
@@ -562,6 +563,9 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
                 stq(fa_out, qadd(a0, qmul(alpha, qsub(a1, a0))));
                 stq(fb_out, qadd(b0, qmul(alpha, qsub(b1, b0))));
                 g_trace.mark("last");
+                // The last kernel read the error words after every earlier kernel of the
+                // stream had ended: both clear means no read-back (and no stream wait).
+                if (words[40] == 0 && words[41] == 0 && ctx->pending.empty()) return ZKML_OK;
                 if ((rc = read_err_flag(ctx))) return rc;
                 return check_err_flag(ctx, "reduce_matmul_layer");
             }
@@ -619,6 +623,11 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
     if ((rc = ctx->fa.ensure(pk * 16)) || (rc = ctx->fb.ensure(pk * 16))) return rc;
     uint4* fa = ctx->fa.as<uint4>();
     uint4* fb = ctx->fb.as<uint4>();
+    // The row side (small) runs on the side stream under the column side's weight stream; it
+    // forks after every earlier operation of the stream (e.g. an input copy) and joins
+    // before the round kernels.
+    const bool side = n_ri != 0 && ctx->row_side_stream && !ctx->timing && ctx->side_stream;
+    if (side) ZK_CUDA(cudaEventRecord(ctx->ev_fork, s));
     // f_b first: the column restriction streams the whole weight and is the long kernel, so it
     // goes to the GPU before the host spends time launching the row side
     if (fb_words) {  // f_b from column-block partial sums added across ranks (zkml_restrict_cols_block)
@@ -656,15 +665,24 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
         ctx->launches++;
     } else {
         if ((rc = ctx->eq_a.ensure(((size_t)16) << n_ri)) || (rc = ctx->acc_a.ensure(k * 32))) return rc;
-        launch_eq_table(r_i, n_ri, ctx->eq_a.as<uint4>(), (size_t)1 << n_ri, s);
-        ZK_CUDA(cudaMemsetAsync(ctx->acc_a.ptr, 0, k * 32, s));
+        cudaStream_t rs = s;
+        if (side) {
+            rs = ctx->side_stream;
+            ZK_CUDA(cudaStreamWaitEvent(rs, ctx->ev_fork, 0));
+        }
+        launch_eq_table(r_i, n_ri, ctx->eq_a.as<uint4>(), (size_t)1 << n_ri, rs);
+        ZK_CUDA(cudaMemsetAsync(ctx->acc_a.ptr, 0, k * 32, rs));
         {
             KTimer t(ctx, KC_RESTRICT_ROWS);
             launch_restrict_rows(A, (uint32_t)m, (uint32_t)k, ctx->eq_a.as<uint4>(),
-                                 ctx->acc_a.as<unsigned long long>(), ctx->err_flag(), s);
+                                 ctx->acc_a.as<unsigned long long>(), ctx->err_flag(), rs);
         }
-        launch_acc_finalize(ctx->acc_a.as<unsigned long long>(), k, fa, pk, s);
+        launch_acc_finalize(ctx->acc_a.as<unsigned long long>(), k, fa, pk, rs);
         ctx->launches += 3;
+        if (side) {
+            ZK_CUDA(cudaEventRecord(ctx->ev_join, rs));
+            ZK_CUDA(cudaStreamWaitEvent(s, ctx->ev_join, 0));
+        }
     }
     return ZKML_OK;
 }
@@ -723,9 +741,20 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
     e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) rc = cuda_error(e, "cudaStreamCreate");
     ctx->stream = ctx->own_stream;
+    if (!rc && (e = cudaStreamCreateWithFlags(&ctx->side_stream, cudaStreamNonBlocking)) != cudaSuccess)
+        rc = cuda_error(e, "cudaStreamCreate");
+    if (!rc && ((e = cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming)) != cudaSuccess ||
+                (e = cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming)) != cudaSuccess))
+        rc = cuda_error(e, "cudaEventCreate");
+    {
+        const char* rv = getenv("ZKML_ROW_SIDE_STREAM");
+        if (rv) ctx->row_side_stream = rv[0] != '0';
+        const char* pv = getenv("ZKML_LA_PDL");
+        if (pv) ctx->la_pdl = pv[0] != '0';
+    }
     if (!rc) rc = ctx->partials.ensure((size_t)ctx->max_round_blocks * 16 * 4);
-    if (!rc) rc = ctx->small.ensure(64 * 4);
-    if (!rc && (e = cudaMemset(ctx->small.ptr, 0, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMemset");
+    if (!rc) rc = ctx->small.ensure(256 * 4);
+    if (!rc && (e = cudaMemset(ctx->small.ptr, 0, 256 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMemset");
     if (!rc && (e = cudaMallocHost(&ctx->h_small, 64 * 4)) != cudaSuccess) rc = cuda_error(e, "cudaMallocHost");
     if (!rc && (e = cudaHostAlloc(&ctx->h_sig, 4096, cudaHostAllocMapped)) != cudaSuccess)
         rc = cuda_error(e, "cudaHostAlloc(mapped)");
@@ -769,6 +798,9 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
     drain_timers(ctx);
     for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
     if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    if (ctx->side_stream) cudaStreamSynchronize(ctx->side_stream), cudaStreamDestroy(ctx->side_stream);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     delete ctx;
     return ZKML_OK;
 }
@@ -904,6 +936,8 @@ static int matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n
     };
     std::vector<uint32_t> chal(4 * (log_k + 1));
     g_trace.start();
+    const uint32_t seq_lo = ctx->sig_seq + 1;
+    if (g_trace.on) la_stamps_enable(true);
     int rc = reduce_matmul_internal(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
                                     chs, out_round_polys, chal.data(), out_final_a, out_final_b, &hook, fb_words);
     if (rc) return rc;
@@ -913,6 +947,7 @@ static int matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n
     ch.mix_qm31(ldq(out_final_b));
     g_trace.mark("final");
     g_trace.print();
+    if (g_trace.on) la_stamps_print(seq_lo, ctx->sig_seq);
     if (out_next_point) {
         memcpy(out_next_point, claim_point, 16 * log_m);
         memcpy(out_next_point + 4 * log_m, chal.data(), 16 * log_k);

@@ -6,6 +6,7 @@
 // 4 x 4 64-bit accumulators per thread, reducing modulo 2^31 - 1 only every
 // four products (each product < 2^62, so four of them plus a reduced residue
 // still fit in 64 bits).
+#include <cstdio>
 #include "kernels.cuh"
 #include "round_arith.cuh"
 #include "imma.cuh"
@@ -892,6 +893,9 @@ __global__ void __launch_bounds__(256) fold_round_m31_kernel(const uint32_t* __r
 // and the product are out-of-line device functions called in loops, and the
 // 40 result words are reduced through shared memory by a rolled loop.
 constexpr int LA_WORDS = 40;
+// Words 40-41 of a last round's publication: the M31 input-error word and the
+// look-ahead wait status, read after every earlier kernel of the stream ended.
+constexpr int LA_FLAG_WORDS = 2;
 constexpr int LA_THREADS = 256;
 constexpr unsigned long long kLaSpinLimit = 1ull << 21;  // a few seconds with the back-off below
 
@@ -901,9 +905,64 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
     return v;
 }
 
+// Optional device timeline of the look-ahead kernels (ZKML_LAYER_TRACE=1): per
+// signal sequence number (mod 64) the %globaltimer at kernel entry (0), when the
+// challenge was seen (1), two intermediate points (3, 4: block 0 done and the
+// last block's start; the tail's fold and products done), when the data were
+// ready (5: the predecessor grid waited for, the tail's vectors loaded) and when
+// the words were published (2).  Off by default: the
+// kernels then read one flag word.
+__device__ unsigned long long g_la_stamp[64][6];
+__device__ int g_la_stamp_on;
+
+__device__ __forceinline__ void la_stamp(uint32_t seq, int what) {
+    if (*(volatile int*)&g_la_stamp_on) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        g_la_stamp[seq & 63][what] = t;
+    }
+}
+
+void la_stamps_enable(bool on) {
+    const int v = on ? 1 : 0;
+    cudaMemcpyToSymbol(g_la_stamp_on, &v, sizeof(v));
+    if (on) {
+        static const unsigned long long zero[64][6] = {};
+        cudaMemcpyToSymbol(g_la_stamp, zero, sizeof(zero));
+    }
+}
+
+// Prints the stamps of sequence numbers [lo, hi] in microseconds from the first one.
+void la_stamps_print(uint32_t lo, uint32_t hi) {
+    unsigned long long st[64][6];
+    if (cudaMemcpyFromSymbol(st, g_la_stamp, sizeof(st)) != cudaSuccess) return;
+    unsigned long long t0 = ~0ull;
+    for (uint32_t q = lo; q <= hi && q - lo < 64; q++)
+        for (int w = 0; w < 6; w++)
+            if (st[q & 63][w] && st[q & 63][w] < t0) t0 = st[q & 63][w];
+    fprintf(stderr, "[zkml device]");
+    for (uint32_t q = lo; q <= hi && q - lo < 64; q++) {
+        const unsigned long long* e = st[q & 63];
+        auto us = [&](unsigned long long v) { return v ? (double)(v - t0) / 1e3 : -1.0; };
+        fprintf(stderr, " %u:%.1f/%.1f/%.1f/%.1f/%.1f/%.1f", q - lo, us(e[0]), us(e[5]), us(e[1]), us(e[3]), us(e[4]),
+                us(e[2]));
+    }
+    fprintf(stderr, "\n");
+}
+
+// The 8-word challenge slot [tag, 4 challenge words, abort, -, -] in mapped host
+// memory as two 16-byte loads issued together (one PCIe round trip instead of
+// one per word); called after the acquire load that saw the tag.
+__device__ __forceinline__ void load_slot(const uint32_t* slot, uint4& lo, uint4& hi) {
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w) : "l"(slot) : "memory");
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w) : "l"(slot + 4) : "memory");
+}
+
 __device__ __noinline__ qm31 la_fold(const uint4* V, size_t p, size_t L, int fold, const AlphaRows* m) {
-    const qm31 lo = u2q(V[p]);
-    return fold ? fold_qq(lo, u2q(V[p + L]), *m) : lo;
+    const qm31 lo = u2q(__ldcg(V + p));  // through L2: V may have been folded by the kernel before
+    return fold ? fold_qq(lo, u2q(__ldcg(V + p + L)), *m) : lo;
 }
 
 __device__ __noinline__ qm31 la_mul(qm31 x, qm31 y) {
@@ -925,16 +984,20 @@ __device__ __forceinline__ qm31 shfl_q(const qm31& v, int src) {
 
 __global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __restrict__ A, uint4* __restrict__ B,
                                                                      size_t L, int fold, const AlphaRows m,
-                                                                     uint32_t* partials, unsigned int* ticket,
+                                                                     unsigned long long* gacc, unsigned int* ticket,
                                                                      uint32_t* sig, uint32_t seq,
                                                                      const uint32_t* wait_msg, uint32_t wait_seq,
-                                                                     uint32_t* status, uint32_t* mailbox) {
+                                                                     uint32_t* status, uint32_t* mailbox,
+                                                                     const uint32_t* err_word) {
     constexpr int COLS = 2 * LA_THREADS / 32;  // two half-warps per warp
     __shared__ uint32_t sh[11][4][COLS];
     __shared__ AlphaRows ms;
     __shared__ int skip;
+    // A queued successor may become resident now (it waits for its own challenge).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (threadIdx.x == 0) {
         skip = 0;
+        if (blockIdx.x == 0) la_stamp(seq, 0);
         if (wait_msg) {
             // Block 0 polls the host slot and forwards the challenge through a
             // device mailbox [tag, 4 challenge words, abort] that the other
@@ -953,8 +1016,10 @@ __global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __re
                     __nanosleep(it < 4096 ? 32 : 256);
                 }
                 if (ok) {
-                    volatile const uint32_t* hm = wait_msg;
-                    for (int k = 0; k < 5; k++) w[k] = hm[1 + k];
+                    la_stamp(seq, 1);
+                    uint4 lo, hi;
+                    load_slot(wait_msg, lo, hi);
+                    w[0] = lo.y; w[1] = lo.z; w[2] = lo.w; w[3] = hi.x; w[4] = hi.y;
                 }
                 for (int k = 0; k < 5; k++) box[1 + k] = w[k];
                 __threadfence();
@@ -986,6 +1051,10 @@ __global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __re
         }
     }
     __syncthreads();
+    // A kernel launched early behind its predecessor reads the vectors only after
+    // the acquires that saw its challenge (host slot, then the mailbox): the
+    // predecessor's folds were complete when it published the words the host's
+    // challenge follows.
     if (skip) L = 0;  // no work: publish zeros so the queue drains
     const unsigned lane = threadIdx.x & 31, sub = lane & 15, half = lane >> 4, warp = threadIdx.x >> 5;
     const int col = 2 * warp + half;
@@ -1052,7 +1121,7 @@ __global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __re
         sh[sub][3][col] = acc.d;
     }
     __syncthreads();
-    if (threadIdx.x < LA_WORDS) {
+    if (threadIdx.x < LA_WORDS) {  // the block's word, added into the grid's 64-bit accumulator
         const int g = threadIdx.x >> 2, c = threadIdx.x & 3;
         uint32_t v = 0;
 #pragma unroll 1
@@ -1060,47 +1129,60 @@ __global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __re
             v = madd(v, sh[g][c][k]);
             if (g == 4 && L > 2) v = madd(v, sh[10][c][k]);
         }
-        partials[blockIdx.x * LA_WORDS + threadIdx.x] = v;
+        if (v) atomicAdd(gacc + threadIdx.x, (unsigned long long)v);
     }
     __shared__ bool is_last;
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) is_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0) la_stamp(seq, 3);
+        is_last = (atomicAdd(ticket, 1u) == gridDim.x - 1);
+    }
     __syncthreads();
     if (!is_last) return;
+    if (threadIdx.x == 0) la_stamp(seq, 4);
     __threadfence();
-    // Last block: warp k sums words k, k+8, ...; its lanes stride over the
-    // blocks' partials so the loads of a word are issued in parallel.
-    __shared__ uint32_t res[LA_WORDS];
-    const int nwarps = LA_THREADS / 32;
-#pragma unroll 1
-    for (int k = warp; k < LA_WORDS; k += nwarps) {
-        unsigned long long sacc = 0;
-        for (unsigned b = lane; b < gridDim.x; b += 32) sacc += __ldcg(partials + b * LA_WORDS + k);
-        uint32_t v = red64(sacc);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v = madd(v, __shfl_xor_sync(0xffffffffu, v, off));
-        if (lane == 0) res[k] = v;
-    }
+    // Last block: every block's words are in the accumulators (each block's
+    // atomics precede its fence and ticket); take them and leave zeros for the
+    // next look-ahead kernel.
+    __shared__ uint32_t res[LA_WORDS + LA_FLAG_WORDS];
+    if (threadIdx.x < LA_WORDS) res[threadIdx.x] = red64(atomicExch(gacc + threadIdx.x, 0ull));
     __syncthreads();
     if (threadIdx.x == 0) {
         *ticket = 0;
-        if (sig) publish(sig, seq, res, LA_WORDS);
+        la_stamp(seq, 2);
+        int n = LA_WORDS;
+        if (L == 2 && err_word) {  // last round: the error words ride with the final values
+            res[LA_WORDS] = *(volatile const uint32_t*)err_word;
+            res[LA_WORDS + 1] = status ? *(volatile const uint32_t*)status : 0u;
+            n += LA_FLAG_WORDS;
+        }
+        if (sig) publish(sig, seq, res, n);
     }
 }
 
 void launch_round_lookahead(uint4* A, uint4* B, size_t L, bool fold, qm31 alpha, const RoundScratch& rs,
                             cudaStream_t s, const uint32_t* wait_msg, uint32_t wait_seq, uint32_t* status,
-                            uint32_t* mailbox) {
+                            uint32_t* mailbox, const uint32_t* err_word, bool pdl) {
     size_t blocks = L >= 4 ? (L / 4 + 15) / 16 : 1;  // 16 quads per block per pass
     const size_t cap = (size_t)rs.max_blocks * 16 / LA_WORDS;
     if (blocks > cap) blocks = cap;
     if (blocks == 0) blocks = 1;
     // the 40 result words go to the host signal area only (rs.out holds 32 words)
-    static_assert(LA_WORDS <= 48, "signal area");
-    round_lookahead_kernel<<<(unsigned)blocks, LA_THREADS, 0, s>>>(A, B, L, fold ? 1 : 0, alpha_rows(alpha),
-                                                                   rs.partials, rs.ticket, rs.sig, rs.seq, wait_msg,
-                                                                   wait_seq, status, mailbox);
+    static_assert(LA_WORDS + LA_FLAG_WORDS <= 48, "signal area");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(LA_THREADS);
+    cfg.stream = s;
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaLaunchKernelEx(&cfg, round_lookahead_kernel, A, B, L, fold ? 1 : 0, alpha_rows(alpha), rs.la_acc, rs.ticket,
+                       rs.sig, rs.seq, wait_msg, wait_seq, status, mailbox, err_word);
 }
 
 // ---------------------------------------------------------------------------
@@ -1117,19 +1199,43 @@ void launch_round_lookahead(uint4* A, uint4* B, size_t L, bool fold, qm31 alpha,
 constexpr int TAIL_THREADS = 1024;
 constexpr int TAIL_COLS = 93;  // 11 * 93 = 1023 product threads
 
-__device__ __forceinline__ void la_factors(int k, const qm31* a, const qm31* b, qm31& px, qm31& py) {
-    switch (k) {
-        case 0: px = a[0]; py = b[0]; break;
-        case 1: px = a[1]; py = b[1]; break;
-        case 2: px = a[2]; py = b[2]; break;
-        case 3: px = a[3]; py = b[3]; break;
-        case 4: px = at_two(a[0], a[2]); py = at_two(b[0], b[2]); break;
-        case 5: px = qsub(a[2], a[0]); py = qsub(b[2], b[0]); break;
-        case 6: px = qsub(a[3], a[1]); py = qsub(b[3], b[1]); break;
-        case 7: px = at_two(a[0], a[1]); py = at_two(b[0], b[1]); break;
-        case 8: px = at_two(qsub(a[2], a[0]), qsub(a[3], a[1])); py = at_two(qsub(b[2], b[0]), qsub(b[3], b[1])); break;
-        case 9: px = at_two(a[2], a[3]); py = at_two(b[2], b[3]); break;
-        default: px = at_two(a[1], a[3]); py = at_two(b[1], b[3]); break;  // 10: second half of T
+// Product kind K over the quads c, c + TAIL_COLS, ... of the resident vectors, with
+// a0..a3 = A[i], A[i + q], A[i + h], A[i + q + h] (the same for B): kinds 0-3 are
+// a_K b_K, then (a0, a2) at two, a2 - a0, a3 - a1, (a0, a1) at two, (a2 - a0,
+// a3 - a1) at two, (a2, a3) at two and (a1, a3) at two -- the products of
+// round_lookahead_kernel.  Accumulated lazily; only the elements kind K needs are
+// read from shared memory.
+template <int K>
+__device__ __forceinline__ void tail_kind(const uint4* SA, const uint4* SB, int c, int q, int h, QAcc& s) {
+    for (int i = c; i < q; i += TAIL_COLS) {
+        qm31 px, py;
+        if (K < 4) {
+            const int o = i + ((K & 1) ? q : 0) + ((K & 2) ? h : 0);
+            px = u2q(SA[o]);
+            py = u2q(SB[o]);
+        } else if (K == 4) {  // at two, first variable: (a0, a2)
+            px = at_two(u2q(SA[i]), u2q(SA[i + h]));
+            py = at_two(u2q(SB[i]), u2q(SB[i + h]));
+        } else if (K == 5) {
+            px = qsub(u2q(SA[i + h]), u2q(SA[i]));
+            py = qsub(u2q(SB[i + h]), u2q(SB[i]));
+        } else if (K == 6) {
+            px = qsub(u2q(SA[i + q + h]), u2q(SA[i + q]));
+            py = qsub(u2q(SB[i + q + h]), u2q(SB[i + q]));
+        } else if (K == 7) {  // at two, second variable: (a0, a1)
+            px = at_two(u2q(SA[i]), u2q(SA[i + q]));
+            py = at_two(u2q(SB[i]), u2q(SB[i + q]));
+        } else if (K == 8) {
+            px = at_two(qsub(u2q(SA[i + h]), u2q(SA[i])), qsub(u2q(SA[i + q + h]), u2q(SA[i + q])));
+            py = at_two(qsub(u2q(SB[i + h]), u2q(SB[i])), qsub(u2q(SB[i + q + h]), u2q(SB[i + q])));
+        } else if (K == 9) {
+            px = at_two(u2q(SA[i + h]), u2q(SA[i + q + h]));
+            py = at_two(u2q(SB[i + h]), u2q(SB[i + q + h]));
+        } else {  // 10: (a1, a3), the second half of T
+            px = at_two(u2q(SA[i + q]), u2q(SA[i + q + h]));
+            py = at_two(u2q(SB[i + q]), u2q(SB[i + q + h]));
+        }
+        qacc_mul(s, px, py);
     }
 }
 
@@ -1139,57 +1245,90 @@ __global__ void __launch_bounds__(TAIL_THREADS, 1) lookahead_tail_kernel(const u
                                                                          uint32_t* sig,
                                                                          uint32_t seq_base, const uint32_t* msg,
                                                                          uint32_t tag_base, int slots,
-                                                                         uint32_t* status) {
+                                                                         uint32_t* status,
+                                                                         const uint32_t* err_word) {
     extern __shared__ uint4 tail_sh[];
     uint4* SA = tail_sh;
     uint4* SB = tail_sh + L0;
     __shared__ uint32_t red[11][4][32];
-    __shared__ uint32_t res[LA_WORDS];
+    __shared__ uint32_t res[LA_WORDS + LA_FLAG_WORDS];
     __shared__ AlphaRows ms;
     __shared__ int state;  // 0 run, 1 stop
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     const int k = t / TAIL_COLS, c = t % TAIL_COLS;
-    for (int i = t; i < L0; i += TAIL_THREADS) {
-        SA[i] = A[i];
-        SB[i] = B[i];
-    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (t == 0) la_stamp(seq_base, 0);
+    // Thread 0 takes round j's challenge (sets ms, or state = 1 to stop).
+    auto take = [&](int j) {
+        state = 0;
+        if (j == 0 && !wait0) {
+            if (fold0) ms = alpha_rows(alpha0);
+            return;
+        }
+        const uint32_t* slot = msg + 8 * ((tag_base + j) % slots);
+        const uint32_t want = tag_base + j;
+        unsigned long long it = 0;
+        bool ok = false;
+        while (true) {
+            if (ld_acquire_sys_u32(slot) == want) {
+                ok = true;
+                break;
+            }
+            if (++it > kLaSpinLimit) break;
+            __nanosleep(it < 4096 ? 32 : 256);
+        }
+        if (!ok) {
+            atomicOr(status, 1u);
+            state = 1;
+            return;
+        }
+        uint4 lo, hi;
+        load_slot(slot, lo, hi);
+        if (hi.y != 0) {  // abort
+            state = 1;
+        } else {
+            la_stamp(seq_base + j, 1);
+            ms = alpha_rows(qm(lo.y, lo.z, lo.w, hi.x));
+        }
+    };
+    // Round 0's challenge first: a kernel launched early behind the previous round's
+    // kernel reads the vectors only after the acquire that saw the challenge (the
+    // previous kernel published before the host posted it), through L2.
+    if (t == 0) take(0);
+    __syncthreads();
+    if (state) return;
     int L = L0;
-    for (int j = 0;; j++) {
-        // challenge of the previous round
-        bool fold = j > 0 || fold0;
-        if (t == 0) {
-            state = 0;
-            if (j == 0 && !wait0) {
-                if (fold0) ms = alpha_rows(alpha0);
-            } else {
-                const uint32_t* slot = msg + 8 * ((tag_base + j) % slots);
-                const uint32_t want = tag_base + j;
-                unsigned long long it = 0;
-                bool ok = false;
-                while (true) {
-                    if (ld_acquire_sys_u32(slot) == want) {
-                        ok = true;
-                        break;
-                    }
-                    if (++it > kLaSpinLimit) break;
-                    __nanosleep(it < 4096 ? 32 : 256);
-                }
-                volatile const uint32_t* w = slot;
-                if (!ok) {
-                    atomicOr(status, 1u);
-                    state = 1;
-                } else if (w[5] != 0) {
-                    state = 1;
-                } else {
-                    ms = alpha_rows(qm(w[1], w[2], w[3], w[4]));
-                }
+    if (fold0) {  // fold on load: V_0 = fold(input), both halves read from global memory
+        L = L0 / 2;
+#pragma unroll
+        for (int r = 0; r < 2 * (int)LA_TAIL_MAX * 2 / TAIL_THREADS; r++) {
+            const int p = t + r * TAIL_THREADS;
+            if (p < 2 * L) {
+                const int e = p < L ? p : p - L;
+                const uint4* V = p < L ? A : B;
+                const qm31 x = fold_qq(u2q(__ldcg(V + e)), u2q(__ldcg(V + e + L)), ms);
+                st_q((p < L ? SA : SB) + e, x);
             }
         }
-        __syncthreads();
-        if (state) return;
-        if (fold) {  // V_j = fold(V_{j-1}) in place: thread writes p < L, reads p and p + L
+    } else {
+#pragma unroll
+        for (int r = 0; r < 2 * (int)LA_TAIL_MAX / TAIL_THREADS; r++) {
+            const int i = t + r * TAIL_THREADS;
+            if (i < L0) {
+                SA[i] = __ldcg(A + i);
+                SB[i] = __ldcg(B + i);
+            }
+        }
+    }
+    __syncthreads();
+    if (t == 0) la_stamp(seq_base, 5);
+    for (int j = 0;; j++) {
+        if (j > 0) {  // challenge of the previous round, then V_j = fold(V_{j-1}) in place
+            if (t == 0) take(j);
+            __syncthreads();
+            if (state) return;
             L /= 2;
-            for (int p = t; p < 2 * L; p += TAIL_THREADS) {
+            for (int p = t; p < 2 * L; p += TAIL_THREADS) {  // thread writes p < L, reads p and p + L
                 const int e = p < L ? p : p - L;
                 uint4* V = p < L ? SA : SB;
                 const qm31 x = fold_qq(u2q(V[e]), u2q(V[e + L]), ms);
@@ -1197,6 +1336,7 @@ __global__ void __launch_bounds__(TAIL_THREADS, 1) lookahead_tail_kernel(const u
             }
             __syncthreads();
         }
+        if (t == 0) la_stamp(seq_base + j, 3);
         qm31 acc = qzero();
         if (L == 2) {
             if (t < 7) {
@@ -1213,24 +1353,42 @@ __global__ void __launch_bounds__(TAIL_THREADS, 1) lookahead_tail_kernel(const u
                 res[4 * t] = res[4 * t + 1] = res[4 * t + 2] = res[4 * t + 3] = 0;
             }
             __syncthreads();
-            if (t == 0) publish(sig, seq_base + j, res, LA_WORDS);
+            if (t == 0) {
+                la_stamp(seq_base + j, 2);
+                int n = LA_WORDS;
+                if (err_word) {  // the error words ride with the final values
+                    res[LA_WORDS] = *(volatile const uint32_t*)err_word;
+                    res[LA_WORDS + 1] = *(volatile const uint32_t*)status;
+                    n += LA_FLAG_WORDS;
+                }
+                publish(sig, seq_base + j, res, n);
+            }
             return;
         }
         const int h = L / 2, q = L / 4;
         if (k < 11) {
-            for (int i = c; i < q; i += TAIL_COLS) {
-                qm31 a[4], b[4];
-                a[0] = u2q(SA[i]); a[1] = u2q(SA[i + q]); a[2] = u2q(SA[i + h]); a[3] = u2q(SA[i + q + h]);
-                b[0] = u2q(SB[i]); b[1] = u2q(SB[i + q]); b[2] = u2q(SB[i + h]); b[3] = u2q(SB[i + q + h]);
-                qm31 px, py;
-                la_factors(k, a, b, px, py);
-                acc = qadd(acc, la_mul(px, py));
+            QAcc sacc;
+            qacc_zero(sacc);
+            switch (k) {
+                case 0: tail_kind<0>(SA, SB, c, q, h, sacc); break;
+                case 1: tail_kind<1>(SA, SB, c, q, h, sacc); break;
+                case 2: tail_kind<2>(SA, SB, c, q, h, sacc); break;
+                case 3: tail_kind<3>(SA, SB, c, q, h, sacc); break;
+                case 4: tail_kind<4>(SA, SB, c, q, h, sacc); break;
+                case 5: tail_kind<5>(SA, SB, c, q, h, sacc); break;
+                case 6: tail_kind<6>(SA, SB, c, q, h, sacc); break;
+                case 7: tail_kind<7>(SA, SB, c, q, h, sacc); break;
+                case 8: tail_kind<8>(SA, SB, c, q, h, sacc); break;
+                case 9: tail_kind<9>(SA, SB, c, q, h, sacc); break;
+                default: tail_kind<10>(SA, SB, c, q, h, sacc); break;
             }
+            acc = qacc_value(sacc);
         }
         // per product kind: warp w < 11 sums the TAIL_COLS partials of kind w
         __shared__ qm31 part[TAIL_THREADS];
         part[t] = acc;
         __syncthreads();
+        if (t == 0) la_stamp(seq_base + j, 4);
         if (warp < 11) {
             qm31 v = qzero();
             for (int i = lane; i < TAIL_COLS; i += 32) v = qadd(v, part[warp * TAIL_COLS + i]);
@@ -1252,14 +1410,17 @@ __global__ void __launch_bounds__(TAIL_THREADS, 1) lookahead_tail_kernel(const u
             res[t] = v;
         }
         __syncthreads();
-        if (t == 0) publish(sig, seq_base + j, res, LA_WORDS);
+        if (t == 0) {
+            la_stamp(seq_base + j, 2);
+            publish(sig, seq_base + j, res, LA_WORDS);
+        }
         __syncthreads();
     }
 }
 
 int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0, bool wait0, qm31 alpha0,
                           uint32_t* sig, uint32_t seq_base, const uint32_t* msg, uint32_t tag_base, int slots,
-                          uint32_t* status, cudaStream_t s) {
+                          uint32_t* status, cudaStream_t s, const uint32_t* err_word, bool pdl) {
     const size_t smem = 2 * L0 * sizeof(uint4);
     static bool attr_set = false;
     if (!attr_set) {
@@ -1268,8 +1429,20 @@ int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0,
             return -1;
         attr_set = true;
     }
-    lookahead_tail_kernel<<<1, TAIL_THREADS, smem, s>>>(A, B, (int)L0, fold0 ? 1 : 0, wait0 ? 1 : 0, alpha0, sig,
-                                                        seq_base, msg, tag_base, slots, status);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(TAIL_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    if (pdl) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaLaunchKernelEx(&cfg, lookahead_tail_kernel, A, B, (int)L0, fold0 ? 1 : 0, wait0 ? 1 : 0, alpha0, sig, seq_base,
+                       msg, tag_base, slots, status, err_word);
     return 0;
 }
 

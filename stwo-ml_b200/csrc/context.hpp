@@ -114,6 +114,7 @@ struct zkml_ctx {
     cudaStream_t side_stream = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     bool row_side_stream = true;
+    bool rows_fused = true;  // launch_restrict_rows_fused for A of at most 2^8 rows (ZKML_ROWS_FUSED=0: off)
     // Queued look-ahead kernels that wait for a challenge launch as programmatic
     // dependents of the kernel before them (ZKML_LA_PDL=0: plain launches).
     bool la_pdl = true;

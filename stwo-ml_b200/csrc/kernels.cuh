@@ -36,6 +36,12 @@ void launch_restrict_cols(const uint32_t* B, uint32_t k, uint32_t n, const uint4
 // Row restriction of a row-major m x k M31 matrix: acc[j] += sum_i A[i][j] L_i.
 void launch_restrict_rows(const uint32_t* A, uint32_t m, uint32_t k, const uint4* L,
                           unsigned long long* acc, uint32_t* err, cudaStream_t s);
+// f_a (pk entries, zero past k) from an m x k M31 matrix and the n_ri <= 8 row
+// challenges in one launch, plus f_b[i] = acc_b[i] mod P (i < k_b, zero up to pk)
+// when acc_b is set.  Returns nonzero (nothing launched) outside those bounds.
+int launch_restrict_rows_fused(const uint32_t* A, uint32_t m, uint32_t k, const qm31* r_i, int n_ri,
+                               const unsigned long long* acc_b, size_t k_b, uint4* fa, uint4* fb, size_t pk,
+                               uint32_t* err, cudaStream_t s);
 // out[i] = acc[i] mod P for i < n_rows, zero for n_rows <= i < out_len.
 void launch_acc_finalize(const unsigned long long* acc, size_t n_rows, uint4* out, size_t out_len,
                          cudaStream_t s);
@@ -108,6 +114,9 @@ void launch_round_lookahead(uint4* A, uint4* B, size_t L, bool fold, qm31 alpha,
 // as words 40-41.  pdl as for launch_round_lookahead (wait0 set).  Returns
 // nonzero if the launch could not be configured.
 constexpr size_t LA_TAIL_MAX = 2048;
+// Word 6 of a posted challenge slot: tag ^ words 1-5 ^ LA_SLOT_MIX (the kernels read
+// the slot in one PCIe round trip and retry a read that straddles a post).
+constexpr uint32_t LA_SLOT_MIX = 0x9E3779B9u;
 void la_stamps_enable(bool on);
 void la_stamps_print(uint32_t lo, uint32_t hi);
 int launch_lookahead_tail(const uint4* A, const uint4* B, size_t L0, bool fold0, bool wait0, qm31 alpha0,

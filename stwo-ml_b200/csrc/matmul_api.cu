@@ -424,11 +424,13 @@ struct LaQueue {
     int post(int j, const qm31& a, bool abort) {
         if (!queued) return abort ? ZKML_OK : launch_one(j, true, a, nullptr, 0);
         volatile uint32_t* m = ctx->h_la_msg() + 8 * slot[j];
+        const uint32_t ab = abort ? 1u : 0u;
         m[1] = a.a;
         m[2] = a.b;
         m[3] = a.c;
         m[4] = a.d;
-        m[5] = abort ? 1u : 0u;
+        m[5] = ab;
+        m[6] = tag[j] ^ a.a ^ a.b ^ a.c ^ a.d ^ ab ^ LA_SLOT_MIX;  // lets the GPU take the slot in one read
         std::atomic_thread_fence(std::memory_order_release);
         m[0] = tag[j];
         return ZKML_OK;
@@ -626,8 +628,12 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
     // The row side (small) runs on the side stream under the column side's weight stream; it
     // forks after every earlier operation of the stream (e.g. an input copy) and joins
     // before the round kernels.
-    const bool side = n_ri != 0 && ctx->row_side_stream && !ctx->timing && ctx->side_stream;
+    // Up to 2^8 rows: the row side and the finalisations are one launch after the column
+    // restriction (launch_restrict_rows_fused); larger A runs its own row pass.
+    const bool fused = n_ri >= 1 && n_ri <= 8 && ctx->rows_fused && !ctx->timing;
+    const bool side = n_ri != 0 && !fused && ctx->row_side_stream && !ctx->timing && ctx->side_stream;
     if (side) ZK_CUDA(cudaEventRecord(ctx->ev_fork, s));
+    bool acc_b_pending = false;  // f_b still in acc_b (finalised by the fused row launch)
     // f_b first: the column restriction streams the whole weight and is the long kernel, so it
     // goes to the GPU before the host spends time launching the row side
     if (fb_words) {  // f_b from column-block partial sums added across ranks (zkml_restrict_cols_block)
@@ -657,10 +663,21 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
                 launch_restrict_cols(B, (uint32_t)k, (uint32_t)n, ctx->eq_hi.as<uint4>(), ctx->eq_lo.as<uint4>(),
                                      ctx->acc_b.as<unsigned long long>(), ctx->err_flag(), ctx->num_sms, s);
         }
-        launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
-        ctx->launches += 2;
+        ctx->launches++;
+        if (!fused) {
+            launch_acc_finalize(ctx->acc_b.as<unsigned long long>(), k, fb, pk, s);
+            ctx->launches++;
+        }
+        acc_b_pending = true;
     }
-    if (n_ri == 0) {  // m == 1: f_a is A's single row
+    if (fused) {
+        if (launch_restrict_rows_fused(A, (uint32_t)m, (uint32_t)k, r_i, (int)n_ri,
+                                       acc_b_pending ? ctx->acc_b.as<unsigned long long>() : nullptr, k, fa, fb, pk,
+                                       ctx->err_flag(), s))
+            return set_error(ZKML_ERR_INVALID_ARG, "row restriction bounds");
+        ZK_CUDA(cudaGetLastError());
+        ctx->launches++;
+    } else if (n_ri == 0) {  // m == 1: f_a is A's single row
         launch_m31_to_qm31(A, k, fa, pk, ctx->err_flag(), s);
         ctx->launches++;
     } else {
@@ -751,6 +768,8 @@ int zkml_ctx_create(int device, zkml_ctx** out) {
         if (rv) ctx->row_side_stream = rv[0] != '0';
         const char* pv = getenv("ZKML_LA_PDL");
         if (pv) ctx->la_pdl = pv[0] != '0';
+        const char* fv = getenv("ZKML_ROWS_FUSED");
+        if (fv) ctx->rows_fused = fv[0] != '0';
     }
     if (!rc) rc = ctx->partials.ensure((size_t)ctx->max_round_blocks * 16 * 4);
     if (!rc) rc = ctx->small.ensure(256 * 4);
@@ -871,10 +890,13 @@ int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size
         return set_error(ZKML_ERR_INVALID_ARG, "matrix too large");
     if ((n_ri && !r_i) || (n_rj && !r_j)) return set_error(ZKML_ERR_INVALID_ARG, "NULL challenge point");
     if (n_rj > MAX_EQ_VARS || n_ri > MAX_EQ_VARS) return set_error(ZKML_ERR_INVALID_ARG, "too many variables");
+    g_trace.mark("checks");
     ZK_CUDA(cudaSetDevice(ctx->device));
+    g_trace.mark("setdev");
     const void* A = nullptr;
     const void* B = nullptr;
     int rc = device_view(ctx, a, a_rows * a_cols * 4, ctx->a_in, &A);
+    g_trace.mark("viewA");
     if (!rc && !fb_words) rc = device_view(ctx, b, b_rows * b_cols * 4, ctx->b_in, &B);
     if (rc) return rc;
     const uint32_t* Ad = static_cast<const uint32_t*>(A);
@@ -935,9 +957,9 @@ static int matmul_layer_gkr(zkml_ctx* ctx, const uint32_t* claim_point, size_t n
         c.mix_qm31(ldq(sd->value));
     };
     std::vector<uint32_t> chal(4 * (log_k + 1));
-    g_trace.start();
+    if (g_trace.on) la_stamps_enable(true);  // synchronous copies: before the timeline starts
     const uint32_t seq_lo = ctx->sig_seq + 1;
-    if (g_trace.on) la_stamps_enable(true);
+    g_trace.start();
     int rc = reduce_matmul_internal(ctx, a, m, k, b, k, n, claim_point, log_m, claim_point + 4 * log_m, log_n, pk,
                                     chs, out_round_polys, chal.data(), out_final_a, out_final_b, &hook, fb_words);
     if (rc) return rc;

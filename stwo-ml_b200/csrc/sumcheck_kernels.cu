@@ -522,6 +522,96 @@ void launch_restrict_rows(const uint32_t* A, uint32_t m, uint32_t k, const uint4
     restrict_rows_kernel<<<grid, 256, 0, s>>>(A, m, k, L, acc, err);
 }
 
+// Row restriction and both finalisations in one launch, for m <= 2^RF_MAX_VARS rows:
+// f_a[j] = sum_i A[i][j] eq(i, r_i) written directly as QM31 (each block builds the
+// eq table of the row variables in shared memory, its 8 warps take 1/8 of the rows
+// of its 32 columns each and add their partials), zeros for k <= j < pk; and,
+// when acc_b is set, f_b[i] = acc_b[i] mod P for i < k_b, zeros up to pk.  Replaces
+// eq_table + memset + restrict_rows + two acc_finalize launches between the column
+// restriction and the first round kernel.
+constexpr int RF_MAX_VARS = 8;
+constexpr int RF_COLS = 32;
+
+__global__ void __launch_bounds__(256) restrict_rows_fused_kernel(const uint32_t* __restrict__ A, uint32_t m,
+                                                                  uint32_t k, EqChallenges ch,
+                                                                  const unsigned long long* __restrict__ acc_b,
+                                                                  size_t k_b, uint4* __restrict__ fa,
+                                                                  uint4* __restrict__ fb, size_t pk,
+                                                                  uint32_t* __restrict__ err) {
+    __shared__ uint4 eq[2][1 << RF_MAX_VARS];
+    __shared__ uint32_t part[8][4][RF_COLS];
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    // f_b first (independent of the table)
+    if (acc_b)
+        for (size_t i = blockIdx.x * (size_t)blockDim.x + t; i < pk; i += (size_t)gridDim.x * blockDim.x) {
+            uint4 r = make_uint4(0, 0, 0, 0);
+            if (i < k_b) {
+                r.x = red64(acc_b[4 * i + 0]);
+                r.y = red64(acc_b[4 * i + 1]);
+                r.z = red64(acc_b[4 * i + 2]);
+                r.w = red64(acc_b[4 * i + 3]);
+            }
+            fb[i] = r;
+        }
+    // eq table of the v row variables, most significant first, by doubling
+    const int v = ch.v;
+    if (t == 0) st_q(&eq[0][0], qone());
+    int cur = 0;
+    for (int l = 0; l < v; l++) {
+        __syncthreads();
+        const qm31 c = ch.c[l], c1 = qsub(qone(), c);
+        for (int e = t; e < (1 << l); e += blockDim.x) {
+            const qm31 w = ld_q(&eq[cur][e]);
+            st_q(&eq[cur ^ 1][2 * e], qmul(w, c1));
+            st_q(&eq[cur ^ 1][2 * e + 1], qmul(w, c));
+        }
+        cur ^= 1;
+    }
+    __syncthreads();
+    const uint32_t j = blockIdx.x * RF_COLS + lane;
+    const uint32_t per = (m + 7) / 8, i0 = warp * per, i1 = min(m, i0 + per);
+    unsigned long long acc[4] = {0, 0, 0, 0};
+    uint32_t bad = 0;
+    if (j < k) {
+#pragma unroll 4
+        for (uint32_t i = i0; i < i1; i++) {
+            const uint32_t a = __ldg(A + (size_t)i * k + j);
+            bad |= a;
+            const uint4 l = eq[cur][i];
+            acc[0] += (unsigned long long)a * l.x;
+            acc[1] += (unsigned long long)a * l.y;
+            acc[2] += (unsigned long long)a * l.z;
+            acc[3] += (unsigned long long)a * l.w;
+            if (((i - i0) & 3) == 3)
+                for (int c = 0; c < 4; c++) acc[c] = lazy(acc[c]);
+        }
+    }
+    for (int c = 0; c < 4; c++) part[warp][c][lane] = red64(acc[c]);
+    if (bad & 0x80000000u) atomicOr(err, 1u);
+    __syncthreads();
+    if (warp == 0 && j < pk) {
+        uint32_t r[4];
+        for (int c = 0; c < 4; c++) {
+            uint32_t x = 0;
+            for (int w = 0; w < 8; w++) x = madd(x, part[w][c][lane]);
+            r[c] = x;
+        }
+        fa[j] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
+}
+
+int launch_restrict_rows_fused(const uint32_t* A, uint32_t m, uint32_t k, const qm31* r_i, int n_ri,
+                               const unsigned long long* acc_b, size_t k_b, uint4* fa, uint4* fb, size_t pk,
+                               uint32_t* err, cudaStream_t s) {
+    if (n_ri < 1 || n_ri > RF_MAX_VARS || pk < k) return -1;
+    EqChallenges ch;
+    ch.v = n_ri;
+    for (int i = 0; i < n_ri; i++) ch.c[i] = r_i[i];
+    const size_t blocks = (pk + RF_COLS - 1) / RF_COLS;
+    restrict_rows_fused_kernel<<<(unsigned)blocks, 256, 0, s>>>(A, m, k, ch, acc_b, k_b, fa, fb, pk, err);
+    return 0;
+}
+
 __global__ void acc_finalize_kernel(const unsigned long long* __restrict__ acc, size_t n_rows,
                                     uint4* __restrict__ out, size_t out_len) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < out_len;
@@ -950,14 +1040,31 @@ void la_stamps_print(uint32_t lo, uint32_t hi) {
     fprintf(stderr, "\n");
 }
 
-// The 8-word challenge slot [tag, 4 challenge words, abort, -, -] in mapped host
-// memory as two 16-byte loads issued together (one PCIe round trip instead of
-// one per word); called after the acquire load that saw the tag.
+// The 8-word challenge slot [tag, 4 challenge words, abort, check, -] in mapped
+// host memory, read as two 16-byte loads issued together (one PCIe round trip).
+// The host writes words 1-6 before the tag; check = tag ^ words 1-5 ^ LA_SLOT_MIX,
+// so a read whose two halves straddle a post fails the check and is retried.
+
 __device__ __forceinline__ void load_slot(const uint32_t* slot, uint4& lo, uint4& hi) {
     asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w) : "l"(slot) : "memory");
     asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w) : "l"(slot + 4) : "memory");
+}
+
+// Polls the slot until it holds tag `want` with a valid check (bounded; false on
+// timeout).  The fence after a hit orders this thread's later loads after it.
+__device__ __forceinline__ bool poll_slot(const uint32_t* slot, uint32_t want, uint4& lo, uint4& hi) {
+    unsigned long long it = 0;
+    while (true) {
+        load_slot(slot, lo, hi);
+        if (lo.x == want && hi.z == (lo.x ^ lo.y ^ lo.z ^ lo.w ^ hi.x ^ hi.y ^ LA_SLOT_MIX)) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            return true;
+        }
+        if (++it > kLaSpinLimit) return false;
+        __nanosleep(it < 4096 ? 32 : 256);
+    }
 }
 
 __device__ __noinline__ qm31 la_fold(const uint4* V, size_t p, size_t L, int fold, const AlphaRows* m) {
@@ -1007,18 +1114,10 @@ __global__ void __launch_bounds__(LA_THREADS) round_lookahead_kernel(uint4* __re
             bool ok = false;
             unsigned long long it = 0;
             if (blockIdx.x == 0) {
-                while (true) {
-                    if (ld_acquire_sys_u32(wait_msg) == wait_seq) {
-                        ok = true;
-                        break;
-                    }
-                    if (++it > kLaSpinLimit) break;
-                    __nanosleep(it < 4096 ? 32 : 256);
-                }
+                uint4 lo, hi;
+                ok = poll_slot(wait_msg, wait_seq, lo, hi);
                 if (ok) {
                     la_stamp(seq, 1);
-                    uint4 lo, hi;
-                    load_slot(wait_msg, lo, hi);
                     w[0] = lo.y; w[1] = lo.z; w[2] = lo.w; w[3] = hi.x; w[4] = hi.y;
                 }
                 for (int k = 0; k < 5; k++) box[1 + k] = w[k];
@@ -1266,24 +1365,12 @@ __global__ void __launch_bounds__(TAIL_THREADS, 1) lookahead_tail_kernel(const u
             return;
         }
         const uint32_t* slot = msg + 8 * ((tag_base + j) % slots);
-        const uint32_t want = tag_base + j;
-        unsigned long long it = 0;
-        bool ok = false;
-        while (true) {
-            if (ld_acquire_sys_u32(slot) == want) {
-                ok = true;
-                break;
-            }
-            if (++it > kLaSpinLimit) break;
-            __nanosleep(it < 4096 ? 32 : 256);
-        }
-        if (!ok) {
+        uint4 lo, hi;
+        if (!poll_slot(slot, tag_base + j, lo, hi)) {
             atomicOr(status, 1u);
             state = 1;
             return;
         }
-        uint4 lo, hi;
-        load_slot(slot, lo, hi);
         if (hi.y != 0) {  // abort
             state = 1;
         } else {

@@ -110,11 +110,11 @@ struct zkml_ctx {
     cudaStream_t stream = nullptr;
     cudaStream_t own_stream = nullptr;
     // The row side of a restriction runs on side_stream under the column side
-    // (fork / join events; off with ZKML_ROW_SIDE_STREAM=0 or while kernel timing is on).
+    // (fork / join events; off with ZKML_ROW_SIDE_STREAM=0 or while the row class is timed).
     cudaStream_t side_stream = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     bool row_side_stream = true;
-    bool rows_fused = true;  // launch_restrict_rows_fused for A of at most 2^8 rows (ZKML_ROWS_FUSED=0: off)
+    bool rows_fused = true;  // launch_restrict_rows_fused for A of at most 2^8 rows (ZKML_ROWS_FUSED=0: off; off while the row class is timed)
     // Queued look-ahead kernels that wait for a challenge launch as programmatic
     // dependents of the kernel before them (ZKML_LA_PDL=0: plain launches).
     bool la_pdl = true;

@@ -122,6 +122,29 @@ static void drain_timers(zkml_ctx* ctx) {
     ctx->pending.clear();
 }
 
+// Accumulate the event pairs whose end event has completed, without a stream sync;
+// the others stay pending.
+static void drain_done_timers(zkml_ctx* ctx) {
+    std::vector<zkml_ctx::PendingEv> keep;
+    for (auto& p : ctx->pending) {
+        const cudaError_t q = cudaEventQuery(p.e1);
+        if (q == cudaErrorNotReady) {
+            keep.push_back(p);
+            continue;
+        }
+        float ms = 0;
+        if (q == cudaSuccess && cudaEventElapsedTime(&ms, p.e0, p.e1) == cudaSuccess) {
+            ctx->ktime[p.cls].ms += ms;
+            ctx->ktime[p.cls].launches++;
+        } else {
+            cudaGetLastError();
+        }
+        ctx->ev_pool.push_back(p.e0);
+        ctx->ev_pool.push_back(p.e1);
+    }
+    ctx->pending.swap(keep);
+}
+
 // Host wall-time accumulator for a pseudo kernel class (timing mode only).
 struct HostTimer {
     zkml_ctx* ctx;
@@ -567,7 +590,10 @@ int run_sumcheck(zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const u
                 g_trace.mark("last");
                 // The last kernel read the error words after every earlier kernel of the
                 // stream had ended: both clear means no read-back (and no stream wait).
-                if (words[40] == 0 && words[41] == 0 && ctx->pending.empty()) return ZKML_OK;
+                if (words[40] == 0 && words[41] == 0) {
+                    if (!ctx->pending.empty()) drain_done_timers(ctx);
+                    if (ctx->pending.empty()) return ZKML_OK;
+                }
                 if ((rc = read_err_flag(ctx))) return rc;
                 return check_err_flag(ctx, "reduce_matmul_layer");
             }
@@ -630,8 +656,9 @@ static int restrict_ab(zkml_ctx* ctx, const uint32_t* A, size_t m, size_t k, con
     // before the round kernels.
     // Up to 2^8 rows: the row side and the finalisations are one launch after the column
     // restriction (launch_restrict_rows_fused); larger A runs its own row pass.
-    const bool fused = n_ri >= 1 && n_ri <= 8 && ctx->rows_fused && !ctx->timing;
-    const bool side = n_ri != 0 && !fused && ctx->row_side_stream && !ctx->timing && ctx->side_stream;
+    const bool rows_timed = ctx->timing && (ctx->timing_mask & (1u << KC_RESTRICT_ROWS));
+    const bool fused = n_ri >= 1 && n_ri <= 8 && ctx->rows_fused && !rows_timed;
+    const bool side = n_ri != 0 && !fused && ctx->row_side_stream && !rows_timed && ctx->side_stream;
     if (side) ZK_CUDA(cudaEventRecord(ctx->ev_fork, s));
     bool acc_b_pending = false;  // f_b still in acc_b (finalised by the fused row launch)
     // f_b first: the column restriction streams the whole weight and is the long kernel, so it

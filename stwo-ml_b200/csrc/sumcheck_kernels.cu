@@ -1045,23 +1045,22 @@ void la_stamps_print(uint32_t lo, uint32_t hi) {
 // The host writes words 1-6 before the tag; check = tag ^ words 1-5 ^ LA_SLOT_MIX,
 // so a read whose two halves straddle a post fails the check and is retried.
 
+// Both halves in one round trip: the second half relaxed, the first (with the tag)
+// an acquire, issued back to back (the acquire orders only what follows it).
 __device__ __forceinline__ void load_slot(const uint32_t* slot, uint4& lo, uint4& hi) {
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w) : "l"(slot) : "memory");
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w) : "l"(slot + 4) : "memory");
+    asm volatile("ld.acquire.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w) : "l"(slot) : "memory");
 }
 
 // Polls the slot until it holds tag `want` with a valid check (bounded; false on
-// timeout).  The fence after a hit orders this thread's later loads after it.
+// timeout).  Later loads of this thread are ordered after the acquire that saw it.
 __device__ __forceinline__ bool poll_slot(const uint32_t* slot, uint32_t want, uint4& lo, uint4& hi) {
     unsigned long long it = 0;
     while (true) {
         load_slot(slot, lo, hi);
-        if (lo.x == want && hi.z == (lo.x ^ lo.y ^ lo.z ^ lo.w ^ hi.x ^ hi.y ^ LA_SLOT_MIX)) {
-            asm volatile("fence.acq_rel.sys;" ::: "memory");
-            return true;
-        }
+        if (lo.x == want && hi.z == (lo.x ^ lo.y ^ lo.z ^ lo.w ^ hi.x ^ hi.y ^ LA_SLOT_MIX)) return true;
         if (++it > kLaSpinLimit) return false;
         __nanosleep(it < 4096 ? 32 : 256);
     }

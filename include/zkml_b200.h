@@ -492,8 +492,7 @@ int zkml_selftest_wait_timeout(zkml_ctx *ctx, uint32_t *status_out);
  *            synchronises that stream before returning.
  * Limits: rows <= ZKML_NOALLOC_MAX_ROWS, cols <= ZKML_NOALLOC_MAX_COLS; larger
  * sizes return ZKML_ERR_INVALID_ARG.  The first call on each device resolves
- * the array's device address: make that first call before any stream capture.
- * All calls share the one array, so calls whose GPU work overlaps (other
+ * the array's device address.  All calls share the one array, so calls whose GPU work overlaps (other
  * threads, other streams) race and must be serialised by the caller. */
 #define ZKML_NOALLOC_MAX_ROWS 65536
 #define ZKML_NOALLOC_MAX_COLS (1 << 20)

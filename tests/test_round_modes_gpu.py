@@ -1,8 +1,11 @@
 """The sumcheck round schedules give the same proofs.
 
-The restriction has a tensor-pipe and a generic kernel, and the round loop has four schedules (look-ahead rounds queued up front with a
-resident-block tail; queued without the tail; launched one at a time; and the
-plain fold-and-sum rounds).  Each is selected by environment variables read
+The restriction has a tensor-pipe and a generic kernel, the row side a fused
+launch (up to 2^8 rows; the last two shapes sit on either side of that bound), a
+second-stream and a same-stream form, and the round loop has four schedules
+(look-ahead rounds queued up front with a resident-block tail; queued without the
+tail; launched one at a time; and the plain fold-and-sum rounds), the queued ones
+with or without programmatic dependent launches.  Each is selected by environment variables read
 when a context is created, so every schedule runs in its own process and is
 checked against the oracle on products that stay small, cross the look-ahead
 threshold, and matrices that go through the restrictions.
@@ -40,7 +43,7 @@ for lg in (1, 2, 5, 11, 12, 17):
     n = 1 << lg
     check(uniform_m31(n, lg).reshape(1, n), uniform_m31(n, lg + 50).reshape(n, 1), np.zeros((0, 4), np.uint32), np.zeros((0, 4), np.uint32))
 for (m, k, n) in ((4, 96, 80), (8, 3000, 64), (2, 8192, 16), (3, 37, 1028), (16, 300, 2052), (5, 17, 6),
-                  (2, 33, 4100), (4, 1000, 3072)):
+                  (2, 33, 4100), (4, 1000, 3072), (256, 64, 96), (300, 40, 70)):
     a = int_matrix_m31(m, k, 1)
     b = int_matrix_m31(k, n, 2)
     lm = (m - 1).bit_length()
@@ -55,6 +58,9 @@ MODES = {
     "unqueued": {"ZKML_LA_QUEUE": "0"},
     "plain_rounds": {"ZKML_LOOKAHEAD_MAX": "0"},
     "generic_restriction": {"ZKML_RESTRICT_TC": "0"},
+    "plain_dependent_launches": {"ZKML_LA_PDL": "0"},
+    "rows_unfused_side_stream": {"ZKML_ROWS_FUSED": "0"},
+    "rows_unfused_one_stream": {"ZKML_ROWS_FUSED": "0", "ZKML_ROW_SIDE_STREAM": "0"},
 }
 
 

@@ -261,8 +261,8 @@ class PoseidonChannel:
         lib().zkml_channel_init(C.byref(self._st))
 
     def clone(self) -> "PoseidonChannel":
-        c = PoseidonChannel()
-        C.memmove(C.byref(c._st), C.byref(self._st), C.sizeof(_Channel))
+        c = PoseidonChannel.__new__(PoseidonChannel)
+        c._st = _Channel.from_buffer_copy(self._st)
         return c
 
     @property

@@ -16,6 +16,8 @@ the splits of one proof across the N GPUs, each timed the same way:
                the low index bits; the 12 round words are added across the GPUs
                inside the round kernels and the folded vectors are gathered by
                peer stores (the peer mesh); strong scaling;
+  c5_sweep     the same split proof at 2^20, 2^22, ..., 2^28 elements (config 5's
+               sweep; 2^30 is c5), each with its HBM fraction per GPU;
   c2_colsplit  one C2 layer with B split by column blocks, the partial words
                exchanged by peer stores; strong scaling;
 and "parity_vs_1gpu": rank 0 recomputes both proofs on one GPU (untimed) and
@@ -353,6 +355,7 @@ def run_b200(args):
 
 
 C5_LOG_N = 30
+C5_SWEEP = (20, 22, 24, 26, 28)  # the rest of config 5's 2^20 ... 2^30 sweep
 # config 4: Qwen2.5-14B decoder layer at 64 tokens (hidden 5120, 40 x 128 query width, SwiGLU 13824)
 C4_M, C4_D, C4_Q, C4_FF = 64, 5120, 5120, 13824
 
@@ -486,10 +489,37 @@ def measure_sharded(Z, torch, dist, world, rank, ctx, stream, steps=5, warmup=3,
             ref = prove_product_sharded_native(ga, gb, n, Z.PoseidonChannel(), solo, ctx=ctx)
             parity &= bool((proof_words(ref.round_polys, ref.final_a, ref.final_b) == got).all())
         mesh.close()
-    if solo is not None:
-        solo.close()
     del ga, gb, la, lb
     torch.cuda.empty_cache()
+    # ---- C5 sweep: the same split proof at 2^20 ... 2^28 elements -----------------------------
+    sweep = []
+    for lg in C5_SWEEP:
+        ns = 1 << lg
+        ga, gb, la, lb = c5_inputs(torch, ns, world, rank)
+        mesh = PeerMesh(ctx=ctx, max_gather_bytes=32 << 17) if world > 1 else None
+        if mesh is not None:
+            def c5s():
+                return prove_product_sharded_mesh(la, lb, ns, Z.PoseidonChannel(), mesh)
+        else:
+            def c5s():
+                return prove_product_sharded_native(la, lb, ns, Z.PoseidonChannel(), solo, ctx=ctx)
+        mss, proof = timed_steps(torch, dist, world, stream, c5s, 10, 3)
+        per_gpu = product_bytes(ns // world)
+        sweep.append({"log_n": lg, "ms": round(mss, 4), "elems_folded_per_s_per_gpu": 2 * (2 * ns - 2) / (mss * 1e-3) / world,
+                      "hbm_frac_per_gpu": per_gpu / (mss * 1e-3) / 1e9 / peak})
+        if world > 1:
+            got = proof_words(proof.round_polys, proof.final_a, proof.final_b)
+            if rank == 0:
+                ref = prove_product_sharded_native(ga, gb, ns, Z.PoseidonChannel(), solo, ctx=ctx)
+                parity &= bool((proof_words(ref.round_polys, ref.final_a, ref.final_b) == got).all())
+            torch.cuda.synchronize()
+            dist.barrier()
+            mesh.close()
+        del ga, gb, la, lb
+        torch.cuda.empty_cache()
+    out["c5_sweep"] = sweep
+    if solo is not None:
+        solo.close()
     # ---- C2 layer split by column blocks ---------------------------------------------------
     if world > 1:
         a, b = make_inputs(0)
@@ -706,11 +736,12 @@ def time_next_rows(Z, torch, ta, tb, reps=5):
     claim = Z.AggregatedWeightClaim(B, 0, random_qm31(log2(PK) + log2(PN), rng), val, com)
     out["aggregated_binding_ms"] = wall(lambda: Z.prove_aggregated_binding([claim], Z.PoseidonChannel()), 1)
     out["merkle_2e24"] = time_merkle_vs_reference(Z, torch)
+    out["merkle_sweep"] = [time_merkle_vs_reference(Z, torch, log_n=lg, with_reference=False) for lg in (20, 22, 26)]
     out["shapes"] = {"gemm": [M, K, N], "activation": [M, N], "rmsnorm": [M, K], "binding_weight": [K, N]}
     return {k: (round(v, 3) if isinstance(v, float) else v) for k, v in out.items()}
 
 
-def time_merkle_vs_reference(Z, torch, log_n=24, reps=3):
+def time_merkle_vs_reference(Z, torch, log_n=24, reps=3, with_reference=True):
     """Poseidon-252 Merkle commitment of 2^log_n QM31 leaves: this library's kernels against the
     reference's own layer kernel compiled from its source (oracle/_ref, a measuring stick; leaf
     felts precomputed for it, as the reference converts leaves on the CPU), both on this GPU,
@@ -733,7 +764,7 @@ def time_merkle_vs_reference(Z, torch, log_n=24, reps=3):
 
     ms, root = events(lambda: Z.commit_mle_root(leaves))
     res = {"leaves": n, "ms": round(ms, 3), "hashes_per_s": (n - 1) / (ms * 1e-3)}
-    if R.available():
+    if with_reference and R.available():
         felts = torch.from_numpy(R.leaf_felts(leaves.cpu().numpy().view(np.uint32)).view(np.int64)).cuda()
         rc = torch.from_numpy(R.limbs(R.compressed_round_keys()).view(np.int64)).cuda()
         scratch = torch.zeros((n, 4), dtype=torch.int64, device="cuda")

@@ -68,6 +68,13 @@ int zkml_ctx_destroy(zkml_ctx *ctx);
 int zkml_ctx_device(const zkml_ctx *ctx);
 /* Kernel launches of this context so far (instrumentation for benchmarks). */
 uint64_t zkml_ctx_kernel_launches(const zkml_ctx *ctx);
+/* Host -> device bytes of the input-matrix uploads of this context so far (instrumentation for
+ * benchmarks).  B of zkml_reduce_matmul_layer / _gkr in host memory with at least 2^22 words
+ * (ZKML_PACK_MIN) crosses PCIe in chunks of 2^20 words packed by host threads into one byte per
+ * word when every word of the chunk is the M31 image of a signed byte (x >= 0 ? x : p + x, the
+ * reference's int8 quantisation); other chunks are copied as they are.  The device receives the
+ * same field elements either way.  ZKML_PACK_H2D=0 turns the packing off. */
+uint64_t zkml_ctx_h2d_bytes(const zkml_ctx *ctx);
 /* Per-kernel device timing with CUDA events (off by default).  `enable` is 0
  * (off), -1 (every class) or a bit mask of classes in the order listed below
  * (bit 0 = "restrict_cols").  Each launch of a timed class is bracketed by events on the

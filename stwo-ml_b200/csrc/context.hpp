@@ -63,6 +63,11 @@ int run_sumcheck(::zkml_ctx* ctx, uint4* A, uint4* B, const uint32_t* A32, const
 // Shared host helpers (matmul_api.cu).
 // device_view: `p` itself if it is device memory of the context's GPU, else a copy in `stage`.
 int device_view(::zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const void** out);
+// device_view of an M31 matrix of `count` words: a large host matrix goes through
+// upload_m31_packed (values that fit a signed byte cross PCIe as bytes; ZKML_PACK_H2D=0 turns it
+// off, ZKML_PACK_MIN sets the size in words from which it is used, default 2^22).
+int matrix_view(::zkml_ctx* ctx, const uint32_t* p, size_t count, DevBuf& stage, const void** out);
+int upload_m31_packed(::zkml_ctx* ctx, const uint32_t* host, size_t count, DevBuf& dst, const void** out);
 // Spin (bounded) until a kernel publishes `seq` in the mapped signal words; copy n words.
 int wait_signal(::zkml_ctx* ctx, uint32_t seq, uint32_t* words, int n);
 int read_err_flag(::zkml_ctx* ctx);
@@ -134,6 +139,12 @@ struct zkml_ctx {
     zk::DevBuf mesh_stage;          // this rank's contribution to a mesh gather
     uint8_t* h_stage = nullptr;     // pinned host staging for the sharded gather
     size_t h_stage_bytes = 0;
+    // packed upload of host matrices (h2d_pack.cu)
+    uint8_t* pack_host = nullptr;   // pinned byte staging
+    size_t pack_host_bytes = 0;
+    zk::DevBuf pack_dev;            // packed bytes on the device
+    cudaEvent_t pack_event = nullptr;  // after the last upload's copies
+    uint64_t h2d_bytes = 0;         // host -> device bytes of the matrix uploads
     // stepwise product-sumcheck session (zkml_sumcheck_*)
     zk::DevBuf sc_a, sc_b;          // staged M31 inputs
     const uint32_t* sc_a32 = nullptr;

@@ -191,8 +191,24 @@ int device_view(zkml_ctx* ctx, const void* p, size_t bytes, DevBuf& stage, const
     int rc = stage.ensure(bytes);
     if (rc) return rc;
     ZK_CUDA(cudaMemcpyAsync(stage.ptr, p, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    ctx->h2d_bytes += bytes;
     *out = stage.ptr;
     return ZKML_OK;
+}
+
+int matrix_view(zkml_ctx* ctx, const uint32_t* p, size_t count, DevBuf& stage, const void** out) {
+    const char* on = getenv("ZKML_PACK_H2D");
+    const char* mn = getenv("ZKML_PACK_MIN");
+    const size_t min_words = mn ? (size_t)strtoull(mn, nullptr, 10) : ((size_t)1 << 22);
+    if ((on && on[0] == '0') || count < min_words || count == 0) return device_view(ctx, p, count * 4, stage, out);
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+        cudaGetLastError();
+        attr.type = cudaMemoryTypeUnregistered;
+    }
+    if (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged)
+        return device_view(ctx, p, count * 4, stage, out);
+    return upload_m31_packed(ctx, p, count, stage, out);
 }
 
 int check_err_flag(zkml_ctx* ctx, const char* what) {
@@ -837,6 +853,9 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
     ctx->gather_dev.release();
     ctx->mesh_stage.release();
     if (ctx->h_stage) cudaFreeHost(ctx->h_stage);
+    ctx->pack_dev.release();
+    if (ctx->pack_host) cudaFreeHost(ctx->pack_host);
+    if (ctx->pack_event) cudaEventDestroy(ctx->pack_event);
     ctx->sc_a.release();
     ctx->sc_b.release();
     if (ctx->h_small) cudaFreeHost(ctx->h_small);
@@ -853,6 +872,7 @@ int zkml_ctx_destroy(zkml_ctx* ctx) {
 
 int zkml_ctx_device(const zkml_ctx* ctx) { return ctx ? ctx->device : -1; }
 uint64_t zkml_ctx_kernel_launches(const zkml_ctx* ctx) { return ctx ? ctx->launches : 0; }
+uint64_t zkml_ctx_h2d_bytes(const zkml_ctx* ctx) { return ctx ? ctx->h2d_bytes : 0; }
 
 int zkml_ctx_enable_timing(zkml_ctx* ctx, int enable) {
     if (!ctx) return set_error(ZKML_ERR_INVALID_ARG, "ctx is NULL");
@@ -924,7 +944,7 @@ int reduce_matmul_internal(zkml_ctx* ctx, const uint32_t* a, size_t a_rows, size
     const void* B = nullptr;
     int rc = device_view(ctx, a, a_rows * a_cols * 4, ctx->a_in, &A);
     g_trace.mark("viewA");
-    if (!rc && !fb_words) rc = device_view(ctx, b, b_rows * b_cols * 4, ctx->b_in, &B);
+    if (!rc && !fb_words) rc = matrix_view(ctx, b, b_rows * b_cols, ctx->b_in, &B);
     if (rc) return rc;
     const uint32_t* Ad = static_cast<const uint32_t*>(A);
     const uint32_t* Bd = static_cast<const uint32_t*>(B);

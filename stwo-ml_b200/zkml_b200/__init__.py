@@ -72,6 +72,7 @@ _SIGS = {
     "zkml_ctx_destroy": (C.c_int, [C.c_void_p]),
     "zkml_ctx_device": (C.c_int, [C.c_void_p]),
     "zkml_ctx_kernel_launches": (C.c_uint64, [C.c_void_p]),
+    "zkml_ctx_h2d_bytes": (C.c_uint64, [C.c_void_p]),
     "zkml_ctx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
     "zkml_ctx_enable_timing": (C.c_int, [C.c_void_p, C.c_int]),
     "zkml_ctx_kernel_time": (C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
@@ -400,6 +401,10 @@ class Context:
 
     def kernel_launches(self) -> int:
         return int(lib().zkml_ctx_kernel_launches(self.handle))
+
+    def h2d_bytes(self) -> int:
+        """Host -> device bytes of this context's input-matrix uploads so far."""
+        return int(lib().zkml_ctx_h2d_bytes(self.handle))
 
     KERNEL_CLASSES = ("restrict_cols", "restrict_rows", "sumcheck_round", "merkle", "host_sync", "host_channel")
 

@@ -229,6 +229,9 @@ def run_b200(args):
     dev = torch.cuda.current_device()
     if world > 1:  # one rank alone keeps every host CPU: the packed upload of B runs on them
         bind_to_gpu_cpus(dev)
+        # several ranks share the host's memory bandwidth, which packing spends more of than
+        # the plain copy (it reads every word on the CPUs): B goes over as words
+        os.environ.setdefault("ZKML_PACK_H2D", "0")
     stream = torch.cuda.current_stream()
     ctx = Z.Context(dev)
     ctx.set_stream(stream.cuda_stream)

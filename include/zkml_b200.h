@@ -70,7 +70,7 @@ int zkml_ctx_device(const zkml_ctx *ctx);
 uint64_t zkml_ctx_kernel_launches(const zkml_ctx *ctx);
 /* Host -> device bytes of the input-matrix uploads of this context so far (instrumentation for
  * benchmarks).  B of zkml_reduce_matmul_layer / _gkr in host memory with at least 2^22 words
- * (ZKML_PACK_MIN) crosses PCIe in chunks of 2^20 words packed by host threads into one byte per
+ * (ZKML_PACK_MIN) crosses PCIe in chunks of 2^18 words packed by host threads into one byte per
  * word when every word of the chunk is the M31 image of a signed byte (x >= 0 ? x : p + x, the
  * reference's int8 quantisation); other chunks are copied as they are.  The device receives the
  * same field elements either way.  ZKML_PACK_H2D=0 turns the packing off. */

@@ -1,7 +1,7 @@
 """Packed host -> device upload of B (csrc/h2d_pack.cu) inside zkml_reduce_matmul_layer.
 
 A host B whose words are the M31 images of signed bytes crosses PCIe as one byte per word, in
-chunks of 2^20 words; a chunk with any other word goes over unchanged.  The proof must be the
+chunks of 2^18 words; a chunk with any other word goes over unchanged.  The proof must be the
 oracle's, bit for bit, whichever way each chunk travelled, and the bytes the context counts must
 show which way that was.  ZKML_PACK_MIN=1 makes every host B take the packed path here (the
 default threshold is 2^22 words; the full config-2 B of tests/test_matmul_gpu.py takes it by
@@ -16,7 +16,7 @@ from helpers import M31_P, int_matrix_m31, log2, next_pow2, random_qm31
 
 pytestmark = pytest.mark.gpu
 
-CHUNK = 1 << 20
+CHUNK = 1 << 18
 
 
 def prove(a, b, seed):
@@ -42,6 +42,10 @@ def same(got, ref):
     assert (got.final_a_eval == ref["final_a"]).all() and (got.final_b_eval == ref["final_b"]).all()
 
 
+def chunks(b):
+    return -(-b.size // CHUNK)  # one packed/raw flag byte per chunk also crosses
+
+
 def byte_matrix(k, n, seed):
     b = int_matrix_m31(k, n, seed, bound=128)  # [-128, 128]: 128 is out of range, clamp it
     b[b == 128] = 127
@@ -58,10 +62,10 @@ def pack_small(monkeypatch):
 
 def test_packed_chunks_match_oracle(pack_small):
     a = int_matrix_m31(4, 1100, 31)
-    b = byte_matrix(1100, 1000, 32)  # 1.1 M words: two chunks, the second ragged
+    b = byte_matrix(1100, 1000, 32)  # 1.1 M words: five chunks, the last ragged
     got, h2d, pts = prove(a, b, 5)
     same(got, oracle(a, b, pts))
-    assert h2d == a.size * 4 + b.size  # A as words, every chunk of B as bytes
+    assert h2d == a.size * 4 + b.size + chunks(b)  # A as words, every chunk of B as bytes
 
 
 def test_raw_chunk_beside_packed_one(pack_small):
@@ -70,7 +74,7 @@ def test_raw_chunk_beside_packed_one(pack_small):
     b.reshape(-1)[CHUNK + 5] = 1000  # not a signed byte: the second chunk goes as words
     got, h2d, pts = prove(a, b, 6)
     same(got, oracle(a, b, pts))
-    assert h2d == a.size * 4 + CHUNK + (b.size - CHUNK) * 4
+    assert h2d == a.size * 4 + (b.size - CHUNK) + CHUNK * 4 + chunks(b)
 
 
 def test_packing_off_gives_the_same_proof(monkeypatch):
@@ -83,7 +87,7 @@ def test_packing_off_gives_the_same_proof(monkeypatch):
     same(packed, oracle(a, b, pts))
     for x, y in zip(packed.round_polys, plain.round_polys):
         assert (x.c0 == y.c0).all() and (x.c1 == y.c1).all() and (x.c2 == y.c2).all()
-    assert h_on == a.size * 4 + b.size and h_off == (a.size + b.size) * 4
+    assert h_on == a.size * 4 + b.size + chunks(b) and h_off == (a.size + b.size) * 4
 
 
 def test_word_with_bit31_still_rejected(pack_small):

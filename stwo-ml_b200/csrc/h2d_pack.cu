@@ -19,6 +19,7 @@
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
+#include <exception>
 #include <memory>
 #include <thread>
 #include <vector>
@@ -124,7 +125,11 @@ int upload_m31_packed(::zkml_ctx* ctx, const uint32_t* host, size_t count, DevBu
     const int nt = (int)std::min<size_t>((size_t)threads, chunks);
     std::vector<std::thread> pool;
     pool.reserve(nt);
-    for (int t = 0; t < nt; t++) pool.emplace_back(worker);
+    try {
+        for (int t = 0; t < nt; t++) pool.emplace_back(worker);
+    } catch (const std::exception&) {  // no more threads: go on with those that started
+    }
+    if (pool.empty()) return device_view(ctx, host, count * 4, dst, out);
     uint32_t* dev = static_cast<uint32_t*>(dst.ptr);
     int8_t* dp = ctx->pack_dev.as<int8_t>();
     size_t packed_bytes = 0;
